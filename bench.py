@@ -1,0 +1,335 @@
+"""Benchmark of the MoE expert-FFN path (one JSON line on rank 0).
+
+Workload: a Qwen-Next-style decode MoE layer,
+H=2048, 512 routed experts of I=512 + 1 shared expert, MXFP4 blobs, top-10
+softmax routing, 64 tokens per step and per GPU, seeded synthetic inputs.
+A step is one layer forward through the public API (router -> sort -> expert
+GEMVs -> shared expert -> combine).  Each step uses the next of 8 token
+batches, so routes change; L2 is flushed (a 256 MB write) before every timed
+step.  `value` is whole-job tokens/s from device events (inputs resident);
+`e2e` is the same through the public call with pinned host input/output and
+the copies inside the timed region.  With --gpus N > 1 every rank runs its
+own batch.  `--impl reference` times the CPU oracle (the restatement of the
+reference's arithmetic) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE-layer tokens/s (prefill, decode) at 1/2/4/8 B200; % of HBM / FP4-TC roofline"
+H, I, E, K = 2048, 512, 512, 10
+BLOB = 1_671_168  # bytes of one expert blob (gate_up + scales + down + scales)
+GATE_UP_BYTES = 2 * I * H // 2 + 2 * I * H // 32
+DOWN_BYTES = H * I // 2 + H * I // 32
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = ROOT / "gpurun_out" / f"clocks_rank{index}.csv"
+
+    def __enter__(self):
+        try:
+            self.path.parent.mkdir(exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index),
+                 "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            self.proc.wait(timeout=5)
+            self.f.close()
+
+    def summary(self) -> dict:
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[3:7]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_init():
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def cpu_sample(layer_np, xb, idx, w, min_seconds: float, tokens: int):
+    """Oracle forward on `tokens` tokens, repeated for at least min_seconds; tokens/s."""
+    import numpy as np
+    sub = np.arange(tokens, dtype=np.int32)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        layer_np.forward(xb, idx, w, tokens=sub)
+        n += 1
+        dt = time.perf_counter() - t0
+        if dt >= min_seconds:
+            return tokens * n / dt
+
+
+def run_reference(args) -> None:
+    """The reference arm: the CPU oracle on the box's host cores."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+    import torch
+    import oracle
+    from oracle import adapter
+    from whallm_b200 import synth
+
+    cores = len(os.sched_getaffinity(0))
+    wl = synth.config(1, device="cpu", batch=64)
+    layer_np = adapter.from_layer(wl.layer)
+    xb = adapter.bits(wl.x)
+    logits = oracle.router_logits(xb, adapter.bits(wl.layer.router.weight))
+    idx, w = oracle.route(oracle.ROUTER_SOFTMAX, logits, K)
+    sample = 8
+    sub = np.arange(sample, dtype=np.int32)
+    for _ in range(args.warmup):
+        layer_np.forward(xb, idx, w, tokens=sub)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        layer_np.forward(xb, idx, w, tokens=sub)
+    dt = time.perf_counter() - t0
+    tps = sample * args.steps / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded, BASELINE configs[1] shapes)",
+        "config": {"workload": "config1 decode layer, 64-token batch (8-token sample per step)", "H": H, "I": I,
+                   "E": E, "K": K, "shared_expert": True},
+        "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{sample} tokens of a 64-token config-1 batch per step, OpenMP over {cores} cores"},
+        "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run(args) -> None:
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from whallm_b200 import lib, synth
+    from whallm_b200.moe import Engine
+
+    world, rank, local = dist_init()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    B = args.batch
+    wl = synth.config(1, device=dev, batch=B, seed=0)
+    layer = wl.layer
+    nb = 8
+    xs = [synth.activations(B, H, torch.Generator(device=dev).manual_seed(1000 * rank + i), dev) for i in range(nb)]
+    eng = Engine(local, max_tokens=max(B, 64), hidden=H, inter=I, experts=E, topk=K)
+    x_static = xs[0].clone()
+    out_static = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    # launches of our kernels in one step (counted on an eager call)
+    c0 = eng.ctx.counters().launches
+    eng.forward(layer, x_static, K, out=out_static)
+    eng.sync()
+    launches_per_step = eng.ctx.counters().launches - c0
+
+    # capture one step as a CUDA graph (router -> plan -> GEMVs -> combine)
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            eng.forward(layer, x_static, K, out=out_static)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            eng.forward(layer, x_static, K, out=out_static)
+    torch.cuda.synchronize()
+
+    def step(i, timed_events=None):
+        x_static.copy_(xs[i % nb])
+        flush.zero_()
+        if timed_events is not None:
+            timed_events[0].record(stream)
+        graph.replay()
+        if timed_events is not None:
+            timed_events[1].record(stream)
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with Clocks(local) as clocks:
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            for i in range(args.steps):
+                step(i, evs[i])
+        torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in evs)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    value = world * B * args.steps / (ms / 1e3)
+
+    # per-kernel durations (library CUDA events) over the same steps, eager
+    eng.ctx.profile(True)
+    eng.ctx.profile_reset()
+    uniq = []
+    with torch.cuda.stream(stream):
+        for i in range(args.steps):
+            x_static.copy_(xs[i % nb])
+            flush.zero_()
+            _, (rw, ri) = eng.forward(layer, x_static, K, out=out_static, return_routes=True)
+            uniq.append(int(torch.unique(ri).numel()))
+    torch.cuda.synchronize()
+    prof = eng.ctx.profile_read()
+    eng.ctx.profile(False)
+    U = statistics.mean(uniq)
+    gu_n, gu_ms = prof.get("gemv_gate_up", (1, float("nan")))
+    dn_n, dn_ms = prof.get("gemv_down", (1, float("nan")))
+    gu_bytes = (U + 1) * GATE_UP_BYTES + B * H * 2 + B * 2 * I * 2  # weights + x + act written
+    dn_bytes = (U + 1) * DOWN_BYTES + (B * K + B) * (I * 2 + H * 2)
+    gu_avg = gu_ms / gu_n
+    pk = peaks()
+    achieved = gu_bytes / (gu_avg / 1e3) / 1e9
+    kernels = {name: {"launches": n, "avg_us": 1e3 * t / n} for name, (n, t) in prof.items()}
+
+    # end to end through the public call with pinned host buffers
+    xh = [x.cpu().pin_memory() for x in xs]
+    oh = torch.empty((B, H), dtype=torch.bfloat16).pin_memory()
+    e_evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            xd = xh[i % nb].to(dev, non_blocking=True)
+            oh.copy_(eng.forward(layer, xd, K), non_blocking=True)
+        torch.cuda.synchronize()
+        for i in range(args.steps):
+            flush.zero_()
+            e_evs[i][0].record(stream)
+            xd = xh[i % nb].to(dev, non_blocking=True)
+            oh.copy_(eng.forward(layer, xd, K), non_blocking=True)
+            e_evs[i][1].record(stream)
+    torch.cuda.synchronize()
+    e_ms = sum(a.elapsed_time(b) for a, b in e_evs)
+    if world > 1:
+        t = torch.tensor([e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = float(t.item())
+    e2e = world * B * args.steps / (e_ms / 1e3)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        import oracle
+        from oracle import adapter
+        layer_np = adapter.from_layer(layer)
+        xb = adapter.bits(xs[0])
+        _, (rw, ri) = eng.forward(layer, xs[0], K, return_routes=True)
+        cores = len(os.sched_getaffinity(0))
+        tps = cpu_sample(layer_np, xb, ri.cpu().numpy(), rw.cpu().numpy(), min_seconds=10.0, tokens=16)
+        cpu = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"16 tokens of a config-1 batch, repeated for >= 10 s, OpenMP over {cores} cores"}
+
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32-accumulate MXFP4 x bf16",
+        "data": "synthetic (seeded; BASELINE configs[1] value distributions)",
+        "config": {"workload": f"config1 decode layer, {B} tokens per step per GPU", "H": H, "I": I, "E": E,
+                   "K": K, "shared_expert": True, "router": "softmax top-10",
+                   "l2": "flushed (256 MB write) before every timed step",
+                   "timing": "CUDA graph replay per step, device events, max over ranks",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "unique_experts_per_step": U},
+        "roofline": {"bound": "hbm", "kernel": "gemv_gate_up", "achieved": achieved, "peak": pk["hbm_gbs"],
+                     "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "peak_source": pk["source"],
+                     "traffic": None, "algorithmic_bytes_per_launch": gu_bytes,
+                     "down_achieved_gbs": dn_bytes / (dn_ms / dn_n / 1e3) / 1e9},
+        "kernels": kernels,
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": B * H * 2, "d2h_bytes_per_step": B * H * 2},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,202 @@
+/*
+ * whallm_moe.h -- C ABI of the B200 MoE expert-FFN library (libwhallm_moe.so).
+ *
+ * Replaces the expert arithmetic that Whallm's Python runtime reaches through
+ * MLX and its native engines reach through Metal:
+ *
+ *   mx.gather_qmm / mx.quantized_matmul(mode="mxfp4", group_size=32)
+ *       runtime/deepseek_v4_ssd/model.py:435-513, qwen4_exp.py:774-783, 853-904
+ *   router + top-k        qwen4_exp.py:1009-1047, deepseek_v41/moe.py:46-74,
+ *                         mimo/model.py:132-150, Native/QwenNative/engine.mm:2085-2101,
+ *                         Native/DeepSeekNative/engine.mm:1863-1890
+ *   sort / permute        qwen_expert_waves.py:23-51, Native/QwenNative/engine.mm:2105-2127
+ *   SwiGLU + combine      qwen4_exp.py:815-818, 1049-1051; deepseek_v41/moe.py:30-43, 105-112;
+ *                         Native/QwenNative/kernels.metal:175-194, 756-765
+ *   shared expert         qwen4_exp.py:1046, deepseek_v41/moe.py:77-93
+ *
+ * Conventions follow the reference's native C ABI (Native/QwenNative/capi.h:1-5):
+ * an opaque handle; functions returning int return 0 on success, 1 on an error
+ * (text from wm_error) and 2 when a call was cancelled; calls on one handle
+ * come from one host thread at a time.  Unlike the reference, a failed call
+ * leaves the handle usable.
+ *
+ * Every pointer named "device" is CUDA device memory of the handle's GPU
+ * (the caller owns it; PyTorch tensors in practice).  Every call is enqueued
+ * on the caller's CUDA stream (`stream`, a cudaStream_t; NULL = the legacy
+ * default stream) and returns without waiting for the GPU; wm_sync waits and
+ * reports errors that kernels recorded on the device.
+ *
+ * Expert weights are used in place, in the reference's on-disk blob layout
+ * (runtime/deepseek_v4_ssd/expert_layout.py:8-166): a projection of expert e
+ * starts at `weight + e * weight_stride`, its scales at
+ * `scale + e * scale_stride`.  This covers both the slot-major arena and the
+ * region-major layer buffer of batched_layer_layout (expert_layout.py:83-119),
+ * whose (base, stride, inner) triple becomes weight = buffer + base + inner,
+ * weight_stride = stride.
+ */
+#ifndef WHALLM_MOE_H
+#define WHALLM_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+#define WM_EXPORT __attribute__((visibility("default")))
+extern "C" {
+#else
+#define WM_EXPORT __attribute__((visibility("default")))
+#endif
+
+#define WM_OK 0
+#define WM_ERROR 1
+#define WM_CANCELLED 2
+
+typedef struct wm_ctx wm_ctx;
+
+/* Expert blob layouts (the weights of one expert). */
+enum wm_layout {
+  /* Qwen: gate_up.weight | gate_up.scale | down.weight | down.scale;
+     gate rows [0, I) then up rows [I, 2I) (Sources/DeepSeekRepack/Qwen.swift:51-65). */
+  WM_LAYOUT_QWEN_GATE_UP_MXFP4 = 0,
+  /* DeepSeek / MiMo: w3 | w1 | w2 | w3.s | w1.s | w2.s, w13 = [w3; w1]:
+     up rows first (expert_layout.py:8-63, model.py:452-461). */
+  WM_LAYOUT_DS_W13_MXFP4 = 1,
+  /* FP8 E4M3 experts with fp32 128x128 block scales: w13.weight | w2.weight |
+     w13.scale | w2.scale, w13 = [w3; w1] (up rows first).  New layout: the
+     reference decodes this format only for resident tensors
+     (mimo/weights.py:17-43). */
+  WM_LAYOUT_W13_FP8_B128 = 2,
+};
+
+/* Weight formats for wm_dequant. */
+enum wm_format {
+  WM_FORMAT_MXFP4 = 0,     /* packed E2M1 [rows, cols/2] + E8M0 [rows, cols/32] */
+  WM_FORMAT_FP8_B128 = 1,  /* E4M3 [rows, cols] + fp32 [ceil(rows/128), ceil(cols/128)] */
+  WM_FORMAT_FP8_B32 = 2,   /* E4M3 [rows, cols] + UE8M0 [ceil(rows/32), ceil(cols/32)] */
+};
+
+/* Decode conventions where the reference's two decoders differ. */
+enum wm_convention {
+  WM_CONV_MLX = 0,    /* E2M1 code 8 -> +0; E8M0 byte 0 -> 2^-127 (deepseek_v41/dequant.py:27-35) */
+  WM_CONV_METAL = 1,  /* code 8 -> -0; byte 0 -> 0 (Native/QwenNative/kernels.metal:701-702, 727) */
+};
+
+enum wm_router_kind {
+  WM_ROUTER_SOFTMAX = 0,         /* Qwen: softmax, top-k, renormalised (qwen4_exp.py:1009-1047) */
+  WM_ROUTER_SQRTSOFTPLUS = 1,    /* DeepSeek V4.1: sqrt(softplus), bias selects (moe.py:58-74) */
+  WM_ROUTER_SIGMOID = 2,         /* MiMo: sigmoid + correction bias (mimo/model.py:139-150) */
+  WM_ROUTER_SIGMOID_GROUPED = 3, /* sigmoid + bias, group-limited selection (not in the reference) */
+};
+
+enum wm_shared_gate {
+  WM_SHARED_NONE = 0,          /* no shared expert */
+  WM_SHARED_SIGMOID_GATE = 1,  /* Qwen: sigmoid(x . g) * shared(x) (qwen4_exp.py:1046) */
+  WM_SHARED_ONE = 2,           /* DeepSeek: shared(x) added as is (moe.py:110-112) */
+};
+
+/* Sizes that bound every later call; wm_create reserves the device workspace. */
+typedef struct {
+  int64_t max_tokens;       /* largest T of any call */
+  int32_t max_hidden;       /* largest H */
+  int32_t max_inter;        /* largest I */
+  int32_t max_experts;      /* largest E (routed experts) */
+  int32_t max_topk;         /* largest K */
+  int32_t gemv_max_tokens;  /* T up to this runs the decode GEMV kernels; 0 = default 64, -1 = never */
+  int32_t flags;            /* reserved, 0 */
+} wm_options;
+
+/* One projection of every expert: expert e's matrix at weight + e * weight_stride
+   bytes, its scales at scale + e * scale_stride bytes (device pointers). */
+typedef struct {
+  const void* weight;
+  int64_t weight_stride;
+  const void* scale;
+  int64_t scale_stride;
+} wm_matrix;
+
+typedef struct {
+  int32_t T, H, I, E, K;
+  int32_t layout;                 /* enum wm_layout */
+  wm_matrix w13;                  /* fused gate/up projection, [2I, H] per expert */
+  wm_matrix w2;                   /* down projection, [H, I] per expert */
+  wm_matrix shared_w13;           /* the shared expert (strides ignored); weight NULL = none */
+  wm_matrix shared_w2;
+  int32_t shared_gate;            /* enum wm_shared_gate */
+  const void* shared_gate_weight; /* bf16 [H] for WM_SHARED_SIGMOID_GATE */
+  const void* x;                  /* bf16 [T, H] */
+  /* Routing: router weights, or (router_weight NULL) precomputed routes. */
+  int32_t router;                 /* enum wm_router_kind */
+  const void* router_weight;      /* bf16 [E, H] */
+  const float* router_bias;       /* fp32 [E] selection bias, or NULL */
+  int32_t n_groups, topk_groups;  /* WM_ROUTER_SIGMOID_GROUPED only */
+  float route_scale;              /* multiplies the routing weights (1.0 for Qwen / MiMo) */
+  const int32_t* routes_idx;      /* int32 [T, K] expert ids (when router_weight is NULL) */
+  const float* routes_w;          /* fp32 [T, K] routing weights */
+  float swiglu_limit;             /* > 0: silu(min(g, L)) * clamp(u, -L, L); else silu(g) * u */
+  void* out;                      /* bf16 [T, H] combined output */
+  int32_t* out_idx;               /* optional int32 [T, K]: routes used */
+  float* out_w;                   /* optional fp32 [T, K] */
+} wm_moe_args;
+
+typedef struct {
+  int64_t calls_forward, calls_pairs, calls_route, calls_dequant;
+  int64_t launches;            /* kernels enqueued by this handle */
+  int64_t gemv_calls, gemm_calls;
+} wm_counters;
+
+typedef struct {
+  char name[32];      /* kernel group: router, plan, gather_rows, gemv_gate_up, ... */
+  int64_t launches;   /* timed launches since the last reset */
+  double total_ms;    /* summed CUDA-event durations */
+} wm_profile_entry;
+
+/* Creates a handle on CUDA device `device`.  NULL on failure, with a message in
+   error[0 .. error_size).  Replaces wq_open's engine set-up
+   (Native/QwenNative/capi.h:41) for the expert path only. */
+WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* error, size_t error_size);
+WM_EXPORT void wm_destroy(wm_ctx* ctx);
+/* The message of the last failed call (Native/QwenNative/capi.h:43). */
+WM_EXPORT const char* wm_error(const wm_ctx* ctx);
+/* Waits for `stream`; returns 1 if a kernel recorded an error since the last
+   wm_sync (e.g. an expert id out of range), with the text in wm_error. */
+WM_EXPORT int wm_sync(wm_ctx* ctx, void* stream);
+WM_EXPORT void wm_counters_get(const wm_ctx* ctx, wm_counters* out);
+
+/* Dequantise one matrix to bf16 [rows, cols] (device): the decode of
+   deepseek_v41/dequant.py:53-68 (MXFP4), mimo/weights.py:17-43 (FP8 128x128)
+   and dequant.py:45-50 (FP8 32x32 UE8M0), bit for bit. */
+WM_EXPORT int wm_dequant(wm_ctx* ctx, int32_t format, const void* weight, const void* scale, int64_t rows,
+                         int64_t cols, int32_t convention, void* out_bf16, void* stream);
+
+/* Router logits and top-k: logits (optional, fp32 [T, E]), idx int32 [T, K],
+   w fp32 [T, K] (SparseMoE.route/_gates, qwen4_exp.py:1009-1047; Gate,
+   deepseek_v41/moe.py:58-74; Router, mimo/model.py:139-150).  Uses
+   args->{T, H, E, K, x, router, router_weight, router_bias, n_groups,
+   topk_groups, route_scale}. */
+WM_EXPORT int wm_route(wm_ctx* ctx, const wm_moe_args* args, float* logits, int32_t* idx, float* w, void* stream);
+
+/* Routed expert rows without the combine: routed bf16 [T, K, H] with row
+   (t, k) = expert idx[t, k] applied to x[t] -- the output of
+   StreamingExperts.__call__ (qwen4_exp.py:853-904) and
+   _StreamingSwitchGLU.__call__ (model.py:325-501).  Uses args->routes_idx. */
+WM_EXPORT int wm_expert_pairs(wm_ctx* ctx, const wm_moe_args* args, void* routed, void* stream);
+
+/* The whole MoE block: route, sort, experts, shared expert, combine
+   (SparseMoE.__call__, qwen4_exp.py:1015-1051; _streaming_moe, model.py:526-546;
+   MoE.__call__, deepseek_v41/moe.py:105-112). */
+WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* args, void* stream);
+
+/* Per-kernel-group timing with CUDA events recorded on the calls' streams
+   (the counterpart of the native engines' gpu_seconds counters,
+   Native/QwenNative/capi.h:28-35).  Off by default; while on, calls must not
+   be captured into CUDA graphs. */
+WM_EXPORT int wm_profile_enable(wm_ctx* ctx, int32_t enable);
+/* Waits for the timed work, then copies up to max_entries accumulated groups;
+   returns the number copied. */
+WM_EXPORT int32_t wm_profile_read(wm_ctx* ctx, wm_profile_entry* out, int32_t max_entries);
+WM_EXPORT void wm_profile_reset(wm_ctx* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* WHALLM_MOE_H */

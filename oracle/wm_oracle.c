@@ -427,11 +427,12 @@ static void route_token(int router, const float* logits, const float* bias, int6
   double* key = (double*)malloc((size_t)E * sizeof(double));
   unsigned char* allowed = NULL;
   if (router == WMO_ROUTER_SOFTMAX) {
-    for (int64_t e = 0; e < E; ++e) key[e] = logits[e];
+    /* an optional additive logit bias (used by the synthetic Zipf workload) */
+    for (int64_t e = 0; e < E; ++e) key[e] = bias ? (double)(float)(logits[e] + bias[e]) : (double)logits[e];
     topk_desc(key, E, K, NULL, idx);
-    double top = logits[idx[0]], kept = 0.0;
-    for (int64_t k = 0; k < K; ++k) kept += exp((double)logits[idx[k]] - top);
-    for (int64_t k = 0; k < K; ++k) w[k] = (float)(exp((double)logits[idx[k]] - top) / kept);
+    double top = key[idx[0]], kept = 0.0;
+    for (int64_t k = 0; k < K; ++k) kept += exp(key[idx[k]] - top);
+    for (int64_t k = 0; k < K; ++k) w[k] = (float)(exp(key[idx[k]] - top) / kept * route_scale);
   } else {
     for (int64_t e = 0; e < E; ++e) {
       double v = logits[e];

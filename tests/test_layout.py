@@ -1,0 +1,49 @@
+"""Blob-layout mirror (expert_layout.py:8-166) on the host (no GPU)."""
+import pytest
+import torch
+
+from whallm_b200 import layout as L
+
+
+def test_qwen_blob_size_matches_config_shapes():
+    regs = L.qwen_regions(2048, 512)
+    assert L.blob_size(regs, L.QWEN_BATCHED) == 1_671_168
+
+
+def test_fused_blob_size_and_w13_view():
+    regs = L.fused_regions(7168, 2048)
+    assert L.blob_size(regs, L.FUSED_BATCHED) == 23_396_352
+    assert regs["w13.weight"].offset == 0 and regs["w13.weight"].length == 2 * regs["w1.weight"].length
+    assert regs["w13.scale"].offset == regs["w3.scale"].offset
+
+
+def test_fp8_blob_size():
+    regs = L.fp8_regions(7168, 2048)
+    assert L.blob_size(regs, L.FP8_BATCHED) == 44_050_944
+
+
+def test_batched_layer_layout_places_regions():
+    regs = L.fused_regions(256, 128)
+    size = L.blob_size(regs, L.FUSED_BATCHED)
+    lay = L.batched_layer_layout(regs, L.FUSED_BATCHED, size, 5)
+    base, stride, inner = lay["w1.weight"]
+    assert base == 0 and stride == regs["w13.weight"].length and inner == regs["w3.weight"].length
+    b2, s2, i2 = lay["w2.scale"]
+    assert s2 == regs["w2.scale"].length and i2 == 0
+    assert lay["w13.scale"][0] == 5 * (regs["w13.weight"].length + regs["w2.weight"].length)
+
+
+def test_batched_layer_layout_rejects_bad_partitions():
+    regs = L.qwen_regions(256, 128)
+    with pytest.raises(ValueError):
+        L.batched_layer_layout(regs, ("gate_up.weight", "down.weight"), 0, 2)
+    with pytest.raises(ValueError):
+        L.batched_layer_layout(regs, L.QWEN_BATCHED, 1, 2)
+
+
+def test_projection_strides_follow_region_major_views():
+    buf = torch.zeros(10 * 96, dtype=torch.uint8)
+    w = torch.as_strided(buf, (10, 4, 16), (96, 16, 1), 8)  # expert stride 96, inner offset 8
+    s = torch.zeros(10, 4, 2, dtype=torch.uint8)
+    p = L.Projection.stacked(w, s)
+    assert p.weight_stride == 96 and p.scale_stride == 8

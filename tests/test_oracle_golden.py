@@ -1,0 +1,98 @@
+"""The oracle against the reference's own known answers (no GPU)."""
+import hashlib
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def kat_cases():
+    return json.loads((GOLDEN / "mxfp4_kat.json").read_text())["cases"]
+
+
+@pytest.mark.parametrize("case", kat_cases(), ids=lambda c: c["name"])
+def test_quantiser_matches_swift_known_answers(case):
+    """MXFP4.swift quantiser restatement reproduces DeepSeekRepackTests.swift:336-415."""
+    if case["kind"] == "bf16":
+        src = np.array(case["source_bf16"], np.uint16).reshape(case["rows"], case["cols"])
+        w, s = oracle.quantize_bf16_mxfp4(src)
+    else:
+        src = np.array(case["source_u8"], np.uint8).reshape(case["rows"], case["cols"])
+        inv = np.array(case["inverse_scale_bytes"], np.uint8).view(np.uint16)
+        w, s = oracle.quantize_fp8_mxfp4(src, inv)
+    if "expect" in case:
+        for e in case["expect"]:
+            got = (w if e["field"] == "weights" else s).reshape(-1)[: len(e["bytes"])]
+            assert got.tolist() == e["bytes"], e["field"]
+    else:
+        assert hashlib.sha256(w.tobytes()).hexdigest() == case["expect_sha256"]["weights"]
+        assert hashlib.sha256(s.tobytes()).hexdigest() == case["expect_sha256"]["scales"]
+
+
+def test_e2m1_table_and_conventions():
+    mags = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0]
+    for code in range(16):
+        v = oracle.e2m1(code, oracle.CONV_MLX)
+        expect = (-1.0 if code & 8 else 1.0) * mags[code & 7]
+        assert v == expect
+    assert np.signbit(oracle.e2m1(8, oracle.CONV_METAL)) and not np.signbit(oracle.e2m1(8, oracle.CONV_MLX))
+
+
+def test_e8m0_conventions():
+    for b in range(1, 255):
+        assert oracle.e8m0(b, oracle.CONV_MLX) == 2.0 ** (b - 127) == oracle.e8m0(b, oracle.CONV_METAL)
+    assert oracle.e8m0(0, oracle.CONV_MLX) == np.float32(2.0 ** -127)
+    assert oracle.e8m0(0, oracle.CONV_METAL) == 0.0
+    assert np.isinf(oracle.e8m0(255, oracle.CONV_MLX))
+
+
+def test_e4m3_matches_torch_float8_for_every_code():
+    codes = torch.arange(256, dtype=torch.uint8)
+    ref = codes.view(torch.float8_e4m3fn).float().numpy()
+    for b in range(256):
+        v = oracle.e4m3(b)
+        if np.isnan(ref[b]):
+            assert np.isnan(v)
+        else:
+            assert v == ref[b], b
+
+
+def test_dequant_mxfp4_matches_product_definition():
+    rng = np.random.default_rng(1)
+    w = rng.integers(0, 256, (7, 64), dtype=np.uint8)
+    s = rng.integers(100, 150, (7, 4), dtype=np.uint8)
+    out = oracle.bf16_to_f32(oracle.dequant_mxfp4(w, s))
+    lo, hi = w & 15, w >> 4
+    codes = np.stack([lo, hi], -1).reshape(7, 128)
+    mags = np.array([0, .5, 1, 1.5, 2, 3, 4, 6], np.float32)
+    vals = np.where(codes & 8, -1, 1) * mags[codes & 7] * np.exp2(s.astype(np.float32) - 127).repeat(32, 1)
+    np.testing.assert_array_equal(out, vals.astype(np.float32))
+
+
+def test_quantise_then_dequantise_is_a_fixed_point():
+    """Requantising dequantised MXFP4 values reproduces the same bytes."""
+    rng = np.random.default_rng(2)
+    w = rng.integers(0, 256, (16, 64), dtype=np.uint8)
+    s = rng.integers(110, 140, (16, 4), dtype=np.uint8)
+    # groups whose largest magnitude code is 6.0 keep their scale exactly
+    w[:, ::16] = (w[:, ::16] & 0xF0) | 0x07
+    deq = oracle.dequant_mxfp4(w, s)
+    w2, s2 = oracle.quantize_bf16_mxfp4(deq)
+    np.testing.assert_array_equal(oracle.dequant_mxfp4(w2, s2), deq)
+    np.testing.assert_array_equal(s2, s)
+
+
+def test_fp8_block_decode_rejects_reserved_codes_and_rounds_once():
+    w = np.full((128, 128), 0x38, np.uint8)  # 1.0
+    s = np.array([[0.1]], np.float32)
+    out = oracle.bf16_to_f32(oracle.dequant_fp8_b128(w, s))
+    assert out[0, 0] == oracle.bf16_to_f32(oracle.f32_to_bf16(np.float32(0.1)))
+    w[3, 5] = 0x7F
+    with pytest.raises(ValueError):
+        oracle.dequant_fp8_b128(w, s)

@@ -1,0 +1,482 @@
+// C ABI of libwhallm_moe.so: handle, workspace, validation and the
+// stream-ordered orchestration of the expert-FFN kernels.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+
+#include "wm_kernels.h"
+#include "wm_profile.h"
+
+struct wm_ctx {
+  int device = 0;
+  int num_sms = 148;
+  wm_options opt{};
+  std::string err;
+  wm_counters counters{};
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  wm::Plan plan{};
+  uint16_t* xs = nullptr;      // sorted input rows (GEMM path)
+  uint16_t* act = nullptr;     // sorted SwiGLU rows
+  uint16_t* routed = nullptr;  // sorted expert output rows
+  float* logits = nullptr;
+  int32_t* idx = nullptr;
+  float* w = nullptr;
+  float* sg = nullptr;
+  uint32_t* status = nullptr;  // [4]
+  int max_rows = 0, max_mtiles = 0, max_chunks = 0;
+  PFN_cuTensorMapEncodeTiled_v12000 encode_tiled = nullptr;
+  wm::Profiler prof;
+};
+
+namespace {
+
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int device) {
+    cudaGetDevice(&prev_);
+    if (prev_ != device) cudaSetDevice(device);
+  }
+  ~DeviceGuard() { cudaSetDevice(prev_); }
+
+ private:
+  int prev_ = 0;
+};
+
+int fail(wm_ctx* ctx, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  ctx->err = buf;
+  return WM_ERROR;
+}
+
+int check_launch(wm_ctx* ctx, const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(ctx, "%s: CUDA launch failed: %s", what, cudaGetErrorString(e));
+  return WM_OK;
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int fmt_of(int layout) { return layout == WM_LAYOUT_W13_FP8_B128 ? wm::kFmtFp8B128 : wm::kFmtMxfp4; }
+
+// Validates the shape / pointer contract shared by every expert call.
+int validate_experts(wm_ctx* ctx, const wm_moe_args* a, bool need_router) {
+  const wm_options& o = ctx->opt;
+  if (a == nullptr) return fail(ctx, "args is NULL");
+  if (a->T < 0) return fail(ctx, "T must be >= 0 (got %d)", a->T);
+  if (a->T > o.max_tokens) return fail(ctx, "T = %d exceeds the handle's max_tokens %lld", a->T, (long long)o.max_tokens);
+  if (a->H <= 0 || a->H > o.max_hidden) return fail(ctx, "H = %d outside (0, max_hidden %d]", a->H, o.max_hidden);
+  if (a->I <= 0 || a->I > o.max_inter) return fail(ctx, "I = %d outside (0, max_inter %d]", a->I, o.max_inter);
+  if (a->E <= 0 || a->E > o.max_experts) return fail(ctx, "E = %d outside (0, max_experts %d]", a->E, o.max_experts);
+  if (a->K <= 0 || a->K > o.max_topk || a->K > a->E)
+    return fail(ctx, "K = %d outside (0, min(E, max_topk %d)]", a->K, o.max_topk);
+  if (a->H % 64 || a->I % 64) return fail(ctx, "H (%d) and I (%d) must be multiples of 64", a->H, a->I);
+  if (a->layout < WM_LAYOUT_QWEN_GATE_UP_MXFP4 || a->layout > WM_LAYOUT_W13_FP8_B128)
+    return fail(ctx, "unknown expert layout %d", a->layout);
+  if (a->x == nullptr || !aligned(a->x, 16)) return fail(ctx, "x must be a 16-byte aligned device pointer");
+  const wm_matrix* ms[2] = {&a->w13, &a->w2};
+  for (const wm_matrix* m : ms) {
+    if (m->weight == nullptr || m->scale == nullptr) return fail(ctx, "expert weights and scales must be given");
+    if (!aligned(m->weight, 16) || m->weight_stride % 16)
+      return fail(ctx, "expert weight regions must start on 16-byte boundaries (pointer and per-expert stride)");
+    if (a->layout == WM_LAYOUT_W13_FP8_B128 && (!aligned(m->scale, 4) || m->scale_stride % 4))
+      return fail(ctx, "FP8 block scales must be 4-byte aligned");
+  }
+  if (a->shared_gate != WM_SHARED_NONE) {
+    if (a->shared_gate != WM_SHARED_SIGMOID_GATE && a->shared_gate != WM_SHARED_ONE)
+      return fail(ctx, "unknown shared_gate %d", a->shared_gate);
+    if (a->shared_w13.weight == nullptr || a->shared_w2.weight == nullptr || a->shared_w13.scale == nullptr ||
+        a->shared_w2.scale == nullptr)
+      return fail(ctx, "shared expert weights and scales must be given");
+    if (!aligned(a->shared_w13.weight, 16) || !aligned(a->shared_w2.weight, 16))
+      return fail(ctx, "shared expert weights must be 16-byte aligned");
+    if (a->shared_gate == WM_SHARED_SIGMOID_GATE && (a->shared_gate_weight == nullptr || !aligned(a->shared_gate_weight, 16)))
+      return fail(ctx, "the sigmoid shared gate needs a 16-byte aligned bf16 [H] weight");
+  }
+  if (need_router) {
+    if (a->router_weight != nullptr) {
+      if (!aligned(a->router_weight, 16)) return fail(ctx, "router_weight must be 16-byte aligned");
+      if (a->router < WM_ROUTER_SOFTMAX || a->router > WM_ROUTER_SIGMOID_GROUPED)
+        return fail(ctx, "unknown router kind %d", a->router);
+      if (a->E > 1024) return fail(ctx, "the router supports at most 1024 experts");
+      if (a->router == WM_ROUTER_SIGMOID_GROUPED) {
+        if (a->n_groups < 1 || a->n_groups > 32 || a->E % a->n_groups)
+          return fail(ctx, "n_groups must divide E and be in [1, 32]");
+        if (a->topk_groups < 1 || a->topk_groups > a->n_groups) return fail(ctx, "topk_groups outside [1, n_groups]");
+        if (a->K > a->topk_groups * (a->E / a->n_groups))
+          return fail(ctx, "K exceeds the experts of the kept groups");
+      }
+    } else if (a->routes_idx == nullptr || a->routes_w == nullptr) {
+      return fail(ctx, "give router_weight or routes_idx and routes_w");
+    }
+  }
+  if (a->layout == WM_LAYOUT_W13_FP8_B128 && (a->H % 128 || a->I % 128))
+    return fail(ctx, "FP8 128x128 experts need H and I multiples of 128");
+  return WM_OK;
+}
+
+wm::ExpertWeights weights_of(const wm_moe_args* a, bool with_shared) {
+  wm::ExpertWeights w{};
+  w.w13 = static_cast<const uint8_t*>(a->w13.weight);
+  w.w13_stride = a->w13.weight_stride;
+  w.s13 = static_cast<const uint8_t*>(a->w13.scale);
+  w.s13_stride = a->w13.scale_stride;
+  w.w2 = static_cast<const uint8_t*>(a->w2.weight);
+  w.w2_stride = a->w2.weight_stride;
+  w.s2 = static_cast<const uint8_t*>(a->w2.scale);
+  w.s2_stride = a->w2.scale_stride;
+  if (with_shared) {
+    w.sh_w13 = static_cast<const uint8_t*>(a->shared_w13.weight);
+    w.sh_s13 = static_cast<const uint8_t*>(a->shared_w13.scale);
+    w.sh_w2 = static_cast<const uint8_t*>(a->shared_w2.weight);
+    w.sh_s2 = static_cast<const uint8_t*>(a->shared_w2.scale);
+  }
+  w.E = a->E;
+  return w;
+}
+
+// Router logits + top-k into idx / w (and sg for the sigmoid shared gate).
+int run_router(wm_ctx* ctx, const wm_moe_args* a, float* logits, int32_t* idx, float* w, cudaStream_t s) {
+  const uint16_t* sg_w =
+      a->shared_gate == WM_SHARED_SIGMOID_GATE ? static_cast<const uint16_t*>(a->shared_gate_weight) : nullptr;
+  wm::prof_begin(&ctx->prof, wm::kProfRouter, s);
+  wm::launch_router_logits(static_cast<const uint16_t*>(a->x), static_cast<const uint16_t*>(a->router_weight), sg_w,
+                           a->T, a->H, a->E, logits, ctx->sg, s);
+  wm::launch_router_topk(logits, a->router_bias, a->T, a->E, a->K, a->router, a->n_groups, a->topk_groups,
+                         a->route_scale, idx, w, s);
+  wm::prof_end(&ctx->prof, wm::kProfRouter, s);
+  ctx->counters.launches += 2;
+  return check_launch(ctx, "router");
+}
+
+// Runs the experts of a plan already built on `s` (rows in ctx->routed).
+int run_experts(wm_ctx* ctx, const wm_moe_args* a, bool has_shared, bool gemm, cudaStream_t s) {
+  const wm::ExpertWeights wts = weights_of(a, has_shared);
+  const int gate_first = a->layout == WM_LAYOUT_QWEN_GATE_UP_MXFP4 ? 1 : 0;
+  if (!gemm) {
+    wm::GemvArgs g{};
+    g.plan = ctx->plan;
+    g.wts = wts;
+    g.x = static_cast<const uint16_t*>(a->x);
+    g.act = ctx->act;
+    g.routed = ctx->routed;
+    g.H = a->H;
+    g.I = a->I;
+    g.gate_first = gate_first;
+    g.limit = a->swiglu_limit;
+    const int max_unique = std::min(a->E, a->T * a->K) + (has_shared ? 1 : 0);
+    wm::launch_gemv(g, fmt_of(a->layout), max_unique, s, &ctx->prof);
+    ctx->counters.launches += 2;
+    ctx->counters.gemv_calls += 1;
+    return check_launch(ctx, "expert GEMV");
+  }
+  return fail(ctx, "the grouped GEMM path is not available in this build");
+}
+
+}  // namespace
+
+extern "C" {
+
+WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* error, size_t error_size) {
+  auto report = [&](const char* msg) {
+    if (error && error_size) snprintf(error, error_size, "%s", msg);
+  };
+  if (options == nullptr) {
+    report("options is NULL");
+    return nullptr;
+  }
+  wm_options o = *options;
+  if (o.gemv_max_tokens == 0) o.gemv_max_tokens = 64;
+  if (o.max_tokens <= 0 || o.max_hidden <= 0 || o.max_inter <= 0 || o.max_experts <= 0 || o.max_topk <= 0) {
+    report("every max_* option must be positive");
+    return nullptr;
+  }
+  if (o.max_experts > 1024 || o.max_topk > 64) {
+    report("max_experts must be <= 1024 and max_topk <= 64");
+    return nullptr;
+  }
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count) {
+    report("no such CUDA device");
+    return nullptr;
+  }
+  DeviceGuard guard(device);
+  cudaDeviceProp prop{};
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) {
+    report("cudaGetDeviceProperties failed");
+    return nullptr;
+  }
+  if (prop.major != 10) {
+    report("libwhallm_moe needs an sm_100 (B200-class) GPU");
+    return nullptr;
+  }
+  wm_ctx* ctx = new (std::nothrow) wm_ctx();
+  if (ctx == nullptr) {
+    report("out of host memory");
+    return nullptr;
+  }
+  ctx->device = device;
+  ctx->num_sms = prop.multiProcessorCount;
+  ctx->opt = o;
+  const int64_t T = o.max_tokens, K = o.max_topk, E = o.max_experts, H = o.max_hidden, I = o.max_inter;
+  const int64_t rows = T * K + T + int64_t(wm::kTileM) * (E + 1);
+  ctx->max_rows = int(rows);
+  ctx->max_mtiles = int(rows / wm::kTileM + E + 2);
+  ctx->max_chunks = 1024;
+  // workspace layout
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = off;
+    off = align_up(off + bytes, 256);
+    return at;
+  };
+  const size_t o_counts = take((E + 1) * 4), o_offsets = take((E + 2) * 4), o_pair = take(T * K * 4),
+               o_rowtok = take(rows * 4), o_unique = take((E + 1) * 4), o_nunique = take(4),
+               o_mtiles = take(size_t(ctx->max_mtiles) * 8), o_nm = take(4),
+               o_hist = take(size_t(ctx->max_chunks) * (E + 1) * 4), o_xs = take(rows * H * 2),
+               o_act = take(rows * I * 2), o_routed = take(rows * H * 2), o_logits = take(T * E * 4),
+               o_idx = take(T * K * 4), o_w = take(T * K * 4), o_sg = take(T * 4), o_status = take(16);
+  ctx->ws_bytes = off;
+  if (cudaMalloc(&ctx->ws, ctx->ws_bytes) != cudaSuccess) {
+    cudaGetLastError();
+    char msg[160];
+    snprintf(msg, sizeof(msg), "cudaMalloc of the %.1f MB workspace failed", ctx->ws_bytes / 1e6);
+    report(msg);
+    delete ctx;
+    return nullptr;
+  }
+  uint8_t* base = static_cast<uint8_t*>(ctx->ws);
+  ctx->plan.counts = reinterpret_cast<int32_t*>(base + o_counts);
+  ctx->plan.offsets = reinterpret_cast<int32_t*>(base + o_offsets);
+  ctx->plan.pair_pos = reinterpret_cast<int32_t*>(base + o_pair);
+  ctx->plan.row_token = reinterpret_cast<int32_t*>(base + o_rowtok);
+  ctx->plan.unique = reinterpret_cast<int32_t*>(base + o_unique);
+  ctx->plan.n_unique = reinterpret_cast<int32_t*>(base + o_nunique);
+  ctx->plan.mtiles = reinterpret_cast<int32_t*>(base + o_mtiles);
+  ctx->plan.n_mtiles = reinterpret_cast<int32_t*>(base + o_nm);
+  ctx->plan.hist = reinterpret_cast<int32_t*>(base + o_hist);
+  ctx->xs = reinterpret_cast<uint16_t*>(base + o_xs);
+  ctx->act = reinterpret_cast<uint16_t*>(base + o_act);
+  ctx->routed = reinterpret_cast<uint16_t*>(base + o_routed);
+  ctx->logits = reinterpret_cast<float*>(base + o_logits);
+  ctx->idx = reinterpret_cast<int32_t*>(base + o_idx);
+  ctx->w = reinterpret_cast<float*>(base + o_w);
+  ctx->sg = reinterpret_cast<float*>(base + o_sg);
+  ctx->status = reinterpret_cast<uint32_t*>(base + o_status);
+  cudaMemset(ctx->status, 0, 16);
+  const size_t gemv_smem = wm::gemv_smem_bytes(int(H), int(I));
+  if (gemv_smem > size_t(prop.sharedMemPerBlockOptin)) {
+    report("max_hidden is too large for the decode GEMV's shared-memory staging");
+    cudaFree(ctx->ws);
+    delete ctx;
+    return nullptr;
+  }
+  wm::gemv_init_attributes(int(gemv_smem));
+  cudaDriverEntryPointQueryResult q{};
+  void* fn = nullptr;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+      q == cudaDriverEntryPointSuccess)
+    ctx->encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  if (cudaDeviceSynchronize() != cudaSuccess) {
+    report("device initialisation failed");
+    cudaFree(ctx->ws);
+    delete ctx;
+    return nullptr;
+  }
+  return ctx;
+}
+
+WM_EXPORT void wm_destroy(wm_ctx* ctx) {
+  if (ctx == nullptr) return;
+  {
+    DeviceGuard guard(ctx->device);
+    cudaFree(ctx->ws);
+  }
+  delete ctx;
+}
+
+WM_EXPORT const char* wm_error(const wm_ctx* ctx) { return ctx ? ctx->err.c_str() : "no handle"; }
+
+WM_EXPORT void wm_counters_get(const wm_ctx* ctx, wm_counters* out) {
+  if (ctx && out) *out = ctx->counters;
+}
+
+WM_EXPORT int wm_sync(wm_ctx* ctx, void* stream) {
+  if (ctx == nullptr) return WM_ERROR;
+  DeviceGuard guard(ctx->device);
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(ctx, "stream synchronisation failed: %s", cudaGetErrorString(e));
+  uint32_t st[2] = {0, 0};
+  e = cudaMemcpy(st, ctx->status, sizeof(st), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return fail(ctx, "reading the device status failed: %s", cudaGetErrorString(e));
+  if (st[0] == wm::kStatusOk) return WM_OK;
+  cudaMemset(ctx->status, 0, 16);
+  switch (st[0]) {
+    case wm::kStatusBadExpert:
+      return fail(ctx, "expert ID is outside the model (pair %u)", st[1]);
+    case wm::kStatusOverflow:
+      return fail(ctx, "sorted rows exceeded the workspace (%u)", st[1]);
+    case wm::kStatusWaitTimeout:
+      return fail(ctx, "a GEMM pipeline wait timed out (role %u); results are invalid", st[1]);
+    case wm::kStatusNanCode:
+      return fail(ctx, "FP8 weights contain reserved NaN codes (row %u)", st[1]);
+    default:
+      return fail(ctx, "device status %u (%u)", st[0], st[1]);
+  }
+}
+
+WM_EXPORT int wm_dequant(wm_ctx* ctx, int32_t format, const void* weight, const void* scale, int64_t rows,
+                         int64_t cols, int32_t convention, void* out_bf16, void* stream) {
+  if (ctx == nullptr) return WM_ERROR;
+  if (format < WM_FORMAT_MXFP4 || format > WM_FORMAT_FP8_B32) return fail(ctx, "unknown format %d", format);
+  if (rows < 0 || cols <= 0 || cols % 32) return fail(ctx, "cols must be a positive multiple of 32");
+  if (rows == 0) return WM_OK;
+  if (!weight || !scale || !out_bf16) return fail(ctx, "weight, scale and out must be device pointers");
+  if (!aligned(weight, 8) || !aligned(out_bf16, 16)) return fail(ctx, "weight must be 8-byte and out 16-byte aligned");
+  if (format == WM_FORMAT_FP8_B128 && !aligned(scale, 4)) return fail(ctx, "fp32 block scales must be 4-byte aligned");
+  DeviceGuard guard(ctx->device);
+  wm::launch_dequant(format, weight, scale, rows, cols, convention, static_cast<uint16_t*>(out_bf16), ctx->status,
+                     static_cast<cudaStream_t>(stream));
+  ctx->counters.calls_dequant += 1;
+  ctx->counters.launches += 1;
+  return check_launch(ctx, "dequant");
+}
+
+WM_EXPORT int wm_route(wm_ctx* ctx, const wm_moe_args* a, float* logits, int32_t* idx, float* w, void* stream) {
+  if (ctx == nullptr) return WM_ERROR;
+  if (a == nullptr) return fail(ctx, "args is NULL");
+  if (a->router_weight == nullptr) return fail(ctx, "wm_route needs router_weight");
+  if (idx == nullptr || w == nullptr) return fail(ctx, "idx and w outputs must be given");
+  wm_moe_args b = *a;
+  b.shared_gate = WM_SHARED_NONE;
+  // only the router part of the contract applies
+  const wm_options& o = ctx->opt;
+  if (b.T < 0 || b.T > o.max_tokens) return fail(ctx, "T = %d outside [0, max_tokens]", b.T);
+  if (b.E <= 0 || b.E > std::min(o.max_experts, 1024)) return fail(ctx, "E = %d outside (0, max_experts]", b.E);
+  if (b.K <= 0 || b.K > b.E || b.K > o.max_topk) return fail(ctx, "K = %d outside (0, min(E, max_topk)]", b.K);
+  if (b.H <= 0 || b.H % 8 || b.H > o.max_hidden) return fail(ctx, "H = %d must be a multiple of 8 within max_hidden", b.H);
+  if (!b.x || !aligned(b.x, 16) || !aligned(b.router_weight, 16)) return fail(ctx, "x and router_weight must be 16-byte aligned");
+  if (b.router < WM_ROUTER_SOFTMAX || b.router > WM_ROUTER_SIGMOID_GROUPED) return fail(ctx, "unknown router kind %d", b.router);
+  if (b.router == WM_ROUTER_SIGMOID_GROUPED &&
+      (b.n_groups < 1 || b.n_groups > 32 || b.E % b.n_groups || b.topk_groups < 1 || b.topk_groups > b.n_groups ||
+       b.K > b.topk_groups * (b.E / b.n_groups)))
+    return fail(ctx, "invalid group-limited routing shape");
+  if (b.T == 0) return WM_OK;
+  DeviceGuard guard(ctx->device);
+  ctx->counters.calls_route += 1;
+  return run_router(ctx, &b, logits ? logits : ctx->logits, idx, w, static_cast<cudaStream_t>(stream));
+}
+
+WM_EXPORT int wm_expert_pairs(wm_ctx* ctx, const wm_moe_args* a, void* routed, void* stream) {
+  if (ctx == nullptr) return WM_ERROR;
+  wm_moe_args b = *a;
+  b.shared_gate = WM_SHARED_NONE;
+  b.router_weight = nullptr;
+  if (int rc = validate_experts(ctx, &b, false)) return rc;
+  if (b.routes_idx == nullptr) return fail(ctx, "wm_expert_pairs needs routes_idx");
+  if (routed == nullptr || !aligned(routed, 16)) return fail(ctx, "routed must be a 16-byte aligned device pointer");
+  if (b.T == 0) return WM_OK;
+  DeviceGuard guard(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool gemm = b.T > ctx->opt.gemv_max_tokens && ctx->opt.gemv_max_tokens >= 0 && false;
+  int launches = 0;
+  wm::prof_begin(&ctx->prof, wm::kProfPlan, s);
+  wm::launch_plan(b.routes_idx, b.T, b.K, b.E, false, gemm ? wm::kTileM : 1, ctx->plan, ctx->max_rows,
+                  ctx->max_mtiles, ctx->max_chunks, ctx->status, s, &launches);
+  wm::prof_end(&ctx->prof, wm::kProfPlan, s);
+  ctx->counters.launches += launches;
+  if (int rc = check_launch(ctx, "plan")) return rc;
+  if (int rc = run_experts(ctx, &b, false, gemm, s)) return rc;
+  wm::launch_unpermute(ctx->routed, ctx->plan, b.T * b.K, b.H, static_cast<uint16_t*>(routed), ctx->num_sms, s);
+  ctx->counters.launches += 1;
+  ctx->counters.calls_pairs += 1;
+  return check_launch(ctx, "unpermute");
+}
+
+WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* a, void* stream) {
+  if (ctx == nullptr) return WM_ERROR;
+  if (int rc = validate_experts(ctx, a, true)) return rc;
+  if (a->out == nullptr || !aligned(a->out, 16)) return fail(ctx, "out must be a 16-byte aligned device pointer");
+  if (a->T == 0) return WM_OK;
+  DeviceGuard guard(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool has_shared = a->shared_gate != WM_SHARED_NONE;
+  const bool gemm = false;
+  const int32_t* idx;
+  const float* w;
+  if (a->router_weight != nullptr) {
+    int32_t* di = a->out_idx ? a->out_idx : ctx->idx;
+    float* dw = a->out_w ? a->out_w : ctx->w;
+    if (int rc = run_router(ctx, a, ctx->logits, di, dw, s)) return rc;
+    idx = di;
+    w = dw;
+  } else {
+    idx = a->routes_idx;
+    w = a->routes_w;
+    if (a->shared_gate == WM_SHARED_SIGMOID_GATE) {
+      wm::launch_router_logits(static_cast<const uint16_t*>(a->x), nullptr,
+                               static_cast<const uint16_t*>(a->shared_gate_weight), a->T, a->H, 0, nullptr, ctx->sg,
+                               s);
+      ctx->counters.launches += 1;
+    }
+  }
+  int launches = 0;
+  wm::prof_begin(&ctx->prof, wm::kProfPlan, s);
+  wm::launch_plan(idx, a->T, a->K, a->E, has_shared, gemm ? wm::kTileM : 1, ctx->plan, ctx->max_rows,
+                  ctx->max_mtiles, ctx->max_chunks, ctx->status, s, &launches);
+  wm::prof_end(&ctx->prof, wm::kProfPlan, s);
+  ctx->counters.launches += launches;
+  if (int rc = check_launch(ctx, "plan")) return rc;
+  if (int rc = run_experts(ctx, a, has_shared, gemm, s)) return rc;
+  wm::prof_begin(&ctx->prof, wm::kProfCombine, s);
+  wm::launch_combine(ctx->routed, ctx->plan, w, ctx->sg, a->shared_gate, a->T, a->H, a->E, a->K,
+                     static_cast<uint16_t*>(a->out), s);
+  wm::prof_end(&ctx->prof, wm::kProfCombine, s);
+  ctx->counters.launches += 1;
+  ctx->counters.calls_forward += 1;
+  return check_launch(ctx, "combine");
+}
+
+WM_EXPORT int wm_profile_enable(wm_ctx* ctx, int32_t enable) {
+  if (ctx == nullptr) return WM_ERROR;
+  DeviceGuard guard(ctx->device);
+  ctx->prof.collect();
+  ctx->prof.enabled = enable != 0;
+  return WM_OK;
+}
+
+WM_EXPORT int32_t wm_profile_read(wm_ctx* ctx, wm_profile_entry* out, int32_t max_entries) {
+  if (ctx == nullptr || out == nullptr) return 0;
+  DeviceGuard guard(ctx->device);
+  ctx->prof.collect();
+  int32_t n = 0;
+  for (int sl = 0; sl < wm::kProfSlots && n < max_entries; ++sl) {
+    if (ctx->prof.launches[sl] == 0) continue;
+    snprintf(out[n].name, sizeof(out[n].name), "%s", wm::prof_name(sl));
+    out[n].launches = ctx->prof.launches[sl];
+    out[n].total_ms = ctx->prof.total_ms[sl];
+    ++n;
+  }
+  return n;
+}
+
+WM_EXPORT void wm_profile_reset(wm_ctx* ctx) {
+  if (ctx == nullptr) return;
+  DeviceGuard guard(ctx->device);
+  ctx->prof.reset();
+}
+
+}  // extern "C"

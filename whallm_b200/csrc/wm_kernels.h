@@ -1,0 +1,82 @@
+// Kernel launchers of the MoE expert-FFN library (host-callable, stream-ordered).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "../../include/whallm_moe.h"
+#include "wm_device.cuh"
+#include "wm_types.h"
+
+namespace wm {
+
+// ---- optional per-kernel timing with CUDA events (wm_profile_*)
+enum ProfSlot : int {
+  kProfRouter = 0,
+  kProfPlan,
+  kProfGather,
+  kProfGemvGateUp,
+  kProfGemvDown,
+  kProfGemmGateUp,
+  kProfGemmDown,
+  kProfCombine,
+  kProfSlots
+};
+struct Profiler;  // defined in wm_profile.cu
+void prof_begin(Profiler* p, int slot, cudaStream_t s);
+void prof_end(Profiler* p, int slot, cudaStream_t s);
+
+// ---- dequant probe (wm_dequant.cu)
+void launch_dequant(int format, const void* weight, const void* scale, int64_t rows, int64_t cols, int convention,
+                    uint16_t* out, uint32_t* status, cudaStream_t stream);
+
+// ---- router (wm_route.cu)
+void launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* sg_w, int T, int H, int E,
+                          float* logits, float* sg, cudaStream_t stream);
+void launch_router_topk(const float* logits, const float* bias, int T, int E, int K, int kind, int n_groups,
+                        int topk_groups, float route_scale, int32_t* idx, float* w, cudaStream_t stream);
+
+// ---- sort / permute / combine (wm_plan.cu)
+void launch_plan(const int32_t* idx, int T, int K, int E, bool has_shared, int align, const Plan& p, int max_rows,
+                 int max_mtiles, int max_chunks, uint32_t* status, cudaStream_t stream, int* launches);
+void launch_gather_rows(const uint16_t* x, const Plan& p, int E, int H, uint16_t* xs, int num_sms,
+                        cudaStream_t stream);
+void launch_combine(const uint16_t* routed, const Plan& p, const float* w, const float* sg, int shared_kind, int T,
+                    int H, int E, int K, uint16_t* out, cudaStream_t stream);
+void launch_unpermute(const uint16_t* routed, const Plan& p, int TK, int H, uint16_t* out, int num_sms,
+                      cudaStream_t stream);
+
+// ---- decode GEMV (wm_gemv.cu)
+struct GemvArgs {
+  Plan plan;
+  ExpertWeights wts;
+  const uint16_t* x;  // [T, H] bf16 (rows gathered through plan.row_token)
+  uint16_t* act;      // [rows, I] bf16, sorted rows
+  uint16_t* routed;   // [rows, H] bf16, sorted rows
+  int H, I;
+  int gate_first;     // 1: gate rows [0, I), up rows [I, 2I); 0: the reverse
+  float limit;        // SwiGLU clamp (<= 0: none)
+};
+void gemv_init_attributes(int max_smem);
+size_t gemv_smem_bytes(int H, int I);
+void launch_gemv(const GemvArgs& a, int fmt, int max_unique, cudaStream_t stream, Profiler* prof);
+
+// ---- prefill grouped GEMM on tcgen05 (wm_gemm_sm100.cu)
+struct GemmArgs {
+  Plan plan;
+  ExpertWeights wts;
+  const void* tmap_a;   // device copy of the A operand's CUtensorMap (bf16 [rows, Kdim], 128B swizzle)
+  uint16_t* out;        // gate/up: act [rows, I]; down: routed [rows, H]
+  int Kdim;             // H (gate/up) or I (down)
+  int N;                // 2I (gate/up) or H (down)
+  int I;
+  int gate_first;
+  float limit;
+  int fmt;
+  uint32_t* status;
+};
+// `kind`: 0 = gate/up + SwiGLU, 1 = down.  tmap_a points to a CUtensorMap
+// passed by value to the kernel.
+void launch_gemm(const GemmArgs& a, int kind, const void* tmap_host, int num_sms, cudaStream_t stream);
+
+}  // namespace wm

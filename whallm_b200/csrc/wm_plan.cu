@@ -1,0 +1,333 @@
+// Token sort / permute / unpermute on the device.
+//
+// The reference groups the flattened (token, k) pairs by expert with a stable
+// sort (np.argsort(kind="stable"), qwen_expert_waves.py:39-51;
+// std::stable_sort, Native/QwenNative/engine.mm:2105-2127) and gathers the rows
+// of each group (gather_rows16, QwenNative/kernels.metal:691-700).  Here the
+// same stable grouping is a counting sort: per-expert counts, an exclusive
+// scan into row offsets, then a scatter that walks the tokens in order, so a
+// group's rows stay in ascending (token, k) order.  The shared expert is
+// expert index E with one row per token.  Nothing here synchronises with the
+// host: routes never leave the GPU (the reference waits for them on the CPU,
+// qwen4_exp.py:899-902).
+#include "wm_kernels.h"
+
+namespace wm {
+
+namespace {
+
+__device__ __forceinline__ int round_up(int v, int a) { return (v + a - 1) / a * a; }
+
+// Exclusive scan over n values given by value(i); store(i, prefix) for each.
+// Returns the total.  Every thread of the block must call it.
+template <typename F, typename G>
+__device__ int block_exclusive_scan(int n, F value, G store) {
+  __shared__ int warp_sums[32];
+  __shared__ int carry;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = (blockDim.x + 31) >> 5;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < n; base += blockDim.x) {
+    const int i = base + threadIdx.x;
+    const int v = i < n ? value(i) : 0;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      int s = lane < nwarps ? warp_sums[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, s, o);
+        if (lane >= o) s += y;
+      }
+      warp_sums[lane] = s;
+    }
+    __syncthreads();
+    const int prefix = carry + (warp > 0 ? warp_sums[warp - 1] : 0) + x - v;
+    if (i < n) store(i, prefix);
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = prefix + v;
+    __syncthreads();
+  }
+  return carry;
+}
+
+// From per-expert counts in shared memory: offsets, unique list, 128-row tile
+// list and padding rows.  `cnt` holds E + 1 counts (index E = shared expert).
+__device__ void finish_plan(const int* cnt, int* off, int E, int align, Plan p, int max_rows, int max_mtiles,
+                            uint32_t* status) {
+  const int total = block_exclusive_scan(
+      E + 1, [&](int i) { return round_up(cnt[i], align); }, [&](int i, int v) { off[i] = v; });
+  if (threadIdx.x == 0) {
+    off[E + 1] = total;
+    if (total > max_rows) report_status(status, kStatusOverflow, (uint32_t)total);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) {
+    p.counts[i] = cnt[i];
+    p.offsets[i] = off[i];
+  }
+  if (threadIdx.x == 0) p.offsets[E + 1] = total;
+  const int nu = block_exclusive_scan(
+      E + 1, [&](int i) { return cnt[i] > 0 ? 1 : 0; },
+      [&](int i, int v) {
+        if (cnt[i] > 0) p.unique[v] = i;
+      });
+  const int nm = block_exclusive_scan(
+      E + 1, [&](int i) { return (cnt[i] + kTileM - 1) / kTileM; },
+      [&](int i, int v) {
+        const int m_tiles = (cnt[i] + kTileM - 1) / kTileM;
+        for (int m = 0; m < m_tiles && v + m < max_mtiles; ++m) {
+          p.mtiles[2 * (v + m)] = i;
+          p.mtiles[2 * (v + m) + 1] = off[i] + kTileM * m;
+        }
+      });
+  if (threadIdx.x == 0) {
+    *p.n_unique = nu;
+    *p.n_mtiles = min(nm, max_mtiles);
+    if (nm > max_mtiles) report_status(status, kStatusOverflow, (uint32_t)nm);
+  }
+  if (total > max_rows) return;
+  for (int e = threadIdx.x; e <= E; e += blockDim.x)
+    for (int r = off[e] + cnt[e]; r < off[e + 1]; ++r) p.row_token[r] = -1;
+}
+
+// Warp 0 assigns sorted rows to the pairs of tokens [t_begin, t_end), in
+// (token, k) order.  run[e] holds the next free row of expert e.  Repeated
+// experts within a token keep k order (ranked with __match_any_sync).
+__device__ void scatter_pairs(const int32_t* idx, int t_begin, int t_end, int K, int E, int* run, Plan p,
+                              uint32_t* status) {
+  const int lane = threadIdx.x & 31;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int t = t_begin; t < t_end; ++t) {
+    for (int k0 = 0; k0 < K; k0 += 32) {
+      const int k = k0 + lane;
+      int e = -1;
+      if (k < K) {
+        e = idx[(int64_t)t * K + k];
+        if (e < 0 || e >= E) {
+          report_status(status, kStatusBadExpert, (uint32_t)(t * K + k));
+          p.pair_pos[(int64_t)t * K + k] = -1;
+          e = -1;
+        }
+      }
+      const unsigned same = __match_any_sync(0xffffffffu, e);
+      const int rank = __popc(same & lt_mask);
+      const int base = e >= 0 ? run[e] : 0;
+      if (e >= 0) {
+        const int pos = base + rank;
+        p.pair_pos[(int64_t)t * K + k] = pos;
+        p.row_token[pos] = t;
+      }
+      __syncwarp();
+      if (e >= 0 && rank == 0) run[e] = base + __popc(same);
+      __syncwarp();
+    }
+  }
+}
+
+}  // namespace
+
+// Single-block plan for small calls (decode).  1024 threads.
+__global__ void __launch_bounds__(1024) plan_small_kernel(const int32_t* __restrict__ idx, int T, int K, int E,
+                                                          int has_shared, int align, Plan p, int max_rows,
+                                                          int max_mtiles, uint32_t* status) {
+  extern __shared__ int sm[];
+  int* cnt = sm;            // E + 1
+  int* off = cnt + E + 1;   // E + 2
+  int* run = off + E + 2;   // E + 1
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < T * K; i += blockDim.x) {
+    const int e = idx[i];
+    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) cnt[E] = has_shared ? T : 0;
+  __syncthreads();
+  finish_plan(cnt, off, E, align, p, max_rows, max_mtiles, status);
+  __syncthreads();
+  if (off[E + 1] > max_rows) return;
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) run[i] = off[i];
+  if (has_shared)
+    for (int t = threadIdx.x; t < T; t += blockDim.x) p.row_token[off[E] + t] = t;
+  __syncthreads();
+  if (threadIdx.x < 32) scatter_pairs(idx, 0, T, K, E, run, p, status);
+}
+
+// Large calls: per-chunk counts ...
+__global__ void __launch_bounds__(256) plan_count_kernel(const int32_t* __restrict__ idx, int T, int K, int E,
+                                                         int chunk_tokens, Plan p) {
+  extern __shared__ int cnt[];  // E + 1
+  const int c = blockIdx.x;
+  const int t0 = c * chunk_tokens, t1 = min(T, t0 + chunk_tokens);
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  for (int i = t0 * K + threadIdx.x; i < t1 * K; i += blockDim.x) {
+    const int e = idx[i];
+    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) p.hist[(int64_t)c * (E + 1) + i] = cnt[i];
+}
+
+// ... one block turns them into per-chunk start rows and the expert offsets ...
+__global__ void __launch_bounds__(1024) plan_scan_kernel(int T, int E, int chunks, int has_shared, int align, Plan p,
+                                                         int max_rows, int max_mtiles, uint32_t* status) {
+  extern __shared__ int sm[];
+  int* cnt = sm;           // E + 1
+  int* off = cnt + E + 1;  // E + 2
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int running = 0;
+    for (int c = 0; c < chunks; ++c) {
+      const int h = p.hist[(int64_t)c * (E + 1) + e];
+      p.hist[(int64_t)c * (E + 1) + e] = running;
+      running += h;
+    }
+    cnt[e] = running;
+  }
+  if (threadIdx.x == 0) cnt[E] = has_shared ? T : 0;
+  __syncthreads();
+  finish_plan(cnt, off, E, align, p, max_rows, max_mtiles, status);
+}
+
+// ... and each chunk scatters its pairs (and its shared-expert rows).
+__global__ void __launch_bounds__(256) plan_scatter_kernel(const int32_t* __restrict__ idx, int T, int K, int E,
+                                                           int chunk_tokens, int has_shared, Plan p, int max_rows,
+                                                           uint32_t* status) {
+  extern __shared__ int run[];  // E + 1
+  const int c = blockIdx.x;
+  const int t0 = c * chunk_tokens, t1 = min(T, t0 + chunk_tokens);
+  if (p.offsets[E + 1] > max_rows) return;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) run[e] = p.offsets[e] + p.hist[(int64_t)c * (E + 1) + e];
+  if (has_shared) {
+    const int base = p.offsets[E];
+    for (int t = t0 + threadIdx.x; t < t1; t += blockDim.x) p.row_token[base + t] = t;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) scatter_pairs(idx, t0, t1, K, E, run, p, status);
+}
+
+// x_sorted[r] = x[row_token[r]] (zeros for padding rows).  One warp per row.
+__global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __restrict__ x, Plan p, int E, int H,
+                                                          uint16_t* __restrict__ xs) {
+  const int rows = p.offsets[E + 1];
+  const int lane = threadIdx.x & 31;
+  const int pieces = H / 8;
+  for (int r = blockIdx.x * 8 + (threadIdx.x >> 5); r < rows; r += gridDim.x * 8) {
+    const int t = p.row_token[r];
+    uint4* dst = reinterpret_cast<uint4*>(xs + (int64_t)r * H);
+    if (t >= 0) {
+      const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)t * H);
+      for (int i = lane; i < pieces; i += 32) dst[i] = src[i];
+    } else {
+      for (int i = lane; i < pieces; i += 32) dst[i] = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+// out[t] = sum_k w[t, k] * routed[pair_pos[t, k]] + g(t) * routed[offsets[E] + t],
+// an fp32 sum in k order, rounded once to bf16 (qwen4_exp.py:1049-1051,
+// deepseek_v41/moe.py:110-112, QwenNative/kernels.metal:185-194).
+// g(t) = sg[t] (sigmoid gate) or 1.  Eight columns per thread.
+__global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict__ routed, Plan p,
+                                                      const float* __restrict__ w, const float* __restrict__ sg,
+                                                      int shared_kind, int T, int H, int E, int K,
+                                                      uint16_t* __restrict__ out) {
+  const int t = blockIdx.y;
+  const int h0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (h0 >= H) return;
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+  for (int k = 0; k < K; ++k) {
+    const int pos = p.pair_pos[(int64_t)t * K + k];
+    if (pos < 0) continue;
+    const float wk = w[(int64_t)t * K + k];
+    const uint4 v = *reinterpret_cast<const uint4*>(routed + (int64_t)pos * H + h0);
+    float2 f;
+    f = unpack_bf16x2(v.x); acc[0] = fmaf(wk, f.x, acc[0]); acc[1] = fmaf(wk, f.y, acc[1]);
+    f = unpack_bf16x2(v.y); acc[2] = fmaf(wk, f.x, acc[2]); acc[3] = fmaf(wk, f.y, acc[3]);
+    f = unpack_bf16x2(v.z); acc[4] = fmaf(wk, f.x, acc[4]); acc[5] = fmaf(wk, f.y, acc[5]);
+    f = unpack_bf16x2(v.w); acc[6] = fmaf(wk, f.x, acc[6]); acc[7] = fmaf(wk, f.y, acc[7]);
+  }
+  if (shared_kind != WM_SHARED_NONE) {
+    const float g = shared_kind == WM_SHARED_SIGMOID_GATE ? sg[t] : 1.0f;
+    const uint4 v = *reinterpret_cast<const uint4*>(routed + (int64_t)(p.offsets[E] + t) * H + h0);
+    float2 f;
+    f = unpack_bf16x2(v.x); acc[0] = fmaf(g, f.x, acc[0]); acc[1] = fmaf(g, f.y, acc[1]);
+    f = unpack_bf16x2(v.y); acc[2] = fmaf(g, f.x, acc[2]); acc[3] = fmaf(g, f.y, acc[3]);
+    f = unpack_bf16x2(v.z); acc[4] = fmaf(g, f.x, acc[4]); acc[5] = fmaf(g, f.y, acc[5]);
+    f = unpack_bf16x2(v.w); acc[6] = fmaf(g, f.x, acc[6]); acc[7] = fmaf(g, f.y, acc[7]);
+  }
+  uint4 o;
+  o.x = pack_bf16x2(acc[0], acc[1]);
+  o.y = pack_bf16x2(acc[2], acc[3]);
+  o.z = pack_bf16x2(acc[4], acc[5]);
+  o.w = pack_bf16x2(acc[6], acc[7]);
+  *reinterpret_cast<uint4*>(out + (int64_t)t * H + h0) = o;
+}
+
+// routed_out[t, k] = routed[pair_pos[t, k]] (the [T, K, H] layout of
+// StreamingExperts.__call__).  One warp per pair.
+__global__ void __launch_bounds__(256) unpermute_kernel(const uint16_t* __restrict__ routed, Plan p, int TK, int H,
+                                                        uint16_t* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  for (int i = blockIdx.x * 8 + (threadIdx.x >> 5); i < TK; i += gridDim.x * 8) {
+    const int pos = p.pair_pos[i];
+    uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)i * H);
+    if (pos < 0) {
+      for (int j = lane; j < H / 8; j += 32) dst[j] = make_uint4(0, 0, 0, 0);
+      continue;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(routed + (int64_t)pos * H);
+    for (int j = lane; j < H / 8; j += 32) dst[j] = src[j];
+  }
+}
+
+// ------------------------------------------------------------------ launchers
+
+void launch_plan(const int32_t* idx, int T, int K, int E, bool has_shared, int align, const Plan& p, int max_rows,
+                 int max_mtiles, int max_chunks, uint32_t* status, cudaStream_t stream, int* launches) {
+  if (T * K <= 8192) {
+    const size_t smem = size_t(3 * (E + 2)) * sizeof(int);
+    plan_small_kernel<<<1, 1024, smem, stream>>>(idx, T, K, E, has_shared ? 1 : 0, align, p, max_rows, max_mtiles,
+                                                  status);
+    *launches += 1;
+    return;
+  }
+  int chunk_tokens = 64;
+  while ((T + chunk_tokens - 1) / chunk_tokens > max_chunks) chunk_tokens *= 2;
+  const int chunks = (T + chunk_tokens - 1) / chunk_tokens;
+  const size_t smem1 = size_t(E + 1) * sizeof(int);
+  plan_count_kernel<<<chunks, 256, smem1, stream>>>(idx, T, K, E, chunk_tokens, p);
+  const size_t smem2 = size_t(2 * (E + 2)) * sizeof(int);
+  plan_scan_kernel<<<1, 1024, smem2, stream>>>(T, E, chunks, has_shared ? 1 : 0, align, p, max_rows, max_mtiles,
+                                               status);
+  plan_scatter_kernel<<<chunks, 256, smem1, stream>>>(idx, T, K, E, chunk_tokens, has_shared ? 1 : 0, p, max_rows,
+                                                      status);
+  *launches += 3;
+}
+
+void launch_gather_rows(const uint16_t* x, const Plan& p, int E, int H, uint16_t* xs, int num_sms,
+                        cudaStream_t stream) {
+  gather_rows_kernel<<<num_sms * 8, 256, 0, stream>>>(x, p, E, H, xs);
+}
+
+void launch_combine(const uint16_t* routed, const Plan& p, const float* w, const float* sg, int shared_kind, int T,
+                    int H, int E, int K, uint16_t* out, cudaStream_t stream) {
+  dim3 grid((H / 8 + 255) / 256, T);
+  combine_kernel<<<grid, 256, 0, stream>>>(routed, p, w, sg, shared_kind, T, H, E, K, out);
+}
+
+void launch_unpermute(const uint16_t* routed, const Plan& p, int TK, int H, uint16_t* out, int num_sms,
+                      cudaStream_t stream) {
+  unpermute_kernel<<<num_sms * 4, 256, 0, stream>>>(routed, p, TK, H, out);
+}
+
+}  // namespace wm

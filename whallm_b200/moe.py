@@ -1,0 +1,264 @@
+"""PyTorch front end of the MoE expert-FFN path.
+
+``Engine`` owns one library handle per device and enqueues every call on the
+current PyTorch CUDA stream.  The classes below it keep the call shapes of the
+reference's Python layer, so a caller switches by swapping the module:
+
+  StreamingExperts.__call__(value [1, T, H], indices [1, T, K]) -> [1, T, K, H]
+      runtime/deepseek_v4_ssd/qwen4_exp.py:797-904
+  SparseMoE.route(value) / __call__(value, routes=None) -> [1, T, H]
+      qwen4_exp.py:998-1051
+  StreamingSwitchGLU.__call__(x, indices) -> [..., K, H]      model.py:318-501
+  streaming_moe(x) (gate -> shared -> routed -> reduce)        model.py:526-546
+  MoE (DeepSeek V4.1: clamped SwiGLU, sqrt-softplus gate)      deepseek_v41/moe.py:96-112
+
+Weights are the blob bytes as [E, ...] tensor views (layout.QwenBatchedExperts
+and friends), exactly as ExpertCache.current_batched returns them.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+from . import lib
+from .layout import FP8BatchedExperts, Projection, QwenBatchedExperts, projections
+
+__all__ = [
+    "Engine", "LayerWeights", "RouterWeights", "SharedExpert",
+    "StreamingExperts", "SparseMoE", "StreamingSwitchGLU", "MoE",
+]
+
+
+@dataclass
+class SharedExpert:
+    """The shared expert: one blob in the layer's layout, and its gate kind."""
+    w13: Projection
+    w2: Projection
+    gate: int = lib.SHARED_ONE            # SHARED_SIGMOID_GATE (Qwen) or SHARED_ONE (DeepSeek)
+    gate_weight: torch.Tensor | None = None  # bf16 [H] for the sigmoid gate
+
+
+@dataclass
+class RouterWeights:
+    weight: torch.Tensor                   # bf16 [E, H]
+    kind: int = lib.ROUTER_SOFTMAX
+    bias: torch.Tensor | None = None       # fp32 [E]
+    n_groups: int = 1
+    topk_groups: int = 1
+    route_scale: float = 1.0
+
+
+@dataclass
+class LayerWeights:
+    """Everything of one MoE layer the expert kernels read."""
+    layout: int
+    H: int
+    I: int
+    E: int
+    w13: Projection
+    w2: Projection
+    shared: SharedExpert | None = None
+    router: RouterWeights | None = None
+    swiglu_limit: float = 0.0
+    keep: list = field(default_factory=list)  # tensors the views point into
+
+    @staticmethod
+    def from_batched(batched, H: int, I: int, **kw) -> "LayerWeights":
+        layout, w13, w2 = projections(batched)
+        return LayerWeights(layout, H, I, w13.weight.shape[0], w13, w2, keep=[batched], **kw)
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _check_bf16(name: str, t: torch.Tensor, shape: tuple[int, ...] | None = None) -> None:
+    if t.dtype != torch.bfloat16 or not t.is_cuda or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous bf16 CUDA tensor")
+    if shape is not None and tuple(t.shape) != shape:
+        raise ValueError(f"{name} has shape {tuple(t.shape)}, expected {shape}")
+
+
+class Engine:
+    """A library handle sized for the largest call it will see."""
+
+    def __init__(self, device: int | torch.device = 0, *, max_tokens: int, hidden: int, inter: int, experts: int,
+                 topk: int, gemv_max_tokens: int = 0):
+        dev = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        if dev.type != "cuda":
+            raise ValueError("the expert kernels run on CUDA devices only")
+        self.device = dev
+        with torch.cuda.device(dev):
+            self.ctx = lib.Context(dev.index or 0, max_tokens=max_tokens, max_hidden=hidden, max_inter=inter,
+                                   max_experts=experts, max_topk=topk, gemv_max_tokens=gemv_max_tokens)
+
+    # ---------------------------------------------------------------- argument block
+    def _args(self, layer: LayerWeights, x: torch.Tensor, K: int) -> lib.MoeArgs:
+        T = x.shape[0]
+        _check_bf16("x", x, (T, layer.H))
+        a = lib.MoeArgs()
+        a.T, a.H, a.I, a.E, a.K = T, layer.H, layer.I, layer.E, K
+        a.layout = layer.layout
+        a.w13 = layer.w13.matrix()
+        a.w2 = layer.w2.matrix()
+        a.x = x.data_ptr()
+        a.swiglu_limit = layer.swiglu_limit
+        a.route_scale = 1.0
+        return a
+
+    def _with_shared(self, a: lib.MoeArgs, layer: LayerWeights) -> None:
+        if layer.shared is None:
+            a.shared_gate = lib.SHARED_NONE
+            return
+        a.shared_w13 = layer.shared.w13.matrix()
+        a.shared_w2 = layer.shared.w2.matrix()
+        a.shared_gate = layer.shared.gate
+        a.shared_gate_weight = _ptr(layer.shared.gate_weight)
+
+    def _with_router(self, a: lib.MoeArgs, r: RouterWeights) -> None:
+        a.router = r.kind
+        a.router_weight = r.weight.data_ptr()
+        a.router_bias = _ptr(r.bias)
+        a.n_groups, a.topk_groups, a.route_scale = r.n_groups, r.topk_groups, r.route_scale
+
+    # ---------------------------------------------------------------- calls
+    def route(self, layer: LayerWeights, x: torch.Tensor, K: int, with_logits: bool = False):
+        """(weights fp32 [T, K], indices int32 [T, K][, logits fp32 [T, E]])."""
+        if layer.router is None:
+            raise ValueError("the layer has no router weights")
+        a = self._args(layer, x, K)
+        self._with_router(a, layer.router)
+        T = x.shape[0]
+        idx = torch.empty((T, K), dtype=torch.int32, device=x.device)
+        w = torch.empty((T, K), dtype=torch.float32, device=x.device)
+        logits = torch.empty((T, layer.E), dtype=torch.float32, device=x.device) if with_logits else None
+        self.ctx.route(a, _ptr(logits), idx.data_ptr(), w.data_ptr(), _stream())
+        return (w, idx, logits) if with_logits else (w, idx)
+
+    def expert_pairs(self, layer: LayerWeights, x: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
+        """routed bf16 [T, K, H]: row (t, k) = expert indices[t, k] applied to x[t]."""
+        T = x.shape[0]
+        idx = indices.reshape(T, -1).to(torch.int32).contiguous()
+        K = idx.shape[1]
+        a = self._args(layer, x, K)
+        a.routes_idx = idx.data_ptr()
+        out = torch.empty((T, K, layer.H), dtype=torch.bfloat16, device=x.device)
+        self.ctx.expert_pairs(a, out.data_ptr(), _stream())
+        return out
+
+    def forward(self, layer: LayerWeights, x: torch.Tensor, K: int, routes: tuple | None = None,
+                out: torch.Tensor | None = None, return_routes: bool = False):
+        """Combined output bf16 [T, H].  `routes` = (weights fp32 [T, K], indices
+        int32 [T, K]) skips the router."""
+        T = x.shape[0]
+        a = self._args(layer, x, K)
+        self._with_shared(a, layer)
+        keep = []
+        if routes is None:
+            self._with_router(a, layer.router)
+            if return_routes:
+                ri = torch.empty((T, K), dtype=torch.int32, device=x.device)
+                rw = torch.empty((T, K), dtype=torch.float32, device=x.device)
+                a.out_idx, a.out_w = ri.data_ptr(), rw.data_ptr()
+        else:
+            rw, ri = routes
+            rw = rw.reshape(T, K).to(torch.float32).contiguous()
+            ri = ri.reshape(T, K).to(torch.int32).contiguous()
+            keep += [rw, ri]
+            a.routes_idx, a.routes_w = ri.data_ptr(), rw.data_ptr()
+        if out is None:
+            out = torch.empty((T, layer.H), dtype=torch.bfloat16, device=x.device)
+        _check_bf16("out", out, (T, layer.H))
+        a.out = out.data_ptr()
+        self.ctx.moe_forward(a, _stream())
+        if return_routes:
+            return out, (rw, ri)
+        return out
+
+    def dequant(self, fmt: int, weight: torch.Tensor, scale: torch.Tensor, rows: int, cols: int,
+                convention: int = lib.CONV_MLX) -> torch.Tensor:
+        out = torch.empty((rows, cols), dtype=torch.bfloat16, device=weight.device)
+        self.ctx.dequant(fmt, weight.data_ptr(), scale.data_ptr(), rows, cols, convention, out.data_ptr(), _stream())
+        return out
+
+    def sync(self) -> None:
+        """Wait for the current stream and raise any error a kernel recorded."""
+        self.ctx.sync(_stream())
+
+
+# -------------------------------------------------------------------- reference-shaped wrappers
+
+class StreamingExperts:
+    """qwen4_exp.StreamingExperts: routed rows of the batched layer, no combine."""
+
+    def __init__(self, layer: int, cache, engine: Engine):
+        self.layer, self.cache, self.engine = layer, cache, engine
+
+    def __call__(self, value: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
+        batched = self.cache.current_batched(self.layer)
+        H = value.shape[-1]
+        lw = LayerWeights.from_batched(batched, H, _inter(batched, H))
+        flat = value.reshape(-1, H).contiguous()
+        out = self.engine.expert_pairs(lw, flat, indices)
+        return out.reshape(*indices.shape, H)
+
+
+class StreamingSwitchGLU(StreamingExperts):
+    """model._StreamingSwitchGLU over the fused w13 = [w3; w1] layout; the
+    activation is silu(gate) * up, clamped when `swiglu_limit` > 0."""
+
+    def __init__(self, layer: int, cache, engine: Engine, swiglu_limit: float = 0.0):
+        super().__init__(layer, cache, engine)
+        self.swiglu_limit = swiglu_limit
+
+    def __call__(self, x: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
+        batched = self.cache.current_batched(self.layer)
+        H = x.shape[-1]
+        lw = LayerWeights.from_batched(batched, H, _inter(batched, H), swiglu_limit=self.swiglu_limit)
+        out = self.engine.expert_pairs(lw, x.reshape(-1, H).contiguous(), indices)
+        return out.reshape(*indices.shape, H)
+
+
+class SparseMoE:
+    """qwen4_exp.SparseMoE: softmax top-k router (renormalised), sigmoid-gated
+    shared expert and the weighted combine, in one library call."""
+
+    def __init__(self, engine: Engine, layer: LayerWeights, top_k: int):
+        self.engine, self.layer, self.top_k = engine, layer, top_k
+
+    def route(self, value: torch.Tensor):
+        """(scores fp32 [..., K] renormalised over the kept experts, indices int32 [..., K])."""
+        H = value.shape[-1]
+        w, idx = self.engine.route(self.layer, value.reshape(-1, H).contiguous(), self.top_k)
+        return w.reshape(*value.shape[:-1], self.top_k), idx.reshape(*value.shape[:-1], self.top_k)
+
+    def __call__(self, value: torch.Tensor, routes=None) -> torch.Tensor:
+        H = value.shape[-1]
+        flat = value.reshape(-1, H).contiguous()
+        r = None if routes is None else tuple(t.reshape(flat.shape[0], self.top_k) for t in routes)
+        out = self.engine.forward(self.layer, flat, self.top_k, routes=r)
+        return out.reshape(value.shape)
+
+
+class MoE(SparseMoE):
+    """deepseek_v41.moe.MoE: sqrt-softplus gate with selection bias, weights
+    / (sum + 1e-20) * route_scale, clamped SwiGLU, ungated shared expert."""
+
+
+def streaming_moe(engine: Engine, layer: LayerWeights, x: torch.Tensor, top_k: int) -> torch.Tensor:
+    """model._streaming_moe: gate -> shared -> routed -> route_reduce + shared."""
+    H = x.shape[-1]
+    return engine.forward(layer, x.reshape(-1, H).contiguous(), top_k).reshape(x.shape)
+
+
+def _inter(batched, H: int) -> int:
+    if isinstance(batched, QwenBatchedExperts):
+        return batched.gate_up.shape[1] // 2
+    if isinstance(batched, FP8BatchedExperts):
+        return batched.w13.shape[1] // 2
+    return batched.w13.shape[1] // 2
