@@ -1,0 +1,138 @@
+"""The tcgen05 grouped-GEMM (prefill) path vs the CPU oracle (needs a B200).
+
+Same tolerance as the decode path: max|y - y_ref| / max|y_ref| <= 1e-2 on bf16
+outputs.  Full-size layers are checked on sampled tokens (the oracle runs only
+the experts those tokens reach) plus whole-output properties.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from oracle import adapter
+from whallm_b200 import lib, synth
+from whallm_b200.layout import Projection
+from whallm_b200.moe import Engine, LayerWeights, RouterWeights, SharedExpert
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+DEV = "cuda"
+
+
+def rel(y_bits, ref_bits):
+    return oracle.max_rel_error(oracle.bf16_to_f32(y_bits), oracle.bf16_to_f32(ref_bits))
+
+
+def small_layer(layout, E, H, I, seed, gate=lib.SHARED_NONE, limit=0.0):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    proj = synth.fp8_projection if layout == lib.LAYOUT_W13_FP8_B128 else synth.mxfp4_projection
+    w13, s13 = proj(E, 2 * I, H, g, DEV)
+    w2, s2 = proj(E, H, I, g, DEV)
+    shared = None
+    if gate != lib.SHARED_NONE:
+        a, b = proj(1, 2 * I, H, g, DEV)
+        c, d = proj(1, H, I, g, DEV)
+        gw = (torch.randn((H,), generator=g, device=DEV) / H ** 0.5).to(torch.bfloat16)
+        shared = SharedExpert(Projection.stacked(a, b), Projection.stacked(c, d), gate,
+                              gw if gate == lib.SHARED_SIGMOID_GATE else None)
+    wr = (torch.randn((E, H), generator=g, device=DEV) / H ** 0.5).to(torch.bfloat16)
+    return LayerWeights(layout, H, I, E, Projection.stacked(w13, s13), Projection.stacked(w2, s2), shared=shared,
+                        router=RouterWeights(wr, lib.ROUTER_SOFTMAX), swiglu_limit=limit)
+
+
+@pytest.fixture(scope="module")
+def gemm_engine():
+    eng = Engine(0, max_tokens=1024, hidden=1024, inter=512, experts=16, topk=8, gemv_max_tokens=-1)
+    yield eng
+    eng.ctx.close()
+
+
+@pytest.fixture(scope="module")
+def gemv_engine():
+    eng = Engine(0, max_tokens=1024, hidden=1024, inter=512, experts=16, topk=8, gemv_max_tokens=100000)
+    yield eng
+    eng.ctx.close()
+
+
+def test_gemm_single_tile(gemm_engine):
+    """One expert, one 128-row tile: the smallest grouped GEMM."""
+    layer = small_layer(lib.LAYOUT_QWEN_GATE_UP_MXFP4, 1, 256, 128, seed=1)
+    x = synth.activations(100, 256, torch.Generator(device=DEV).manual_seed(2), DEV)
+    idx = torch.zeros((100, 1), dtype=torch.int32, device=DEV)
+    out = gemm_engine.expert_pairs(layer, x, idx)
+    gemm_engine.sync()
+    assert gemm_engine.ctx.counters().gemm_calls >= 1
+    ref = adapter.from_layer(layer).pairs(adapter.bits(x), idx.cpu().numpy())
+    assert rel(adapter.bits(out), ref) <= TOL
+
+
+@pytest.mark.parametrize("layout,limit", [(lib.LAYOUT_QWEN_GATE_UP_MXFP4, 0.0), (lib.LAYOUT_DS_W13_MXFP4, 10.0),
+                                          (lib.LAYOUT_W13_FP8_B128, 0.0)])
+@pytest.mark.parametrize("T", [1, 65, 300])
+def test_gemm_expert_pairs_match_oracle(gemm_engine, layout, limit, T):
+    E, H, I, K = 16, 512, 256, 4
+    layer = small_layer(layout, E, H, I, seed=10 + layout, limit=limit)
+    g = torch.Generator(device=DEV).manual_seed(20 + T)
+    x = synth.activations(T, H, g, DEV)
+    idx = torch.stack([torch.randperm(E, generator=g, device=DEV)[:K] for _ in range(T)]).to(torch.int32)
+    out = gemm_engine.expert_pairs(layer, x, idx)
+    gemm_engine.sync()
+    ref = adapter.from_layer(layer).pairs(adapter.bits(x), idx.cpu().numpy())
+    assert rel(adapter.bits(out), ref) <= TOL
+
+
+@pytest.mark.parametrize("layout,gate", [(lib.LAYOUT_QWEN_GATE_UP_MXFP4, lib.SHARED_SIGMOID_GATE),
+                                         (lib.LAYOUT_W13_FP8_B128, lib.SHARED_ONE)])
+def test_gemm_forward_matches_gemv_and_oracle(gemm_engine, gemv_engine, layout, gate):
+    E, H, I, K, T = 16, 1024, 512, 8, 257
+    layer = small_layer(layout, E, H, I, seed=30 + layout, gate=gate)
+    x = synth.activations(T, H, torch.Generator(device=DEV).manual_seed(31), DEV)
+    out_a, (w, idx) = gemm_engine.forward(layer, x, K, return_routes=True)
+    out_b = gemv_engine.forward(layer, x, K, routes=(w, idx))
+    gemm_engine.sync()
+    gemv_engine.sync()
+    assert rel(adapter.bits(out_a), adapter.bits(out_b)) <= TOL
+    ref = adapter.from_layer(layer).forward(adapter.bits(x), idx.cpu().numpy(), w.cpu().numpy())
+    assert rel(adapter.bits(out_a), ref) <= TOL
+
+
+def _check_sampled(layer, x, out, w, idx, tokens):
+    """Oracle on `tokens` only, over the experts they reach (remapped)."""
+    ii = idx.cpu().numpy()[tokens]
+    ww = w.cpu().numpy()[tokens]
+    experts = sorted(set(ii.reshape(-1).tolist()))
+    remap = {e: i for i, e in enumerate(experts)}
+    sub_idx = np.vectorize(remap.get)(ii).astype(np.int32)
+    ref = adapter.from_layer(layer, experts=experts).forward(adapter.bits(x[tokens]), sub_idx, ww)
+    got = adapter.bits(out[tokens])
+    return rel(got, ref)
+
+
+def test_config2_prefill_full_size():
+    wl = synth.config(2, device=DEV)
+    eng = Engine(0, max_tokens=16384, hidden=2048, inter=512, experts=512, topk=10)
+    out, (w, idx) = eng.forward(wl.layer, wl.x, wl.K, return_routes=True)
+    eng.sync()
+    assert eng.ctx.counters().gemm_calls == 1
+    assert torch.isfinite(out.float()).all()
+    counts = torch.bincount(idx.reshape(-1).long(), minlength=512)
+    assert counts.sum().item() == 16384 * 10 and counts.max().item() > 20 * counts.float().median().item()
+    tokens = np.random.default_rng(0).choice(16384, 16, replace=False)
+    assert _check_sampled(wl.layer, wl.x, out, w, idx, tokens) <= TOL
+    eng.ctx.close()
+
+
+def test_config3_fp8_full_size():
+    wl = synth.config(3, device=DEV)
+    eng = Engine(0, max_tokens=8192, hidden=7168, inter=2048, experts=256, topk=8)
+    out, (w, idx) = eng.forward(wl.layer, wl.x, wl.K, return_routes=True)
+    eng.sync()
+    assert torch.isfinite(out.float()).all()
+    # group-limited routing: every token's experts lie in at most 4 of the 8 groups
+    groups = (idx.long() // 32)
+    per_token = [torch.unique(r).numel() for r in groups[:256]]
+    assert max(per_token) <= 4
+    tokens = np.random.default_rng(1).choice(8192, 3, replace=False)
+    assert _check_sampled(wl.layer, wl.x, out, w, idx, tokens) <= TOL
+    eng.ctx.close()

@@ -86,6 +86,7 @@ int validate_experts(wm_ctx* ctx, const wm_moe_args* a, bool need_router) {
   if (a->H % 64 || a->I % 64) return fail(ctx, "H (%d) and I (%d) must be multiples of 64", a->H, a->I);
   if (a->layout < WM_LAYOUT_QWEN_GATE_UP_MXFP4 || a->layout > WM_LAYOUT_W13_FP8_B128)
     return fail(ctx, "unknown expert layout %d", a->layout);
+  if (a->T == 0) return WM_OK;  // nothing is read or written
   if (a->x == nullptr || !aligned(a->x, 16)) return fail(ctx, "x must be a 16-byte aligned device pointer");
   const wm_matrix* ms[2] = {&a->w13, &a->w2};
   for (const wm_matrix* m : ms) {
@@ -162,6 +163,26 @@ int run_router(wm_ctx* ctx, const wm_moe_args* a, float* logits, int32_t* idx, f
   return check_launch(ctx, "router");
 }
 
+// TMA descriptor of a sorted-row buffer: bf16 [max_rows, kdim], 64 x 128
+// boxes with the 128-byte swizzle the MMA operand layout expects.
+bool encode_rows(wm_ctx* ctx, CUtensorMap* map, const void* base, int kdim) {
+  if (ctx->encode_tiled == nullptr) return false;
+  cuuint64_t dims[2] = {cuuint64_t(kdim), cuuint64_t(ctx->max_rows)};
+  cuuint64_t strides[1] = {cuuint64_t(kdim) * 2};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Whether a call of T tokens takes the tcgen05 grouped GEMM (else the GEMV kernels).
+bool use_gemm(const wm_ctx* ctx, const wm_moe_args* a) {
+  const int g = ctx->opt.gemv_max_tokens;
+  return (g < 0 || a->T > g) && wm::gemm_shape_ok(a->H, a->I) && ctx->encode_tiled != nullptr;
+}
+
 // Runs the experts of a plan already built on `s` (rows in ctx->routed).
 int run_experts(wm_ctx* ctx, const wm_moe_args* a, bool has_shared, bool gemm, cudaStream_t s) {
   const wm::ExpertWeights wts = weights_of(a, has_shared);
@@ -183,7 +204,36 @@ int run_experts(wm_ctx* ctx, const wm_moe_args* a, bool has_shared, bool gemm, c
     ctx->counters.gemv_calls += 1;
     return check_launch(ctx, "expert GEMV");
   }
-  return fail(ctx, "the grouped GEMM path is not available in this build");
+  // Grouped GEMM: gather the sorted rows, then gate/up (+SwiGLU) and down on tcgen05.
+  wm::prof_begin(&ctx->prof, wm::kProfGather, s);
+  wm::launch_gather_rows(static_cast<const uint16_t*>(a->x), ctx->plan, a->E, a->H, ctx->xs, ctx->num_sms, s);
+  wm::prof_end(&ctx->prof, wm::kProfGather, s);
+  CUtensorMap map_x, map_act;
+  if (!encode_rows(ctx, &map_x, ctx->xs, a->H) || !encode_rows(ctx, &map_act, ctx->act, a->I))
+    return fail(ctx, "cuTensorMapEncodeTiled failed for the sorted-row buffers");
+  wm::GemmArgs g{};
+  g.plan = ctx->plan;
+  g.wts = wts;
+  g.I = a->I;
+  g.gate_first = gate_first;
+  g.limit = a->swiglu_limit;
+  g.fmt = fmt_of(a->layout);
+  g.status = ctx->status;
+  g.out = ctx->act;
+  g.Kdim = a->H;
+  g.N = 2 * a->I;
+  wm::prof_begin(&ctx->prof, wm::kProfGemmGateUp, s);
+  wm::launch_gemm(g, 0, &map_x, ctx->num_sms, s);
+  wm::prof_end(&ctx->prof, wm::kProfGemmGateUp, s);
+  g.out = ctx->routed;
+  g.Kdim = a->I;
+  g.N = a->H;
+  wm::prof_begin(&ctx->prof, wm::kProfGemmDown, s);
+  wm::launch_gemm(g, 1, &map_act, ctx->num_sms, s);
+  wm::prof_end(&ctx->prof, wm::kProfGemmDown, s);
+  ctx->counters.launches += 3;
+  ctx->counters.gemm_calls += 1;
+  return check_launch(ctx, "expert GEMM");
 }
 
 }  // namespace
@@ -285,6 +335,8 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
     return nullptr;
   }
   wm::gemv_init_attributes(int(gemv_smem));
+  wm::gemm_init_attributes();
+  wm::router_init_attributes(int(H));
   cudaDriverEntryPointQueryResult q{};
   void* fn = nullptr;
   if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
@@ -386,12 +438,12 @@ WM_EXPORT int wm_expert_pairs(wm_ctx* ctx, const wm_moe_args* a, void* routed, v
   b.shared_gate = WM_SHARED_NONE;
   b.router_weight = nullptr;
   if (int rc = validate_experts(ctx, &b, false)) return rc;
+  if (b.T == 0) return WM_OK;
   if (b.routes_idx == nullptr) return fail(ctx, "wm_expert_pairs needs routes_idx");
   if (routed == nullptr || !aligned(routed, 16)) return fail(ctx, "routed must be a 16-byte aligned device pointer");
-  if (b.T == 0) return WM_OK;
   DeviceGuard guard(ctx->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const bool gemm = b.T > ctx->opt.gemv_max_tokens && ctx->opt.gemv_max_tokens >= 0 && false;
+  const bool gemm = use_gemm(ctx, &b);
   int launches = 0;
   wm::prof_begin(&ctx->prof, wm::kProfPlan, s);
   wm::launch_plan(b.routes_idx, b.T, b.K, b.E, false, gemm ? wm::kTileM : 1, ctx->plan, ctx->max_rows,
@@ -409,12 +461,12 @@ WM_EXPORT int wm_expert_pairs(wm_ctx* ctx, const wm_moe_args* a, void* routed, v
 WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* a, void* stream) {
   if (ctx == nullptr) return WM_ERROR;
   if (int rc = validate_experts(ctx, a, true)) return rc;
-  if (a->out == nullptr || !aligned(a->out, 16)) return fail(ctx, "out must be a 16-byte aligned device pointer");
   if (a->T == 0) return WM_OK;
+  if (a->out == nullptr || !aligned(a->out, 16)) return fail(ctx, "out must be a 16-byte aligned device pointer");
   DeviceGuard guard(ctx->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool has_shared = a->shared_gate != WM_SHARED_NONE;
-  const bool gemm = false;
+  const bool gemm = use_gemm(ctx, a);
   const int32_t* idx;
   const float* w;
   if (a->router_weight != nullptr) {

@@ -31,6 +31,8 @@ void launch_dequant(int format, const void* weight, const void* scale, int64_t r
                     uint16_t* out, uint32_t* status, cudaStream_t stream);
 
 // ---- router (wm_route.cu)
+size_t router_smem_bytes(int H);
+void router_init_attributes(int max_hidden);
 void launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* sg_w, int T, int H, int E,
                           float* logits, float* sg, cudaStream_t stream);
 void launch_router_topk(const float* logits, const float* bias, int T, int E, int K, int kind, int n_groups,
@@ -65,7 +67,6 @@ void launch_gemv(const GemvArgs& a, int fmt, int max_unique, cudaStream_t stream
 struct GemmArgs {
   Plan plan;
   ExpertWeights wts;
-  const void* tmap_a;   // device copy of the A operand's CUtensorMap (bf16 [rows, Kdim], 128B swizzle)
   uint16_t* out;        // gate/up: act [rows, I]; down: routed [rows, H]
   int Kdim;             // H (gate/up) or I (down)
   int N;                // 2I (gate/up) or H (down)
@@ -77,6 +78,8 @@ struct GemmArgs {
 };
 // `kind`: 0 = gate/up + SwiGLU, 1 = down.  tmap_a points to a CUtensorMap
 // passed by value to the kernel.
+void gemm_init_attributes();
+bool gemm_shape_ok(int H, int I);
 void launch_gemm(const GemmArgs& a, int kind, const void* tmap_host, int num_sms, cudaStream_t stream);
 
 }  // namespace wm

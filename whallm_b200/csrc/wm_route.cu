@@ -212,6 +212,13 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
   }
 }
 
+size_t router_smem_bytes(int H) { return size_t(8) * H * 2; }
+
+void router_init_attributes(int max_hidden) {
+  cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       int(router_smem_bytes(max_hidden)));
+}
+
 void launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* sg_w, int T, int H, int E,
                           float* logits, float* sg, cudaStream_t stream) {
   const int rows = E + (sg_w != nullptr ? 1 : 0);
