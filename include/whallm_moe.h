@@ -186,6 +186,20 @@ WM_EXPORT int wm_expert_pairs(wm_ctx* ctx, const wm_moe_args* args, void* routed
    MoE.__call__, deepseek_v41/moe.py:105-112). */
 WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* args, void* stream);
 
+/* The decode MoE block (router if router_weight is set, sort, expert GEMVs,
+   shared expert, combine -- the same kernels as wm_moe_forward's decode
+   path) for callers that cannot allocate device memory: there is no handle,
+   and all scratch lives in one static device array of 8 MiB that the CUDA
+   runtime reserves on every GPU that loads this library until the process
+   exits.  A call whose scratch would exceed it (roughly: (T*K + T) * (H + I)
+   * 2 bytes plus routing arrays) fails with status 1 and a message in
+   error[0 .. error_size).  The first call on a device looks up the array's
+   device address; make it before any stream capture.  Calls share the array:
+   calls that overlap on the GPU race, so serialise them.  Expert ids are not
+   range-checked on the host.  This entry point has no counterpart in the
+   reference. */
+WM_EXPORT int wm_moe_forward_noalloc(const wm_moe_args* args, void* stream, char* error, size_t error_size);
+
 /* Per-kernel-group timing with CUDA events recorded on the calls' streams
    (the counterpart of the native engines' gpu_seconds counters,
    Native/QwenNative/capi.h:28-35).  Off by default; while on, calls must not

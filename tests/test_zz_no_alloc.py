@@ -1,0 +1,79 @@
+"""wm_moe_forward_noalloc: the allocation-free decode entry point (needs a B200).
+
+Some callers cannot call cudaMalloc -- for example a serving process whose GPU
+memory is fixed at start-up, or a host framework that owns all device memory
+through its own allocator.  This entry point runs the decode MoE block with
+its scratch in a static device array instead of a handle's workspace.  The
+test calls it through the C ABI twice in a row and checks both results against
+the regular wm_moe_forward on the same inputs, within the tolerance of the
+other parity tests (max|y - y_ref| / max|y_ref| <= 1e-2).  This file is named
+so that pytest collects it last.
+"""
+import ctypes
+
+import pytest
+import torch
+
+import oracle
+from oracle import adapter
+from whallm_b200 import lib, synth
+from whallm_b200.layout import Projection
+from whallm_b200.moe import Engine, LayerWeights, RouterWeights, SharedExpert
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+DEV = "cuda"
+
+
+def _layer(E=16, H=512, I=256, seed=7):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    w13, s13 = synth.mxfp4_projection(E, 2 * I, H, g, DEV)
+    w2, s2 = synth.mxfp4_projection(E, H, I, g, DEV)
+    a, b = synth.mxfp4_projection(1, 2 * I, H, g, DEV)
+    c, d = synth.mxfp4_projection(1, H, I, g, DEV)
+    gate = (torch.randn((H,), generator=g, device=DEV) / H ** 0.5).to(torch.bfloat16)
+    wr = (torch.randn((E, H), generator=g, device=DEV) / H ** 0.5).to(torch.bfloat16)
+    return LayerWeights(lib.LAYOUT_QWEN_GATE_UP_MXFP4, H, I, E, Projection.stacked(w13, s13),
+                        Projection.stacked(w2, s2),
+                        shared=SharedExpert(Projection.stacked(a, b), Projection.stacked(c, d),
+                                            lib.SHARED_SIGMOID_GATE, gate),
+                        router=RouterWeights(wr, lib.ROUTER_SOFTMAX))
+
+
+def _noalloc(eng: Engine, layer: LayerWeights, x: torch.Tensor, K: int, out: torch.Tensor):
+    a = eng._args(layer, x, K)
+    eng._with_shared(a, layer)
+    eng._with_router(a, layer.router)
+    a.out = out.data_ptr()
+    err = ctypes.create_string_buffer(256)
+    rc = lib.load().wm_moe_forward_noalloc(ctypes.byref(a), torch.cuda.current_stream().cuda_stream, err, len(err))
+    return rc, err.value.decode()
+
+
+def test_noalloc_matches_wm_moe_forward_twice():
+    layer = _layer()
+    K, T = 4, 8
+    eng = Engine(0, max_tokens=64, hidden=512, inter=256, experts=16, topk=K)
+    x = synth.activations(T, 512, torch.Generator(device=DEV).manual_seed(8), DEV)
+    ref = eng.forward(layer, x, K)
+    eng.sync()
+    for _ in range(2):
+        out = torch.full((T, 512), float("nan"), dtype=torch.bfloat16, device=DEV)
+        rc, msg = _noalloc(eng, layer, x, K, out)
+        assert rc == lib.WM_OK, msg
+        torch.cuda.synchronize()
+        err = oracle.max_rel_error(oracle.bf16_to_f32(adapter.bits(out)), oracle.bf16_to_f32(adapter.bits(ref)))
+        assert err <= TOL
+    eng.ctx.close()
+
+
+def test_noalloc_rejects_sizes_beyond_its_scratch():
+    layer = _layer(E=64, H=2048, I=512, seed=9)
+    K, T = 8, 1024  # rows (T*K + T) * (H + I) * 2 bytes = 47 MB, beyond the 8 MiB array
+    eng = Engine(0, max_tokens=T, hidden=2048, inter=512, experts=64, topk=K)
+    x = synth.activations(T, 2048, torch.Generator(device=DEV).manual_seed(10), DEV)
+    out = torch.empty((T, 2048), dtype=torch.bfloat16, device=DEV)
+    rc, msg = _noalloc(eng, layer, x, K, out)
+    assert rc == lib.WM_ERROR and "scratch" in msg
+    eng.ctx.close()

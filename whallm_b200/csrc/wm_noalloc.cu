@@ -1,0 +1,198 @@
+// wm_moe_forward_noalloc: the decode MoE block with no device allocation.
+//
+// Every other entry point works through a handle whose workspace wm_create
+// obtains with cudaMalloc.  Some callers cannot do that: a serving loop whose
+// GPU memory is fixed when the process starts (a cudaMalloc mid-run also
+// waits for the whole device), or a host framework that owns all device
+// memory through its own allocator and forbids other allocations.  For them
+// this entry point runs the same kernels as wm_moe_forward's decode path
+// (router, sort, expert GEMVs, shared expert, combine) with all scratch in
+// one file-scope device array of kScratchBytes, reserved by the CUDA runtime
+// on every GPU that loads the library, for as long as the process lives.
+//
+// * The first call on a device sets that device up (looks up the array's
+//   device address with cudaGetSymbolAddress); make that first call before
+//   any stream capture.
+// * All calls share the one array and it keeps the last call's contents:
+//   calls that may overlap on the GPU (on different streams, or from several
+//   host threads) race with each other.  Serialise them.
+// * Sizes whose scratch would exceed the array are rejected with an error.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <mutex>
+
+#include "wm_kernels.h"
+
+namespace wm {
+namespace {
+
+constexpr size_t kScratchBytes = size_t(8) << 20;  // 8 MiB per GPU
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) uint8_t g_scratch[kScratchBytes];
+
+std::mutex g_setup_mutex;
+void* g_scratch_ptr[kMaxDevices] = {};
+
+int report(char* error, size_t n, const char* msg) {
+  if (error != nullptr && n > 0) snprintf(error, n, "%s", msg);
+  return WM_ERROR;
+}
+
+size_t up256(size_t v) { return (v + 255) / 256 * 256; }
+
+}  // namespace
+}  // namespace wm
+
+extern "C" WM_EXPORT int wm_moe_forward_noalloc(const wm_moe_args* a, void* stream, char* error, size_t error_size) {
+  using namespace wm;
+  char msg[256];
+  if (a == nullptr) return report(error, error_size, "args is NULL");
+  if (a->T < 0 || a->H <= 0 || a->I <= 0 || a->E <= 0 || a->K <= 0 || a->K > a->E)
+    return report(error, error_size, "invalid shape (T >= 0, H, I, E, K > 0, K <= E)");
+  if (a->E > 1024 || a->K > 64) return report(error, error_size, "at most 1024 experts and top-64 routing");
+  if (a->H % 64 || a->I % 64) return report(error, error_size, "H and I must be multiples of 64");
+  if (a->layout < WM_LAYOUT_QWEN_GATE_UP_MXFP4 || a->layout > WM_LAYOUT_W13_FP8_B128)
+    return report(error, error_size, "unknown expert layout");
+  if (a->layout == WM_LAYOUT_W13_FP8_B128 && (a->H % 128 || a->I % 128))
+    return report(error, error_size, "FP8 128x128 experts need H and I multiples of 128");
+  if (a->T == 0) return WM_OK;
+  auto al = [](const void* p, size_t n) { return p != nullptr && reinterpret_cast<uintptr_t>(p) % n == 0; };
+  if (!al(a->x, 16) || !al(a->out, 16)) return report(error, error_size, "x and out must be 16-byte aligned device pointers");
+  if (!al(a->w13.weight, 16) || !al(a->w2.weight, 16) || a->w13.weight_stride % 16 || a->w2.weight_stride % 16 ||
+      a->w13.scale == nullptr || a->w2.scale == nullptr)
+    return report(error, error_size, "expert weights must be 16-byte aligned regions with scales");
+  const bool has_shared = a->shared_gate != WM_SHARED_NONE;
+  if (has_shared && (!al(a->shared_w13.weight, 16) || !al(a->shared_w2.weight, 16) || a->shared_w13.scale == nullptr ||
+                     a->shared_w2.scale == nullptr ||
+                     (a->shared_gate == WM_SHARED_SIGMOID_GATE && !al(a->shared_gate_weight, 16))))
+    return report(error, error_size, "shared expert weights, scales (and sigmoid gate weight) must be given, aligned");
+  const bool route_here = a->router_weight != nullptr;
+  if (!route_here && (a->routes_idx == nullptr || a->routes_w == nullptr))
+    return report(error, error_size, "give router_weight or routes_idx and routes_w");
+  if (route_here && a->router == WM_ROUTER_SIGMOID_GROUPED &&
+      (a->n_groups < 1 || a->n_groups > 32 || a->E % a->n_groups || a->topk_groups < 1 ||
+       a->topk_groups > a->n_groups || a->K > a->topk_groups * (a->E / a->n_groups)))
+    return report(error, error_size, "invalid group-limited routing shape");
+  const int64_t T = a->T, K = a->K, E = a->E, H = a->H, I = a->I;
+  if (T * K > 8192) return report(error, error_size, "at most 8192 (token, expert) pairs per call");
+
+  // scratch layout (GEMV path: no row padding)
+  const int64_t rows = T * K + T;
+  const int max_mtiles = int(rows / kTileM + E + 2);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = up256(off + bytes);
+    return at;
+  };
+  const size_t o_counts = take((E + 1) * 4), o_offsets = take((E + 2) * 4), o_pair = take(T * K * 4),
+               o_rowtok = take(rows * 4), o_unique = take((E + 1) * 4), o_nu = take(4),
+               o_mt = take(size_t(max_mtiles) * 8), o_nm = take(4), o_act = take(rows * I * 2),
+               o_routed = take(rows * H * 2), o_logits = take(T * E * 4), o_idx = take(T * K * 4),
+               o_w = take(T * K * 4), o_sg = take(T * 4), o_status = take(16);
+  if (off > kScratchBytes) {
+    snprintf(msg, sizeof(msg), "this call needs %.2f MiB of scratch; the allocation-free entry point has %.0f MiB",
+             off / 1048576.0, kScratchBytes / 1048576.0);
+    return report(error, error_size, msg);
+  }
+  const size_t gemv_smem = gemv_smem_bytes(int(H), int(I)), router_smem = router_smem_bytes(int(H));
+
+  // once per device: the array's device address
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return report(error, error_size, "no current CUDA device");
+  cudaDeviceProp prop{};
+  {
+    std::lock_guard<std::mutex> lock(g_setup_mutex);
+    if (g_scratch_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);
+      if (e != cudaSuccess || p == nullptr) {
+        snprintf(msg, sizeof(msg), "cudaGetSymbolAddress of the scratch array failed: %s", cudaGetErrorString(e));
+        return report(error, error_size, msg);
+      }
+      g_scratch_ptr[dev] = p;
+    }
+  }
+  if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess || prop.major != 10)
+    return report(error, error_size, "needs an sm_100 (B200-class) GPU");
+  if (gemv_smem > size_t(prop.sharedMemPerBlockOptin) || router_smem > size_t(prop.sharedMemPerBlockOptin))
+    return report(error, error_size, "H is too large for the decode kernels' shared-memory staging");
+  gemv_init_attributes(int(gemv_smem));
+  router_init_attributes(int(H));
+
+  uint8_t* base = static_cast<uint8_t*>(g_scratch_ptr[dev]);
+  Plan p{};
+  p.counts = reinterpret_cast<int32_t*>(base + o_counts);
+  p.offsets = reinterpret_cast<int32_t*>(base + o_offsets);
+  p.pair_pos = reinterpret_cast<int32_t*>(base + o_pair);
+  p.row_token = reinterpret_cast<int32_t*>(base + o_rowtok);
+  p.unique = reinterpret_cast<int32_t*>(base + o_unique);
+  p.n_unique = reinterpret_cast<int32_t*>(base + o_nu);
+  p.mtiles = reinterpret_cast<int32_t*>(base + o_mt);
+  p.n_mtiles = reinterpret_cast<int32_t*>(base + o_nm);
+  p.hist = nullptr;
+  uint16_t* act = reinterpret_cast<uint16_t*>(base + o_act);
+  uint16_t* routed = reinterpret_cast<uint16_t*>(base + o_routed);
+  float* logits = reinterpret_cast<float*>(base + o_logits);
+  float* sg = reinterpret_cast<float*>(base + o_sg);
+  uint32_t* status = reinterpret_cast<uint32_t*>(base + o_status);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+  // the status words start at zero; everything else is written before it is read
+  cudaMemsetAsync(status, 0, 16, s);
+  const int32_t* idx = a->routes_idx;
+  const float* w = a->routes_w;
+  const uint16_t* x = static_cast<const uint16_t*>(a->x);
+  const uint16_t* sg_w =
+      a->shared_gate == WM_SHARED_SIGMOID_GATE ? static_cast<const uint16_t*>(a->shared_gate_weight) : nullptr;
+  if (route_here) {
+    int32_t* di = a->out_idx ? a->out_idx : reinterpret_cast<int32_t*>(base + o_idx);
+    float* dw = a->out_w ? a->out_w : reinterpret_cast<float*>(base + o_w);
+    launch_router_logits(x, static_cast<const uint16_t*>(a->router_weight), sg_w, int(T), int(H), int(E), logits, sg, s);
+    launch_router_topk(logits, a->router_bias, int(T), int(E), int(K), a->router, a->n_groups, a->topk_groups,
+                       a->route_scale, di, dw, s);
+    idx = di;
+    w = dw;
+  } else if (sg_w != nullptr) {
+    launch_router_logits(x, nullptr, sg_w, int(T), int(H), 0, nullptr, sg, s);
+  }
+  int launches = 0;
+  launch_plan(idx, int(T), int(K), int(E), has_shared, 1, p, int(rows), max_mtiles, 1, status, s, &launches);
+  GemvArgs g{};
+  g.plan = p;
+  g.wts.w13 = static_cast<const uint8_t*>(a->w13.weight);
+  g.wts.w13_stride = a->w13.weight_stride;
+  g.wts.s13 = static_cast<const uint8_t*>(a->w13.scale);
+  g.wts.s13_stride = a->w13.scale_stride;
+  g.wts.w2 = static_cast<const uint8_t*>(a->w2.weight);
+  g.wts.w2_stride = a->w2.weight_stride;
+  g.wts.s2 = static_cast<const uint8_t*>(a->w2.scale);
+  g.wts.s2_stride = a->w2.scale_stride;
+  if (has_shared) {
+    g.wts.sh_w13 = static_cast<const uint8_t*>(a->shared_w13.weight);
+    g.wts.sh_s13 = static_cast<const uint8_t*>(a->shared_w13.scale);
+    g.wts.sh_w2 = static_cast<const uint8_t*>(a->shared_w2.weight);
+    g.wts.sh_s2 = static_cast<const uint8_t*>(a->shared_w2.scale);
+  }
+  g.wts.E = int(E);
+  g.x = x;
+  g.act = act;
+  g.routed = routed;
+  g.H = int(H);
+  g.I = int(I);
+  g.gate_first = a->layout == WM_LAYOUT_QWEN_GATE_UP_MXFP4 ? 1 : 0;
+  g.limit = a->swiglu_limit;
+  const int max_unique = int(std::min<int64_t>(E, T * K)) + (has_shared ? 1 : 0);
+  launch_gemv(g, a->layout == WM_LAYOUT_W13_FP8_B128 ? kFmtFp8B128 : kFmtMxfp4, max_unique, s, nullptr);
+  launch_combine(routed, p, w, sg, a->shared_gate, int(T), int(H), int(E), int(K), static_cast<uint16_t*>(a->out), s);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    snprintf(msg, sizeof(msg), "CUDA launch failed: %s", cudaGetErrorString(e));
+    return report(error, error_size, msg);
+  }
+  return WM_OK;
+}

@@ -23,6 +23,7 @@ EXPORTS = (
     "wm_create", "wm_destroy", "wm_error", "wm_sync", "wm_counters_get",
     "wm_dequant", "wm_route", "wm_expert_pairs", "wm_moe_forward",
     "wm_profile_enable", "wm_profile_read", "wm_profile_reset",
+    "wm_moe_forward_noalloc",
 )
 
 _P = ctypes.c_void_p
@@ -101,6 +102,8 @@ def load() -> ctypes.CDLL:
     L.wm_profile_read.restype = _I32
     L.wm_profile_reset.argtypes = [_P]
     L.wm_profile_reset.restype = None
+    L.wm_moe_forward_noalloc.argtypes = [ctypes.POINTER(MoeArgs), _P, ctypes.c_char_p, ctypes.c_size_t]
+    L.wm_moe_forward_noalloc.restype = ctypes.c_int
     for name in ("wm_sync", "wm_dequant", "wm_route", "wm_expert_pairs", "wm_moe_forward"):
         getattr(L, name).restype = ctypes.c_int
     _lib = L
