@@ -142,6 +142,7 @@ typedef struct {
   int64_t calls_forward, calls_pairs, calls_route, calls_dequant;
   int64_t launches;            /* kernels enqueued by this handle */
   int64_t gemv_calls, gemm_calls;
+  int64_t decode_calls;        /* calls that took the tcgen05 decode kernels */
 } wm_counters;
 
 typedef struct {

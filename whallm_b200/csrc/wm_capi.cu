@@ -31,6 +31,10 @@ struct wm_ctx {
   float* w = nullptr;
   float* sg = nullptr;
   uint32_t* status = nullptr;  // [4]
+  uint16_t* act16 = nullptr;   // [rows, I] f16 activation rows (decode path)
+  float* rowscale = nullptr;   // [rows] prescale of the f16 x rows (decode path)
+  float* actscale = nullptr;   // [rows] prescale of the f16 act rows (decode path)
+  uint32_t* rowmax = nullptr;  // [rows] per-row |act| maxima (decode path)
   int max_rows = 0, max_mtiles = 0, max_chunks = 0;
   PFN_cuTensorMapEncodeTiled_v12000 encode_tiled = nullptr;
   wm::Profiler prof;
@@ -156,25 +160,32 @@ int run_router(wm_ctx* ctx, const wm_moe_args* a, float* logits, int32_t* idx, f
   wm::prof_begin(&ctx->prof, wm::kProfRouter, s);
   wm::launch_router_logits(static_cast<const uint16_t*>(a->x), static_cast<const uint16_t*>(a->router_weight), sg_w,
                            a->T, a->H, a->E, logits, ctx->sg, s);
+  wm::prof_end(&ctx->prof, wm::kProfRouter, s);
+  wm::prof_begin(&ctx->prof, wm::kProfTopk, s);
   wm::launch_router_topk(logits, a->router_bias, a->T, a->E, a->K, a->router, a->n_groups, a->topk_groups,
                          a->route_scale, idx, w, s);
-  wm::prof_end(&ctx->prof, wm::kProfRouter, s);
+  wm::prof_end(&ctx->prof, wm::kProfTopk, s);
   ctx->counters.launches += 2;
   return check_launch(ctx, "router");
 }
 
 // TMA descriptor of a sorted-row buffer: bf16 [max_rows, kdim], 64 x 128
 // boxes with the 128-byte swizzle the MMA operand layout expects.
-bool encode_rows(wm_ctx* ctx, CUtensorMap* map, const void* base, int kdim) {
+bool encode_rows_box(wm_ctx* ctx, CUtensorMap* map, const void* base, int kdim, CUtensorMapDataType dtype,
+                     int box_rows) {
   if (ctx->encode_tiled == nullptr) return false;
   cuuint64_t dims[2] = {cuuint64_t(kdim), cuuint64_t(ctx->max_rows)};
   cuuint64_t strides[1] = {cuuint64_t(kdim) * 2};
-  cuuint32_t box[2] = {64, 128};
+  cuuint32_t box[2] = {64, cuuint32_t(box_rows)};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
-                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  CUresult r = ctx->encode_tiled(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+bool encode_rows(wm_ctx* ctx, CUtensorMap* map, const void* base, int kdim) {
+  return encode_rows_box(ctx, map, base, kdim, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 128);
 }
 
 // Whether a call of T tokens takes the tcgen05 grouped GEMM (else the GEMV kernels).
@@ -183,11 +194,97 @@ bool use_gemm(const wm_ctx* ctx, const wm_moe_args* a) {
   return (g < 0 || a->T > g) && wm::gemm_shape_ok(a->H, a->I) && ctx->encode_tiled != nullptr;
 }
 
+enum Path { kPathGemv = 0, kPathDecode = 1, kPathGemm = 2 };
+
+// Which expert kernels a call takes: the tcgen05 grouped GEMM for long calls,
+// the tcgen05 decode kernel (weights as the M operand) for short MXFP4 calls
+// whose scale rows allow 16-byte loads, else the CUDA-core GEMV.
+Path expert_path(const wm_ctx* ctx, const wm_moe_args* a, bool has_shared) {
+  if (use_gemm(ctx, a)) return kPathGemm;
+  if (a->layout == WM_LAYOUT_W13_FP8_B128 || ctx->encode_tiled == nullptr || !wm::decode_shape_ok(a->H, a->I))
+    return kPathGemv;
+  const wm_matrix* ms[4] = {&a->w13, &a->w2, &a->shared_w13, &a->shared_w2};
+  for (int i = 0; i < (has_shared ? 4 : 2); ++i)
+    if (!aligned(ms[i]->scale, 16) || (i < 2 && ms[i]->scale_stride % 16)) return kPathGemv;
+  return kPathDecode;
+}
+
+// TMA descriptor over one projection's packed weights of `experts` experts:
+// uint8 [experts][rows][row_bytes], boxes of 32 bytes x box_rows x 1.
+bool encode_weights(wm_ctx* ctx, CUtensorMap* map, const void* base, int64_t row_bytes, int64_t rows,
+                    int64_t experts, int64_t expert_stride, int box_bytes, int box_rows) {
+  if (ctx->encode_tiled == nullptr) return false;
+  cuuint64_t dims[3] = {cuuint64_t(row_bytes), cuuint64_t(rows), cuuint64_t(experts)};
+  cuuint64_t strides[2] = {cuuint64_t(row_bytes), cuuint64_t(experts > 1 ? expert_stride : row_bytes * rows)};
+  cuuint32_t box[3] = {cuuint32_t(box_bytes), cuuint32_t(box_rows), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// The tcgen05 decode path: per-token prescale, gate/up (+SwiGLU), down.
+int run_decode(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts, bool has_shared, cudaStream_t s) {
+  const int H = a->H, I = a->I;
+  // packed weights (32-byte boxes along K) and E8M0 scales (one box per row tile)
+  CUtensorMap w13, w13s, w2, w2s, s13, s13s, s2, s2s;
+  bool ok = encode_weights(ctx, &w13, a->w13.weight, H / 2, 2 * I, a->E, a->w13.weight_stride, 32, 64) &&
+            encode_weights(ctx, &w2, a->w2.weight, I / 2, H, a->E, a->w2.weight_stride, 32, 128) &&
+            encode_weights(ctx, &s13, a->w13.scale, H / 32, 2 * I, a->E, a->w13.scale_stride, H / 32, 64) &&
+            encode_weights(ctx, &s2, a->w2.scale, I / 32, H, a->E, a->w2.scale_stride, I / 32, 128);
+  if (has_shared)
+    ok = ok && encode_weights(ctx, &w13s, a->shared_w13.weight, H / 2, 2 * I, 1, 0, 32, 64) &&
+         encode_weights(ctx, &w2s, a->shared_w2.weight, I / 2, H, 1, 0, 32, 128) &&
+         encode_weights(ctx, &s13s, a->shared_w13.scale, H / 32, 2 * I, 1, 0, H / 32, 64) &&
+         encode_weights(ctx, &s2s, a->shared_w2.scale, I / 32, H, 1, 0, I / 32, 128);
+  if (!ok) return fail(ctx, "cuTensorMapEncodeTiled failed for the expert weights");
+  // f16 activation rows (the B operand) and their TMA descriptors
+  uint16_t* xh = ctx->xs;      // [max_rows, H]
+  uint16_t* acth = ctx->act16; // [max_rows, I]
+  CUtensorMap bx, bact;
+  if (!encode_rows_box(ctx, &bx, xh, H, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 16) ||
+      !encode_rows_box(ctx, &bact, acth, I, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 16))
+    return fail(ctx, "cuTensorMapEncodeTiled failed for the activation rows");
+  wm::Plan plan = ctx->plan;
+  plan.rowmax = ctx->rowmax;
+  wm::DecodeArgs d{};
+  d.plan = plan;
+  d.wts = wts;
+  d.act = ctx->act;
+  d.routed = ctx->routed;
+  d.H = H;
+  d.I = I;
+  d.gate_first = a->layout == WM_LAYOUT_QWEN_GATE_UP_MXFP4 ? 1 : 0;
+  d.limit = a->swiglu_limit;
+  d.status = ctx->status;
+  wm::prof_begin(&ctx->prof, wm::kProfGather, s);
+  wm::launch_gather_f16(static_cast<const uint16_t*>(a->x), plan, a->E, H, xh, ctx->rowscale, ctx->num_sms, s);
+  wm::prof_end(&ctx->prof, wm::kProfGather, s);
+  d.bscale = ctx->rowscale;
+  wm::prof_begin(&ctx->prof, wm::kProfGemvGateUp, s);
+  const void* maps0[5] = {&w13, has_shared ? &w13s : &w13, &s13, has_shared ? &s13s : &s13, &bx};
+  wm::launch_decode(d, 0, maps0, ctx->num_sms, s);
+  wm::prof_end(&ctx->prof, wm::kProfGemvGateUp, s);
+  wm::prof_begin(&ctx->prof, wm::kProfActF16, s);
+  wm::launch_act_f16(ctx->act, plan, a->E, I, acth, ctx->actscale, ctx->num_sms, s);
+  wm::prof_end(&ctx->prof, wm::kProfActF16, s);
+  d.bscale = ctx->actscale;
+  wm::prof_begin(&ctx->prof, wm::kProfGemvDown, s);
+  const void* maps1[5] = {&w2, has_shared ? &w2s : &w2, &s2, has_shared ? &s2s : &s2, &bact};
+  wm::launch_decode(d, 1, maps1, ctx->num_sms, s);
+  wm::prof_end(&ctx->prof, wm::kProfGemvDown, s);
+  ctx->counters.launches += 4;
+  ctx->counters.decode_calls += 1;
+  return check_launch(ctx, "expert decode");
+}
+
 // Runs the experts of a plan already built on `s` (rows in ctx->routed).
-int run_experts(wm_ctx* ctx, const wm_moe_args* a, bool has_shared, bool gemm, cudaStream_t s) {
+int run_experts(wm_ctx* ctx, const wm_moe_args* a, bool has_shared, Path path, cudaStream_t s) {
   const wm::ExpertWeights wts = weights_of(a, has_shared);
   const int gate_first = a->layout == WM_LAYOUT_QWEN_GATE_UP_MXFP4 ? 1 : 0;
-  if (!gemm) {
+  if (path == kPathDecode) return run_decode(ctx, a, wts, has_shared, s);
+  if (path == kPathGemv) {
     wm::GemvArgs g{};
     g.plan = ctx->plan;
     g.wts = wts;
@@ -284,7 +381,7 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
   const int64_t T = o.max_tokens, K = o.max_topk, E = o.max_experts, H = o.max_hidden, I = o.max_inter;
   const int64_t rows = T * K + T + int64_t(wm::kTileM) * (E + 1);
   ctx->max_rows = int(rows);
-  ctx->max_mtiles = int(rows / wm::kTileM + E + 2);
+  ctx->max_mtiles = int(std::max(rows / wm::kTileM + E + 2, (T * K + T) / 16 + E + 2));
   ctx->max_chunks = 1024;
   // workspace layout
   size_t off = 0;
@@ -298,7 +395,9 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
                o_mtiles = take(size_t(ctx->max_mtiles) * 8), o_nm = take(4),
                o_hist = take(size_t(ctx->max_chunks) * (E + 1) * 4), o_xs = take(rows * H * 2),
                o_act = take(rows * I * 2), o_routed = take(rows * H * 2), o_logits = take(T * E * 4),
-               o_idx = take(T * K * 4), o_w = take(T * K * 4), o_sg = take(T * 4), o_status = take(16);
+               o_idx = take(T * K * 4), o_w = take(T * K * 4), o_sg = take(T * 4), o_status = take(16),
+               o_act16 = take(rows * I * 2), o_rowscale = take(rows * 4), o_actscale = take(rows * 4),
+               o_rowmax = take(rows * 4);
   ctx->ws_bytes = off;
   if (cudaMalloc(&ctx->ws, ctx->ws_bytes) != cudaSuccess) {
     cudaGetLastError();
@@ -326,6 +425,10 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
   ctx->w = reinterpret_cast<float*>(base + o_w);
   ctx->sg = reinterpret_cast<float*>(base + o_sg);
   ctx->status = reinterpret_cast<uint32_t*>(base + o_status);
+  ctx->act16 = reinterpret_cast<uint16_t*>(base + o_act16);
+  ctx->rowscale = reinterpret_cast<float*>(base + o_rowscale);
+  ctx->actscale = reinterpret_cast<float*>(base + o_actscale);
+  ctx->rowmax = reinterpret_cast<uint32_t*>(base + o_rowmax);
   cudaMemset(ctx->status, 0, 16);
   const size_t gemv_smem = wm::gemv_smem_bytes(int(H), int(I));
   if (gemv_smem > size_t(prop.sharedMemPerBlockOptin)) {
@@ -336,6 +439,7 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
   }
   wm::gemv_init_attributes(int(gemv_smem));
   wm::gemm_init_attributes();
+  wm::decode_init_attributes();
   wm::router_init_attributes(int(H));
   cudaDriverEntryPointQueryResult q{};
   void* fn = nullptr;
@@ -443,15 +547,17 @@ WM_EXPORT int wm_expert_pairs(wm_ctx* ctx, const wm_moe_args* a, void* routed, v
   if (routed == nullptr || !aligned(routed, 16)) return fail(ctx, "routed must be a 16-byte aligned device pointer");
   DeviceGuard guard(ctx->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const bool gemm = use_gemm(ctx, &b);
+  const Path path = expert_path(ctx, &b, false);
+  wm::Plan plan = ctx->plan;
+  if (path == kPathDecode) plan.rowmax = ctx->rowmax;
   int launches = 0;
   wm::prof_begin(&ctx->prof, wm::kProfPlan, s);
-  wm::launch_plan(b.routes_idx, b.T, b.K, b.E, false, gemm ? wm::kTileM : 1, ctx->plan, ctx->max_rows,
+  wm::launch_plan(b.routes_idx, b.T, b.K, b.E, false, path == kPathGemm ? wm::kTileM : 1, plan, ctx->max_rows,
                   ctx->max_mtiles, ctx->max_chunks, ctx->status, s, &launches);
   wm::prof_end(&ctx->prof, wm::kProfPlan, s);
   ctx->counters.launches += launches;
   if (int rc = check_launch(ctx, "plan")) return rc;
-  if (int rc = run_experts(ctx, &b, false, gemm, s)) return rc;
+  if (int rc = run_experts(ctx, &b, false, path, s)) return rc;
   wm::launch_unpermute(ctx->routed, ctx->plan, b.T * b.K, b.H, static_cast<uint16_t*>(routed), ctx->num_sms, s);
   ctx->counters.launches += 1;
   ctx->counters.calls_pairs += 1;
@@ -466,7 +572,9 @@ WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* a, void* stream) {
   DeviceGuard guard(ctx->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool has_shared = a->shared_gate != WM_SHARED_NONE;
-  const bool gemm = use_gemm(ctx, a);
+  const Path path = expert_path(ctx, a, has_shared);
+  wm::Plan plan = ctx->plan;
+  if (path == kPathDecode) plan.rowmax = ctx->rowmax;
   const int32_t* idx;
   const float* w;
   if (a->router_weight != nullptr) {
@@ -487,12 +595,12 @@ WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* a, void* stream) {
   }
   int launches = 0;
   wm::prof_begin(&ctx->prof, wm::kProfPlan, s);
-  wm::launch_plan(idx, a->T, a->K, a->E, has_shared, gemm ? wm::kTileM : 1, ctx->plan, ctx->max_rows,
+  wm::launch_plan(idx, a->T, a->K, a->E, has_shared, path == kPathGemm ? wm::kTileM : 1, plan, ctx->max_rows,
                   ctx->max_mtiles, ctx->max_chunks, ctx->status, s, &launches);
   wm::prof_end(&ctx->prof, wm::kProfPlan, s);
   ctx->counters.launches += launches;
   if (int rc = check_launch(ctx, "plan")) return rc;
-  if (int rc = run_experts(ctx, a, has_shared, gemm, s)) return rc;
+  if (int rc = run_experts(ctx, a, has_shared, path, s)) return rc;
   wm::prof_begin(&ctx->prof, wm::kProfCombine, s);
   wm::launch_combine(ctx->routed, ctx->plan, w, ctx->sg, a->shared_gate, a->T, a->H, a->E, a->K,
                      static_cast<uint16_t*>(a->out), s);

@@ -13,7 +13,9 @@ namespace wm {
 // ---- optional per-kernel timing with CUDA events (wm_profile_*)
 enum ProfSlot : int {
   kProfRouter = 0,
+  kProfTopk,
   kProfPlan,
+  kProfActF16,
   kProfGather,
   kProfGemvGateUp,
   kProfGemvDown,
@@ -62,6 +64,32 @@ struct GemvArgs {
 void gemv_init_attributes(int max_smem);
 size_t gemv_smem_bytes(int H, int I);
 void launch_gemv(const GemvArgs& a, int fmt, int max_unique, cudaStream_t stream, Profiler* prof);
+
+// ---- decode on tcgen05, weights as the M operand (wm_decode_sm100.cu)
+struct DecodeArgs {
+  Plan plan;            // 16-row tiles, no padding, rowmax set
+  ExpertWeights wts;
+  const float* bscale;  // [rows] power-of-two prescale of the f16 activation rows
+  uint16_t* act;        // [rows, I] bf16 (gate/up output)
+  uint16_t* routed;     // [rows, H] bf16 (down output)
+  int H, I;
+  int gate_first;
+  float limit;
+  uint32_t* status;
+};
+void decode_init_attributes();
+bool decode_shape_ok(int H, int I);
+// f16 sorted activation rows with their per-row prescale (x rows for gate/up,
+// act rows for down).
+void launch_gather_f16(const uint16_t* x, const Plan& p, int E, int H, uint16_t* out, float* scale, int num_sms,
+                       cudaStream_t stream);
+void launch_act_f16(const uint16_t* act, const Plan& p, int E, int I, uint16_t* out, float* scale, int num_sms,
+                    cudaStream_t stream);
+// maps[0..4]: CUtensorMaps of the routed experts' packed weights, the shared
+// expert's packed weights (3-D uint8 [E][rows][row bytes], boxes 32 x 64 for
+// gate/up, 32 x 128 for down), the routed and shared E8M0 scales (boxes
+// K/32 x 64 or 128), and the f16 activation rows (2-D, 64 x 16, 128B swizzle).
+void launch_decode(const DecodeArgs& a, int kind, const void* const* maps, int num_sms, cudaStream_t stream);
 
 // ---- prefill grouped GEMM on tcgen05 (wm_gemm_sm100.cu)
 struct GemmArgs {

@@ -57,8 +57,10 @@ __device__ int block_exclusive_scan(int n, F value, G store) {
   return carry;
 }
 
-// From per-expert counts in shared memory: offsets, unique list, 128-row tile
+// From per-expert counts in shared memory: offsets, unique list, row-tile
 // list and padding rows.  `cnt` holds E + 1 counts (index E = shared expert).
+// Tiles are `align` rows (the GEMM's 128-row tiles) when the groups are
+// padded, else 16 rows (the decode kernel's token chunks).
 __device__ void finish_plan(const int* cnt, int* off, int E, int align, Plan p, int max_rows, int max_mtiles,
                             uint32_t* status) {
   const int total = block_exclusive_scan(
@@ -78,13 +80,14 @@ __device__ void finish_plan(const int* cnt, int* off, int E, int align, Plan p, 
       [&](int i, int v) {
         if (cnt[i] > 0) p.unique[v] = i;
       });
+  const int tile = align > 16 ? align : 16;
   const int nm = block_exclusive_scan(
-      E + 1, [&](int i) { return (cnt[i] + kTileM - 1) / kTileM; },
+      E + 1, [&](int i) { return (cnt[i] + tile - 1) / tile; },
       [&](int i, int v) {
-        const int m_tiles = (cnt[i] + kTileM - 1) / kTileM;
+        const int m_tiles = (cnt[i] + tile - 1) / tile;
         for (int m = 0; m < m_tiles && v + m < max_mtiles; ++m) {
           p.mtiles[2 * (v + m)] = i;
-          p.mtiles[2 * (v + m) + 1] = off[i] + kTileM * m;
+          p.mtiles[2 * (v + m) + 1] = off[i] + tile * m;
         }
       });
   if (threadIdx.x == 0) {
@@ -95,6 +98,8 @@ __device__ void finish_plan(const int* cnt, int* off, int E, int align, Plan p, 
   if (total > max_rows) return;
   for (int e = threadIdx.x; e <= E; e += blockDim.x)
     for (int r = off[e] + cnt[e]; r < off[e + 1]; ++r) p.row_token[r] = -1;
+  if (p.rowmax != nullptr)
+    for (int r = threadIdx.x; r < total; r += blockDim.x) p.rowmax[r] = 0u;
 }
 
 // Warp 0 assigns sorted rows to the pairs of tokens [t_begin, t_end), in
@@ -156,6 +161,39 @@ __global__ void __launch_bounds__(1024) plan_small_kernel(const int32_t* __restr
   for (int i = threadIdx.x; i <= E; i += blockDim.x) run[i] = off[i];
   if (has_shared)
     for (int t = threadIdx.x; t < T; t += blockDim.x) p.row_token[off[E] + t] = t;
+  if (T <= 64) {
+    // Every pair at once: a pair's rank within its expert is the number of
+    // earlier tokens that chose the expert (a 64-bit token mask per expert),
+    // valid when no token names an expert twice.
+    unsigned long long* mask =
+        reinterpret_cast<unsigned long long*>((reinterpret_cast<uintptr_t>(run + E + 2) + 7) & ~uintptr_t(7));
+    __shared__ int repeated;
+    if (threadIdx.x == 0) repeated = 0;
+    for (int i = threadIdx.x; i <= E; i += blockDim.x) mask[i] = 0ull;
+    __syncthreads();
+    for (int i = threadIdx.x; i < T * K; i += blockDim.x) {
+      const int e = idx[i], t = i / K;
+      if (e < 0 || e >= E) continue;
+      atomicOr(&mask[e], 1ull << t);
+      for (int j = t * K; j < i; ++j)
+        if (idx[j] == e) repeated = 1;
+    }
+    __syncthreads();
+    if (!repeated) {
+      for (int i = threadIdx.x; i < T * K; i += blockDim.x) {
+        const int e = idx[i], t = i / K;
+        if (e < 0 || e >= E) {
+          report_status(status, kStatusBadExpert, (uint32_t)i);
+          p.pair_pos[i] = -1;
+          continue;
+        }
+        const int pos = off[e] + __popcll(mask[e] & ((1ull << t) - 1ull));
+        p.pair_pos[i] = pos;
+        p.row_token[pos] = t;
+      }
+      return;
+    }
+  }
   __syncthreads();
   if (threadIdx.x < 32) scatter_pairs(idx, 0, T, K, E, run, p, status);
 }
@@ -245,16 +283,29 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict
   float acc[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
-  for (int k = 0; k < K; ++k) {
-    const int pos = p.pair_pos[(int64_t)t * K + k];
-    if (pos < 0) continue;
-    const float wk = w[(int64_t)t * K + k];
-    const uint4 v = *reinterpret_cast<const uint4*>(routed + (int64_t)pos * H + h0);
-    float2 f;
-    f = unpack_bf16x2(v.x); acc[0] = fmaf(wk, f.x, acc[0]); acc[1] = fmaf(wk, f.y, acc[1]);
-    f = unpack_bf16x2(v.y); acc[2] = fmaf(wk, f.x, acc[2]); acc[3] = fmaf(wk, f.y, acc[3]);
-    f = unpack_bf16x2(v.z); acc[4] = fmaf(wk, f.x, acc[4]); acc[5] = fmaf(wk, f.y, acc[5]);
-    f = unpack_bf16x2(v.w); acc[6] = fmaf(wk, f.x, acc[6]); acc[7] = fmaf(wk, f.y, acc[7]);
+  // eight pairs' loads in flight at a time; the sum keeps k order
+  for (int k0 = 0; k0 < K; k0 += 8) {
+    int pos[8];
+    float wk[8];
+    uint4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int k = k0 + j;
+      pos[j] = k < K ? p.pair_pos[(int64_t)t * K + k] : -1;
+      wk[j] = k < K ? w[(int64_t)t * K + k] : 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      v[j] = pos[j] >= 0 ? *reinterpret_cast<const uint4*>(routed + (int64_t)pos[j] * H + h0) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (pos[j] < 0) continue;
+      float2 f;
+      f = unpack_bf16x2(v[j].x); acc[0] = fmaf(wk[j], f.x, acc[0]); acc[1] = fmaf(wk[j], f.y, acc[1]);
+      f = unpack_bf16x2(v[j].y); acc[2] = fmaf(wk[j], f.x, acc[2]); acc[3] = fmaf(wk[j], f.y, acc[3]);
+      f = unpack_bf16x2(v[j].z); acc[4] = fmaf(wk[j], f.x, acc[4]); acc[5] = fmaf(wk[j], f.y, acc[5]);
+      f = unpack_bf16x2(v[j].w); acc[6] = fmaf(wk[j], f.x, acc[6]); acc[7] = fmaf(wk[j], f.y, acc[7]);
+    }
   }
   if (shared_kind != WM_SHARED_NONE) {
     const float g = shared_kind == WM_SHARED_SIGMOID_GATE ? sg[t] : 1.0f;
@@ -295,7 +346,7 @@ __global__ void __launch_bounds__(256) unpermute_kernel(const uint16_t* __restri
 void launch_plan(const int32_t* idx, int T, int K, int E, bool has_shared, int align, const Plan& p, int max_rows,
                  int max_mtiles, int max_chunks, uint32_t* status, cudaStream_t stream, int* launches) {
   if (T * K <= 8192) {
-    const size_t smem = size_t(3 * (E + 2)) * sizeof(int);
+    const size_t smem = size_t(3 * (E + 2)) * sizeof(int) + size_t(E + 2) * sizeof(unsigned long long);
     plan_small_kernel<<<1, 1024, smem, stream>>>(idx, T, K, E, has_shared ? 1 : 0, align, p, max_rows, max_mtiles,
                                                   status);
     *launches += 1;

@@ -8,6 +8,8 @@
 //
 // Selection ties go to the lower expert index (DeepSeekNative/engine.mm:1880);
 // the reference's argpartition leaves tie order unspecified.
+#include <algorithm>
+
 #include "wm_kernels.h"
 
 namespace wm {
@@ -24,7 +26,7 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __re
   const int row = blockIdx.x * 8 + warp;
   const int rows_total = E + (sg_w != nullptr ? 1 : 0);
   const uint16_t* w = row < E ? wr + (int64_t)row * H : sg_w;
-  for (int t0 = 0; t0 < T; t0 += 8) {
+  for (int t0 = blockIdx.y * 8; t0 < T; t0 += 8 * gridDim.y) {
     const int nt = min(8, T - t0);
     __syncthreads();
     // stage x[t0 .. t0 + nt) (16-byte pieces)
@@ -88,9 +90,8 @@ __device__ __forceinline__ void warp_argmax(float& key, int& idx) {
   }
 }
 
-constexpr int kMaxExpertsPerLane = 32;  // E <= 1024
-
-// One warp per token.  Lane l holds experts e = l + 32 j.
+// One warp per token.  Lane l holds experts e = l + 32 j, j < EPL (E <= 32 EPL).
+template <int EPL>
 __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits,
                                                           const float* __restrict__ bias, int T, int E, int K,
                                                           int kind, int n_groups, int topk_groups, float route_scale,
@@ -100,10 +101,10 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
   if (t >= T) return;
   const float* row = logits + (int64_t)t * E;
   const int per_lane = (E + 31) / 32;
-  float score[kMaxExpertsPerLane], key[kMaxExpertsPerLane];
+  float score[EPL], key[EPL];
   uint32_t taken = 0;  // bit j: slot j is selected or not eligible
 #pragma unroll
-  for (int j = 0; j < kMaxExpertsPerLane; ++j) {
+  for (int j = 0; j < EPL; ++j) {
     const int e = lane + 32 * j;
     float l = (j < per_lane && e < E) ? row[e] : -INFINITY;
     // A softmax router takes `bias` as an additive logit bias (the reference's
@@ -131,7 +132,7 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
     for (int g = 0; g < n_groups; ++g) {
       float best = -INFINITY, second = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < kMaxExpertsPerLane; ++j) {
+      for (int j = 0; j < EPL; ++j) {
         const int e = lane + 32 * j;
         if (j < per_lane && e < E && e / per_group == g) {
           const float v = key[j];
@@ -163,7 +164,7 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
       group_keep |= 1u << gi;
     }
 #pragma unroll
-    for (int j = 0; j < kMaxExpertsPerLane; ++j) {
+    for (int j = 0; j < EPL; ++j) {
       const int e = lane + 32 * j;
       if (j < per_lane && e < E && !((group_keep >> (e / per_group)) & 1u)) taken |= 1u << j;
     }
@@ -174,7 +175,7 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
     float best = -INFINITY;
     int bi = 0x7fffffff;
 #pragma unroll
-    for (int j = 0; j < kMaxExpertsPerLane; ++j) {
+    for (int j = 0; j < EPL; ++j) {
       const int e = lane + 32 * j;
       if (!((taken >> j) & 1u) && (key[j] > best || (key[j] == best && e < bi))) {
         best = key[j];
@@ -186,7 +187,7 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
     if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
     float s_sel = 0.0f;
 #pragma unroll
-    for (int j = 0; j < kMaxExpertsPerLane; ++j)
+    for (int j = 0; j < EPL; ++j)
       if (lane + 32 * j == bi) s_sel = score[j];
     s_sel = __shfl_sync(0xffffffffu, s_sel, bi & 31);
     if (kind == WM_ROUTER_SOFTMAX) {
@@ -222,15 +223,24 @@ void router_init_attributes(int max_hidden) {
 void launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* sg_w, int T, int H, int E,
                           float* logits, float* sg, cudaStream_t stream) {
   const int rows = E + (sg_w != nullptr ? 1 : 0);
-  const int blocks = (rows + 7) / 8;
+  // experts in groups of 8 (one per warp) x token chunks of 8 (up to 64 chunks in flight)
+  const dim3 blocks((rows + 7) / 8, std::min((T + 7) / 8, 64));
   const size_t smem = size_t(8) * H * 2;
   router_logits_kernel<<<blocks, 256, smem, stream>>>(x, wr, sg_w, T, H, E, logits, sg);
 }
 
 void launch_router_topk(const float* logits, const float* bias, int T, int E, int K, int kind, int n_groups,
                         int topk_groups, float route_scale, int32_t* idx, float* w, cudaStream_t stream) {
-  router_topk_kernel<<<(T + 7) / 8, 256, 0, stream>>>(logits, bias, T, E, K, kind, n_groups, topk_groups,
-                                                      route_scale, idx, w);
+  const int blocks = (T + 7) / 8;
+  if (E <= 256)
+    router_topk_kernel<8><<<blocks, 256, 0, stream>>>(logits, bias, T, E, K, kind, n_groups, topk_groups,
+                                                       route_scale, idx, w);
+  else if (E <= 512)
+    router_topk_kernel<16><<<blocks, 256, 0, stream>>>(logits, bias, T, E, K, kind, n_groups, topk_groups,
+                                                        route_scale, idx, w);
+  else
+    router_topk_kernel<32><<<blocks, 256, 0, stream>>>(logits, bias, T, E, K, kind, n_groups, topk_groups,
+                                                        route_scale, idx, w);
 }
 
 }  // namespace wm

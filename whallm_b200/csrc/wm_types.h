@@ -23,6 +23,7 @@ struct Plan {
   int32_t* mtiles;     // [2 * max_mtiles] (expert, first row) of each 128-row tile
   int32_t* n_mtiles;   // [1]
   int32_t* hist;       // [chunks * (E + 1)] per-chunk counts (large-T sort)
+  uint32_t* rowmax;    // [max_rows] or null: zeroed by the plan (decode activation maxima)
 };
 
 // Where the weights of every expert live (expert E = the shared expert).

@@ -64,7 +64,7 @@ class MoeArgs(ctypes.Structure):
 class Counters(ctypes.Structure):
     _fields_ = [
         ("calls_forward", _I64), ("calls_pairs", _I64), ("calls_route", _I64), ("calls_dequant", _I64),
-        ("launches", _I64), ("gemv_calls", _I64), ("gemm_calls", _I64),
+        ("launches", _I64), ("gemv_calls", _I64), ("gemm_calls", _I64), ("decode_calls", _I64),
     ]
 
 
