@@ -209,17 +209,19 @@ Path expert_path(const wm_ctx* ctx, const wm_moe_args* a, bool has_shared) {
   return kPathDecode;
 }
 
-// TMA descriptor over one projection's packed weights of `experts` experts:
-// uint8 [experts][rows][row_bytes], boxes of 32 bytes x box_rows x 1.
+// TMA descriptor over one projection's packed weights (or scales) of
+// `experts` experts: uint8 [experts][rows][row_bytes], boxes of box_bytes x
+// box_rows x 1.
 bool encode_weights(wm_ctx* ctx, CUtensorMap* map, const void* base, int64_t row_bytes, int64_t rows,
-                    int64_t experts, int64_t expert_stride, int box_bytes, int box_rows) {
+                    int64_t experts, int64_t expert_stride, int box_bytes, int box_rows,
+                    CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
   if (ctx->encode_tiled == nullptr) return false;
   cuuint64_t dims[3] = {cuuint64_t(row_bytes), cuuint64_t(rows), cuuint64_t(experts)};
   cuuint64_t strides[2] = {cuuint64_t(row_bytes), cuuint64_t(experts > 1 ? expert_stride : row_bytes * rows)};
   cuuint32_t box[3] = {cuuint32_t(box_bytes), cuuint32_t(box_rows), 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box,
-                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -227,15 +229,17 @@ bool encode_weights(wm_ctx* ctx, CUtensorMap* map, const void* base, int64_t row
 // The tcgen05 decode path: per-token prescale, gate/up (+SwiGLU), down.
 int run_decode(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts, bool has_shared, cudaStream_t s) {
   const int H = a->H, I = a->I;
-  // packed weights (32-byte boxes along K) and E8M0 scales (one box per row tile)
+  // packed weights (128-byte boxes along K = 256 E2M1, 128-byte swizzle) and
+  // E8M0 scales (one box per row tile)
   CUtensorMap w13, w13s, w2, w2s, s13, s13s, s2, s2s;
-  bool ok = encode_weights(ctx, &w13, a->w13.weight, H / 2, 2 * I, a->E, a->w13.weight_stride, 32, 64) &&
-            encode_weights(ctx, &w2, a->w2.weight, I / 2, H, a->E, a->w2.weight_stride, 32, 128) &&
+  constexpr CUtensorMapSwizzle kSw = CU_TENSOR_MAP_SWIZZLE_128B;
+  bool ok = encode_weights(ctx, &w13, a->w13.weight, H / 2, 2 * I, a->E, a->w13.weight_stride, 128, 64, kSw) &&
+            encode_weights(ctx, &w2, a->w2.weight, I / 2, H, a->E, a->w2.weight_stride, 128, 128, kSw) &&
             encode_weights(ctx, &s13, a->w13.scale, H / 32, 2 * I, a->E, a->w13.scale_stride, H / 32, 64) &&
             encode_weights(ctx, &s2, a->w2.scale, I / 32, H, a->E, a->w2.scale_stride, I / 32, 128);
   if (has_shared)
-    ok = ok && encode_weights(ctx, &w13s, a->shared_w13.weight, H / 2, 2 * I, 1, 0, 32, 64) &&
-         encode_weights(ctx, &w2s, a->shared_w2.weight, I / 2, H, 1, 0, 32, 128) &&
+    ok = ok && encode_weights(ctx, &w13s, a->shared_w13.weight, H / 2, 2 * I, 1, 0, 128, 64, kSw) &&
+         encode_weights(ctx, &w2s, a->shared_w2.weight, I / 2, H, 1, 0, 128, 128, kSw) &&
          encode_weights(ctx, &s13s, a->shared_w13.scale, H / 32, 2 * I, 1, 0, H / 32, 64) &&
          encode_weights(ctx, &s2s, a->shared_w2.scale, I / 32, H, 1, 0, I / 32, 128);
   if (!ok) return fail(ctx, "cuTensorMapEncodeTiled failed for the expert weights");

@@ -18,23 +18,26 @@
 //     element within 2^-24 of the row's largest; the epilogue divides by 2^k.
 // So the MMA sums the same products as the reference, in fp32.
 //
-// Per weight value the producers spend one hardware E2M1 -> f16x2 conversion
-// per pair and one f16x2 multiply per pair: about one instruction per weight,
-// which keeps the path bound by HBM rather than by instruction issue.  Every
-// operand reaches shared memory by TMA (packed nibbles, the item's E8M0 tile,
-// the f16 activation tile), so no thread waits on a global load in the loop.
+// The weight operand goes to the tensor cores through TMEM: the producers
+// convert nibbles to f16 in registers (one hardware E2M1 -> f16x2 conversion
+// and one f16x2 multiply per pair, about one instruction per weight) and
+// store them with tcgen05.st; the MMA reads A from TMEM ("[a-tmem]" form).
+// Every other operand reaches shared memory by TMA (packed nibbles, the
+// item's E8M0 tile, the f16 activation tile), so no thread waits on a global
+// load.  At N = 16 an MMA moves little data, so the kernel is bound by how
+// fast tiles, MMAs and barrier round trips flow: MMAs are issued by
+// converged warps through elect.sync, two warps split the K blocks, and the
+// weight and activation tiles of a K block complete on one barrier.
 //
-// Warp roles (608 threads, one persistent CTA per SM):
-//   warp 0      TMA: per item the E8M0 scale tile (2-slot ring), per K block
-//               the raw packed-nibble tile (128 rows x 32 bytes, 16-deep ring)
-//   warp 1      TMEM allocator and the MMA-issuing thread
-//   warp 2      TMA: the f16 activation tile (16 rows x 64 K, 128-byte
-//               swizzle) into its own 16-deep ring, far ahead of the MMA
-//   warps 3-10  weight producers: raw nibbles + E8M0 -> f16 tile, four
-//               groups of two warps taking K blocks round-robin (two rows
-//               per thread)
-//   warps 11-18 epilogue, two groups of four, one per TMEM accumulator:
-//               TMEM -> scaling -> SwiGLU (gate/up) or bf16 rows (down)
+// Warp roles (one persistent CTA per SM):
+//   warp 0      TMA: per item the E8M0 scale tile (2-slot ring); per 4 K
+//               blocks the packed nibbles (128 rows x 128 bytes)
+//   warps 1, 3  MMA issue, even / odd K blocks (warp 1 also owns TMEM)
+//   warp 2      TMA: the f16 activation tile (16 rows x 64 K, 128-byte swizzle)
+//   warps 4-19  weight producers: four groups of four warps (one per TMEM
+//               lane quarter), K blocks round-robin; a thread converts its row
+//   warps 20-23 epilogue: TMEM -> scaling -> SwiGLU (gate/up) or bf16 rows
+//               (down), accumulator sets alternating between items
 // Every mbarrier wait is bounded; a timeout reports status and unwinds.
 #include <cuda.h>
 
@@ -45,21 +48,45 @@ namespace wm {
 namespace {
 
 constexpr int DM = 128, DN = 16, DK = 64;
-constexpr int RAW_STAGES = 16, OP_STAGES = 4, B_STAGES = 16;
-constexpr int RAW_BYTES = DM * DK / 2;       // 4 KB of nibbles
-constexpr int A_OP_BYTES = DM * DK * 2;      // 16 KB f16
+// A stage = one K block: the f16 weight tile (TMEM) and the f16 activation
+// tile (shared memory), completed on one barrier.  A raw stage = RAW_KB K
+// blocks of packed nibbles, 128 rows x 128 bytes with the 128-byte swizzle:
+// the TMA engine's cost grows with the rows of a box, so long rows keep it
+// ahead of HBM, and the swizzle keeps the producers' 16-byte reads of eight
+// consecutive rows on distinct banks.
+constexpr int RAW_KB = 4, RAW_STAGES = 6, A_STAGES = 8;
+constexpr int RAW_ROW = DK * RAW_KB / 2;     // 128 bytes
+constexpr int RAW_BYTES = DM * RAW_ROW;      // 16 KB of nibbles
 constexpr int B_OP_BYTES = DN * DK * 2;      // 2 KB f16
-constexpr int NTHREADS = 608;
-constexpr int DQW0 = 3, DQW = 8, DQG = 4, EPW0 = 11;  // DQG weight-producer groups of DQW / DQG warps
-static_assert(OP_STAGES >= DQG, "each producer group needs its own operand stage");
-constexpr uint32_t TMEM_COLS = 32;
-constexpr int XCHG_BYTES = 2 * 64 * DN * 4;  // per epilogue group: [64 rows][16 tokens] fp32
-constexpr int FIXED_SMEM = OP_STAGES * A_OP_BYTES + B_STAGES * B_OP_BYTES + RAW_STAGES * RAW_BYTES + XCHG_BYTES;
+constexpr int MMA_WARP0 = 1, MMA_WARP1 = 3;  // issue the even / the odd K blocks
+// Weight producers: DQG groups of four warps (one per TMEM lane quarter)
+// taking K blocks round-robin.  A group's step is a chain of barrier round
+// trips, shared loads and the TMEM store that is long next to its ~100 cycles
+// of conversion work, so several groups keep chains in flight at once.
+constexpr int DQG = 4, DQ_WARPS = 4;
+static_assert(8 % DQG == 0, "a group's K blocks take the same 16-byte scale chunk in turn");
+static_assert(RAW_ROW == 128, "one swizzle atom row per weight row");
+constexpr int DQW0 = 4, DQW = DQG * DQ_WARPS;
+constexpr int EPG = 1;                       // epilogue groups of four warps
+constexpr int EPW0 = DQW0 + DQW;
+constexpr int NTHREADS = 32 * (EPW0 + 4 * EPG);
+static_assert(DQW0 % 4 == 0 && EPW0 % 4 == 0, "a group's warp w serves TMEM lane quarter w % 4");
+// An item's K steps rotate over NACC accumulators of DN columns: consecutive
+// MMAs into one accumulator wait for each other, and at N = 16 that latency,
+// not the tensor pipe, would pace the kernel.  The epilogue sums them.
+constexpr int NACC = 8;
+constexpr uint32_t ACC_COLS = NACC * DN;     // one accumulator set (of two)
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t A_COL0 = 2 * ACC_COLS;    // A stages: 32 columns (64 f16 per lane) each
+static_assert(A_COL0 + A_STAGES * 32 <= TMEM_COLS, "TMEM layout");
+static_assert((DK / 16) * 2 == NACC, "an even and an odd K block cover the accumulators once");
+static_assert(A_STAGES % DQG == 0 && DQG % 2 == 0, "an A stage always belongs to the same producer group and MMA warp");
+constexpr int XCHG_BYTES = EPG * 64 * DN * 4;  // per epilogue group: [64 rows][16 tokens] fp32
+constexpr int FIXED_SMEM = A_STAGES * B_OP_BYTES + RAW_STAGES * RAW_BYTES + XCHG_BYTES;
 
 struct Shared {
   uint64_t raw_full[RAW_STAGES], raw_empty[RAW_STAGES];
-  uint64_t op_full[OP_STAGES], op_empty[OP_STAGES];  // f16 weight tiles
-  uint64_t b_full[B_STAGES], b_empty[B_STAGES];      // f16 activation tiles
+  uint64_t a_full[A_STAGES], a_empty[A_STAGES];  // f16 weight (TMEM) + activation (smem) tiles
   uint64_t tmem_full[2], tmem_empty[2];
   uint64_t x_full[2], x_empty[2];    // gate/up exchange inside each epilogue group
   uint64_t sc_full[2], sc_empty[2];  // the items' E8M0 tiles
@@ -71,11 +98,6 @@ struct Shared {
 // 128 rows x Kdim/32 bytes + alignment slack + barriers.
 size_t smem_bytes(int kdim) { return size_t(FIXED_SMEM) + 2 * size_t(DM) * (kdim / 32) + 1024 + 1024; }
 static_assert(sizeof(Shared) <= 1024, "barrier block must fit its reserve");
-
-__device__ __forceinline__ void sts_v4(uint32_t addr, uint4 v) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-               : "memory");
-}
 
 __device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
   uint4 v;
@@ -97,7 +119,7 @@ __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
 }
 
 // 8 E2M1 nibbles of `w` (element j = nibble j) times the f16x2 scale -> 4 f16x2.
-__device__ __forceinline__ uint4 e2m1x8_f16_scaled(uint32_t w, uint32_t scale2) {
+__device__ __forceinline__ void e2m1x8_f16_scaled(uint32_t w, uint32_t scale2, uint32_t* out) {
   uint32_t h0, h1, h2, h3;
   asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
       "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
@@ -107,7 +129,10 @@ __device__ __forceinline__ uint4 e2m1x8_f16_scaled(uint32_t w, uint32_t scale2) 
       "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
       : "=r"(h0), "=r"(h1), "=r"(h2), "=r"(h3)
       : "r"(w));
-  return make_uint4(hmul2(h0, scale2), hmul2(h1, scale2), hmul2(h2, scale2), hmul2(h3, scale2));
+  out[0] = hmul2(h0, scale2);
+  out[1] = hmul2(h1, scale2);
+  out[2] = hmul2(h2, scale2);
+  out[3] = hmul2(h3, scale2);
 }
 
 // f16x2 holding 2^d twice (d <= 0; below f16's range -> 0).
@@ -170,14 +195,30 @@ __device__ __forceinline__ void tma_load_2d_u32(uint32_t dst, const void* tmap, 
       : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld_16cols(uint32_t taddr, uint32_t* r) {
+// 32 consecutive TMEM columns of this warp's 32 lanes <- 32 registers per thread.
+__device__ __forceinline__ void tmem_st_32cols(uint32_t taddr, const uint32_t* v) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
 }
+
+// 16 consecutive TMEM columns of this warp's 32 lanes <- 16 registers per thread.
+__device__ __forceinline__ void tmem_st_16cols(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // kind::f16 instruction descriptor: f16 A and B, fp32 D, K-major, M x N.
 constexpr uint32_t idesc_f16(uint32_t M, uint32_t N) { return (1u << 4) | ((N >> 3) << 17) | ((M >> 4) << 24); }
@@ -200,11 +241,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const uint32_t raw0 = smem_u32(smem_raw);
   const uint32_t base = (raw0 + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw0);
-  const uint32_t a_op = base;                             // OP_STAGES x 16 KB (1024-aligned)
-  const uint32_t b_op = a_op + OP_STAGES * A_OP_BYTES;    // B_STAGES x 2 KB (1024-aligned)
-  const uint32_t raw = b_op + B_STAGES * B_OP_BYTES;      // RAW_STAGES x 4 KB
+  const uint32_t b_op = base;                             // A_STAGES x 2 KB (1024-aligned)
+  const uint32_t raw = b_op + A_STAGES * B_OP_BYTES;      // RAW_STAGES x 16 KB (1024-aligned)
   const uint32_t scl = raw + RAW_STAGES * RAW_BYTES;      // 2 x sc_bytes
-  float* xchg = reinterpret_cast<float*>(gbase + (scl - base) + 2 * sc_bytes);  // [2][64][16]
+  float* xchg = reinterpret_cast<float*>(gbase + (scl - base) + 2 * sc_bytes);  // [EPG][64][16]
   Shared& sh = *reinterpret_cast<Shared*>(reinterpret_cast<uint8_t*>(xchg) + XCHG_BYTES);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -214,28 +254,25 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < RAW_STAGES; ++s) {
       mbar_init(&sh.raw_full[s], 1);
-      mbar_init(&sh.raw_empty[s], DQW / DQG);
+      mbar_init(&sh.raw_empty[s], RAW_KB * DQ_WARPS);  // each of its K blocks: one group
     }
-    for (int s = 0; s < OP_STAGES; ++s) {
-      mbar_init(&sh.op_full[s], DQW / DQG);
-      mbar_init(&sh.op_empty[s], 1);
-    }
-    for (int s = 0; s < B_STAGES; ++s) {
-      mbar_init(&sh.b_full[s], 1);
-      mbar_init(&sh.b_empty[s], 1);
+    for (int s = 0; s < A_STAGES; ++s) {
+      mbar_init(&sh.a_full[s], DQ_WARPS + 1);  // the group's producer warps + the activation TMA
+      mbar_init(&sh.a_empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&sh.tmem_full[i], 1);
+      mbar_init(&sh.tmem_full[i], 2);   // both MMA warps
+
       mbar_init(&sh.tmem_empty[i], 4);
       mbar_init(&sh.x_full[i], 2);
       mbar_init(&sh.x_empty[i], 2);
       mbar_init(&sh.sc_full[i], 1);
-      mbar_init(&sh.sc_empty[i], DQW + 4);
+      mbar_init(&sh.sc_empty[i], DQW + 4 * EPG);
     }
     sh.abort = 0;
     fence_mbarrier_init();
   }
-  if (warp == 1) {
+  if (warp == MMA_WARP0) {
     tmem_alloc(&sh.tmem_base, TMEM_COLS);
     tmem_relinquish();
   }
@@ -280,7 +317,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         const CUtensorMap* tm = routed ? &tm_w : &tm_sh;
         bool ok = true;
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        for (int kq = 0; kq < kblocks / RAW_KB; ++kq, ++it) {
           const int s = it % RAW_STAGES;
           const uint32_t ph = (it / RAW_STAGES) & 1u;
           if (!mbar_wait(&sh.raw_empty[s], ph ^ 1u, abort)) {
@@ -291,49 +328,53 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           mbar_arrive_expect_tx(&sh.raw_full[s], RAW_BYTES);
           const uint32_t dst = raw + s * RAW_BYTES;
           if (KIND == 0) {
-            tma_load_3d(dst, tm, kb * (DK / 2), gate_base + mt * (DM / 2), z, &sh.raw_full[s]);
-            tma_load_3d(dst + RAW_BYTES / 2, tm, kb * (DK / 2), up_base + mt * (DM / 2), z, &sh.raw_full[s]);
+            tma_load_3d(dst, tm, kq * RAW_ROW, gate_base + mt * (DM / 2), z, &sh.raw_full[s]);
+            tma_load_3d(dst + RAW_BYTES / 2, tm, kq * RAW_ROW, up_base + mt * (DM / 2), z, &sh.raw_full[s]);
           } else {
-            tma_load_3d(dst, tm, kb * (DK / 2), mt * DM, z, &sh.raw_full[s]);
+            tma_load_3d(dst, tm, kq * RAW_ROW, mt * DM, z, &sh.raw_full[s]);
           }
         }
         if (!ok) break;
       }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16(DM, DN);
-      uint32_t it = 0, lt = 0;
-      for (int t = blockIdx.x; t < total && !*abort; t += gridDim.x, ++lt) {
-        const uint32_t acc = lt & 1u, acc_ph = (lt >> 1) & 1u;
-        if (!mbar_wait(&sh.tmem_empty[acc], acc_ph ^ 1u, abort)) {
-          fail(sh, a.status, 21);
+  } else if (warp == MMA_WARP0 || warp == MMA_WARP1) {
+    // ------------------------------------------------------------ MMA issuers
+    // Two warps, one for the even and one for the odd K blocks of each item
+    // (accumulators 0-3 and 4-7): a warp's issue loop is latency-bound, two
+    // of them keep the tensor pipe twice as busy.  The whole warp runs the
+    // loop (its waits are warp-uniform) and one elected lane issues.
+    const int par = warp == MMA_WARP0 ? 0 : 1;
+    constexpr uint32_t idesc = idesc_f16(DM, DN);
+    uint32_t it0 = 0, lt = 0;
+    for (int t = blockIdx.x; t < total && !warp_aborted(abort); t += gridDim.x, ++lt) {
+      const uint32_t acc = lt & 1u, acc_ph = (lt >> 1) & 1u;
+      if (!warp_wait(&sh.tmem_empty[acc], acc_ph ^ 1u, abort)) {
+        if (lane == 0) fail(sh, a.status, 21);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d0 = tmem + acc * ACC_COLS + par * (DK / 16) * DN;
+      bool ok = true;
+      for (int kb = par; kb < kblocks; kb += 2) {
+        const uint32_t it = it0 + kb;
+        const int s = it % A_STAGES;
+        if (!warp_wait(&sh.a_full[s], (it / A_STAGES) & 1u, abort)) {
+          if (lane == 0) fail(sh, a.status, 22);
+          ok = false;
           break;
         }
         tc_fence_after();
-        bool ok = true;
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
-          const int s = it % OP_STAGES, sb = it % B_STAGES;
-          const uint32_t ph = (it / OP_STAGES) & 1u, phb = (it / B_STAGES) & 1u;
-          if (!mbar_wait(&sh.b_full[sb], phb, abort) || !mbar_wait(&sh.op_full[s], ph, abort)) {
-            fail(sh, a.status, 22);
-            ok = false;
-            break;
-          }
-          tc_fence_after();
+        const uint32_t a0 = tmem + A_COL0 + s * 32;
+        const uint64_t b0 = umma_desc_sw128(b_op + s * B_OP_BYTES);
+        const uint32_t accumulate = kb >= 2 ? 1u : 0u;
 #pragma unroll
-          for (int k = 0; k < DK / 16; ++k) {
-            const uint64_t da = umma_desc_sw128(a_op + s * A_OP_BYTES + k * 32);
-            const uint64_t db = umma_desc_sw128(b_op + sb * B_OP_BYTES + k * 32);
-            umma_f16(tmem + acc * DN, da, db, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-          }
-          umma_commit(&sh.op_empty[s]);
-          umma_commit(&sh.b_empty[sb]);
-        }
-        if (!ok) break;
-        umma_commit(&sh.tmem_full[acc]);
+        for (int k = 0; k < DK / 16; ++k)  // K16 step: 8 TMEM columns of A, 32 bytes (2 in the descriptor) of B
+          umma_f16_ts_elect(d0 + k * DN, a0 + k * 8, b0 + 2 * k, idesc, accumulate);
+        umma_commit_elect(&sh.a_empty[s]);
       }
+      if (!ok) break;
+      umma_commit_elect(&sh.tmem_full[acc]);
+      it0 += kblocks;
     }
   } else if (warp == 2) {
     // ------------------------------------------------------------ activation tiles (TMA)
@@ -343,73 +384,84 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int row0 = a.plan.mtiles[2 * (t / n_mt) + 1];
         bool ok = true;
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
-          const int s = it % B_STAGES;
-          const uint32_t ph = (it / B_STAGES) & 1u;
-          if (!mbar_wait(&sh.b_empty[s], ph ^ 1u, abort)) {
+          const int s = it % A_STAGES;
+          const uint32_t ph = (it / A_STAGES) & 1u;
+          if (!mbar_wait(&sh.a_empty[s], ph ^ 1u, abort)) {
             fail(sh, a.status, 23);
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&sh.b_full[s], B_OP_BYTES);
-          tma_load_2d_u32(b_op + s * B_OP_BYTES, &tm_b, kb * DK, row0, &sh.b_full[s]);
+          mbar_arrive_expect_tx(&sh.a_full[s], B_OP_BYTES);
+          tma_load_2d_u32(b_op + s * B_OP_BYTES, &tm_b, kb * DK, row0, &sh.a_full[s]);
         }
         if (!ok) break;
       }
     }
   } else if (warp < EPW0) {
     // ------------------------------------------------------------ weight producers
-    // DQG groups of two warps take an item's K blocks round-robin, so DQG K
-    // blocks are converted at once (one group's chain of waits, loads,
-    // conversions and stores would otherwise pace the whole pipeline); each
-    // thread converts two whole rows (r and r + 64) of its group's K block.
-    const int grp = (warp - DQW0) >> 1;
-    const int tid = ((warp - DQW0) & 1) * 32 + lane;  // 0..63
-    uint32_t it0 = 0, lt = 0;  // global K-block counter at the item's start
-    for (int t = blockIdx.x; t < total && !*abort; t += gridDim.x, ++lt) {
+    // DQG groups take an item's K blocks round-robin; warp w of a group
+    // serves TMEM lane quarter w % 4, one weight row per thread.
+    const int grp = (warp - DQW0) / DQ_WARPS;
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // tile row
+    uint32_t it0 = 0, lt = 0;           // global K-block counter at the item's start
+    for (int t = blockIdx.x; t < total && !warp_aborted(abort); t += gridDim.x, ++lt) {
       const uint32_t slot = lt & 1u, sph = (lt >> 1) & 1u;
-      if (!mbar_wait(&sh.sc_full[slot], sph, abort)) {
-        fail(sh, a.status, 30);
+      if (!warp_wait(&sh.sc_full[slot], sph, abort)) {
+        if (lane == 0) fail(sh, a.status, 30);
         break;
       }
-      const uint32_t srow0 = scl + slot * sc_bytes + tid * sc_row;
-      const uint32_t srow1 = srow0 + (DM / 2) * sc_row;
-      const int smax0 = int(smem_max_scale(srow0, sc_row)), smax1 = int(smem_max_scale(srow1, sc_row));
+      const uint32_t srow = scl + slot * sc_bytes + r * sc_row;
+      const int smax = int(smem_max_scale(srow, sc_row));
       bool ok = true;
+      uint4 sq = make_uint4(0u, 0u, 0u, 0u);
       for (int kb = grp; kb < kblocks; kb += DQG) {
-        const uint32_t it = it0 + kb;
-        const int rs = it % RAW_STAGES, os = it % OP_STAGES;
-        const uint32_t rph = (it / RAW_STAGES) & 1u, oph = (it / OP_STAGES) & 1u;
-        if (!mbar_wait(&sh.raw_full[rs], rph, abort)) {
-          fail(sh, a.status, 24);
+        const uint32_t it = it0 + kb, rit = it / RAW_KB;
+        const int rs = rit % RAW_STAGES, as = it % A_STAGES;
+        const uint32_t rph = (rit / RAW_STAGES) & 1u, aph = (it / A_STAGES) & 1u;
+        // The scale tile is resident: take this block's two E8M0 bytes before
+        // waiting for the nibbles.  Rows are Kdim/32 bytes apart, so a warp's
+        // byte loads would share two banks; one 16-byte load per row serves
+        // eight K blocks instead.
+        if (kb % 8 < DQG) sq = lds_v4(srow + (kb / 8) * 16);
+        const int wi = (kb % 8) >> 1;
+        const uint32_t word = wi == 0 ? sq.x : wi == 1 ? sq.y : wi == 2 ? sq.z : sq.w;
+        const uint32_t pair = (kb & 1) ? (word >> 16) : (word & 0xffffu);
+        const int s0 = int(pair & 0xffu), s1 = int(pair >> 8);
+        const uint32_t c0 = s0 == 0 ? 0u : pow2_f16x2(s0 - smax), c1 = s1 == 0 ? 0u : pow2_f16x2(s1 - smax);
+        if (!warp_wait(&sh.raw_full[rs], rph, abort)) {
+          if (lane == 0) fail(sh, a.status, 24);
           ok = false;
           break;
         }
-        const uint32_t rsrc = raw + rs * RAW_BYTES + tid * 32;
-        const uint4 n00 = lds_v4(rsrc), n01 = lds_v4(rsrc + 16);
-        const uint4 n10 = lds_v4(rsrc + (DM / 2) * 32), n11 = lds_v4(rsrc + (DM / 2) * 32 + 16);
+        // 32 bytes = 64 E2M1 = the row's two scale groups of this K block:
+        // 16-byte chunks 2j, 2j+1 of the row, swizzled by row % 8
+        const uint32_t rrow = raw + rs * RAW_BYTES + r * RAW_ROW;
+        const uint32_t j2 = uint32_t(kb % RAW_KB) * 2u;
+        const uint4 lo = lds_v4(rrow + ((j2 ^ uint32_t(r & 7)) << 4));
+        const uint4 hi = lds_v4(rrow + (((j2 + 1u) ^ uint32_t(r & 7)) << 4));
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh.raw_empty[rs]);
-        const int s00 = int(lds_u8(srow0 + kb * 2)), s01 = int(lds_u8(srow0 + kb * 2 + 1));
-        const int s10 = int(lds_u8(srow1 + kb * 2)), s11 = int(lds_u8(srow1 + kb * 2 + 1));
-        if (!mbar_wait(&sh.op_empty[os], oph ^ 1u, abort)) {
-          fail(sh, a.status, 25);
+        uint32_t v[32];
+        e2m1x8_f16_scaled(lo.x, c0, v + 0);
+        e2m1x8_f16_scaled(lo.y, c0, v + 4);
+        e2m1x8_f16_scaled(lo.z, c0, v + 8);
+        e2m1x8_f16_scaled(lo.w, c0, v + 12);
+        e2m1x8_f16_scaled(hi.x, c1, v + 16);
+        e2m1x8_f16_scaled(hi.y, c1, v + 20);
+        e2m1x8_f16_scaled(hi.z, c1, v + 24);
+        e2m1x8_f16_scaled(hi.w, c1, v + 28);
+        if (!warp_wait(&sh.a_empty[as], aph ^ 1u, abort)) {
+          if (lane == 0) fail(sh, a.status, 25);
           ok = false;
           break;
         }
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int r = tid + j * (DM / 2);
-          const uint4 lo = j == 0 ? n00 : n10, hi = j == 0 ? n01 : n11;
-          const int sa = j == 0 ? s00 : s10, sb = j == 0 ? s01 : s11, sm = j == 0 ? smax0 : smax1;
-          const uint32_t c0 = sa == 0 ? 0u : pow2_f16x2(sa - sm), c1 = sb == 0 ? 0u : pow2_f16x2(sb - sm);
-          const uint32_t row_addr = a_op + os * A_OP_BYTES + r * 128;
-          const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-#pragma unroll
-          for (int c = 0; c < 8; ++c) sts_v4(row_addr + ((c ^ (r & 7)) << 4), e2m1x8_f16_scaled(w[c], c < 4 ? c0 : c1));
-        }
-        fence_proxy_async_smem();
+        tc_fence_after();
+        tmem_st_32cols(tmem + A_COL0 + as * 32 + (uint32_t(quarter * 32) << 16), v);
+        tmem_st_wait();
+        tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sh.op_full[os]);
+        if (lane == 0) mbar_arrive(&sh.a_full[as]);
       }
       if (!ok) break;
       it0 += kblocks;
@@ -417,15 +469,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (lane == 0) mbar_arrive(&sh.sc_empty[slot]);
     }
   } else {
-    // ------------------------------------------------------------ epilogue (two groups)
-    const int grp = (warp - EPW0) >> 2;  // handles the items of TMEM accumulator / scale slot `grp`
+    // ------------------------------------------------------------ epilogue
+    const int grp = (warp - EPW0) >> 2;  // handles items lt with lt % EPG == grp
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;   // TMEM lane = weight row of the tile
     float* xg = xchg + grp * 64 * DN;
     uint32_t lt = 0;
     for (int t = blockIdx.x; t < total && !*abort; t += gridDim.x, ++lt) {
-      if (int(lt & 1u) != grp) continue;
-      const uint32_t acc = lt & 1u, ph2 = (lt >> 1) & 1u;
+      if (int(lt % EPG) != grp) continue;
+      const uint32_t acc = lt & 1u, ph2 = (lt >> 1) & 1u, xph = (lt / EPG) & 1u;
       const int ent = t / n_mt;
       const int e = a.plan.mtiles[2 * ent], row0 = a.plan.mtiles[2 * ent + 1];
       const int mt = t % n_mt;
@@ -445,20 +497,27 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         break;
       }
       tc_fence_after();
-      uint32_t v[DN];
-      tmem_ld_16cols(tmem + acc * DN + (uint32_t(quarter * 32) << 16), v);
-      tmem_ld_wait();
+      float y[DN];
+#pragma unroll
+      for (int n = 0; n < DN; ++n) y[n] = 0.0f;
+#pragma unroll
+      for (int c = 0; c < NACC; c += 2) {
+        uint32_t v[2 * DN];
+        tmem_ld_32cols(tmem + acc * ACC_COLS + c * DN + (uint32_t(quarter * 32) << 16), v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int n = 0; n < DN; ++n) y[n] += __uint_as_float(v[n]) + __uint_as_float(v[DN + n]);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh.tmem_empty[acc]);
-      float y[DN];
 #pragma unroll
-      for (int n = 0; n < DN; ++n) y[n] = n < valid ? __uint_as_float(v[n]) * (rowf / bs[n]) : 0.0f;
+      for (int n = 0; n < DN; ++n) y[n] = n < valid ? y[n] * (rowf / bs[n]) : 0.0f;
       if (KIND == 0) {
         // rows 64..127 hold the up projections of the features of rows 0..63;
         // they pass them to the gate rows through `xg` (bounded waits).
         if (r >= DM / 2) {
-          if (!mbar_wait(&sh.x_empty[grp], ph2 ^ 1u, abort)) {
+          if (!mbar_wait(&sh.x_empty[grp], xph ^ 1u, abort)) {
             fail(sh, a.status, 27);
             break;
           }
@@ -468,7 +527,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           if (lane == 0) mbar_arrive(&sh.x_full[grp]);
           continue;
         }
-        if (!mbar_wait(&sh.x_full[grp], ph2, abort)) {
+        if (!mbar_wait(&sh.x_full[grp], xph, abort)) {
           fail(sh, a.status, 28);
           break;
         }
@@ -499,7 +558,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == MMA_WARP0) {
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
   }

@@ -146,12 +146,13 @@ __device__ __forceinline__ void fence_mbarrier_init() {
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+  // the phase token is not needed: the sink lets the warp go on without waiting for it
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
                    smem_u32(bar)),
                "r"(bytes)
                : "memory");
@@ -169,6 +170,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe of a phase.  On B200 it answers in about half the time
+// try_wait takes on an already-completed phase, so it is the fast path.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -178,18 +193,32 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 // Bounded wait on an mbarrier phase.  Gives up after `timeout_ns` of wall time,
 // or as soon as another role raised `*abort`, and returns false then; the
 // caller reports the status and unwinds.  A healthy wait lasts microseconds.
+// `sleep_ns` > 0 backs off between polls: a waiting warp then leaves the
+// issue slots to the working warps of its SM instead of polling.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          uint64_t timeout_ns = 2000000000ull) {
-  if (mbar_try_wait(bar, parity)) return true;
+                                          uint32_t sleep_ns = 0, uint64_t timeout_ns = 2000000000ull) {
+  if (mbar_test_wait(bar, parity)) return true;
   uint64_t start = global_timer_ns();
   for (uint32_t spin = 1;; ++spin) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((spin & 255u) == 0u) {
+    if (sleep_ns != 0u) __nanosleep(sleep_ns);
+    if ((spin & 15u) == 0u) {
       if (*abort) return false;
       if (global_timer_ns() - start > timeout_ns) return false;
     }
   }
 }
+
+// mbar_wait by every lane of a converged warp; the result is warp-uniform
+// (false if any lane gave up), so the warp stays converged after it.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          uint32_t sleep_ns = 0) {
+  const bool ok = mbar_wait(bar, parity, abort, sleep_ns);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// Warp-uniform read of the abort flag.
+__device__ __forceinline__ bool warp_aborted(volatile int* abort) { return __any_sync(0xffffffffu, *abort != 0); }
 
 // ------------------------------------------------------------------ proxy fences
 
@@ -249,6 +278,41 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint6
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
+}
+
+// Warp-wide MMA issue: every lane of a converged warp calls these with the
+// same arguments and one elected lane issues the instruction.  Measured on
+// B200, an M128 x K16 MMA issued this way costs ~60 cycles when one warp
+// issues, against ~200 cycles from a single thread inside a lane branch.
+__device__ __forceinline__ void umma_f16_elect(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16, issued by one elected lane.
+__device__ __forceinline__ void umma_f16_ts_elect(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                  uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit_elect(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
 }
 
 // 32 consecutive TMEM columns of this warp's 32 lanes -> 32 registers per thread.

@@ -154,38 +154,37 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(BM, BN);
-      uint32_t it = 0, lt = 0;
-      for (int t = blockIdx.x; t < total && !*abort; t += gridDim.x, ++lt) {
-        const uint32_t acc = lt & 1u, acc_ph = (lt >> 1) & 1u;
-        if (!mbar_wait(&sh.tmem_empty[acc], acc_ph ^ 1u, abort)) {
-          fail(sh, a.status, 11);
+    // The whole warp runs the loop (its waits are warp-uniform) and one
+    // elected lane issues each tcgen05 instruction.
+    constexpr uint32_t idesc = umma_idesc_bf16(BM, BN);
+    uint32_t it = 0, lt = 0;
+    for (int t = blockIdx.x; t < total && !warp_aborted(abort); t += gridDim.x, ++lt) {
+      const uint32_t acc = lt & 1u, acc_ph = (lt >> 1) & 1u;
+      if (!warp_wait(&sh.tmem_empty[acc], acc_ph ^ 1u, abort)) {
+        if (lane == 0) fail(sh, a.status, 11);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem + acc * BN;
+      bool ok = true;
+      for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1u;
+        if (!warp_wait(&sh.full[s], ph, abort)) {
+          if (lane == 0) fail(sh, a.status, 12);
+          ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem + acc * BN;
-        bool ok = true;
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
-          const int s = it % STAGES;
-          const uint32_t ph = (it / STAGES) & 1u;
-          if (!mbar_wait(&sh.full[s], ph, abort)) {
-            fail(sh, a.status, 12);
-            ok = false;
-            break;
-          }
-          tc_fence_after();
+        const uint64_t da = umma_desc_sw128(a_smem + s * A_BYTES);
+        const uint64_t db = umma_desc_sw128(b_smem + s * B_BYTES);
 #pragma unroll
-          for (int k = 0; k < BK / UMMA_K; ++k) {
-            const uint64_t da = umma_desc_sw128(a_smem + s * A_BYTES + k * UMMA_K * 2);
-            const uint64_t db = umma_desc_sw128(b_smem + s * B_BYTES + k * UMMA_K * 2);
-            umma_f16(d_tmem, da, db, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-          }
-          umma_commit(&sh.empty[s]);
-        }
-        if (!ok) break;
-        umma_commit(&sh.tmem_full[acc]);
+        for (int k = 0; k < BK / UMMA_K; ++k)  // K16 step = 32 bytes = 2 in the descriptor's address field
+          umma_f16_elect(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+        umma_commit_elect(&sh.empty[s]);
       }
+      if (!ok) break;
+      umma_commit_elect(&sh.tmem_full[acc]);
     }
   } else if (warp < EPI_WARP0) {
     // ---------------------------------------------------------------- weight producers
