@@ -8,9 +8,14 @@ GEMVs -> shared expert -> combine).  Each step uses the next of 8 token
 batches, so routes change; L2 is flushed (a 256 MB write) before every timed
 step.  `value` is whole-job tokens/s from device events (inputs resident);
 `e2e` is the same through the public call with pinned host input/output and
-the copies inside the timed region.  With --gpus N > 1 every rank runs its
-own batch.  `--impl reference` times the CPU oracle (the restatement of the
-reference's arithmetic) on a bounded sample of the same workload.
+the copies inside the timed region.  With --gpus N > 1 the layer runs
+expert-parallel (whallm_b200.ep): every rank owns E/N experts and its own
+64-token batch, and pairs travel to their experts' ranks and back by NCCL
+all-to-all (weak scaling; eager steps, since the split sizes are read on the
+host).  At N = 1 the line also carries a `prefill` section: the config-2
+layer (16,384 tokens, Zipf(1.1) routing) through the grouped-GEMM path.
+`--impl reference` times the CPU oracle (the restatement of the reference's
+arithmetic) on a bounded sample of the same workload.
 """
 from __future__ import annotations
 
@@ -158,6 +163,160 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def prefill_section(args, dev, pk) -> dict:
+    """Config 2 (T = 16,384, Zipf(1.1) popularity) through the public call."""
+    import torch
+    from whallm_b200 import synth
+    from whallm_b200.moe import Engine
+
+    wl = synth.config(2, device=dev)
+    T = wl.x.shape[0]
+    eng = Engine(dev.index, max_tokens=T, hidden=H, inter=I, experts=E, topk=K)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(3):
+        eng.forward(wl.layer, wl.x, K)
+    torch.cuda.synchronize()
+    steps = max(3, min(args.steps, 10))
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        evs[i][0].record()
+        eng.forward(wl.layer, wl.x, K)
+        evs[i][1].record()
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in evs) / steps
+    eng.ctx.profile(True)
+    eng.ctx.profile_reset()
+    _, (w, idx) = eng.forward(wl.layer, wl.x, K, return_routes=True)
+    torch.cuda.synchronize()
+    prof = eng.ctx.profile_read()
+    eng.ctx.profile(False)
+    counts = torch.bincount(idx.reshape(-1).long(), minlength=E).cpu()
+    rows = T * K + T  # routed pairs + shared-expert rows
+    gu_flops, dn_flops = 2.0 * rows * H * 2 * I, 2.0 * rows * I * H
+    gu_n, gu_ms = prof.get("gemm_gate_up", (1, float("nan")))
+    dn_n, dn_ms = prof.get("gemm_down", (1, float("nan")))
+    tf_gu = gu_flops / (gu_ms / gu_n / 1e3) / 1e12
+    tf_dn = dn_flops / (dn_ms / dn_n / 1e3) / 1e12
+    layer_tf = (gu_flops + dn_flops) / (ms / 1e3) / 1e12
+    fp4_nominal = 9000.0
+    return {
+        "workload": "config2 prefill layer, 16384 tokens, Zipf(1.1) expert popularity", "tokens_per_s": T / (ms / 1e3),
+        "ms_per_layer": ms, "layer_tflops": layer_tf,
+        "roofline": {"bound": "tensor", "kernel": "gemm_gate_up", "achieved": tf_gu, "unit": "TFLOP/s",
+                     "peak_bf16": pk["bf16_tflops"], "frac_bf16": tf_gu / pk["bf16_tflops"],
+                     "peak_fp4_nominal": fp4_nominal, "frac_fp4_nominal": tf_gu / fp4_nominal,
+                     "mma_kind": "kind::f16 (bf16 operands, exact dequantised weights)", "peak_source": pk["source"],
+                     "down_tflops": tf_dn, "algorithmic_flops_per_launch": gu_flops},
+        "kernels": {n: {"launches": c, "avg_us": 1e3 * t / c} for n, (c, t) in prof.items()},
+        "expert_rows": {"max": int(counts.max()), "median": float(counts.float().median()), "min": int(counts.min())},
+        "l2": "flushed before every timed step",
+    }
+
+
+def run_ep(args, world: int, rank: int, local: int) -> None:
+    """--gpus N > 1: the config-1 layer expert-parallel over N ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from whallm_b200 import synth
+    from whallm_b200.ep import ExpertParallelMoE
+    from whallm_b200.moe import Engine
+
+    dev = torch.device("cuda", local)
+    B = args.batch
+    wl = synth.config(1, device=dev, batch=B, seed=0)  # same seed: every rank holds the same layer
+    layer = wl.layer
+    nb = 8
+    xs = [synth.activations(B, H, torch.Generator(device=dev).manual_seed(1000 * rank + i), dev) for i in range(nb)]
+    # rows a rank receives are at most all ranks' pairs; decode kernels throughout
+    cap = world * B * K
+    eng = Engine(local, max_tokens=cap, hidden=H, inter=I, experts=E, topk=K, gemv_max_tokens=cap)
+    ep = ExpertParallelMoE(eng, layer, K)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def fwd(x):
+        return ep(x)
+
+    for i in range(args.warmup):
+        fwd(xs[i % nb])
+    torch.cuda.synchronize()
+    c0 = eng.ctx.counters().launches
+    fwd(xs[0])
+    torch.cuda.synchronize()
+    launches_per_step = eng.ctx.counters().launches - c0
+    dist.barrier()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    recv = []
+    with Clocks(local) as clocks:
+        torch.cuda.synchronize()
+        for i in range(args.steps):
+            flush.zero_()
+            dist.barrier()
+            evs[i][0].record()
+            fwd(xs[i % nb])
+            evs[i][1].record()
+            recv.append(ep.stats.received)
+        torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in evs)
+    t = torch.tensor([ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    value = world * B * args.steps / (ms / 1e3)
+
+    # per-kernel durations on this rank (library CUDA events), eager
+    eng.ctx.profile(True)
+    eng.ctx.profile_reset()
+    for i in range(args.steps):
+        flush.zero_()
+        fwd(xs[i % nb])
+    torch.cuda.synchronize()
+    prof = eng.ctx.profile_read()
+    eng.ctx.profile(False)
+    kernels = {name: {"launches": n, "avg_us": 1e3 * tt / n} for name, (n, tt) in prof.items()}
+
+    # end to end with pinned host buffers
+    xh = [x.cpu().pin_memory() for x in xs]
+    oh = torch.empty((B, H), dtype=torch.bfloat16).pin_memory()
+    e_evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.zero_()
+        dist.barrier()
+        e_evs[i][0].record()
+        oh.copy_(fwd(xh[i % nb].to(dev, non_blocking=True)), non_blocking=True)
+        e_evs[i][1].record()
+    torch.cuda.synchronize()
+    e_ms = sum(a.elapsed_time(b) for a, b in e_evs)
+    t = torch.tensor([e_ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e_ms = float(t.item())
+    e2e = world * B * args.steps / (e_ms / 1e3)
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32-accumulate MXFP4 x bf16",
+        "data": "synthetic (seeded; BASELINE configs[1] value distributions)",
+        "config": {"workload": f"config1 decode layer, {B} tokens per step per GPU", "H": H, "I": I, "E": E,
+                   "K": K, "shared_expert": True, "router": "softmax top-10",
+                   "l2": "flushed (256 MB write) before every timed step",
+                   "timing": "eager steps, device events, max over ranks",
+                   "parallelism": f"expert-parallel x{world} ({E // world} experts per GPU), NCCL all-to-all",
+                   "pairs_received_per_step_rank0": statistics.mean(recv)},
+        "roofline": None,
+        "kernels": kernels,
+        "cpu_baseline": None,
+        "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": world * B * H * 2,
+                "d2h_bytes_per_step": world * B * H * 2},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run(args) -> None:
     import numpy as np
     import torch
@@ -167,6 +326,9 @@ def run(args) -> None:
     from whallm_b200.moe import Engine
 
     world, rank, local = dist_init()
+    if world > 1:
+        run_ep(args, world, rank, local)
+        return
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     B = args.batch
@@ -285,11 +447,7 @@ def run(args) -> None:
                "sample": f"16 tokens of a config-1 batch, repeated for >= 10 s, OpenMP over {cores} cores"}
 
     del graph
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank != 0:
-        return
+    prefill = None if args.no_prefill else prefill_section(args, dev, pk)
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
@@ -299,7 +457,7 @@ def run(args) -> None:
                    "K": K, "shared_expert": True, "router": "softmax top-10",
                    "l2": "flushed (256 MB write) before every timed step",
                    "timing": "CUDA graph replay per step, device events, max over ranks",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "parallelism": "single GPU",
                    "unique_experts_per_step": U},
         "roofline": {"bound": "hbm", "kernel": "gemv_gate_up", "achieved": achieved, "peak": pk["hbm_gbs"],
                      "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "peak_source": pk["source"],
@@ -310,6 +468,7 @@ def run(args) -> None:
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": B * H * 2, "d2h_bytes_per_step": B * H * 2},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
+        "prefill": prefill,
     }
     print(json.dumps(line), flush=True)
 
@@ -322,6 +481,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

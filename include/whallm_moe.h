@@ -101,7 +101,8 @@ typedef struct {
   int32_t max_inter;        /* largest I */
   int32_t max_experts;      /* largest E (routed experts) */
   int32_t max_topk;         /* largest K */
-  int32_t gemv_max_tokens;  /* T up to this runs the decode GEMV kernels; 0 = default 64, -1 = never */
+  int32_t gemv_max_tokens;  /* T up to this runs the decode kernels; -1 = never; 0 = automatic: the
+                               decode kernels while the expert rows average <= 32 per expert */
   int32_t flags;            /* reserved, 0 */
 } wm_options;
 
@@ -181,6 +182,20 @@ WM_EXPORT int wm_route(wm_ctx* ctx, const wm_moe_args* args, float* logits, int3
    StreamingExperts.__call__ (qwen4_exp.py:853-904) and
    _StreamingSwitchGLU.__call__ (model.py:325-501).  Uses args->routes_idx. */
 WM_EXPORT int wm_expert_pairs(wm_ctx* ctx, const wm_moe_args* args, void* routed, void* stream);
+
+/* Weighted combine of expert rows given in (token, k) order -- the step that
+   closes the MoE block (_route_reduce, model.py:545-546; MoE.__call__,
+   deepseek_v41/moe.py:110-112; moe_combine, QwenNative/kernels.metal:185-194):
+     out[t] = sum_k w[t, k] * pairs[t * K + k] + g_t * shared[t]   (bf16 out)
+   summed in fp32 in k order with the same arithmetic as wm_moe_forward's
+   combine, where g_t = sigmoid(x[t] . shared_gate_weight) for
+   WM_SHARED_SIGMOID_GATE, 1 for WM_SHARED_ONE, and no shared term for
+   WM_SHARED_NONE.  pairs bf16 [T * K, H], w fp32 [T, K], shared bf16 [T, H];
+   T <= the handle's max_tokens.  Used by the expert-parallel path, where the
+   expert rows come back from other GPUs. */
+WM_EXPORT int wm_combine(wm_ctx* ctx, int64_t T, int32_t H, int32_t K, const void* pairs, const float* w,
+                         const void* shared, int32_t shared_gate, const void* x, const void* shared_gate_weight,
+                         void* out, void* stream);
 
 /* The whole MoE block: route, sort, experts, shared expert, combine
    (SparseMoE.__call__, qwen4_exp.py:1015-1051; _streaming_moe, model.py:526-546;

@@ -188,10 +188,23 @@ bool encode_rows(wm_ctx* ctx, CUtensorMap* map, const void* base, int kdim) {
   return encode_rows_box(ctx, map, base, kdim, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 128);
 }
 
-// Whether a call of T tokens takes the tcgen05 grouped GEMM (else the GEMV kernels).
+// Expert rows per expert (on average) above which a call takes the grouped
+// GEMM: its 128-row tiles read each expert's weights once, the decode
+// kernels' 16-row tiles once per 16 rows.
+constexpr int64_t kDecodeMaxRowsPerExpert = 32;
+
+// Whether a call takes the tcgen05 grouped GEMM (else the decode kernels).
+// gemv_max_tokens: -1 always, > 0 above that many tokens, 0 by rows per expert.
 bool use_gemm(const wm_ctx* ctx, const wm_moe_args* a) {
   const int g = ctx->opt.gemv_max_tokens;
-  return (g < 0 || a->T > g) && wm::gemm_shape_ok(a->H, a->I) && ctx->encode_tiled != nullptr;
+  bool gemm;
+  if (g < 0)
+    gemm = true;
+  else if (g > 0)
+    gemm = a->T > g;
+  else
+    gemm = (a->T * int64_t(a->K) + a->E - 1) / a->E > kDecodeMaxRowsPerExpert;
+  return gemm && wm::gemm_shape_ok(a->H, a->I) && ctx->encode_tiled != nullptr;
 }
 
 enum Path { kPathGemv = 0, kPathDecode = 1, kPathGemm = 2 };
@@ -350,7 +363,6 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
     return nullptr;
   }
   wm_options o = *options;
-  if (o.gemv_max_tokens == 0) o.gemv_max_tokens = 64;
   if (o.max_tokens <= 0 || o.max_hidden <= 0 || o.max_inter <= 0 || o.max_experts <= 0 || o.max_topk <= 0) {
     report("every max_* option must be positive");
     return nullptr;
@@ -566,6 +578,37 @@ WM_EXPORT int wm_expert_pairs(wm_ctx* ctx, const wm_moe_args* a, void* routed, v
   ctx->counters.launches += 1;
   ctx->counters.calls_pairs += 1;
   return check_launch(ctx, "unpermute");
+}
+
+WM_EXPORT int wm_combine(wm_ctx* ctx, int64_t T, int32_t H, int32_t K, const void* pairs, const float* w,
+                         const void* shared, int32_t shared_gate, const void* x, const void* shared_gate_weight,
+                         void* out, void* stream) {
+  if (ctx == nullptr) return WM_ERROR;
+  if (T < 0 || T > ctx->opt.max_tokens) return fail(ctx, "T out of range for this handle");
+  if (T == 0) return WM_OK;
+  if (H <= 0 || H % 8 != 0 || H > ctx->opt.max_hidden) return fail(ctx, "H must be a positive multiple of 8 within max_hidden");
+  if (K <= 0 || K > ctx->opt.max_topk) return fail(ctx, "K out of range for this handle");
+  if (shared_gate != WM_SHARED_NONE && shared_gate != WM_SHARED_SIGMOID_GATE && shared_gate != WM_SHARED_ONE)
+    return fail(ctx, "unknown shared_gate");
+  if (pairs == nullptr || !aligned(pairs, 16) || out == nullptr || !aligned(out, 16) || w == nullptr)
+    return fail(ctx, "pairs and out must be 16-byte aligned device pointers, w non-null");
+  if (shared_gate != WM_SHARED_NONE && (shared == nullptr || !aligned(shared, 16)))
+    return fail(ctx, "the shared term needs 16-byte aligned shared rows");
+  if (shared_gate == WM_SHARED_SIGMOID_GATE && (x == nullptr || shared_gate_weight == nullptr))
+    return fail(ctx, "the sigmoid shared gate needs x and shared_gate_weight");
+  DeviceGuard guard(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (shared_gate == WM_SHARED_SIGMOID_GATE) {
+    wm::launch_router_logits(static_cast<const uint16_t*>(x), nullptr, static_cast<const uint16_t*>(shared_gate_weight),
+                             int(T), H, 0, nullptr, ctx->sg, s);
+    ctx->counters.launches += 1;
+  }
+  wm::prof_begin(&ctx->prof, wm::kProfCombine, s);
+  wm::launch_combine_dense(static_cast<const uint16_t*>(pairs), w, ctx->sg, shared_gate, int(T), H, K,
+                           static_cast<const uint16_t*>(shared), static_cast<uint16_t*>(out), s);
+  wm::prof_end(&ctx->prof, wm::kProfCombine, s);
+  ctx->counters.launches += 1;
+  return check_launch(ctx, "combine");
 }
 
 WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* a, void* stream) {

@@ -47,6 +47,9 @@ void launch_gather_rows(const uint16_t* x, const Plan& p, int E, int H, uint16_t
                         cudaStream_t stream);
 void launch_combine(const uint16_t* routed, const Plan& p, const float* w, const float* sg, int shared_kind, int T,
                     int H, int E, int K, uint16_t* out, cudaStream_t stream);
+// The same sum over pairs given in (t, k) order and shared rows [T, H].
+void launch_combine_dense(const uint16_t* pairs, const float* w, const float* sg, int shared_kind, int T, int H,
+                          int K, const uint16_t* shared_rows, uint16_t* out, cudaStream_t stream);
 void launch_unpermute(const uint16_t* routed, const Plan& p, int TK, int H, uint16_t* out, int num_sms,
                       cudaStream_t stream);
 

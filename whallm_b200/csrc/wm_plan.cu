@@ -273,9 +273,13 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
 // an fp32 sum in k order, rounded once to bf16 (qwen4_exp.py:1049-1051,
 // deepseek_v41/moe.py:110-112, QwenNative/kernels.metal:185-194).
 // g(t) = sg[t] (sigmoid gate) or 1.  Eight columns per thread.
+// DENSE: `routed` holds the pairs in (t, k) order and `shared_rows` the
+// shared expert's rows; otherwise both come from the plan's sorted rows.
+template <bool DENSE>
 __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict__ routed, Plan p,
                                                       const float* __restrict__ w, const float* __restrict__ sg,
                                                       int shared_kind, int T, int H, int E, int K,
+                                                      const uint16_t* __restrict__ shared_rows,
                                                       uint16_t* __restrict__ out) {
   const int t = blockIdx.y;
   const int h0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
@@ -291,7 +295,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int k = k0 + j;
-      pos[j] = k < K ? p.pair_pos[(int64_t)t * K + k] : -1;
+      pos[j] = k < K ? (DENSE ? t * K + k : p.pair_pos[(int64_t)t * K + k]) : -1;
       wk[j] = k < K ? w[(int64_t)t * K + k] : 0.0f;
     }
 #pragma unroll
@@ -309,7 +313,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict
   }
   if (shared_kind != WM_SHARED_NONE) {
     const float g = shared_kind == WM_SHARED_SIGMOID_GATE ? sg[t] : 1.0f;
-    const uint4 v = *reinterpret_cast<const uint4*>(routed + (int64_t)(p.offsets[E] + t) * H + h0);
+    const uint16_t* srow = DENSE ? shared_rows + (int64_t)t * H : routed + (int64_t)(p.offsets[E] + t) * H;
+    const uint4 v = *reinterpret_cast<const uint4*>(srow + h0);
     float2 f;
     f = unpack_bf16x2(v.x); acc[0] = fmaf(g, f.x, acc[0]); acc[1] = fmaf(g, f.y, acc[1]);
     f = unpack_bf16x2(v.y); acc[2] = fmaf(g, f.x, acc[2]); acc[3] = fmaf(g, f.y, acc[3]);
@@ -373,7 +378,13 @@ void launch_gather_rows(const uint16_t* x, const Plan& p, int E, int H, uint16_t
 void launch_combine(const uint16_t* routed, const Plan& p, const float* w, const float* sg, int shared_kind, int T,
                     int H, int E, int K, uint16_t* out, cudaStream_t stream) {
   dim3 grid((H / 8 + 255) / 256, T);
-  combine_kernel<<<grid, 256, 0, stream>>>(routed, p, w, sg, shared_kind, T, H, E, K, out);
+  combine_kernel<false><<<grid, 256, 0, stream>>>(routed, p, w, sg, shared_kind, T, H, E, K, nullptr, out);
+}
+
+void launch_combine_dense(const uint16_t* pairs, const float* w, const float* sg, int shared_kind, int T, int H,
+                          int K, const uint16_t* shared_rows, uint16_t* out, cudaStream_t stream) {
+  dim3 grid((H / 8 + 255) / 256, T);
+  combine_kernel<true><<<grid, 256, 0, stream>>>(pairs, Plan{}, w, sg, shared_kind, T, H, 0, K, shared_rows, out);
 }
 
 void launch_unpermute(const uint16_t* routed, const Plan& p, int TK, int H, uint16_t* out, int num_sms,

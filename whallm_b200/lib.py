@@ -21,7 +21,7 @@ SHARED_NONE, SHARED_SIGMOID_GATE, SHARED_ONE = 0, 1, 2
 # Every entry point the header declares (checked by the CPU test suite).
 EXPORTS = (
     "wm_create", "wm_destroy", "wm_error", "wm_sync", "wm_counters_get",
-    "wm_dequant", "wm_route", "wm_expert_pairs", "wm_moe_forward",
+    "wm_dequant", "wm_route", "wm_expert_pairs", "wm_combine", "wm_moe_forward",
     "wm_profile_enable", "wm_profile_read", "wm_profile_reset",
     "wm_moe_forward_noalloc",
 )
@@ -96,6 +96,7 @@ def load() -> ctypes.CDLL:
     L.wm_route.argtypes = [_P, ctypes.POINTER(MoeArgs), _P, _P, _P, _P]
     L.wm_expert_pairs.argtypes = [_P, ctypes.POINTER(MoeArgs), _P, _P]
     L.wm_moe_forward.argtypes = [_P, ctypes.POINTER(MoeArgs), _P]
+    L.wm_combine.argtypes = [_P, _I64, _I32, _I32, _P, _P, _P, _I32, _P, _P, _P, _P]
     L.wm_profile_enable.argtypes = [_P, _I32]
     L.wm_profile_enable.restype = ctypes.c_int
     L.wm_profile_read.argtypes = [_P, ctypes.POINTER(ProfileEntry), _I32]
@@ -104,7 +105,7 @@ def load() -> ctypes.CDLL:
     L.wm_profile_reset.restype = None
     L.wm_moe_forward_noalloc.argtypes = [ctypes.POINTER(MoeArgs), _P, ctypes.c_char_p, ctypes.c_size_t]
     L.wm_moe_forward_noalloc.restype = ctypes.c_int
-    for name in ("wm_sync", "wm_dequant", "wm_route", "wm_expert_pairs", "wm_moe_forward"):
+    for name in ("wm_sync", "wm_dequant", "wm_route", "wm_expert_pairs", "wm_combine", "wm_moe_forward"):
         getattr(L, name).restype = ctypes.c_int
     _lib = L
     return L
@@ -176,6 +177,11 @@ class Context:
 
     def expert_pairs(self, args: MoeArgs, routed: int, stream: int | None) -> None:
         self.check(self._lib.wm_expert_pairs(self.handle, ctypes.byref(args), routed, stream))
+
+    def combine(self, T: int, H: int, K: int, pairs: int, w: int, shared: int | None, shared_gate: int,
+                x: int | None, shared_gate_weight: int | None, out: int, stream: int | None) -> None:
+        self.check(self._lib.wm_combine(self.handle, T, H, K, pairs, w, shared, shared_gate, x, shared_gate_weight,
+                                        out, stream))
 
     def moe_forward(self, args: MoeArgs, stream: int | None) -> None:
         self.check(self._lib.wm_moe_forward(self.handle, ctypes.byref(args), stream))

@@ -68,6 +68,22 @@ class LayerWeights:
         layout, w13, w2 = projections(batched)
         return LayerWeights(layout, H, I, w13.weight.shape[0], w13, w2, keep=[batched], **kw)
 
+    def experts(self, e0: int, e1: int) -> "LayerWeights":
+        """Routed experts [e0, e1) only (views, no copy): an expert-parallel shard."""
+        if not 0 <= e0 < e1 <= self.E:
+            raise ValueError(f"expert range [{e0}, {e1}) outside [0, {self.E})")
+        def cut(p: Projection) -> Projection:
+            return Projection(p.weight[e0:e1], p.weight_stride, p.scale[e0:e1], p.scale_stride)
+        return LayerWeights(self.layout, self.H, self.I, e1 - e0, cut(self.w13), cut(self.w2),
+                            swiglu_limit=self.swiglu_limit, keep=self.keep)
+
+    def shared_only(self) -> "LayerWeights":
+        """The shared expert as a one-expert layer."""
+        if self.shared is None:
+            raise ValueError("the layer has no shared expert")
+        return LayerWeights(self.layout, self.H, self.I, 1, self.shared.w13, self.shared.w2,
+                            swiglu_limit=self.swiglu_limit, keep=self.keep)
+
 
 def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
@@ -178,6 +194,22 @@ class Engine:
         self.ctx.moe_forward(a, _stream())
         if return_routes:
             return out, (rw, ri)
+        return out
+
+    def combine(self, pairs: torch.Tensor, w: torch.Tensor, shared_rows: torch.Tensor | None = None,
+                shared_gate: int = lib.SHARED_NONE, x: torch.Tensor | None = None,
+                gate_weight: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+        """out[t] = sum_k w[t, k] * pairs[t, k] + g_t * shared_rows[t] (bf16 [T, H]), the
+        same arithmetic as forward's combine; pairs bf16 [T, K, H] in (t, k) order."""
+        T, K, H = pairs.shape
+        _check_bf16("pairs", pairs, (T, K, H))
+        w = w.reshape(T, K).to(torch.float32).contiguous()
+        if shared_gate != lib.SHARED_NONE:
+            _check_bf16("shared_rows", shared_rows, (T, H))
+        if out is None:
+            out = torch.empty((T, H), dtype=torch.bfloat16, device=pairs.device)
+        self.ctx.combine(T, H, K, pairs.data_ptr(), w.data_ptr(), _ptr(shared_rows), shared_gate, _ptr(x),
+                         _ptr(gate_weight), out.data_ptr(), _stream())
         return out
 
     def dequant(self, fmt: int, weight: torch.Tensor, scale: torch.Tensor, rows: int, cols: int,
