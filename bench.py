@@ -219,7 +219,7 @@ def run_ep(args, world: int, rank: int, local: int) -> None:
     import torch
     import torch.distributed as dist
 
-    from whallm_b200 import synth
+    from whallm_b200 import lib, synth
     from whallm_b200.ep import ExpertParallelMoE
     from whallm_b200.moe import Engine
 
@@ -231,32 +231,64 @@ def run_ep(args, world: int, rank: int, local: int) -> None:
     xs = [synth.activations(B, H, torch.Generator(device=dev).manual_seed(1000 * rank + i), dev) for i in range(nb)]
     # rows a rank receives are at most all ranks' pairs; decode kernels throughout
     cap = world * B * K
-    eng = Engine(local, max_tokens=cap, hidden=H, inter=I, experts=E, topk=K, gemv_max_tokens=cap)
-    ep = ExpertParallelMoE(eng, layer, K)
+    eng = Engine(local, max_tokens=cap, hidden=H, inter=I, experts=E, topk=K, gemv_max_tokens=cap,
+                 flags=lib.FLAG_SKIP_NEGATIVE_ROUTES)
+    shared_eng = Engine(local, max_tokens=B, hidden=H, inter=I, experts=1, topk=1, gemv_max_tokens=B)
+    # fixed-size exchanges (B * K slots per peer): no host round trip, so a
+    # whole step is one CUDA graph (router, plan, 3 all-to-alls, experts,
+    # shared expert on a side stream, combine)
+    ep = ExpertParallelMoE(eng, layer, K, shared_engine=shared_eng, fixed_capacity=B)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    x_static = xs[0].clone()
 
     def fwd(x):
         return ep(x)
 
-    for i in range(args.warmup):
-        fwd(xs[i % nb])
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            fwd(xs[i % nb])
     torch.cuda.synchronize()
-    c0 = eng.ctx.counters().launches
-    fwd(xs[0])
+    c0 = eng.ctx.counters().launches + shared_eng.ctx.counters().launches
+    with torch.cuda.stream(stream):
+        fwd(xs[0])
     torch.cuda.synchronize()
-    launches_per_step = eng.ctx.counters().launches - c0
+    launches_per_step = eng.ctx.counters().launches + shared_eng.ctx.counters().launches - c0
+    graph, graph_error = None, None
+    try:
+        with torch.cuda.stream(stream):
+            fwd(x_static)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            out_static = fwd(x_static)
+        torch.cuda.synchronize()
+    except Exception as exc:  # eager steps then
+        graph, graph_error = None, f"{type(exc).__name__}: {exc}"[:200]
+        torch.cuda.synchronize()
     dist.barrier()
+
+    def step(i, ev=None):
+        if graph is not None:
+            x_static.copy_(xs[i % nb])
+        flush.zero_()
+        if ev is not None:
+            ev[0].record(stream)
+        if graph is not None:
+            graph.replay()
+        else:
+            fwd(xs[i % nb])
+        if ev is not None:
+            ev[1].record(stream)
+
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    recv = []
     with Clocks(local) as clocks:
         torch.cuda.synchronize()
-        for i in range(args.steps):
-            flush.zero_()
-            dist.barrier()
-            evs[i][0].record()
-            fwd(xs[i % nb])
-            evs[i][1].record()
-            recv.append(ep.stats.received)
+        with torch.cuda.stream(stream):
+            for i in range(args.warmup):
+                step(i)
+            for i in range(args.steps):
+                step(i, evs[i])
         torch.cuda.synchronize()
     ms = sum(a.elapsed_time(b) for a, b in evs)
     t = torch.tensor([ms], device=dev)
@@ -267,30 +299,46 @@ def run_ep(args, world: int, rank: int, local: int) -> None:
     # per-kernel durations on this rank (library CUDA events), eager
     eng.ctx.profile(True)
     eng.ctx.profile_reset()
-    for i in range(args.steps):
-        flush.zero_()
-        fwd(xs[i % nb])
+    with torch.cuda.stream(stream):
+        for i in range(args.steps):
+            flush.zero_()
+            fwd(xs[i % nb])
     torch.cuda.synchronize()
     prof = eng.ctx.profile_read()
     eng.ctx.profile(False)
     kernels = {name: {"launches": n, "avg_us": 1e3 * tt / n} for name, (n, tt) in prof.items()}
+    # the same steps' host-side time split (rank 0): where an eager step goes
+    t_host = []
+    with torch.cuda.stream(stream):
+        for i in range(min(args.steps, 10)):
+            torch.cuda.synchronize()
+            h0 = time.perf_counter()
+            fwd(xs[i % nb])
+            torch.cuda.synchronize()
+            t_host.append(1e3 * (time.perf_counter() - h0))
 
     # end to end with pinned host buffers
     xh = [x.cpu().pin_memory() for x in xs]
     oh = torch.empty((B, H), dtype=torch.bfloat16).pin_memory()
     e_evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    for i in range(args.steps):
-        flush.zero_()
-        dist.barrier()
-        e_evs[i][0].record()
-        oh.copy_(fwd(xh[i % nb].to(dev, non_blocking=True)), non_blocking=True)
-        e_evs[i][1].record()
+    with torch.cuda.stream(stream):
+        for i in range(args.steps):
+            flush.zero_()
+            e_evs[i][0].record(stream)
+            if graph is not None:
+                x_static.copy_(xh[i % nb], non_blocking=True)
+                graph.replay()
+                oh.copy_(out_static, non_blocking=True)
+            else:
+                oh.copy_(fwd(xh[i % nb].to(dev, non_blocking=True)), non_blocking=True)
+            e_evs[i][1].record(stream)
     torch.cuda.synchronize()
     e_ms = sum(a.elapsed_time(b) for a, b in e_evs)
     t = torch.tensor([e_ms], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e_ms = float(t.item())
     e2e = world * B * args.steps / (e_ms / 1e3)
+    del graph  # holds NCCL work: release before the process group goes
     dist.barrier()
     dist.destroy_process_group()
     if rank != 0:
@@ -303,9 +351,12 @@ def run_ep(args, world: int, rank: int, local: int) -> None:
         "config": {"workload": f"config1 decode layer, {B} tokens per step per GPU", "H": H, "I": I, "E": E,
                    "K": K, "shared_expert": True, "router": "softmax top-10",
                    "l2": "flushed (256 MB write) before every timed step",
-                   "timing": "eager steps, device events, max over ranks",
+                   "timing": ("CUDA graph replay per step" if graph_error is None else "eager steps")
+                   + ", device events, max over ranks",
+                   "graph_error": graph_error,
                    "parallelism": f"expert-parallel x{world} ({E // world} experts per GPU), NCCL all-to-all",
-                   "pairs_received_per_step_rank0": statistics.mean(recv)},
+                   "exchange": f"fixed {B * K} slots per peer each way",
+                   "wall_ms_per_step_rank0": statistics.median(t_host)},
         "roofline": None,
         "kernels": kernels,
         "cpu_baseline": None,

@@ -103,8 +103,13 @@ typedef struct {
   int32_t max_topk;         /* largest K */
   int32_t gemv_max_tokens;  /* T up to this runs the decode kernels; -1 = never; 0 = automatic: the
                                decode kernels while the expert rows average <= 32 per expert */
-  int32_t flags;            /* reserved, 0 */
+  int32_t flags;            /* WM_FLAG_* bits, else 0 */
 } wm_options;
+
+/* Routes with a negative expert id are padding: they get no row and a zero
+   output row (wm_expert_pairs), instead of an error.  For fixed-capacity
+   exchange buffers (the expert-parallel path). */
+#define WM_FLAG_SKIP_NEGATIVE_ROUTES 1
 
 /* One projection of every expert: expert e's matrix at weight + e * weight_stride
    bytes, its scales at scale + e * scale_stride bytes (device pointers). */
@@ -191,11 +196,28 @@ WM_EXPORT int wm_expert_pairs(wm_ctx* ctx, const wm_moe_args* args, void* routed
    combine, where g_t = sigmoid(x[t] . shared_gate_weight) for
    WM_SHARED_SIGMOID_GATE, 1 for WM_SHARED_ONE, and no shared term for
    WM_SHARED_NONE.  pairs bf16 [T * K, H], w fp32 [T, K], shared bf16 [T, H];
-   T <= the handle's max_tokens.  Used by the expert-parallel path, where the
-   expert rows come back from other GPUs. */
-WM_EXPORT int wm_combine(wm_ctx* ctx, int64_t T, int32_t H, int32_t K, const void* pairs, const float* w,
-                         const void* shared, int32_t shared_gate, const void* x, const void* shared_gate_weight,
-                         void* out, void* stream);
+   T <= the handle's max_tokens.  pair_pos int32 [T * K] (optional): pair
+   (t, k) is row pair_pos[t * K + k] of `pairs` instead of row t * K + k.
+   Used by the expert-parallel path, where the expert rows come back from
+   other GPUs in send order. */
+WM_EXPORT int wm_combine(wm_ctx* ctx, int64_t T, int32_t H, int32_t K, const void* pairs, const int32_t* pair_pos,
+                         const float* w, const void* shared, int32_t shared_gate, const void* x,
+                         const void* shared_gate_weight, void* out, void* stream);
+
+/* Expert-parallel dispatch plan for T tokens with routes idx int32 [T, K]
+   over `world` ranks that hold `experts_per_rank` consecutive experts each:
+   orders the pairs by owning rank (stable: (t, k) order within a rank) and
+   writes send_counts int32 [world] (pairs per rank), pair_pos int32 [T * K]
+   (slot of pair (t, k)), send_eid int32 (expert id local to its owner, per
+   slot) and send_x bf16 [slots, H] (x[t] per slot).  capacity 0: the slots
+   are packed, T * K of them.  capacity C >= T * K: rank r's pairs take slots
+   [r * C, r * C + count_r) of world * C slots, unused slots get expert id -1
+   (fixed-size exchanges, no host round trip; see
+   WM_FLAG_SKIP_NEGATIVE_ROUTES).  No counterpart in the reference, whose
+   experts run on one device. */
+WM_EXPORT int wm_ep_plan(wm_ctx* ctx, int64_t T, int32_t K, int32_t experts_per_rank, int32_t world,
+                         int32_t capacity, const int32_t* idx, const void* x, int32_t H, int32_t* send_counts,
+                         int32_t* pair_pos, int32_t* send_eid, void* send_x, void* stream);
 
 /* The whole MoE block: route, sort, experts, shared expert, combine
    (SparseMoE.__call__, qwen4_exp.py:1015-1051; _streaming_moe, model.py:526-546;

@@ -55,13 +55,39 @@ class CpuEngine:
         for t in range(T):
             for k in range(idx.shape[1]):
                 e = int(idx[t, k])
+                if e < 0:  # padding slot of a fixed-capacity exchange
+                    out[t, k] = 0
+                    continue
                 gu = layer.w13.weight[e].double() @ x[t].double()
                 act = torch.nn.functional.silu(gu[:layer.I]) * gu[layer.I:]
                 out[t, k] = (layer.w2.weight[e].double() @ act).to(torch.bfloat16)
         return out
 
-    def combine(self, pairs, w, shared_rows=None, shared_gate=lib.SHARED_NONE, x=None, gate_weight=None):
-        T, k, _ = pairs.shape
+    def ep_plan(self, idx, x, per_rank, world, capacity=0):
+        T, k = idx.shape
+        owner = (idx.reshape(-1).long() // per_rank)
+        order = torch.argsort(owner, stable=True)
+        pair_pos = torch.empty_like(order)
+        pair_pos[order] = torch.arange(order.numel())
+        counts = torch.bincount(owner, minlength=world).to(torch.int32)
+        send_eid = (idx.reshape(-1).long()[order] % per_rank).to(torch.int32)
+        send_x = x[order // k]
+        if capacity:
+            starts = torch.cumsum(counts, 0) - counts
+            slot = owner[order] * capacity + (torch.arange(order.numel()) - starts[owner[order]])
+            eid = torch.full((world * capacity,), -1, dtype=torch.int32)
+            rows = torch.zeros((world * capacity, x.shape[1]), dtype=x.dtype)
+            eid[slot] = send_eid
+            rows[slot] = send_x
+            pair_pos[order] = slot
+            send_eid, send_x = eid, rows
+        return counts, pair_pos.view(T, k).to(torch.int32), send_eid, send_x
+
+    def combine(self, pairs, w, shared_rows=None, shared_gate=lib.SHARED_NONE, x=None, gate_weight=None,
+                pair_pos=None):
+        T, k = w.shape
+        if pair_pos is not None:
+            pairs = pairs[pair_pos.reshape(-1).long()].view(T, k, -1)
         acc = torch.zeros((T, pairs.shape[2]), dtype=torch.float32)
         for j in range(k):
             acc = acc + w[:, j:j + 1] * pairs[:, j].float()
@@ -85,7 +111,7 @@ def _tokens(rank: int, n: int) -> torch.Tensor:
     return torch.randn((n, H), generator=torch.Generator().manual_seed(100 + rank)).to(torch.bfloat16)
 
 
-def _worker(rank: int, world: int, port: int, shared: bool, skew: bool, q) -> None:
+def _worker(rank: int, world: int, port: int, shared: bool, skew: bool, fixed: bool, q) -> None:
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -100,7 +126,7 @@ def _worker(rank: int, world: int, port: int, shared: bool, skew: bool, q) -> No
         x = _tokens(rank, 5 + 4 * rank)  # uneven token counts per rank
         if skew:
             x[:, 0] = 1.0
-        ep = ExpertParallelMoE(eng, layer, K)
+        ep = ExpertParallelMoE(eng, layer, K, fixed_capacity=16 if fixed else 0)
         got = ep(x)
         want = eng.forward(layer, x, K)
         q.put((rank, bool(torch.equal(got, want)), ep.stats.sent, ep.stats.received))
@@ -114,13 +140,14 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("shared,skew", [(True, False), (False, False), (True, True)])
-def test_ep_matches_single_process(shared, skew):
+@pytest.mark.parametrize("shared,skew,fixed", [(True, False, False), (False, False, False), (True, True, False),
+                                               (True, False, True), (True, True, True)])
+def test_ep_matches_single_process(shared, skew, fixed):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     world = 2
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, shared, skew, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, shared, skew, fixed, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=120) for _ in range(world)]
@@ -130,7 +157,8 @@ def test_ep_matches_single_process(shared, skew):
     results.sort()
     for rank, equal, sent, received in results:
         assert equal, f"rank {rank}: expert-parallel output differs from the single-process layer"
-        assert sent == (5 + 4 * rank) * K
-    if skew:
+        if not fixed:
+            assert sent == (5 + 4 * rank) * K
+    if skew and not fixed:
         assert results[1][3] == 0  # rank 1 owns no chosen expert
 

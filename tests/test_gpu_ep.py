@@ -13,7 +13,7 @@ import torch.multiprocessing as mp
 
 import oracle
 from oracle import adapter
-from whallm_b200 import synth
+from whallm_b200 import lib, synth
 from whallm_b200.moe import Engine
 
 pytestmark = pytest.mark.gpu
@@ -29,21 +29,28 @@ def _free_port() -> int:
 
 def _engine(dev: int, world: int) -> Engine:
     cap = world * B * K
-    return Engine(dev, max_tokens=cap, hidden=H, inter=I, experts=E, topk=K, gemv_max_tokens=cap)
+    return Engine(dev, max_tokens=cap, hidden=H, inter=I, experts=E, topk=K, gemv_max_tokens=cap,
+                  flags=lib.FLAG_SKIP_NEGATIVE_ROUTES)
 
 
-def test_ep_one_rank_equals_forward():
+def _shared_engine(dev: int) -> Engine:
+    return Engine(dev, max_tokens=B, hidden=H, inter=I, experts=1, topk=1, gemv_max_tokens=B)
+
+
+@pytest.mark.parametrize("fixed", [0, B])
+def test_ep_one_rank_equals_forward(fixed):
     from whallm_b200.ep import ExpertParallelMoE
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{_free_port()}", rank=0, world_size=1,
                             device_id=torch.device("cuda", 0))
     try:
         wl = synth.config(1, device="cuda", batch=B)
         eng = _engine(0, 1)
-        ep = ExpertParallelMoE(eng, wl.layer, K)
+        ep = ExpertParallelMoE(eng, wl.layer, K, shared_engine=_shared_engine(0), fixed_capacity=fixed)
         got = ep(wl.x)
         want, (w, idx) = eng.forward(wl.layer, wl.x, K, return_routes=True)
         eng.sync()
-        assert ep.stats.sent == B * K and ep.stats.received == B * K
+        if not fixed:
+            assert ep.stats.sent == B * K and ep.stats.received == B * K
         assert torch.equal(got, want), "expert-parallel layer (one rank) differs from the single-GPU layer"
         tokens = np.arange(8, dtype=np.int32)
         layer_np = adapter.from_layer(wl.layer)
@@ -54,7 +61,7 @@ def test_ep_one_rank_equals_forward():
         dist.destroy_process_group()
 
 
-def _worker(rank: int, world: int, port: int, q) -> None:
+def _worker(rank: int, world: int, port: int, fixed: int, q) -> None:
     from whallm_b200.ep import ExpertParallelMoE
     torch.cuda.set_device(rank)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -66,7 +73,7 @@ def _worker(rank: int, world: int, port: int, q) -> None:
         wl = synth.config(1, device=dev, batch=B)
         x = synth.activations(B, H, torch.Generator(device=dev).manual_seed(77 + rank), dev)
         eng = _engine(rank, world)
-        got = ExpertParallelMoE(eng, wl.layer, K)(x)
+        got = ExpertParallelMoE(eng, wl.layer, K, shared_engine=_shared_engine(rank), fixed_capacity=fixed)(x)
         want = eng.forward(wl.layer, x, K)
         eng.sync()
         q.put((rank, bool(torch.equal(got, want)), float((got.float() - want.float()).abs().max())))
@@ -75,11 +82,12 @@ def _worker(rank: int, world: int, port: int, q) -> None:
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_ep_two_ranks_equal_single_gpu():
+@pytest.mark.parametrize("fixed", [0, B])
+def test_ep_two_ranks_equal_single_gpu(fixed):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, fixed, q)) for r in range(2)]
     for p in procs:
         p.start()
     res = sorted(q.get(timeout=300) for _ in range(2))

@@ -363,6 +363,10 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
     return nullptr;
   }
   wm_options o = *options;
+  if (o.flags & ~int32_t(WM_FLAG_SKIP_NEGATIVE_ROUTES)) {
+    report("unknown flags");
+    return nullptr;
+  }
   if (o.max_tokens <= 0 || o.max_hidden <= 0 || o.max_inter <= 0 || o.max_experts <= 0 || o.max_topk <= 0) {
     report("every max_* option must be positive");
     return nullptr;
@@ -566,6 +570,7 @@ WM_EXPORT int wm_expert_pairs(wm_ctx* ctx, const wm_moe_args* a, void* routed, v
   const Path path = expert_path(ctx, &b, false);
   wm::Plan plan = ctx->plan;
   if (path == kPathDecode) plan.rowmax = ctx->rowmax;
+  plan.skip_negative = (ctx->opt.flags & WM_FLAG_SKIP_NEGATIVE_ROUTES) ? 1 : 0;
   int launches = 0;
   wm::prof_begin(&ctx->prof, wm::kProfPlan, s);
   wm::launch_plan(b.routes_idx, b.T, b.K, b.E, false, path == kPathGemm ? wm::kTileM : 1, plan, ctx->max_rows,
@@ -580,9 +585,9 @@ WM_EXPORT int wm_expert_pairs(wm_ctx* ctx, const wm_moe_args* a, void* routed, v
   return check_launch(ctx, "unpermute");
 }
 
-WM_EXPORT int wm_combine(wm_ctx* ctx, int64_t T, int32_t H, int32_t K, const void* pairs, const float* w,
-                         const void* shared, int32_t shared_gate, const void* x, const void* shared_gate_weight,
-                         void* out, void* stream) {
+WM_EXPORT int wm_combine(wm_ctx* ctx, int64_t T, int32_t H, int32_t K, const void* pairs, const int32_t* pair_pos,
+                         const float* w, const void* shared, int32_t shared_gate, const void* x,
+                         const void* shared_gate_weight, void* out, void* stream) {
   if (ctx == nullptr) return WM_ERROR;
   if (T < 0 || T > ctx->opt.max_tokens) return fail(ctx, "T out of range for this handle");
   if (T == 0) return WM_OK;
@@ -604,11 +609,43 @@ WM_EXPORT int wm_combine(wm_ctx* ctx, int64_t T, int32_t H, int32_t K, const voi
     ctx->counters.launches += 1;
   }
   wm::prof_begin(&ctx->prof, wm::kProfCombine, s);
-  wm::launch_combine_dense(static_cast<const uint16_t*>(pairs), w, ctx->sg, shared_gate, int(T), H, K,
+  wm::launch_combine_dense(static_cast<const uint16_t*>(pairs), pair_pos, w, ctx->sg, shared_gate, int(T), H, K,
                            static_cast<const uint16_t*>(shared), static_cast<uint16_t*>(out), s);
   wm::prof_end(&ctx->prof, wm::kProfCombine, s);
   ctx->counters.launches += 1;
   return check_launch(ctx, "combine");
+}
+
+WM_EXPORT int wm_ep_plan(wm_ctx* ctx, int64_t T, int32_t K, int32_t experts_per_rank, int32_t world,
+                         int32_t capacity, const int32_t* idx, const void* x, int32_t H, int32_t* send_counts,
+                         int32_t* pair_pos, int32_t* send_eid, void* send_x, void* stream) {
+  if (ctx == nullptr) return WM_ERROR;
+  if (T < 0 || T > ctx->opt.max_tokens) return fail(ctx, "T out of range for this handle");
+  if (K <= 0 || K > ctx->opt.max_topk) return fail(ctx, "K out of range for this handle");
+  if (world <= 0 || world > ctx->opt.max_experts || experts_per_rank <= 0)
+    return fail(ctx, "world must be in [1, max_experts] and experts_per_rank positive");
+  if (H <= 0 || H % 8 != 0 || H > ctx->opt.max_hidden) return fail(ctx, "H must be a positive multiple of 8 within max_hidden");
+  if (capacity != 0 && capacity < T * K) return fail(ctx, "capacity below T * K could drop pairs");
+  if (T == 0) return WM_OK;
+  if (idx == nullptr || x == nullptr || send_counts == nullptr || pair_pos == nullptr || send_eid == nullptr ||
+      send_x == nullptr || !aligned(x, 16) || !aligned(send_x, 16))
+    return fail(ctx, "wm_ep_plan needs device buffers (x and send_x 16-byte aligned)");
+  DeviceGuard guard(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int P = int(T) * K;
+  int launches = 0;
+  wm::launch_ep_owner(idx, P, experts_per_rank, world, ctx->idx, ctx->status, ctx->num_sms, s);
+  wm::Plan plan = ctx->plan;
+  plan.rowmax = nullptr;
+  wm::launch_plan(ctx->idx, int(T), K, world, false, 1, plan, ctx->max_rows, ctx->max_mtiles, ctx->max_chunks,
+                  ctx->status, s, &launches);
+  wm::launch_ep_finish(idx, plan, int(T), K, experts_per_rank, world, capacity, send_counts, pair_pos, send_eid,
+                       static_cast<const uint16_t*>(x), H, static_cast<uint16_t*>(send_x), ctx->num_sms, s);
+  if (capacity == 0)
+    wm::launch_gather_rows(static_cast<const uint16_t*>(x), plan, world, H, static_cast<uint16_t*>(send_x),
+                           ctx->num_sms, s);
+  ctx->counters.launches += launches + (capacity == 0 ? 3 : 2);
+  return check_launch(ctx, "expert-parallel plan");
 }
 
 WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* a, void* stream) {
@@ -622,6 +659,7 @@ WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* a, void* stream) {
   const Path path = expert_path(ctx, a, has_shared);
   wm::Plan plan = ctx->plan;
   if (path == kPathDecode) plan.rowmax = ctx->rowmax;
+  plan.skip_negative = (ctx->opt.flags & WM_FLAG_SKIP_NEGATIVE_ROUTES) ? 1 : 0;
   const int32_t* idx;
   const float* w;
   if (a->router_weight != nullptr) {

@@ -47,9 +47,18 @@ void launch_gather_rows(const uint16_t* x, const Plan& p, int E, int H, uint16_t
                         cudaStream_t stream);
 void launch_combine(const uint16_t* routed, const Plan& p, const float* w, const float* sg, int shared_kind, int T,
                     int H, int E, int K, uint16_t* out, cudaStream_t stream);
-// The same sum over pairs given in (t, k) order and shared rows [T, H].
-void launch_combine_dense(const uint16_t* pairs, const float* w, const float* sg, int shared_kind, int T, int H,
-                          int K, const uint16_t* shared_rows, uint16_t* out, cudaStream_t stream);
+// The same sum over pairs at rows pair_pos[t * K + k] (t * K + k when null)
+// and shared rows [T, H].
+void launch_combine_dense(const uint16_t* pairs, const int32_t* pair_pos, const float* w, const float* sg,
+                          int shared_kind, int T, int H, int K, const uint16_t* shared_rows, uint16_t* out,
+                          cudaStream_t stream);
+// Expert-parallel dispatch plan: owners of the pairs, then (after a plan over
+// owners) slots, owner-local expert ids and per-owner counts.
+void launch_ep_owner(const int32_t* idx, int P, int per_rank, int world, int32_t* owner, uint32_t* status,
+                     int num_sms, cudaStream_t stream);
+void launch_ep_finish(const int32_t* idx, const Plan& p, int T, int K, int per_rank, int world, int capacity,
+                      int32_t* send_counts, int32_t* pair_pos, int32_t* send_eid, const uint16_t* x, int H,
+                      uint16_t* send_x, int num_sms, cudaStream_t stream);
 void launch_unpermute(const uint16_t* routed, const Plan& p, int TK, int H, uint16_t* out, int num_sms,
                       cudaStream_t stream);
 

@@ -107,32 +107,34 @@ __device__ void finish_plan(const int* cnt, int* off, int E, int align, Plan p, 
 // experts within a token keep k order (ranked with __match_any_sync).
 __device__ void scatter_pairs(const int32_t* idx, int t_begin, int t_end, int K, int E, int* run, Plan p,
                               uint32_t* status) {
+  // Pairs in flat (t, k) order, 32 per step: a pair's slot is its expert's
+  // running count plus the number of earlier lanes naming the same expert,
+  // so the order within an expert stays the flat pair order.
   const int lane = threadIdx.x & 31;
   const unsigned lt_mask = (1u << lane) - 1u;
-  for (int t = t_begin; t < t_end; ++t) {
-    for (int k0 = 0; k0 < K; k0 += 32) {
-      const int k = k0 + lane;
-      int e = -1;
-      if (k < K) {
-        e = idx[(int64_t)t * K + k];
-        if (e < 0 || e >= E) {
-          report_status(status, kStatusBadExpert, (uint32_t)(t * K + k));
-          p.pair_pos[(int64_t)t * K + k] = -1;
-          e = -1;
-        }
+  const int i_end = t_end * K;
+  for (int i0 = t_begin * K; i0 < i_end; i0 += 32) {
+    const int i = i0 + lane;
+    int e = -1;
+    if (i < i_end) {
+      e = idx[i];
+      if (e < 0 || e >= E) {
+        if (e >= 0 || !p.skip_negative) report_status(status, kStatusBadExpert, (uint32_t)i);
+        p.pair_pos[i] = -1;
+        e = -1;
       }
-      const unsigned same = __match_any_sync(0xffffffffu, e);
-      const int rank = __popc(same & lt_mask);
-      const int base = e >= 0 ? run[e] : 0;
-      if (e >= 0) {
-        const int pos = base + rank;
-        p.pair_pos[(int64_t)t * K + k] = pos;
-        p.row_token[pos] = t;
-      }
-      __syncwarp();
-      if (e >= 0 && rank == 0) run[e] = base + __popc(same);
-      __syncwarp();
     }
+    const unsigned same = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(same & lt_mask);
+    const int base = e >= 0 ? run[e] : 0;
+    if (e >= 0) {
+      const int pos = base + rank;
+      p.pair_pos[i] = pos;
+      p.row_token[pos] = i / K;
+    }
+    __syncwarp();
+    if (e >= 0 && rank == 0) run[e] = base + __popc(same);
+    __syncwarp();
   }
 }
 
@@ -183,7 +185,7 @@ __global__ void __launch_bounds__(1024) plan_small_kernel(const int32_t* __restr
       for (int i = threadIdx.x; i < T * K; i += blockDim.x) {
         const int e = idx[i], t = i / K;
         if (e < 0 || e >= E) {
-          report_status(status, kStatusBadExpert, (uint32_t)i);
+          if (e >= 0 || !p.skip_negative) report_status(status, kStatusBadExpert, (uint32_t)i);
           p.pair_pos[i] = -1;
           continue;
         }
@@ -273,7 +275,8 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
 // an fp32 sum in k order, rounded once to bf16 (qwen4_exp.py:1049-1051,
 // deepseek_v41/moe.py:110-112, QwenNative/kernels.metal:185-194).
 // g(t) = sg[t] (sigmoid gate) or 1.  Eight columns per thread.
-// DENSE: `routed` holds the pairs in (t, k) order and `shared_rows` the
+// DENSE: `routed` holds the pairs -- pair (t, k) at row p.pair_pos[t * K + k]
+// when p.pair_pos is set, else at row t * K + k -- and `shared_rows` the
 // shared expert's rows; otherwise both come from the plan's sorted rows.
 template <bool DENSE>
 __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict__ routed, Plan p,
@@ -295,7 +298,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int k = k0 + j;
-      pos[j] = k < K ? (DENSE ? t * K + k : p.pair_pos[(int64_t)t * K + k]) : -1;
+      pos[j] = k < K ? ((DENSE && p.pair_pos == nullptr) ? t * K + k : p.pair_pos[(int64_t)t * K + k]) : -1;
       wk[j] = k < K ? w[(int64_t)t * K + k] : 0.0f;
     }
 #pragma unroll
@@ -381,10 +384,81 @@ void launch_combine(const uint16_t* routed, const Plan& p, const float* w, const
   combine_kernel<false><<<grid, 256, 0, stream>>>(routed, p, w, sg, shared_kind, T, H, E, K, nullptr, out);
 }
 
-void launch_combine_dense(const uint16_t* pairs, const float* w, const float* sg, int shared_kind, int T, int H,
-                          int K, const uint16_t* shared_rows, uint16_t* out, cudaStream_t stream) {
+void launch_combine_dense(const uint16_t* pairs, const int32_t* pair_pos, const float* w, const float* sg,
+                          int shared_kind, int T, int H, int K, const uint16_t* shared_rows, uint16_t* out,
+                          cudaStream_t stream) {
   dim3 grid((H / 8 + 255) / 256, T);
-  combine_kernel<true><<<grid, 256, 0, stream>>>(pairs, Plan{}, w, sg, shared_kind, T, H, 0, K, shared_rows, out);
+  Plan p{};
+  p.pair_pos = const_cast<int32_t*>(pair_pos);
+  combine_kernel<true><<<grid, 256, 0, stream>>>(pairs, p, w, sg, shared_kind, T, H, 0, K, shared_rows, out);
+}
+
+// owner[i] = idx[i] / per_rank (the rank that holds expert idx[i]).
+__global__ void ep_owner_kernel(const int32_t* __restrict__ idx, int P, int per_rank, int world,
+                                int32_t* __restrict__ owner, uint32_t* status) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < P; i += gridDim.x * blockDim.x) {
+    const int e = idx[i];
+    if (e < 0 || e >= per_rank * world) {
+      report_status(status, kStatusBadExpert, (uint32_t)i);
+      owner[i] = -1;
+    } else {
+      owner[i] = e / per_rank;
+    }
+  }
+}
+
+// After the plan over owners: each pair's slot in send order, its expert id
+// local to the owner at that slot, and the per-owner counts.  With
+// capacity > 0 owner r's pairs take slots [r * capacity, r * capacity +
+// count_r), the other slots get expert id -1 (padding), and the x rows are
+// copied here (one warp per pair); with capacity 0 the slots are packed.
+__global__ void ep_finish_kernel(const int32_t* __restrict__ idx, Plan p, int T, int K, int per_rank, int world,
+                                 int capacity, int32_t* __restrict__ send_counts, int32_t* __restrict__ pair_pos,
+                                 int32_t* __restrict__ send_eid, const uint16_t* __restrict__ x, int H,
+                                 uint16_t* __restrict__ send_x) {
+  const int P = T * K;
+  const int gtid = blockIdx.x * blockDim.x + threadIdx.x, nthreads = gridDim.x * blockDim.x;
+  if (capacity > 0)
+    for (int i = gtid; i < world * capacity; i += nthreads) {
+      const int r = i / capacity, j = i - r * capacity;
+      if (j >= p.counts[r]) send_eid[i] = -1;
+    }
+  for (int i = gtid; i < P; i += nthreads) {
+    const int pos = p.pair_pos[i];
+    if (pos < 0) {
+      pair_pos[i] = -1;
+      continue;
+    }
+    const int e = idx[i], r = e / per_rank;
+    const int slot = capacity > 0 ? r * capacity + (pos - p.offsets[r]) : pos;
+    pair_pos[i] = slot;
+    send_eid[slot] = e - r * per_rank;
+  }
+  if (blockIdx.x == 0)
+    for (int r = threadIdx.x; r < world; r += blockDim.x) send_counts[r] = p.counts[r];
+  if (capacity > 0) {
+    const int lane = threadIdx.x & 31, warps = nthreads >> 5;
+    for (int i = gtid >> 5; i < P; i += warps) {
+      const int pos = p.pair_pos[i];
+      if (pos < 0) continue;
+      const int r = idx[i] / per_rank;
+      const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)(i / K) * H);
+      uint4* dst = reinterpret_cast<uint4*>(send_x + (int64_t)(r * capacity + (pos - p.offsets[r])) * H);
+      for (int j = lane; j < H / 8; j += 32) dst[j] = src[j];
+    }
+  }
+}
+
+void launch_ep_owner(const int32_t* idx, int P, int per_rank, int world, int32_t* owner, uint32_t* status,
+                     int num_sms, cudaStream_t stream) {
+  ep_owner_kernel<<<num_sms, 256, 0, stream>>>(idx, P, per_rank, world, owner, status);
+}
+
+void launch_ep_finish(const int32_t* idx, const Plan& p, int T, int K, int per_rank, int world, int capacity,
+                      int32_t* send_counts, int32_t* pair_pos, int32_t* send_eid, const uint16_t* x, int H,
+                      uint16_t* send_x, int num_sms, cudaStream_t stream) {
+  ep_finish_kernel<<<num_sms, 256, 0, stream>>>(idx, p, T, K, per_rank, world, capacity, send_counts, pair_pos,
+                                                send_eid, x, H, send_x);
 }
 
 void launch_unpermute(const uint16_t* routed, const Plan& p, int TK, int H, uint16_t* out, int num_sms,

@@ -5,16 +5,19 @@ the shared expert are replicated and every rank keeps its own tokens.  One
 layer forward (the survey's hot-path rows a6-a8 split across GPUs):
 
   1. route the local tokens with the full router -> (w, idx) [T, K];
-  2. order the (t, k) pairs by owning rank (stable, so k order is kept per
-     token) and exchange the per-rank pair counts (all-to-all of W int32);
-  3. dispatch: all-to-all-v of the pairs' activation rows (bf16 [n, H]) and
-     their expert ids local to the owner (int32 [n]);
+  2. wm_ep_plan orders the (t, k) pairs by owning rank (stable, so k order
+     is kept per token), gathers their activation rows and owner-local
+     expert ids; the per-rank pair counts are exchanged (all-to-all of W
+     int32) and read on the host for the split sizes;
+  3. dispatch: all-to-all-v of the rows (bf16 [n, H]) and the expert ids;
   4. the owner applies its experts to the rows it received
      (wm_expert_pairs: sort, expert kernels, unpermute);
   5. combine: the reverse all-to-all-v brings each pair's expert row back to
-     the token's rank, which scatters it to (t, k) order and forms
-     sum_k w[t, k] * y[t, k] + g_t * shared(x[t]) with wm_combine -- the same
-     arithmetic as the single-GPU layer.
+     the token's rank in send order, and wm_combine forms
+     sum_k w[t, k] * y[t, k] + g_t * shared(x[t]) reading pair (t, k) at its
+     send slot -- the same arithmetic as the single-GPU layer.  The shared
+     expert of the local tokens runs on a side stream (its own handle) while
+     the pairs are exchanged.
 
 Expert rows are independent of which other rows share their GPU, so a
 layer split over W GPUs returns what one GPU computes for the same tokens
@@ -22,7 +25,7 @@ whenever both take the same expert kernels (the exchanges only move rows).
 The reference runs its experts on one device; this module is the
 B200-native counterpart of the survey's expert-parallel plan, not a port.
 
-The engine is anything with route / expert_pairs / combine of
+The engine is anything with route / ep_plan / expert_pairs / combine of
 whallm_b200.moe.Engine's signatures, so the exchange logic can be tested with
 CPU stand-ins on gloo.
 """
@@ -45,12 +48,25 @@ class EPStats:
 
 
 class ExpertParallelMoE:
-    """One MoE layer whose routed experts are split evenly over a process group."""
+    """One MoE layer whose routed experts are split evenly over a process group.
 
-    def __init__(self, engine, layer: LayerWeights, top_k: int, group=None):
+    `shared_engine`, when given, computes the shared expert on a side stream
+    while the pairs are exchanged (it must be a different handle: a handle's
+    workspace serves one stream at a time).
+
+    `fixed_capacity` = M > 0 (the most tokens any rank passes in one call,
+    the same on every rank): every rank sends every other rank M * K slots
+    (the most pairs it can have for one rank), padding marked by expert id -1,
+    so the exchanges have fixed sizes, nothing is read on the host and a step
+    can be captured in a CUDA graph.  `engine` must then be a handle created
+    with lib.FLAG_SKIP_NEGATIVE_ROUTES and room for W * M * K rows."""
+
+    def __init__(self, engine, layer: LayerWeights, top_k: int, group=None, shared_engine=None,
+                 fixed_capacity: int = 0):
         if not dist.is_initialized():
             raise RuntimeError("torch.distributed is not initialised")
         self.engine, self.layer, self.K, self.group = engine, layer, top_k, group
+        self.shared_engine = shared_engine
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         if layer.E % self.world:
@@ -61,32 +77,81 @@ class ExpertParallelMoE:
         e0 = self.rank * self.E_local
         self.local = layer.experts(e0, e0 + self.E_local)
         self.shared = layer.shared_only() if layer.shared is not None else None
+        self.fixed = fixed_capacity
         self.stats = EPStats()
+        self._side = None
 
     def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits: list[int], in_splits: list[int]) -> None:
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
 
+    def _shared_rows(self, eng, x: torch.Tensor) -> torch.Tensor:
+        zero = torch.zeros((x.shape[0], 1), dtype=torch.int32, device=x.device)
+        return eng.expert_pairs(self.shared, x, zero).view(x.shape[0], x.shape[1])
+
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        w, idx = self.engine.route(self.layer, x, self.K)
+
+        # the shared expert of the local tokens, beside the exchange
+        shared_rows = None
+        side = None
+        if self.shared is not None and self.shared_engine is not None and x.is_cuda:
+            if self._side is None:
+                self._side = torch.cuda.Stream(device=x.device)
+            side = self._side
+            side.wait_stream(torch.cuda.current_stream(x.device))
+            with torch.cuda.stream(side):
+                shared_rows = self._shared_rows(self.shared_engine, x)
+
+        if self.fixed:
+            back, pair_pos = self._exchange_fixed(x, idx)
+        else:
+            back, pair_pos = self._exchange_exact(x, idx)
+
+        gate, gate_w = lib.SHARED_NONE, None
+        if self.shared is not None:
+            if side is not None:
+                main = torch.cuda.current_stream(x.device)
+                main.wait_stream(side)
+                shared_rows.record_stream(main)
+            else:
+                shared_rows = self._shared_rows(self.engine, x)
+            gate, gate_w = self.layer.shared.gate, self.layer.shared.gate_weight
+        return self.engine.combine(back, w, shared_rows, gate, x, gate_w, pair_pos=pair_pos)
+
+    def _exchange_fixed(self, x: torch.Tensor, idx: torch.Tensor):
+        """Fixed-size exchanges: W * T * K slots each way, padding skipped."""
         T, H = x.shape
-        K, W, El = self.K, self.world, self.E_local
-        w, idx = self.engine.route(self.layer, x, K)
-        flat = idx.reshape(-1).to(torch.int64)
-        owner = torch.div(flat, El, rounding_mode="floor")
-        order = torch.argsort(owner, stable=True)
-        send_counts = torch.bincount(owner, minlength=W).to(torch.int64)
+        if T > self.fixed:
+            raise ValueError(f"{T} tokens exceed the fixed capacity of {self.fixed} per rank")
+        W, El, C = self.world, self.E_local, self.fixed * self.K
+        _, pair_pos, send_eid, send_x = self.engine.ep_plan(idx, x, El, W, capacity=C)
+        recv_x = torch.empty_like(send_x)
+        recv_e = torch.empty_like(send_eid)
+        dist.all_to_all_single(recv_x, send_x, group=self.group)
+        dist.all_to_all_single(recv_e, send_eid, group=self.group)
+        y = self.engine.expert_pairs(self.local, recv_x, recv_e.view(W * C, 1)).view(W * C, H)
+        back = torch.empty_like(y)
+        dist.all_to_all_single(back, y, group=self.group)
+        self.stats = EPStats(sent=-1, received=-1)
+        return back, pair_pos
+
+    def _exchange_exact(self, x: torch.Tensor, idx: torch.Tensor):
+        """Exchanges sized by the pair counts (read on the host)."""
+        T, H = x.shape
+        W, El = self.world, self.E_local
+        # pairs in owner order, then the counts each rank sends and receives
+        send_counts, pair_pos, send_eid, send_x = self.engine.ep_plan(idx, x, El, W)
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=self.group)
         counts = torch.stack([send_counts, recv_counts]).cpu()  # the one host sync: split sizes
         send_splits, recv_splits = counts[0].tolist(), counts[1].tolist()
         n_send, n_recv = sum(send_splits), sum(recv_splits)
 
-        # dispatch: activation rows and owner-local expert ids, grouped by owner
-        send_x = x.index_select(0, torch.div(order, K, rounding_mode="floor"))
-        send_e = (flat.index_select(0, order) - owner.index_select(0, order) * El).to(torch.int32)
+        # dispatch: activation rows and owner-local expert ids
         recv_x = torch.empty((n_recv, H), dtype=x.dtype, device=x.device)
         recv_e = torch.empty((n_recv,), dtype=torch.int32, device=x.device)
         self._a2a(recv_x, send_x, recv_splits, send_splits)
-        self._a2a(recv_e, send_e, recv_splits, send_splits)
+        self._a2a(recv_e, send_eid, recv_splits, send_splits)
 
         # this rank's experts on the rows it received
         if n_recv:
@@ -94,16 +159,8 @@ class ExpertParallelMoE:
         else:
             y = torch.empty((0, H), dtype=x.dtype, device=x.device)
 
-        # combine: rows back to the tokens' ranks, then (t, k) order
+        # rows back in send order; pair (t, k) sits at pair_pos[t, k]
         back = torch.empty((n_send, H), dtype=x.dtype, device=x.device)
         self._a2a(back, y, send_splits, recv_splits)
-        pairs = torch.empty((T * K, H), dtype=x.dtype, device=x.device)
-        pairs.index_copy_(0, order, back)
-
-        shared_rows, gate, gate_w = None, lib.SHARED_NONE, None
-        if self.shared is not None:
-            zero = torch.zeros((T, 1), dtype=torch.int32, device=x.device)
-            shared_rows = self.engine.expert_pairs(self.shared, x, zero).view(T, H)
-            gate, gate_w = self.layer.shared.gate, self.layer.shared.gate_weight
         self.stats = EPStats(sent=n_send, received=n_recv)
-        return self.engine.combine(pairs.view(T, K, H), w, shared_rows, gate, x, gate_w)
+        return back, pair_pos

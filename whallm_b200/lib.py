@@ -17,11 +17,12 @@ FORMAT_MXFP4, FORMAT_FP8_B128, FORMAT_FP8_B32 = 0, 1, 2
 CONV_MLX, CONV_METAL = 0, 1
 ROUTER_SOFTMAX, ROUTER_SQRTSOFTPLUS, ROUTER_SIGMOID, ROUTER_SIGMOID_GROUPED = 0, 1, 2, 3
 SHARED_NONE, SHARED_SIGMOID_GATE, SHARED_ONE = 0, 1, 2
+FLAG_SKIP_NEGATIVE_ROUTES = 1
 
 # Every entry point the header declares (checked by the CPU test suite).
 EXPORTS = (
     "wm_create", "wm_destroy", "wm_error", "wm_sync", "wm_counters_get",
-    "wm_dequant", "wm_route", "wm_expert_pairs", "wm_combine", "wm_moe_forward",
+    "wm_dequant", "wm_route", "wm_expert_pairs", "wm_combine", "wm_ep_plan", "wm_moe_forward",
     "wm_profile_enable", "wm_profile_read", "wm_profile_reset",
     "wm_moe_forward_noalloc",
 )
@@ -96,7 +97,8 @@ def load() -> ctypes.CDLL:
     L.wm_route.argtypes = [_P, ctypes.POINTER(MoeArgs), _P, _P, _P, _P]
     L.wm_expert_pairs.argtypes = [_P, ctypes.POINTER(MoeArgs), _P, _P]
     L.wm_moe_forward.argtypes = [_P, ctypes.POINTER(MoeArgs), _P]
-    L.wm_combine.argtypes = [_P, _I64, _I32, _I32, _P, _P, _P, _I32, _P, _P, _P, _P]
+    L.wm_combine.argtypes = [_P, _I64, _I32, _I32, _P, _P, _P, _P, _I32, _P, _P, _P, _P]
+    L.wm_ep_plan.argtypes = [_P, _I64, _I32, _I32, _I32, _I32, _P, _P, _I32, _P, _P, _P, _P, _P]
     L.wm_profile_enable.argtypes = [_P, _I32]
     L.wm_profile_enable.restype = ctypes.c_int
     L.wm_profile_read.argtypes = [_P, ctypes.POINTER(ProfileEntry), _I32]
@@ -105,7 +107,8 @@ def load() -> ctypes.CDLL:
     L.wm_profile_reset.restype = None
     L.wm_moe_forward_noalloc.argtypes = [ctypes.POINTER(MoeArgs), _P, ctypes.c_char_p, ctypes.c_size_t]
     L.wm_moe_forward_noalloc.restype = ctypes.c_int
-    for name in ("wm_sync", "wm_dequant", "wm_route", "wm_expert_pairs", "wm_combine", "wm_moe_forward"):
+    for name in ("wm_sync", "wm_dequant", "wm_route", "wm_expert_pairs", "wm_combine", "wm_ep_plan",
+                 "wm_moe_forward"):
         getattr(L, name).restype = ctypes.c_int
     _lib = L
     return L
@@ -115,11 +118,11 @@ class Context:
     """One library handle on one CUDA device, sized by its maxima."""
 
     def __init__(self, device: int = 0, *, max_tokens: int, max_hidden: int, max_inter: int, max_experts: int,
-                 max_topk: int, gemv_max_tokens: int = 0):
+                 max_topk: int, gemv_max_tokens: int = 0, flags: int = 0):
         L = load()
         self._lib = L
         opt = Options(max_tokens=max_tokens, max_hidden=max_hidden, max_inter=max_inter,
-                      max_experts=max_experts, max_topk=max_topk, gemv_max_tokens=gemv_max_tokens, flags=0)
+                      max_experts=max_experts, max_topk=max_topk, gemv_max_tokens=gemv_max_tokens, flags=flags)
         err = ctypes.create_string_buffer(512)
         handle = L.wm_create(device, ctypes.byref(opt), err, len(err))
         if not handle:
@@ -178,10 +181,15 @@ class Context:
     def expert_pairs(self, args: MoeArgs, routed: int, stream: int | None) -> None:
         self.check(self._lib.wm_expert_pairs(self.handle, ctypes.byref(args), routed, stream))
 
-    def combine(self, T: int, H: int, K: int, pairs: int, w: int, shared: int | None, shared_gate: int,
-                x: int | None, shared_gate_weight: int | None, out: int, stream: int | None) -> None:
-        self.check(self._lib.wm_combine(self.handle, T, H, K, pairs, w, shared, shared_gate, x, shared_gate_weight,
-                                        out, stream))
+    def combine(self, T: int, H: int, K: int, pairs: int, pair_pos: int | None, w: int, shared: int | None,
+                shared_gate: int, x: int | None, shared_gate_weight: int | None, out: int, stream: int | None) -> None:
+        self.check(self._lib.wm_combine(self.handle, T, H, K, pairs, pair_pos, w, shared, shared_gate, x,
+                                        shared_gate_weight, out, stream))
+
+    def ep_plan(self, T: int, K: int, per_rank: int, world: int, capacity: int, idx: int, x: int, H: int,
+                send_counts: int, pair_pos: int, send_eid: int, send_x: int, stream: int | None) -> None:
+        self.check(self._lib.wm_ep_plan(self.handle, T, K, per_rank, world, capacity, idx, x, H, send_counts,
+                                        pair_pos, send_eid, send_x, stream))
 
     def moe_forward(self, args: MoeArgs, stream: int | None) -> None:
         self.check(self._lib.wm_moe_forward(self.handle, ctypes.byref(args), stream))

@@ -104,14 +104,15 @@ class Engine:
     """A library handle sized for the largest call it will see."""
 
     def __init__(self, device: int | torch.device = 0, *, max_tokens: int, hidden: int, inter: int, experts: int,
-                 topk: int, gemv_max_tokens: int = 0):
+                 topk: int, gemv_max_tokens: int = 0, flags: int = 0):
         dev = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
         if dev.type != "cuda":
             raise ValueError("the expert kernels run on CUDA devices only")
         self.device = dev
         with torch.cuda.device(dev):
             self.ctx = lib.Context(dev.index or 0, max_tokens=max_tokens, max_hidden=hidden, max_inter=inter,
-                                   max_experts=experts, max_topk=topk, gemv_max_tokens=gemv_max_tokens)
+                                   max_experts=experts, max_topk=topk, gemv_max_tokens=gemv_max_tokens,
+                                   flags=flags)
 
     # ---------------------------------------------------------------- argument block
     def _args(self, layer: LayerWeights, x: torch.Tensor, K: int) -> lib.MoeArgs:
@@ -198,19 +199,45 @@ class Engine:
 
     def combine(self, pairs: torch.Tensor, w: torch.Tensor, shared_rows: torch.Tensor | None = None,
                 shared_gate: int = lib.SHARED_NONE, x: torch.Tensor | None = None,
-                gate_weight: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
-        """out[t] = sum_k w[t, k] * pairs[t, k] + g_t * shared_rows[t] (bf16 [T, H]), the
-        same arithmetic as forward's combine; pairs bf16 [T, K, H] in (t, k) order."""
-        T, K, H = pairs.shape
-        _check_bf16("pairs", pairs, (T, K, H))
+                gate_weight: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                pair_pos: torch.Tensor | None = None) -> torch.Tensor:
+        """out[t] = sum_k w[t, k] * y(t, k) + g_t * shared_rows[t] (bf16 [T, H]), the same
+        arithmetic as forward's combine.  y(t, k) = pairs[t, k] for pairs bf16 [T, K, H],
+        or pairs[pair_pos[t, k]] for pairs bf16 [rows, H] with pair_pos int32 [T, K]."""
+        T, K = w.shape
+        H = pairs.shape[-1]
+        if pair_pos is None:
+            _check_bf16("pairs", pairs, (T, K, H))
+        else:
+            _check_bf16("pairs", pairs, (pairs.shape[0], H))
+            pair_pos = pair_pos.reshape(T, K).to(torch.int32).contiguous()
         w = w.reshape(T, K).to(torch.float32).contiguous()
         if shared_gate != lib.SHARED_NONE:
             _check_bf16("shared_rows", shared_rows, (T, H))
         if out is None:
             out = torch.empty((T, H), dtype=torch.bfloat16, device=pairs.device)
-        self.ctx.combine(T, H, K, pairs.data_ptr(), w.data_ptr(), _ptr(shared_rows), shared_gate, _ptr(x),
-                         _ptr(gate_weight), out.data_ptr(), _stream())
+        self.ctx.combine(T, H, K, pairs.data_ptr(), _ptr(pair_pos), w.data_ptr(), _ptr(shared_rows), shared_gate,
+                         _ptr(x), _ptr(gate_weight), out.data_ptr(), _stream())
         return out
+
+    def ep_plan(self, idx: torch.Tensor, x: torch.Tensor, per_rank: int, world: int, capacity: int = 0):
+        """Dispatch plan of routes idx [T, K] over `world` ranks of `per_rank`
+        experts: (send_counts int32 [world], pair_pos int32 [T, K], send_eid int32
+        [slots], send_x bf16 [slots, H]) -- pairs in owner order, x rows per slot;
+        slots = T * K packed, or world * capacity with padding ids -1."""
+        T, K = idx.shape
+        H = x.shape[1]
+        idx = idx.to(torch.int32).contiguous()
+        _check_bf16("x", x, (T, H))
+        dev = x.device
+        slots = world * capacity if capacity else T * K
+        counts = torch.empty((world,), dtype=torch.int32, device=dev)
+        pair_pos = torch.empty((T, K), dtype=torch.int32, device=dev)
+        send_eid = torch.empty((slots,), dtype=torch.int32, device=dev)
+        send_x = torch.empty((slots, H), dtype=torch.bfloat16, device=dev)
+        self.ctx.ep_plan(T, K, per_rank, world, capacity, idx.data_ptr(), x.data_ptr(), H, counts.data_ptr(),
+                         pair_pos.data_ptr(), send_eid.data_ptr(), send_x.data_ptr(), _stream())
+        return counts, pair_pos, send_eid, send_x
 
     def dequant(self, fmt: int, weight: torch.Tensor, scale: torch.Tensor, rows: int, cols: int,
                 convention: int = lib.CONV_MLX) -> torch.Tensor:
