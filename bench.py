@@ -35,6 +35,8 @@ METRIC = "MoE-layer tokens/s (prefill, decode) at 1/2/4/8 B200; % of HBM / FP4-T
 H, I, E, K = 2048, 512, 512, 10
 BLOB = 1_671_168  # bytes of one expert blob (gate_up + scales + down + scales)
 GATE_UP_BYTES = 2 * I * H // 2 + 2 * I * H // 32
+# dram bytes (read + write) of one gate/up decode launch at this workload, from an ncu capture
+NCU_GATE_UP_TRAFFIC = 411.845632e6 + 4.414976e6
 DOWN_BYTES = H * I // 2 + H * I // 32
 
 
@@ -453,8 +455,8 @@ def run(args) -> None:
     prof = eng.ctx.profile_read()
     eng.ctx.profile(False)
     U = statistics.mean(uniq)
-    gu_n, gu_ms = prof.get("gemv_gate_up", (1, float("nan")))
-    dn_n, dn_ms = prof.get("gemv_down", (1, float("nan")))
+    gu_n, gu_ms = prof.get("decode_gate_up", (1, float("nan")))
+    dn_n, dn_ms = prof.get("decode_down", (1, float("nan")))
     gu_bytes = (U + 1) * GATE_UP_BYTES + B * H * 2 + B * 2 * I * 2  # weights + x + act written
     dn_bytes = (U + 1) * DOWN_BYTES + (B * K + B) * (I * 2 + H * 2)
     gu_avg = gu_ms / gu_n
@@ -510,9 +512,12 @@ def run(args) -> None:
                    "timing": "CUDA graph replay per step, device events, max over ranks",
                    "parallelism": "single GPU",
                    "unique_experts_per_step": U},
-        "roofline": {"bound": "hbm", "kernel": "gemv_gate_up", "achieved": achieved, "peak": pk["hbm_gbs"],
-                     "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "peak_source": pk["source"],
-                     "traffic": None, "algorithmic_bytes_per_launch": gu_bytes,
+        "roofline": {"bound": "hbm", "kernel": "decode_kernel<0> (gate/up + SwiGLU)", "achieved": achieved,
+                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                     "peak_source": pk["source"], "traffic": NCU_GATE_UP_TRAFFIC,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch, "
+                                       "profiles/decode_config1_b64.txt",
+                     "algorithmic_bytes_per_launch": gu_bytes,
                      "down_achieved_gbs": dn_bytes / (dn_ms / dn_n / 1e3) / 1e9},
         "kernels": kernels,
         "cpu_baseline": cpu,

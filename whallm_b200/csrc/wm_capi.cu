@@ -279,18 +279,18 @@ int run_decode(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts, 
   wm::launch_gather_f16(static_cast<const uint16_t*>(a->x), plan, a->E, H, xh, ctx->rowscale, ctx->num_sms, s);
   wm::prof_end(&ctx->prof, wm::kProfGather, s);
   d.bscale = ctx->rowscale;
-  wm::prof_begin(&ctx->prof, wm::kProfGemvGateUp, s);
+  wm::prof_begin(&ctx->prof, wm::kProfDecodeGateUp, s);
   const void* maps0[5] = {&w13, has_shared ? &w13s : &w13, &s13, has_shared ? &s13s : &s13, &bx};
   wm::launch_decode(d, 0, maps0, ctx->num_sms, s);
-  wm::prof_end(&ctx->prof, wm::kProfGemvGateUp, s);
+  wm::prof_end(&ctx->prof, wm::kProfDecodeGateUp, s);
   wm::prof_begin(&ctx->prof, wm::kProfActF16, s);
   wm::launch_act_f16(ctx->act, plan, a->E, I, acth, ctx->actscale, ctx->num_sms, s);
   wm::prof_end(&ctx->prof, wm::kProfActF16, s);
   d.bscale = ctx->actscale;
-  wm::prof_begin(&ctx->prof, wm::kProfGemvDown, s);
+  wm::prof_begin(&ctx->prof, wm::kProfDecodeDown, s);
   const void* maps1[5] = {&w2, has_shared ? &w2s : &w2, &s2, has_shared ? &s2s : &s2, &bact};
   wm::launch_decode(d, 1, maps1, ctx->num_sms, s);
-  wm::prof_end(&ctx->prof, wm::kProfGemvDown, s);
+  wm::prof_end(&ctx->prof, wm::kProfDecodeDown, s);
   ctx->counters.launches += 4;
   ctx->counters.decode_calls += 1;
   return check_launch(ctx, "expert decode");

@@ -22,6 +22,8 @@ enum ProfSlot : int {
   kProfGemmGateUp,
   kProfGemmDown,
   kProfCombine,
+  kProfDecodeGateUp,
+  kProfDecodeDown,
   kProfSlots
 };
 struct Profiler;  // defined in wm_profile.cu
