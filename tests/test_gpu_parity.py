@@ -113,6 +113,38 @@ def test_router_matches_oracle(engine_factory, kind, E, K, bias, groups, topg, s
     assert [set(r) for r in idx.cpu().numpy().tolist()] == [set(r) for r in ri.tolist()]
 
 
+@pytest.mark.parametrize("kind,E,K,groups,topg", [(lib.ROUTER_SOFTMAX, 512, 10, 1, 1),
+                                                   (lib.ROUTER_SIGMOID_GROUPED, 256, 8, 8, 4),
+                                                   (lib.ROUTER_SIGMOID, 384, 8, 1, 1)])
+def test_router_tensor_cores_long_call(engine_factory, kind, E, K, groups, topg):
+    """T >= 256 takes the tcgen05 logits GEMM; T = 300 leaves a partial 128-row tile."""
+    H, T = 2048, 300
+    eng = engine_factory(512, H, 512, E, K)
+    g = torch.Generator(device=DEV).manual_seed(31 + kind)
+    layer = synth.qwen_layer(E=8, H=H, I=64, device=DEV, seed=3, shared=False, router=False)
+    wr = (torch.randn((E, H), generator=g, device=DEV) / H ** 0.5).to(torch.bfloat16)
+    layer = LayerWeights(layer.layout, H, 64, E, layer.w13, layer.w2,
+                         router=RouterWeights(wr, kind, None, groups, topg, 1.0))
+    x = synth.activations(T, H, g, DEV)
+    w, idx, logits = eng.route(layer, x, K, with_logits=True)
+    eng.sync()
+    ref_logits = oracle.router_logits(adapter.bits(x), adapter.bits(wr))
+    np.testing.assert_allclose(logits.cpu().numpy(), ref_logits, rtol=2e-5, atol=2e-5)
+    oi, ow = oracle.route(kind, logits.cpu().numpy(), K, None, groups, topg, 1.0)
+    np.testing.assert_array_equal(idx.cpu().numpy(), oi)
+    np.testing.assert_allclose(w.cpu().numpy(), ow, rtol=1e-5, atol=1e-7)
+    # end to end: identical index sets, except where the reference's K-th and
+    # (K+1)-th logits are closer than the two sums' rounding can separate
+    ri, _ = oracle.route(kind, ref_logits, K, None, groups, topg, 1.0)
+    srt = -np.sort(-ref_logits, axis=1)
+    for t in range(T):
+        if kind == lib.ROUTER_SOFTMAX and srt[t, K - 1] - srt[t, K] < 1e-4:
+            continue
+        if kind != lib.ROUTER_SOFTMAX and np.min(np.abs(np.diff(srt[t]))) < 1e-4:
+            continue
+        assert set(idx[t].tolist()) == set(ri[t].tolist()), t
+
+
 # ---------------------------------------------------------------- experts and the whole layer
 
 def _small_layer(layout, E, H, I, seed, shared_gate=lib.SHARED_NONE, limit=0.0):

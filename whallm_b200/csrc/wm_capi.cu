@@ -154,12 +154,25 @@ wm::ExpertWeights weights_of(const wm_moe_args* a, bool with_shared) {
 }
 
 // Router logits + top-k into idx / w (and sg for the sigmoid shared gate).
+bool encode_2d_bf16(wm_ctx* ctx, CUtensorMap* map, const void* base, int cols, int rows, int box_rows);
+
 int run_router(wm_ctx* ctx, const wm_moe_args* a, float* logits, int32_t* idx, float* w, cudaStream_t s) {
   const uint16_t* sg_w =
       a->shared_gate == WM_SHARED_SIGMOID_GATE ? static_cast<const uint16_t*>(a->shared_gate_weight) : nullptr;
   wm::prof_begin(&ctx->prof, wm::kProfRouter, s);
-  wm::launch_router_logits(static_cast<const uint16_t*>(a->x), static_cast<const uint16_t*>(a->router_weight), sg_w,
-                           a->T, a->H, a->E, logits, ctx->sg, s);
+  CUtensorMap mx, mw;
+  if (wm::router_gemm_shape_ok(a->T, a->H, a->E) && aligned(a->x, 16) && aligned(a->router_weight, 16) &&
+      encode_2d_bf16(ctx, &mx, a->x, a->H, a->T, 128) && encode_2d_bf16(ctx, &mw, a->router_weight, a->H, a->E, 128)) {
+    // long calls: the logits GEMM on the tensor cores, the shared gate (one row) on the CUDA cores
+    wm::launch_router_gemm(&mx, &mw, a->T, a->H, a->E, logits, ctx->status, ctx->num_sms, s);
+    if (sg_w != nullptr) {
+      wm::launch_shared_gate(static_cast<const uint16_t*>(a->x), sg_w, a->T, a->H, ctx->sg, s);
+      ctx->counters.launches += 1;
+    }
+  } else {
+    wm::launch_router_logits(static_cast<const uint16_t*>(a->x), static_cast<const uint16_t*>(a->router_weight),
+                             sg_w, a->T, a->H, a->E, logits, ctx->sg, s);
+  }
   wm::prof_end(&ctx->prof, wm::kProfRouter, s);
   wm::prof_begin(&ctx->prof, wm::kProfTopk, s);
   wm::launch_router_topk(logits, a->router_bias, a->T, a->E, a->K, a->router, a->n_groups, a->topk_groups,
@@ -180,6 +193,20 @@ bool encode_rows_box(wm_ctx* ctx, CUtensorMap* map, const void* base, int kdim, 
   cuuint32_t estr[2] = {1, 1};
   CUresult r = ctx->encode_tiled(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
                                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// TMA descriptor of a caller's bf16 matrix [rows, cols] (row-major), boxes
+// of 64 columns x box_rows rows with the 128-byte swizzle.
+bool encode_2d_bf16(wm_ctx* ctx, CUtensorMap* map, const void* base, int cols, int rows, int box_rows) {
+  if (ctx->encode_tiled == nullptr) return false;
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(cols) * 2};
+  cuuint32_t box[2] = {64, cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -461,6 +488,7 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
   wm::gemm_init_attributes();
   wm::decode_init_attributes();
   wm::router_init_attributes(int(H));
+  wm::router_gemm_init_attributes();
   cudaDriverEntryPointQueryResult q{};
   void* fn = nullptr;
   if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
@@ -604,8 +632,8 @@ WM_EXPORT int wm_combine(wm_ctx* ctx, int64_t T, int32_t H, int32_t K, const voi
   DeviceGuard guard(ctx->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (shared_gate == WM_SHARED_SIGMOID_GATE) {
-    wm::launch_router_logits(static_cast<const uint16_t*>(x), nullptr, static_cast<const uint16_t*>(shared_gate_weight),
-                             int(T), H, 0, nullptr, ctx->sg, s);
+    wm::launch_shared_gate(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(shared_gate_weight), int(T),
+                           H, ctx->sg, s);
     ctx->counters.launches += 1;
   }
   wm::prof_begin(&ctx->prof, wm::kProfCombine, s);
@@ -672,9 +700,8 @@ WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* a, void* stream) {
     idx = a->routes_idx;
     w = a->routes_w;
     if (a->shared_gate == WM_SHARED_SIGMOID_GATE) {
-      wm::launch_router_logits(static_cast<const uint16_t*>(a->x), nullptr,
-                               static_cast<const uint16_t*>(a->shared_gate_weight), a->T, a->H, 0, nullptr, ctx->sg,
-                               s);
+      wm::launch_shared_gate(static_cast<const uint16_t*>(a->x),
+                             static_cast<const uint16_t*>(a->shared_gate_weight), a->T, a->H, ctx->sg, s);
       ctx->counters.launches += 1;
     }
   }

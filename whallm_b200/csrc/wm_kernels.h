@@ -39,8 +39,16 @@ size_t router_smem_bytes(int H);
 void router_init_attributes(int max_hidden);
 void launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* sg_w, int T, int H, int E,
                           float* logits, float* sg, cudaStream_t stream);
+void launch_shared_gate(const uint16_t* x, const uint16_t* g, int T, int H, float* sg, cudaStream_t stream);
 void launch_router_topk(const float* logits, const float* bias, int T, int E, int K, int kind, int n_groups,
                         int topk_groups, float route_scale, int32_t* idx, float* w, cudaStream_t stream);
+
+// ---- router logits on tcgen05 for long calls (wm_router_sm100.cu); tm_x / tm_w
+// point to CUtensorMaps of x [T, H] and W_r [E, H] (bf16, 64 x 128 boxes, 128B swizzle)
+bool router_gemm_shape_ok(int T, int H, int E);
+void router_gemm_init_attributes();
+void launch_router_gemm(const void* tm_x, const void* tm_w, int T, int H, int E, float* logits, uint32_t* status,
+                        int num_sms, cudaStream_t stream);
 
 // ---- sort / permute / combine (wm_plan.cu)
 void launch_plan(const int32_t* idx, int T, int K, int E, bool has_shared, int align, const Plan& p, int max_rows,

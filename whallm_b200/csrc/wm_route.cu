@@ -220,6 +220,37 @@ void router_init_attributes(int max_hidden) {
                        int(router_smem_bytes(max_hidden)));
 }
 
+// sg[t] = sigmoid(x[t] . g) alone, one warp per token, with the per-lane
+// order and the xor reduction of router_logits_kernel's gate row (the same
+// bits), for calls whose logits come from elsewhere.
+__global__ void __launch_bounds__(256) shared_gate_kernel(const uint16_t* __restrict__ x,
+                                                          const uint16_t* __restrict__ g, int T, int H,
+                                                          float* __restrict__ sg) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const uint16_t* xr = x + (int64_t)t * H;
+  float acc = 0.0f;
+  for (int c = lane; c < H / 8; c += 32) {
+    const uint4 wv = *reinterpret_cast<const uint4*>(g + c * 8);
+    const uint4 xv = *reinterpret_cast<const uint4*>(xr + c * 8);
+    float2 p, a;
+    float s = 0.0f;
+    p = unpack_bf16x2(wv.x); a = unpack_bf16x2(xv.x); s = fmaf(a.x, p.x, s); s = fmaf(a.y, p.y, s);
+    p = unpack_bf16x2(wv.y); a = unpack_bf16x2(xv.y); s = fmaf(a.x, p.x, s); s = fmaf(a.y, p.y, s);
+    p = unpack_bf16x2(wv.z); a = unpack_bf16x2(xv.z); s = fmaf(a.x, p.x, s); s = fmaf(a.y, p.y, s);
+    p = unpack_bf16x2(wv.w); a = unpack_bf16x2(xv.w); s = fmaf(a.x, p.x, s); s = fmaf(a.y, p.y, s);
+    acc += s;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) sg[t] = 1.0f / (1.0f + expf(-acc));
+}
+
+void launch_shared_gate(const uint16_t* x, const uint16_t* g, int T, int H, float* sg, cudaStream_t stream) {
+  shared_gate_kernel<<<(T + 7) / 8, 256, 0, stream>>>(x, g, T, H, sg);
+}
+
 void launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* sg_w, int T, int H, int E,
                           float* logits, float* sg, cudaStream_t stream) {
   const int rows = E + (sg_w != nullptr ? 1 : 0);
