@@ -6,9 +6,11 @@ sm_100 part, every call raises -- there is no CPU fallback.
 from __future__ import annotations
 
 import ctypes
+import os
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "libwhallm_moe.so"
+# the in-tree build; WHALLM_MOE_LIB names another build of the same library
+LIB_PATH = Path(os.environ.get("WHALLM_MOE_LIB") or Path(__file__).resolve().parent / "libwhallm_moe.so")
 
 WM_OK, WM_ERROR, WM_CANCELLED = 0, 1, 2
 
