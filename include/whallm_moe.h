@@ -111,6 +111,11 @@ typedef struct {
    exchange buffers (the expert-parallel path). */
 #define WM_FLAG_SKIP_NEGATIVE_ROUTES 1
 
+/* Short MXFP4 calls take the tcgen05 decode kernel (weights dequantised into
+   TMEM) instead of the default register-direct decode kernel.  Both compute
+   the same products; kept for comparison. */
+#define WM_FLAG_TCGEN05_DECODE 2
+
 /* One projection of every expert: expert e's matrix at weight + e * weight_stride
    bytes, its scales at scale + e * scale_stride bytes (device pointers). */
 typedef struct {

@@ -1,5 +1,7 @@
-"""The tcgen05 decode kernels (weights as the M operand, f16 operands with
-exact power-of-two scaling) vs the CPU oracle (needs a B200).
+"""The decode kernels vs the CPU oracle (needs a B200): the default
+register-direct kernel (weights dequantised in registers into warp MMAs) and
+the tcgen05 kernel (weights as the M operand in TMEM), both with f16 operands
+under exact power-of-two scaling.
 
 Tolerance as elsewhere: max|y - y_ref| / max|y_ref| <= 1e-2 on bf16 outputs.
 """
@@ -40,9 +42,9 @@ def layer(layout=lib.LAYOUT_QWEN_GATE_UP_MXFP4, seed=3, gate=lib.SHARED_NONE, li
                         router=RouterWeights(wr, lib.ROUTER_SOFTMAX), swiglu_limit=limit)
 
 
-@pytest.fixture(scope="module")
-def eng():
-    e = Engine(0, max_tokens=64, hidden=H, inter=I, experts=E, topk=8)
+@pytest.fixture(scope="module", params=[0, lib.FLAG_TCGEN05_DECODE], ids=["mma", "tcgen05"])
+def eng(request):
+    e = Engine(0, max_tokens=64, hidden=H, inter=I, experts=E, topk=8, flags=request.param)
     yield e
     e.ctx.close()
 

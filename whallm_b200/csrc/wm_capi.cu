@@ -234,19 +234,28 @@ bool use_gemm(const wm_ctx* ctx, const wm_moe_args* a) {
   return gemm && wm::gemm_shape_ok(a->H, a->I) && ctx->encode_tiled != nullptr;
 }
 
-enum Path { kPathGemv = 0, kPathDecode = 1, kPathGemm = 2 };
+enum Path { kPathGemv = 0, kPathDecode = 1, kPathGemm = 2, kPathDecodeMma = 3 };
 
-// Which expert kernels a call takes: the tcgen05 grouped GEMM for long calls,
-// the tcgen05 decode kernel (weights as the M operand) for short MXFP4 calls
-// whose scale rows allow 16-byte loads, else the CUDA-core GEMV.
+// Which expert kernels a call takes: the tcgen05 grouped GEMM for long calls;
+// for short MXFP4 calls whose weights and scale rows allow 16-byte loads the
+// register-direct decode kernel (or, with WM_FLAG_TCGEN05_DECODE, the tcgen05
+// decode kernel); else the CUDA-core GEMV.
 Path expert_path(const wm_ctx* ctx, const wm_moe_args* a, bool has_shared) {
   if (use_gemm(ctx, a)) return kPathGemm;
-  if (a->layout == WM_LAYOUT_W13_FP8_B128 || ctx->encode_tiled == nullptr || !wm::decode_shape_ok(a->H, a->I))
-    return kPathGemv;
+  if (a->layout == WM_LAYOUT_W13_FP8_B128 || ctx->encode_tiled == nullptr) return kPathGemv;
   const wm_matrix* ms[4] = {&a->w13, &a->w2, &a->shared_w13, &a->shared_w2};
   for (int i = 0; i < (has_shared ? 4 : 2); ++i)
     if (!aligned(ms[i]->scale, 16) || (i < 2 && ms[i]->scale_stride % 16)) return kPathGemv;
-  return kPathDecode;
+  if (ctx->opt.flags & WM_FLAG_TCGEN05_DECODE) return wm::decode_shape_ok(a->H, a->I) ? kPathDecode : kPathGemv;
+  for (int i = 0; i < (has_shared ? 4 : 2); ++i)
+    if (!aligned(ms[i]->weight, 16) || (i < 2 && ms[i]->weight_stride % 16)) return kPathGemv;
+  return wm::decode_mma_shape_ok(a->H, a->I) ? kPathDecodeMma : kPathGemv;
+}
+
+// Plan fields of the expert kernels of `path`.
+void plan_for_path(const wm_ctx* ctx, Path path, wm::Plan* plan) {
+  if (path == kPathDecode || path == kPathDecodeMma) plan->rowmax = ctx->rowmax;
+  if (path == kPathDecodeMma) plan->tile_rows = 8;
 }
 
 // TMA descriptor over one projection's packed weights (or scales) of
@@ -264,6 +273,46 @@ bool encode_weights(wm_ctx* ctx, CUtensorMap* map, const void* base, int64_t row
                                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+// The register-direct decode path: per-token prescale, gate/up (+SwiGLU), down.
+int run_decode_mma(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts, cudaStream_t s) {
+  const int H = a->H, I = a->I;
+  uint16_t* xh = ctx->xs;       // [max_rows, H] f16 token rows
+  uint16_t* acth = ctx->act16;  // [max_rows, I] f16 act rows
+  CUtensorMap bx, bact;
+  if (!encode_rows_box(ctx, &bx, xh, H, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 8) ||
+      !encode_rows_box(ctx, &bact, acth, I, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 8))
+    return fail(ctx, "cuTensorMapEncodeTiled failed for the activation rows");
+  wm::Plan plan = ctx->plan;
+  plan_for_path(ctx, kPathDecodeMma, &plan);
+  wm::DecodeArgs d{};
+  d.plan = plan;
+  d.wts = wts;
+  d.act = ctx->act;
+  d.routed = ctx->routed;
+  d.H = H;
+  d.I = I;
+  d.gate_first = a->layout == WM_LAYOUT_QWEN_GATE_UP_MXFP4 ? 1 : 0;
+  d.limit = a->swiglu_limit;
+  d.status = ctx->status;
+  wm::prof_begin(&ctx->prof, wm::kProfGather, s);
+  wm::launch_gather_f16(static_cast<const uint16_t*>(a->x), plan, a->E, H, xh, ctx->rowscale, ctx->num_sms, s);
+  wm::prof_end(&ctx->prof, wm::kProfGather, s);
+  d.bscale = ctx->rowscale;
+  wm::prof_begin(&ctx->prof, wm::kProfDecodeGateUp, s);
+  wm::launch_decode_mma(d, 0, &bx, ctx->num_sms, s);
+  wm::prof_end(&ctx->prof, wm::kProfDecodeGateUp, s);
+  wm::prof_begin(&ctx->prof, wm::kProfActF16, s);
+  wm::launch_act_f16(ctx->act, plan, a->E, I, acth, ctx->actscale, ctx->num_sms, s);
+  wm::prof_end(&ctx->prof, wm::kProfActF16, s);
+  d.bscale = ctx->actscale;
+  wm::prof_begin(&ctx->prof, wm::kProfDecodeDown, s);
+  wm::launch_decode_mma(d, 1, &bact, ctx->num_sms, s);
+  wm::prof_end(&ctx->prof, wm::kProfDecodeDown, s);
+  ctx->counters.launches += 4;
+  ctx->counters.decode_calls += 1;
+  return check_launch(ctx, "expert decode");
 }
 
 // The tcgen05 decode path: per-token prescale, gate/up (+SwiGLU), down.
@@ -328,6 +377,7 @@ int run_experts(wm_ctx* ctx, const wm_moe_args* a, bool has_shared, Path path, c
   const wm::ExpertWeights wts = weights_of(a, has_shared);
   const int gate_first = a->layout == WM_LAYOUT_QWEN_GATE_UP_MXFP4 ? 1 : 0;
   if (path == kPathDecode) return run_decode(ctx, a, wts, has_shared, s);
+  if (path == kPathDecodeMma) return run_decode_mma(ctx, a, wts, s);
   if (path == kPathGemv) {
     wm::GemvArgs g{};
     g.plan = ctx->plan;
@@ -390,7 +440,7 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
     return nullptr;
   }
   wm_options o = *options;
-  if (o.flags & ~int32_t(WM_FLAG_SKIP_NEGATIVE_ROUTES)) {
+  if (o.flags & ~int32_t(WM_FLAG_SKIP_NEGATIVE_ROUTES | WM_FLAG_TCGEN05_DECODE)) {
     report("unknown flags");
     return nullptr;
   }
@@ -428,7 +478,7 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
   const int64_t T = o.max_tokens, K = o.max_topk, E = o.max_experts, H = o.max_hidden, I = o.max_inter;
   const int64_t rows = T * K + T + int64_t(wm::kTileM) * (E + 1);
   ctx->max_rows = int(rows);
-  ctx->max_mtiles = int(std::max(rows / wm::kTileM + E + 2, (T * K + T) / 16 + E + 2));
+  ctx->max_mtiles = int(std::max(rows / wm::kTileM + E + 2, (T * K + T) / 8 + E + 2));
   ctx->max_chunks = 1024;
   // workspace layout
   size_t off = 0;
@@ -487,6 +537,7 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
   wm::gemv_init_attributes(int(gemv_smem));
   wm::gemm_init_attributes();
   wm::decode_init_attributes();
+  wm::decode_mma_init_attributes(int(H), int(I));
   wm::router_init_attributes(int(H));
   wm::router_gemm_init_attributes();
   cudaDriverEntryPointQueryResult q{};
@@ -597,7 +648,7 @@ WM_EXPORT int wm_expert_pairs(wm_ctx* ctx, const wm_moe_args* a, void* routed, v
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const Path path = expert_path(ctx, &b, false);
   wm::Plan plan = ctx->plan;
-  if (path == kPathDecode) plan.rowmax = ctx->rowmax;
+  plan_for_path(ctx, path, &plan);
   plan.skip_negative = (ctx->opt.flags & WM_FLAG_SKIP_NEGATIVE_ROUTES) ? 1 : 0;
   int launches = 0;
   wm::prof_begin(&ctx->prof, wm::kProfPlan, s);
@@ -686,7 +737,7 @@ WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* a, void* stream) {
   const bool has_shared = a->shared_gate != WM_SHARED_NONE;
   const Path path = expert_path(ctx, a, has_shared);
   wm::Plan plan = ctx->plan;
-  if (path == kPathDecode) plan.rowmax = ctx->rowmax;
+  plan_for_path(ctx, path, &plan);
   plan.skip_negative = (ctx->opt.flags & WM_FLAG_SKIP_NEGATIVE_ROUTES) ? 1 : 0;
   const int32_t* idx;
   const float* w;

@@ -1,0 +1,421 @@
+// Decode path, register-direct: every warp streams its own weight rows with
+// 16-byte loads, dequantises the E2M1 nibbles in registers straight into the
+// A fragments of mma.sync.m16n8k16 (f16 x f16 -> fp32), and multiplies them
+// by the (at most 8) token rows of its item, the N = 8 operand.  No weight
+// byte passes through shared memory or TMEM and no warp waits on another
+// warp inside an item, so the loads of many warps stay in flight at once and
+// HBM, not a chain of hand-offs, sets the pace.
+//
+// Reference arithmetic: the decode GEMVs expert_linear4 / expert_group<R, K>
+// (QwenNative/kernels.metal:1186-1219, DeepSeekNative/kernels.metal:933-987)
+// and mx.quantized_matmul(mode="mxfp4") (model.py:504-513): exact dequantised
+// weights times the activation rows, fp32 accumulation.  The f16 operands are
+// exact, as in the tcgen05 decode kernel:
+//   * weight = E2M1 * 2^(s - smax_r) with smax_r the row's largest E8M0 byte
+//     (<= 6: exact in f16 for every group within 23 binades of the row's
+//     largest); the epilogue applies 2^(smax_r - 127);
+//   * activation rows are the f16 copies of gather_f16 / act_f16, scaled by
+//     2^k per row; the epilogue divides by 2^k.
+//
+// Work: an item is (8-token tile of one expert, block of weight rows).  A CTA
+// of 16 warps takes one item at a time; warp w owns 32 of its weight rows
+// (two 16-row MMA tiles).  For gate/up a 16-row tile is 8 gate rows and the
+// 8 up rows of the same features, so SwiGLU runs on the accumulators.  The
+// item's f16 token tile (TMA, 128-byte swizzle) and its E8M0 scale block (one
+// or two bulk copies) land in shared memory, double-buffered; the warp that
+// finishes an item last refills that buffer for the item after next.  The
+// weight loads run kStages chunks ahead across item boundaries.
+//
+// Per thread (lane = 4g + t): weight row g and g + 8 of each 16-row tile, and
+// for chunk c (128 K) the 16 bytes at K offset 128c + 32t: 32 consecutive
+// weights = exactly one scale group (4c + t).  K step j (of 8) of the chunk
+// feeds MMA slots {2t, 2t+1} with K offsets 4j, 4j+1 and slots {2t+8, 2t+9}
+// with 4j+2, 4j+3; the token operand uses the same K positions, so the MMA
+// sums the same products as the reference in another order.
+#include <cuda.h>
+
+#include "wm_kernels.h"
+
+namespace wm {
+
+namespace {
+
+constexpr int kWarps = 16;
+constexpr int kThreads = 32 * kWarps;
+constexpr int kTok = 8;      // tokens per item (the MMA's N)
+constexpr int kRG = 2;       // 16-row MMA tiles per warp
+constexpr int kStages = 3;   // chunks of weight loads in flight per thread
+constexpr int kFeatItem = kWarps * kRG * 8;   // gate/up: features per item
+constexpr int kRowsItem = kWarps * kRG * 16;  // down: output rows per item
+
+struct QShared {
+  uint64_t full[2];
+  int done[2];  // warps finished with the buffer's item
+  int abort;
+};
+
+__host__ __device__ constexpr int q_round1k(int v) { return (v + 1023) & ~1023; }
+
+// Bytes of one buffer: the token tile (K/64 boxes of 8 rows x 128 B) and the scale block.
+__host__ __device__ inline int q_xbytes(int K) { return kTok * K * 2; }
+__host__ __device__ inline int q_sbytes(int kind, int K) { return (kind == 0 ? 2 * kFeatItem : kRowsItem) * (K / 32); }
+__host__ __device__ inline int q_bufbytes(int kind, int K) { return q_round1k(q_xbytes(K) + q_sbytes(kind, K)); }
+
+size_t q_smem_bytes(int kind, int K) { return size_t(2 * q_bufbytes(kind, K)) + 1024 + 128; }
+
+__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint32_t lds_u8q(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint4 lds_v4q(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint32_t hmul2q(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// Four E2M1 pairs of one word -> four f16x2 (pair p = byte p, low nibble in the low half).
+__device__ __forceinline__ void e2m1x8_f16x2(uint32_t w, uint32_t* h) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+      : "r"(w));
+}
+
+// f16x2 holding 2^(s - smax) twice; 0 for the E8M0 byte 0 and below f16's range.
+__device__ __forceinline__ uint32_t group_mult(uint32_t s, int smax) {
+  const int d = max(int(s) - smax, -100);
+  const float f = __uint_as_float(uint32_t(d + 127) << 23);
+  uint32_t h;
+  asm("cvt.rn.f16x2.f32 %0, %1, %1;" : "=r"(h) : "f"(f));
+  return s == 0u ? 0u : h;
+}
+
+__device__ __forceinline__ void mma_f16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_q(uint32_t dst, const void* tmap, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(dst),
+      "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Item -> (expert, first sorted row, valid tokens, row block).
+struct QItem {
+  int e, row0, valid, blk;
+};
+
+__device__ __forceinline__ QItem q_item(const DecodeArgs& a, int q, int nb) {
+  QItem it;
+  const int ent = q / nb;
+  it.blk = q - ent * nb;
+  it.e = a.plan.mtiles[2 * ent];
+  it.row0 = a.plan.mtiles[2 * ent + 1];
+  it.valid = min(kTok, a.plan.counts[it.e] - (it.row0 - a.plan.offsets[it.e]));
+  return it;
+}
+
+}  // namespace
+
+// KIND 0: gate/up (+SwiGLU) -> act [rows, I] bf16 and per-row |act| maxima;
+// KIND 1: down -> routed [rows, H] bf16.  tm_x: the f16 token rows
+// ([max_rows, K], boxes of 64 x 8, 128-byte swizzle).
+template <int KIND>
+__global__ void __launch_bounds__(kThreads, 1) decode_mma_kernel(const __grid_constant__ CUtensorMap tm_x,
+                                                                 const DecodeArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  const int K = KIND == 0 ? a.H : a.I;
+  const int S = K / 32;       // E8M0 bytes per weight row
+  const int KC = K / 128;     // chunks per row
+  const int64_t rowb = K / 2; // packed bytes per weight row
+  const int xbytes = q_xbytes(K), bufbytes = q_bufbytes(KIND, K);
+  const uint32_t raw0 = smem_u32(smem_raw);
+  const uint32_t base = (raw0 + 1023u) & ~1023u;
+  QShared& sh = *reinterpret_cast<QShared*>(smem_raw + (base - raw0) + 2 * bufbytes);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int nb = KIND == 0 ? a.I / kFeatItem : a.H / kRowsItem;  // row blocks per token tile
+  const int n_items = *a.plan.n_mtiles * nb;
+  const int gate_base = a.gate_first ? 0 : a.I, up_base = a.gate_first ? a.I : 0;
+
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sh.full[b], 1);
+      sh.done[b] = 0;
+    }
+    sh.abort = 0;
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  volatile int* abort = &sh.abort;
+
+  // Issues the token tile and scale block of item q into buffer b.
+  auto issue = [&](int q, int b) {
+    const QItem it = q_item(a, q, nb);
+    const uint32_t xdst = base + b * bufbytes, sdst = xdst + xbytes;
+    mbar_arrive_expect_tx(&sh.full[b], uint32_t(xbytes + q_sbytes(KIND, K)));
+    for (int kb = 0; kb < K / 64; ++kb) tma_load_2d_q(xdst + kb * 1024, &tm_x, kb * 64, it.row0, &sh.full[b]);
+    if (KIND == 0) {
+      const uint8_t* s = a.wts.s13_of(it.e);
+      bulk_load(sdst, s + int64_t(gate_base + it.blk * kFeatItem) * S, kFeatItem * S, &sh.full[b]);
+      bulk_load(sdst + kFeatItem * S, s + int64_t(up_base + it.blk * kFeatItem) * S, kFeatItem * S, &sh.full[b]);
+    } else {
+      bulk_load(sdst, a.wts.s2_of(it.e) + int64_t(it.blk) * kRowsItem * S, kRowsItem * S, &sh.full[b]);
+    }
+  };
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tm_x);
+    for (int b = 0; b < 2; ++b)
+      if (int(blockIdx.x) + b * int(gridDim.x) < n_items) issue(blockIdx.x + b * gridDim.x, b);
+  }
+
+  // This thread's four weight rows, j = 2r + h: MMA tile r, fragment row g (h = 0) or g + 8 (h = 1).
+  // Weight-row offsets from row j = 0, and scale-block rows.
+  int64_t roff[2 * kRG];
+  int srow[2 * kRG];
+#pragma unroll
+  for (int r = 0; r < kRG; ++r)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      if (KIND == 0) {
+        roff[2 * r + h] = (int64_t(h ? up_base - gate_base : 0) + 8 * r) * rowb;
+        srow[2 * r + h] = h * kFeatItem + warp * (kRG * 8) + 8 * r + g;
+      } else {
+        roff[2 * r + h] = int64_t(16 * r + 8 * h) * rowb;
+        srow[2 * r + h] = warp * (kRG * 16) + 16 * r + 8 * h + g;
+      }
+    }
+  // First weight row of this thread in item `it` (plus its 16-byte column).
+  auto row_ptr = [&](const QItem& it) -> const uint8_t* {
+    if (KIND == 0)
+      return a.wts.w13_of(it.e) + int64_t(gate_base + it.blk * kFeatItem + warp * (kRG * 8) + g) * rowb + 16 * t;
+    return a.wts.w2_of(it.e) + int64_t(it.blk * kRowsItem + warp * (kRG * 16) + g) * rowb + 16 * t;
+  };
+
+  // Load cursor: item (lq) and chunk (lc) of the next chunk to load.
+  int lq = blockIdx.x, lc = 0;
+  const uint8_t* lp = lq < n_items ? row_ptr(q_item(a, lq, nb)) : nullptr;
+  uint4 wr[kStages][2 * kRG];
+  auto load_next = [&](uint4 (&dst)[2 * kRG]) {
+    if (lq < n_items) {
+#pragma unroll
+      for (int j = 0; j < 2 * kRG; ++j) dst[j] = ldg_nc_v4(lp + roff[j] + 64 * lc);
+      if (++lc == KC) {
+        lc = 0;
+        lq += gridDim.x;
+        if (lq < n_items) lp = row_ptr(q_item(a, lq, nb));
+      }
+    }
+  };
+#pragma unroll
+  for (int s = 0; s < kStages; ++s) load_next(wr[s]);
+
+  // Consumer state of the current item.
+  int cq = blockIdx.x, cc = 0, li = 0;  // item, chunk, local item counter
+  QItem cur{};
+  int smax[2 * kRG];
+  float acc[kRG][4];
+  uint32_t xb = 0, sb = 0;
+  bool alive = cq < n_items;
+
+  auto begin_item = [&]() -> bool {
+    cur = q_item(a, cq, nb);
+    const int b = li & 1;
+    if (!warp_wait(&sh.full[b], (li >> 1) & 1, abort)) {
+      if (lane == 0 && !*abort) {
+        report_status(a.status, kStatusWaitTimeout, 40 + KIND);
+        sh.abort = 1;
+      }
+      return false;
+    }
+    xb = base + b * bufbytes;
+    sb = xb + xbytes;
+    // largest E8M0 byte of each of this thread's rows (the four t lanes split a row)
+#pragma unroll
+    for (int j = 0; j < 2 * kRG; ++j) {
+      const uint32_t rb = sb + srow[j] * S + t * (S / 4);
+      uint32_t m = 0;
+      if ((S & 15) == 0) {  // a lane's S / 4 bytes are whole, aligned words
+        for (int i = 0; i < S / 4; i += 4) m = __vmaxu4(m, lds_u32(rb + i));
+        m = max(max(m & 0xffu, (m >> 8) & 0xffu), max((m >> 16) & 0xffu, m >> 24));
+      } else {
+        for (int i = 0; i < S / 4; ++i) m = max(m, lds_u8q(rb + i));
+      }
+      m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+      m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
+      smax[j] = int(m);
+    }
+#pragma unroll
+    for (int r = 0; r < kRG; ++r)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[r][i] = 0.0f;
+    return true;
+  };
+
+  auto end_item = [&]() {
+    const int n0 = 2 * t, n1 = 2 * t + 1;
+    const float is0 = n0 < cur.valid ? 1.0f / a.bscale[cur.row0 + n0] : 0.0f;
+    const float is1 = n1 < cur.valid ? 1.0f / a.bscale[cur.row0 + n1] : 0.0f;
+    if (KIND == 0) {
+      float m0 = 0.0f, m1 = 0.0f;
+#pragma unroll
+      for (int r = 0; r < kRG; ++r) {
+        const float fg = e8m0_to_f32(uint32_t(smax[2 * r])), fu = e8m0_to_f32(uint32_t(smax[2 * r + 1]));
+        const int f = cur.blk * kFeatItem + warp * (kRG * 8) + 8 * r + g;
+        if (n0 < cur.valid) {
+          const float gv = bf16_round(acc[r][0] * fg * is0), uv = bf16_round(acc[r][2] * fu * is0);
+          const uint16_t bits = f32_to_bf16_bits(swiglu_f32(gv, uv, a.limit));
+          a.act[int64_t(cur.row0 + n0) * a.I + f] = bits;
+          m0 = fmaxf(m0, fabsf(bf16_bits_to_f32(bits)));
+        }
+        if (n1 < cur.valid) {
+          const float gv = bf16_round(acc[r][1] * fg * is1), uv = bf16_round(acc[r][3] * fu * is1);
+          const uint16_t bits = f32_to_bf16_bits(swiglu_f32(gv, uv, a.limit));
+          a.act[int64_t(cur.row0 + n1) * a.I + f] = bits;
+          m1 = fmaxf(m1, fabsf(bf16_bits_to_f32(bits)));
+        }
+      }
+      // per-token maxima over the warp's features (lanes with the same t)
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+      }
+      if (g == 0) {
+        if (n0 < cur.valid) atomicMax(a.plan.rowmax + cur.row0 + n0, __float_as_uint(m0));
+        if (n1 < cur.valid) atomicMax(a.plan.rowmax + cur.row0 + n1, __float_as_uint(m1));
+      }
+    } else {
+#pragma unroll
+      for (int r = 0; r < kRG; ++r)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float fr = e8m0_to_f32(uint32_t(smax[2 * r + h]));
+          const int hc = cur.blk * kRowsItem + warp * (kRG * 16) + 16 * r + 8 * h + g;
+          if (n0 < cur.valid) a.routed[int64_t(cur.row0 + n0) * a.H + hc] = f32_to_bf16_bits(acc[r][2 * h] * fr * is0);
+          if (n1 < cur.valid)
+            a.routed[int64_t(cur.row0 + n1) * a.H + hc] = f32_to_bf16_bits(acc[r][2 * h + 1] * fr * is1);
+        }
+    }
+    // release the buffer; the last warp refills it with the item after next
+    __syncwarp();
+    if (lane == 0) {
+      const int b = li & 1;
+      __threadfence_block();
+      if (atomicAdd(&sh.done[b], 1) == kWarps - 1) {
+        sh.done[b] = 0;
+        const int nq = cq + 2 * gridDim.x;
+        if (nq < n_items && !*abort) issue(nq, b);
+      }
+    }
+    __syncwarp();
+  };
+
+  // One chunk of the current item from the weight registers w.
+  auto chunk = [&](const uint4 (&w)[2 * kRG]) {
+    uint32_t mult[2 * kRG];
+#pragma unroll
+    for (int j = 0; j < 2 * kRG; ++j) mult[j] = group_mult(lds_u8q(sb + srow[j] * S + 4 * cc + t), smax[j]);
+    // token operand: 32 f16 at K offset 128cc + 32t of token row g (4 swizzled 16-byte units)
+    const int kb = 2 * cc + (t >> 1);
+    const uint32_t xrow = xb + kb * 1024 + g * 128;
+    uint4 xv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) xv[u] = lds_v4q(xrow + (((4 * (t & 1) + u) ^ g) << 4));
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {  // word q of the 16 bytes: K offsets 8q .. 8q + 7 = steps 2q, 2q + 1
+      const uint32_t xw[4] = {xv[q].x, xv[q].y, xv[q].z, xv[q].w};
+#pragma unroll
+      for (int r = 0; r < kRG; ++r) {
+        const uint4& wa = w[2 * r];
+        const uint4& wb = w[2 * r + 1];
+        const uint32_t va = q == 0 ? wa.x : q == 1 ? wa.y : q == 2 ? wa.z : wa.w;
+        const uint32_t vb = q == 0 ? wb.x : q == 1 ? wb.y : q == 2 ? wb.z : wb.w;
+        uint32_t ha[4], hb[4];
+        e2m1x8_f16x2(va, ha);
+        e2m1x8_f16x2(vb, hb);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          ha[p] = hmul2q(ha[p], mult[2 * r]);
+          hb[p] = hmul2q(hb[p], mult[2 * r + 1]);
+        }
+        // step 2q: bytes 0, 1 (K 8q .. 8q+3); step 2q + 1: bytes 2, 3 (K 8q+4 .. 8q+7)
+        mma_f16(acc[r], ha[0], hb[0], ha[1], hb[1], xw[0], xw[1]);
+        mma_f16(acc[r], ha[2], hb[2], ha[3], hb[3], xw[2], xw[3]);
+      }
+    }
+  };
+
+  if (alive) alive = begin_item();
+  while (alive) {
+#pragma unroll
+    for (int s = 0; s < kStages && alive; ++s) {
+      chunk(wr[s]);
+      load_next(wr[s]);
+      if (++cc == KC) {
+        end_item();
+        cc = 0;
+        ++li;
+        cq += gridDim.x;
+        alive = cq < n_items && !warp_aborted(abort);
+        if (alive) alive = begin_item();
+      }
+    }
+  }
+  __syncthreads();
+}
+
+bool decode_mma_shape_ok(int H, int I) {
+  return I % kFeatItem == 0 && H % kRowsItem == 0 && H % 128 == 0 && I % 128 == 0 &&
+         q_smem_bytes(0, H) <= 227 * 1024 && q_smem_bytes(1, I) <= 227 * 1024;
+}
+
+void decode_mma_init_attributes(int max_h, int max_i) {
+  cudaFuncSetAttribute(decode_mma_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       int(q_smem_bytes(0, max_h)));
+  cudaFuncSetAttribute(decode_mma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       int(q_smem_bytes(1, max_i)));
+}
+
+void launch_decode_mma(const DecodeArgs& a, int kind, const void* tmap_x, int num_sms, cudaStream_t stream) {
+  const CUtensorMap& x = *static_cast<const CUtensorMap*>(tmap_x);
+  if (kind == 0)
+    decode_mma_kernel<0><<<num_sms, kThreads, q_smem_bytes(0, a.H), stream>>>(x, a);
+  else
+    decode_mma_kernel<1><<<num_sms, kThreads, q_smem_bytes(1, a.I), stream>>>(x, a);
+}
+
+}  // namespace wm

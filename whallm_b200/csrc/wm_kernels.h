@@ -113,6 +113,13 @@ void launch_act_f16(const uint16_t* act, const Plan& p, int E, int I, uint16_t* 
 // K/32 x 64 or 128), and the f16 activation rows (2-D, 64 x 16, 128B swizzle).
 void launch_decode(const DecodeArgs& a, int kind, const void* const* maps, int num_sms, cudaStream_t stream);
 
+// ---- decode, register-direct warp MMAs (wm_decode_mma.cu): plan tiles of 8
+// rows; tmap_x points to a CUtensorMap of the f16 activation rows [max_rows, K]
+// (boxes of 64 x 8, 128-byte swizzle), K = H for kind 0 (gate/up) and I for kind 1.
+bool decode_mma_shape_ok(int H, int I);
+void decode_mma_init_attributes(int max_h, int max_i);
+void launch_decode_mma(const DecodeArgs& a, int kind, const void* tmap_x, int num_sms, cudaStream_t stream);
+
 // ---- prefill grouped GEMM on tcgen05 (wm_gemm_sm100.cu)
 struct GemmArgs {
   Plan plan;

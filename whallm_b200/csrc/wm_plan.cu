@@ -60,7 +60,7 @@ __device__ int block_exclusive_scan(int n, F value, G store) {
 // From per-expert counts in shared memory: offsets, unique list, row-tile
 // list and padding rows.  `cnt` holds E + 1 counts (index E = shared expert).
 // Tiles are `align` rows (the GEMM's 128-row tiles) when the groups are
-// padded, else 16 rows (the decode kernel's token chunks).
+// padded, else p.tile_rows rows (the decode kernels' token chunks; 16 when 0).
 __device__ void finish_plan(const int* cnt, int* off, int E, int align, Plan p, int max_rows, int max_mtiles,
                             uint32_t* status) {
   const int total = block_exclusive_scan(
@@ -80,7 +80,7 @@ __device__ void finish_plan(const int* cnt, int* off, int E, int align, Plan p, 
       [&](int i, int v) {
         if (cnt[i] > 0) p.unique[v] = i;
       });
-  const int tile = align > 16 ? align : 16;
+  const int tile = align > 1 ? align : (p.tile_rows > 0 ? p.tile_rows : 16);
   const int nm = block_exclusive_scan(
       E + 1, [&](int i) { return (cnt[i] + tile - 1) / tile; },
       [&](int i, int v) {

@@ -25,6 +25,7 @@ struct Plan {
   int32_t* hist;       // [chunks * (E + 1)] per-chunk counts (large-T sort)
   uint32_t* rowmax;    // [max_rows] or null: zeroed by the plan (decode activation maxima)
   int32_t skip_negative;  // 1: routes < 0 are padding (no row, no error), else an error
+  int32_t tile_rows;      // rows per tile of unpadded groups (0: 16)
 };
 
 // Where the weights of every expert live (expert E = the shared expert).
