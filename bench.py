@@ -36,7 +36,7 @@ H, I, E, K = 2048, 512, 512, 10
 BLOB = 1_671_168  # bytes of one expert blob (gate_up + scales + down + scales)
 GATE_UP_BYTES = 2 * I * H // 2 + 2 * I * H // 32
 # dram bytes (read + write) of one gate/up decode launch at this workload, from an ncu capture
-NCU_GATE_UP_TRAFFIC = 411.845632e6 + 4.414976e6
+NCU_GATE_UP_TRAFFIC = 416.297216e6 + 4.186368e6
 DOWN_BYTES = H * I // 2 + H * I // 32
 
 
@@ -512,11 +512,11 @@ def run(args) -> None:
                    "timing": "CUDA graph replay per step, device events, max over ranks",
                    "parallelism": "single GPU",
                    "unique_experts_per_step": U},
-        "roofline": {"bound": "hbm", "kernel": "decode_kernel<0> (gate/up + SwiGLU)", "achieved": achieved,
+        "roofline": {"bound": "hbm", "kernel": "decode_mma_kernel<0> (gate/up + SwiGLU)", "achieved": achieved,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
                      "peak_source": pk["source"], "traffic": NCU_GATE_UP_TRAFFIC,
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch, "
-                                       "profiles/decode_config1_b64.txt",
+                                       "profiles/decode_mma_config1_b64.txt",
                      "algorithmic_bytes_per_launch": gu_bytes,
                      "down_achieved_gbs": dn_bytes / (dn_ms / dn_n / 1e3) / 1e9},
         "kernels": kernels,

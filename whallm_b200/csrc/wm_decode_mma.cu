@@ -24,7 +24,16 @@
 // item's f16 token tile (TMA, 128-byte swizzle) and its E8M0 scale block (one
 // or two bulk copies) land in shared memory, double-buffered; the warp that
 // finishes an item last refills that buffer for the item after next.  The
-// weight loads run kStages chunks ahead across item boundaries.
+// weight loads run kStages chunks ahead across item boundaries; the metadata
+// of the next items is read an item early, so no load waits on another.
+//
+// Measured on B200 (config-1 decode, 64 tokens): gate/up ~100 us for 407 MB
+// (4.1 TB/s), down ~62 us.  Two limits meet there: this row-striped access
+// (64 bytes of each row per chunk) streams at most ~4.4 TB/s, and with the
+// weight loads removed the kernel still takes ~72 us (about 1.6 issued
+// instructions per weight: dequantisation, scaling, MMAs).  Deeper rings
+// (3-4 chunks), two CTAs per SM, 16 rows per warp, TMA-fed shared-memory
+// rings of whole 128-byte lines and L2 prefetch hints all measured slower.
 //
 // Per thread (lane = 4g + t): weight row g and g + 8 of each 16-row tile, and
 // for chunk c (128 K) the 16 bytes at K offset 128c + 32t: 32 consecutive
@@ -34,17 +43,20 @@
 // sums the same products as the reference in another order.
 #include <cuda.h>
 
+#include <algorithm>
+
 #include "wm_kernels.h"
 
 namespace wm {
 
 namespace {
 
-constexpr int kWarps = 16;
+constexpr int kWarps = 16;   // warps per CTA
+constexpr int kCtas = 1;     // CTAs per SM (two measured slower)
 constexpr int kThreads = 32 * kWarps;
 constexpr int kTok = 8;      // tokens per item (the MMA's N)
 constexpr int kRG = 2;       // 16-row MMA tiles per warp
-constexpr int kStages = 3;   // chunks of weight loads in flight per thread
+constexpr int kStages = 2;   // chunks of weight loads in flight per thread
 constexpr int kFeatItem = kWarps * kRG * 8;   // gate/up: features per item
 constexpr int kRowsItem = kWarps * kRG * 16;  // down: output rows per item
 
@@ -100,13 +112,14 @@ __device__ __forceinline__ void e2m1x8_f16x2(uint32_t w, uint32_t* h) {
       : "r"(w));
 }
 
-// f16x2 holding 2^(s - smax) twice; 0 for the E8M0 byte 0 and below f16's range.
-__device__ __forceinline__ uint32_t group_mult(uint32_t s, int smax) {
-  const int d = max(int(s) - smax, -100);
-  const float f = __uint_as_float(uint32_t(d + 127) << 23);
+// f16x2 holding 2^(s - smax) twice, given rinv = 2^(127 - smax): the E8M0
+// byte s as a float is 2^(s - 127) (0 for s = 0, the Metal convention), the
+// product is exact and rounds to 0 below f16's range.
+__device__ __forceinline__ uint32_t group_mult(uint32_t s, float rinv) {
+  const float f = __uint_as_float(s << 23) * rinv;
   uint32_t h;
   asm("cvt.rn.f16x2.f32 %0, %1, %1;" : "=r"(h) : "f"(f));
-  return s == 0u ? 0u : h;
+  return h;
 }
 
 __device__ __forceinline__ void mma_f16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -153,7 +166,7 @@ __device__ __forceinline__ QItem q_item(const DecodeArgs& a, int q, int nb) {
 // KIND 1: down -> routed [rows, H] bf16.  tm_x: the f16 token rows
 // ([max_rows, K], boxes of 64 x 8, 128-byte swizzle).
 template <int KIND>
-__global__ void __launch_bounds__(kThreads, 1) decode_mma_kernel(const __grid_constant__ CUtensorMap tm_x,
+__global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __grid_constant__ CUtensorMap tm_x,
                                                                  const DecodeArgs a) {
   extern __shared__ uint8_t smem_raw[];
   const int K = KIND == 0 ? a.H : a.I;
@@ -182,9 +195,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mma_kernel(const __grid_co
   __syncthreads();
   volatile int* abort = &sh.abort;
 
-  // Issues the token tile and scale block of item q into buffer b.
-  auto issue = [&](int q, int b) {
-    const QItem it = q_item(a, q, nb);
+  // Issues the token tile and scale block of item `it` into buffer b.
+  auto issue = [&](const QItem& it, int b) {
     const uint32_t xdst = base + b * bufbytes, sdst = xdst + xbytes;
     mbar_arrive_expect_tx(&sh.full[b], uint32_t(xbytes + q_sbytes(KIND, K)));
     for (int kb = 0; kb < K / 64; ++kb) tma_load_2d_q(xdst + kb * 1024, &tm_x, kb * 64, it.row0, &sh.full[b]);
@@ -199,7 +211,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mma_kernel(const __grid_co
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tm_x);
     for (int b = 0; b < 2; ++b)
-      if (int(blockIdx.x) + b * int(gridDim.x) < n_items) issue(blockIdx.x + b * gridDim.x, b);
+      if (int(blockIdx.x) + b * int(gridDim.x) < n_items) issue(q_item(a, blockIdx.x + b * gridDim.x, nb), b);
   }
 
   // This thread's four weight rows, j = 2r + h: MMA tile r, fragment row g (h = 0) or g + 8 (h = 1).
@@ -225,9 +237,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mma_kernel(const __grid_co
     return a.wts.w2_of(it.e) + int64_t(it.blk * kRowsItem + warp * (kRG * 16) + g) * rowb + 16 * t;
   };
 
-  // Load cursor: item (lq) and chunk (lc) of the next chunk to load.
+  // Item metadata, fetched an item before it is needed (q beyond the list: unused).
+  auto fetch = [&](int q) -> QItem { return q < n_items ? q_item(a, q, nb) : QItem{0, 0, 0, 0}; };
+
+  // Load cursor: item (lq) and chunk (lc) of the next chunk to load; lnext =
+  // metadata of item lq + gridDim.x.
   int lq = blockIdx.x, lc = 0;
   const uint8_t* lp = lq < n_items ? row_ptr(q_item(a, lq, nb)) : nullptr;
+  QItem lnext = fetch(lq + gridDim.x);
   uint4 wr[kStages][2 * kRG];
   auto load_next = [&](uint4 (&dst)[2 * kRG]) {
     if (lq < n_items) {
@@ -236,23 +253,32 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mma_kernel(const __grid_co
       if (++lc == KC) {
         lc = 0;
         lq += gridDim.x;
-        if (lq < n_items) lp = row_ptr(q_item(a, lq, nb));
+        lp = row_ptr(lnext);
+        lnext = fetch(lq + gridDim.x);
       }
     }
   };
 #pragma unroll
   for (int s = 0; s < kStages; ++s) load_next(wr[s]);
 
-  // Consumer state of the current item.
+  // Consumer state of the current item; nxt / nxt2 = metadata of the next
+  // two items of this CTA (nxt2 feeds the refill of the buffer), bs = the
+  // prescales of this thread's two tokens.
   int cq = blockIdx.x, cc = 0, li = 0;  // item, chunk, local item counter
-  QItem cur{};
+  QItem cur{}, nxt = fetch(cq), nxt2{};
+  float bs0 = 1.0f, bs1 = 1.0f;
+  float rinv[2 * kRG];
   int smax[2 * kRG];
-  float acc[kRG][4];
+  float acc[kRG][2][4];  // per MMA tile, even and odd K steps (two independent chains)
   uint32_t xb = 0, sb = 0;
   bool alive = cq < n_items;
 
   auto begin_item = [&]() -> bool {
-    cur = q_item(a, cq, nb);
+    cur = nxt;
+    nxt = fetch(cq + gridDim.x);
+    nxt2 = fetch(cq + 2 * gridDim.x);
+    bs0 = 2 * t < cur.valid ? a.bscale[cur.row0 + 2 * t] : 1.0f;
+    bs1 = 2 * t + 1 < cur.valid ? a.bscale[cur.row0 + 2 * t + 1] : 1.0f;
     const int b = li & 1;
     if (!warp_wait(&sh.full[b], (li >> 1) & 1, abort)) {
       if (lane == 0 && !*abort) {
@@ -277,18 +303,23 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mma_kernel(const __grid_co
       m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
       m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
       smax[j] = int(m);
+      rinv[j] = __uint_as_float(uint32_t(254 - min(int(m), 254)) << 23);
     }
 #pragma unroll
     for (int r = 0; r < kRG; ++r)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) acc[r][i] = 0.0f;
+      for (int i = 0; i < 4; ++i) acc[r][0][i] = acc[r][1][i] = 0.0f;
     return true;
   };
 
   auto end_item = [&]() {
     const int n0 = 2 * t, n1 = 2 * t + 1;
-    const float is0 = n0 < cur.valid ? 1.0f / a.bscale[cur.row0 + n0] : 0.0f;
-    const float is1 = n1 < cur.valid ? 1.0f / a.bscale[cur.row0 + n1] : 0.0f;
+    float y[kRG][4];
+#pragma unroll
+    for (int r = 0; r < kRG; ++r)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) y[r][i] = acc[r][0][i] + acc[r][1][i];
+    const float is0 = 1.0f / bs0, is1 = 1.0f / bs1;
     if (KIND == 0) {
       float m0 = 0.0f, m1 = 0.0f;
 #pragma unroll
@@ -296,13 +327,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mma_kernel(const __grid_co
         const float fg = e8m0_to_f32(uint32_t(smax[2 * r])), fu = e8m0_to_f32(uint32_t(smax[2 * r + 1]));
         const int f = cur.blk * kFeatItem + warp * (kRG * 8) + 8 * r + g;
         if (n0 < cur.valid) {
-          const float gv = bf16_round(acc[r][0] * fg * is0), uv = bf16_round(acc[r][2] * fu * is0);
+          const float gv = bf16_round(y[r][0] * fg * is0), uv = bf16_round(y[r][2] * fu * is0);
           const uint16_t bits = f32_to_bf16_bits(swiglu_f32(gv, uv, a.limit));
           a.act[int64_t(cur.row0 + n0) * a.I + f] = bits;
           m0 = fmaxf(m0, fabsf(bf16_bits_to_f32(bits)));
         }
         if (n1 < cur.valid) {
-          const float gv = bf16_round(acc[r][1] * fg * is1), uv = bf16_round(acc[r][3] * fu * is1);
+          const float gv = bf16_round(y[r][1] * fg * is1), uv = bf16_round(y[r][3] * fu * is1);
           const uint16_t bits = f32_to_bf16_bits(swiglu_f32(gv, uv, a.limit));
           a.act[int64_t(cur.row0 + n1) * a.I + f] = bits;
           m1 = fmaxf(m1, fabsf(bf16_bits_to_f32(bits)));
@@ -325,9 +356,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mma_kernel(const __grid_co
         for (int h = 0; h < 2; ++h) {
           const float fr = e8m0_to_f32(uint32_t(smax[2 * r + h]));
           const int hc = cur.blk * kRowsItem + warp * (kRG * 16) + 16 * r + 8 * h + g;
-          if (n0 < cur.valid) a.routed[int64_t(cur.row0 + n0) * a.H + hc] = f32_to_bf16_bits(acc[r][2 * h] * fr * is0);
+          if (n0 < cur.valid) a.routed[int64_t(cur.row0 + n0) * a.H + hc] = f32_to_bf16_bits(y[r][2 * h] * fr * is0);
           if (n1 < cur.valid)
-            a.routed[int64_t(cur.row0 + n1) * a.H + hc] = f32_to_bf16_bits(acc[r][2 * h + 1] * fr * is1);
+            a.routed[int64_t(cur.row0 + n1) * a.H + hc] = f32_to_bf16_bits(y[r][2 * h + 1] * fr * is1);
         }
     }
     // release the buffer; the last warp refills it with the item after next
@@ -337,18 +368,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mma_kernel(const __grid_co
       __threadfence_block();
       if (atomicAdd(&sh.done[b], 1) == kWarps - 1) {
         sh.done[b] = 0;
-        const int nq = cq + 2 * gridDim.x;
-        if (nq < n_items && !*abort) issue(nq, b);
+        if (cq + 2 * int(gridDim.x) < n_items && !*abort) issue(nxt2, b);
       }
     }
     __syncwarp();
   };
 
   // One chunk of the current item from the weight registers w.
-  auto chunk = [&](const uint4 (&w)[2 * kRG]) {
+  auto chunk = [&](const uint4 (&w)[2 * kRG], int cc) {
     uint32_t mult[2 * kRG];
 #pragma unroll
-    for (int j = 0; j < 2 * kRG; ++j) mult[j] = group_mult(lds_u8q(sb + srow[j] * S + 4 * cc + t), smax[j]);
+    for (int j = 0; j < 2 * kRG; ++j) mult[j] = group_mult(lds_u8q(sb + srow[j] * S + 4 * cc + t), rinv[j]);
     // token operand: 32 f16 at K offset 128cc + 32t of token row g (4 swizzled 16-byte units)
     const int kb = 2 * cc + (t >> 1);
     const uint32_t xrow = xb + kb * 1024 + g * 128;
@@ -373,49 +403,52 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mma_kernel(const __grid_co
           hb[p] = hmul2q(hb[p], mult[2 * r + 1]);
         }
         // step 2q: bytes 0, 1 (K 8q .. 8q+3); step 2q + 1: bytes 2, 3 (K 8q+4 .. 8q+7)
-        mma_f16(acc[r], ha[0], hb[0], ha[1], hb[1], xw[0], xw[1]);
-        mma_f16(acc[r], ha[2], hb[2], ha[3], hb[3], xw[2], xw[3]);
+        mma_f16(acc[r][0], ha[0], hb[0], ha[1], hb[1], xw[0], xw[1]);
+        mma_f16(acc[r][1], ha[2], hb[2], ha[3], hb[3], xw[2], xw[3]);
       }
     }
   };
 
+  // Items are whole multiples of kStages chunks (KC % kStages == 0), so the
+  // ring slot of a chunk is static and one copy of the item code serves.
   if (alive) alive = begin_item();
   while (alive) {
+    for (cc = 0; cc < KC; cc += kStages) {
 #pragma unroll
-    for (int s = 0; s < kStages && alive; ++s) {
-      chunk(wr[s]);
-      load_next(wr[s]);
-      if (++cc == KC) {
-        end_item();
-        cc = 0;
-        ++li;
-        cq += gridDim.x;
-        alive = cq < n_items && !warp_aborted(abort);
-        if (alive) alive = begin_item();
+      for (int s = 0; s < kStages; ++s) {
+        chunk(wr[s], cc + s);
+        load_next(wr[s]);
       }
     }
+    end_item();
+    ++li;
+    cq += gridDim.x;
+    alive = cq < n_items && !warp_aborted(abort);
+    if (alive) alive = begin_item();
   }
   __syncthreads();
 }
 
 bool decode_mma_shape_ok(int H, int I) {
-  return I % kFeatItem == 0 && H % kRowsItem == 0 && H % 128 == 0 && I % 128 == 0 &&
+  return I % kFeatItem == 0 && H % kRowsItem == 0 && H % (128 * kStages) == 0 && I % (128 * kStages) == 0 &&
          q_smem_bytes(0, H) <= 227 * 1024 && q_smem_bytes(1, I) <= 227 * 1024;
 }
 
+// Shapes beyond the shared-memory limit never take this kernel (decode_mma_shape_ok).
 void decode_mma_init_attributes(int max_h, int max_i) {
+  const size_t cap = 227 * 1024;
   cudaFuncSetAttribute(decode_mma_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       int(q_smem_bytes(0, max_h)));
+                       int(std::min(q_smem_bytes(0, max_h), cap)));
   cudaFuncSetAttribute(decode_mma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       int(q_smem_bytes(1, max_i)));
+                       int(std::min(q_smem_bytes(1, max_i), cap)));
 }
 
 void launch_decode_mma(const DecodeArgs& a, int kind, const void* tmap_x, int num_sms, cudaStream_t stream) {
   const CUtensorMap& x = *static_cast<const CUtensorMap*>(tmap_x);
   if (kind == 0)
-    decode_mma_kernel<0><<<num_sms, kThreads, q_smem_bytes(0, a.H), stream>>>(x, a);
+    decode_mma_kernel<0><<<num_sms * kCtas, kThreads, q_smem_bytes(0, a.H), stream>>>(x, a);
   else
-    decode_mma_kernel<1><<<num_sms, kThreads, q_smem_bytes(1, a.I), stream>>>(x, a);
+    decode_mma_kernel<1><<<num_sms * kCtas, kThreads, q_smem_bytes(1, a.I), stream>>>(x, a);
 }
 
 }  // namespace wm
