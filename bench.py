@@ -14,6 +14,9 @@ expert-parallel (whallm_b200.ep): every rank owns E/N experts and its own
 all-to-all (weak scaling; eager steps, since the split sizes are read on the
 host).  At N = 1 the line also carries a `prefill` section: the config-2
 layer (16,384 tokens, Zipf(1.1) routing) through the grouped-GEMM path.
+At N = 1 it also carries `long_calls`: one config-3 layer (DeepSeek-style
+FP8, 8192 tokens) and one layer of config 4 (256 decode + 4096 prefill
+tokens, 384 MXFP4 experts of H = 7168, I = 2048), both on the grouped GEMM.
 `--impl reference` times the CPU oracle (the restatement of the reference's
 arithmetic) on a bounded sample of the same workload.
 """
@@ -165,55 +168,77 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def prefill_section(args, dev, pk) -> dict:
-    """Config 2 (T = 16,384, Zipf(1.1) popularity) through the public call."""
+# Long-call sections at N = 1: (config, label, mma kind note).
+LONG_CONFIGS = {
+    2: "config2 prefill layer, 16384 tokens, Zipf(1.1) expert popularity",
+    3: "config3 DeepSeek-style FP8 layer, 8192 tokens, 256 experts (I=2048) + shared, sigmoid group-limited top-8",
+    4: "config4 single layer (of the 8-layer stack): 256 decode + 4096 prefill tokens, 384 MXFP4 experts (I=2048)"
+       " + shared, top-8",
+}
+
+
+def prefill_section(args, dev, pk, n: int = 2) -> dict:
+    """A long call of config n through the public call (grouped-GEMM path)."""
     import torch
     from whallm_b200 import synth
     from whallm_b200.moe import Engine
 
-    wl = synth.config(2, device=dev)
-    T = wl.x.shape[0]
-    eng = Engine(dev.index, max_tokens=T, hidden=H, inter=I, experts=E, topk=K)
+    wl = synth.config(n, device=dev)
+    T, Hn = wl.x.shape
+    lay = wl.layer
+    En, In, Kn = lay.E, lay.I, wl.K
+    eng = Engine(dev.index, max_tokens=T, hidden=Hn, inter=In, experts=En, topk=Kn)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     for _ in range(3):
-        eng.forward(wl.layer, wl.x, K)
+        eng.forward(lay, wl.x, Kn)
     torch.cuda.synchronize()
     steps = max(3, min(args.steps, 10))
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     for i in range(steps):
         flush.zero_()
         evs[i][0].record()
-        eng.forward(wl.layer, wl.x, K)
+        eng.forward(lay, wl.x, Kn)
         evs[i][1].record()
     torch.cuda.synchronize()
     ms = sum(a.elapsed_time(b) for a, b in evs) / steps
     eng.ctx.profile(True)
     eng.ctx.profile_reset()
-    _, (w, idx) = eng.forward(wl.layer, wl.x, K, return_routes=True)
+    _, (w, idx) = eng.forward(lay, wl.x, Kn, return_routes=True)
     torch.cuda.synchronize()
     prof = eng.ctx.profile_read()
     eng.ctx.profile(False)
-    counts = torch.bincount(idx.reshape(-1).long(), minlength=E).cpu()
-    rows = T * K + T  # routed pairs + shared-expert rows
-    gu_flops, dn_flops = 2.0 * rows * H * 2 * I, 2.0 * rows * I * H
+    counts = torch.bincount(idx.reshape(-1).long(), minlength=En).cpu()
+    rows = T * Kn + T  # routed pairs + shared-expert rows
+    gu_flops, dn_flops = 2.0 * rows * Hn * 2 * In, 2.0 * rows * In * Hn
     gu_n, gu_ms = prof.get("gemm_gate_up", (1, float("nan")))
     dn_n, dn_ms = prof.get("gemm_down", (1, float("nan")))
     tf_gu = gu_flops / (gu_ms / gu_n / 1e3) / 1e12
     tf_dn = dn_flops / (dn_ms / dn_n / 1e3) / 1e12
     layer_tf = (gu_flops + dn_flops) / (ms / 1e3) / 1e12
-    fp4_nominal = 9000.0
-    return {
-        "workload": "config2 prefill layer, 16384 tokens, Zipf(1.1) expert popularity", "tokens_per_s": T / (ms / 1e3),
+    fp8 = lay.layout == lib_layout_fp8()
+    nominal = 4500.0 if fp8 else 9000.0
+    out = {
+        "workload": LONG_CONFIGS[n], "tokens_per_s": T / (ms / 1e3),
         "ms_per_layer": ms, "layer_tflops": layer_tf,
         "roofline": {"bound": "tensor", "kernel": "gemm_gate_up", "achieved": tf_gu, "unit": "TFLOP/s",
                      "peak_bf16": pk["bf16_tflops"], "frac_bf16": tf_gu / pk["bf16_tflops"],
-                     "peak_fp4_nominal": fp4_nominal, "frac_fp4_nominal": tf_gu / fp4_nominal,
+                     ("peak_fp8_nominal" if fp8 else "peak_fp4_nominal"): nominal,
+                     ("frac_fp8_nominal" if fp8 else "frac_fp4_nominal"): tf_gu / nominal,
                      "mma_kind": "kind::f16 (bf16 operands, exact dequantised weights)", "peak_source": pk["source"],
                      "down_tflops": tf_dn, "algorithmic_flops_per_launch": gu_flops},
-        "kernels": {n: {"launches": c, "avg_us": 1e3 * t / c} for n, (c, t) in prof.items()},
+        "kernels": {nm: {"launches": c, "avg_us": 1e3 * t / c} for nm, (c, t) in prof.items()},
         "expert_rows": {"max": int(counts.max()), "median": float(counts.float().median()), "min": int(counts.min())},
         "l2": "flushed before every timed step",
     }
+    eng.ctx.close()
+    del wl, lay, eng
+    torch.cuda.empty_cache()
+    return out
+
+
+def lib_layout_fp8() -> int:
+    from whallm_b200 import lib
+    return lib.LAYOUT_W13_FP8_B128
 
 
 def run_ep(args, world: int, rank: int, local: int) -> None:
@@ -500,7 +525,10 @@ def run(args) -> None:
                "sample": f"16 tokens of a config-1 batch, repeated for >= 10 s, OpenMP over {cores} cores"}
 
     del graph
-    prefill = None if args.no_prefill else prefill_section(args, dev, pk)
+    prefill = None if args.no_prefill else prefill_section(args, dev, pk, 2)
+    long_calls = None
+    if not args.no_prefill and not args.no_long:
+        long_calls = {"config3": prefill_section(args, dev, pk, 3), "config4_layer": prefill_section(args, dev, pk, 4)}
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
@@ -525,6 +553,7 @@ def run(args) -> None:
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
         "prefill": prefill,
+        "long_calls": long_calls,
     }
     print(json.dumps(line), flush=True)
 
@@ -538,6 +567,7 @@ def main():
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-long", action="store_true", help="skip the config-3 and config-4 long-call sections")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -85,6 +85,7 @@ ROUTERS = [
     (lib.ROUTER_SQRTSOFTPLUS, 384, 6, "bias", 1, 1, 1.5),
     (lib.ROUTER_SIGMOID, 256, 8, "bias", 1, 1, 1.0),
     (lib.ROUTER_SIGMOID_GROUPED, 256, 8, "bias", 8, 4, 2.5),
+    (lib.ROUTER_SIGMOID, 256, 40, "bias", 1, 1, 1.0),  # K > 32: two selections per lane
 ]
 
 

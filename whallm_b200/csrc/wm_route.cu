@@ -77,6 +77,100 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __re
   }
 }
 
+// Shared-expert gate of one token by one warp: sigmoid(x[t] . g), lanes over
+// 8-element pieces, fp32, xor-tree reduction (shared_gate_kernel uses the same).
+__device__ __forceinline__ float shared_gate_row(const uint16_t* __restrict__ xr, const uint16_t* __restrict__ g,
+                                                 int H, int lane) {
+  float acc = 0.0f;
+  for (int c = lane; c < H / 8; c += 32) {
+    const uint4 wv = *reinterpret_cast<const uint4*>(g + c * 8);
+    const uint4 xv = *reinterpret_cast<const uint4*>(xr + c * 8);
+    float2 p, a;
+    float s = 0.0f;
+    p = unpack_bf16x2(wv.x); a = unpack_bf16x2(xv.x); s = fmaf(a.x, p.x, s); s = fmaf(a.y, p.y, s);
+    p = unpack_bf16x2(wv.y); a = unpack_bf16x2(xv.y); s = fmaf(a.x, p.x, s); s = fmaf(a.y, p.y, s);
+    p = unpack_bf16x2(wv.z); a = unpack_bf16x2(xv.z); s = fmaf(a.x, p.x, s); s = fmaf(a.y, p.y, s);
+    p = unpack_bf16x2(wv.w); a = unpack_bf16x2(xv.w); s = fmaf(a.x, p.x, s); s = fmaf(a.y, p.y, s);
+    acc += s;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  return 1.0f / (1.0f + expf(-acc));
+}
+
+// Logits of short calls on warp MMAs (mma.sync.m16n8k16, bf16 operands,
+// fp32 accumulation).  A CTA computes 16 tokens x 8 experts; its 8 warps split
+// H into 8 slices (all of a slice's loads go out before its MMAs), and warp 0
+// adds the 8 partial tiles in slice order.  Per 64-K step lane (g, t) reads 16
+// contiguous K (32 bytes) of token rows g, g + 8 and of expert row g; MMA step
+// j takes K offsets 16t + 4j .. 16t + 4j + 3 of them for both operands.  The
+// CTA column past the experts computes the shared-expert gate, a warp per token.
+constexpr int kRouterWarps = 8;
+constexpr int kRouterSteps = 4;  // 64-K steps per warp per batch of loads
+__global__ void __launch_bounds__(32 * kRouterWarps) router_logits_mma_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr, const uint16_t* __restrict__ sg_w, int T, int H,
+    int E, float* __restrict__ logits, float* __restrict__ sg) {
+  __shared__ float part[kRouterWarps][32][4];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int t0 = blockIdx.y * 16;
+  if (int(blockIdx.x) * 8 >= E) {  // shared-expert gate
+    for (int r = warp; r < 16; r += kRouterWarps)
+      if (t0 + r < T) {
+        const float v = shared_gate_row(x + int64_t(t0 + r) * H, sg_w, H, lane);
+        if (lane == 0) sg[t0 + r] = v;
+      }
+    return;
+  }
+  const int e = blockIdx.x * 8 + g;
+  const int ra = min(t0 + g, T - 1), rb = min(t0 + g + 8, T - 1);  // rows past T read row T-1, not stored
+  const int steps = H / 64 / kRouterWarps;                          // 64-K steps of this warp's slice
+  const int64_t k0 = int64_t(warp) * steps * 8;                     // first uint4 of the slice
+  const uint4* xa = reinterpret_cast<const uint4*>(x + int64_t(ra) * H) + k0 + 2 * t;
+  const uint4* xb = reinterpret_cast<const uint4*>(x + int64_t(rb) * H) + k0 + 2 * t;
+  const uint4* wp = reinterpret_cast<const uint4*>(wr + int64_t(e) * H) + k0 + 2 * t;
+  float d[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+  for (int k = 0; k < steps; k += kRouterSteps) {
+    uint4 a[kRouterSteps][2], b[kRouterSteps][2], w[kRouterSteps][2];
+#pragma unroll
+    for (int i = 0; i < kRouterSteps; ++i)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const bool in = k + i < steps;
+        a[i][h] = in ? __ldg(xa + 8 * (k + i) + h) : make_uint4(0, 0, 0, 0);
+        b[i][h] = in ? __ldg(xb + 8 * (k + i) + h) : make_uint4(0, 0, 0, 0);
+        w[i][h] = in ? __ldg(wp + 8 * (k + i) + h) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+    for (int i = 0; i < kRouterSteps; ++i) {
+      const uint32_t av[8] = {a[i][0].x, a[i][0].y, a[i][0].z, a[i][0].w, a[i][1].x, a[i][1].y, a[i][1].z, a[i][1].w};
+      const uint32_t bv[8] = {b[i][0].x, b[i][0].y, b[i][0].z, b[i][0].w, b[i][1].x, b[i][1].y, b[i][1].z, b[i][1].w};
+      const uint32_t wv[8] = {w[i][0].x, w[i][0].y, w[i][0].z, w[i][0].w, w[i][1].x, w[i][1].y, w[i][1].z, w[i][1].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {  // word 2j = K 4j, 4j+1; word 2j+1 = K 4j+2, 4j+3
+        float* dd = d[j & 1];
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+            "{%0, %1, %2, %3};"
+            : "+f"(dd[0]), "+f"(dd[1]), "+f"(dd[2]), "+f"(dd[3])
+            : "r"(av[2 * j]), "r"(bv[2 * j]), "r"(av[2 * j + 1]), "r"(bv[2 * j + 1]), "r"(wv[2 * j]),
+              "r"(wv[2 * j + 1]));
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) part[warp][lane][i] = d[0][i] + d[1][i];
+  __syncthreads();
+  if (warp != 0) return;
+  float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  for (int w8 = 0; w8 < kRouterWarps; ++w8)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] += part[w8][lane][i];
+  const int ec = blockIdx.x * 8 + 2 * t;  // D: rows g / g + 8 = tokens, columns 2t, 2t+1 = experts
+  if (t0 + g < T) *reinterpret_cast<float2*>(logits + int64_t(t0 + g) * E + ec) = make_float2(v[0], v[1]);
+  if (t0 + g + 8 < T) *reinterpret_cast<float2*>(logits + int64_t(t0 + g + 8) * E + ec) = make_float2(v[2], v[3]);
+}
+
 // Warp-wide argmax of (key, index): larger key wins, equal keys -> lower index.
 __device__ __forceinline__ void warp_argmax(float& key, int& idx) {
 #pragma unroll
@@ -169,45 +263,57 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
       if (j < per_lane && e < E && !((group_keep >> (e / per_group)) & 1u)) taken |= 1u << j;
     }
   }
-  // top-k by key
-  float sum = 0.0f, top_logit = 0.0f;
-  for (int k = 0; k < K; ++k) {
-    float best = -INFINITY;
-    int bi = 0x7fffffff;
-#pragma unroll
-    for (int j = 0; j < EPL; ++j) {
-      const int e = lane + 32 * j;
-      if (!((taken >> j) & 1u) && (key[j] > best || (key[j] == best && e < bi))) {
-        best = key[j];
-        bi = e;
-      }
-    }
-    warp_argmax(best, bi);
-    if (bi == 0x7fffffff) bi = 0;  // fewer eligible experts than K: cannot happen for valid shapes
-    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-    float s_sel = 0.0f;
+  // top-k by key: every lane keeps its best remaining slot; each round the
+  // warp's best wins, only its lane rescans.  Lane k keeps selection k.
+  float lbest = -INFINITY;
+  int lidx = 0x7fffffff;
+  auto rescan = [&]() {
+    lbest = -INFINITY;
+    lidx = 0x7fffffff;
 #pragma unroll
     for (int j = 0; j < EPL; ++j)
-      if (lane + 32 * j == bi) s_sel = score[j];
+      if (!((taken >> j) & 1u) && key[j] > lbest) {  // ascending j: ties keep the lower expert
+        lbest = key[j];
+        lidx = lane + 32 * j;
+      }
+  };
+  rescan();
+  float sum = 0.0f, top_logit = 0.0f, my_w[2] = {0.0f, 0.0f};  // selections lane and lane + 32
+  int my_idx[2] = {0, 0};
+  for (int k = 0; k < K; ++k) {
+    float best = lbest;
+    int bi = lidx;
+    warp_argmax(best, bi);
+    if (bi == 0x7fffffff) bi = 0;  // fewer eligible experts than K: cannot happen for valid shapes
+    float s_sel = 0.0f;
+    if ((bi & 31) == lane) {
+      taken |= 1u << (bi >> 5);
+#pragma unroll
+      for (int j = 0; j < EPL; ++j)
+        if (j == (bi >> 5)) s_sel = score[j];
+      rescan();
+    }
     s_sel = __shfl_sync(0xffffffffu, s_sel, bi & 31);
     if (kind == WM_ROUTER_SOFTMAX) {
       if (k == 0) top_logit = s_sel;
       s_sel = expf(s_sel - top_logit);
     }
     sum += s_sel;
-    if (lane == 0) {
-      idx_out[(int64_t)t * K + k] = bi;
-      w_out[(int64_t)t * K + k] = s_sel;
+    if (lane == (k & 31)) {
+      my_idx[k >> 5] = bi;
+      my_w[k >> 5] = s_sel;
     }
   }
-  __syncwarp();
-  if (lane == 0) {
-    for (int k = 0; k < K; ++k) {
-      float v = w_out[(int64_t)t * K + k];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int k = lane + 32 * h;
+    if (k < K) {
+      float v = my_w[h];
       if (kind == WM_ROUTER_SOFTMAX)
         v = v / sum;
       else if (K > 1)
         v = v / (sum + 1e-20f);
+      idx_out[(int64_t)t * K + k] = my_idx[h];
       w_out[(int64_t)t * K + k] = v * route_scale;
     }
   }
@@ -253,6 +359,11 @@ void launch_shared_gate(const uint16_t* x, const uint16_t* g, int T, int H, floa
 
 void launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* sg_w, int T, int H, int E,
                           float* logits, float* sg, cudaStream_t stream) {
+  if (H % (64 * kRouterWarps) == 0 && E % 8 == 0 && T <= 4096) {
+    const dim3 blocks(E / 8 + (sg_w != nullptr ? 1 : 0), (T + 15) / 16);
+    router_logits_mma_kernel<<<blocks, 32 * kRouterWarps, 0, stream>>>(x, wr, sg_w, T, H, E, logits, sg);
+    return;
+  }
   const int rows = E + (sg_w != nullptr ? 1 : 0);
   // experts in groups of 8 (one per warp) x token chunks of 8 (up to 64 chunks in flight)
   const dim3 blocks((rows + 7) / 8, std::min((T + 7) / 8, 64));

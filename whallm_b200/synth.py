@@ -139,4 +139,8 @@ def config(n: int, device="cuda", seed: int = 0, batch: int = 64) -> Workload:
     if n == 3:
         layer = deepseek_fp8_layer(device=device, seed=seed)
         return Workload(layer, activations(8192, 7168, _gen(seed + 1, device), device), 8, "config3")
+    if n == 4:
+        # one layer of the config-4 stack: 256 decode tokens and a 4096-token prefill chunk in one call
+        layer = deepseek_mxfp4_layer(device=device, seed=seed)
+        return Workload(layer, activations(256 + 4096, 7168, _gen(seed + 1, device), device), 8, "config4-layer")
     raise ValueError(f"no single-layer workload for config {n}")
