@@ -254,7 +254,7 @@ Path expert_path(const wm_ctx* ctx, const wm_moe_args* a, bool has_shared) {
 
 // Plan fields of the expert kernels of `path`.
 void plan_for_path(const wm_ctx* ctx, Path path, wm::Plan* plan) {
-  if (path == kPathDecode || path == kPathDecodeMma) plan->rowmax = ctx->rowmax;
+  if (path == kPathDecode || path == kPathDecodeMma || path == kPathGemm) plan->rowmax = ctx->rowmax;
   if (path == kPathDecodeMma) plan->tile_rows = 8;
 }
 
@@ -395,15 +395,26 @@ int run_experts(wm_ctx* ctx, const wm_moe_args* a, bool has_shared, Path path, c
     ctx->counters.gemv_calls += 1;
     return check_launch(ctx, "expert GEMV");
   }
-  // Grouped GEMM: gather the sorted rows, then gate/up (+SwiGLU) and down on tcgen05.
+  // Grouped GEMM: gather the sorted rows, then gate/up (+SwiGLU) and down on
+  // tcgen05.  MXFP4 runs on f16 rows scaled by 2^k per row (gather_f16, and
+  // act_f16 between the two GEMMs), FP8 on bf16 rows.
+  const bool f16 = fmt_of(a->layout) == wm::kFmtMxfp4;
+  wm::Plan plan = ctx->plan;
+  plan_for_path(ctx, kPathGemm, &plan);
   wm::prof_begin(&ctx->prof, wm::kProfGather, s);
-  wm::launch_gather_rows(static_cast<const uint16_t*>(a->x), ctx->plan, a->E, a->H, ctx->xs, ctx->num_sms, s);
+  if (f16)
+    wm::launch_gather_f16(static_cast<const uint16_t*>(a->x), plan, a->E, a->H, ctx->xs, ctx->rowscale, ctx->num_sms,
+                          s);
+  else
+    wm::launch_gather_rows(static_cast<const uint16_t*>(a->x), plan, a->E, a->H, ctx->xs, ctx->num_sms, s);
   wm::prof_end(&ctx->prof, wm::kProfGather, s);
   CUtensorMap map_x, map_act;
-  if (!encode_rows(ctx, &map_x, ctx->xs, a->H) || !encode_rows(ctx, &map_act, ctx->act, a->I))
+  const CUtensorMapDataType dt = f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if (!encode_rows_box(ctx, &map_x, ctx->xs, a->H, dt, 128) ||
+      !encode_rows_box(ctx, &map_act, f16 ? ctx->act16 : ctx->act, a->I, dt, 128))
     return fail(ctx, "cuTensorMapEncodeTiled failed for the sorted-row buffers");
   wm::GemmArgs g{};
-  g.plan = ctx->plan;
+  g.plan = plan;
   g.wts = wts;
   g.I = a->I;
   g.gate_first = gate_first;
@@ -413,12 +424,22 @@ int run_experts(wm_ctx* ctx, const wm_moe_args* a, bool has_shared, Path path, c
   g.out = ctx->act;
   g.Kdim = a->H;
   g.N = 2 * a->I;
+  g.ascale = f16 ? ctx->rowscale : nullptr;
+  g.rowmax = f16 ? ctx->rowmax : nullptr;
   wm::prof_begin(&ctx->prof, wm::kProfGemmGateUp, s);
   wm::launch_gemm(g, 0, &map_x, ctx->num_sms, s);
   wm::prof_end(&ctx->prof, wm::kProfGemmGateUp, s);
+  if (f16) {
+    wm::prof_begin(&ctx->prof, wm::kProfActF16, s);
+    wm::launch_act_f16(ctx->act, plan, a->E, a->I, ctx->act16, ctx->actscale, ctx->num_sms, s);
+    wm::prof_end(&ctx->prof, wm::kProfActF16, s);
+    ctx->counters.launches += 1;
+  }
   g.out = ctx->routed;
   g.Kdim = a->I;
   g.N = a->H;
+  g.ascale = f16 ? ctx->actscale : nullptr;
+  g.rowmax = nullptr;
   wm::prof_begin(&ctx->prof, wm::kProfGemmDown, s);
   wm::launch_gemm(g, 1, &map_act, ctx->num_sms, s);
   wm::prof_end(&ctx->prof, wm::kProfGemmDown, s);

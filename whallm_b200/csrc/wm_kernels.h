@@ -132,8 +132,11 @@ struct GemmArgs {
   float limit;
   int fmt;
   uint32_t* status;
+  const float* ascale;  // MXFP4: [rows] 2^k prescale of the f16 A rows
+  uint32_t* rowmax;     // MXFP4 gate/up: [rows] per-row |act| maxima (float bits), or null
 };
-// `kind`: 0 = gate/up + SwiGLU, 1 = down.  tmap_a points to a CUtensorMap
+// `kind`: 0 = gate/up + SwiGLU, 1 = down.  MXFP4 takes f16 A rows (gather_f16 /
+// act_f16), FP8 bf16 rows (gather_rows / the bf16 act).  tmap_a points to a CUtensorMap
 // passed by value to the kernel.
 void gemm_init_attributes();
 bool gemm_shape_ok(int H, int I);
