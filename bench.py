@@ -140,6 +140,8 @@ def run_reference(args) -> None:
     from whallm_b200 import synth
 
     cores = len(os.sched_getaffinity(0))
+    oracle.set_threads(cores)  # torchrun sets OMP_NUM_THREADS=1 for every rank
+    threads = oracle.max_threads()
     wl = synth.config(1, device="cpu", batch=64)
     layer_np = adapter.from_layer(wl.layer)
     xb = adapter.bits(wl.x)
@@ -161,8 +163,9 @@ def run_reference(args) -> None:
         "data": "synthetic (seeded, BASELINE configs[1] shapes)",
         "config": {"workload": "config1 decode layer, 64-token batch (8-token sample per step)", "H": H, "I": I,
                    "E": E, "K": K, "shared_expert": True},
-        "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{sample} tokens of a 64-token config-1 batch per step, OpenMP over {cores} cores"},
+        "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{sample} tokens of a 64-token config-1 batch per step, OpenMP threads {threads} "
+                                   f"on {cores} cores"},
         "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -520,9 +523,11 @@ def run(args) -> None:
         xb = adapter.bits(xs[0])
         _, (rw, ri) = eng.forward(layer, xs[0], K, return_routes=True)
         cores = len(os.sched_getaffinity(0))
+        oracle.set_threads(cores)
+        threads = oracle.max_threads()
         tps = cpu_sample(layer_np, xb, ri.cpu().numpy(), rw.cpu().numpy(), min_seconds=10.0, tokens=16)
-        cpu = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
-               "sample": f"16 tokens of a config-1 batch, repeated for >= 10 s, OpenMP over {cores} cores"}
+        cpu = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": f"16 tokens of a config-1 batch, repeated for >= 10 s, OpenMP threads {threads} on {cores} cores"}
 
     del graph
     prefill = None if args.no_prefill else prefill_section(args, dev, pk, 2)

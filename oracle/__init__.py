@@ -92,6 +92,8 @@ def _declare(L: ctypes.CDLL) -> None:
     L.wmo_moe_forward.argtypes = [ctypes.POINTER(WmoLayer), P, P, P, P, I64, P]
     L.wmo_expert_pairs.argtypes = [ctypes.POINTER(WmoLayer), P, P, P]
     L.wmo_max_threads.restype = ctypes.c_int
+    L.wmo_set_threads.argtypes = [ctypes.c_int]
+    L.wmo_set_threads.restype = None
 
 
 def _p(a: np.ndarray | None):
@@ -281,6 +283,11 @@ class Layer:
 
 def max_threads() -> int:
     return int(lib().wmo_max_threads())
+
+
+def set_threads(n: int) -> None:
+    """OpenMP threads of the oracle's later calls from this thread."""
+    lib().wmo_set_threads(int(n))
 
 
 def max_rel_error(y: np.ndarray, ref: np.ndarray) -> float:

@@ -648,6 +648,16 @@ WMO_EXPORT int wmo_expert_pairs(const wmo_layer* L, const uint16_t* x, const int
   return status;
 }
 
+/* Threads of later parallel regions of the calling thread (launchers such as
+   torchrun set OMP_NUM_THREADS=1 for every process). */
+WMO_EXPORT void wmo_set_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
+
 WMO_EXPORT int wmo_max_threads(void) {
 #ifdef _OPENMP
   return omp_get_max_threads();
