@@ -186,12 +186,12 @@ __device__ __forceinline__ void warp_argmax(float& key, int& idx) {
 
 // One warp per token.  Lane l holds experts e = l + 32 j, j < EPL (E <= 32 EPL).
 template <int EPL>
-__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits,
+__global__ void __launch_bounds__(64) router_topk_kernel(const float* __restrict__ logits,
                                                           const float* __restrict__ bias, int T, int E, int K,
                                                           int kind, int n_groups, int topk_groups, float route_scale,
                                                           int32_t* __restrict__ idx_out, float* __restrict__ w_out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 8 + warp;
+  const int t = blockIdx.x * 2 + warp;  // two warps (tokens) per block: short calls spread over SMs
   if (t >= T) return;
   const float* row = logits + (int64_t)t * E;
   const int per_lane = (E + 31) / 32;
@@ -263,28 +263,44 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
       if (j < per_lane && e < E && !((group_keep >> (e / per_group)) & 1u)) taken |= 1u << j;
     }
   }
-  // top-k by key: every lane keeps its best remaining slot; each round the
-  // warp's best wins, only its lane rescans.  Lane k keeps selection k.
+  // top-k by key: every lane keeps its best remaining slot (a tree over its
+  // slots, ties to the lower slot); each round two warp reductions find the
+  // largest key and, among equal keys, the lowest expert index; only the
+  // winner's lane rescans.  Lane k keeps selection k.
   float lbest = -INFINITY;
   int lidx = 0x7fffffff;
   auto rescan = [&]() {
-    lbest = -INFINITY;
-    lidx = 0x7fffffff;
+    float bk[EPL];
+    int bj[EPL];
 #pragma unroll
-    for (int j = 0; j < EPL; ++j)
-      if (!((taken >> j) & 1u) && key[j] > lbest) {  // ascending j: ties keep the lower expert
-        lbest = key[j];
-        lidx = lane + 32 * j;
-      }
+    for (int j = 0; j < EPL; ++j) {
+      bk[j] = ((taken >> j) & 1u) ? -INFINITY : key[j];
+      bj[j] = j;
+    }
+#pragma unroll
+    for (int w = EPL / 2; w > 0; w >>= 1)
+#pragma unroll
+      for (int j = 0; j < w; ++j)
+        if (bk[j + w] > bk[j] || (bk[j + w] == bk[j] && bj[j + w] < bj[j])) {
+          bk[j] = bk[j + w];
+          bj[j] = bj[j + w];
+        }
+    lbest = bk[0];
+    lidx = lane + 32 * bj[0];
+  };
+  // larger key -> larger unsigned value
+  auto ordered = [](float f) {
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
   };
   rescan();
   float sum = 0.0f, top_logit = 0.0f, my_w[2] = {0.0f, 0.0f};  // selections lane and lane + 32
   int my_idx[2] = {0, 0};
   for (int k = 0; k < K; ++k) {
-    float best = lbest;
-    int bi = lidx;
-    warp_argmax(best, bi);
-    if (bi == 0x7fffffff) bi = 0;  // fewer eligible experts than K: cannot happen for valid shapes
+    const uint32_t u = ordered(lbest);
+    const uint32_t top = __reduce_max_sync(0xffffffffu, u);
+    int bi = int(__reduce_min_sync(0xffffffffu, u == top ? uint32_t(lidx) : 0xffffffffu));
+    if (bi < 0 || bi >= 32 * EPL) bi = 0;  // fewer eligible experts than K: cannot happen for valid shapes
     float s_sel = 0.0f;
     if ((bi & 31) == lane) {
       taken |= 1u << (bi >> 5);
@@ -299,9 +315,14 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
       s_sel = expf(s_sel - top_logit);
     }
     sum += s_sel;
-    if (lane == (k & 31)) {
-      my_idx[k >> 5] = bi;
-      my_w[k >> 5] = s_sel;
+    if (lane == (k & 31)) {  // static register indices: selection k goes to slot k / 32
+      if (k < 32) {
+        my_idx[0] = bi;
+        my_w[0] = s_sel;
+      } else {
+        my_idx[1] = bi;
+        my_w[1] = s_sel;
+      }
     }
   }
 #pragma unroll
@@ -373,15 +394,15 @@ void launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t*
 
 void launch_router_topk(const float* logits, const float* bias, int T, int E, int K, int kind, int n_groups,
                         int topk_groups, float route_scale, int32_t* idx, float* w, cudaStream_t stream) {
-  const int blocks = (T + 7) / 8;
+  const int blocks = (T + 1) / 2;
   if (E <= 256)
-    router_topk_kernel<8><<<blocks, 256, 0, stream>>>(logits, bias, T, E, K, kind, n_groups, topk_groups,
+    router_topk_kernel<8><<<blocks, 64, 0, stream>>>(logits, bias, T, E, K, kind, n_groups, topk_groups,
                                                        route_scale, idx, w);
   else if (E <= 512)
-    router_topk_kernel<16><<<blocks, 256, 0, stream>>>(logits, bias, T, E, K, kind, n_groups, topk_groups,
+    router_topk_kernel<16><<<blocks, 64, 0, stream>>>(logits, bias, T, E, K, kind, n_groups, topk_groups,
                                                         route_scale, idx, w);
   else
-    router_topk_kernel<32><<<blocks, 256, 0, stream>>>(logits, bias, T, E, K, kind, n_groups, topk_groups,
+    router_topk_kernel<32><<<blocks, 64, 0, stream>>>(logits, bias, T, E, K, kind, n_groups, topk_groups,
                                                         route_scale, idx, w);
 }
 
