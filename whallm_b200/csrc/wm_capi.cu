@@ -426,6 +426,12 @@ int run_experts(wm_ctx* ctx, const wm_moe_args* a, bool has_shared, Path path, c
   g.N = 2 * a->I;
   g.ascale = f16 ? ctx->rowscale : nullptr;
   g.rowmax = f16 ? ctx->rowmax : nullptr;
+  {
+    const wm_matrix* ms[4] = {&a->w13, &a->w2, &a->shared_w13, &a->shared_w2};
+    g.w32 = 1;
+    for (int i = 0; i < (has_shared ? 4 : 2); ++i)
+      if (!aligned(ms[i]->weight, 32) || (i < 2 && ms[i]->weight_stride % 32)) g.w32 = 0;
+  }
   wm::prof_begin(&ctx->prof, wm::kProfGemmGateUp, s);
   wm::launch_gemm(g, 0, &map_x, ctx->num_sms, s);
   wm::prof_end(&ctx->prof, wm::kProfGemmGateUp, s);

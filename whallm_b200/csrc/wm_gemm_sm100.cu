@@ -114,10 +114,19 @@ __device__ __forceinline__ void sts_v4(uint32_t addr, uint4 v) {
                : "memory");
 }
 
-__device__ __forceinline__ void stg_v4(void* p, uint4 v) {
-  asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+// 32 bytes per lane (one full sector): 256-bit global accesses (sm_100).
+__device__ __forceinline__ void ldg_nc_v8(const void* p, uint4& lo, uint4& hi) {
+  asm volatile("ld.global.nc.L1::no_allocate.v8.u32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(lo.x), "=r"(lo.y), "=r"(lo.z), "=r"(lo.w), "=r"(hi.x), "=r"(hi.y), "=r"(hi.z), "=r"(hi.w)
+               : "l"(p));
+}
+
+__device__ __forceinline__ void stg_v8(void* p, const uint32_t* v) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(v[0]), "r"(v[1]), "r"(v[2]),
+               "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
                : "memory");
 }
+
 
 __device__ __forceinline__ void fail(Shared& sh, uint32_t* status, uint32_t role) {
   report_status(status, kStatusWaitTimeout, role);
@@ -262,7 +271,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     auto load_next = [&](uint4 (&w)[NW], uint32_t& sv) {
       if (lt_t >= total) return;
 #pragma unroll
-      for (int i = 0; i < NW; ++i) w[i] = ldg_nc_v4(lw + lkb * (16 * NW) + 16 * i);
+      for (int i = 0; i < NW; i += 2) {  // a weight row's K block: whole 32-byte sectors when aligned
+        const uint8_t* src = lw + lkb * (16 * NW) + 16 * i;
+        if (a.w32) {
+          ldg_nc_v8(src, w[i], w[i + 1]);
+        } else {
+          w[i] = ldg_nc_v4(src);
+          w[i + 1] = ldg_nc_v4(src + 16);
+        }
+      }
       if (FMT == kFmtMxfp4) {
         uint16_t v;
         asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(v) : "l"(ls + lkb * 2));
@@ -408,9 +425,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             pk[i] = pack_bf16x2(a0, a1);
             amax = fmaxf(amax, fmaxf(fabsf(bf16_round(a0)), fabsf(bf16_round(a1))));
           }
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            stg_v4(dst + jc * 32 + i * 8, make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]));
+          stg_v8(dst + jc * 32, pk);  // 64 bytes of the row: two full sectors
+          stg_v8(dst + jc * 32 + 16, pk + 8);
         }
         if (a.rowmax != nullptr) atomicMax(a.rowmax + row, __float_as_uint(amax));
       } else {
@@ -430,9 +446,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             pk[i] = pack_bf16x2(v0, v1);
           }
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            stg_v4(dst + jc * 32 + i * 8, make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]));
+          stg_v8(dst + jc * 32, pk);
+          stg_v8(dst + jc * 32 + 16, pk + 8);
         }
       }
       tc_fence_before();

@@ -134,6 +134,7 @@ struct GemmArgs {
   uint32_t* status;
   const float* ascale;  // MXFP4: [rows] 2^k prescale of the f16 A rows
   uint32_t* rowmax;     // MXFP4 gate/up: [rows] per-row |act| maxima (float bits), or null
+  int w32;              // 1: every expert's weight rows start 32-byte aligned (256-bit loads)
 };
 // `kind`: 0 = gate/up + SwiGLU, 1 = down.  MXFP4 takes f16 A rows (gather_f16 /
 // act_f16), FP8 bf16 rows (gather_rows / the bf16 act).  tmap_a points to a CUtensorMap
