@@ -14,7 +14,8 @@ expert-parallel (whallm_b200.ep): every rank owns E/N experts and its own
 all-to-all (weak scaling; eager steps, since the split sizes are read on the
 host).  At N = 1 the line also carries a `prefill` section: the config-2
 layer (16,384 tokens, Zipf(1.1) routing) through the grouped-GEMM path.
-At N = 1 it also carries `long_calls`: one config-3 layer (DeepSeek-style
+At N = 1 it also carries `decode_batches` (the same layer at batch 1 and 8)
+and `long_calls`: one config-3 layer (DeepSeek-style
 FP8, 8192 tokens) and one layer of config 4 (256 decode + 4096 prefill
 tokens, 384 MXFP4 experts of H = 7168, I = 2048), both on the grouped GEMM.
 `--impl reference` times the CPU oracle (the restatement of the reference's
@@ -398,6 +399,48 @@ def run_ep(args, world: int, rank: int, local: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def decode_batch_line(eng, layer, dev, B: int, steps: int, flush) -> dict:
+    """Config-1 decode at batch B (graph replay per step, L2 flushed, device
+    events): latency, tokens/s and the layer's bytes per second."""
+    import torch
+    from whallm_b200 import synth
+
+    xs = [synth.activations(B, H, torch.Generator(device=dev).manual_seed(500 + i), dev) for i in range(8)]
+    x_static = xs[0].clone()
+    out = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            eng.forward(layer, x_static, K, out=out)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            eng.forward(layer, x_static, K, out=out)
+    torch.cuda.synchronize()
+    uniq = []
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    with torch.cuda.stream(stream):
+        for i in range(3 + steps):
+            x_static.copy_(xs[i % 8])
+            flush.zero_()
+            if i >= 3:
+                evs[i - 3][0].record(stream)
+            graph.replay()
+            if i >= 3:
+                evs[i - 3][1].record(stream)
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in evs) / steps
+    for i in range(8):
+        _, (_, ri) = eng.forward(layer, xs[i], K, return_routes=True)
+        uniq.append(int(torch.unique(ri).numel()))
+    torch.cuda.synchronize()
+    del graph
+    U = sum(uniq) / len(uniq)
+    layer_bytes = (U + 1) * BLOB + E * H * 2 + H * 2 + 4 * B * H  # experts + router + shared gate + x/out
+    return {"batch": B, "ms_per_step": ms, "tokens_per_s": B / (ms / 1e3), "unique_experts": U,
+            "layer_bytes": layer_bytes, "achieved_gbs": layer_bytes / (ms / 1e3) / 1e9}
+
+
 def run(args) -> None:
     import numpy as np
     import torch
@@ -530,6 +573,7 @@ def run(args) -> None:
                "sample": f"16 tokens of a config-1 batch, repeated for >= 10 s, OpenMP threads {threads} on {cores} cores"}
 
     del graph
+    decode_batches = [decode_batch_line(eng, layer, dev, b, max(10, min(args.steps, 30)), flush) for b in (1, 8)]
     prefill = None if args.no_prefill else prefill_section(args, dev, pk, 2)
     long_calls = None
     if not args.no_prefill and not args.no_long:
@@ -557,6 +601,7 @@ def run(args) -> None:
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": B * H * 2, "d2h_bytes_per_step": B * H * 2},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
+        "decode_batches": decode_batches,
         "prefill": prefill,
         "long_calls": long_calls,
     }

@@ -147,6 +147,18 @@ typedef struct {
   void* out;                      /* bf16 [T, H] combined output */
   int32_t* out_idx;               /* optional int32 [T, K]: routes used */
   float* out_w;                   /* optional fp32 [T, K] */
+  /* Pre-MoE RMSNorm (optional): with norm_weight set, the block's input is
+       xn[t] = bf16((x[t] * (1 / sqrt(mean_h(x[t, h]^2) + norm_eps))) * norm_weight)
+     (fp32 sums of squares, bf16 output), computed once and used by the router,
+     the shared-expert gate and the experts -- the post_attention_layernorm that
+     the reference runs right before the gate (engine.mm:1846 with
+     kernels.metal:443-465, rms_norm_tg; GroupRMSNorm, qwen4_exp.py:93-117).
+     Short calls fuse it into the router kernel.  x_norm (optional, bf16
+     [T, H], must not overlap x) receives xn; when NULL it stays in the
+     handle's workspace.  wm_moe_forward_noalloc requires x_norm. */
+  const void* norm_weight;        /* bf16 [H], or NULL: x is used as given */
+  float norm_eps;                 /* >= 0, e.g. 1e-6 */
+  void* x_norm;                   /* bf16 [T, H] output of xn, or NULL */
 } wm_moe_args;
 
 typedef struct {

@@ -193,6 +193,19 @@ def linear(layout: int, w: np.ndarray, scale: np.ndarray, x_bits: np.ndarray, co
     return out
 
 
+def rms_norm(x_bits: np.ndarray, w_bits: np.ndarray, eps: float) -> np.ndarray:
+    """Pre-MoE RMSNorm as bf16 bits [T, H]: bf16((x * r) * w) in fp32 with
+    r = 1 / sqrt(mean(x^2) + eps) -- rms_norm_tg (DeepSeekNative/kernels.metal:443-465)
+    and the float32 branch of GroupRMSNorm (qwen4_exp.py:93-117).  The sum of
+    squares is taken in float64 here, so r can differ from a float32 sum in the
+    last place."""
+    x = bf16_to_f32(np.ascontiguousarray(x_bits, dtype=np.uint16))
+    w = bf16_to_f32(np.ascontiguousarray(w_bits, dtype=np.uint16))
+    ms = np.mean(np.square(x.astype(np.float64)), axis=-1, keepdims=True).astype(np.float32)
+    r = (np.float32(1.0) / np.sqrt(ms + np.float32(eps))).astype(np.float32)
+    return f32_to_bf16((x * r) * w)
+
+
 def router_logits(x_bits: np.ndarray, w_bits: np.ndarray) -> np.ndarray:
     x_bits = np.ascontiguousarray(x_bits, dtype=np.uint16)
     w_bits = np.ascontiguousarray(w_bits, dtype=np.uint16)

@@ -238,7 +238,9 @@ def test_empty_call_and_bad_expert(engine_factory):
         eng.forward(layer, synth.activations(65, H, torch.Generator(device=DEV).manual_seed(1), DEV), K)
 
 
-@pytest.mark.parametrize("batch", [1, 8, 64])
+# 1 / 8 / 64: BASELINE config 1; 2, 4, 16: the reference's small-row
+# verification batches (READY_VERIFICATION_ROWS = 16, qwen4_exp.py:786-788)
+@pytest.mark.parametrize("batch", [1, 2, 4, 8, 16, 64])
 def test_config1_decode_layer_matches_oracle(engine_factory, batch):
     wl = synth.config(1, device=DEV, batch=batch)
     eng = engine_factory(64, 2048, 512, 512, 10)

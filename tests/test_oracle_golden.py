@@ -96,3 +96,28 @@ def test_fp8_block_decode_rejects_reserved_codes_and_rounds_once():
     w[3, 5] = 0x7F
     with pytest.raises(ValueError):
         oracle.dequant_fp8_b128(w, s)
+
+
+def test_rms_norm_matches_the_reference_known_answer():
+    """[3, 4] normalises to [3, 4] / sqrt(12.5 + 1e-6) (the RMS part of
+    test_gated_delta_norm_uses_sigmoid, runtime/tests/test_qwen.py:715-727),
+    then multiplies by the weight (rms_norm_tg, kernels.metal:443-465)."""
+    x = oracle.f32_to_bf16(np.array([[3.0, 4.0]], np.float32))
+    one = oracle.f32_to_bf16(np.ones(2, np.float32))
+    expected = np.array([[3.0, 4.0]], np.float64) / np.sqrt(12.5 + 1e-6)
+    got = oracle.bf16_to_f32(oracle.rms_norm(x, one, 1e-6))
+    np.testing.assert_array_equal(got, oracle.bf16_to_f32(oracle.f32_to_bf16(expected.astype(np.float32))))
+    w = oracle.f32_to_bf16(np.array([0.5, -2.0], np.float32))
+    got = oracle.bf16_to_f32(oracle.rms_norm(x, w, 1e-6))
+    np.testing.assert_allclose(got, expected * [0.5, -2.0], rtol=2 ** -8)
+
+
+def test_rms_norm_is_scale_invariant_and_follows_eps():
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((4, 256)).astype(np.float32)
+    w = oracle.f32_to_bf16(rng.standard_normal(256).astype(np.float32))
+    a = oracle.rms_norm(oracle.f32_to_bf16(x), w, 0.0)
+    b = oracle.rms_norm(oracle.f32_to_bf16(x * 4.0), w, 0.0)  # powers of two scale bf16 exactly
+    np.testing.assert_array_equal(a, b)
+    zero = np.zeros((1, 256), np.uint16)
+    assert not oracle.bf16_to_f32(oracle.rms_norm(zero, w, 1e-6)).any()  # zero rows stay zero (signed)

@@ -77,3 +77,36 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
     rc, msg = _noalloc(eng, layer, x, K, out)
     assert rc == lib.WM_ERROR and "scratch" in msg
     eng.ctx.close()
+
+
+@pytest.mark.parametrize("H", [512, 576])  # 512: norm fused into the router; 576: the RMSNorm kernel first
+def test_noalloc_with_pre_moe_norm(H):
+    """With a norm weight the caller supplies x_norm; the result matches
+    wm_moe_forward with the same norm, and x_norm holds the normalised rows."""
+    from whallm_b200.moe import PreNorm
+    layer = _layer(H=H, seed=11)
+    g = torch.Generator(device=DEV).manual_seed(12)
+    layer.norm = PreNorm((1.0 + 0.2 * torch.randn((H,), generator=g, device=DEV)).to(torch.bfloat16), 1e-6)
+    K, T = 4, 8
+    eng = Engine(0, max_tokens=64, hidden=H, inter=256, experts=16, topk=K)
+    x = synth.activations(T, H, torch.Generator(device=DEV).manual_seed(13), DEV)
+    xn_ref = torch.empty_like(x)
+    ref = eng.forward(layer, x, K, x_norm=xn_ref)
+    eng.sync()
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=DEV)
+    xn = torch.empty_like(x)
+    a = eng._args(layer, x, K)
+    eng._with_shared(a, layer)
+    eng._with_router(a, layer.router)
+    a.out, a.x_norm = out.data_ptr(), xn.data_ptr()
+    err = ctypes.create_string_buffer(256)
+    rc = lib.load().wm_moe_forward_noalloc(ctypes.byref(a), torch.cuda.current_stream().cuda_stream, err, len(err))
+    assert rc == lib.WM_OK, err.value.decode()
+    torch.cuda.synchronize()
+    assert torch.equal(xn.view(torch.int16), xn_ref.view(torch.int16))
+    e = oracle.max_rel_error(oracle.bf16_to_f32(adapter.bits(out)), oracle.bf16_to_f32(adapter.bits(ref)))
+    assert e <= TOL
+    a.x_norm = None  # a norm without the caller's rows is refused
+    rc = lib.load().wm_moe_forward_noalloc(ctypes.byref(a), torch.cuda.current_stream().cuda_stream, err, len(err))
+    assert rc == lib.WM_ERROR and "x_norm" in err.value.decode()
+    eng.ctx.close()

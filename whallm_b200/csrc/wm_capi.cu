@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -35,6 +36,7 @@ struct wm_ctx {
   float* rowscale = nullptr;   // [rows] prescale of the f16 x rows (decode path)
   float* actscale = nullptr;   // [rows] prescale of the f16 act rows (decode path)
   uint32_t* rowmax = nullptr;  // [rows] per-row |act| maxima (decode path)
+  uint16_t* xn = nullptr;      // [T, H] normalised input rows (pre-MoE RMSNorm)
   int max_rows = 0, max_mtiles = 0, max_chunks = 0;
   PFN_cuTensorMapEncodeTiled_v12000 encode_tiled = nullptr;
   wm::Profiler prof;
@@ -77,6 +79,33 @@ bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) %
 int fmt_of(int layout) { return layout == WM_LAYOUT_W13_FP8_B128 ? wm::kFmtFp8B128 : wm::kFmtMxfp4; }
 
 // Validates the shape / pointer contract shared by every expert call.
+// The pre-MoE RMSNorm fields (x checked by the caller).
+int validate_norm(wm_ctx* ctx, const wm_moe_args* a) {
+  if (a->norm_weight == nullptr) return WM_OK;
+  if (!aligned(a->norm_weight, 16)) return fail(ctx, "norm_weight must be a 16-byte aligned device pointer");
+  if (!(a->norm_eps >= 0.0f) || !std::isfinite(a->norm_eps)) return fail(ctx, "norm_eps must be finite and >= 0");
+  if (a->x_norm != nullptr) {
+    if (!aligned(a->x_norm, 16)) return fail(ctx, "x_norm must be 16-byte aligned");
+    const uintptr_t x0 = uintptr_t(a->x), n0 = uintptr_t(a->x_norm), bytes = uintptr_t(a->T) * a->H * 2;
+    if (n0 < x0 + bytes && x0 < n0 + bytes) return fail(ctx, "x_norm must not overlap x");
+  }
+  return WM_OK;
+}
+
+// Where a call with a norm weight keeps its normalised rows.
+uint16_t* norm_rows(wm_ctx* ctx, const wm_moe_args* a) {
+  return static_cast<uint16_t*>(a->x_norm != nullptr ? a->x_norm : ctx->xn);
+}
+
+// Normalises x into norm_rows (a call whose router does not fuse the norm).
+void run_rmsnorm(wm_ctx* ctx, const wm_moe_args* a, cudaStream_t s) {
+  wm::prof_begin(&ctx->prof, wm::kProfNorm, s);
+  wm::launch_rmsnorm(static_cast<const uint16_t*>(a->x), static_cast<const uint16_t*>(a->norm_weight), a->T, a->H,
+                     a->norm_eps, norm_rows(ctx, a), s);
+  wm::prof_end(&ctx->prof, wm::kProfNorm, s);
+  ctx->counters.launches += 1;
+}
+
 int validate_experts(wm_ctx* ctx, const wm_moe_args* a, bool need_router) {
   const wm_options& o = ctx->opt;
   if (a == nullptr) return fail(ctx, "args is NULL");
@@ -92,6 +121,7 @@ int validate_experts(wm_ctx* ctx, const wm_moe_args* a, bool need_router) {
     return fail(ctx, "unknown expert layout %d", a->layout);
   if (a->T == 0) return WM_OK;  // nothing is read or written
   if (a->x == nullptr || !aligned(a->x, 16)) return fail(ctx, "x must be a 16-byte aligned device pointer");
+  if (int rc = validate_norm(ctx, a)) return rc;
   const wm_matrix* ms[2] = {&a->w13, &a->w2};
   for (const wm_matrix* m : ms) {
     if (m->weight == nullptr || m->scale == nullptr) return fail(ctx, "expert weights and scales must be given");
@@ -156,22 +186,34 @@ wm::ExpertWeights weights_of(const wm_moe_args* a, bool with_shared) {
 // Router logits + top-k into idx / w (and sg for the sigmoid shared gate).
 bool encode_2d_bf16(wm_ctx* ctx, CUtensorMap* map, const void* base, int cols, int rows, int box_rows);
 
+// With a norm weight the router sees the normalised rows, which it leaves in
+// norm_rows: short calls normalise inside the logits kernel, long calls (and
+// shapes that kernel does not take) run the RMSNorm kernel first.
 int run_router(wm_ctx* ctx, const wm_moe_args* a, float* logits, int32_t* idx, float* w, cudaStream_t s) {
   const uint16_t* sg_w =
       a->shared_gate == WM_SHARED_SIGMOID_GATE ? static_cast<const uint16_t*>(a->shared_gate_weight) : nullptr;
-  wm::prof_begin(&ctx->prof, wm::kProfRouter, s);
+  const bool norm = a->norm_weight != nullptr;
+  const uint16_t* x = static_cast<const uint16_t*>(a->x);
   CUtensorMap mx, mw;
-  if (wm::router_gemm_shape_ok(a->T, a->H, a->E) && aligned(a->x, 16) && aligned(a->router_weight, 16) &&
-      encode_2d_bf16(ctx, &mx, a->x, a->H, a->T, 128) && encode_2d_bf16(ctx, &mw, a->router_weight, a->H, a->E, 128)) {
+  const bool gemm = wm::router_gemm_shape_ok(a->T, a->H, a->E) && aligned(a->router_weight, 16) &&
+                    encode_2d_bf16(ctx, &mw, a->router_weight, a->H, a->E, 128);
+  if (norm && (gemm || !wm::router_logits_fused_ok(a->T, a->H, a->E))) {
+    run_rmsnorm(ctx, a, s);
+    x = norm_rows(ctx, a);
+  }
+  wm::prof_begin(&ctx->prof, wm::kProfRouter, s);
+  if (gemm && encode_2d_bf16(ctx, &mx, x, a->H, a->T, 128)) {
     // long calls: the logits GEMM on the tensor cores, the shared gate (one row) on the CUDA cores
     wm::launch_router_gemm(&mx, &mw, a->T, a->H, a->E, logits, ctx->status, ctx->num_sms, s);
     if (sg_w != nullptr) {
-      wm::launch_shared_gate(static_cast<const uint16_t*>(a->x), sg_w, a->T, a->H, ctx->sg, s);
+      wm::launch_shared_gate(x, sg_w, a->T, a->H, ctx->sg, s);
       ctx->counters.launches += 1;
     }
   } else {
-    wm::launch_router_logits(static_cast<const uint16_t*>(a->x), static_cast<const uint16_t*>(a->router_weight),
-                             sg_w, a->T, a->H, a->E, logits, ctx->sg, s);
+    const bool fused = norm && x == a->x;
+    wm::launch_router_logits(x, static_cast<const uint16_t*>(a->router_weight), sg_w, a->T, a->H, a->E, logits,
+                             ctx->sg, s, fused ? static_cast<const uint16_t*>(a->norm_weight) : nullptr,
+                             a->norm_eps, fused ? norm_rows(ctx, a) : nullptr);
   }
   wm::prof_end(&ctx->prof, wm::kProfRouter, s);
   wm::prof_begin(&ctx->prof, wm::kProfTopk, s);
@@ -521,7 +563,7 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
                o_act = take(rows * I * 2), o_routed = take(rows * H * 2), o_logits = take(T * E * 4),
                o_idx = take(T * K * 4), o_w = take(T * K * 4), o_sg = take(T * 4), o_status = take(16),
                o_act16 = take(rows * I * 2), o_rowscale = take(rows * 4), o_actscale = take(rows * 4),
-               o_rowmax = take(rows * 4);
+               o_rowmax = take(rows * 4), o_xn = take(T * H * 2);
   ctx->ws_bytes = off;
   if (cudaMalloc(&ctx->ws, ctx->ws_bytes) != cudaSuccess) {
     cudaGetLastError();
@@ -553,6 +595,7 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
   ctx->rowscale = reinterpret_cast<float*>(base + o_rowscale);
   ctx->actscale = reinterpret_cast<float*>(base + o_actscale);
   ctx->rowmax = reinterpret_cast<uint32_t*>(base + o_rowmax);
+  ctx->xn = reinterpret_cast<uint16_t*>(base + o_xn);
   cudaMemset(ctx->status, 0, 16);
   const size_t gemv_smem = wm::gemv_smem_bytes(int(H), int(I));
   if (gemv_smem > size_t(prop.sharedMemPerBlockOptin)) {
@@ -651,6 +694,7 @@ WM_EXPORT int wm_route(wm_ctx* ctx, const wm_moe_args* a, float* logits, int32_t
   if (b.K <= 0 || b.K > b.E || b.K > o.max_topk) return fail(ctx, "K = %d outside (0, min(E, max_topk)]", b.K);
   if (b.H <= 0 || b.H % 8 || b.H > o.max_hidden) return fail(ctx, "H = %d must be a multiple of 8 within max_hidden", b.H);
   if (!b.x || !aligned(b.x, 16) || !aligned(b.router_weight, 16)) return fail(ctx, "x and router_weight must be 16-byte aligned");
+  if (int rc = validate_norm(ctx, &b)) return rc;
   if (b.router < WM_ROUTER_SOFTMAX || b.router > WM_ROUTER_SIGMOID_GROUPED) return fail(ctx, "unknown router kind %d", b.router);
   if (b.router == WM_ROUTER_SIGMOID_GROUPED &&
       (b.n_groups < 1 || b.n_groups > 32 || b.E % b.n_groups || b.topk_groups < 1 || b.topk_groups > b.n_groups ||
@@ -673,6 +717,11 @@ WM_EXPORT int wm_expert_pairs(wm_ctx* ctx, const wm_moe_args* a, void* routed, v
   if (routed == nullptr || !aligned(routed, 16)) return fail(ctx, "routed must be a 16-byte aligned device pointer");
   DeviceGuard guard(ctx->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (b.norm_weight != nullptr) {  // the experts read the normalised rows
+    run_rmsnorm(ctx, &b, s);
+    b.x = norm_rows(ctx, &b);
+    b.norm_weight = nullptr;
+  }
   const Path path = expert_path(ctx, &b, false);
   wm::Plan plan = ctx->plan;
   plan_for_path(ctx, path, &plan);
@@ -754,13 +803,22 @@ WM_EXPORT int wm_ep_plan(wm_ctx* ctx, int64_t T, int32_t K, int32_t experts_per_
   return check_launch(ctx, "expert-parallel plan");
 }
 
-WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* a, void* stream) {
+WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* args, void* stream) {
   if (ctx == nullptr) return WM_ERROR;
-  if (int rc = validate_experts(ctx, a, true)) return rc;
-  if (a->T == 0) return WM_OK;
-  if (a->out == nullptr || !aligned(a->out, 16)) return fail(ctx, "out must be a 16-byte aligned device pointer");
+  if (int rc = validate_experts(ctx, args, true)) return rc;
+  if (args->T == 0) return WM_OK;
+  if (args->out == nullptr || !aligned(args->out, 16)) return fail(ctx, "out must be a 16-byte aligned device pointer");
   DeviceGuard guard(ctx->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // With a pre-MoE norm, everything after the router reads the normalised
+  // rows: the router writes them (or the RMSNorm kernel does, without one).
+  wm_moe_args na = *args;
+  const wm_moe_args* a = &na;
+  if (args->norm_weight != nullptr) {
+    na.x = norm_rows(ctx, args);
+    na.norm_weight = nullptr;
+    if (args->router_weight == nullptr) run_rmsnorm(ctx, args, s);
+  }
   const bool has_shared = a->shared_gate != WM_SHARED_NONE;
   const Path path = expert_path(ctx, a, has_shared);
   wm::Plan plan = ctx->plan;
@@ -771,7 +829,7 @@ WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* a, void* stream) {
   if (a->router_weight != nullptr) {
     int32_t* di = a->out_idx ? a->out_idx : ctx->idx;
     float* dw = a->out_w ? a->out_w : ctx->w;
-    if (int rc = run_router(ctx, a, ctx->logits, di, dw, s)) return rc;
+    if (int rc = run_router(ctx, args, ctx->logits, di, dw, s)) return rc;
     idx = di;
     w = dw;
   } else {

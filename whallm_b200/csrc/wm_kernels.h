@@ -24,6 +24,7 @@ enum ProfSlot : int {
   kProfCombine,
   kProfDecodeGateUp,
   kProfDecodeDown,
+  kProfNorm,
   kProfSlots
 };
 struct Profiler;  // defined in wm_profile.cu
@@ -37,8 +38,16 @@ void launch_dequant(int format, const void* weight, const void* scale, int64_t r
 // ---- router (wm_route.cu)
 size_t router_smem_bytes(int H);
 void router_init_attributes(int max_hidden);
+// With nw (bf16 [H] RMSNorm weight) a call that router_logits_fused_ok takes
+// routes bf16((x * rstd) * nw) and writes those rows to xn (when non-null);
+// other calls ignore nw -- normalise first with launch_rmsnorm.
 void launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* sg_w, int T, int H, int E,
-                          float* logits, float* sg, cudaStream_t stream);
+                          float* logits, float* sg, cudaStream_t stream, const uint16_t* nw = nullptr,
+                          float eps = 0.0f, uint16_t* xn = nullptr);
+bool router_logits_fused_ok(int T, int H, int E);
+// xn[t] = bf16((x[t] * rsqrt(mean(x[t]^2) + eps)) * nw), H % 8 == 0
+void launch_rmsnorm(const uint16_t* x, const uint16_t* nw, int T, int H, float eps, uint16_t* xn,
+                    cudaStream_t stream);
 void launch_shared_gate(const uint16_t* x, const uint16_t* g, int T, int H, float* sg, cudaStream_t stream);
 void launch_router_topk(const float* logits, const float* bias, int T, int E, int K, int kind, int n_groups,
                         int topk_groups, float route_scale, int32_t* idx, float* w, cudaStream_t stream);

@@ -69,6 +69,14 @@ extern "C" WM_EXPORT int wm_moe_forward_noalloc(const wm_moe_args* a, void* stre
                      a->shared_w2.scale == nullptr ||
                      (a->shared_gate == WM_SHARED_SIGMOID_GATE && !al(a->shared_gate_weight, 16))))
     return report(error, error_size, "shared expert weights, scales (and sigmoid gate weight) must be given, aligned");
+  const bool norm = a->norm_weight != nullptr;
+  if (norm) {
+    if (!al(a->norm_weight, 16) || !al(a->x_norm, 16))
+      return report(error, error_size, "a norm weight needs 16-byte aligned norm_weight and x_norm (the caller's rows)");
+    const uintptr_t x0 = uintptr_t(a->x), n0 = uintptr_t(a->x_norm), bytes = uintptr_t(a->T) * a->H * 2;
+    if (n0 < x0 + bytes && x0 < n0 + bytes) return report(error, error_size, "x_norm must not overlap x");
+    if (!(a->norm_eps >= 0.0f) || a->norm_eps > 3.0e38f) return report(error, error_size, "norm_eps must be finite and >= 0");
+  }
   const bool route_here = a->router_weight != nullptr;
   if (!route_here && (a->routes_idx == nullptr || a->routes_w == nullptr))
     return report(error, error_size, "give router_weight or routes_idx and routes_w");
@@ -149,10 +157,20 @@ extern "C" WM_EXPORT int wm_moe_forward_noalloc(const wm_moe_args* a, void* stre
   const uint16_t* x = static_cast<const uint16_t*>(a->x);
   const uint16_t* sg_w =
       a->shared_gate == WM_SHARED_SIGMOID_GATE ? static_cast<const uint16_t*>(a->shared_gate_weight) : nullptr;
+  // the pre-MoE RMSNorm: fused into the router's logits kernel where it takes the shape
+  uint16_t* xn = static_cast<uint16_t*>(a->x_norm);
+  const uint16_t* nw = static_cast<const uint16_t*>(a->norm_weight);
+  const bool fused = norm && route_here && router_logits_fused_ok(int(T), int(H), int(E));
+  if (norm && !fused) {
+    launch_rmsnorm(x, nw, int(T), int(H), a->norm_eps, xn, s);
+    x = xn;
+  }
   if (route_here) {
     int32_t* di = a->out_idx ? a->out_idx : reinterpret_cast<int32_t*>(base + o_idx);
     float* dw = a->out_w ? a->out_w : reinterpret_cast<float*>(base + o_w);
-    launch_router_logits(x, static_cast<const uint16_t*>(a->router_weight), sg_w, int(T), int(H), int(E), logits, sg, s);
+    launch_router_logits(x, static_cast<const uint16_t*>(a->router_weight), sg_w, int(T), int(H), int(E), logits, sg, s,
+                         fused ? nw : nullptr, a->norm_eps, fused ? xn : nullptr);
+    if (fused) x = xn;
     launch_router_topk(logits, a->router_bias, int(T), int(E), int(K), a->router, a->n_groups, a->topk_groups,
                        a->route_scale, di, dw, s);
     idx = di;

@@ -66,7 +66,7 @@ void prof_end(Profiler* p, int slot, cudaStream_t s) {
 const char* prof_name(int slot) {
   static const char* names[kProfSlots] = {"router_logits", "router_topk", "plan",     "act_f16",     "gather_rows",
                                           "gemv_gate_up",  "gemv_down",   "gemm_gate_up", "gemm_down", "combine",
-                                          "decode_gate_up", "decode_down"};
+                                          "decode_gate_up", "decode_down", "rmsnorm"};
   return slot >= 0 && slot < kProfSlots ? names[slot] : "?";
 }
 

@@ -77,14 +77,29 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __re
   }
 }
 
+// 8 bf16 of x times the row's rstd times 8 bf16 norm weights, rounded to bf16:
+// ((x * rstd) * w), the order of the reference's rms_norm kernels.
+__device__ __forceinline__ uint4 rms_scale8(uint4 xv, uint4 wv, float r) {
+  const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w}, ws[4] = {wv.x, wv.y, wv.z, wv.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 a = unpack_bf16x2(xs[i]), b = unpack_bf16x2(ws[i]);
+    o[i] = pack_bf16x2(a.x * r * b.x, a.y * r * b.y);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 // Shared-expert gate of one token by one warp: sigmoid(x[t] . g), lanes over
 // 8-element pieces, fp32, xor-tree reduction (shared_gate_kernel uses the same).
 __device__ __forceinline__ float shared_gate_row(const uint16_t* __restrict__ xr, const uint16_t* __restrict__ g,
-                                                 int H, int lane) {
+                                                 int H, int lane, const uint16_t* __restrict__ nw = nullptr,
+                                                 float r = 1.0f) {
   float acc = 0.0f;
   for (int c = lane; c < H / 8; c += 32) {
     const uint4 wv = *reinterpret_cast<const uint4*>(g + c * 8);
-    const uint4 xv = *reinterpret_cast<const uint4*>(xr + c * 8);
+    uint4 xv = *reinterpret_cast<const uint4*>(xr + c * 8);
+    if (nw != nullptr) xv = rms_scale8(xv, *reinterpret_cast<const uint4*>(nw + c * 8), r);
     float2 p, a;
     float s = 0.0f;
     p = unpack_bf16x2(wv.x); a = unpack_bf16x2(xv.x); s = fmaf(a.x, p.x, s); s = fmaf(a.y, p.y, s);
@@ -98,6 +113,9 @@ __device__ __forceinline__ float shared_gate_row(const uint16_t* __restrict__ xr
   return 1.0f / (1.0f + expf(-acc));
 }
 
+constexpr int kRouterWarps = 8;
+constexpr int kRouterSteps = 4;  // 64-K steps per warp per batch of loads
+
 // Logits of short calls on warp MMAs (mma.sync.m16n8k16, bf16 operands,
 // fp32 accumulation).  A CTA computes 16 tokens x 8 experts; its 8 warps split
 // H into 8 slices (all of a slice's loads go out before its MMAs), and warp 0
@@ -105,30 +123,76 @@ __device__ __forceinline__ float shared_gate_row(const uint16_t* __restrict__ xr
 // contiguous K (32 bytes) of token rows g, g + 8 and of expert row g; MMA step
 // j takes K offsets 16t + 4j .. 16t + 4j + 3 of them for both operands.  The
 // CTA column past the experts computes the shared-expert gate, a warp per token.
-constexpr int kRouterWarps = 8;
-constexpr int kRouterSteps = 4;  // 64-K steps per warp per batch of loads
+//
+// With a norm weight `nw` the layer input is RMSNorm(x): every CTA first forms
+// the 1 / sqrt(mean(x^2) + eps) of its 16 rows the same way (lane partial sums
+// over the lane's K pieces, the t lanes, then the 8 warps, in a fixed order),
+// so every CTA of a token tile normalises identically; the A operands are
+// bf16((x * rstd) * w), and the CTA of expert group 0 writes them to xn for
+// the expert kernels (DeepSeekNative/kernels.metal:443-465, rms_norm_tg; the
+// norm before the gate, engine.mm:1846; GroupRMSNorm, qwen4_exp.py:93-117).
 __global__ void __launch_bounds__(32 * kRouterWarps) router_logits_mma_kernel(
     const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr, const uint16_t* __restrict__ sg_w, int T, int H,
-    int E, float* __restrict__ logits, float* __restrict__ sg) {
+    int E, float* __restrict__ logits, float* __restrict__ sg, const uint16_t* __restrict__ nw, float eps,
+    uint16_t* __restrict__ xn) {
   __shared__ float part[kRouterWarps][32][4];
+  __shared__ float ssq[kRouterWarps][16];
+  __shared__ float rstd_s[16];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int t0 = blockIdx.y * 16;
-  if (int(blockIdx.x) * 8 >= E) {  // shared-expert gate
-    for (int r = warp; r < 16; r += kRouterWarps)
-      if (t0 + r < T) {
-        const float v = shared_gate_row(x + int64_t(t0 + r) * H, sg_w, H, lane);
-        if (lane == 0) sg[t0 + r] = v;
-      }
-    return;
-  }
-  const int e = blockIdx.x * 8 + g;
   const int ra = min(t0 + g, T - 1), rb = min(t0 + g + 8, T - 1);  // rows past T read row T-1, not stored
   const int steps = H / 64 / kRouterWarps;                          // 64-K steps of this warp's slice
   const int64_t k0 = int64_t(warp) * steps * 8;                     // first uint4 of the slice
   const uint4* xa = reinterpret_cast<const uint4*>(x + int64_t(ra) * H) + k0 + 2 * t;
   const uint4* xb = reinterpret_cast<const uint4*>(x + int64_t(rb) * H) + k0 + 2 * t;
+  const uint4* np = nw != nullptr ? reinterpret_cast<const uint4*>(nw) + k0 + 2 * t : nullptr;
+  float ra_r = 1.0f, rb_r = 1.0f;
+  if (nw != nullptr) {
+    float sa = 0.0f, sb = 0.0f;
+    for (int k = 0; k < steps; ++k)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint4 va = __ldg(xa + 8 * k + h), vb = __ldg(xb + 8 * k + h);
+        const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 fa = unpack_bf16x2(wa[i]), fb = unpack_bf16x2(wb[i]);
+          sa = fmaf(fa.y, fa.y, fmaf(fa.x, fa.x, sa));
+          sb = fmaf(fb.y, fb.y, fmaf(fb.x, fb.x, sb));
+        }
+      }
+    sa += __shfl_xor_sync(0xffffffffu, sa, 1);
+    sb += __shfl_xor_sync(0xffffffffu, sb, 1);
+    sa += __shfl_xor_sync(0xffffffffu, sa, 2);
+    sb += __shfl_xor_sync(0xffffffffu, sb, 2);
+    if (t == 0) {
+      ssq[warp][g] = sa;
+      ssq[warp][g + 8] = sb;
+    }
+    __syncthreads();
+    if (threadIdx.x < 16) {
+      float total = 0.0f;
+      for (int w8 = 0; w8 < kRouterWarps; ++w8) total += ssq[w8][threadIdx.x];
+      rstd_s[threadIdx.x] = 1.0f / sqrtf(total / float(H) + eps);
+    }
+    __syncthreads();
+    ra_r = rstd_s[g];
+    rb_r = rstd_s[g + 8];
+  }
+  if (int(blockIdx.x) * 8 >= E) {  // shared-expert gate, on the normalised rows when there is a norm
+    for (int r = warp; r < 16; r += kRouterWarps) {
+      if (t0 + r >= T) continue;
+      const float v = shared_gate_row(x + int64_t(t0 + r) * H, sg_w, H, lane, nw, nw != nullptr ? rstd_s[r] : 1.0f);
+      if (lane == 0) sg[t0 + r] = v;
+    }
+    return;
+  }
+  const int e = blockIdx.x * 8 + g;
   const uint4* wp = reinterpret_cast<const uint4*>(wr + int64_t(e) * H) + k0 + 2 * t;
+  const bool write_xn = nw != nullptr && xn != nullptr && blockIdx.x == 0;
+  uint4* xna = write_xn ? reinterpret_cast<uint4*>(xn + int64_t(t0 + g) * H) + k0 + 2 * t : nullptr;
+  uint4* xnb = write_xn ? reinterpret_cast<uint4*>(xn + int64_t(t0 + g + 8) * H) + k0 + 2 * t : nullptr;
   float d[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
   for (int k = 0; k < steps; k += kRouterSteps) {
     uint4 a[kRouterSteps][2], b[kRouterSteps][2], w[kRouterSteps][2];
@@ -141,6 +205,21 @@ __global__ void __launch_bounds__(32 * kRouterWarps) router_logits_mma_kernel(
         b[i][h] = in ? __ldg(xb + 8 * (k + i) + h) : make_uint4(0, 0, 0, 0);
         w[i][h] = in ? __ldg(wp + 8 * (k + i) + h) : make_uint4(0, 0, 0, 0);
       }
+    if (nw != nullptr) {
+#pragma unroll
+      for (int i = 0; i < kRouterSteps; ++i)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (k + i >= steps) continue;
+          const uint4 nv = __ldg(np + 8 * (k + i) + h);
+          a[i][h] = rms_scale8(a[i][h], nv, ra_r);
+          b[i][h] = rms_scale8(b[i][h], nv, rb_r);
+          if (write_xn) {
+            if (t0 + g < T) xna[8 * (k + i) + h] = a[i][h];
+            if (t0 + g + 8 < T) xnb[8 * (k + i) + h] = b[i][h];
+          }
+        }
+    }
 #pragma unroll
     for (int i = 0; i < kRouterSteps; ++i) {
       const uint32_t av[8] = {a[i][0].x, a[i][0].y, a[i][0].z, a[i][0].w, a[i][1].x, a[i][1].y, a[i][1].z, a[i][1].w};
@@ -170,6 +249,42 @@ __global__ void __launch_bounds__(32 * kRouterWarps) router_logits_mma_kernel(
   if (t0 + g < T) *reinterpret_cast<float2*>(logits + int64_t(t0 + g) * E + ec) = make_float2(v[0], v[1]);
   if (t0 + g + 8 < T) *reinterpret_cast<float2*>(logits + int64_t(t0 + g + 8) * E + ec) = make_float2(v[2], v[3]);
 }
+
+// RMSNorm of whole rows for calls the fused kernel does not take: one CTA of
+// 256 threads per token, partial sums in a fixed order (rms_norm_tg).
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ nw,
+                                                     int H, float eps, uint16_t* __restrict__ xn) {
+  __shared__ float part[8];
+  const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + int64_t(row) * H);
+  float ss = 0.0f;
+  for (int c = threadIdx.x; c < H / 8; c += 256) {
+    const uint4 v = xr[c];
+    const uint32_t ws[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack_bf16x2(ws[i]);
+      ss = fmaf(f.y, f.y, fmaf(f.x, f.x, ss));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) part[warp] = ss;
+  __syncthreads();
+  float total = 0.0f;
+  for (int k = 0; k < 8; ++k) total += part[k];
+  const float r = 1.0f / sqrtf(total / float(H) + eps);
+  uint4* out = reinterpret_cast<uint4*>(xn + int64_t(row) * H);
+  const uint4* wv = reinterpret_cast<const uint4*>(nw);
+  for (int c = threadIdx.x; c < H / 8; c += 256) out[c] = rms_scale8(xr[c], wv[c], r);
+}
+
+void launch_rmsnorm(const uint16_t* x, const uint16_t* nw, int T, int H, float eps, uint16_t* xn,
+                    cudaStream_t stream) {
+  rmsnorm_kernel<<<T, 256, 0, stream>>>(x, nw, H, eps, xn);
+}
+
+bool router_logits_fused_ok(int T, int H, int E) { return H % (64 * kRouterWarps) == 0 && E % 8 == 0 && T <= 4096; }
 
 // Warp-wide argmax of (key, index): larger key wins, equal keys -> lower index.
 __device__ __forceinline__ void warp_argmax(float& key, int& idx) {
@@ -379,10 +494,12 @@ void launch_shared_gate(const uint16_t* x, const uint16_t* g, int T, int H, floa
 }
 
 void launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* sg_w, int T, int H, int E,
-                          float* logits, float* sg, cudaStream_t stream) {
-  if (H % (64 * kRouterWarps) == 0 && E % 8 == 0 && T <= 4096) {
+                          float* logits, float* sg, cudaStream_t stream, const uint16_t* nw, float eps,
+                          uint16_t* xn) {
+  if (router_logits_fused_ok(T, H, E)) {
     const dim3 blocks(E / 8 + (sg_w != nullptr ? 1 : 0), (T + 15) / 16);
-    router_logits_mma_kernel<<<blocks, 32 * kRouterWarps, 0, stream>>>(x, wr, sg_w, T, H, E, logits, sg);
+    router_logits_mma_kernel<<<blocks, 32 * kRouterWarps, 0, stream>>>(x, wr, sg_w, T, H, E, logits, sg, nw, eps,
+                                                                        xn);
     return;
   }
   const int rows = E + (sg_w != nullptr ? 1 : 0);

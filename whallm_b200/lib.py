@@ -62,6 +62,7 @@ class MoeArgs(ctypes.Structure):
         ("routes_idx", _P), ("routes_w", _P),
         ("swiglu_limit", ctypes.c_float),
         ("out", _P), ("out_idx", _P), ("out_w", _P),
+        ("norm_weight", _P), ("norm_eps", ctypes.c_float), ("x_norm", _P),
     ]
 
 

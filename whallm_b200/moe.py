@@ -25,7 +25,7 @@ from . import lib
 from .layout import FP8BatchedExperts, Projection, QwenBatchedExperts, projections
 
 __all__ = [
-    "Engine", "LayerWeights", "RouterWeights", "SharedExpert",
+    "Engine", "LayerWeights", "PreNorm", "RouterWeights", "SharedExpert",
     "StreamingExperts", "SparseMoE", "StreamingSwitchGLU", "MoE",
 ]
 
@@ -50,6 +50,15 @@ class RouterWeights:
 
 
 @dataclass
+class PreNorm:
+    """The RMSNorm in front of the MoE block (post_attention_layernorm):
+    xn = bf16((x * rsqrt(mean(x^2) + eps)) * weight), engine.mm:1846 with
+    kernels.metal:443-465 (rms_norm_tg), GroupRMSNorm in qwen4_exp.py:93-117."""
+    weight: torch.Tensor                   # bf16 [H]
+    eps: float = 1e-6
+
+
+@dataclass
 class LayerWeights:
     """Everything of one MoE layer the expert kernels read."""
     layout: int
@@ -61,6 +70,7 @@ class LayerWeights:
     shared: SharedExpert | None = None
     router: RouterWeights | None = None
     swiglu_limit: float = 0.0
+    norm: PreNorm | None = None            # applied to x first when set
     keep: list = field(default_factory=list)  # tensors the views point into
 
     @staticmethod
@@ -126,7 +136,20 @@ class Engine:
         a.x = x.data_ptr()
         a.swiglu_limit = layer.swiglu_limit
         a.route_scale = 1.0
+        if layer.norm is not None:
+            _check_bf16("norm weight", layer.norm.weight, (layer.H,))
+            a.norm_weight = layer.norm.weight.data_ptr()
+            a.norm_eps = layer.norm.eps
         return a
+
+    @staticmethod
+    def _with_x_norm(a: lib.MoeArgs, layer: LayerWeights, x: torch.Tensor, x_norm: torch.Tensor | None) -> None:
+        if x_norm is None:
+            return
+        if layer.norm is None:
+            raise ValueError("x_norm is written only for layers with a pre-MoE norm")
+        _check_bf16("x_norm", x_norm, tuple(x.shape))
+        a.x_norm = x_norm.data_ptr()
 
     def _with_shared(self, a: lib.MoeArgs, layer: LayerWeights) -> None:
         if layer.shared is None:
@@ -144,11 +167,15 @@ class Engine:
         a.n_groups, a.topk_groups, a.route_scale = r.n_groups, r.topk_groups, r.route_scale
 
     # ---------------------------------------------------------------- calls
-    def route(self, layer: LayerWeights, x: torch.Tensor, K: int, with_logits: bool = False):
-        """(weights fp32 [T, K], indices int32 [T, K][, logits fp32 [T, E]])."""
+    def route(self, layer: LayerWeights, x: torch.Tensor, K: int, with_logits: bool = False,
+              x_norm: torch.Tensor | None = None):
+        """(weights fp32 [T, K], indices int32 [T, K][, logits fp32 [T, E]]).
+        With layer.norm the routes are those of the normalised rows (written
+        to x_norm when given)."""
         if layer.router is None:
             raise ValueError("the layer has no router weights")
         a = self._args(layer, x, K)
+        self._with_x_norm(a, layer, x, x_norm)
         self._with_router(a, layer.router)
         T = x.shape[0]
         idx = torch.empty((T, K), dtype=torch.int32, device=x.device)
@@ -157,23 +184,29 @@ class Engine:
         self.ctx.route(a, _ptr(logits), idx.data_ptr(), w.data_ptr(), _stream())
         return (w, idx, logits) if with_logits else (w, idx)
 
-    def expert_pairs(self, layer: LayerWeights, x: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
-        """routed bf16 [T, K, H]: row (t, k) = expert indices[t, k] applied to x[t]."""
+    def expert_pairs(self, layer: LayerWeights, x: torch.Tensor, indices: torch.Tensor,
+                     x_norm: torch.Tensor | None = None) -> torch.Tensor:
+        """routed bf16 [T, K, H]: row (t, k) = expert indices[t, k] applied to x[t]
+        (to the normalised x[t] with layer.norm)."""
         T = x.shape[0]
         idx = indices.reshape(T, -1).to(torch.int32).contiguous()
         K = idx.shape[1]
         a = self._args(layer, x, K)
+        self._with_x_norm(a, layer, x, x_norm)
         a.routes_idx = idx.data_ptr()
         out = torch.empty((T, K, layer.H), dtype=torch.bfloat16, device=x.device)
         self.ctx.expert_pairs(a, out.data_ptr(), _stream())
         return out
 
     def forward(self, layer: LayerWeights, x: torch.Tensor, K: int, routes: tuple | None = None,
-                out: torch.Tensor | None = None, return_routes: bool = False):
+                out: torch.Tensor | None = None, return_routes: bool = False,
+                x_norm: torch.Tensor | None = None):
         """Combined output bf16 [T, H].  `routes` = (weights fp32 [T, K], indices
-        int32 [T, K]) skips the router."""
+        int32 [T, K]) skips the router.  With layer.norm every part of the block
+        reads the normalised rows, which x_norm (bf16 [T, H]) receives when given."""
         T = x.shape[0]
         a = self._args(layer, x, K)
+        self._with_x_norm(a, layer, x, x_norm)
         self._with_shared(a, layer)
         keep = []
         if routes is None:
