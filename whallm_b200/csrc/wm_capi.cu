@@ -190,6 +190,7 @@ bool encode_2d_bf16(wm_ctx* ctx, CUtensorMap* map, const void* base, int cols, i
 // norm_rows: short calls normalise inside the logits kernel, long calls (and
 // shapes that kernel does not take) run the RMSNorm kernel first.
 int run_router(wm_ctx* ctx, const wm_moe_args* a, float* logits, int32_t* idx, float* w, cudaStream_t s) {
+  const wm::TopkArgs tk{a->router_bias, a->K, a->router, a->n_groups, a->topk_groups, a->route_scale, idx, w};
   const uint16_t* sg_w =
       a->shared_gate == WM_SHARED_SIGMOID_GATE ? static_cast<const uint16_t*>(a->shared_gate_weight) : nullptr;
   const bool norm = a->norm_weight != nullptr;
@@ -217,8 +218,7 @@ int run_router(wm_ctx* ctx, const wm_moe_args* a, float* logits, int32_t* idx, f
   }
   wm::prof_end(&ctx->prof, wm::kProfRouter, s);
   wm::prof_begin(&ctx->prof, wm::kProfTopk, s);
-  wm::launch_router_topk(logits, a->router_bias, a->T, a->E, a->K, a->router, a->n_groups, a->topk_groups,
-                         a->route_scale, idx, w, s);
+  wm::launch_router_topk(logits, a->T, a->E, tk, s);
   wm::prof_end(&ctx->prof, wm::kProfTopk, s);
   ctx->counters.launches += 2;
   return check_launch(ctx, "router");
@@ -342,15 +342,20 @@ int run_decode_mma(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& w
   wm::launch_gather_f16(static_cast<const uint16_t*>(a->x), plan, a->E, H, xh, ctx->rowscale, ctx->num_sms, s);
   wm::prof_end(&ctx->prof, wm::kProfGather, s);
   d.bscale = ctx->rowscale;
+  // 8-token tiles of the call, about: one per routed expert hit (at most
+  // min(E, T * K)), more where an expert gets over 8 rows, plus the shared expert's
+  const int64_t pairs = int64_t(a->T) * a->K;
+  const int64_t has_sh = a->shared_gate != WM_SHARED_NONE ? 1 : 0;
+  const int tiles = int(std::min<int64_t>(a->E, pairs) + (a->T > 8 ? pairs / 8 : 0) + has_sh * ((a->T + 7) / 8));
   wm::prof_begin(&ctx->prof, wm::kProfDecodeGateUp, s);
-  wm::launch_decode_mma(d, 0, &bx, ctx->num_sms, s);
+  wm::launch_decode_mma(d, 0, &bx, ctx->num_sms, s, wm::decode_mma_split(0, H, I, tiles, ctx->num_sms));
   wm::prof_end(&ctx->prof, wm::kProfDecodeGateUp, s);
   wm::prof_begin(&ctx->prof, wm::kProfActF16, s);
   wm::launch_act_f16(ctx->act, plan, a->E, I, acth, ctx->actscale, ctx->num_sms, s);
   wm::prof_end(&ctx->prof, wm::kProfActF16, s);
   d.bscale = ctx->actscale;
   wm::prof_begin(&ctx->prof, wm::kProfDecodeDown, s);
-  wm::launch_decode_mma(d, 1, &bact, ctx->num_sms, s);
+  wm::launch_decode_mma(d, 1, &bact, ctx->num_sms, s, wm::decode_mma_split(1, H, I, tiles, ctx->num_sms));
   wm::prof_end(&ctx->prof, wm::kProfDecodeDown, s);
   ctx->counters.launches += 4;
   ctx->counters.decode_calls += 1;
@@ -826,6 +831,7 @@ WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* args, void* stream)
   plan.skip_negative = (ctx->opt.flags & WM_FLAG_SKIP_NEGATIVE_ROUTES) ? 1 : 0;
   const int32_t* idx;
   const float* w;
+  const int align = path == kPathGemm ? wm::kTileM : 1;
   if (a->router_weight != nullptr) {
     int32_t* di = a->out_idx ? a->out_idx : ctx->idx;
     float* dw = a->out_w ? a->out_w : ctx->w;
@@ -843,8 +849,8 @@ WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* args, void* stream)
   }
   int launches = 0;
   wm::prof_begin(&ctx->prof, wm::kProfPlan, s);
-  wm::launch_plan(idx, a->T, a->K, a->E, has_shared, path == kPathGemm ? wm::kTileM : 1, plan, ctx->max_rows,
-                  ctx->max_mtiles, ctx->max_chunks, ctx->status, s, &launches);
+  wm::launch_plan(idx, a->T, a->K, a->E, has_shared, align, plan, ctx->max_rows, ctx->max_mtiles, ctx->max_chunks,
+                  ctx->status, s, &launches);
   wm::prof_end(&ctx->prof, wm::kProfPlan, s);
   ctx->counters.launches += launches;
   if (int rc = check_launch(ctx, "plan")) return rc;

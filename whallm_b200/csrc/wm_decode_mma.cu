@@ -57,11 +57,20 @@ constexpr int kThreads = 32 * kWarps;
 constexpr int kTok = 8;      // tokens per item (the MMA's N)
 constexpr int kRG = 2;       // 16-row MMA tiles per warp
 constexpr int kStages = 2;   // chunks of weight loads in flight per thread
-constexpr int kFeatItem = kWarps * kRG * 8;   // gate/up: features per item
-constexpr int kRowsItem = kWarps * kRG * 16;  // down: output rows per item
+// Split K: with KS > 1 the CTA's warps form kWarps / KS row groups of KS
+// warps, each warp taking 1 / KS of the K chunks of its group's rows, so an
+// item covers 1 / KS of the rows and short calls (few token tiles) still
+// spread over every SM.  The sums do not depend on the split: K is cut into
+// q_nseg(K) segments, each summed from zero, and a row's result is
+// (((0 + s_0) + s_1) + ...) in segment order.  A split warp parks its
+// segment sums in shared memory; the group's first warp adds them in order
+// and runs the epilogue.
+__host__ __device__ constexpr int q_feat_item(int ks) { return kWarps / ks * kRG * 8; }   // gate/up features
+__host__ __device__ constexpr int q_rows_item(int ks) { return kWarps / ks * kRG * 16; }  // down output rows
 
 struct QShared {
   uint64_t full[2];
+  uint64_t red_full[2][kWarps];  // per buffer and row group: the K-slice partials are in
   int done[2];  // warps finished with the buffer's item
   int abort;
 };
@@ -70,10 +79,27 @@ __host__ __device__ constexpr int q_round1k(int v) { return (v + 1023) & ~1023; 
 
 // Bytes of one buffer: the token tile (K/64 boxes of 8 rows x 128 B) and the scale block.
 __host__ __device__ inline int q_xbytes(int K) { return kTok * K * 2; }
-__host__ __device__ inline int q_sbytes(int kind, int K) { return (kind == 0 ? 2 * kFeatItem : kRowsItem) * (K / 32); }
-__host__ __device__ inline int q_bufbytes(int kind, int K) { return q_round1k(q_xbytes(K) + q_sbytes(kind, K)); }
+__host__ __device__ inline int q_sbytes(int kind, int K, int ks) {
+  return (kind == 0 ? 2 * q_feat_item(ks) : q_rows_item(ks)) * (K / 32);
+}
+__host__ __device__ inline int q_bufbytes(int kind, int K, int ks) { return q_round1k(q_xbytes(K) + q_sbytes(kind, K, ks)); }
+// Segments of K: the most (up to 8, a power of two) that divide its chunks
+// into whole rings of kStages chunks.  A split KS must divide it.
+__host__ __device__ inline int q_nseg(int K) {
+  const int rings = K / 128 / kStages;
+  int n = 1;
+  while (n < 8 && rings % (2 * n) == 0) n *= 2;
+  return n;
+}
+// Segment sums of the K slices 1 .. KS-1: per buffer, per slice, per segment
+// of the slice and per warp, 32 lanes x kRG * 4 floats.
+__host__ __device__ inline int q_redbytes(int ks, int nseg) {
+  return ks > 1 ? 2 * (ks - 1) * (nseg / ks) * (kWarps / ks) * 32 * kRG * 16 : 0;
+}
 
-size_t q_smem_bytes(int kind, int K) { return size_t(2 * q_bufbytes(kind, K)) + 1024 + 128; }
+size_t q_smem_bytes(int kind, int K, int ks) {
+  return size_t(2 * q_bufbytes(kind, K, ks)) + q_redbytes(ks, q_nseg(K)) + 1024 + sizeof(QShared) + 16;
+}
 
 __device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
   uint32_t v;
@@ -165,20 +191,28 @@ __device__ __forceinline__ QItem q_item(const DecodeArgs& a, int q, int nb) {
 // KIND 0: gate/up (+SwiGLU) -> act [rows, I] bf16 and per-row |act| maxima;
 // KIND 1: down -> routed [rows, H] bf16.  tm_x: the f16 token rows
 // ([max_rows, K], boxes of 64 x 8, 128-byte swizzle).
-template <int KIND>
+template <int KIND, int KS>
 __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __grid_constant__ CUtensorMap tm_x,
                                                                  const DecodeArgs a) {
+  constexpr int kFeatItem = q_feat_item(KS), kRowsItem = q_rows_item(KS);
+  constexpr int kRowWarps = kWarps / KS;
   extern __shared__ uint8_t smem_raw[];
   const int K = KIND == 0 ? a.H : a.I;
   const int S = K / 32;       // E8M0 bytes per weight row
   const int KC = K / 128;     // chunks per row
+  const int KCw = KC / KS;    // chunks of this warp's K slice
+  const int nseg = q_nseg(K), SEGC = KC / nseg;  // segments of K, chunks per segment
+  const int wseg = nseg / KS;                     // segments of this warp's slice
   const int64_t rowb = K / 2; // packed bytes per weight row
-  const int xbytes = q_xbytes(K), bufbytes = q_bufbytes(KIND, K);
+  const int xbytes = q_xbytes(K), bufbytes = q_bufbytes(KIND, K, KS);
   const uint32_t raw0 = smem_u32(smem_raw);
   const uint32_t base = (raw0 + 1023u) & ~1023u;
-  QShared& sh = *reinterpret_cast<QShared*>(smem_raw + (base - raw0) + 2 * bufbytes);
+  float* red = reinterpret_cast<float*>(smem_raw + (base - raw0) + 2 * bufbytes);
+  QShared& sh = *reinterpret_cast<QShared*>(smem_raw + (base - raw0) + 2 * bufbytes + q_redbytes(KS, nseg));
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp_id = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = warp_id % kRowWarps;  // row group
+  const int ks = warp_id / kRowWarps;    // K slice: chunks [ks * KCw, (ks + 1) * KCw)
   const int g = lane >> 2, t = lane & 3;
   const int nb = KIND == 0 ? a.I / kFeatItem : a.H / kRowsItem;  // row blocks per token tile
   const int n_items = *a.plan.n_mtiles * nb;
@@ -187,6 +221,7 @@ __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __gri
   if (threadIdx.x == 0) {
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sh.full[b], 1);
+      for (int w = 0; w < kRowWarps; ++w) mbar_init(&sh.red_full[b][w], (KS - 1) * 32);
       sh.done[b] = 0;
     }
     sh.abort = 0;
@@ -198,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __gri
   // Issues the token tile and scale block of item `it` into buffer b.
   auto issue = [&](const QItem& it, int b) {
     const uint32_t xdst = base + b * bufbytes, sdst = xdst + xbytes;
-    mbar_arrive_expect_tx(&sh.full[b], uint32_t(xbytes + q_sbytes(KIND, K)));
+    mbar_arrive_expect_tx(&sh.full[b], uint32_t(xbytes + q_sbytes(KIND, K, KS)));
     for (int kb = 0; kb < K / 64; ++kb) tma_load_2d_q(xdst + kb * 1024, &tm_x, kb * 64, it.row0, &sh.full[b]);
     if (KIND == 0) {
       const uint8_t* s = a.wts.s13_of(it.e);
@@ -230,11 +265,13 @@ __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __gri
         srow[2 * r + h] = warp * (kRG * 16) + 16 * r + 8 * h + g;
       }
     }
-  // First weight row of this thread in item `it` (plus its 16-byte column).
+  // First weight row of this thread in item `it` (plus its 16-byte column of
+  // the first chunk of its K slice).
   auto row_ptr = [&](const QItem& it) -> const uint8_t* {
+    const int64_t col = 16 * t + int64_t(64) * KCw * ks;
     if (KIND == 0)
-      return a.wts.w13_of(it.e) + int64_t(gate_base + it.blk * kFeatItem + warp * (kRG * 8) + g) * rowb + 16 * t;
-    return a.wts.w2_of(it.e) + int64_t(it.blk * kRowsItem + warp * (kRG * 16) + g) * rowb + 16 * t;
+      return a.wts.w13_of(it.e) + int64_t(gate_base + it.blk * kFeatItem + warp * (kRG * 8) + g) * rowb + col;
+    return a.wts.w2_of(it.e) + int64_t(it.blk * kRowsItem + warp * (kRG * 16) + g) * rowb + col;
   };
 
   // Item metadata, fetched an item before it is needed (q beyond the list: unused).
@@ -250,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __gri
     if (lq < n_items) {
 #pragma unroll
       for (int j = 0; j < 2 * kRG; ++j) dst[j] = ldg_nc_v4(lp + roff[j] + 64 * lc);
-      if (++lc == KC) {
+      if (++lc == KCw) {
         lc = 0;
         lq += gridDim.x;
         lp = row_ptr(lnext);
@@ -270,6 +307,7 @@ __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __gri
   float rinv[2 * kRG];
   int smax[2 * kRG];
   float acc[kRG][2][4];  // per MMA tile, even and odd K steps (two independent chains)
+  float y[kRG][4];       // the row sums so far: ((0 + s_0) + s_1) + ... over segments
   uint32_t xb = 0, sb = 0;
   bool alive = cq < n_items;
 
@@ -308,19 +346,70 @@ __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __gri
 #pragma unroll
     for (int r = 0; r < kRG; ++r)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) acc[r][0][i] = acc[r][1][i] = 0.0f;
+      for (int i = 0; i < 4; ++i) acc[r][0][i] = acc[r][1][i] = y[r][i] = 0.0f;
     return true;
+  };
+
+  // red: [buffer][K slice 1 .. KS-1][segment of the slice][row group][tile r][lane] float4.
+  // A buffer's slots are rewritten two items later, after every warp
+  // released that buffer, so the group's first warp has read them by then.
+  auto red_slot = [&](int b, int k, int sg) {
+    return reinterpret_cast<float4*>(red) + (((b * (KS - 1) + k - 1) * wseg + sg) * kRowWarps + warp) * 32 * kRG + lane;
+  };
+  // End of segment sg of this warp's slice: its sum s = chain0 + chain1 goes
+  // into y (the group's first warp) or to shared memory; the chains restart.
+  auto end_segment = [&](int sg) {
+    const int b = li & 1;
+#pragma unroll
+    for (int r = 0; r < kRG; ++r) {
+      float sv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        sv[i] = acc[r][0][i] + acc[r][1][i];
+        acc[r][0][i] = acc[r][1][i] = 0.0f;
+      }
+      if (ks == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) y[r][i] += sv[i];
+      } else {
+        red_slot(b, ks, sg)[32 * r] = make_float4(sv[0], sv[1], sv[2], sv[3]);
+      }
+    }
   };
 
   auto end_item = [&]() {
     const int n0 = 2 * t, n1 = 2 * t + 1;
-    float y[kRG][4];
-#pragma unroll
-    for (int r = 0; r < kRG; ++r)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) y[r][i] = acc[r][0][i] + acc[r][1][i];
     const float is0 = 1.0f / bs0, is1 = 1.0f / bs1;
-    if (KIND == 0) {
+    bool lead = true;  // this warp runs the epilogue of its rows
+    if (KS > 1) {
+      const int b = li & 1;
+      if (ks > 0) {  // the segment sums are in place
+        mbar_arrive(&sh.red_full[b][warp]);
+        lead = false;
+      } else if (!warp_wait(&sh.red_full[b][warp], (li >> 1) & 1, abort)) {
+        if (lane == 0 && !*abort) {
+          report_status(a.status, kStatusWaitTimeout, 44 + KIND);
+          sh.abort = 1;
+        }
+        lead = false;
+      } else {
+        for (int k = 1; k < KS; ++k)  // segment order: slices are consecutive segments
+          for (int sg = 0; sg < wseg; ++sg) {
+            const float4* src = red_slot(b, k, sg);
+#pragma unroll
+            for (int r = 0; r < kRG; ++r) {
+              const float4 v = src[32 * r];
+              y[r][0] += v.x;
+              y[r][1] += v.y;
+              y[r][2] += v.z;
+              y[r][3] += v.w;
+            }
+          }
+      }
+    }
+    if (!lead) {
+      // partial sums only: the group's first warp writes these rows
+    } else if (KIND == 0) {
       float m0 = 0.0f, m1 = 0.0f;
 #pragma unroll
       for (int r = 0; r < kRG; ++r) {
@@ -411,14 +500,18 @@ __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __gri
 
   // Items are whole multiples of kStages chunks (KC % kStages == 0), so the
   // ring slot of a chunk is static and one copy of the item code serves.
+  const int c0 = ks * KCw;  // first chunk of this warp's K slice
   if (alive) alive = begin_item();
   while (alive) {
-    for (cc = 0; cc < KC; cc += kStages) {
+    for (int sg = 0; sg < wseg; ++sg) {
+      for (cc = 0; cc < SEGC; cc += kStages) {
 #pragma unroll
-      for (int s = 0; s < kStages; ++s) {
-        chunk(wr[s], cc + s);
-        load_next(wr[s]);
+        for (int s = 0; s < kStages; ++s) {
+          chunk(wr[s], c0 + sg * SEGC + cc + s);
+          load_next(wr[s]);
+        }
       }
+      end_segment(sg);
     }
     end_item();
     ++li;
@@ -430,25 +523,64 @@ __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __gri
 }
 
 bool decode_mma_shape_ok(int H, int I) {
-  return I % kFeatItem == 0 && H % kRowsItem == 0 && H % (128 * kStages) == 0 && I % (128 * kStages) == 0 &&
-         q_smem_bytes(0, H) <= 227 * 1024 && q_smem_bytes(1, I) <= 227 * 1024;
+  return I % q_feat_item(1) == 0 && H % q_rows_item(1) == 0 && H % (128 * kStages) == 0 &&
+         I % (128 * kStages) == 0 && q_smem_bytes(0, H, 1) <= 227 * 1024 && q_smem_bytes(1, I, 1) <= 227 * 1024;
 }
+
+namespace {
+
+template <int KIND, int KS>
+void set_smem(int K) {
+  cudaFuncSetAttribute(decode_mma_kernel<KIND, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       int(std::min(q_smem_bytes(KIND, K, KS), size_t(227 * 1024))));
+}
+
+template <int KIND, int KS>
+void launch_ks(const DecodeArgs& a, const CUtensorMap& x, int num_sms, cudaStream_t stream) {
+  const int K = KIND == 0 ? a.H : a.I;
+  decode_mma_kernel<KIND, KS><<<num_sms * kCtas, kThreads, q_smem_bytes(KIND, K, KS), stream>>>(x, a);
+}
+
+}  // namespace
 
 // Shapes beyond the shared-memory limit never take this kernel (decode_mma_shape_ok).
 void decode_mma_init_attributes(int max_h, int max_i) {
-  const size_t cap = 227 * 1024;
-  cudaFuncSetAttribute(decode_mma_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       int(std::min(q_smem_bytes(0, max_h), cap)));
-  cudaFuncSetAttribute(decode_mma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       int(std::min(q_smem_bytes(1, max_i), cap)));
+  set_smem<0, 1>(max_h);
+  set_smem<0, 2>(max_h);
+  set_smem<0, 4>(max_h);
+  set_smem<0, 8>(max_h);
+  set_smem<1, 1>(max_i);
+  set_smem<1, 2>(max_i);
+  set_smem<1, 4>(max_i);
+  set_smem<1, 8>(max_i);
 }
 
-void launch_decode_mma(const DecodeArgs& a, int kind, const void* tmap_x, int num_sms, cudaStream_t stream) {
+int decode_mma_split(int kind, int H, int I, int tiles, int num_sms) {
+  const int K = kind == 0 ? H : I;
+  const int nb = kind == 0 ? I / q_feat_item(1) : H / q_rows_item(1);  // row blocks of an unsplit item
+  // Split while the items would leave over half of the SMs idle (measured on
+  // config-1 decode: batch 1 gate/up 22 -> 88 items, down 44 -> 88; from
+  // about 80 unsplit items on, splitting costs more than it spreads).
+  int ks = 1;
+  while (2 * ks <= q_nseg(K) && int64_t(tiles) * nb * ks * 2 < num_sms &&
+         q_smem_bytes(kind, K, 2 * ks) <= 227 * 1024)
+    ks *= 2;
+  return ks;
+}
+
+void launch_decode_mma(const DecodeArgs& a, int kind, const void* tmap_x, int num_sms, cudaStream_t stream, int ks) {
   const CUtensorMap& x = *static_cast<const CUtensorMap*>(tmap_x);
-  if (kind == 0)
-    decode_mma_kernel<0><<<num_sms * kCtas, kThreads, q_smem_bytes(0, a.H), stream>>>(x, a);
-  else
-    decode_mma_kernel<1><<<num_sms * kCtas, kThreads, q_smem_bytes(1, a.I), stream>>>(x, a);
+  if (kind == 0) {
+    if (ks >= 8) launch_ks<0, 8>(a, x, num_sms, stream);
+    else if (ks >= 4) launch_ks<0, 4>(a, x, num_sms, stream);
+    else if (ks >= 2) launch_ks<0, 2>(a, x, num_sms, stream);
+    else launch_ks<0, 1>(a, x, num_sms, stream);
+  } else {
+    if (ks >= 8) launch_ks<1, 8>(a, x, num_sms, stream);
+    else if (ks >= 4) launch_ks<1, 4>(a, x, num_sms, stream);
+    else if (ks >= 2) launch_ks<1, 2>(a, x, num_sms, stream);
+    else launch_ks<1, 1>(a, x, num_sms, stream);
+  }
 }
 
 }  // namespace wm

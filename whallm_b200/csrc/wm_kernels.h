@@ -38,6 +38,16 @@ void launch_dequant(int format, const void* weight, const void* scale, int64_t r
 // ---- router (wm_route.cu)
 size_t router_smem_bytes(int H);
 void router_init_attributes(int max_hidden);
+// Top-k selection: parameters and outputs idx int32 / w fp32 [T, K].
+struct TopkArgs {
+  const float* bias;  // fp32 [E] or null
+  int K, kind, n_groups, topk_groups;
+  float route_scale;
+  int32_t* idx;
+  float* w;
+};
+
+
 // With nw (bf16 [H] RMSNorm weight) a call that router_logits_fused_ok takes
 // routes bf16((x * rstd) * nw) and writes those rows to xn (when non-null);
 // other calls ignore nw -- normalise first with launch_rmsnorm.
@@ -49,8 +59,7 @@ bool router_logits_fused_ok(int T, int H, int E);
 void launch_rmsnorm(const uint16_t* x, const uint16_t* nw, int T, int H, float eps, uint16_t* xn,
                     cudaStream_t stream);
 void launch_shared_gate(const uint16_t* x, const uint16_t* g, int T, int H, float* sg, cudaStream_t stream);
-void launch_router_topk(const float* logits, const float* bias, int T, int E, int K, int kind, int n_groups,
-                        int topk_groups, float route_scale, int32_t* idx, float* w, cudaStream_t stream);
+void launch_router_topk(const float* logits, int T, int E, const TopkArgs& tk, cudaStream_t stream);
 
 // ---- router logits on tcgen05 for long calls (wm_router_sm100.cu); tm_x / tm_w
 // point to CUtensorMaps of x [T, H] and W_r [E, H] (bf16, 64 x 128 boxes, 128B swizzle)
@@ -127,7 +136,13 @@ void launch_decode(const DecodeArgs& a, int kind, const void* const* maps, int n
 // (boxes of 64 x 8, 128-byte swizzle), K = H for kind 0 (gate/up) and I for kind 1.
 bool decode_mma_shape_ok(int H, int I);
 void decode_mma_init_attributes(int max_h, int max_i);
-void launch_decode_mma(const DecodeArgs& a, int kind, const void* tmap_x, int num_sms, cudaStream_t stream);
+// ks: K split (1, 2, 4, 8; see decode_mma_split) -- items of 1 / ks of the
+// rows, each warp over 1 / ks of K
+void launch_decode_mma(const DecodeArgs& a, int kind, const void* tmap_x, int num_sms, cudaStream_t stream,
+                       int ks = 1);
+// The K split for a call of about `tiles` 8-token tiles: the smallest that
+// gives every SM an item (K / 128 chunks must divide evenly).
+int decode_mma_split(int kind, int H, int I, int tiles, int num_sms);
 
 // ---- prefill grouped GEMM on tcgen05 (wm_gemm_sm100.cu)
 struct GemmArgs {

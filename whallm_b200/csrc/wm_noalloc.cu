@@ -171,8 +171,9 @@ extern "C" WM_EXPORT int wm_moe_forward_noalloc(const wm_moe_args* a, void* stre
     launch_router_logits(x, static_cast<const uint16_t*>(a->router_weight), sg_w, int(T), int(H), int(E), logits, sg, s,
                          fused ? nw : nullptr, a->norm_eps, fused ? xn : nullptr);
     if (fused) x = xn;
-    launch_router_topk(logits, a->router_bias, int(T), int(E), int(K), a->router, a->n_groups, a->topk_groups,
-                       a->route_scale, di, dw, s);
+    launch_router_topk(logits, int(T), int(E),
+                       TopkArgs{a->router_bias, int(K), a->router, a->n_groups, a->topk_groups, a->route_scale, di, dw},
+                       s);
     idx = di;
     w = dw;
   } else if (sg_w != nullptr) {

@@ -113,6 +113,192 @@ __device__ __forceinline__ float shared_gate_row(const uint16_t* __restrict__ xr
   return 1.0f / (1.0f + expf(-acc));
 }
 
+// Warp-wide argmax of (key, index): larger key wins, equal keys -> lower index.
+__device__ __forceinline__ void warp_argmax(float& key, int& idx) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float k2 = __shfl_xor_sync(0xffffffffu, key, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (k2 > key || (k2 == key && i2 < idx)) {
+      key = k2;
+      idx = i2;
+    }
+  }
+}
+
+// Top-k of one token by one warp.  Lane l holds experts e = l + 32 j, j < EPL
+// (E <= 32 EPL).
+template <int EPL>
+__device__ __forceinline__ void topk_token(const float* __restrict__ row, const TopkArgs& tk, int E, int t,
+                                           int lane) {
+  const float* __restrict__ bias = tk.bias;
+  const int K = tk.K, kind = tk.kind, n_groups = tk.n_groups, topk_groups = tk.topk_groups;
+  const float route_scale = tk.route_scale;
+  int32_t* __restrict__ idx_out = tk.idx;
+  float* __restrict__ w_out = tk.w;
+  const int per_lane = (E + 31) / 32;
+  float score[EPL], key[EPL], lg[EPL], bs[EPL];
+  uint32_t taken = 0;  // bit j: slot j is selected or not eligible
+  // every load first (branch-free, predicated), so they are in flight together
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int e = lane + 32 * j;
+    const bool in = j < per_lane && e < E;
+    lg[j] = in ? row[e] : -INFINITY;
+    bs[j] = in && bias != nullptr ? __ldg(bias + e) : 0.0f;
+  }
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int e = lane + 32 * j;
+    float l = lg[j];
+    // A softmax router takes `bias` as an additive logit bias (the reference's
+    // Qwen router has none; the synthetic Zipf-skewed workload uses one).
+    if (kind == WM_ROUTER_SOFTMAX && bias != nullptr) l += bs[j];
+    float s = l;
+    if (kind == WM_ROUTER_SQRTSOFTPLUS)
+      s = sqrtf(fmaxf(l, 0.0f) + log1pf(expf(-fabsf(l))));
+    else if (kind == WM_ROUTER_SIGMOID || kind == WM_ROUTER_SIGMOID_GROUPED)
+      s = 1.0f / (1.0f + expf(-l));
+    score[j] = s;
+    float k = kind == WM_ROUTER_SOFTMAX ? l : s + bs[j];
+    if (!(j < per_lane && e < E)) {
+      k = -INFINITY;
+      taken |= 1u << j;
+    }
+    key[j] = k;
+  }
+  if (kind == WM_ROUTER_SIGMOID_GROUPED && n_groups > 1) {
+    // Group score: sum of the two largest biased scores of its E / n_groups
+    // contiguous experts.  The top `topk_groups` groups stay eligible.
+    const int per_group = E / n_groups;
+    uint32_t group_keep = 0;  // bit g (n_groups <= 32)
+    float gscore_lane = -INFINITY;  // lane g holds group g's score
+    for (int g = 0; g < n_groups; ++g) {
+      float best = -INFINITY, second = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < EPL; ++j) {
+        const int e = lane + 32 * j;
+        if (j < per_lane && e < E && e / per_group == g) {
+          const float v = key[j];
+          if (v > best) {
+            second = best;
+            best = v;
+          } else if (v > second) {
+            second = v;
+          }
+        }
+      }
+      // merge (best, second) across lanes
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float b2 = __shfl_xor_sync(0xffffffffu, best, o);
+        const float s2 = __shfl_xor_sync(0xffffffffu, second, o);
+        const float nb = fmaxf(best, b2);
+        const float ns = fmaxf(fminf(best, b2), fmaxf(second, s2));
+        best = nb;
+        second = ns;
+      }
+      if (lane == g) gscore_lane = best + second;
+    }
+    for (int i = 0; i < topk_groups; ++i) {
+      float k = (group_keep >> lane) & 1u ? -INFINITY : gscore_lane;
+      int gi = lane < n_groups ? lane : 0x7fffffff;
+      if (lane >= n_groups) k = -INFINITY;
+      warp_argmax(k, gi);
+      group_keep |= 1u << gi;
+    }
+#pragma unroll
+    for (int j = 0; j < EPL; ++j) {
+      const int e = lane + 32 * j;
+      if (j < per_lane && e < E && !((group_keep >> (e / per_group)) & 1u)) taken |= 1u << j;
+    }
+  }
+  // top-k by key: every lane keeps its best remaining slot (a tree over its
+  // slots, ties to the lower slot); each round two warp reductions find the
+  // largest key and, among equal keys, the lowest expert index; only the
+  // winner's lane rescans.  Lane k keeps selection k.
+  float lbest = -INFINITY;
+  int lidx = 0x7fffffff;
+  auto rescan = [&]() {
+    float bk[EPL];
+    int bj[EPL];
+#pragma unroll
+    for (int j = 0; j < EPL; ++j) {
+      bk[j] = ((taken >> j) & 1u) ? -INFINITY : key[j];
+      bj[j] = j;
+    }
+#pragma unroll
+    for (int w = EPL / 2; w > 0; w >>= 1)
+#pragma unroll
+      for (int j = 0; j < w; ++j)
+        if (bk[j + w] > bk[j] || (bk[j + w] == bk[j] && bj[j + w] < bj[j])) {
+          bk[j] = bk[j + w];
+          bj[j] = bj[j + w];
+        }
+    lbest = bk[0];
+    lidx = lane + 32 * bj[0];
+  };
+  // larger key -> larger unsigned value
+  auto ordered = [](float f) {
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  };
+  rescan();
+  float sum = 0.0f, top_logit = 0.0f, my_w[2] = {0.0f, 0.0f};  // selections lane and lane + 32
+  int my_idx[2] = {0, 0};
+  for (int k = 0; k < K; ++k) {
+    const uint32_t u = ordered(lbest);
+    const uint32_t top = __reduce_max_sync(0xffffffffu, u);
+    int bi = int(__reduce_min_sync(0xffffffffu, u == top ? uint32_t(lidx) : 0xffffffffu));
+    if (bi < 0 || bi >= 32 * EPL) bi = 0;  // fewer eligible experts than K: cannot happen for valid shapes
+    float s_sel = 0.0f;
+    if ((bi & 31) == lane) {
+      taken |= 1u << (bi >> 5);
+#pragma unroll
+      for (int j = 0; j < EPL; ++j)
+        if (j == (bi >> 5)) s_sel = score[j];
+      rescan();
+    }
+    s_sel = __shfl_sync(0xffffffffu, s_sel, bi & 31);
+    if (kind == WM_ROUTER_SOFTMAX) {
+      if (k == 0) top_logit = s_sel;
+      s_sel = expf(s_sel - top_logit);
+    }
+    sum += s_sel;
+    if (lane == (k & 31)) {  // static register indices: selection k goes to slot k / 32
+      if (k < 32) {
+        my_idx[0] = bi;
+        my_w[0] = s_sel;
+      } else {
+        my_idx[1] = bi;
+        my_w[1] = s_sel;
+      }
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int k = lane + 32 * h;
+    if (k < K) {
+      float v = my_w[h];
+      if (kind == WM_ROUTER_SOFTMAX)
+        v = v / sum;
+      else if (K > 1)
+        v = v / (sum + 1e-20f);
+      idx_out[(int64_t)t * K + k] = my_idx[h];
+      w_out[(int64_t)t * K + k] = v * route_scale;
+    }
+  }
+}
+
+// Top-k: one warp per token, two per block, so short calls spread over SMs.
+template <int EPL>
+__global__ void __launch_bounds__(64) router_topk_kernel(const float* __restrict__ logits, int T, int E,
+                                                          const TopkArgs tk) {
+  const int t = blockIdx.x * 2 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  topk_token<EPL>(logits + int64_t(t) * E, tk, E, t, threadIdx.x & 31);
+}
+
 constexpr int kRouterWarps = 8;
 constexpr int kRouterSteps = 4;  // 64-K steps per warp per batch of loads
 
@@ -286,175 +472,6 @@ void launch_rmsnorm(const uint16_t* x, const uint16_t* nw, int T, int H, float e
 
 bool router_logits_fused_ok(int T, int H, int E) { return H % (64 * kRouterWarps) == 0 && E % 8 == 0 && T <= 4096; }
 
-// Warp-wide argmax of (key, index): larger key wins, equal keys -> lower index.
-__device__ __forceinline__ void warp_argmax(float& key, int& idx) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float k2 = __shfl_xor_sync(0xffffffffu, key, o);
-    const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
-    if (k2 > key || (k2 == key && i2 < idx)) {
-      key = k2;
-      idx = i2;
-    }
-  }
-}
-
-// One warp per token.  Lane l holds experts e = l + 32 j, j < EPL (E <= 32 EPL).
-template <int EPL>
-__global__ void __launch_bounds__(64) router_topk_kernel(const float* __restrict__ logits,
-                                                          const float* __restrict__ bias, int T, int E, int K,
-                                                          int kind, int n_groups, int topk_groups, float route_scale,
-                                                          int32_t* __restrict__ idx_out, float* __restrict__ w_out) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 2 + warp;  // two warps (tokens) per block: short calls spread over SMs
-  if (t >= T) return;
-  const float* row = logits + (int64_t)t * E;
-  const int per_lane = (E + 31) / 32;
-  float score[EPL], key[EPL];
-  uint32_t taken = 0;  // bit j: slot j is selected or not eligible
-#pragma unroll
-  for (int j = 0; j < EPL; ++j) {
-    const int e = lane + 32 * j;
-    float l = (j < per_lane && e < E) ? row[e] : -INFINITY;
-    // A softmax router takes `bias` as an additive logit bias (the reference's
-    // Qwen router has none; the synthetic Zipf-skewed workload uses one).
-    if (kind == WM_ROUTER_SOFTMAX && bias != nullptr && e < E) l += bias[e];
-    float s = l;
-    if (kind == WM_ROUTER_SQRTSOFTPLUS)
-      s = sqrtf(fmaxf(l, 0.0f) + log1pf(expf(-fabsf(l))));
-    else if (kind == WM_ROUTER_SIGMOID || kind == WM_ROUTER_SIGMOID_GROUPED)
-      s = 1.0f / (1.0f + expf(-l));
-    score[j] = s;
-    float k = kind == WM_ROUTER_SOFTMAX ? l : s + (bias != nullptr && e < E ? bias[e] : 0.0f);
-    if (!(j < per_lane && e < E)) {
-      k = -INFINITY;
-      taken |= 1u << j;
-    }
-    key[j] = k;
-  }
-  if (kind == WM_ROUTER_SIGMOID_GROUPED && n_groups > 1) {
-    // Group score: sum of the two largest biased scores of its E / n_groups
-    // contiguous experts.  The top `topk_groups` groups stay eligible.
-    const int per_group = E / n_groups;
-    uint32_t group_keep = 0;  // bit g (n_groups <= 32)
-    float gscore_lane = -INFINITY;  // lane g holds group g's score
-    for (int g = 0; g < n_groups; ++g) {
-      float best = -INFINITY, second = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < EPL; ++j) {
-        const int e = lane + 32 * j;
-        if (j < per_lane && e < E && e / per_group == g) {
-          const float v = key[j];
-          if (v > best) {
-            second = best;
-            best = v;
-          } else if (v > second) {
-            second = v;
-          }
-        }
-      }
-      // merge (best, second) across lanes
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float b2 = __shfl_xor_sync(0xffffffffu, best, o);
-        const float s2 = __shfl_xor_sync(0xffffffffu, second, o);
-        const float nb = fmaxf(best, b2);
-        const float ns = fmaxf(fminf(best, b2), fmaxf(second, s2));
-        best = nb;
-        second = ns;
-      }
-      if (lane == g) gscore_lane = best + second;
-    }
-    for (int i = 0; i < topk_groups; ++i) {
-      float k = (group_keep >> lane) & 1u ? -INFINITY : gscore_lane;
-      int gi = lane < n_groups ? lane : 0x7fffffff;
-      if (lane >= n_groups) k = -INFINITY;
-      warp_argmax(k, gi);
-      group_keep |= 1u << gi;
-    }
-#pragma unroll
-    for (int j = 0; j < EPL; ++j) {
-      const int e = lane + 32 * j;
-      if (j < per_lane && e < E && !((group_keep >> (e / per_group)) & 1u)) taken |= 1u << j;
-    }
-  }
-  // top-k by key: every lane keeps its best remaining slot (a tree over its
-  // slots, ties to the lower slot); each round two warp reductions find the
-  // largest key and, among equal keys, the lowest expert index; only the
-  // winner's lane rescans.  Lane k keeps selection k.
-  float lbest = -INFINITY;
-  int lidx = 0x7fffffff;
-  auto rescan = [&]() {
-    float bk[EPL];
-    int bj[EPL];
-#pragma unroll
-    for (int j = 0; j < EPL; ++j) {
-      bk[j] = ((taken >> j) & 1u) ? -INFINITY : key[j];
-      bj[j] = j;
-    }
-#pragma unroll
-    for (int w = EPL / 2; w > 0; w >>= 1)
-#pragma unroll
-      for (int j = 0; j < w; ++j)
-        if (bk[j + w] > bk[j] || (bk[j + w] == bk[j] && bj[j + w] < bj[j])) {
-          bk[j] = bk[j + w];
-          bj[j] = bj[j + w];
-        }
-    lbest = bk[0];
-    lidx = lane + 32 * bj[0];
-  };
-  // larger key -> larger unsigned value
-  auto ordered = [](float f) {
-    const uint32_t u = __float_as_uint(f);
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  };
-  rescan();
-  float sum = 0.0f, top_logit = 0.0f, my_w[2] = {0.0f, 0.0f};  // selections lane and lane + 32
-  int my_idx[2] = {0, 0};
-  for (int k = 0; k < K; ++k) {
-    const uint32_t u = ordered(lbest);
-    const uint32_t top = __reduce_max_sync(0xffffffffu, u);
-    int bi = int(__reduce_min_sync(0xffffffffu, u == top ? uint32_t(lidx) : 0xffffffffu));
-    if (bi < 0 || bi >= 32 * EPL) bi = 0;  // fewer eligible experts than K: cannot happen for valid shapes
-    float s_sel = 0.0f;
-    if ((bi & 31) == lane) {
-      taken |= 1u << (bi >> 5);
-#pragma unroll
-      for (int j = 0; j < EPL; ++j)
-        if (j == (bi >> 5)) s_sel = score[j];
-      rescan();
-    }
-    s_sel = __shfl_sync(0xffffffffu, s_sel, bi & 31);
-    if (kind == WM_ROUTER_SOFTMAX) {
-      if (k == 0) top_logit = s_sel;
-      s_sel = expf(s_sel - top_logit);
-    }
-    sum += s_sel;
-    if (lane == (k & 31)) {  // static register indices: selection k goes to slot k / 32
-      if (k < 32) {
-        my_idx[0] = bi;
-        my_w[0] = s_sel;
-      } else {
-        my_idx[1] = bi;
-        my_w[1] = s_sel;
-      }
-    }
-  }
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int k = lane + 32 * h;
-    if (k < K) {
-      float v = my_w[h];
-      if (kind == WM_ROUTER_SOFTMAX)
-        v = v / sum;
-      else if (K > 1)
-        v = v / (sum + 1e-20f);
-      idx_out[(int64_t)t * K + k] = my_idx[h];
-      w_out[(int64_t)t * K + k] = v * route_scale;
-    }
-  }
-}
-
 size_t router_smem_bytes(int H) { return size_t(8) * H * 2; }
 
 void router_init_attributes(int max_hidden) {
@@ -509,18 +526,14 @@ void launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t*
   router_logits_kernel<<<blocks, 256, smem, stream>>>(x, wr, sg_w, T, H, E, logits, sg);
 }
 
-void launch_router_topk(const float* logits, const float* bias, int T, int E, int K, int kind, int n_groups,
-                        int topk_groups, float route_scale, int32_t* idx, float* w, cudaStream_t stream) {
+void launch_router_topk(const float* logits, int T, int E, const TopkArgs& tk, cudaStream_t stream) {
   const int blocks = (T + 1) / 2;
   if (E <= 256)
-    router_topk_kernel<8><<<blocks, 64, 0, stream>>>(logits, bias, T, E, K, kind, n_groups, topk_groups,
-                                                       route_scale, idx, w);
+    router_topk_kernel<8><<<blocks, 64, 0, stream>>>(logits, T, E, tk);
   else if (E <= 512)
-    router_topk_kernel<16><<<blocks, 64, 0, stream>>>(logits, bias, T, E, K, kind, n_groups, topk_groups,
-                                                        route_scale, idx, w);
+    router_topk_kernel<16><<<blocks, 64, 0, stream>>>(logits, T, E, tk);
   else
-    router_topk_kernel<32><<<blocks, 64, 0, stream>>>(logits, bias, T, E, K, kind, n_groups, topk_groups,
-                                                        route_scale, idx, w);
+    router_topk_kernel<32><<<blocks, 64, 0, stream>>>(logits, T, E, tk);
 }
 
 }  // namespace wm
