@@ -66,6 +66,13 @@ enum wm_layout {
      reference decodes this format only for resident tensors
      (mimo/weights.py:17-43). */
   WM_LAYOUT_W13_FP8_B128 = 2,
+  /* FP8 E4M3 experts with UE8M0 32x32 block scales (the V4.1 dense FP8
+     format, dequant.py:45-50): w13 = [w3; w1] (up rows first) E4M3 [2I, H]
+     with scales [2I/32, H/32] bytes, w2 E4M3 [H, I] with scales [H/32, I/32];
+     scale rows 2-byte aligned.  For the V4.1 shared expert and dense FP8
+     FFNs (one expert, every token routed to it).  New layout: the reference
+     keeps this format only for resident tensors. */
+  WM_LAYOUT_W13_FP8_B32 = 3,
 };
 
 /* Weight formats for wm_dequant. */

@@ -27,7 +27,7 @@ HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "libwm_oracle.so"
 
 CONV_MLX, CONV_METAL = 0, 1
-LAYOUT_QWEN_GATE_UP_MXFP4, LAYOUT_DS_W13_MXFP4, LAYOUT_W13_FP8_B128 = 0, 1, 2
+LAYOUT_QWEN_GATE_UP_MXFP4, LAYOUT_DS_W13_MXFP4, LAYOUT_W13_FP8_B128, LAYOUT_W13_FP8_B32 = 0, 1, 2, 3
 ROUTER_SOFTMAX, ROUTER_SQRTSOFTPLUS, ROUTER_SIGMOID, ROUTER_SIGMOID_GROUPED = 0, 1, 2, 3
 SHARED_NONE, SHARED_SIGMOID_GATE, SHARED_ONE = 0, 1, 2
 NUMERICS_BF16, NUMERICS_FP32 = 0, 1

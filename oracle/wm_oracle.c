@@ -45,7 +45,7 @@
 #define WMO_EXPORT __attribute__((visibility("default")))
 
 enum { WMO_CONV_MLX = 0, WMO_CONV_METAL = 1 };
-enum { WMO_LAYOUT_QWEN_GATE_UP_MXFP4 = 0, WMO_LAYOUT_DS_W13_MXFP4 = 1, WMO_LAYOUT_W13_FP8_B128 = 2 };
+enum { WMO_LAYOUT_QWEN_GATE_UP_MXFP4 = 0, WMO_LAYOUT_DS_W13_MXFP4 = 1, WMO_LAYOUT_W13_FP8_B128 = 2, WMO_LAYOUT_W13_FP8_B32 = 3 };
 enum { WMO_ROUTER_SOFTMAX = 0, WMO_ROUTER_SQRTSOFTPLUS = 1, WMO_ROUTER_SIGMOID = 2, WMO_ROUTER_SIGMOID_GROUPED = 3 };
 enum { WMO_SHARED_NONE = 0, WMO_SHARED_SIGMOID_GATE = 1, WMO_SHARED_ONE = 2 };
 enum { WMO_NUMERICS_BF16 = 0, WMO_NUMERICS_FP32 = 1 };
@@ -277,6 +277,11 @@ static inline float weight_at(int32_t layout, const uint8_t* w, const void* scal
   if (layout == WMO_LAYOUT_W13_FP8_B128) {
     const float* s = (const float*)scale;
     volatile float prod = wmo_e4m3(w[o * cols + k]) * s[(o / 128) * ((cols + 127) / 128) + k / 128];
+    return bf16_f32(f32_bf16(prod));
+  }
+  if (layout == WMO_LAYOUT_W13_FP8_B32) { /* dequant.py:45-50, as wmo_dequant_fp8_b32 */
+    const uint8_t* s = (const uint8_t*)scale;
+    volatile float prod = wmo_e4m3(w[o * cols + k]) * wmo_e8m0(s[(o / 32) * ((cols + 31) / 32) + k / 32], WMO_CONV_MLX);
     return bf16_f32(f32_bf16(prod));
   }
   uint8_t byte = w[o * (cols / 2) + k / 2];

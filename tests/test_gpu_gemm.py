@@ -26,7 +26,7 @@ def rel(y_bits, ref_bits):
 
 def small_layer(layout, E, H, I, seed, gate=lib.SHARED_NONE, limit=0.0):
     g = torch.Generator(device=DEV).manual_seed(seed)
-    proj = synth.fp8_projection if layout == lib.LAYOUT_W13_FP8_B128 else synth.mxfp4_projection
+    proj = synth.projection_for(layout)
     w13, s13 = proj(E, 2 * I, H, g, DEV)
     w2, s2 = proj(E, H, I, g, DEV)
     shared = None
@@ -68,7 +68,7 @@ def test_gemm_single_tile(gemm_engine):
 
 
 @pytest.mark.parametrize("layout,limit", [(lib.LAYOUT_QWEN_GATE_UP_MXFP4, 0.0), (lib.LAYOUT_DS_W13_MXFP4, 10.0),
-                                          (lib.LAYOUT_W13_FP8_B128, 0.0)])
+                                          (lib.LAYOUT_W13_FP8_B128, 0.0), (lib.LAYOUT_W13_FP8_B32, 0.0)])
 @pytest.mark.parametrize("T", [1, 65, 300])
 def test_gemm_expert_pairs_match_oracle(gemm_engine, layout, limit, T):
     E, H, I, K = 16, 512, 256, 4
@@ -83,7 +83,8 @@ def test_gemm_expert_pairs_match_oracle(gemm_engine, layout, limit, T):
 
 
 @pytest.mark.parametrize("layout,gate", [(lib.LAYOUT_QWEN_GATE_UP_MXFP4, lib.SHARED_SIGMOID_GATE),
-                                         (lib.LAYOUT_W13_FP8_B128, lib.SHARED_ONE)])
+                                         (lib.LAYOUT_W13_FP8_B128, lib.SHARED_ONE),
+                                         (lib.LAYOUT_W13_FP8_B32, lib.SHARED_ONE)])
 def test_gemm_forward_matches_gemv_and_oracle(gemm_engine, gemv_engine, layout, gate):
     E, H, I, K, T = 16, 1024, 512, 8, 257
     layer = small_layer(layout, E, H, I, seed=30 + layout, gate=gate)

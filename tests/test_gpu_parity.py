@@ -150,14 +150,10 @@ def test_router_tensor_cores_long_call(engine_factory, kind, E, K, groups, topg)
 
 def _small_layer(layout, E, H, I, seed, shared_gate=lib.SHARED_NONE, limit=0.0):
     g = torch.Generator(device=DEV).manual_seed(seed)
-    if layout == lib.LAYOUT_W13_FP8_B128:
-        w13, s13 = synth.fp8_projection(E, 2 * I, H, g, DEV)
-        w2, s2 = synth.fp8_projection(E, H, I, g, DEV)
-        sh = [synth.fp8_projection(1, 2 * I, H, g, DEV), synth.fp8_projection(1, H, I, g, DEV)]
-    else:
-        w13, s13 = synth.mxfp4_projection(E, 2 * I, H, g, DEV)
-        w2, s2 = synth.mxfp4_projection(E, H, I, g, DEV)
-        sh = [synth.mxfp4_projection(1, 2 * I, H, g, DEV), synth.mxfp4_projection(1, H, I, g, DEV)]
+    proj = synth.projection_for(layout)
+    w13, s13 = proj(E, 2 * I, H, g, DEV)
+    w2, s2 = proj(E, H, I, g, DEV)
+    sh = [proj(1, 2 * I, H, g, DEV), proj(1, H, I, g, DEV)]
     shared = None
     if shared_gate != lib.SHARED_NONE:
         gate_w = (torch.randn((H,), generator=g, device=DEV) / H ** 0.5).to(torch.bfloat16)
@@ -179,7 +175,7 @@ def test_config0_single_expert_pairs(engine_factory):
 
 
 @pytest.mark.parametrize("layout,limit", [(lib.LAYOUT_QWEN_GATE_UP_MXFP4, 0.0), (lib.LAYOUT_DS_W13_MXFP4, 10.0),
-                                          (lib.LAYOUT_W13_FP8_B128, 0.0)])
+                                          (lib.LAYOUT_W13_FP8_B128, 0.0), (lib.LAYOUT_W13_FP8_B32, 0.0)])
 @pytest.mark.parametrize("T", [1, 5, 33])
 def test_expert_pairs_match_oracle(engine_factory, layout, limit, T):
     E, H, I, K = 16, 512, 256, 4
@@ -196,7 +192,8 @@ def test_expert_pairs_match_oracle(engine_factory, layout, limit, T):
 
 @pytest.mark.parametrize("layout,gate", [(lib.LAYOUT_QWEN_GATE_UP_MXFP4, lib.SHARED_SIGMOID_GATE),
                                          (lib.LAYOUT_DS_W13_MXFP4, lib.SHARED_ONE),
-                                         (lib.LAYOUT_W13_FP8_B128, lib.SHARED_ONE)])
+                                         (lib.LAYOUT_W13_FP8_B128, lib.SHARED_ONE),
+                                         (lib.LAYOUT_W13_FP8_B32, lib.SHARED_ONE)])
 def test_forward_matches_oracle_small(engine_factory, layout, gate):
     E, H, I, K, T = 16, 512, 256, 4, 24
     layer = _small_layer(layout, E, H, I, seed=51 + layout, shared_gate=gate)

@@ -121,3 +121,18 @@ def test_rms_norm_is_scale_invariant_and_follows_eps():
     np.testing.assert_array_equal(a, b)
     zero = np.zeros((1, 256), np.uint16)
     assert not oracle.bf16_to_f32(oracle.rms_norm(zero, w, 1e-6)).any()  # zero rows stay zero (signed)
+
+
+def test_fp8_b32_layer_weights_are_the_dequantised_blocks():
+    """The layer restatement of the FP8 32x32 layout multiplies by exactly the
+    weights dequant.py:45-50 produces (wmo_dequant_fp8_b32)."""
+    rng = np.random.default_rng(7)
+    O, I = 96, 128
+    codes = rng.integers(0, 254, (O, I))
+    w = np.where(codes < 127, codes, codes + 1).astype(np.uint8)
+    s = (127 + rng.integers(-10, -3, (O // 32, I // 32))).astype(np.uint8)
+    x = oracle.f32_to_bf16(rng.standard_normal((3, I)).astype(np.float32))
+    y = oracle.linear(oracle.LAYOUT_W13_FP8_B32, w, s, x)
+    deq = oracle.bf16_to_f32(oracle.dequant_fp8_b32(w, s)).astype(np.float64)
+    want = oracle.bf16_to_f32(x).astype(np.float64) @ deq.T
+    np.testing.assert_allclose(y, want, rtol=1e-6, atol=1e-6)

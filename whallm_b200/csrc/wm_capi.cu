@@ -76,9 +76,14 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-int fmt_of(int layout) { return layout == WM_LAYOUT_W13_FP8_B128 ? wm::kFmtFp8B128 : wm::kFmtMxfp4; }
+int fmt_of(int layout) {
+  return layout == WM_LAYOUT_W13_FP8_B128 ? wm::kFmtFp8B128
+         : layout == WM_LAYOUT_W13_FP8_B32 ? wm::kFmtFp8B32
+                                           : wm::kFmtMxfp4;
+}
 
-// Validates the shape / pointer contract shared by every expert call.
+bool is_fp8(int layout) { return layout == WM_LAYOUT_W13_FP8_B128 || layout == WM_LAYOUT_W13_FP8_B32; }
+
 // The pre-MoE RMSNorm fields (x checked by the caller).
 int validate_norm(wm_ctx* ctx, const wm_moe_args* a) {
   if (a->norm_weight == nullptr) return WM_OK;
@@ -106,6 +111,7 @@ void run_rmsnorm(wm_ctx* ctx, const wm_moe_args* a, cudaStream_t s) {
   ctx->counters.launches += 1;
 }
 
+// Validates the shape / pointer contract shared by every expert call.
 int validate_experts(wm_ctx* ctx, const wm_moe_args* a, bool need_router) {
   const wm_options& o = ctx->opt;
   if (a == nullptr) return fail(ctx, "args is NULL");
@@ -117,7 +123,7 @@ int validate_experts(wm_ctx* ctx, const wm_moe_args* a, bool need_router) {
   if (a->K <= 0 || a->K > o.max_topk || a->K > a->E)
     return fail(ctx, "K = %d outside (0, min(E, max_topk %d)]", a->K, o.max_topk);
   if (a->H % 64 || a->I % 64) return fail(ctx, "H (%d) and I (%d) must be multiples of 64", a->H, a->I);
-  if (a->layout < WM_LAYOUT_QWEN_GATE_UP_MXFP4 || a->layout > WM_LAYOUT_W13_FP8_B128)
+  if (a->layout < WM_LAYOUT_QWEN_GATE_UP_MXFP4 || a->layout > WM_LAYOUT_W13_FP8_B32)
     return fail(ctx, "unknown expert layout %d", a->layout);
   if (a->T == 0) return WM_OK;  // nothing is read or written
   if (a->x == nullptr || !aligned(a->x, 16)) return fail(ctx, "x must be a 16-byte aligned device pointer");
@@ -129,6 +135,8 @@ int validate_experts(wm_ctx* ctx, const wm_moe_args* a, bool need_router) {
       return fail(ctx, "expert weight regions must start on 16-byte boundaries (pointer and per-expert stride)");
     if (a->layout == WM_LAYOUT_W13_FP8_B128 && (!aligned(m->scale, 4) || m->scale_stride % 4))
       return fail(ctx, "FP8 block scales must be 4-byte aligned");
+    if (a->layout == WM_LAYOUT_W13_FP8_B32 && (!aligned(m->scale, 2) || m->scale_stride % 2))
+      return fail(ctx, "UE8M0 block scales must be 2-byte aligned");
   }
   if (a->shared_gate != WM_SHARED_NONE) {
     if (a->shared_gate != WM_SHARED_SIGMOID_GATE && a->shared_gate != WM_SHARED_ONE)
@@ -138,6 +146,9 @@ int validate_experts(wm_ctx* ctx, const wm_moe_args* a, bool need_router) {
       return fail(ctx, "shared expert weights and scales must be given");
     if (!aligned(a->shared_w13.weight, 16) || !aligned(a->shared_w2.weight, 16))
       return fail(ctx, "shared expert weights must be 16-byte aligned");
+    const size_t sal = a->layout == WM_LAYOUT_W13_FP8_B128 ? 4 : a->layout == WM_LAYOUT_W13_FP8_B32 ? 2 : 1;
+    if (!aligned(a->shared_w13.scale, sal) || !aligned(a->shared_w2.scale, sal))
+      return fail(ctx, "shared expert block scales must be %zu-byte aligned", sal);
     if (a->shared_gate == WM_SHARED_SIGMOID_GATE && (a->shared_gate_weight == nullptr || !aligned(a->shared_gate_weight, 16)))
       return fail(ctx, "the sigmoid shared gate needs a 16-byte aligned bf16 [H] weight");
   }
@@ -284,7 +295,7 @@ enum Path { kPathGemv = 0, kPathDecode = 1, kPathGemm = 2, kPathDecodeMma = 3 };
 // decode kernel); else the CUDA-core GEMV.
 Path expert_path(const wm_ctx* ctx, const wm_moe_args* a, bool has_shared) {
   if (use_gemm(ctx, a)) return kPathGemm;
-  if (a->layout == WM_LAYOUT_W13_FP8_B128 || ctx->encode_tiled == nullptr) return kPathGemv;
+  if (is_fp8(a->layout) || ctx->encode_tiled == nullptr) return kPathGemv;
   const wm_matrix* ms[4] = {&a->w13, &a->w2, &a->shared_w13, &a->shared_w2};
   for (int i = 0; i < (has_shared ? 4 : 2); ++i)
     if (!aligned(ms[i]->scale, 16) || (i < 2 && ms[i]->scale_stride % 16)) return kPathGemv;

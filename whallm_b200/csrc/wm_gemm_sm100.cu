@@ -7,7 +7,8 @@
 // 23 binades of it), one hardware conversion and one f16x2 multiply per two
 // weights; the epilogue applies 2^(smax - 127) per column and 2^-k per row.
 // FP8 experts run with bf16 operands (each weight rounded to bf16 after its
-// fp32 block scale, as the reference decodes them).
+// fp32 128x128 block scale, as the reference decodes them, or after its
+// UE8M0 32x32 block scale, two per 64-K block).
 //
 // Reference arithmetic: mx.gather_qmm(..., mode="mxfp4", group_size=32,
 // sorted_indices=True) over expert-sorted rows (model.py:435-501,
@@ -243,7 +244,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int j = (warp - DQ_WARP0) * 32 + lane;  // B-tile row 0..255
     const int gate_base = a.gate_first ? 0 : a.I, up_base = a.gate_first ? a.I : 0;
     const int64_t rb = FMT == kFmtMxfp4 ? a.Kdim / 2 : a.Kdim;   // weight row bytes
-    const int S32 = a.Kdim / 32;                                  // E8M0 bytes per row (MXFP4)
+    const int S32 = a.Kdim / 32;  // scale bytes per row: E8M0 (MXFP4) or UE8M0 per 32-row block (FP8 32x32)
     auto grow_of = [&](int t) {
       const int nt = t % n_tiles_n;
       if (KIND == 0) return j < BN / 2 ? gate_base + nt * (BN / 2) + j : up_base + nt * (BN / 2) + (j - BN / 2);
@@ -259,6 +260,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int e = expert_of(t);
       const uint8_t* sb = KIND == 0 ? a.wts.s13_of(e) : a.wts.s2_of(e);
       if (FMT == kFmtMxfp4) return sb + int64_t(grow_of(t)) * S32;
+      if (FMT == kFmtFp8B32) return sb + int64_t(grow_of(t) / 32) * S32;  // UE8M0 row of the 32-row block
       return sb + (int64_t(grow_of(t) / 128) * (a.Kdim / 128)) * 4;
     };
     auto byte_max = [](uint32_t m) { return max(max(m & 0xffu, (m >> 8) & 0xffu), max((m >> 16) & 0xffu, m >> 24)); };
@@ -267,7 +269,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint8_t* lw = lt_t < total ? wrow_of(lt_t) : nullptr;
     const uint8_t* ls = lt_t < total ? srow_of(lt_t) : nullptr;
     uint4 wq[PF][NW];
-    uint32_t sq[PF];  // MXFP4: the K block's two E8M0 bytes; FP8: the block scale's bits
+    uint32_t sq[PF];  // MXFP4 / FP8 32x32: the K block's two scale bytes; FP8 128x128: the block scale's bits
     auto load_next = [&](uint4 (&w)[NW], uint32_t& sv) {
       if (lt_t >= total) return;
 #pragma unroll
@@ -280,7 +282,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           w[i + 1] = ldg_nc_v4(src + 16);
         }
       }
-      if (FMT == kFmtMxfp4) {
+      if (FMT == kFmtMxfp4 || FMT == kFmtFp8B32) {
         uint16_t v;
         asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(v) : "l"(ls + lkb * 2));
         sv = v;
@@ -348,15 +350,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           q[6] = dq_mxfp4_word_f16(w[1].z, m1);
           q[7] = dq_mxfp4_word_f16(w[1].w, m1);
         } else {
-          const float sc = __uint_as_float(sv);
-          q[0] = dq_fp8_8(w[0].x, w[0].y, sc);
-          q[1] = dq_fp8_8(w[0].z, w[0].w, sc);
-          q[2] = dq_fp8_8(w[1].x, w[1].y, sc);
-          q[3] = dq_fp8_8(w[1].z, w[1].w, sc);
-          q[4] = dq_fp8_8(w[NW - 2].x, w[NW - 2].y, sc);
-          q[5] = dq_fp8_8(w[NW - 2].z, w[NW - 2].w, sc);
-          q[6] = dq_fp8_8(w[NW - 1].x, w[NW - 1].y, sc);
-          q[7] = dq_fp8_8(w[NW - 1].z, w[NW - 1].w, sc);
+          // FP8 128x128: one fp32 scale per K block; 32x32: a UE8M0 scale per 32 K
+          const float sc0 = FMT == kFmtFp8B32 ? e8m0_to_f32(sv & 0xffu, true) : __uint_as_float(sv);
+          const float sc1 = FMT == kFmtFp8B32 ? e8m0_to_f32(sv >> 8, true) : sc0;
+          q[0] = dq_fp8_8(w[0].x, w[0].y, sc0);
+          q[1] = dq_fp8_8(w[0].z, w[0].w, sc0);
+          q[2] = dq_fp8_8(w[1].x, w[1].y, sc0);
+          q[3] = dq_fp8_8(w[1].z, w[1].w, sc0);
+          q[4] = dq_fp8_8(w[NW - 2].x, w[NW - 2].y, sc1);
+          q[5] = dq_fp8_8(w[NW - 2].z, w[NW - 2].w, sc1);
+          q[6] = dq_fp8_8(w[NW - 1].x, w[NW - 1].y, sc1);
+          q[7] = dq_fp8_8(w[NW - 1].z, w[NW - 1].w, sc1);
         }
         if (!mbar_wait(&sh.empty[s], ph ^ 1u, abort)) {
           fail(sh, a.status, 13);
@@ -478,6 +482,8 @@ void gemm_init_attributes() {
   set_attr<kFmtMxfp4, 1>();
   set_attr<kFmtFp8B128, 0>();
   set_attr<kFmtFp8B128, 1>();
+  set_attr<kFmtFp8B32, 0>();
+  set_attr<kFmtFp8B32, 1>();
 }
 
 bool gemm_shape_ok(int H, int I) { return H % BN == 0 && I % (BN / 2) == 0 && H % BK == 0 && I % BK == 0; }
@@ -490,6 +496,11 @@ void launch_gemm(const GemmArgs& a, int kind, const void* tmap_host, int num_sms
       gemm_kernel<kFmtMxfp4, 0><<<grid, block, SMEM_BYTES, stream>>>(tm, a);
     else
       gemm_kernel<kFmtMxfp4, 1><<<grid, block, SMEM_BYTES, stream>>>(tm, a);
+  } else if (a.fmt == kFmtFp8B32) {
+    if (kind == 0)
+      gemm_kernel<kFmtFp8B32, 0><<<grid, block, SMEM_BYTES, stream>>>(tm, a);
+    else
+      gemm_kernel<kFmtFp8B32, 1><<<grid, block, SMEM_BYTES, stream>>>(tm, a);
   } else {
     if (kind == 0)
       gemm_kernel<kFmtFp8B128, 0><<<grid, block, SMEM_BYTES, stream>>>(tm, a);

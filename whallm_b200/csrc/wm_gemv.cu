@@ -6,7 +6,8 @@
 // fp32 accumulation, each group's E8M0 scale applied to the group's partial
 // sum -- for the MXFP4 blob layout, and the same for FP8 E4M3 experts with
 // fp32 128x128 block scales (each weight rounded to bf16 after scaling, as
-// mimo/weights.py:17-43 decodes them).
+// mimo/weights.py:17-43 decodes them) or UE8M0 32x32 block scales (the same
+// rounding, deepseek_v41/dequant.py:45-50).
 //
 // Layout of the work: one CTA per (expert with rows, slab of outputs).  Each
 // CTA reads its slab of weights once with 16-byte non-allocating loads and
@@ -42,6 +43,9 @@ struct Traits<kFmtFp8B128> {
   static constexpr int kUnits = 4;
   __host__ __device__ static int64_t row_bytes(int cols) { return cols; }
 };
+
+template <>
+struct Traits<kFmtFp8B32> : Traits<kFmtFp8B128> {};
 
 // Shared-memory index of value k of a staged row (16-byte units XOR-swizzled
 // within each chunk by the chunk index).
@@ -152,6 +156,8 @@ template <int FMT>
 __device__ __forceinline__ float chunk_scale(const uint8_t* s, int64_t row, int cols, int c) {
   if constexpr (FMT == kFmtMxfp4) {
     return e8m0_to_f32(ldg_nc_u8(s + row * (cols / 32) + c));
+  } else if constexpr (FMT == kFmtFp8B32) {  // UE8M0 32x32 blocks (dequant.py:45-50)
+    return e8m0_to_f32(ldg_nc_u8(s + (row / 32) * ((cols + 31) / 32) + (c * 16) / 32), true);
   } else {
     const float* sf = reinterpret_cast<const float*>(s);
     return __ldg(sf + (row / 128) * ((cols + 127) / 128) + (c * 16) / 128);
@@ -292,6 +298,8 @@ void gemv_init_attributes(int max_smem) {
   cudaFuncSetAttribute(gemv_down_kernel<kFmtMxfp4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(gemv_gateup_kernel<kFmtFp8B128>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(gemv_down_kernel<kFmtFp8B128>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(gemv_gateup_kernel<kFmtFp8B32>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(gemv_down_kernel<kFmtFp8B32>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
 }
 
 size_t gemv_smem_bytes(int H, int I) { return size_t(kRows) * std::max(H, I) * sizeof(float); }
@@ -311,6 +319,13 @@ void launch_gemv(const GemvArgs& a, int fmt, int max_unique, cudaStream_t stream
     prof_end(prof, kProfGemvGateUp, stream);
     prof_begin(prof, kProfGemvDown, stream);
     gemv_down_kernel<kFmtMxfp4><<<grid_dn, 256, smem_dn, stream>>>(a);
+    prof_end(prof, kProfGemvDown, stream);
+  } else if (fmt == kFmtFp8B32) {
+    prof_begin(prof, kProfGemvGateUp, stream);
+    gemv_gateup_kernel<kFmtFp8B32><<<grid_gu, 256, smem_gu, stream>>>(a);
+    prof_end(prof, kProfGemvGateUp, stream);
+    prof_begin(prof, kProfGemvDown, stream);
+    gemv_down_kernel<kFmtFp8B32><<<grid_dn, 256, smem_dn, stream>>>(a);
     prof_end(prof, kProfGemvDown, stream);
   } else {
     prof_begin(prof, kProfGemvGateUp, stream);

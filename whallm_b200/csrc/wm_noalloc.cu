@@ -54,7 +54,7 @@ extern "C" WM_EXPORT int wm_moe_forward_noalloc(const wm_moe_args* a, void* stre
     return report(error, error_size, "invalid shape (T >= 0, H, I, E, K > 0, K <= E)");
   if (a->E > 1024 || a->K > 64) return report(error, error_size, "at most 1024 experts and top-64 routing");
   if (a->H % 64 || a->I % 64) return report(error, error_size, "H and I must be multiples of 64");
-  if (a->layout < WM_LAYOUT_QWEN_GATE_UP_MXFP4 || a->layout > WM_LAYOUT_W13_FP8_B128)
+  if (a->layout < WM_LAYOUT_QWEN_GATE_UP_MXFP4 || a->layout > WM_LAYOUT_W13_FP8_B32)
     return report(error, error_size, "unknown expert layout");
   if (a->layout == WM_LAYOUT_W13_FP8_B128 && (a->H % 128 || a->I % 128))
     return report(error, error_size, "FP8 128x128 experts need H and I multiples of 128");
@@ -206,7 +206,11 @@ extern "C" WM_EXPORT int wm_moe_forward_noalloc(const wm_moe_args* a, void* stre
   g.gate_first = a->layout == WM_LAYOUT_QWEN_GATE_UP_MXFP4 ? 1 : 0;
   g.limit = a->swiglu_limit;
   const int max_unique = int(std::min<int64_t>(E, T * K)) + (has_shared ? 1 : 0);
-  launch_gemv(g, a->layout == WM_LAYOUT_W13_FP8_B128 ? kFmtFp8B128 : kFmtMxfp4, max_unique, s, nullptr);
+  launch_gemv(g,
+              a->layout == WM_LAYOUT_W13_FP8_B128  ? kFmtFp8B128
+              : a->layout == WM_LAYOUT_W13_FP8_B32 ? kFmtFp8B32
+                                                   : kFmtMxfp4,
+              max_unique, s, nullptr);
   launch_combine(routed, p, w, sg, a->shared_gate, int(T), int(H), int(E), int(K), static_cast<uint16_t*>(a->out), s);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {

@@ -6,7 +6,7 @@
 namespace wm {
 
 // Weight formats the expert kernels decode.
-enum Fmt : int { kFmtMxfp4 = 0, kFmtFp8B128 = 1 };
+enum Fmt : int { kFmtMxfp4 = 0, kFmtFp8B128 = 1, kFmtFp8B32 = 2 };
 
 // Sorted-row plan of one call.  The (token, k) pairs are grouped by expert in
 // a stable order (ascending token, then k), each expert's group starting at

@@ -14,7 +14,7 @@ LIB_PATH = Path(os.environ.get("WHALLM_MOE_LIB") or Path(__file__).resolve().par
 
 WM_OK, WM_ERROR, WM_CANCELLED = 0, 1, 2
 
-LAYOUT_QWEN_GATE_UP_MXFP4, LAYOUT_DS_W13_MXFP4, LAYOUT_W13_FP8_B128 = 0, 1, 2
+LAYOUT_QWEN_GATE_UP_MXFP4, LAYOUT_DS_W13_MXFP4, LAYOUT_W13_FP8_B128, LAYOUT_W13_FP8_B32 = 0, 1, 2, 3
 FORMAT_MXFP4, FORMAT_FP8_B128, FORMAT_FP8_B32 = 0, 1, 2
 CONV_MLX, CONV_METAL = 0, 1
 ROUTER_SOFTMAX, ROUTER_SQRTSOFTPLUS, ROUTER_SIGMOID, ROUTER_SIGMOID_GROUPED = 0, 1, 2, 3

@@ -50,6 +50,21 @@ def fp8_projection(E: int, rows: int, cols: int, g: torch.Generator, device) -> 
     return w, s
 
 
+def fp8_b32_projection(E: int, rows: int, cols: int, g: torch.Generator, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """E4M3 [E, rows, cols] over the finite codes + UE8M0 [E, rows/32, cols/32] scale bytes 127 + U{-10..-4}."""
+    r = torch.randint(0, 254, (E, rows, cols), generator=g, device=device, dtype=torch.int16)
+    w = torch.where(r < 127, r, r + 1).to(torch.uint8)
+    s = (127 + torch.randint(-10, -3, (E, rows // 32, cols // 32), generator=g, device=device,
+                             dtype=torch.int16)).to(torch.uint8)
+    return w, s
+
+
+def projection_for(layout: int):
+    """The generator of a layout's projections (weights + scales)."""
+    return {lib.LAYOUT_W13_FP8_B128: fp8_projection, lib.LAYOUT_W13_FP8_B32: fp8_b32_projection}.get(
+        layout, mxfp4_projection)
+
+
 def activations(T: int, H: int, g: torch.Generator, device) -> torch.Tensor:
     return torch.randn((T, H), generator=g, device=device, dtype=torch.float32).to(torch.bfloat16)
 
