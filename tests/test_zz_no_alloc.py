@@ -110,3 +110,30 @@ def test_noalloc_with_pre_moe_norm(H):
     rc = lib.load().wm_moe_forward_noalloc(ctypes.byref(a), torch.cuda.current_stream().cuda_stream, err, len(err))
     assert rc == lib.WM_ERROR and "x_norm" in err.value.decode()
     eng.ctx.close()
+
+
+def test_small_noalloc_call_keeps_a_larger_handles_limits():
+    """Kernel shared-memory limits only ever grow: an allocation-free call with
+    a small H after a handle sized for H = 7168 must not lower the GEMV's limit
+    that handle's FP8 calls need (CUDA would refuse their launches)."""
+    H, I, E, K, T = 7168, 256, 4, 2, 3
+    g = torch.Generator(device=DEV).manual_seed(21)
+    w13, s13 = synth.fp8_projection(E, 2 * I, H, g, DEV)
+    w2, s2 = synth.fp8_projection(E, H, I, g, DEV)
+    big = LayerWeights(lib.LAYOUT_W13_FP8_B128, H, I, E, Projection.stacked(w13, s13), Projection.stacked(w2, s2))
+    eng = Engine(0, max_tokens=8, hidden=H, inter=I, experts=E, topk=K)
+    x = synth.activations(T, H, g, DEV)
+    idx = torch.tensor([[0, 1], [2, 3], [1, 2]], dtype=torch.int32, device=DEV)
+    want = eng.expert_pairs(big, x, idx)
+    eng.sync()
+    small = _layer()
+    small_eng = Engine(0, max_tokens=64, hidden=512, inter=256, experts=16, topk=4)
+    xs = synth.activations(4, 512, g, DEV)
+    out = torch.empty((4, 512), dtype=torch.bfloat16, device=DEV)
+    rc, msg = _noalloc(small_eng, small, xs, 4, out)
+    assert rc == lib.WM_OK, msg
+    got = eng.expert_pairs(big, x, idx)
+    eng.sync()
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    small_eng.ctx.close()
+    eng.ctx.close()

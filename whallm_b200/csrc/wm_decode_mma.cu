@@ -44,6 +44,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "wm_kernels.h"
 
@@ -545,6 +546,15 @@ void launch_ks(const DecodeArgs& a, const CUtensorMap& x, int num_sms, cudaStrea
 
 // Shapes beyond the shared-memory limit never take this kernel (decode_mma_shape_ok).
 void decode_mma_init_attributes(int max_h, int max_i) {
+  static std::mutex mu;
+  static int set_h[kMaxDevices] = {}, set_i[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return;
+  std::lock_guard<std::mutex> lock(mu);  // only ever raised (see gemv_init_attributes)
+  max_h = std::max(max_h, set_h[dev]);
+  max_i = std::max(max_i, set_i[dev]);
+  set_h[dev] = max_h;
+  set_i[dev] = max_i;
   set_smem<0, 1>(max_h);
   set_smem<0, 2>(max_h);
   set_smem<0, 4>(max_h);

@@ -17,6 +17,7 @@
 // row together and writes silu(g) * u (bf16) -- the reference's separate
 // expert_act / swiglu_pairs dispatch is fused away.
 #include <algorithm>
+#include <mutex>
 
 #include "wm_kernels.h"
 
@@ -293,7 +294,17 @@ __global__ void __launch_bounds__(256) gemv_down_kernel(GemvArgs a) {
   }
 }
 
+// Only ever raises the current device's limit: a handle sized for large
+// shapes and a later, smaller call (another handle, the allocation-free
+// entry point) launch the same kernels.
 void gemv_init_attributes(int max_smem) {
+  static std::mutex mu;
+  static int set_to[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return;
+  std::lock_guard<std::mutex> lock(mu);
+  if (max_smem <= set_to[dev]) return;
+  set_to[dev] = max_smem;
   cudaFuncSetAttribute(gemv_gateup_kernel<kFmtMxfp4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(gemv_down_kernel<kFmtMxfp4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(gemv_gateup_kernel<kFmtFp8B128>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);

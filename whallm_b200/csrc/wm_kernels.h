@@ -10,6 +10,8 @@
 
 namespace wm {
 
+constexpr int kMaxDevices = 64;  // per-device state of the attribute setters
+
 // ---- optional per-kernel timing with CUDA events (wm_profile_*)
 enum ProfSlot : int {
   kProfRouter = 0,

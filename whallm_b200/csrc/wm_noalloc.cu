@@ -29,12 +29,14 @@ namespace wm {
 namespace {
 
 constexpr size_t kScratchBytes = size_t(8) << 20;  // 8 MiB per GPU
-constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) uint8_t g_scratch[kScratchBytes];
 
 std::mutex g_setup_mutex;
 void* g_scratch_ptr[kMaxDevices] = {};
+int g_major[kMaxDevices] = {};          // compute capability, 0 = not looked up
+int g_smem_optin[kMaxDevices] = {};     // largest opt-in shared memory per block
+
 
 int report(char* error, size_t n, const char* msg) {
   if (error != nullptr && n > 0) snprintf(error, n, "%s", msg);
@@ -112,7 +114,6 @@ extern "C" WM_EXPORT int wm_moe_forward_noalloc(const wm_moe_args* a, void* stre
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return report(error, error_size, "no current CUDA device");
-  cudaDeviceProp prop{};
   {
     std::lock_guard<std::mutex> lock(g_setup_mutex);
     if (g_scratch_ptr[dev] == nullptr) {
@@ -124,12 +125,21 @@ extern "C" WM_EXPORT int wm_moe_forward_noalloc(const wm_moe_args* a, void* stre
       }
       g_scratch_ptr[dev] = p;
     }
+    // device queries and kernel attributes once per device (and size): a
+    // cudaGetDeviceProperties per call costs milliseconds of host time
+    if (g_major[dev] == 0) {
+      int major = 0, optin = 0;
+      if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+          cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+        return report(error, error_size, "CUDA device attributes could not be read");
+      g_major[dev] = major;
+      g_smem_optin[dev] = optin;
+    }
+    if (g_major[dev] != 10) return report(error, error_size, "needs an sm_100 (B200-class) GPU");
+    if (gemv_smem > size_t(g_smem_optin[dev]) || router_smem > size_t(g_smem_optin[dev]))
+      return report(error, error_size, "H is too large for the decode kernels' shared-memory staging");
   }
-  if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess || prop.major != 10)
-    return report(error, error_size, "needs an sm_100 (B200-class) GPU");
-  if (gemv_smem > size_t(prop.sharedMemPerBlockOptin) || router_smem > size_t(prop.sharedMemPerBlockOptin))
-    return report(error, error_size, "H is too large for the decode kernels' shared-memory staging");
-  gemv_init_attributes(int(gemv_smem));
+  gemv_init_attributes(int(gemv_smem));  // raise-only, cheap after the first call
   router_init_attributes(int(H));
 
   uint8_t* base = static_cast<uint8_t*>(g_scratch_ptr[dev]);

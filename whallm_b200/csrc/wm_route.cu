@@ -9,6 +9,7 @@
 // Selection ties go to the lower expert index (DeepSeekNative/engine.mm:1880);
 // the reference's argpartition leaves tie order unspecified.
 #include <algorithm>
+#include <mutex>
 
 #include "wm_kernels.h"
 
@@ -474,7 +475,15 @@ bool router_logits_fused_ok(int T, int H, int E) { return H % (64 * kRouterWarps
 
 size_t router_smem_bytes(int H) { return size_t(8) * H * 2; }
 
+// Only ever raises the current device's limit (see gemv_init_attributes).
 void router_init_attributes(int max_hidden) {
+  static std::mutex mu;
+  static int set_to[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return;
+  std::lock_guard<std::mutex> lock(mu);
+  if (max_hidden <= set_to[dev]) return;
+  set_to[dev] = max_hidden;
   cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        int(router_smem_bytes(max_hidden)));
 }
