@@ -265,10 +265,17 @@ def run_ep(args, world: int, rank: int, local: int) -> None:
     eng = Engine(local, max_tokens=cap, hidden=H, inter=I, experts=E, topk=K, gemv_max_tokens=cap,
                  flags=lib.FLAG_SKIP_NEGATIVE_ROUTES)
     shared_eng = Engine(local, max_tokens=B, hidden=H, inter=I, experts=1, topk=1, gemv_max_tokens=B)
-    # fixed-size exchanges (B * K slots per peer): no host round trip, so a
-    # whole step is one CUDA graph (router, plan, 3 all-to-alls, experts,
-    # shared expert on a side stream, combine)
-    ep = ExpertParallelMoE(eng, layer, K, shared_engine=shared_eng, fixed_capacity=B)
+    # fixed-capacity exchanges (B * K slots per peer): no host round trip, so a
+    # whole step is one CUDA graph (router, plan, the exchanges, experts,
+    # shared expert on a side stream, combine); over NVLink peer memory by
+    # default, NCCL all-to-all with --exchange nccl or when peer mapping fails
+    exchange = args.exchange
+    try:
+        ep = ExpertParallelMoE(eng, layer, K, shared_engine=shared_eng, fixed_capacity=B,
+                               peer_memory=exchange == "peer")
+    except RuntimeError:  # every rank sees the same failure: all fall back together
+        exchange = "nccl"
+        ep = ExpertParallelMoE(eng, layer, K, shared_engine=shared_eng, fixed_capacity=B)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.Stream(device=dev)
     x_static = xs[0].clone()
@@ -370,6 +377,7 @@ def run_ep(args, world: int, rank: int, local: int) -> None:
     e_ms = float(t.item())
     e2e = world * B * args.steps / (e_ms / 1e3)
     del graph  # holds NCCL work: release before the process group goes
+    ep.close()
     dist.barrier()
     dist.destroy_process_group()
     if rank != 0:
@@ -385,8 +393,10 @@ def run_ep(args, world: int, rank: int, local: int) -> None:
                    "timing": ("CUDA graph replay per step" if graph_error is None else "eager steps")
                    + ", device events, max over ranks",
                    "graph_error": graph_error,
-                   "parallelism": f"expert-parallel x{world} ({E // world} experts per GPU), NCCL all-to-all",
-                   "exchange": f"fixed {B * K} slots per peer each way",
+                   "parallelism": f"expert-parallel x{world} ({E // world} experts per GPU)",
+                   "exchange": (f"NVLink peer-memory stores of the real pairs ({B * K} slots per peer), "
+                                "device flags" if exchange == "peer"
+                                else f"NCCL all-to-all, fixed {B * K} slots per peer each way"),
                    "wall_ms_per_step_rank0": statistics.median(t_host)},
         "roofline": None,
         "kernels": kernels,
@@ -618,6 +628,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-long", action="store_true", help="skip the config-3 and config-4 long-call sections")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="N > 1: expert-parallel exchanges over peer memory (default) or NCCL all-to-all")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -243,6 +243,41 @@ WM_EXPORT int wm_ep_plan(wm_ctx* ctx, int64_t T, int32_t K, int32_t experts_per_
                          int32_t capacity, const int32_t* idx, const void* x, int32_t H, int32_t* send_counts,
                          int32_t* pair_pos, int32_t* send_eid, void* send_x, void* stream);
 
+/* Expert-parallel exchanges over NVLink peer memory, without a collective
+   library: one process per GPU, `world` <= 8 ranks on distinct GPUs of one
+   box.  wm_ep_create reserves this rank's exchange buffer (recv_x bf16
+   [world * capacity, H], recv_e int32 [world * capacity], back bf16
+   [world * capacity, H], flags); each rank passes wm_ep_ipc_handle's 64 bytes
+   to every peer (e.g. an all-gather), which maps it with wm_ep_open_peer.
+   One layer step, every rank in the same order:
+     wm_ep_dispatch   routes idx int32 [T, K] (T * K <= capacity) of x bf16
+                      [T, H]: each pair's row and owner-local expert id go
+                      straight into its owner's recv block for this rank;
+                      pair_pos int32 [T, K] receives each pair's slot
+                      (owner * capacity + j) in `back`;
+     wm_ep_wait(0)    until every peer's rows have arrived;
+     wm_expert_pairs  on recv_x / recv_e (WM_FLAG_SKIP_NEGATIVE_ROUTES handle),
+                      giving y bf16 [world * capacity, H];
+     wm_ep_return     each valid row of y back to the rank that sent it;
+     wm_ep_wait(1)    until every peer's rows are back; then wm_combine reads
+                      `back` at pair_pos.
+   Waits are bounded (2 s, then a timeout in wm_sync's status); the step
+   number lives on the device, so the sequence can be captured in a CUDA
+   graph.  Destroy only after every peer has finished its last step.  No
+   counterpart in the reference, whose experts run on one device. */
+typedef struct wm_ep wm_ep;
+WM_EXPORT wm_ep* wm_ep_create(int32_t device, int32_t world, int32_t rank, int64_t capacity, int32_t H, char* error,
+                              size_t error_size);
+WM_EXPORT void wm_ep_destroy(wm_ep* ep);
+WM_EXPORT int wm_ep_ipc_handle(wm_ep* ep, void* handle64);
+WM_EXPORT int wm_ep_open_peer(wm_ep* ep, int32_t peer, const void* handle64);
+/* 0: recv_x, 1: recv_e, 2: back (device pointers into this rank's buffer) */
+WM_EXPORT void* wm_ep_buffer(wm_ep* ep, int32_t which);
+WM_EXPORT int wm_ep_dispatch(wm_ctx* ctx, wm_ep* ep, int64_t T, int32_t K, int32_t experts_per_rank,
+                             const int32_t* idx, const void* x, int32_t* pair_pos, void* stream);
+WM_EXPORT int wm_ep_return(wm_ctx* ctx, wm_ep* ep, const void* y, void* stream);
+WM_EXPORT int wm_ep_wait(wm_ctx* ctx, wm_ep* ep, int32_t which, void* stream);
+
 /* The whole MoE block: route, sort, experts, shared expert, combine
    (SparseMoE.__call__, qwen4_exp.py:1015-1051; _streaming_moe, model.py:526-546;
    MoE.__call__, deepseek_v41/moe.py:105-112). */

@@ -37,21 +37,29 @@ def _shared_engine(dev: int) -> Engine:
     return Engine(dev, max_tokens=B, hidden=H, inter=I, experts=1, topk=1, gemv_max_tokens=B)
 
 
-@pytest.mark.parametrize("fixed", [0, B])
-def test_ep_one_rank_equals_forward(fixed):
+MODES = {"exact": (0, False), "fixed": (B, False), "peer": (B, True)}
+
+
+@pytest.mark.parametrize("mode", list(MODES))
+def test_ep_one_rank_equals_forward(mode):
+    fixed, peer = MODES[mode]
     from whallm_b200.ep import ExpertParallelMoE
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{_free_port()}", rank=0, world_size=1,
                             device_id=torch.device("cuda", 0))
     try:
         wl = synth.config(1, device="cuda", batch=B)
         eng = _engine(0, 1)
-        ep = ExpertParallelMoE(eng, wl.layer, K, shared_engine=_shared_engine(0), fixed_capacity=fixed)
+        ep = ExpertParallelMoE(eng, wl.layer, K, shared_engine=_shared_engine(0), fixed_capacity=fixed,
+                               peer_memory=peer)
         got = ep(wl.x)
+        got2 = ep(wl.x)  # a second step: the exchange flags move on to the next step number
         want, (w, idx) = eng.forward(wl.layer, wl.x, K, return_routes=True)
         eng.sync()
         if not fixed:
             assert ep.stats.sent == B * K and ep.stats.received == B * K
         assert torch.equal(got, want), "expert-parallel layer (one rank) differs from the single-GPU layer"
+        assert torch.equal(got2, want)
+        ep.close()
         tokens = np.arange(8, dtype=np.int32)
         layer_np = adapter.from_layer(wl.layer)
         ref = layer_np.forward(adapter.bits(wl.x), idx.cpu().numpy(), w.cpu().numpy(), tokens=tokens)
@@ -61,7 +69,8 @@ def test_ep_one_rank_equals_forward(fixed):
         dist.destroy_process_group()
 
 
-def _worker(rank: int, world: int, port: int, fixed: int, q) -> None:
+def _worker(rank: int, world: int, port: int, mode: str, q) -> None:
+    fixed, peer = MODES[mode]
     from whallm_b200.ep import ExpertParallelMoE
     torch.cuda.set_device(rank)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -73,21 +82,26 @@ def _worker(rank: int, world: int, port: int, fixed: int, q) -> None:
         wl = synth.config(1, device=dev, batch=B)
         x = synth.activations(B, H, torch.Generator(device=dev).manual_seed(77 + rank), dev)
         eng = _engine(rank, world)
-        got = ExpertParallelMoE(eng, wl.layer, K, shared_engine=_shared_engine(rank), fixed_capacity=fixed)(x)
+        ep = ExpertParallelMoE(eng, wl.layer, K, shared_engine=_shared_engine(rank), fixed_capacity=fixed,
+                               peer_memory=peer)
+        got = ep(x)
+        got2 = ep(x)
         want = eng.forward(wl.layer, x, K)
         eng.sync()
-        q.put((rank, bool(torch.equal(got, want)), float((got.float() - want.float()).abs().max())))
+        ep.close()
+        ok = bool(torch.equal(got, want)) and bool(torch.equal(got2, want))
+        q.put((rank, ok, float((got.float() - want.float()).abs().max())))
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("fixed", [0, B])
-def test_ep_two_ranks_equal_single_gpu(fixed):
+@pytest.mark.parametrize("mode", list(MODES))
+def test_ep_two_ranks_equal_single_gpu(mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, fixed, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
     for p in procs:
         p.start()
     res = sorted(q.get(timeout=300) for _ in range(2))

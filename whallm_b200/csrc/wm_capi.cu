@@ -819,6 +819,208 @@ WM_EXPORT int wm_ep_plan(wm_ctx* ctx, int64_t T, int32_t K, int32_t experts_per_
   return check_launch(ctx, "expert-parallel plan");
 }
 
+// ---------------------------------------------------------------- expert parallelism over peer memory
+
+struct wm_ep {
+  int device = 0, world = 0, rank = 0, H = 0;
+  int64_t capacity = 0;
+  void* base = nullptr;  // this rank's exchange buffer (one cudaMalloc, exported through IPC)
+  size_t bytes = 0;
+  uint8_t* peer[wm::kMaxEpRanks] = {};  // every rank's buffer in this address space (own one included)
+  size_t o_recv_x = 0, o_recv_e = 0, o_back = 0, o_flags = 0, o_ticket = 0, o_epoch = 0;
+};
+
+namespace {
+
+bool ep_ready(const wm_ep* ep) {
+  for (int r = 0; r < ep->world; ++r)
+    if (ep->peer[r] == nullptr) return false;
+  return true;
+}
+
+// The blocks this rank writes in every rank's buffer for exchange `which`
+// (0: rows and ids to the owners' recv blocks, 1: results to the senders' back blocks).
+wm::EpPeers ep_peers(const wm_ep* ep, int which) {
+  wm::EpPeers pe{};
+  const int64_t blk = int64_t(ep->rank) * ep->capacity;
+  for (int r = 0; r < ep->world; ++r) {
+    uint8_t* b = ep->peer[r];
+    pe.rows[r] = reinterpret_cast<uint16_t*>(b + (which == 0 ? ep->o_recv_x : ep->o_back)) + blk * ep->H;
+    pe.ids[r] = reinterpret_cast<int32_t*>(b + ep->o_recv_e) + blk;
+    pe.flag[r] = reinterpret_cast<uint32_t*>(b + ep->o_flags) + which * ep->world + ep->rank;
+  }
+  uint8_t* own = static_cast<uint8_t*>(ep->base);
+  pe.ticket = reinterpret_cast<uint32_t*>(own + ep->o_ticket) + which;
+  pe.epoch = reinterpret_cast<const uint32_t*>(own + ep->o_epoch);
+  return pe;
+}
+
+}  // namespace
+
+WM_EXPORT wm_ep* wm_ep_create(int32_t device, int32_t world, int32_t rank, int64_t capacity, int32_t H, char* error,
+                              size_t error_size) {
+  auto report = [&](const char* msg) {
+    if (error != nullptr && error_size > 0) snprintf(error, error_size, "%s", msg);
+  };
+  if (world < 1 || world > wm::kMaxEpRanks || rank < 0 || rank >= world) {
+    report("world must be in [1, 8] and rank in [0, world)");
+    return nullptr;
+  }
+  if (capacity <= 0 || H <= 0 || H % 8) {
+    report("capacity must be positive and H a positive multiple of 8");
+    return nullptr;
+  }
+  wm_ep* ep = new (std::nothrow) wm_ep();
+  if (ep == nullptr) {
+    report("out of host memory");
+    return nullptr;
+  }
+  ep->device = device;
+  ep->world = world;
+  ep->rank = rank;
+  ep->capacity = capacity;
+  ep->H = H;
+  const size_t slots = size_t(world) * size_t(capacity);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = align_up(off + bytes, 256);
+    return at;
+  };
+  ep->o_recv_x = take(slots * H * 2);
+  ep->o_recv_e = take(slots * 4);
+  ep->o_back = take(slots * H * 2);
+  ep->o_flags = take(size_t(2 * world) * 4);
+  ep->o_ticket = take(8);
+  ep->o_epoch = take(4);
+  ep->bytes = off;
+  DeviceGuard guard(device);
+  if (cudaMalloc(&ep->base, ep->bytes) != cudaSuccess) {
+    cudaGetLastError();
+    report("cudaMalloc of the exchange buffer failed");
+    delete ep;
+    return nullptr;
+  }
+  uint8_t* b = static_cast<uint8_t*>(ep->base);
+  if (cudaMemset(b + ep->o_flags, 0, off - ep->o_flags) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+    report("initialising the exchange buffer failed");
+    cudaFree(ep->base);
+    delete ep;
+    return nullptr;
+  }
+  ep->peer[rank] = b;
+  return ep;
+}
+
+WM_EXPORT void wm_ep_destroy(wm_ep* ep) {
+  if (ep == nullptr) return;
+  {
+    DeviceGuard guard(ep->device);
+    for (int r = 0; r < ep->world; ++r)
+      if (r != ep->rank && ep->peer[r] != nullptr) cudaIpcCloseMemHandle(ep->peer[r]);
+    cudaFree(ep->base);
+  }
+  delete ep;
+}
+
+WM_EXPORT int wm_ep_ipc_handle(wm_ep* ep, void* handle64) {
+  if (ep == nullptr || handle64 == nullptr) return WM_ERROR;
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handles are 64 bytes");
+  DeviceGuard guard(ep->device);
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, ep->base) != cudaSuccess) {
+    cudaGetLastError();
+    return WM_ERROR;
+  }
+  memcpy(handle64, &h, sizeof(h));
+  return WM_OK;
+}
+
+WM_EXPORT int wm_ep_open_peer(wm_ep* ep, int32_t peer, const void* handle64) {
+  if (ep == nullptr || handle64 == nullptr || peer < 0 || peer >= ep->world || peer == ep->rank) return WM_ERROR;
+  if (ep->peer[peer] != nullptr) return WM_OK;
+  DeviceGuard guard(ep->device);
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    cudaGetLastError();
+    return WM_ERROR;
+  }
+  ep->peer[peer] = static_cast<uint8_t*>(p);
+  return WM_OK;
+}
+
+WM_EXPORT void* wm_ep_buffer(wm_ep* ep, int32_t which) {
+  if (ep == nullptr) return nullptr;
+  uint8_t* b = static_cast<uint8_t*>(ep->base);
+  switch (which) {
+    case 0: return b + ep->o_recv_x;
+    case 1: return b + ep->o_recv_e;
+    case 2: return b + ep->o_back;
+    default: return nullptr;
+  }
+}
+
+WM_EXPORT int wm_ep_dispatch(wm_ctx* ctx, wm_ep* ep, int64_t T, int32_t K, int32_t experts_per_rank,
+                             const int32_t* idx, const void* x, int32_t* pair_pos, void* stream) {
+  if (ctx == nullptr) return WM_ERROR;
+  if (ep == nullptr || !ep_ready(ep)) return fail(ctx, "the exchange buffer has unopened peers");
+  if (ep->device != ctx->device) return fail(ctx, "the exchange buffer lives on another device");
+  if (T < 0 || T > ctx->opt.max_tokens) return fail(ctx, "T out of range for this handle");
+  if (K <= 0 || K > ctx->opt.max_topk || experts_per_rank <= 0) return fail(ctx, "K or experts_per_rank out of range");
+  if (T * K > ep->capacity) return fail(ctx, "T * K = %lld exceeds the exchange capacity %lld", (long long)(T * K),
+                                        (long long)ep->capacity);
+  if (ep->world > ctx->opt.max_experts) return fail(ctx, "world exceeds the handle's max_experts");
+  if (idx == nullptr || x == nullptr || pair_pos == nullptr || !aligned(x, 16))
+    return fail(ctx, "wm_ep_dispatch needs device idx, pair_pos and 16-byte aligned x");
+  DeviceGuard guard(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* own = static_cast<uint8_t*>(ep->base);
+  wm::launch_ep_begin(reinterpret_cast<uint32_t*>(own + ep->o_epoch), s);
+  const int P = int(T) * K;
+  int launches = 0;
+  wm::Plan plan = ctx->plan;
+  plan.rowmax = nullptr;
+  if (P > 0) {
+    wm::launch_ep_owner(idx, P, experts_per_rank, ep->world, ctx->idx, ctx->status, ctx->num_sms, s);
+    wm::launch_plan(ctx->idx, int(T), K, ep->world, false, 1, plan, ctx->max_rows, ctx->max_mtiles, ctx->max_chunks,
+                    ctx->status, s, &launches);
+    launches += 1;
+  } else {
+    cudaMemsetAsync(plan.counts, 0, sizeof(int32_t) * (ep->world + 1), s);  // every block is padding
+  }
+  wm::launch_ep_send(idx, plan, int(T), K, experts_per_rank, ep->world, int(ep->capacity), pair_pos,
+                     static_cast<const uint16_t*>(x), ep->H, ep_peers(ep, 0), ctx->num_sms, s);
+  ctx->counters.launches += launches + 2;
+  return check_launch(ctx, "expert-parallel dispatch");
+}
+
+WM_EXPORT int wm_ep_return(wm_ctx* ctx, wm_ep* ep, const void* y, void* stream) {
+  if (ctx == nullptr) return WM_ERROR;
+  if (ep == nullptr || !ep_ready(ep)) return fail(ctx, "the exchange buffer has unopened peers");
+  if (y == nullptr || !aligned(y, 16)) return fail(ctx, "y must be a 16-byte aligned device pointer");
+  DeviceGuard guard(ctx->device);
+  const uint8_t* own = static_cast<const uint8_t*>(ep->base);
+  wm::launch_ep_return(static_cast<const uint16_t*>(y), reinterpret_cast<const int32_t*>(own + ep->o_recv_e),
+                       ep->world, int(ep->capacity), ep->H, ep_peers(ep, 1), ctx->num_sms,
+                       static_cast<cudaStream_t>(stream));
+  ctx->counters.launches += 1;
+  return check_launch(ctx, "expert-parallel return");
+}
+
+WM_EXPORT int wm_ep_wait(wm_ctx* ctx, wm_ep* ep, int32_t which, void* stream) {
+  if (ctx == nullptr) return WM_ERROR;
+  if (ep == nullptr || which < 0 || which > 1) return fail(ctx, "wm_ep_wait: bad buffer or exchange");
+  DeviceGuard guard(ctx->device);
+  const uint8_t* own = static_cast<const uint8_t*>(ep->base);
+  wm::launch_ep_wait(reinterpret_cast<const uint32_t*>(own + ep->o_flags) + which * ep->world, ep->world,
+                     reinterpret_cast<const uint32_t*>(own + ep->o_epoch), ctx->status, 60 + which,
+                     static_cast<cudaStream_t>(stream));
+  ctx->counters.launches += 1;
+  return check_launch(ctx, "expert-parallel wait");
+}
+
 WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* args, void* stream) {
   if (ctx == nullptr) return WM_ERROR;
   if (int rc = validate_experts(ctx, args, true)) return rc;

@@ -1,0 +1,146 @@
+// Expert-parallel exchanges over NVLink peer memory (no collective library).
+//
+// Every rank owns one exchange buffer (recv_x, recv_e, back, flags), mapped
+// into its peers' address spaces through CUDA IPC.  One layer step:
+//
+//   dispatch  ep_send_kernel stores each (token, k) pair's x row and
+//             owner-local expert id straight into the owner's recv block for
+//             this rank (slot rank * capacity + j), marks the block's unused
+//             slots with id -1, and -- after every CTA's stores are fenced at
+//             system scope -- the last CTA raises this rank's dispatch flag on
+//             every peer to the step number;
+//   wait      ep_wait_kernel: one lane per peer polls the local flag (bounded:
+//             after 2 s it records a timeout in the status word and returns);
+//   experts   the owner runs its experts on recv_x (padding ids skipped);
+//   return    ep_return_kernel stores each valid result row into the source
+//             rank's `back` buffer at the slot the pair was sent from, then
+//             raises the return flags the same way; after a wait the source
+//             rank combines, reading pair (t, k) at its slot.
+//
+// Only real pairs cross NVLink (the fixed-capacity all-to-all of the
+// collective path moves every padded slot), and nothing waits on the host,
+// so a step can be captured in one CUDA graph.  The step number lives on the
+// device (ep_begin_kernel increments it), so graph replays signal fresh
+// values.  The reference runs its experts on one device; this is the
+// B200-native counterpart of the expert-parallel plan, not a port.
+#include "wm_kernels.h"
+
+namespace wm {
+
+namespace {
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// After this CTA's stores to peer memory: fence them at system scope, take a
+// ticket, and let the last CTA of the grid raise the flags (one per peer) to
+// the step number and reset the ticket for the next exchange.
+__device__ __forceinline__ void signal_peers(const EpPeers& pe, int world) {
+  __shared__ int last;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(pe.ticket, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence_system();
+  const uint32_t step = *pe.epoch;
+  if (threadIdx.x < world) st_release_sys(pe.flag[threadIdx.x], step);
+  if (threadIdx.x == 0) *pe.ticket = 0u;
+}
+
+}  // namespace
+
+__global__ void ep_begin_kernel(uint32_t* epoch) { epoch[0] += 1u; }
+
+// Dispatch of the pairs after the plan over owners (as ep_finish_kernel with a
+// capacity, but into the owners' buffers).
+__global__ void __launch_bounds__(256) ep_send_kernel(const int32_t* __restrict__ idx, Plan p, int T, int K,
+                                                      int per_rank, int world, int capacity,
+                                                      int32_t* __restrict__ pair_pos, const uint16_t* __restrict__ x,
+                                                      int H, const EpPeers pe) {
+  const int P = T * K;
+  const int gtid = blockIdx.x * blockDim.x + threadIdx.x, nthreads = gridDim.x * blockDim.x;
+  for (int i = gtid; i < world * capacity; i += nthreads) {
+    const int r = i / capacity, j = i - r * capacity;
+    if (j >= p.counts[r]) pe.ids[r][j] = -1;
+  }
+  for (int i = gtid; i < P; i += nthreads) {
+    const int pos = p.pair_pos[i];
+    if (pos < 0) {
+      pair_pos[i] = -1;
+      continue;
+    }
+    const int e = idx[i], r = e / per_rank, j = pos - p.offsets[r];
+    pair_pos[i] = r * capacity + j;
+    pe.ids[r][j] = e - r * per_rank;
+  }
+  const int lane = threadIdx.x & 31, warps = nthreads >> 5;
+  for (int i = gtid >> 5; i < P; i += warps) {
+    const int pos = p.pair_pos[i];
+    if (pos < 0) continue;
+    const int r = idx[i] / per_rank;
+    const uint4* src = reinterpret_cast<const uint4*>(x + int64_t(i / K) * H);
+    uint4* dst = reinterpret_cast<uint4*>(pe.rows[r] + int64_t(pos - p.offsets[r]) * H);
+    for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
+  }
+  signal_peers(pe, world);
+}
+
+// Result rows back to the ranks that sent the pairs: slot s of recv block r
+// (valid when its expert id is >= 0) goes to slot j of rank r's back block
+// for this rank.
+__global__ void __launch_bounds__(256) ep_return_kernel(const uint16_t* __restrict__ y,
+                                                        const int32_t* __restrict__ recv_e, int world, int capacity,
+                                                        int H, const EpPeers pe) {
+  const int lane = threadIdx.x & 31, warps = gridDim.x * blockDim.x >> 5;
+  for (int s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; s < world * capacity; s += warps) {
+    if (recv_e[s] < 0) continue;
+    const int r = s / capacity, j = s - r * capacity;
+    const uint4* src = reinterpret_cast<const uint4*>(y + int64_t(s) * H);
+    uint4* dst = reinterpret_cast<uint4*>(pe.rows[r] + int64_t(j) * H);
+    for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
+  }
+  signal_peers(pe, world);
+}
+
+// Bounded wait until every peer's flag has reached this step.
+__global__ void ep_wait_kernel(const uint32_t* flags, int world, const uint32_t* epoch, uint32_t* status, int code) {
+  const int r = threadIdx.x;
+  if (r >= world) return;
+  const uint32_t step = *epoch;
+  const uint64_t start = global_timer_ns();
+  for (uint32_t spin = 0; ld_acquire_sys(flags + r) < step; ++spin) {
+    __nanosleep(64);
+    if ((spin & 63u) == 63u && global_timer_ns() - start > 2000000000ull) {
+      report_status(status, kStatusWaitTimeout, uint32_t(code * 16 + r));
+      return;
+    }
+  }
+}
+
+void launch_ep_begin(uint32_t* epoch, cudaStream_t stream) { ep_begin_kernel<<<1, 1, 0, stream>>>(epoch); }
+
+void launch_ep_send(const int32_t* idx, const Plan& p, int T, int K, int per_rank, int world, int capacity,
+                    int32_t* pair_pos, const uint16_t* x, int H, const EpPeers& pe, int num_sms,
+                    cudaStream_t stream) {
+  ep_send_kernel<<<num_sms, 256, 0, stream>>>(idx, p, T, K, per_rank, world, capacity, pair_pos, x, H, pe);
+}
+
+void launch_ep_return(const uint16_t* y, const int32_t* recv_e, int world, int capacity, int H, const EpPeers& pe,
+                      int num_sms, cudaStream_t stream) {
+  ep_return_kernel<<<num_sms, 256, 0, stream>>>(y, recv_e, world, capacity, H, pe);
+}
+
+void launch_ep_wait(const uint32_t* flags, int world, const uint32_t* epoch, uint32_t* status, int code,
+                    cudaStream_t stream) {
+  ep_wait_kernel<<<1, 32, 0, stream>>>(flags, world, epoch, status, code);
+}
+
+}  // namespace wm

@@ -89,6 +89,24 @@ void launch_ep_owner(const int32_t* idx, int P, int per_rank, int world, int32_t
 void launch_ep_finish(const int32_t* idx, const Plan& p, int T, int K, int per_rank, int world, int capacity,
                       int32_t* send_counts, int32_t* pair_pos, int32_t* send_eid, const uint16_t* x, int H,
                       uint16_t* send_x, int num_sms, cudaStream_t stream);
+// ---- expert-parallel exchanges over peer memory (wm_ep_p2p.cu)
+constexpr int kMaxEpRanks = 8;
+// The blocks this rank writes in every rank's exchange buffer (peer r's
+// address space mapped here), and this rank's own step state.
+struct EpPeers {
+  uint16_t* rows[kMaxEpRanks];  // rank r's recv_x (dispatch) or back (return) block for this rank
+  int32_t* ids[kMaxEpRanks];    // rank r's recv_e block for this rank (dispatch)
+  uint32_t* flag[kMaxEpRanks];  // rank r's flag for this rank
+  uint32_t* ticket;             // local: CTAs done with this exchange
+  const uint32_t* epoch;        // local: step number
+};
+void launch_ep_begin(uint32_t* epoch, cudaStream_t stream);
+void launch_ep_send(const int32_t* idx, const Plan& p, int T, int K, int per_rank, int world, int capacity,
+                    int32_t* pair_pos, const uint16_t* x, int H, const EpPeers& pe, int num_sms, cudaStream_t stream);
+void launch_ep_return(const uint16_t* y, const int32_t* recv_e, int world, int capacity, int H, const EpPeers& pe,
+                      int num_sms, cudaStream_t stream);
+void launch_ep_wait(const uint32_t* flags, int world, const uint32_t* epoch, uint32_t* status, int code,
+                    cudaStream_t stream);
 void launch_unpermute(const uint16_t* routed, const Plan& p, int TK, int H, uint16_t* out, int num_sms,
                       cudaStream_t stream);
 

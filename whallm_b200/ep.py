@@ -25,6 +25,13 @@ whenever both take the same expert kernels (the exchanges only move rows).
 The reference runs its experts on one device; this module is the
 B200-native counterpart of the survey's expert-parallel plan, not a port.
 
+With `peer_memory=True` (fixed capacity, one GPU per rank, at most 8) the
+three exchanges of steps 2-5 run without the collective library: every rank
+stores its pairs' rows and ids straight into the owners' exchange buffers over
+NVLink, the owners store the result rows straight back, and bounded device
+waits on per-rank flags replace the all-to-alls (include/whallm_moe.h,
+wm_ep_*).  Only real pairs cross NVLink.
+
 The engine is anything with route / ep_plan / expert_pairs / combine of
 whallm_b200.moe.Engine's signatures, so the exchange logic can be tested with
 CPU stand-ins on gloo.
@@ -62,7 +69,7 @@ class ExpertParallelMoE:
     with lib.FLAG_SKIP_NEGATIVE_ROUTES and room for W * M * K rows."""
 
     def __init__(self, engine, layer: LayerWeights, top_k: int, group=None, shared_engine=None,
-                 fixed_capacity: int = 0):
+                 fixed_capacity: int = 0, peer_memory: bool = False):
         if not dist.is_initialized():
             raise RuntimeError("torch.distributed is not initialised")
         self.engine, self.layer, self.K, self.group = engine, layer, top_k, group
@@ -80,6 +87,53 @@ class ExpertParallelMoE:
         self.fixed = fixed_capacity
         self.stats = EPStats()
         self._side = None
+        self.ep_buf = self._open_exchange() if peer_memory else None
+
+    def _open_exchange(self) -> lib.EpBuffer:
+        """This rank's exchange buffer, mapped into every peer (all ranks call this together)."""
+        if not self.fixed:
+            raise ValueError("peer-memory exchanges need a fixed capacity")
+        if self.world > 8:
+            raise ValueError("peer-memory exchanges support at most 8 ranks")
+        dev = self.engine.device
+        ids = [None] * self.world
+        dist.all_gather_object(ids, str(torch.cuda.get_device_properties(dev).uuid), group=self.group)
+        if len(set(ids)) != self.world:
+            raise ValueError("peer-memory exchanges need every rank on its own GPU")
+        # every rank takes part in every collective below, whatever fails locally,
+        # and all of them agree on the outcome
+        buf, handle, error = None, b"", ""
+        try:
+            buf = lib.EpBuffer(dev.index or 0, self.world, self.rank, self.fixed * self.K, self.layer.H)
+            handle = buf.ipc_handle()
+        except lib.WMError as exc:
+            error = str(exc)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=self.group)
+        if not error:
+            try:
+                for r, h in enumerate(handles):
+                    if r != self.rank:
+                        if not h:
+                            raise lib.WMError(f"rank {r} has no exchange buffer")
+                        buf.open_peer(r, h)
+            except lib.WMError as exc:
+                error = str(exc)
+        errors = [None] * self.world
+        dist.all_gather_object(errors, error, group=self.group)
+        if any(errors):
+            if buf is not None:
+                buf.close()
+            raise RuntimeError("peer-memory exchange unavailable: " + "; ".join(e for e in errors if e))
+        return buf
+
+    def close(self) -> None:
+        """Release the exchange buffer once every rank has finished (collective)."""
+        if self.ep_buf is not None:
+            torch.cuda.synchronize(self.engine.device)
+            dist.barrier(group=self.group)
+            self.ep_buf.close()
+            self.ep_buf = None
 
     def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits: list[int], in_splits: list[int]) -> None:
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
@@ -102,7 +156,9 @@ class ExpertParallelMoE:
             with torch.cuda.stream(side):
                 shared_rows = self._shared_rows(self.shared_engine, x)
 
-        if self.fixed:
+        if self.ep_buf is not None:
+            back, pair_pos = self._exchange_peer(x, idx)
+        elif self.fixed:
             back, pair_pos = self._exchange_fixed(x, idx)
         else:
             back, pair_pos = self._exchange_exact(x, idx)
@@ -116,7 +172,27 @@ class ExpertParallelMoE:
             else:
                 shared_rows = self._shared_rows(self.engine, x)
             gate, gate_w = self.layer.shared.gate, self.layer.shared.gate_weight
+        if isinstance(back, int):  # rows in the exchange buffer
+            return self.engine.combine_at(back, w, shared_rows, gate, x, gate_w, pair_pos)
         return self.engine.combine(back, w, shared_rows, gate, x, gate_w, pair_pos=pair_pos)
+
+    def _exchange_peer(self, x: torch.Tensor, idx: torch.Tensor):
+        """Exchanges through the ranks' buffers over NVLink (no collective)."""
+        T, H = x.shape
+        if T > self.fixed:
+            raise ValueError(f"{T} tokens exceed the fixed capacity of {self.fixed} per rank")
+        W, El, C = self.world, self.E_local, self.fixed * self.K
+        ctx, buf, stream = self.engine.ctx, self.ep_buf, torch.cuda.current_stream(x.device).cuda_stream
+        idx = idx.to(torch.int32).contiguous()
+        pair_pos = torch.empty((T, self.K), dtype=torch.int32, device=x.device)
+        ctx.ep_dispatch(buf, T, self.K, El, idx.data_ptr(), x.data_ptr(), pair_pos.data_ptr(), stream)
+        ctx.ep_wait(buf, 0, stream)
+        y = torch.empty((W * C, H), dtype=x.dtype, device=x.device)
+        self.engine.expert_pairs_at(self.local, W * C, buf.buffer(0), buf.buffer(1), y)
+        ctx.ep_return(buf, y.data_ptr(), stream)
+        ctx.ep_wait(buf, 1, stream)
+        self.stats = EPStats(sent=-1, received=-1)
+        return buf.buffer(2), pair_pos  # the result rows, in this rank's buffer
 
     def _exchange_fixed(self, x: torch.Tensor, idx: torch.Tensor):
         """Fixed-size exchanges: W * T * K slots each way, padding skipped."""

@@ -28,6 +28,8 @@ EXPORTS = (
     "wm_dequant", "wm_route", "wm_expert_pairs", "wm_combine", "wm_ep_plan", "wm_moe_forward",
     "wm_profile_enable", "wm_profile_read", "wm_profile_reset",
     "wm_moe_forward_noalloc",
+    "wm_ep_create", "wm_ep_destroy", "wm_ep_ipc_handle", "wm_ep_open_peer", "wm_ep_buffer",
+    "wm_ep_dispatch", "wm_ep_return", "wm_ep_wait",
 )
 
 _P = ctypes.c_void_p
@@ -111,8 +113,20 @@ def load() -> ctypes.CDLL:
     L.wm_profile_reset.restype = None
     L.wm_moe_forward_noalloc.argtypes = [ctypes.POINTER(MoeArgs), _P, ctypes.c_char_p, ctypes.c_size_t]
     L.wm_moe_forward_noalloc.restype = ctypes.c_int
+    L.wm_ep_create.argtypes = [_I32, _I32, _I32, _I64, _I32, ctypes.c_char_p, ctypes.c_size_t]
+    L.wm_ep_create.restype = _P
+    L.wm_ep_destroy.argtypes = [_P]
+    L.wm_ep_destroy.restype = None
+    L.wm_ep_ipc_handle.argtypes = [_P, _P]
+    L.wm_ep_open_peer.argtypes = [_P, _I32, _P]
+    L.wm_ep_buffer.argtypes = [_P, _I32]
+    L.wm_ep_buffer.restype = _P
+    L.wm_ep_dispatch.argtypes = [_P, _P, _I64, _I32, _I32, _P, _P, _P, _P]
+    L.wm_ep_return.argtypes = [_P, _P, _P, _P]
+    L.wm_ep_wait.argtypes = [_P, _P, _I32, _P]
     for name in ("wm_sync", "wm_dequant", "wm_route", "wm_expert_pairs", "wm_combine", "wm_ep_plan",
-                 "wm_moe_forward"):
+                 "wm_moe_forward", "wm_ep_ipc_handle", "wm_ep_open_peer", "wm_ep_dispatch", "wm_ep_return",
+                 "wm_ep_wait"):
         getattr(L, name).restype = ctypes.c_int
     _lib = L
     return L
@@ -197,3 +211,54 @@ class Context:
 
     def moe_forward(self, args: MoeArgs, stream: int | None) -> None:
         self.check(self._lib.wm_moe_forward(self.handle, ctypes.byref(args), stream))
+
+    def ep_dispatch(self, ep: "EpBuffer", T: int, K: int, per_rank: int, idx: int, x: int, pair_pos: int,
+                    stream: int | None) -> None:
+        self.check(self._lib.wm_ep_dispatch(self.handle, ep.handle, T, K, per_rank, idx, x, pair_pos, stream))
+
+    def ep_return(self, ep: "EpBuffer", y: int, stream: int | None) -> None:
+        self.check(self._lib.wm_ep_return(self.handle, ep.handle, y, stream))
+
+    def ep_wait(self, ep: "EpBuffer", which: int, stream: int | None) -> None:
+        self.check(self._lib.wm_ep_wait(self.handle, ep.handle, which, stream))
+
+
+class EpBuffer:
+    """This rank's exchange buffer for expert-parallel exchanges over peer
+    memory (wm_ep_*): recv_x / recv_e / back regions, mapped into the peers'
+    address spaces through 64-byte CUDA IPC handles."""
+
+    def __init__(self, device: int, world: int, rank: int, capacity: int, hidden: int):
+        L = load()
+        self._lib = L
+        err = ctypes.create_string_buffer(512)
+        handle = L.wm_ep_create(device, world, rank, capacity, hidden, err, len(err))
+        if not handle:
+            raise WMError(err.value.decode() or "wm_ep_create failed")
+        self.handle = handle
+        self.device, self.world, self.rank, self.capacity, self.hidden = device, world, rank, capacity, hidden
+
+    def ipc_handle(self) -> bytes:
+        buf = ctypes.create_string_buffer(64)
+        if self._lib.wm_ep_ipc_handle(self.handle, buf) != WM_OK:
+            raise WMError("cudaIpcGetMemHandle failed for the exchange buffer")
+        return buf.raw
+
+    def open_peer(self, peer: int, handle: bytes) -> None:
+        buf = ctypes.create_string_buffer(bytes(handle), 64)
+        if self._lib.wm_ep_open_peer(self.handle, peer, buf) != WM_OK:
+            raise WMError(f"cudaIpcOpenMemHandle failed for the exchange buffer of rank {peer}")
+
+    def buffer(self, which: int) -> int:
+        return int(self._lib.wm_ep_buffer(self.handle, which))
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self._lib.wm_ep_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

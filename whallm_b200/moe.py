@@ -128,12 +128,15 @@ class Engine:
     def _args(self, layer: LayerWeights, x: torch.Tensor, K: int) -> lib.MoeArgs:
         T = x.shape[0]
         _check_bf16("x", x, (T, layer.H))
+        return self._args_at(layer, T, x.data_ptr(), K)
+
+    def _args_at(self, layer: LayerWeights, T: int, x_ptr: int, K: int) -> lib.MoeArgs:
         a = lib.MoeArgs()
         a.T, a.H, a.I, a.E, a.K = T, layer.H, layer.I, layer.E, K
         a.layout = layer.layout
         a.w13 = layer.w13.matrix()
         a.w2 = layer.w2.matrix()
-        a.x = x.data_ptr()
+        a.x = x_ptr
         a.swiglu_limit = layer.swiglu_limit
         a.route_scale = 1.0
         if layer.norm is not None:
@@ -230,6 +233,15 @@ class Engine:
             return out, (rw, ri)
         return out
 
+    def expert_pairs_at(self, layer: LayerWeights, T: int, x_ptr: int, idx_ptr: int, out: torch.Tensor) -> torch.Tensor:
+        """expert_pairs on rows that live outside torch (an exchange buffer):
+        x bf16 [T, H] at x_ptr, one route per row (int32 [T] at idx_ptr); out bf16 [T, H]."""
+        _check_bf16("out", out, (T, layer.H))
+        a = self._args_at(layer, T, x_ptr, 1)
+        a.routes_idx = idx_ptr
+        self.ctx.expert_pairs(a, out.data_ptr(), _stream())
+        return out
+
     def combine(self, pairs: torch.Tensor, w: torch.Tensor, shared_rows: torch.Tensor | None = None,
                 shared_gate: int = lib.SHARED_NONE, x: torch.Tensor | None = None,
                 gate_weight: torch.Tensor | None = None, out: torch.Tensor | None = None,
@@ -250,6 +262,22 @@ class Engine:
         if out is None:
             out = torch.empty((T, H), dtype=torch.bfloat16, device=pairs.device)
         self.ctx.combine(T, H, K, pairs.data_ptr(), _ptr(pair_pos), w.data_ptr(), _ptr(shared_rows), shared_gate,
+                         _ptr(x), _ptr(gate_weight), out.data_ptr(), _stream())
+        return out
+
+    def combine_at(self, pairs_ptr: int, w: torch.Tensor, shared_rows: torch.Tensor | None,
+                   shared_gate: int, x: torch.Tensor | None, gate_weight: torch.Tensor | None,
+                   pair_pos: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """combine over pair rows outside torch (bf16 [*, H] at pairs_ptr), pair (t, k) at row pair_pos[t, k]."""
+        T, K = w.shape
+        H = x.shape[1]
+        pair_pos = pair_pos.reshape(T, K).to(torch.int32).contiguous()
+        w = w.reshape(T, K).to(torch.float32).contiguous()
+        if shared_gate != lib.SHARED_NONE:
+            _check_bf16("shared_rows", shared_rows, (T, H))
+        if out is None:
+            out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
+        self.ctx.combine(T, H, K, pairs_ptr, pair_pos.data_ptr(), w.data_ptr(), _ptr(shared_rows), shared_gate,
                          _ptr(x), _ptr(gate_weight), out.data_ptr(), _stream())
         return out
 
