@@ -287,6 +287,23 @@ def run_ep(args, world: int, rank: int, local: int) -> None:
         for i in range(args.warmup):
             fwd(xs[i % nb])
     torch.cuda.synchronize()
+    if exchange == "peer":
+        # a bounded wait that ran out shows in the device status: if it did on
+        # any rank, every rank measures the NCCL exchange instead
+        healthy = torch.ones(1, device=dev)
+        try:
+            eng.sync()
+        except lib.WMError:
+            healthy.zero_()
+        dist.all_reduce(healthy, op=dist.ReduceOp.MIN)
+        if healthy.item() == 0:
+            ep.close()
+            exchange = "nccl"
+            ep = ExpertParallelMoE(eng, layer, K, shared_engine=shared_eng, fixed_capacity=B)
+            with torch.cuda.stream(stream):
+                for i in range(args.warmup):
+                    fwd(xs[i % nb])
+            torch.cuda.synchronize()
     c0 = eng.ctx.counters().launches + shared_eng.ctx.counters().launches
     with torch.cuda.stream(stream):
         fwd(xs[0])

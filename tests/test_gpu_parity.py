@@ -249,3 +249,19 @@ def test_config1_decode_layer_matches_oracle(engine_factory, batch):
     assert [set(r) for r in idx.cpu().numpy().tolist()] == [set(r) for r in ri.tolist()]
     ref = adapter.from_layer(wl.layer).forward(xb, idx.cpu().numpy(), w.cpu().numpy())
     assert rel(adapter.bits(out), ref) <= TOL
+
+
+# FP8 experts on the register-direct decode kernel (bf16 MMAs; H, I multiples of 512)
+@pytest.mark.parametrize("layout", [lib.LAYOUT_W13_FP8_B128, lib.LAYOUT_W13_FP8_B32])
+@pytest.mark.parametrize("T", [1, 8, 40])
+def test_fp8_decode_kernel_matches_oracle(engine_factory, layout, T):
+    E, H, I, K = 16, 1024, 512, 4
+    layer = _small_layer(layout, E, H, I, seed=91 + layout, shared_gate=lib.SHARED_ONE)
+    eng = engine_factory(64, 2048, 512, 16, 8)
+    x = synth.activations(T, H, torch.Generator(device=DEV).manual_seed(92 + T), DEV)
+    before = eng.ctx.counters().decode_calls
+    out, (w, idx) = eng.forward(layer, x, K, return_routes=True)
+    eng.sync()
+    assert eng.ctx.counters().decode_calls == before + 1  # the decode kernel ran, not the GEMV
+    ref = adapter.from_layer(layer).forward(adapter.bits(x), idx.cpu().numpy(), w.cpu().numpy())
+    assert rel(adapter.bits(out), ref) <= TOL

@@ -295,14 +295,15 @@ enum Path { kPathGemv = 0, kPathDecode = 1, kPathGemm = 2, kPathDecodeMma = 3 };
 // decode kernel); else the CUDA-core GEMV.
 Path expert_path(const wm_ctx* ctx, const wm_moe_args* a, bool has_shared) {
   if (use_gemm(ctx, a)) return kPathGemm;
-  if (is_fp8(a->layout) || ctx->encode_tiled == nullptr) return kPathGemv;
+  if (ctx->encode_tiled == nullptr) return kPathGemv;
   const wm_matrix* ms[4] = {&a->w13, &a->w2, &a->shared_w13, &a->shared_w2};
   for (int i = 0; i < (has_shared ? 4 : 2); ++i)
     if (!aligned(ms[i]->scale, 16) || (i < 2 && ms[i]->scale_stride % 16)) return kPathGemv;
-  if (ctx->opt.flags & WM_FLAG_TCGEN05_DECODE) return wm::decode_shape_ok(a->H, a->I) ? kPathDecode : kPathGemv;
+  if (!is_fp8(a->layout) && (ctx->opt.flags & WM_FLAG_TCGEN05_DECODE))
+    return wm::decode_shape_ok(a->H, a->I) ? kPathDecode : kPathGemv;
   for (int i = 0; i < (has_shared ? 4 : 2); ++i)
     if (!aligned(ms[i]->weight, 16) || (i < 2 && ms[i]->weight_stride % 16)) return kPathGemv;
-  return wm::decode_mma_shape_ok(a->H, a->I) ? kPathDecodeMma : kPathGemv;
+  return wm::decode_mma_shape_ok(a->H, a->I, fmt_of(a->layout)) ? kPathDecodeMma : kPathGemv;
 }
 
 // Plan fields of the expert kernels of `path`.
@@ -329,13 +330,17 @@ bool encode_weights(wm_ctx* ctx, CUtensorMap* map, const void* base, int64_t row
 }
 
 // The register-direct decode path: per-token prescale, gate/up (+SwiGLU), down.
+// MXFP4 experts multiply f16 copies of the rows prescaled by 2^k (gather_f16,
+// act_f16); FP8 experts the bf16 rows themselves (gather_rows, the bf16 act).
 int run_decode_mma(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts, cudaStream_t s) {
   const int H = a->H, I = a->I;
-  uint16_t* xh = ctx->xs;       // [max_rows, H] f16 token rows
-  uint16_t* acth = ctx->act16;  // [max_rows, I] f16 act rows
+  const int fmt = fmt_of(a->layout);
+  const bool fp4 = fmt == wm::kFmtMxfp4;
+  const CUtensorMapDataType dt = fp4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  uint16_t* xh = ctx->xs;                       // [max_rows, H] token rows
+  uint16_t* acth = fp4 ? ctx->act16 : ctx->act;  // [max_rows, I] act rows
   CUtensorMap bx, bact;
-  if (!encode_rows_box(ctx, &bx, xh, H, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 8) ||
-      !encode_rows_box(ctx, &bact, acth, I, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 8))
+  if (!encode_rows_box(ctx, &bx, xh, H, dt, 8) || !encode_rows_box(ctx, &bact, acth, I, dt, 8))
     return fail(ctx, "cuTensorMapEncodeTiled failed for the activation rows");
   wm::Plan plan = ctx->plan;
   plan_for_path(ctx, kPathDecodeMma, &plan);
@@ -350,25 +355,35 @@ int run_decode_mma(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& w
   d.limit = a->swiglu_limit;
   d.status = ctx->status;
   wm::prof_begin(&ctx->prof, wm::kProfGather, s);
-  wm::launch_gather_f16(static_cast<const uint16_t*>(a->x), plan, a->E, H, xh, ctx->rowscale, ctx->num_sms, s);
+  if (fp4)
+    wm::launch_gather_f16(static_cast<const uint16_t*>(a->x), plan, a->E, H, xh, ctx->rowscale, ctx->num_sms, s);
+  else
+    wm::launch_gather_rows(static_cast<const uint16_t*>(a->x), plan, a->E, H, xh, ctx->num_sms, s);
   wm::prof_end(&ctx->prof, wm::kProfGather, s);
-  d.bscale = ctx->rowscale;
+  d.bscale = fp4 ? ctx->rowscale : nullptr;
   // 8-token tiles of the call, about: one per routed expert hit (at most
   // min(E, T * K)), more where an expert gets over 8 rows, plus the shared expert's
   const int64_t pairs = int64_t(a->T) * a->K;
   const int64_t has_sh = a->shared_gate != WM_SHARED_NONE ? 1 : 0;
   const int tiles = int(std::min<int64_t>(a->E, pairs) + (a->T > 8 ? pairs / 8 : 0) + has_sh * ((a->T + 7) / 8));
   wm::prof_begin(&ctx->prof, wm::kProfDecodeGateUp, s);
-  wm::launch_decode_mma(d, 0, &bx, ctx->num_sms, s, wm::decode_mma_split(0, H, I, tiles, ctx->num_sms));
+  const int ks0 = wm::decode_mma_split(0, H, I, tiles, ctx->num_sms, fmt);
+  const int ks1 = wm::decode_mma_split(1, H, I, tiles, ctx->num_sms, fmt);
+  d.nbuf = wm::decode_mma_buffers(0, H, I, ks0, tiles, ctx->num_sms, fmt);
+  wm::launch_decode_mma(d, 0, &bx, ctx->num_sms, s, ks0, fmt);
   wm::prof_end(&ctx->prof, wm::kProfDecodeGateUp, s);
-  wm::prof_begin(&ctx->prof, wm::kProfActF16, s);
-  wm::launch_act_f16(ctx->act, plan, a->E, I, acth, ctx->actscale, ctx->num_sms, s);
-  wm::prof_end(&ctx->prof, wm::kProfActF16, s);
-  d.bscale = ctx->actscale;
+  if (fp4) {
+    wm::prof_begin(&ctx->prof, wm::kProfActF16, s);
+    wm::launch_act_f16(ctx->act, plan, a->E, I, acth, ctx->actscale, ctx->num_sms, s);
+    wm::prof_end(&ctx->prof, wm::kProfActF16, s);
+    ctx->counters.launches += 1;
+  }
+  d.bscale = fp4 ? ctx->actscale : nullptr;
   wm::prof_begin(&ctx->prof, wm::kProfDecodeDown, s);
-  wm::launch_decode_mma(d, 1, &bact, ctx->num_sms, s, wm::decode_mma_split(1, H, I, tiles, ctx->num_sms));
+  d.nbuf = wm::decode_mma_buffers(1, H, I, ks1, tiles, ctx->num_sms, fmt);
+  wm::launch_decode_mma(d, 1, &bact, ctx->num_sms, s, ks1, fmt);
   wm::prof_end(&ctx->prof, wm::kProfDecodeDown, s);
-  ctx->counters.launches += 4;
+  ctx->counters.launches += 3;
   ctx->counters.decode_calls += 1;
   return check_launch(ctx, "expert decode");
 }

@@ -78,28 +78,43 @@ struct QShared {
 
 __host__ __device__ constexpr int q_round1k(int v) { return (v + 1023) & ~1023; }
 
+// K of a chunk: a lane's 16 bytes of a row are 32 E2M1 weights or 16 E4M3 weights.
+__host__ __device__ constexpr int q_chunk_k(int fmt) { return fmt == kFmtMxfp4 ? 128 : 64; }
+// Weight rows per scale row: MXFP4 one E8M0 byte per 32 K of every row; FP8
+// one scale per 32 x 32 (UE8M0 byte) or 128 x 128 (fp32) block.  A scale row
+// is K / 32 bytes in every format.
+__host__ __device__ constexpr int q_block_rows(int fmt) { return fmt == kFmtMxfp4 ? 1 : fmt == kFmtFp8B32 ? 32 : 128; }
+// Scale rows of `rows` weight rows that start on a multiple of min(rows, block).
+__host__ __device__ constexpr int q_srows(int fmt, int rows) {
+  return (rows + q_block_rows(fmt) - 1) / q_block_rows(fmt);
+}
+
 // Bytes of one buffer: the token tile (K/64 boxes of 8 rows x 128 B) and the scale block.
 __host__ __device__ inline int q_xbytes(int K) { return kTok * K * 2; }
-__host__ __device__ inline int q_sbytes(int kind, int K, int ks) {
-  return (kind == 0 ? 2 * q_feat_item(ks) : q_rows_item(ks)) * (K / 32);
+__host__ __device__ inline int q_sbytes(int kind, int K, int ks, int fmt) {
+  return (kind == 0 ? 2 * q_srows(fmt, q_feat_item(ks)) : q_srows(fmt, q_rows_item(ks))) * (K / 32);
 }
-__host__ __device__ inline int q_bufbytes(int kind, int K, int ks) { return q_round1k(q_xbytes(K) + q_sbytes(kind, K, ks)); }
+__host__ __device__ inline int q_bufbytes(int kind, int K, int ks, int fmt) {
+  return q_round1k(q_xbytes(K) + q_sbytes(kind, K, ks, fmt));
+}
 // Segments of K: the most (up to 8, a power of two) that divide its chunks
 // into whole rings of kStages chunks.  A split KS must divide it.
-__host__ __device__ inline int q_nseg(int K) {
-  const int rings = K / 128 / kStages;
+__host__ __device__ inline int q_nseg(int K, int fmt) {
+  const int rings = K / q_chunk_k(fmt) / kStages;
   int n = 1;
   while (n < 8 && rings % (2 * n) == 0) n *= 2;
   return n;
 }
 // Segment sums of the K slices 1 .. KS-1: per buffer, per slice, per segment
 // of the slice and per warp, 32 lanes x kRG * 4 floats.
-__host__ __device__ inline int q_redbytes(int ks, int nseg) {
-  return ks > 1 ? 2 * (ks - 1) * (nseg / ks) * (kWarps / ks) * 32 * kRG * 16 : 0;
+__host__ __device__ inline int q_redbytes(int ks, int nseg, int nbuf) {
+  return ks > 1 ? nbuf * (ks - 1) * (nseg / ks) * (kWarps / ks) * 32 * kRG * 16 : 0;
 }
 
-size_t q_smem_bytes(int kind, int K, int ks) {
-  return size_t(2 * q_bufbytes(kind, K, ks)) + q_redbytes(ks, q_nseg(K)) + 1024 + sizeof(QShared) + 16;
+// nbuf: token-tile buffers (2: the next item's tile loads during this one)
+size_t q_smem_bytes(int kind, int K, int ks, int fmt, int nbuf) {
+  return size_t(nbuf) * q_bufbytes(kind, K, ks, fmt) + q_redbytes(ks, q_nseg(K, fmt), nbuf) + 1024 + sizeof(QShared) +
+         16;
 }
 
 __device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
@@ -158,6 +173,15 @@ __device__ __forceinline__ void mma_f16(float* d, uint32_t a0, uint32_t a1, uint
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ void mma_bf16q(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                          uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                "l"(src), "r"(bytes), "r"(smem_u32(bar))
@@ -189,27 +213,33 @@ __device__ __forceinline__ QItem q_item(const DecodeArgs& a, int q, int nb) {
 
 }  // namespace
 
-// KIND 0: gate/up (+SwiGLU) -> act [rows, I] bf16 and per-row |act| maxima;
-// KIND 1: down -> routed [rows, H] bf16.  tm_x: the f16 token rows
-// ([max_rows, K], boxes of 64 x 8, 128-byte swizzle).
-template <int KIND, int KS>
+// KIND 0: gate/up (+SwiGLU) -> act [rows, I] bf16 (and, MXFP4, per-row |act|
+// maxima); KIND 1: down -> routed [rows, H] bf16.  tm_x: the token rows
+// ([max_rows, K], boxes of 64 x 8, 128-byte swizzle): f16 prescaled rows for
+// MXFP4 (f16 MMAs), plain bf16 rows for FP8 (bf16 MMAs on weights rounded to
+// bf16 after their block scale, as the reference decodes them).
+template <int KIND, int KS, int FMT>
 __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __grid_constant__ CUtensorMap tm_x,
                                                                  const DecodeArgs a) {
   constexpr int kFeatItem = q_feat_item(KS), kRowsItem = q_rows_item(KS);
   constexpr int kRowWarps = kWarps / KS;
+  constexpr bool kFp4 = FMT == kFmtMxfp4;
+  constexpr int BR = q_block_rows(FMT);
   extern __shared__ uint8_t smem_raw[];
   const int K = KIND == 0 ? a.H : a.I;
-  const int S = K / 32;       // E8M0 bytes per weight row
-  const int KC = K / 128;     // chunks per row
+  const int S = K / 32;       // bytes per scale row (E8M0 per row, or per FP8 block row)
+  const int KC = K / q_chunk_k(FMT);  // chunks per row (64 bytes of each row)
   const int KCw = KC / KS;    // chunks of this warp's K slice
-  const int nseg = q_nseg(K), SEGC = KC / nseg;  // segments of K, chunks per segment
-  const int wseg = nseg / KS;                     // segments of this warp's slice
-  const int64_t rowb = K / 2; // packed bytes per weight row
-  const int xbytes = q_xbytes(K), bufbytes = q_bufbytes(KIND, K, KS);
+  const int nseg = q_nseg(K, FMT), SEGC = KC / nseg;  // segments of K, chunks per segment
+  const int wseg = nseg / KS;                          // segments of this warp's slice
+  const int64_t rowb = kFp4 ? K / 2 : K;  // bytes per weight row
+  const int xbytes = q_xbytes(K), bufbytes = q_bufbytes(KIND, K, KS, FMT);
   const uint32_t raw0 = smem_u32(smem_raw);
   const uint32_t base = (raw0 + 1023u) & ~1023u;
-  float* red = reinterpret_cast<float*>(smem_raw + (base - raw0) + 2 * bufbytes);
-  QShared& sh = *reinterpret_cast<QShared*>(smem_raw + (base - raw0) + 2 * bufbytes + q_redbytes(KS, nseg));
+  const int NB = a.nbuf;  // token-tile buffers: 2, or 1 when the CTA has one item or the tile is large
+  float* red = reinterpret_cast<float*>(smem_raw + (base - raw0) + NB * bufbytes);
+  QShared& sh = *reinterpret_cast<QShared*>(smem_raw + (base - raw0) + NB * bufbytes + q_redbytes(KS, nseg, NB));
+  const int gsrows = q_srows(FMT, kFeatItem);  // scale rows of the gate (and of the up) rows of an item
 
   const int warp_id = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int warp = warp_id % kRowWarps;  // row group
@@ -234,19 +264,21 @@ __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __gri
   // Issues the token tile and scale block of item `it` into buffer b.
   auto issue = [&](const QItem& it, int b) {
     const uint32_t xdst = base + b * bufbytes, sdst = xdst + xbytes;
-    mbar_arrive_expect_tx(&sh.full[b], uint32_t(xbytes + q_sbytes(KIND, K, KS)));
+    mbar_arrive_expect_tx(&sh.full[b], uint32_t(xbytes + q_sbytes(KIND, K, KS, FMT)));
     for (int kb = 0; kb < K / 64; ++kb) tma_load_2d_q(xdst + kb * 1024, &tm_x, kb * 64, it.row0, &sh.full[b]);
     if (KIND == 0) {
       const uint8_t* s = a.wts.s13_of(it.e);
-      bulk_load(sdst, s + int64_t(gate_base + it.blk * kFeatItem) * S, kFeatItem * S, &sh.full[b]);
-      bulk_load(sdst + kFeatItem * S, s + int64_t(up_base + it.blk * kFeatItem) * S, kFeatItem * S, &sh.full[b]);
+      const int n = gsrows * S;
+      bulk_load(sdst, s + int64_t((gate_base + it.blk * kFeatItem) / BR) * S, n, &sh.full[b]);
+      bulk_load(sdst + n, s + int64_t((up_base + it.blk * kFeatItem) / BR) * S, n, &sh.full[b]);
     } else {
-      bulk_load(sdst, a.wts.s2_of(it.e) + int64_t(it.blk) * kRowsItem * S, kRowsItem * S, &sh.full[b]);
+      bulk_load(sdst, a.wts.s2_of(it.e) + int64_t(it.blk * kRowsItem / BR) * S, q_srows(FMT, kRowsItem) * S,
+                &sh.full[b]);
     }
   };
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tm_x);
-    for (int b = 0; b < 2; ++b)
+    for (int b = 0; b < NB; ++b)
       if (int(blockIdx.x) + b * int(gridDim.x) < n_items) issue(q_item(a, blockIdx.x + b * gridDim.x, nb), b);
   }
 
@@ -258,12 +290,14 @@ __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __gri
   for (int r = 0; r < kRG; ++r)
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
+      // scale row in the staged block: the row's block, counted from the item's
+      // first block (items never straddle a block they do not start on)
       if (KIND == 0) {
         roff[2 * r + h] = (int64_t(h ? up_base - gate_base : 0) + 8 * r) * rowb;
-        srow[2 * r + h] = h * kFeatItem + warp * (kRG * 8) + 8 * r + g;
+        srow[2 * r + h] = h * gsrows + (warp * (kRG * 8) + 8 * r + g) / BR;
       } else {
         roff[2 * r + h] = int64_t(16 * r + 8 * h) * rowb;
-        srow[2 * r + h] = warp * (kRG * 16) + 16 * r + 8 * h + g;
+        srow[2 * r + h] = (warp * (kRG * 16) + 16 * r + 8 * h + g) / BR;
       }
     }
   // First weight row of this thread in item `it` (plus its 16-byte column of
@@ -316,10 +350,12 @@ __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __gri
     cur = nxt;
     nxt = fetch(cq + gridDim.x);
     nxt2 = fetch(cq + 2 * gridDim.x);
-    bs0 = 2 * t < cur.valid ? a.bscale[cur.row0 + 2 * t] : 1.0f;
-    bs1 = 2 * t + 1 < cur.valid ? a.bscale[cur.row0 + 2 * t + 1] : 1.0f;
-    const int b = li & 1;
-    if (!warp_wait(&sh.full[b], (li >> 1) & 1, abort)) {
+    if (kFp4) {
+      bs0 = 2 * t < cur.valid ? a.bscale[cur.row0 + 2 * t] : 1.0f;
+      bs1 = 2 * t + 1 < cur.valid ? a.bscale[cur.row0 + 2 * t + 1] : 1.0f;
+    }
+    const int b = li % NB;
+    if (!warp_wait(&sh.full[b], (li / NB) & 1, abort)) {
       if (lane == 0 && !*abort) {
         report_status(a.status, kStatusWaitTimeout, 40 + KIND);
         sh.abort = 1;
@@ -330,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __gri
     sb = xb + xbytes;
     // largest E8M0 byte of each of this thread's rows (the four t lanes split a row)
 #pragma unroll
-    for (int j = 0; j < 2 * kRG; ++j) {
+    for (int j = 0; j < (kFp4 ? 2 * kRG : 0); ++j) {
       const uint32_t rb = sb + srow[j] * S + t * (S / 4);
       uint32_t m = 0;
       if ((S & 15) == 0) {  // a lane's S / 4 bytes are whole, aligned words
@@ -352,7 +388,7 @@ __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __gri
   };
 
   // red: [buffer][K slice 1 .. KS-1][segment of the slice][row group][tile r][lane] float4.
-  // A buffer's slots are rewritten two items later, after every warp
+  // A buffer's slots are rewritten NB items later, after every warp
   // released that buffer, so the group's first warp has read them by then.
   auto red_slot = [&](int b, int k, int sg) {
     return reinterpret_cast<float4*>(red) + (((b * (KS - 1) + k - 1) * wseg + sg) * kRowWarps + warp) * 32 * kRG + lane;
@@ -360,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __gri
   // End of segment sg of this warp's slice: its sum s = chain0 + chain1 goes
   // into y (the group's first warp) or to shared memory; the chains restart.
   auto end_segment = [&](int sg) {
-    const int b = li & 1;
+    const int b = li % NB;
 #pragma unroll
     for (int r = 0; r < kRG; ++r) {
       float sv[4];
@@ -383,11 +419,11 @@ __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __gri
     const float is0 = 1.0f / bs0, is1 = 1.0f / bs1;
     bool lead = true;  // this warp runs the epilogue of its rows
     if (KS > 1) {
-      const int b = li & 1;
+      const int b = li % NB;
       if (ks > 0) {  // the segment sums are in place
         mbar_arrive(&sh.red_full[b][warp]);
         lead = false;
-      } else if (!warp_wait(&sh.red_full[b][warp], (li >> 1) & 1, abort)) {
+      } else if (!warp_wait(&sh.red_full[b][warp], (li / NB) & 1, abort)) {
         if (lane == 0 && !*abort) {
           report_status(a.status, kStatusWaitTimeout, 44 + KIND);
           sh.abort = 1;
@@ -414,7 +450,8 @@ __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __gri
       float m0 = 0.0f, m1 = 0.0f;
 #pragma unroll
       for (int r = 0; r < kRG; ++r) {
-        const float fg = e8m0_to_f32(uint32_t(smax[2 * r])), fu = e8m0_to_f32(uint32_t(smax[2 * r + 1]));
+        const float fg = kFp4 ? e8m0_to_f32(uint32_t(smax[2 * r])) : 1.0f;
+        const float fu = kFp4 ? e8m0_to_f32(uint32_t(smax[2 * r + 1])) : 1.0f;
         const int f = cur.blk * kFeatItem + warp * (kRG * 8) + 8 * r + g;
         if (n0 < cur.valid) {
           const float gv = bf16_round(y[r][0] * fg * is0), uv = bf16_round(y[r][2] * fu * is0);
@@ -435,7 +472,7 @@ __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __gri
         m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
         m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
       }
-      if (g == 0) {
+      if (kFp4 && g == 0) {  // the f16 prescale of the act rows (FP8 keeps bf16 rows)
         if (n0 < cur.valid) atomicMax(a.plan.rowmax + cur.row0 + n0, __float_as_uint(m0));
         if (n1 < cur.valid) atomicMax(a.plan.rowmax + cur.row0 + n1, __float_as_uint(m1));
       }
@@ -444,28 +481,74 @@ __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __gri
       for (int r = 0; r < kRG; ++r)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const float fr = e8m0_to_f32(uint32_t(smax[2 * r + h]));
+          const float fr = kFp4 ? e8m0_to_f32(uint32_t(smax[2 * r + h])) : 1.0f;
           const int hc = cur.blk * kRowsItem + warp * (kRG * 16) + 16 * r + 8 * h + g;
           if (n0 < cur.valid) a.routed[int64_t(cur.row0 + n0) * a.H + hc] = f32_to_bf16_bits(y[r][2 * h] * fr * is0);
           if (n1 < cur.valid)
             a.routed[int64_t(cur.row0 + n1) * a.H + hc] = f32_to_bf16_bits(y[r][2 * h + 1] * fr * is1);
         }
     }
-    // release the buffer; the last warp refills it with the item after next
+    // release the buffer; the last warp refills it with the item NB items on
     __syncwarp();
     if (lane == 0) {
-      const int b = li & 1;
+      const int b = li % NB;
       __threadfence_block();
       if (atomicAdd(&sh.done[b], 1) == kWarps - 1) {
         sh.done[b] = 0;
-        if (cq + 2 * int(gridDim.x) < n_items && !*abort) issue(nxt2, b);
+        if (cq + NB * int(gridDim.x) < n_items && !*abort) issue(NB == 2 ? nxt2 : nxt, b);
       }
     }
     __syncwarp();
   };
 
+  // FP8: lane t's 16 bytes of a row are 16 E4M3 weights at K offset 64cc + 16t,
+  // one block scale; each weight is rounded to bf16 after its fp32 scaling
+  // (the reference's decode), the token operand is the plain bf16 row.  Word
+  // q (4 weights) is one MMA step: slots {2t, 2t+1} <- weights 4q, 4q+1 and
+  // slots {2t+8, 2t+9} <- 4q+2, 4q+3, the token operand at the same K.
+  auto chunk_fp8 = [&](const uint4 (&w)[2 * kRG], int cc) {
+    float sc[2 * kRG];
+#pragma unroll
+    for (int j = 0; j < 2 * kRG; ++j) {
+      const uint32_t sa = sb + srow[j] * S;
+      if (FMT == kFmtFp8B32)
+        sc[j] = e8m0_to_f32(lds_u8q(sa + 2 * cc + (t >> 1)), true);
+      else
+        sc[j] = __uint_as_float(lds_u32(sa + 4 * (cc >> 1)));
+    }
+    const uint32_t xrow = xb + cc * 1024 + g * 128;  // box cc: this chunk's 64 K of token row g
+    uint4 xv[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) xv[u] = lds_v4q(xrow + (((2 * t + u) ^ g) << 4));
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4& xq = xv[q >> 1];
+      const uint32_t x0 = (q & 1) ? xq.z : xq.x, x1 = (q & 1) ? xq.w : xq.y;
+#pragma unroll
+      for (int r = 0; r < kRG; ++r) {
+        const uint4& wa = w[2 * r];
+        const uint4& wb = w[2 * r + 1];
+        const uint32_t va = q == 0 ? wa.x : q == 1 ? wa.y : q == 2 ? wa.z : wa.w;
+        const uint32_t vb = q == 0 ? wb.x : q == 1 ? wb.y : q == 2 ? wb.z : wb.w;
+        float fa[4], fb[4];
+        e4m3x4_to_f32(va, fa);
+        e4m3x4_to_f32(vb, fb);
+        const float sa = sc[2 * r], sbv = sc[2 * r + 1];
+        const uint32_t a01 = pack_bf16x2(__fmul_rn(fa[0], sa), __fmul_rn(fa[1], sa));
+        const uint32_t a23 = pack_bf16x2(__fmul_rn(fa[2], sa), __fmul_rn(fa[3], sa));
+        const uint32_t b01 = pack_bf16x2(__fmul_rn(fb[0], sbv), __fmul_rn(fb[1], sbv));
+        const uint32_t b23 = pack_bf16x2(__fmul_rn(fb[2], sbv), __fmul_rn(fb[3], sbv));
+        mma_bf16q(acc[r][q & 1], a01, b01, a23, b23, x0, x1);
+      }
+    }
+  };
+
   // One chunk of the current item from the weight registers w.
   auto chunk = [&](const uint4 (&w)[2 * kRG], int cc) {
+    if constexpr (!kFp4) {
+      chunk_fp8(w, cc);
+      return;
+    }
     uint32_t mult[2 * kRG];
 #pragma unroll
     for (int j = 0; j < 2 * kRG; ++j) mult[j] = group_mult(lds_u8q(sb + srow[j] * S + 4 * cc + t), rinv[j]);
@@ -523,23 +606,53 @@ __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __gri
   __syncthreads();
 }
 
-bool decode_mma_shape_ok(int H, int I) {
-  return I % q_feat_item(1) == 0 && H % q_rows_item(1) == 0 && H % (128 * kStages) == 0 &&
-         I % (128 * kStages) == 0 && q_smem_bytes(0, H, 1) <= 227 * 1024 && q_smem_bytes(1, I, 1) <= 227 * 1024;
+bool decode_mma_shape_ok(int H, int I, int fmt) {
+  const int ck = q_chunk_k(fmt) * kStages;
+  // FP8 scale rows (K / 32 bytes) are bulk copies: whole 16-byte units
+  const bool scale_rows = fmt == kFmtMxfp4 || (H % 512 == 0 && I % 512 == 0);
+  return I % q_feat_item(1) == 0 && H % q_rows_item(1) == 0 && H % ck == 0 && I % ck == 0 && scale_rows &&
+         q_smem_bytes(0, H, 1, fmt, 1) <= 227 * 1024 && q_smem_bytes(1, I, 1, fmt, 1) <= 227 * 1024;
 }
 
 namespace {
 
-template <int KIND, int KS>
+template <int KIND, int KS, int FMT>
 void set_smem(int K) {
-  cudaFuncSetAttribute(decode_mma_kernel<KIND, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       int(std::min(q_smem_bytes(KIND, K, KS), size_t(227 * 1024))));
+  cudaFuncSetAttribute(decode_mma_kernel<KIND, KS, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       int(std::min(q_smem_bytes(KIND, K, KS, FMT, 2), size_t(227 * 1024))));
 }
 
-template <int KIND, int KS>
+template <int FMT>
+void set_smem_all(int max_h, int max_i) {
+  set_smem<0, 1, FMT>(max_h);
+  set_smem<0, 2, FMT>(max_h);
+  set_smem<0, 4, FMT>(max_h);
+  set_smem<0, 8, FMT>(max_h);
+  set_smem<1, 1, FMT>(max_i);
+  set_smem<1, 2, FMT>(max_i);
+  set_smem<1, 4, FMT>(max_i);
+  set_smem<1, 8, FMT>(max_i);
+}
+
+template <int KIND, int KS, int FMT>
 void launch_ks(const DecodeArgs& a, const CUtensorMap& x, int num_sms, cudaStream_t stream) {
   const int K = KIND == 0 ? a.H : a.I;
-  decode_mma_kernel<KIND, KS><<<num_sms * kCtas, kThreads, q_smem_bytes(KIND, K, KS), stream>>>(x, a);
+  decode_mma_kernel<KIND, KS, FMT>
+      <<<num_sms * kCtas, kThreads, q_smem_bytes(KIND, K, KS, FMT, a.nbuf), stream>>>(x, a);
+}
+
+template <int KIND, int FMT>
+void launch_kind(const DecodeArgs& a, const CUtensorMap& x, int num_sms, cudaStream_t stream, int ks) {
+  if (ks >= 8) launch_ks<KIND, 8, FMT>(a, x, num_sms, stream);
+  else if (ks >= 4) launch_ks<KIND, 4, FMT>(a, x, num_sms, stream);
+  else if (ks >= 2) launch_ks<KIND, 2, FMT>(a, x, num_sms, stream);
+  else launch_ks<KIND, 1, FMT>(a, x, num_sms, stream);
+}
+
+template <int FMT>
+void launch_fmt(const DecodeArgs& a, int kind, const CUtensorMap& x, int num_sms, cudaStream_t stream, int ks) {
+  if (kind == 0) launch_kind<0, FMT>(a, x, num_sms, stream, ks);
+  else launch_kind<1, FMT>(a, x, num_sms, stream, ks);
 }
 
 }  // namespace
@@ -555,42 +668,39 @@ void decode_mma_init_attributes(int max_h, int max_i) {
   max_i = std::max(max_i, set_i[dev]);
   set_h[dev] = max_h;
   set_i[dev] = max_i;
-  set_smem<0, 1>(max_h);
-  set_smem<0, 2>(max_h);
-  set_smem<0, 4>(max_h);
-  set_smem<0, 8>(max_h);
-  set_smem<1, 1>(max_i);
-  set_smem<1, 2>(max_i);
-  set_smem<1, 4>(max_i);
-  set_smem<1, 8>(max_i);
+  set_smem_all<kFmtMxfp4>(max_h, max_i);
+  set_smem_all<kFmtFp8B128>(max_h, max_i);
+  set_smem_all<kFmtFp8B32>(max_h, max_i);
 }
 
-int decode_mma_split(int kind, int H, int I, int tiles, int num_sms) {
+int decode_mma_split(int kind, int H, int I, int tiles, int num_sms, int fmt) {
   const int K = kind == 0 ? H : I;
   const int nb = kind == 0 ? I / q_feat_item(1) : H / q_rows_item(1);  // row blocks of an unsplit item
   // Split while the items would leave over half of the SMs idle (measured on
   // config-1 decode: batch 1 gate/up 22 -> 88 items, down 44 -> 88; from
   // about 80 unsplit items on, splitting costs more than it spreads).
   int ks = 1;
-  while (2 * ks <= q_nseg(K) && int64_t(tiles) * nb * ks * 2 < num_sms &&
-         q_smem_bytes(kind, K, 2 * ks) <= 227 * 1024)
+  while (2 * ks <= q_nseg(K, fmt) && int64_t(tiles) * nb * ks * 2 < num_sms &&
+         q_smem_bytes(kind, K, 2 * ks, fmt, 1) <= 227 * 1024)
     ks *= 2;
   return ks;
 }
 
-void launch_decode_mma(const DecodeArgs& a, int kind, const void* tmap_x, int num_sms, cudaStream_t stream, int ks) {
+int decode_mma_buffers(int kind, int H, int I, int ks, int tiles, int num_sms, int fmt) {
+  const int K = kind == 0 ? H : I;
+  const int64_t items = int64_t(tiles) * (kind == 0 ? I / q_feat_item(ks) : H / q_rows_item(ks));
+  // A second token-tile buffer only pays when CTAs get several items, and
+  // shared memory past ~160 KB leaves the L1 too small for the weight loads
+  // in flight (the carve-out steps of the B200 SM).
+  return items > num_sms && q_smem_bytes(kind, K, ks, fmt, 2) <= 160 * 1024 ? 2 : 1;
+}
+
+void launch_decode_mma(const DecodeArgs& a, int kind, const void* tmap_x, int num_sms, cudaStream_t stream, int ks,
+                       int fmt) {
   const CUtensorMap& x = *static_cast<const CUtensorMap*>(tmap_x);
-  if (kind == 0) {
-    if (ks >= 8) launch_ks<0, 8>(a, x, num_sms, stream);
-    else if (ks >= 4) launch_ks<0, 4>(a, x, num_sms, stream);
-    else if (ks >= 2) launch_ks<0, 2>(a, x, num_sms, stream);
-    else launch_ks<0, 1>(a, x, num_sms, stream);
-  } else {
-    if (ks >= 8) launch_ks<1, 8>(a, x, num_sms, stream);
-    else if (ks >= 4) launch_ks<1, 4>(a, x, num_sms, stream);
-    else if (ks >= 2) launch_ks<1, 2>(a, x, num_sms, stream);
-    else launch_ks<1, 1>(a, x, num_sms, stream);
-  }
+  if (fmt == kFmtFp8B128) launch_fmt<kFmtFp8B128>(a, kind, x, num_sms, stream, ks);
+  else if (fmt == kFmtFp8B32) launch_fmt<kFmtFp8B32>(a, kind, x, num_sms, stream, ks);
+  else launch_fmt<kFmtMxfp4>(a, kind, x, num_sms, stream, ks);
 }
 
 }  // namespace wm

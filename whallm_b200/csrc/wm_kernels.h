@@ -136,6 +136,7 @@ struct DecodeArgs {
   int gate_first;
   float limit;
   uint32_t* status;
+  int nbuf;             // decode_mma_kernel: token-tile buffers, 1 or 2 (decode_mma_buffers)
 };
 void decode_init_attributes();
 bool decode_shape_ok(int H, int I);
@@ -154,15 +155,19 @@ void launch_decode(const DecodeArgs& a, int kind, const void* const* maps, int n
 // ---- decode, register-direct warp MMAs (wm_decode_mma.cu): plan tiles of 8
 // rows; tmap_x points to a CUtensorMap of the f16 activation rows [max_rows, K]
 // (boxes of 64 x 8, 128-byte swizzle), K = H for kind 0 (gate/up) and I for kind 1.
-bool decode_mma_shape_ok(int H, int I);
+// fmt: kFmtMxfp4 (f16 token rows from gather_f16 / act_f16, bscale set) or an
+// FP8 format (bf16 token rows from gather_rows / the bf16 act, bscale unused).
+bool decode_mma_shape_ok(int H, int I, int fmt = kFmtMxfp4);
 void decode_mma_init_attributes(int max_h, int max_i);
 // ks: K split (1, 2, 4, 8; see decode_mma_split) -- items of 1 / ks of the
 // rows, each warp over 1 / ks of K
 void launch_decode_mma(const DecodeArgs& a, int kind, const void* tmap_x, int num_sms, cudaStream_t stream,
-                       int ks = 1);
+                       int ks = 1, int fmt = kFmtMxfp4);
 // The K split for a call of about `tiles` 8-token tiles: the smallest that
-// gives every SM an item (K / 128 chunks must divide evenly).
-int decode_mma_split(int kind, int H, int I, int tiles, int num_sms);
+// spreads the items over the SMs (within the segments of K).
+int decode_mma_split(int kind, int H, int I, int tiles, int num_sms, int fmt = kFmtMxfp4);
+// Token-tile buffers (1 or 2) for a launch with split ks over about `tiles` tiles.
+int decode_mma_buffers(int kind, int H, int I, int ks, int tiles, int num_sms, int fmt = kFmtMxfp4);
 
 // ---- prefill grouped GEMM on tcgen05 (wm_gemm_sm100.cu)
 struct GemmArgs {
