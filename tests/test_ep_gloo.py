@@ -162,3 +162,78 @@ def test_ep_matches_single_process(shared, skew, fixed):
     if skew and not fixed:
         assert results[1][3] == 0  # rank 1 owns no chosen expert
 
+
+
+class _FakeBuffer:
+    """Stands in for lib.EpBuffer; fails where told to."""
+
+    def __init__(self, fail_open: bool):
+        self.fail_open, self.opened, self.closed = fail_open, [], False
+
+    def ipc_handle(self) -> bytes:
+        return b"h" * 64
+
+    def open_peer(self, peer: int, handle: bytes) -> None:
+        if self.fail_open:
+            raise lib.WMError(f"cannot map rank {peer}")
+        self.opened.append(peer)
+
+    def close(self) -> None:
+        self.closed = True
+
+
+def _setup_worker(rank: int, world: int, port: int, case: str, q) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from whallm_b200.ep import ExpertParallelMoE
+
+        made = []
+
+        class Probe(ExpertParallelMoE):
+            def _device_key(self) -> str:
+                return "gpu-0" if case == "same_gpu" else f"gpu-{rank}"
+
+            def _new_buffer(self):
+                if case == "create_fails" and rank == 1:
+                    raise lib.WMError("no device memory")
+                made.append(_FakeBuffer(fail_open=case == "open_fails" and rank == 0))
+                return made[-1]
+
+        try:
+            ep = Probe(CpuEngine(), _layer(7, False), K, fixed_capacity=4, peer_memory=True)
+            q.put((rank, "ok", made[0].opened, False))
+            ep.ep_buf = None
+        except (RuntimeError, ValueError) as exc:
+            q.put((rank, type(exc).__name__ + ": " + str(exc), [], bool(made) and made[0].closed))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("case", ["ok", "create_fails", "open_fails", "same_gpu"])
+def test_peer_exchange_setup_agrees_on_every_rank(case):
+    """A buffer that cannot be created or mapped on any rank makes every rank
+    give up the peer-memory exchange together (so all of them fall back to the
+    collective path instead of waiting on each other); ranks sharing a GPU are
+    refused."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_setup_worker, args=(r, 2, port, case, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    outcomes = [r[1] for r in res]
+    if case == "ok":
+        assert outcomes == ["ok", "ok"] and res[0][2] == [1] and res[1][2] == [0]
+    elif case == "same_gpu":
+        assert all(o.startswith("ValueError") for o in outcomes)
+    else:
+        assert all(o.startswith("RuntimeError: peer-memory exchange unavailable") for o in outcomes), outcomes
+        assert all(("no device memory" if case == "create_fails" else "cannot map") in o for o in outcomes)
+        for rank, _, _, closed in res:  # a buffer that was made is released
+            if case == "open_fails" or rank == 0:
+                assert closed

@@ -22,10 +22,16 @@
 // (two 16-row MMA tiles).  For gate/up a 16-row tile is 8 gate rows and the
 // 8 up rows of the same features, so SwiGLU runs on the accumulators.  The
 // item's f16 token tile (TMA, 128-byte swizzle) and its E8M0 scale block (one
-// or two bulk copies) land in shared memory, double-buffered; the warp that
-// finishes an item last refills that buffer for the item after next.  The
-// weight loads run kStages chunks ahead across item boundaries; the metadata
-// of the next items is read an item early, so no load waits on another.
+// or two bulk copies) land in shared memory, double-buffered (one buffer when
+// a CTA gets a single item or the tile is large); the warp that finishes an
+// item last refills that buffer for the item after next.  The weight loads
+// run kStages chunks ahead across item boundaries; the metadata of the next
+// items is read an item early, so no load waits on another.
+//
+// FP8 experts (E4M3 with 128 x 128 fp32 or 32 x 32 UE8M0 block scales) take
+// the same kernel: a lane's 16 bytes are 16 weights, each rounded to bf16
+// after its fp32 scaling as the reference decodes them, into bf16 MMAs with
+// the plain bf16 token rows (no prescale).
 //
 // Measured on B200 (config-1 decode, 64 tokens): gate/up ~100 us for 407 MB
 // (4.1 TB/s), down ~62 us.  Two limits meet there: this row-striped access

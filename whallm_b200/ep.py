@@ -95,16 +95,15 @@ class ExpertParallelMoE:
             raise ValueError("peer-memory exchanges need a fixed capacity")
         if self.world > 8:
             raise ValueError("peer-memory exchanges support at most 8 ranks")
-        dev = self.engine.device
         ids = [None] * self.world
-        dist.all_gather_object(ids, str(torch.cuda.get_device_properties(dev).uuid), group=self.group)
+        dist.all_gather_object(ids, self._device_key(), group=self.group)
         if len(set(ids)) != self.world:
             raise ValueError("peer-memory exchanges need every rank on its own GPU")
         # every rank takes part in every collective below, whatever fails locally,
         # and all of them agree on the outcome
         buf, handle, error = None, b"", ""
         try:
-            buf = lib.EpBuffer(dev.index or 0, self.world, self.rank, self.fixed * self.K, self.layer.H)
+            buf = self._new_buffer()
             handle = buf.ipc_handle()
         except lib.WMError as exc:
             error = str(exc)
@@ -127,10 +126,19 @@ class ExpertParallelMoE:
             raise RuntimeError("peer-memory exchange unavailable: " + "; ".join(e for e in errors if e))
         return buf
 
+    def _device_key(self) -> str:
+        """Identifies this rank's GPU across processes."""
+        return str(torch.cuda.get_device_properties(self.engine.device).uuid)
+
+    def _new_buffer(self) -> lib.EpBuffer:
+        dev = self.engine.device
+        return lib.EpBuffer(dev.index or 0, self.world, self.rank, self.fixed * self.K, self.layer.H)
+
     def close(self) -> None:
         """Release the exchange buffer once every rank has finished (collective)."""
         if self.ep_buf is not None:
-            torch.cuda.synchronize(self.engine.device)
+            if torch.cuda.is_available():
+                torch.cuda.synchronize(self.engine.device)
             dist.barrier(group=self.group)
             self.ep_buf.close()
             self.ep_buf = None
