@@ -40,7 +40,7 @@ H, I, E, K = 2048, 512, 512, 10
 BLOB = 1_671_168  # bytes of one expert blob (gate_up + scales + down + scales)
 GATE_UP_BYTES = 2 * I * H // 2 + 2 * I * H // 32
 # dram bytes (read + write) of one gate/up decode launch at this workload, from an ncu capture
-NCU_GATE_UP_TRAFFIC = 416.297216e6 + 4.186368e6
+NCU_GATE_UP_TRAFFIC = 412.166656e6 + 3.397376e6
 DOWN_BYTES = H * I // 2 + H * I // 32
 
 
