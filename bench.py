@@ -10,9 +10,10 @@ step.  `value` is whole-job tokens/s from device events (inputs resident);
 `e2e` is the same through the public call with pinned host input/output and
 the copies inside the timed region.  With --gpus N > 1 the layer runs
 expert-parallel (whallm_b200.ep): every rank owns E/N experts and its own
-64-token batch, and pairs travel to their experts' ranks and back by NCCL
-all-to-all (weak scaling; eager steps, since the split sizes are read on the
-host).  At N = 1 the line also carries a `prefill` section: the config-2
+64-token batch, and pairs travel to their experts' ranks and back through
+NVLink peer memory (--exchange nccl: NCCL all-to-all), fixed-capacity
+exchanges, one CUDA graph per step (weak scaling).  At N = 1 the line also
+carries a `prefill` section: the config-2
 layer (16,384 tokens, Zipf(1.1) routing) through the grouped-GEMM path.
 At N = 1 it also carries `decode_batches` (the same layer at batch 1 and 8)
 and `long_calls`: one config-3 layer (DeepSeek-style
