@@ -222,12 +222,19 @@ __global__ void __launch_bounds__(1024) plan_scan_kernel(int T, int E, int chunk
   extern __shared__ int sm[];
   int* cnt = sm;           // E + 1
   int* off = cnt + E + 1;  // E + 2
+  constexpr int kBatch = 16;  // chunk counts loaded together: one L2 round trip per batch, not per chunk
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     int running = 0;
-    for (int c = 0; c < chunks; ++c) {
-      const int h = p.hist[(int64_t)c * (E + 1) + e];
-      p.hist[(int64_t)c * (E + 1) + e] = running;
-      running += h;
+    for (int c0 = 0; c0 < chunks; c0 += kBatch) {
+      int h[kBatch];
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) h[j] = c0 + j < chunks ? p.hist[(int64_t)(c0 + j) * (E + 1) + e] : 0;
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j)
+        if (c0 + j < chunks) {
+          p.hist[(int64_t)(c0 + j) * (E + 1) + e] = running;
+          running += h[j];
+        }
     }
     cnt[e] = running;
   }
