@@ -214,30 +214,27 @@ __device__ __forceinline__ void topk_token(const float* __restrict__ row, const 
       if (j < per_lane && e < E && !((group_keep >> (e / per_group)) & 1u)) taken |= 1u << j;
     }
   }
-  // top-k by key: every lane keeps its best remaining slot (a tree over its
-  // slots, ties to the lower slot); each round two warp reductions find the
+  // top-k by key: every lane keeps its best remaining slot (ties to the
+  // lower slot); each round two warp reductions find the
   // largest key and, among equal keys, the lowest expert index; only the
   // winner's lane rescans.  Lane k keeps selection k.
   float lbest = -INFINITY;
   int lidx = 0x7fffffff;
+  // (a linear pass in slot order, strictly greater wins: the fewest
+  // instructions, which is what long calls pay for)
   auto rescan = [&]() {
-    float bk[EPL];
-    int bj[EPL];
+    float best = ((taken & 1u) != 0u) ? -INFINITY : key[0];
+    int bj = 0;
 #pragma unroll
-    for (int j = 0; j < EPL; ++j) {
-      bk[j] = ((taken >> j) & 1u) ? -INFINITY : key[j];
-      bj[j] = j;
+    for (int j = 1; j < EPL; ++j) {
+      const float kj = ((taken >> j) & 1u) ? -INFINITY : key[j];
+      if (kj > best) {
+        best = kj;
+        bj = j;
+      }
     }
-#pragma unroll
-    for (int w = EPL / 2; w > 0; w >>= 1)
-#pragma unroll
-      for (int j = 0; j < w; ++j)
-        if (bk[j + w] > bk[j] || (bk[j + w] == bk[j] && bj[j + w] < bj[j])) {
-          bk[j] = bk[j + w];
-          bj[j] = bj[j + w];
-        }
-    lbest = bk[0];
-    lidx = lane + 32 * bj[0];
+    lbest = best;
+    lidx = lane + 32 * bj;
   };
   // larger key -> larger unsigned value
   auto ordered = [](float f) {
