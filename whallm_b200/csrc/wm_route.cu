@@ -250,14 +250,23 @@ __device__ __forceinline__ void topk_token(const float* __restrict__ row, const 
     int bi = int(__reduce_min_sync(0xffffffffu, u == top ? uint32_t(lidx) : 0xffffffffu));
     if (bi < 0 || bi >= 32 * EPL) bi = 0;  // fewer eligible experts than K: cannot happen for valid shapes
     float s_sel = 0.0f;
-    if ((bi & 31) == lane) {
-      taken |= 1u << (bi >> 5);
+    if (kind == WM_ROUTER_SOFTMAX) {
+      // the score is the key itself: the winning key, back from its ordered bits
+      s_sel = __uint_as_float((top & 0x80000000u) ? (top & 0x7fffffffu) : ~top);
+      if ((bi & 31) == lane) {
+        taken |= 1u << (bi >> 5);
+        rescan();
+      }
+    } else {
+      if ((bi & 31) == lane) {
+        taken |= 1u << (bi >> 5);
 #pragma unroll
-      for (int j = 0; j < EPL; ++j)
-        if (j == (bi >> 5)) s_sel = score[j];
-      rescan();
+        for (int j = 0; j < EPL; ++j)
+          if (j == (bi >> 5)) s_sel = score[j];
+        rescan();
+      }
+      s_sel = __shfl_sync(0xffffffffu, s_sel, bi & 31);
     }
-    s_sel = __shfl_sync(0xffffffffu, s_sel, bi & 31);
     if (kind == WM_ROUTER_SOFTMAX) {
       if (k == 0) top_logit = s_sel;
       s_sel = expf(s_sel - top_logit);
