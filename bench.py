@@ -30,6 +30,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -56,14 +57,14 @@ def peaks() -> dict:
 class Clocks:
     """nvidia-smi samples during the timed region."""
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, log_dir: str | None = None):
         self.index = index
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_rank{index}.csv"
+        self.path = Path(log_dir or tempfile.gettempdir()) / f"clocks_rank{index}.csv"
 
     def __enter__(self):
         try:
-            self.path.parent.mkdir(exist_ok=True)
+            self.path.parent.mkdir(parents=True, exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index),
@@ -338,7 +339,7 @@ def run_ep(args, world: int, rank: int, local: int) -> None:
             ev[1].record(stream)
 
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    with Clocks(local) as clocks:
+    with Clocks(local, args.clocks_dir) as clocks:
         torch.cuda.synchronize()
         with torch.cuda.stream(stream):
             for i in range(args.warmup):
@@ -526,7 +527,7 @@ def run(args) -> None:
     if world > 1:
         dist.barrier()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    with Clocks(local) as clocks:
+    with Clocks(local, args.clocks_dir) as clocks:
         torch.cuda.synchronize()
         with torch.cuda.stream(stream):
             for i in range(args.steps):
@@ -646,6 +647,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-long", action="store_true", help="skip the config-3 and config-4 long-call sections")
+    ap.add_argument("--clocks-dir", default=None,
+                    help="folder for the raw nvidia-smi clock samples (default: the system temp folder)")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="N > 1: expert-parallel exchanges over peer memory (default) or NCCL all-to-all")
     args = ap.parse_args()
