@@ -627,7 +627,16 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
   ctx->actscale = reinterpret_cast<float*>(base + o_actscale);
   ctx->rowmax = reinterpret_cast<uint32_t*>(base + o_rowmax);
   ctx->xn = reinterpret_cast<uint16_t*>(base + o_xn);
-  cudaMemset(ctx->status, 0, 16);
+  // the whole workspace starts at zero (status word included); padding rows of
+  // the f16 row blocks are never written afterwards, so they hold zeros or an
+  // earlier call's finite rows
+  if (cudaMemset(ctx->ws, 0, ctx->ws_bytes) != cudaSuccess) {
+    cudaGetLastError();
+    report("clearing the workspace failed");
+    cudaFree(ctx->ws);
+    delete ctx;
+    return nullptr;
+  }
   const size_t gemv_smem = wm::gemv_smem_bytes(int(H), int(I));
   if (gemv_smem > size_t(prop.sharedMemPerBlockOptin)) {
     report("max_hidden is too large for the decode GEMV's shared-memory staging");

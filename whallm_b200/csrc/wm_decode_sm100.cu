@@ -590,6 +590,11 @@ __device__ __forceinline__ uint32_t piece_absmax_bits(const uint4 v) {
 // scale[r] = 2^k (largest magnitude of the row lands in [2^14, 2^15)).
 // One warp per sorted row; with NV > 0 (rows of at most 256 NV bf16) the row
 // stays in registers, so it is read once with all its loads in flight.
+// Padding rows (row_token < 0) only get scale 1: their data is left as the
+// workspace holds it (zero from creation, or an earlier call's finite f16
+// row).  Every product and epilogue of the expert kernels is row-local (a row
+// of A gives a row of D, a token column gives a column), and no padding row is
+// read by the combine, so what a padding row holds never reaches an output.
 template <int NV>
 __global__ void __launch_bounds__(256) gather_f16_kernel(const uint16_t* __restrict__ x, Plan p, int E, int H,
                                                          uint16_t* __restrict__ out, float* __restrict__ scale) {
@@ -599,7 +604,11 @@ __global__ void __launch_bounds__(256) gather_f16_kernel(const uint16_t* __restr
   const int pieces = H / 8, per_lane = (pieces + 31) / 32;
   for (int r = blockIdx.x * 8 + (threadIdx.x >> 5); r < rows; r += gridDim.x * 8) {
     const int t = p.row_token[r];
-    const uint4* src = reinterpret_cast<const uint4*>(x + int64_t(t < 0 ? 0 : t) * H);
+    if (t < 0) {
+      if (lane == 0) scale[r] = 1.0f;
+      continue;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(x + int64_t(t) * H);
     uint4* dst = reinterpret_cast<uint4*>(out + int64_t(r) * H);
     if (NV > 0) {
       // the whole row in registers: one read of it, all loads in flight at once
