@@ -297,6 +297,14 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict
   float acc[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+  // the shared expert's row is loaded first (it depends on no pair) and added last
+  uint4 sv = make_uint4(0, 0, 0, 0);
+  float g = 0.0f;
+  if (shared_kind != WM_SHARED_NONE) {
+    g = shared_kind == WM_SHARED_SIGMOID_GATE ? sg[t] : 1.0f;
+    const uint16_t* srow = DENSE ? shared_rows + (int64_t)t * H : routed + (int64_t)(p.offsets[E] + t) * H;
+    sv = *reinterpret_cast<const uint4*>(srow + h0);
+  }
   // eight pairs' loads in flight at a time; the sum keeps k order
   for (int k0 = 0; k0 < K; k0 += 8) {
     int pos[8];
@@ -322,9 +330,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict
     }
   }
   if (shared_kind != WM_SHARED_NONE) {
-    const float g = shared_kind == WM_SHARED_SIGMOID_GATE ? sg[t] : 1.0f;
-    const uint16_t* srow = DENSE ? shared_rows + (int64_t)t * H : routed + (int64_t)(p.offsets[E] + t) * H;
-    const uint4 v = *reinterpret_cast<const uint4*>(srow + h0);
+    const uint4 v = sv;
     float2 f;
     f = unpack_bf16x2(v.x); acc[0] = fmaf(g, f.x, acc[0]); acc[1] = fmaf(g, f.y, acc[1]);
     f = unpack_bf16x2(v.y); acc[2] = fmaf(g, f.x, acc[2]); acc[3] = fmaf(g, f.y, acc[3]);
