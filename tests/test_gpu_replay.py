@@ -50,8 +50,10 @@ def test_replay_equals_forward(T):
     eng.release_replays()
 
 
-def test_replay_rejects_wrong_shape():
+def test_replay_rejects_wrong_shape_and_skips_empty_calls():
     eng = Engine(0, max_tokens=64, hidden=H, inter=I, experts=E, topk=K)
     layer = _layer()
     with pytest.raises(ValueError):
         eng.replay(layer, torch.zeros((4, H + 8), dtype=torch.bfloat16, device=DEV), K)
+    assert eng.replay(layer, torch.zeros((0, H), dtype=torch.bfloat16, device=DEV), K).shape == (0, H)
+    assert not getattr(eng, "_replays", {})

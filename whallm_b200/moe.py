@@ -330,6 +330,11 @@ class Engine:
         layer's tensors.  Calls are stream-ordered on the current stream."""
         T = x.shape[0]
         _check_shape_bf16("x", x, (T, layer.H))
+        if T == 0:  # nothing to run (and nothing worth a graph)
+            if out is None:
+                out = torch.empty((0, layer.H), dtype=torch.bfloat16, device=self.device)
+            _check_shape_bf16("out", out, (0, layer.H))
+            return out
         key = (id(layer), T, K)
         entry = getattr(self, "_replays", {}).get(key)
         if entry is None:
