@@ -13,6 +13,12 @@ the JSON files it writes are committed and the tests read only those.
 * expert_waves.json -- outputs of the reference's own pure-numpy scheduler
   runtime/deepseek_v4_ssd/qwen_expert_waves.py (imported by file path, as the
   reference's portable tests do) on seeded routes.
+* expert_layout.json -- outputs of the reference's own blob-layout code,
+  runtime/deepseek_v4_ssd/expert_layout.py (_fused_slot_regions,
+  _qwen_slot_regions, batched_layer_layout), loaded by file path together with
+  the manifest.py it imports (json / dataclasses / pathlib only): the slot
+  regions of the reference's three expert formats and their region-major
+  placements at several expert counts, plus partitions it refuses.
 """
 from __future__ import annotations
 
@@ -131,6 +137,78 @@ def expert_waves_fixture(ref: Path) -> dict:
             "ref": "runtime/deepseek_v4_ssd/qwen_expert_waves.py:23-51", "cases": cases}
 
 
+def _load_layout_modules(ref: Path):
+    """manifest.py and expert_layout.py as one package (expert_layout imports .manifest)."""
+    import types
+    pkg_dir = ref / "runtime/deepseek_v4_ssd"
+    pkg = types.ModuleType("_ref_ds")
+    pkg.__path__ = [str(pkg_dir)]
+    sys.modules["_ref_ds"] = pkg
+    mods = {}
+    for name in ("manifest", "expert_layout"):
+        spec = importlib.util.spec_from_file_location(f"_ref_ds.{name}", pkg_dir / f"{name}.py")
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[spec.name] = mod
+        spec.loader.exec_module(mod)
+        mods[name] = mod
+    return mods["manifest"], mods["expert_layout"]
+
+
+def expert_layout_fixture(ref: Path) -> dict:
+    manifest, layout = _load_layout_modules(ref)
+    from types import SimpleNamespace
+
+    def regions_json(regs):
+        return {n: [r.offset, r.length] for n, r in regs.items()}
+
+    formats = []
+    for label, table, kind in (("deepseek", manifest.EXPERT_REGIONS, "fused"),
+                               ("deepseek_v41", manifest.DEEPSEEK_V41_EXPERT_REGIONS, "fused"),
+                               ("qwen", manifest.QWEN_EXPERT_REGIONS, "qwen")):
+        tensors = tuple(manifest.Tensor(n, d, tuple(sh), off, ln) for n, d, sh, off, ln in table)
+        model = SimpleNamespace(expert_regions=tensors, expert_blob_size=sum(t.length for t in tensors))
+        if kind == "fused":
+            regs = layout._fused_slot_regions(model)
+            batched = layout.FusedMXFP4Layout.batched_regions
+        else:
+            regs = layout._qwen_slot_regions(model)
+            batched = layout.GateUpMXFP4Layout.batched_regions
+        w1 = {n: sh for n, _, sh, _, _ in table}
+        if kind == "fused":
+            inter, hidden = w1["w1.weight"][0], 2 * w1["w1.weight"][1]
+        else:
+            inter, hidden = w1["gate_up.weight"][0] // 2, 8 * w1["gate_up.weight"][1]
+        placements = {}
+        for experts in (1, 3, 384):
+            got = layout.batched_layer_layout(regs, batched, model.expert_blob_size, experts)
+            placements[str(experts)] = {n: list(v) for n, v in got.items()}
+        formats.append({"name": label, "kind": kind, "hidden": hidden, "inter": inter,
+                        "blob_size": model.expert_blob_size, "batched": list(batched),
+                        "regions": regions_json(regs), "placements": placements})
+
+    # partitions the reference refuses (gap, short cover, region outside every batched region)
+    tensors = {n: manifest.Tensor(n, "U8", (1,), off, ln) for n, off, ln in
+               (("a", 0, 16), ("b", 16, 8), ("c", 24, 40), ("inner", 20, 4), ("straddle", 12, 8))}
+    refused = []
+    for names, batched, blob in ((("a", "c"), ("a", "c"), 64), (("a", "b", "c"), ("a", "b", "c"), 65),
+                                 (("a", "b", "c", "straddle"), ("a", "b", "c"), 64)):
+        regs = {n: tensors[n] for n in names}
+        try:
+            layout.batched_layer_layout(regs, batched, blob, 2)
+            refused.append({"regions": regions_json(regs), "batched": list(batched), "blob_size": blob,
+                            "refused": False})
+        except ValueError:
+            refused.append({"regions": regions_json(regs), "batched": list(batched), "blob_size": blob,
+                            "refused": True})
+    regs = {n: tensors[n] for n in ("a", "b", "c", "inner")}
+    accepted = {n: list(v) for n, v in layout.batched_layer_layout(regs, ("a", "b", "c"), 64, 5).items()}
+    return {"generator": "tests/golden/make_golden.py",
+            "ref": "runtime/deepseek_v4_ssd/expert_layout.py:8-119, manifest.py:17-45",
+            "formats": formats, "refused": refused,
+            "nested": {"regions": regions_json(regs), "batched": ["a", "b", "c"], "blob_size": 64, "experts": 5,
+                       "placements": accepted}}
+
+
 def main() -> None:
     if len(sys.argv) != 2:
         raise SystemExit("usage: make_golden.py <reference checkout root>")
@@ -139,6 +217,8 @@ def main() -> None:
     (OUT / "mxfp4_kat.json").write_text(json.dumps(kat, separators=(",", ":")) + "\n")
     waves = expert_waves_fixture(ref)
     (OUT / "expert_waves.json").write_text(json.dumps(waves, separators=(",", ":")) + "\n")
+    lay = expert_layout_fixture(ref)
+    (OUT / "expert_layout.json").write_text(json.dumps(lay, separators=(",", ":")) + "\n")
     for case in kat["cases"]:
         print(case["name"], {k: (len(v) if isinstance(v, list) else v) for k, v in case.items() if k != "name"})
     print("waves cases:", len(waves["cases"]))

@@ -47,3 +47,47 @@ def test_projection_strides_follow_region_major_views():
     s = torch.zeros(10, 4, 2, dtype=torch.uint8)
     p = L.Projection.stacked(w, s)
     assert p.weight_stride == 96 and p.scale_stride == 8
+
+
+# ---------------------------------------------------------------- pinned by the reference's own layout code
+import json
+from pathlib import Path
+
+GOLDEN = json.loads((Path(__file__).resolve().parent / "golden" / "expert_layout.json").read_text())
+
+
+def _regions(table: dict) -> dict:
+    return {n: L.Region(n, "U8", (1,), off, ln) for n, (off, ln) in table.items()}
+
+
+@pytest.mark.parametrize("fmt", GOLDEN["formats"], ids=[f["name"] for f in GOLDEN["formats"]])
+def test_slot_regions_match_reference(fmt):
+    """qwen_regions / fused_regions give the reference's slot regions (expert_layout.py:8-80)."""
+    mine = (L.fused_regions if fmt["kind"] == "fused" else L.qwen_regions)(fmt["hidden"], fmt["inter"])
+    assert {n: [r.offset, r.length] for n, r in mine.items()} == fmt["regions"]
+    batched = L.FUSED_BATCHED if fmt["kind"] == "fused" else L.QWEN_BATCHED
+    assert list(batched) == fmt["batched"]
+    assert L.blob_size(mine, batched) == fmt["blob_size"]
+
+
+@pytest.mark.parametrize("fmt", GOLDEN["formats"], ids=[f["name"] for f in GOLDEN["formats"]])
+def test_batched_layer_layout_matches_reference(fmt):
+    """batched_layer_layout places every region where expert_layout.py:83-119 does."""
+    regs = _regions(fmt["regions"])
+    for experts, want in fmt["placements"].items():
+        got = L.batched_layer_layout(regs, tuple(fmt["batched"]), fmt["blob_size"], int(experts))
+        assert {n: list(v) for n, v in got.items()} == want
+
+
+def test_batched_layer_layout_refuses_what_reference_refuses():
+    for case in GOLDEN["refused"]:
+        regs = _regions(case["regions"])
+        if case["refused"]:
+            with pytest.raises(ValueError):
+                L.batched_layer_layout(regs, tuple(case["batched"]), case["blob_size"], 2)
+        else:
+            L.batched_layer_layout(regs, tuple(case["batched"]), case["blob_size"], 2)
+    nested = GOLDEN["nested"]
+    got = L.batched_layer_layout(_regions(nested["regions"]), tuple(nested["batched"]), nested["blob_size"],
+                                 nested["experts"])
+    assert {n: list(v) for n, v in got.items()} == nested["placements"]

@@ -7,6 +7,7 @@ an expert's projection is addressed as ``base + e * stride``.
 """
 from __future__ import annotations
 
+import bisect
 from dataclasses import dataclass
 from typing import NamedTuple
 
@@ -82,30 +83,39 @@ def blob_size(regions: dict[str, Region], batched: tuple[str, ...]) -> int:
 
 def batched_layer_layout(regions: dict[str, Region], batched: tuple[str, ...], blob_size: int,
                          expert_count: int) -> dict[str, tuple[int, int, int]]:
-    """Place every slot region in a region-major layer buffer; returns
-    name -> (base, stride, inner): expert e of `name` starts at
-    base + e * stride + inner (expert_layout.py:83-119, same contract)."""
-    spans = sorted((regions[name].offset, regions[name].length, name) for name in batched)
-    expected = 0
-    for offset, length, name in spans:
-        if offset != expected:
-            raise ValueError(f"batched expert region {name} does not partition the slot")
-        expected += length
-    if expected != blob_size:
-        raise ValueError("batched expert regions do not cover the expert slot")
-    bases, base = {}, 0
-    for offset, length, name in spans:
-        bases[name] = (base, offset, length)
-        base += expert_count * length
-    layout = {}
-    for name, region in regions.items():
-        for owner_base, owner_offset, owner_length in bases.values():
-            if owner_offset <= region.offset and region.offset + region.length <= owner_offset + owner_length:
-                layout[name] = (owner_base, owner_length, region.offset - owner_offset)
-                break
-        else:
-            raise ValueError(f"expert slot region {name} is outside every batched region")
-    return layout
+    """Where every region of an expert blob lands in a region-major layer buffer.
+
+    The layer buffer holds the `batched` regions one after another in blob
+    order, each repeated for all `expert_count` experts, so every batched
+    region is one contiguous [E, ...] array.  Returns name -> (base, stride,
+    inner) for every region of `regions`: expert e's bytes of `name` start at
+    base + e * stride + inner, where (base, stride) belong to the batched
+    region that contains it.  This is the contract of the reference's
+    batched_layer_layout (runtime/deepseek_v4_ssd/expert_layout.py:83-119);
+    the batched regions must tile [0, blob_size) exactly."""
+    tiles = sorted((regions[n].offset, regions[n].length, n) for n in batched)
+    # tiling check: each batched region starts where the previous one ended
+    cursor = 0
+    for offset, length, name in tiles:
+        if offset != cursor:
+            raise ValueError(f"batched region {name} at byte {offset} leaves a gap or an overlap in the expert blob "
+                             f"(expected byte {cursor})")
+        cursor = offset + length
+    if cursor != blob_size:
+        raise ValueError(f"batched regions span {cursor} bytes of a {blob_size}-byte expert blob")
+    # layer-buffer base of each tile: the tiles before it, each expert_count times
+    ends = [offset + length for offset, length, _ in tiles]
+    bases = [0] * len(tiles)
+    for j in range(1, len(tiles)):
+        bases[j] = bases[j - 1] + expert_count * tiles[j - 1][1]
+    placed = {}
+    for name, reg in regions.items():
+        # the first tile (in blob order) whose end reaches this region's end
+        j = bisect.bisect_left(ends, reg.offset + reg.length)
+        if j == len(tiles) or tiles[j][0] > reg.offset:
+            raise ValueError(f"region {name} does not lie inside one batched region")
+        placed[name] = (bases[j], tiles[j][1], reg.offset - tiles[j][0])
+    return placed
 
 
 QWEN_BATCHED = ("gate_up.weight", "gate_up.scale", "down.weight", "down.scale")

@@ -22,28 +22,39 @@ import numpy as np
 
 @dataclass(frozen=True)
 class ExpertWave:
+    """One wave: (expert id, positions into the flattened routes) per expert,
+    experts ascending, positions ascending within an expert."""
     groups: tuple[tuple[int, np.ndarray], ...]
 
     @property
     def expert_ids(self) -> tuple[int, ...]:
-        return tuple(expert for expert, _ in self.groups)
+        return tuple(g[0] for g in self.groups)
+
+
+def _count_arg(value, what: str) -> int:
+    # plain ints only: bools, floats and numpy scalars are refused, as the reference does
+    if isinstance(value, bool) or not isinstance(value, int) or value <= 0:
+        raise ValueError(f"{what} must be a positive integer, got {value!r}")
+    return value
+
+
+def _flat_routes(indices, expert_count: int) -> np.ndarray:
+    routes = np.asarray(indices).reshape(-1)
+    if routes.size and routes.dtype.kind not in "iu":
+        raise ValueError(f"routes must hold integer expert ids, not {routes.dtype}")
+    if routes.size and (routes.min() < 0 or routes.max() >= expert_count):
+        raise ValueError(f"an expert id lies outside [0, {expert_count})")
+    return routes
 
 
 def expert_waves(indices, capacity: int, expert_count: int) -> Iterator[ExpertWave]:
     """Visit every flattened routing pair exactly once, in stable expert order,
     at most `capacity` experts per wave; positions index the flattened routes."""
-    if type(capacity) is not int or capacity < 1:
-        raise ValueError("expert wave capacity must be a positive integer")
-    if type(expert_count) is not int or expert_count < 1:
-        raise ValueError("expert count must be a positive integer")
-    selected = np.asarray(indices)
-    if selected.size == 0:
+    _count_arg(capacity, "wave capacity")
+    _count_arg(expert_count, "expert count")
+    flat = _flat_routes(indices, expert_count)
+    if flat.size == 0:
         return
-    if not np.issubdtype(selected.dtype, np.integer):
-        raise ValueError("expert IDs must be integers")
-    flat = selected.reshape(-1)
-    if np.any(flat < 0) or np.any(flat >= expert_count):
-        raise ValueError("expert ID is outside the model")
     # counting sort: bucket sizes, then positions in ascending order per bucket
     counts = np.bincount(flat, minlength=expert_count)
     order = np.argsort(flat, kind="stable")
