@@ -248,6 +248,140 @@ def lib_layout_fp8() -> int:
     return lib.LAYOUT_W13_FP8_B128
 
 
+# Expert-parallel long-call sections (strong scaling: the tokens and the
+# routed experts split evenly over the ranks; router and shared expert on
+# every rank).  config 3: one DeepSeek-style FP8 layer, 8192 tokens.  config 4:
+# the 8-layer MXFP4 stack, 256 decode + 4096 prefill tokens per step, bf16
+# residual adds between layers.
+EP_SECTIONS = {
+    3: ("ep_config3", "config3 FP8 layer (H=7168, 256 experts of I=2048 + shared, sigmoid group-limited top-8), "
+                      "8192 tokens per step split over the GPUs"),
+    4: ("config4_stack", "config4 8-layer MXFP4 stack (H=7168, 384 experts of I=2048 + shared, top-8), "
+                         "256 decode + 4096 prefill tokens per step split over the GPUs, bf16 residual adds"),
+}
+
+
+def long_ep_section(args, n: int, world: int, rank: int, local: int, pk: dict) -> dict:
+    """Config n (3 or 4) over `world` GPUs, expert-parallel over NVLink peer
+    memory when world > 1.  Every rank holds the whole model (so it can check
+    its expert-parallel result against the one-GPU result bit for bit, and
+    rank 0 can time the whole batch on one GPU in the same run); the
+    expert-parallel step reads only the rank's shard of the routed experts."""
+    import torch
+    import torch.distributed as dist
+
+    from whallm_b200 import synth
+    from whallm_b200.ep import ExpertParallelMoE
+    from whallm_b200.moe import Engine
+
+    dev = torch.device("cuda", local)
+    if n == 3:
+        layers, T_total = [synth.deepseek_fp8_layer(device=dev, seed=0)], 8192
+    else:
+        layers, T_total = [synth.deepseek_mxfp4_layer(device=dev, seed=l) for l in range(8)], 256 + 4096
+    lay0 = layers[0]
+    Hn, In, En, Kn = lay0.H, lay0.I, lay0.E, 8
+    if T_total % world or En % world:
+        return {"workload": EP_SECTIONS[n][1], "skipped": f"{T_total} tokens / {En} experts do not split over {world}"}
+    T_loc = T_total // world
+    x_all = synth.activations(T_total, Hn, torch.Generator(device=dev).manual_seed(1), dev)
+    x = x_all[rank * T_loc:(rank + 1) * T_loc].contiguous()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    steps = max(3, min(args.steps, 10))
+
+    def stack(fwd, h):
+        for i, lay in enumerate(layers):
+            y = fwd(i, lay, h)
+            h = y if len(layers) == 1 else h + y  # bf16 residual add between layers
+        return h
+
+    def timed(fwd, h0, nsteps):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(nsteps)]
+        for i in range(nsteps):
+            flush.zero_()
+            evs[i][0].record()
+            stack(fwd, h0)
+            evs[i][1].record()
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in evs) / nsteps
+
+    # one GPU, the whole batch (rank 0; the grouped GEMM throughout)
+    single = None
+    if rank == 0:
+        eng1 = Engine(local, max_tokens=T_total, hidden=Hn, inter=In, experts=En, topk=Kn, gemv_max_tokens=-1)
+        fwd1 = lambda i, lay, h: eng1.forward(lay, h, Kn)  # noqa: E731
+        for _ in range(2):
+            stack(fwd1, x_all)
+        torch.cuda.synchronize()
+        single = T_total / (timed(fwd1, x_all, steps) / 1e3)
+        eng1.ctx.close()
+        del eng1
+    out = {"workload": EP_SECTIONS[n][1], "tokens_per_step": T_total, "tokens_per_gpu": T_loc, "layers": len(layers),
+           "l2": "flushed (256 MB write) before every timed step"}
+    if world == 1:
+        out.update({"tokens_per_s": single, "ms_per_step": T_total / single * 1e3, "single_gpu_tokens_per_s": single,
+                    "efficiency": 1.0, "parallelism": "single GPU"})
+        torch.cuda.empty_cache()
+        return out
+
+    # expert parallel: routing / combine handle, owner handle (single routes
+    # from every peer), shared-expert handle; one exchange buffer for all layers
+    C = T_loc * Kn
+    eng = Engine(local, max_tokens=T_loc, hidden=Hn, inter=In, experts=En, topk=Kn, gemv_max_tokens=-1)
+    owner = Engine(local, max_tokens=world * C, hidden=Hn, inter=In, experts=En // world, topk=1,
+                   gemv_max_tokens=-1)
+    shared = Engine(local, max_tokens=T_loc, hidden=Hn, inter=In, experts=1, topk=1, gemv_max_tokens=-1)
+    eps = []
+    for lay in layers:
+        eps.append(ExpertParallelMoE(eng, lay, Kn, shared_engine=shared, fixed_capacity=T_loc, peer_memory=True,
+                                     owner_engine=owner, peer_buffer=eps[0].ep_buf if eps else None))
+    fwd = lambda i, lay, h: eps[i](h)  # noqa: E731
+    for _ in range(2):
+        stack(fwd, x)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = timed(fwd, x, steps)
+    t = torch.tensor([ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    # per-kernel split of one step on this rank (library events, eager)
+    for e_ in (eng, owner, shared):
+        e_.ctx.profile(True)
+        e_.ctx.profile_reset()
+    stack(fwd, x)
+    torch.cuda.synchronize()
+    kernels = {}
+    for tag, e_ in (("", eng), ("owner_", owner), ("shared_", shared)):
+        for name, (c, tt) in e_.ctx.profile_read().items():
+            kernels[tag + name] = {"launches": c, "avg_us": 1e3 * tt / c, "total_us": 1e3 * tt}
+        e_.ctx.profile(False)
+    # parity: the expert-parallel stack against the one-GPU stack on this rank's tokens
+    got = stack(fwd, x)
+    ref_eng = Engine(local, max_tokens=T_loc, hidden=Hn, inter=In, experts=En, topk=Kn, gemv_max_tokens=-1)
+    want = stack(lambda i, lay, h: ref_eng.forward(lay, h, Kn), x)
+    torch.cuda.synchronize()
+    exact = torch.tensor([1.0 if torch.equal(got.view(torch.int16), want.view(torch.int16)) else 0.0], device=dev)
+    max_abs = (got.float() - want.float()).abs().max().reshape(1)
+    dist.all_reduce(exact, op=dist.ReduceOp.MIN)
+    dist.all_reduce(max_abs, op=dist.ReduceOp.MAX)
+    eps[0].close()  # the shared exchange buffer (collective)
+    for e_ in (eng, owner, shared, ref_eng):
+        e_.ctx.close()
+    tps = T_total / (ms / 1e3)
+    top = max(kernels.items(), key=lambda kv: kv[1]["total_us"])[0] if kernels else None
+    out.update({"tokens_per_s": tps, "ms_per_step": ms, "parallelism": f"expert-parallel x{world} "
+                f"({En // world} experts per GPU per layer), NVLink peer-memory exchanges",
+                "single_gpu_tokens_per_s": single,
+                "efficiency": (tps / (world * single)) if single else None,
+                "efficiency_note": "tokens/s over N GPUs / (N x one GPU's tokens/s on the whole batch, rank 0, same run)",
+                "parity": {"bit_exact": bool(exact.item() == 1.0), "max_abs": float(max_abs.item()),
+                           "against": "the one-GPU stack on each rank's tokens (grouped GEMM on both)"},
+                "kernels_rank0_per_step": kernels if rank == 0 else None, "limiting_kernel": top})
+    del eps, layers
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ep(args, world: int, rank: int, local: int) -> None:
     """--gpus N > 1: the config-1 layer expert-parallel over N ranks."""
     import torch
@@ -397,7 +531,31 @@ def run_ep(args, world: int, rank: int, local: int) -> None:
     e_ms = float(t.item())
     e2e = world * B * args.steps / (e_ms / 1e3)
     del graph  # holds NCCL work: release before the process group goes
+
+    # parity: each rank's expert-parallel layer against the one-GPU layer on the same tokens (decode kernels on both)
+    exact, max_abs = torch.ones(1, device=dev), torch.zeros(1, device=dev)
+    with torch.cuda.stream(stream):
+        for i in range(nb):
+            got = fwd(xs[i]).clone()
+            want = eng.forward(layer, xs[i], K)
+            if not torch.equal(got.view(torch.int16), want.view(torch.int16)):
+                exact.zero_()
+            max_abs = torch.maximum(max_abs, (got.float() - want.float()).abs().max().reshape(1))
+    torch.cuda.synchronize()
+    dist.all_reduce(exact, op=dist.ReduceOp.MIN)
+    dist.all_reduce(max_abs, op=dist.ReduceOp.MAX)
+    parity = {"bit_exact": bool(exact.item() == 1.0), "max_abs": float(max_abs.item()),
+              "against": f"the one-GPU layer on every rank's {nb} batches"}
     ep.close()
+    eng.ctx.close()
+    shared_eng.ctx.close()
+    del ep, eng, shared_eng
+    torch.cuda.empty_cache()
+    long_sections = {}
+    if not args.no_long:
+        pk = peaks()
+        for n in (3, 4):
+            long_sections[EP_SECTIONS[n][0]] = long_ep_section(args, n, world, rank, local, pk)
     dist.barrier()
     dist.destroy_process_group()
     if rank != 0:
@@ -425,6 +583,8 @@ def run_ep(args, world: int, rank: int, local: int) -> None:
                 "d2h_bytes_per_step": world * B * H * 2},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
+        "parity": parity,
+        **long_sections,
     }
     print(json.dumps(line), flush=True)
 
@@ -604,8 +764,11 @@ def run(args) -> None:
     decode_batches = [decode_batch_line(eng, layer, dev, b, max(10, min(args.steps, 30)), flush) for b in (1, 8)]
     prefill = None if args.no_prefill else prefill_section(args, dev, pk, 2)
     long_calls = None
+    long_sections = {}
     if not args.no_prefill and not args.no_long:
         long_calls = {"config3": prefill_section(args, dev, pk, 3), "config4_layer": prefill_section(args, dev, pk, 4)}
+        for n in (3, 4):
+            long_sections[EP_SECTIONS[n][0]] = long_ep_section(args, n, 1, 0, local, pk)
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
@@ -632,6 +795,7 @@ def run(args) -> None:
         "decode_batches": decode_batches,
         "prefill": prefill,
         "long_calls": long_calls,
+        **long_sections,
     }
     print(json.dumps(line), flush=True)
 

@@ -172,7 +172,8 @@ typedef struct {
   int64_t calls_forward, calls_pairs, calls_route, calls_dequant;
   int64_t launches;            /* kernels enqueued by this handle */
   int64_t gemv_calls, gemm_calls;
-  int64_t decode_calls;        /* calls that took the tcgen05 decode kernels */
+  int64_t decode_calls;        /* calls that took the decode kernels (register-direct mma.sync kernel by
+                                  default, the tcgen05 one with WM_FLAG_TCGEN05_DECODE) */
 } wm_counters;
 
 typedef struct {
@@ -277,6 +278,19 @@ WM_EXPORT int wm_ep_dispatch(wm_ctx* ctx, wm_ep* ep, int64_t T, int32_t K, int32
                              const int32_t* idx, const void* x, int32_t* pair_pos, void* stream);
 WM_EXPORT int wm_ep_return(wm_ctx* ctx, wm_ep* ep, const void* y, void* stream);
 WM_EXPORT int wm_ep_wait(wm_ctx* ctx, wm_ep* ep, int32_t which, void* stream);
+/* The owner's half of a step, in place of wm_expert_pairs + wm_ep_return
+   (call it after wm_ep_wait(0)): this rank's experts applied to the rows its
+   peers dispatched to it -- only the real ones, each sender records how many
+   it sent -- and every result row stored straight from the sorted expert
+   rows into its sender's `back` block, then the return flags raised (wait
+   with wm_ep_wait(1)).  args gives this rank's experts (E = experts_per_rank,
+   layout, H equal to the buffer's, I, w13, w2, swiglu_limit); x, routes,
+   router, norm and shared fields are ignored; args->T is the number of rows
+   this rank expects to receive, in [1, world * capacity], which picks the
+   expert kernels as for a call of T single routes (decode kernels or grouped
+   GEMM).  The handle must hold world * capacity tokens.  No counterpart in
+   the reference, whose experts run on one device. */
+WM_EXPORT int wm_ep_experts(wm_ctx* ctx, wm_ep* ep, const wm_moe_args* args, void* stream);
 
 /* The whole MoE block: route, sort, experts, shared expert, combine
    (SparseMoE.__call__, qwen4_exp.py:1015-1051; _streaming_moe, model.py:526-546;
@@ -286,16 +300,28 @@ WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* args, void* stream)
 /* The decode MoE block (router if router_weight is set, sort, expert GEMVs,
    shared expert, combine -- the same kernels as wm_moe_forward's decode
    path) for callers that cannot allocate device memory: there is no handle,
-   and all scratch lives in one static device array of 8 MiB that the CUDA
-   runtime reserves on every GPU that loads this library until the process
-   exits.  A call whose scratch would exceed it (roughly: (T*K + T) * (H + I)
-   * 2 bytes plus routing arrays) fails with status 1 and a message in
-   error[0 .. error_size).  The first call on a device looks up the array's
-   device address; make it before any stream capture.  Calls share the array:
-   calls that overlap on the GPU race, so serialise them.  Expert ids are not
-   range-checked on the host.  This entry point has no counterpart in the
-   reference. */
+   and all scratch lives in one static device array of 8 MiB per GPU, which
+   the CUDA runtime reserves when it loads the library's module on that GPU
+   and keeps until the process exits.  CUDA loads modules lazily by default,
+   so that happens during the first call on a device (which also looks up the
+   array's device address): make the first call, or a call of
+   wm_moe_forward_noalloc_status, at start-up, before device memory is fixed
+   and before any stream capture, or set CUDA_MODULE_LOADING=EAGER.  A call
+   whose scratch would exceed the array (roughly: (T*K + T) * (H + I) * 2
+   bytes plus routing arrays) fails with status 1 and a message in
+   error[0 .. error_size).  Calls share the array: calls that overlap on the
+   GPU race, so serialise them.  Expert ids of caller-given routes are checked
+   on the device, not the host: a route outside [0, E) adds nothing to its
+   token's output and is recorded in the array's status words, which
+   wm_moe_forward_noalloc_status reports (FP8 NaN codes are not checked on
+   this path; wm_moe_forward reports them).  This entry point has
+   no counterpart in the reference. */
 WM_EXPORT int wm_moe_forward_noalloc(const wm_moe_args* args, void* stream, char* error, size_t error_size);
+/* Waits for `stream`, then reports the errors that the kernels of the last
+   wm_moe_forward_noalloc call on the current device recorded: 0 when none,
+   1 with the message in error[0 .. error_size) otherwise (an expert id
+   outside [0, E)).  Each call clears the record when it starts.  Allocates nothing; no counterpart in the reference. */
+WM_EXPORT int wm_moe_forward_noalloc_status(void* stream, char* error, size_t error_size);
 
 /* Per-kernel-group timing with CUDA events recorded on the calls' streams
    (the counterpart of the native engines' gpu_seconds counters,

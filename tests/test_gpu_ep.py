@@ -95,18 +95,104 @@ def _worker(rank: int, world: int, port: int, mode: str, q) -> None:
         dist.destroy_process_group()
 
 
+# every world size the box can hold (2, 4, 8); a 1-GPU box runs the one-rank tests only
+WORLDS = [w for w in (2, 4, 8) if w <= torch.cuda.device_count()] or [2]
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("world", WORLDS)
 @pytest.mark.parametrize("mode", list(MODES))
-def test_ep_two_ranks_equal_single_gpu(mode):
+def test_ep_ranks_equal_single_gpu(mode, world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
     for p in procs:
         p.start()
-    res = sorted(q.get(timeout=300) for _ in range(2))
+    res = sorted(q.get(timeout=300) for _ in range(world))
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
     for rank, equal, diff in res:
         assert equal, f"rank {rank}: expert-parallel output differs from one GPU (max abs diff {diff})"
+
+
+def _gemm_layer(layout, E, H, I, seed):
+    """A small layer of the expert-parallel long-call configs (FP8 128x128 or DS MXFP4) with a shared expert."""
+    from whallm_b200.layout import Projection
+    from whallm_b200.moe import LayerWeights, RouterWeights, SharedExpert
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    proj = synth.projection_for(layout)
+    w13, s13 = proj(E, 2 * I, H, g, "cuda")
+    w2, s2 = proj(E, H, I, g, "cuda")
+    a, b = proj(1, 2 * I, H, g, "cuda")
+    c, d = proj(1, H, I, g, "cuda")
+    wr = (torch.randn((E, H), generator=g, device="cuda") / H ** 0.5).to(torch.bfloat16)
+    return LayerWeights(layout, H, I, E, Projection.stacked(w13, s13), Projection.stacked(w2, s2),
+                        shared=SharedExpert(Projection.stacked(a, b), Projection.stacked(c, d), lib.SHARED_ONE),
+                        router=RouterWeights(wr, lib.ROUTER_SIGMOID))
+
+
+@pytest.mark.parametrize("layout", [lib.LAYOUT_W13_FP8_B128, lib.LAYOUT_DS_W13_MXFP4])
+def test_ep_grouped_gemm_owner_equals_forward(layout):
+    """The owner half on the grouped GEMM (wm_ep_experts: plan over the real
+    rows of each block, experts, result rows straight back from the sorted
+    rows) over peer memory, one rank: bit-identical to the one-GPU layer on
+    the grouped GEMM, two steps in a row, and within tolerance of the oracle."""
+    from whallm_b200.ep import ExpertParallelMoE
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{_free_port()}", rank=0, world_size=1,
+                            device_id=torch.device("cuda", 0))
+    try:
+        E_, H_, I_, K_, T_ = 16, 1024, 512, 4, 300
+        layer = _gemm_layer(layout, E_, H_, I_, seed=90 + layout)
+        x = synth.activations(T_, H_, torch.Generator(device="cuda").manual_seed(91), "cuda")
+        eng = Engine(0, max_tokens=T_, hidden=H_, inter=I_, experts=E_, topk=K_, gemv_max_tokens=-1)
+        owner = Engine(0, max_tokens=T_ * K_, hidden=H_, inter=I_, experts=E_, topk=1, gemv_max_tokens=-1)
+        shared = Engine(0, max_tokens=T_, hidden=H_, inter=I_, experts=1, topk=1, gemv_max_tokens=-1)
+        ep = ExpertParallelMoE(eng, layer, K_, shared_engine=shared, fixed_capacity=T_, peer_memory=True,
+                               owner_engine=owner)
+        got, got2 = ep(x), ep(x)
+        want, (w, idx) = eng.forward(layer, x, K_, return_routes=True)
+        eng.sync()
+        owner.sync()
+        assert owner.ctx.counters().gemm_calls == 2
+        assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+        assert torch.equal(got2.view(torch.int16), want.view(torch.int16))
+        ep.close()
+        tokens = np.arange(0, T_, 37, dtype=np.int32)
+        ref = adapter.from_layer(layer).forward(adapter.bits(x), idx.cpu().numpy(), w.cpu().numpy(), tokens=tokens)
+        err = oracle.max_rel_error(oracle.bf16_to_f32(adapter.bits(got)[tokens]), oracle.bf16_to_f32(ref[tokens]))
+        assert err <= TOL
+        for e_ in (eng, owner, shared):
+            e_.ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_wait_times_out_without_a_peer_and_handle_stays_usable():
+    """The bounded flag wait gives up when no peer ever signals: a dispatch
+    bumps the step number, then a wait for returned rows that no peer sends
+    (no wm_ep_return) runs out after its 2 s limit, records the timeout in
+    the device status (wm_sync reports it) and returns -- the GPU and the
+    handle stay usable, and a normal layer call then succeeds."""
+    wl = synth.config(1, device="cuda", batch=8)
+    eng = _engine(0, 1)
+    buf = lib.EpBuffer(0, 1, 0, 8 * K, H)
+    try:
+        x = wl.x
+        _, idx = eng.route(wl.layer, x, K)
+        pair_pos = torch.empty((8, K), dtype=torch.int32, device="cuda")
+        stream = torch.cuda.current_stream().cuda_stream
+        eng.ctx.ep_dispatch(buf, 8, K, E, idx.data_ptr(), x.data_ptr(), pair_pos.data_ptr(), stream)
+        eng.ctx.ep_wait(buf, 0, stream)  # this rank's own dispatch flag: arrives
+        eng.sync()
+        eng.ctx.ep_wait(buf, 1, stream)  # nothing returns the rows: runs out
+        with pytest.raises(lib.WMError, match="return wait timed out"):
+            eng.sync()
+        eng.sync()  # the record was cleared when it was reported
+        out = eng.forward(wl.layer, x, K)
+        eng.sync()
+        assert torch.isfinite(out.float()).all()
+    finally:
+        buf.close()
+        eng.ctx.close()

@@ -110,6 +110,35 @@ def _check_sampled(layer, x, out, w, idx, tokens):
     return rel(got, ref)
 
 
+def _coverage_sample(idx: torch.Tensor, E: int, rng: np.random.Generator, n_random: int, tile: int = 128,
+                     groups: int = 0) -> np.ndarray:
+    """Tokens for a sampled oracle check of a full-size call: random ones plus
+    the tokens that reach the most popular expert (its last one included), the
+    last token of experts whose rows end in a partial 128-row tile (the sorted
+    rows keep (token, k) order, so an expert's last token owns its last row),
+    the first and last token (the shared expert's first and last rows) and,
+    with `groups`, tokens reaching every expert group."""
+    ii = idx.cpu().numpy()
+    T = ii.shape[0]
+    counts = np.bincount(ii.reshape(-1), minlength=E)
+    head = int(counts.argmax())
+    head_tokens = np.flatnonzero((ii == head).any(axis=1))
+    picks = set(rng.choice(T, n_random, replace=False).tolist())
+    picks.update(head_tokens[:: max(1, head_tokens.size // 7)][:7].tolist())
+    picks.add(int(head_tokens[-1]))
+    partial = [e for e in np.argsort(-counts) if counts[e] % tile and counts[e] > tile][:8]
+    partial += [e for e in np.argsort(counts) if 0 < counts[e] < tile][:4]
+    for e in partial:
+        picks.add(int(np.flatnonzero((ii == e).any(axis=1))[-1]))
+    picks.update((0, T - 1))
+    if groups:
+        size = E // groups
+        for g_ in range(groups):
+            hit = np.flatnonzero(((ii // size) == g_).any(axis=1))
+            picks.update(hit[:2].tolist())
+    return np.array(sorted(picks), dtype=np.int64)
+
+
 def test_config2_prefill_full_size():
     wl = synth.config(2, device=DEV)
     eng = Engine(0, max_tokens=16384, hidden=2048, inter=512, experts=512, topk=10)
@@ -119,7 +148,8 @@ def test_config2_prefill_full_size():
     assert torch.isfinite(out.float()).all()
     counts = torch.bincount(idx.reshape(-1).long(), minlength=512)
     assert counts.sum().item() == 16384 * 10 and counts.max().item() > 20 * counts.float().median().item()
-    tokens = np.random.default_rng(0).choice(16384, 16, replace=False)
+    tokens = _coverage_sample(idx, 512, np.random.default_rng(0), 40)
+    assert tokens.size >= 64
     assert _check_sampled(wl.layer, wl.x, out, w, idx, tokens) <= TOL
     eng.ctx.close()
 
@@ -134,6 +164,43 @@ def test_config3_fp8_full_size():
     groups = (idx.long() // 32)
     per_token = [torch.unique(r).numel() for r in groups[:256]]
     assert max(per_token) <= 4
-    tokens = np.random.default_rng(1).choice(8192, 3, replace=False)
+    tokens = _coverage_sample(idx, 256, np.random.default_rng(1), 30, groups=8)
+    assert tokens.size >= 64
+    hit_groups = set((idx.cpu().numpy()[tokens] // 32).reshape(-1).tolist())
+    assert hit_groups == set(range(8))
     assert _check_sampled(wl.layer, wl.x, out, w, idx, tokens) <= TOL
     eng.ctx.close()
+    del wl, eng
+    torch.cuda.empty_cache()
+
+
+def test_config4_layer_full_size():
+    """One layer of the config-4 stack at its shape -- H=7168, 384 MXFP4
+    experts of I=2048 (w13 = [w3; w1]), ungated shared expert, sigmoid top-8,
+    256 decode + 4096 prefill tokens in one call (grouped GEMM) -- against the
+    oracle on sampled tokens, with the routes checked against the oracle
+    router; then a decode-sized call of 8 tokens (decode kernels)."""
+    wl = synth.config(4, device=DEV)
+    layer = wl.layer
+    T = wl.x.shape[0]
+    eng = Engine(0, max_tokens=T, hidden=7168, inter=2048, experts=384, topk=8)
+    out, (w, idx) = eng.forward(layer, wl.x, wl.K, return_routes=True)
+    eng.sync()
+    assert eng.ctx.counters().gemm_calls == 1
+    assert torch.isfinite(out.float()).all()
+    tokens = _coverage_sample(idx, 384, np.random.default_rng(2), 16)
+    tokens = np.union1d(tokens, np.array([1, 100, 255, 256, 257], dtype=np.int64))  # decode / prefill boundary
+    logits = oracle.router_logits(adapter.bits(wl.x[tokens]), adapter.bits(layer.router.weight))
+    want_idx, _ = oracle.route(oracle.ROUTER_SIGMOID, logits, wl.K)
+    got_idx = idx.cpu().numpy()[tokens]
+    assert [set(r) for r in got_idx.tolist()] == [set(r) for r in want_idx.tolist()]
+    assert _check_sampled(layer, wl.x, out, w, idx, tokens) <= TOL
+    # decode-sized call at this shape
+    xd = wl.x[:8].contiguous()
+    outd, (wd, idd) = eng.forward(layer, xd, wl.K, return_routes=True)
+    eng.sync()
+    assert eng.ctx.counters().gemm_calls == 1  # the short call took the decode kernels
+    assert _check_sampled(layer, xd, outd, wd, idd, np.arange(8)) <= TOL
+    eng.ctx.close()
+    del wl, layer, eng
+    torch.cuda.empty_cache()

@@ -68,6 +68,87 @@ def test_noalloc_matches_wm_moe_forward_twice():
     eng.ctx.close()
 
 
+def _status():
+    err = ctypes.create_string_buffer(256)
+    rc = lib.load().wm_moe_forward_noalloc_status(torch.cuda.current_stream().cuda_stream, err, len(err))
+    return rc, err.value.decode()
+
+
+@pytest.mark.parametrize("B", [1, 8])
+def test_noalloc_config1_decode_matches_oracle(B):
+    """The config-1 decode layer (H=2048, 512 experts of I=512 + shared, top-10
+    softmax) at batch 1 and 8: two calls in a row, each against the CPU
+    oracle on the routes the call chose, and no device error recorded."""
+    wl = synth.config(1, device=DEV, batch=B)
+    layer, K = wl.layer, wl.K
+    eng = Engine(0, max_tokens=64, hidden=2048, inter=512, experts=512, topk=K)
+    layer_np = adapter.from_layer(layer)
+    for call in range(2):
+        x = synth.activations(B, 2048, torch.Generator(device=DEV).manual_seed(40 + call), DEV)
+        out = torch.full((B, 2048), float("nan"), dtype=torch.bfloat16, device=DEV)
+        ri = torch.empty((B, K), dtype=torch.int32, device=DEV)
+        rw = torch.empty((B, K), dtype=torch.float32, device=DEV)
+        a = eng._args(layer, x, K)
+        eng._with_shared(a, layer)
+        eng._with_router(a, layer.router)
+        a.out, a.out_idx, a.out_w = out.data_ptr(), ri.data_ptr(), rw.data_ptr()
+        err = ctypes.create_string_buffer(256)
+        rc = lib.load().wm_moe_forward_noalloc(ctypes.byref(a), torch.cuda.current_stream().cuda_stream, err,
+                                               len(err))
+        assert rc == lib.WM_OK, err.value.decode()
+        rc, msg = _status()
+        assert rc == lib.WM_OK, msg
+        logits = oracle.router_logits(adapter.bits(x), adapter.bits(layer.router.weight))
+        want_idx, _ = oracle.route(oracle.ROUTER_SOFTMAX, logits, K)
+        assert [set(r) for r in ri.cpu().numpy().tolist()] == [set(r) for r in want_idx.tolist()]
+        ref = layer_np.forward(adapter.bits(x), ri.cpu().numpy(), rw.cpu().numpy())
+        e = oracle.max_rel_error(oracle.bf16_to_f32(adapter.bits(out)), oracle.bf16_to_f32(ref))
+        assert e <= TOL
+    eng.ctx.close()
+
+
+def test_noalloc_reports_out_of_range_routes():
+    """A caller-given route naming an expert outside [0, E) is recorded on the
+    device: the status accessor reports it, the bad route adds nothing to its
+    token, and the next clean call clears the record."""
+    layer = _layer()
+    K, T, E = 4, 8, 16
+    eng = Engine(0, max_tokens=64, hidden=512, inter=256, experts=E, topk=K)
+    g = torch.Generator(device=DEV).manual_seed(50)
+    x = synth.activations(T, 512, g, DEV)
+    idx = torch.stack([torch.randperm(E, generator=g, device=DEV)[:K] for _ in range(T)]).to(torch.int32)
+    w = torch.rand((T, K), generator=g, device=DEV)
+    bad = idx.clone()
+    bad[3, 2] = E + 5  # out of range
+    w_bad = w.clone()
+
+    def call(routes_idx, routes_w):
+        out = torch.empty((T, 512), dtype=torch.bfloat16, device=DEV)
+        a = eng._args(layer, x, K)
+        eng._with_shared(a, layer)
+        a.routes_idx, a.routes_w, a.out = routes_idx.data_ptr(), routes_w.data_ptr(), out.data_ptr()
+        err = ctypes.create_string_buffer(256)
+        rc = lib.load().wm_moe_forward_noalloc(ctypes.byref(a), torch.cuda.current_stream().cuda_stream, err,
+                                               len(err))
+        assert rc == lib.WM_OK, err.value.decode()
+        return out
+
+    out = call(bad, w_bad)
+    rc, msg = _status()
+    assert rc == lib.WM_ERROR and "outside the model" in msg, msg
+    # the bad pair contributes nothing: the same as a zero weight on an in-range expert
+    w_zero = w.clone()
+    w_zero[3, 2] = 0.0
+    want = eng.forward(layer, x, K, routes=(w_zero, idx))
+    eng.sync()
+    e = oracle.max_rel_error(oracle.bf16_to_f32(adapter.bits(out)), oracle.bf16_to_f32(adapter.bits(want)))
+    assert e <= TOL
+    call(idx, w)
+    rc, msg = _status()
+    assert rc == lib.WM_OK, msg
+    eng.ctx.close()
+
+
 def test_noalloc_rejects_sizes_beyond_its_scratch():
     layer = _layer(E=64, H=2048, I=512, seed=9)
     K, T = 8, 1024  # rows (T*K + T) * (H + I) * 2 bytes = 47 MB, beyond the 8 MiB array

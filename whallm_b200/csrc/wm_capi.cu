@@ -695,6 +695,9 @@ WM_EXPORT int wm_sync(wm_ctx* ctx, void* stream) {
     case wm::kStatusOverflow:
       return fail(ctx, "sorted rows exceeded the workspace (%u)", st[1]);
     case wm::kStatusWaitTimeout:
+      if (st[1] >= 60u * 16u && st[1] < 62u * 16u)
+        return fail(ctx, "an expert-parallel %s wait timed out (peer %u never signalled); results are invalid",
+                    st[1] < 61u * 16u ? "dispatch" : "return", st[1] % 16u);
       return fail(ctx, "a GEMM pipeline wait timed out (role %u); results are invalid", st[1]);
     case wm::kStatusNanCode:
       return fail(ctx, "FP8 weights contain reserved NaN codes (row %u)", st[1]);
@@ -851,7 +854,7 @@ struct wm_ep {
   void* base = nullptr;  // this rank's exchange buffer (one cudaMalloc, exported through IPC)
   size_t bytes = 0;
   uint8_t* peer[wm::kMaxEpRanks] = {};  // every rank's buffer in this address space (own one included)
-  size_t o_recv_x = 0, o_recv_e = 0, o_back = 0, o_flags = 0, o_ticket = 0, o_epoch = 0;
+  size_t o_recv_x = 0, o_recv_e = 0, o_back = 0, o_flags = 0, o_counts = 0, o_ticket = 0, o_epoch = 0;
 };
 
 namespace {
@@ -872,6 +875,7 @@ wm::EpPeers ep_peers(const wm_ep* ep, int which) {
     pe.rows[r] = reinterpret_cast<uint16_t*>(b + (which == 0 ? ep->o_recv_x : ep->o_back)) + blk * ep->H;
     pe.ids[r] = reinterpret_cast<int32_t*>(b + ep->o_recv_e) + blk;
     pe.flag[r] = reinterpret_cast<uint32_t*>(b + ep->o_flags) + which * ep->world + ep->rank;
+    pe.count[r] = reinterpret_cast<int32_t*>(b + ep->o_counts) + ep->rank;
   }
   uint8_t* own = static_cast<uint8_t*>(ep->base);
   pe.ticket = reinterpret_cast<uint32_t*>(own + ep->o_ticket) + which;
@@ -915,6 +919,7 @@ WM_EXPORT wm_ep* wm_ep_create(int32_t device, int32_t world, int32_t rank, int64
   ep->o_recv_e = take(slots * 4);
   ep->o_back = take(slots * H * 2);
   ep->o_flags = take(size_t(2 * world) * 4);
+  ep->o_counts = take(size_t(world) * 4);
   ep->o_ticket = take(8);
   ep->o_epoch = take(4);
   ep->bytes = off;
@@ -1001,6 +1006,7 @@ WM_EXPORT int wm_ep_dispatch(wm_ctx* ctx, wm_ep* ep, int64_t T, int32_t K, int32
   DeviceGuard guard(ctx->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* own = static_cast<uint8_t*>(ep->base);
+  wm::prof_begin(&ctx->prof, wm::kProfEpSend, s);
   wm::launch_ep_begin(reinterpret_cast<uint32_t*>(own + ep->o_epoch), s);
   const int P = int(T) * K;
   int launches = 0;
@@ -1016,6 +1022,7 @@ WM_EXPORT int wm_ep_dispatch(wm_ctx* ctx, wm_ep* ep, int64_t T, int32_t K, int32
   }
   wm::launch_ep_send(idx, plan, int(T), K, experts_per_rank, ep->world, int(ep->capacity), pair_pos,
                      static_cast<const uint16_t*>(x), ep->H, ep_peers(ep, 0), ctx->num_sms, s);
+  wm::prof_end(&ctx->prof, wm::kProfEpSend, s);
   ctx->counters.launches += launches + 2;
   return check_launch(ctx, "expert-parallel dispatch");
 }
@@ -1026,9 +1033,11 @@ WM_EXPORT int wm_ep_return(wm_ctx* ctx, wm_ep* ep, const void* y, void* stream) 
   if (y == nullptr || !aligned(y, 16)) return fail(ctx, "y must be a 16-byte aligned device pointer");
   DeviceGuard guard(ctx->device);
   const uint8_t* own = static_cast<const uint8_t*>(ep->base);
+  wm::prof_begin(&ctx->prof, wm::kProfEpReturn, static_cast<cudaStream_t>(stream));
   wm::launch_ep_return(static_cast<const uint16_t*>(y), reinterpret_cast<const int32_t*>(own + ep->o_recv_e),
                        ep->world, int(ep->capacity), ep->H, ep_peers(ep, 1), ctx->num_sms,
                        static_cast<cudaStream_t>(stream));
+  wm::prof_end(&ctx->prof, wm::kProfEpReturn, static_cast<cudaStream_t>(stream));
   ctx->counters.launches += 1;
   return check_launch(ctx, "expert-parallel return");
 }
@@ -1038,11 +1047,60 @@ WM_EXPORT int wm_ep_wait(wm_ctx* ctx, wm_ep* ep, int32_t which, void* stream) {
   if (ep == nullptr || which < 0 || which > 1) return fail(ctx, "wm_ep_wait: bad buffer or exchange");
   DeviceGuard guard(ctx->device);
   const uint8_t* own = static_cast<const uint8_t*>(ep->base);
+  const int slot = which == 0 ? wm::kProfEpWaitDispatch : wm::kProfEpWaitReturn;
+  wm::prof_begin(&ctx->prof, slot, static_cast<cudaStream_t>(stream));
   wm::launch_ep_wait(reinterpret_cast<const uint32_t*>(own + ep->o_flags) + which * ep->world, ep->world,
                      reinterpret_cast<const uint32_t*>(own + ep->o_epoch), ctx->status, 60 + which,
                      static_cast<cudaStream_t>(stream));
+  wm::prof_end(&ctx->prof, slot, static_cast<cudaStream_t>(stream));
   ctx->counters.launches += 1;
   return check_launch(ctx, "expert-parallel wait");
+}
+
+WM_EXPORT int wm_ep_experts(wm_ctx* ctx, wm_ep* ep, const wm_moe_args* args, void* stream) {
+  if (ctx == nullptr) return WM_ERROR;
+  if (ep == nullptr || !ep_ready(ep)) return fail(ctx, "the exchange buffer has unopened peers");
+  if (ep->device != ctx->device) return fail(ctx, "the exchange buffer lives on another device");
+  if (args == nullptr) return fail(ctx, "args is NULL");
+  const int64_t slots = int64_t(ep->world) * ep->capacity;
+  if (slots > ctx->opt.max_tokens)
+    return fail(ctx, "the exchange buffer's %lld slots exceed the handle's max_tokens", (long long)slots);
+  if (args->H != ep->H) return fail(ctx, "H = %d differs from the exchange buffer's %d", args->H, ep->H);
+  if (args->T < 1 || args->T > slots) return fail(ctx, "T (the rows expected) must lie in [1, %lld]", (long long)slots);
+  uint8_t* own = static_cast<uint8_t*>(ep->base);
+  // the experts read the received rows as x, one route per slot
+  wm_moe_args b = *args;
+  b.K = 1;
+  b.x = own + ep->o_recv_x;
+  b.routes_idx = reinterpret_cast<const int32_t*>(own + ep->o_recv_e);
+  b.shared_gate = WM_SHARED_NONE;
+  b.router_weight = nullptr;
+  b.norm_weight = nullptr;
+  if (int rc = validate_experts(ctx, &b, false)) return rc;
+  DeviceGuard guard(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the kernels are picked by the rows expected (b.T); the GEMV sizes its grid
+  // by T, so it takes every slot
+  const Path path = expert_path(ctx, &b, false);
+  if (path == kPathGemv) b.T = int32_t(slots);
+  wm::Plan plan = ctx->plan;
+  plan_for_path(ctx, path, &plan);
+  const int32_t* counts = reinterpret_cast<const int32_t*>(own + ep->o_counts);
+  int launches = 0;
+  wm::prof_begin(&ctx->prof, wm::kProfPlan, s);
+  wm::launch_plan_blocks(b.routes_idx, counts, ep->world, int(ep->capacity), b.E, path == kPathGemm ? wm::kTileM : 1,
+                         plan, ctx->max_rows, ctx->max_mtiles, ctx->max_chunks, ctx->status, s, &launches);
+  wm::prof_end(&ctx->prof, wm::kProfPlan, s);
+  ctx->counters.launches += launches;
+  if (int rc = check_launch(ctx, "plan")) return rc;
+  if (int rc = run_experts(ctx, &b, false, path, s)) return rc;
+  wm::prof_begin(&ctx->prof, wm::kProfEpReturn, s);
+  wm::launch_ep_return_sorted(ctx->routed, ctx->plan.pair_pos, counts, ep->world, int(ep->capacity), ep->H,
+                              ep_peers(ep, 1), ctx->num_sms, s);
+  wm::prof_end(&ctx->prof, wm::kProfEpReturn, s);
+  ctx->counters.launches += 1;
+  ctx->counters.calls_pairs += 1;
+  return check_launch(ctx, "expert-parallel experts and return");
 }
 
 WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* args, void* stream) {

@@ -71,6 +71,7 @@ __global__ void __launch_bounds__(256) ep_send_kernel(const int32_t* __restrict_
     const int r = i / capacity, j = i - r * capacity;
     if (j >= p.counts[r]) pe.ids[r][j] = -1;
   }
+  if (gtid < world) pe.count[gtid][0] = p.counts[gtid];  // the owner plans over real pairs only
   for (int i = gtid; i < P; i += nthreads) {
     const int pos = p.pair_pos[i];
     if (pos < 0) {
@@ -110,6 +111,27 @@ __global__ void __launch_bounds__(256) ep_return_kernel(const uint16_t* __restri
   signal_peers(pe, world);
 }
 
+// Result rows back to their senders straight from the owner's sorted rows:
+// slot j < counts[r] of recv block r is row pair_pos[r * capacity + j] of
+// `routed`, and goes to slot j of rank r's back block for this rank.  Fuses
+// the unpermute of the owner's rows with the return.
+__global__ void __launch_bounds__(256) ep_return_sorted_kernel(const uint16_t* __restrict__ routed,
+                                                               const int32_t* __restrict__ pair_pos,
+                                                               const int32_t* __restrict__ counts, int world,
+                                                               int capacity, int H, const EpPeers pe) {
+  const int lane = threadIdx.x & 31, warps = gridDim.x * blockDim.x >> 5;
+  for (int s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; s < world * capacity; s += warps) {
+    const int r = s / capacity, j = s - r * capacity;
+    if (j >= min(counts[r], capacity)) continue;
+    const int row = pair_pos[s];
+    if (row < 0) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(routed + int64_t(row) * H);
+    uint4* dst = reinterpret_cast<uint4*>(pe.rows[r] + int64_t(j) * H);
+    for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
+  }
+  signal_peers(pe, world);
+}
+
 // Bounded wait until every peer's flag has reached this step.
 __global__ void ep_wait_kernel(const uint32_t* flags, int world, const uint32_t* epoch, uint32_t* status, int code) {
   const int r = threadIdx.x;
@@ -136,6 +158,11 @@ void launch_ep_send(const int32_t* idx, const Plan& p, int T, int K, int per_ran
 void launch_ep_return(const uint16_t* y, const int32_t* recv_e, int world, int capacity, int H, const EpPeers& pe,
                       int num_sms, cudaStream_t stream) {
   ep_return_kernel<<<num_sms, 256, 0, stream>>>(y, recv_e, world, capacity, H, pe);
+}
+
+void launch_ep_return_sorted(const uint16_t* routed, const int32_t* pair_pos, const int32_t* counts, int world,
+                             int capacity, int H, const EpPeers& pe, int num_sms, cudaStream_t stream) {
+  ep_return_sorted_kernel<<<num_sms, 256, 0, stream>>>(routed, pair_pos, counts, world, capacity, H, pe);
 }
 
 void launch_ep_wait(const uint32_t* flags, int world, const uint32_t* epoch, uint32_t* status, int code,

@@ -27,6 +27,10 @@ enum ProfSlot : int {
   kProfDecodeGateUp,
   kProfDecodeDown,
   kProfNorm,
+  kProfEpSend,          // expert-parallel dispatch: owner plan + peer stores of the rows
+  kProfEpWaitDispatch,  // waiting for every peer's rows
+  kProfEpReturn,        // result rows back to their senders
+  kProfEpWaitReturn,    // waiting for every peer's result rows
   kProfSlots
 };
 struct Profiler;  // defined in wm_profile.cu
@@ -97,6 +101,7 @@ struct EpPeers {
   uint16_t* rows[kMaxEpRanks];  // rank r's recv_x (dispatch) or back (return) block for this rank
   int32_t* ids[kMaxEpRanks];    // rank r's recv_e block for this rank (dispatch)
   uint32_t* flag[kMaxEpRanks];  // rank r's flag for this rank
+  int32_t* count[kMaxEpRanks];  // rank r's count of the pairs this rank sent it (dispatch)
   uint32_t* ticket;             // local: CTAs done with this exchange
   const uint32_t* epoch;        // local: step number
 };
@@ -107,6 +112,16 @@ void launch_ep_return(const uint16_t* y, const int32_t* recv_e, int world, int c
                       int num_sms, cudaStream_t stream);
 void launch_ep_wait(const uint32_t* flags, int world, const uint32_t* epoch, uint32_t* status, int code,
                     cudaStream_t stream);
+// The owner's plan over its recv blocks: block r holds counts[r] real pairs
+// (ids[r * capacity + j], j < counts[r], local expert ids); slots past a
+// block's count are never read.  row_token[row] = slot, pair_pos[slot] = row.
+void launch_plan_blocks(const int32_t* ids, const int32_t* counts, int world, int capacity, int E, int align,
+                        const Plan& p, int max_rows, int max_mtiles, int max_chunks, uint32_t* status,
+                        cudaStream_t stream, int* launches);
+// Result rows straight from the owner's sorted rows (routed[pair_pos[slot]])
+// into each sender's back block, then the return flags.
+void launch_ep_return_sorted(const uint16_t* routed, const int32_t* pair_pos, const int32_t* counts, int world,
+                             int capacity, int H, const EpPeers& pe, int num_sms, cudaStream_t stream);
 void launch_unpermute(const uint16_t* routed, const Plan& p, int TK, int H, uint16_t* out, int num_sms,
                       cudaStream_t stream);
 

@@ -7,16 +7,25 @@
 // memory through its own allocator and forbids other allocations.  For them
 // this entry point runs the same kernels as wm_moe_forward's decode path
 // (router, sort, expert GEMVs, shared expert, combine) with all scratch in
-// one file-scope device array of kScratchBytes, reserved by the CUDA runtime
-// on every GPU that loads the library, for as long as the process lives.
+// one file-scope device array of kScratchBytes per GPU, which the CUDA
+// runtime reserves when it loads this file's module on that GPU and keeps
+// until the process exits.
 //
-// * The first call on a device sets that device up (looks up the array's
-//   device address with cudaGetSymbolAddress); make that first call before
-//   any stream capture.
+// * The first call on a device sets that device up: it looks up the array's
+//   device address with cudaGetSymbolAddress, which is also when the runtime
+//   loads the module and reserves the array (CUDA loads modules lazily by
+//   default).  Make that first call -- or a call of
+//   wm_moe_forward_noalloc_status -- at start-up, before device memory is
+//   fixed and before any stream capture, or run with CUDA_MODULE_LOADING=EAGER.
 // * All calls share the one array and it keeps the last call's contents:
 //   calls that may overlap on the GPU (on different streams, or from several
 //   host threads) race with each other.  Serialise them.
 // * Sizes whose scratch would exceed the array are rejected with an error.
+// * Errors the kernels find on the device (an expert id outside [0, E)) are
+//   recorded in the array's status words; wm_moe_forward_noalloc_status waits
+//   for the stream and reports them.  A route with a bad expert id
+//   contributes nothing to its token's output.  FP8 NaN codes are not checked
+//   on this path (wm_moe_forward reports them).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -44,6 +53,46 @@ int report(char* error, size_t n, const char* msg) {
 }
 
 size_t up256(size_t v) { return (v + 255) / 256 * 256; }
+
+// The array's device address and the device's limits, looked up once per
+// device (the current one).  The status words sit at the array's start.
+constexpr size_t kStatusBytes = 256;
+
+bool device_setup(int* dev_out, char* msg, size_t n) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    snprintf(msg, n, "no current CUDA device");
+    return false;
+  }
+  std::lock_guard<std::mutex> lock(g_setup_mutex);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      snprintf(msg, n, "cudaGetSymbolAddress of the scratch array failed: %s", cudaGetErrorString(e));
+      return false;
+    }
+    g_scratch_ptr[dev] = p;
+  }
+  // device queries once per device: a cudaGetDeviceProperties per call costs
+  // milliseconds of host time
+  if (g_major[dev] == 0) {
+    int major = 0, optin = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) {
+      snprintf(msg, n, "CUDA device attributes could not be read");
+      return false;
+    }
+    g_major[dev] = major;
+    g_smem_optin[dev] = optin;
+  }
+  if (g_major[dev] != 10) {
+    snprintf(msg, n, "needs an sm_100 (B200-class) GPU");
+    return false;
+  }
+  *dev_out = dev;
+  return true;
+}
 
 }  // namespace
 }  // namespace wm
@@ -91,8 +140,9 @@ extern "C" WM_EXPORT int wm_moe_forward_noalloc(const wm_moe_args* a, void* stre
 
   // scratch layout (GEMV path: no row padding)
   const int64_t rows = T * K + T;
-  const int max_mtiles = int(rows / kTileM + E + 2);
-  size_t off = 0;
+  // unpadded groups are cut into 16-row tiles: at most rows / 16 + one partial tile per group
+  const int max_mtiles = int(rows / 16 + E + 2);
+  size_t off = kStatusBytes;  // the status words come first
   auto take = [&](size_t bytes) {
     const size_t at = off;
     off = up256(off + bytes);
@@ -102,7 +152,7 @@ extern "C" WM_EXPORT int wm_moe_forward_noalloc(const wm_moe_args* a, void* stre
                o_rowtok = take(rows * 4), o_unique = take((E + 1) * 4), o_nu = take(4),
                o_mt = take(size_t(max_mtiles) * 8), o_nm = take(4), o_act = take(rows * I * 2),
                o_routed = take(rows * H * 2), o_logits = take(T * E * 4), o_idx = take(T * K * 4),
-               o_w = take(T * K * 4), o_sg = take(T * 4), o_status = take(16);
+               o_w = take(T * K * 4), o_sg = take(T * 4);
   if (off > kScratchBytes) {
     snprintf(msg, sizeof(msg), "this call needs %.2f MiB of scratch; the allocation-free entry point has %.0f MiB",
              off / 1048576.0, kScratchBytes / 1048576.0);
@@ -112,33 +162,9 @@ extern "C" WM_EXPORT int wm_moe_forward_noalloc(const wm_moe_args* a, void* stre
 
   // once per device: the array's device address
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
-    return report(error, error_size, "no current CUDA device");
-  {
-    std::lock_guard<std::mutex> lock(g_setup_mutex);
-    if (g_scratch_ptr[dev] == nullptr) {
-      void* p = nullptr;
-      cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);
-      if (e != cudaSuccess || p == nullptr) {
-        snprintf(msg, sizeof(msg), "cudaGetSymbolAddress of the scratch array failed: %s", cudaGetErrorString(e));
-        return report(error, error_size, msg);
-      }
-      g_scratch_ptr[dev] = p;
-    }
-    // device queries and kernel attributes once per device (and size): a
-    // cudaGetDeviceProperties per call costs milliseconds of host time
-    if (g_major[dev] == 0) {
-      int major = 0, optin = 0;
-      if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
-          cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
-        return report(error, error_size, "CUDA device attributes could not be read");
-      g_major[dev] = major;
-      g_smem_optin[dev] = optin;
-    }
-    if (g_major[dev] != 10) return report(error, error_size, "needs an sm_100 (B200-class) GPU");
-    if (gemv_smem > size_t(g_smem_optin[dev]) || router_smem > size_t(g_smem_optin[dev]))
-      return report(error, error_size, "H is too large for the decode kernels' shared-memory staging");
-  }
+  if (!device_setup(&dev, msg, sizeof(msg))) return report(error, error_size, msg);
+  if (gemv_smem > size_t(g_smem_optin[dev]) || router_smem > size_t(g_smem_optin[dev]))
+    return report(error, error_size, "H is too large for the decode kernels' shared-memory staging");
   gemv_init_attributes(int(gemv_smem));  // raise-only, cheap after the first call
   router_init_attributes(int(H));
 
@@ -157,7 +183,7 @@ extern "C" WM_EXPORT int wm_moe_forward_noalloc(const wm_moe_args* a, void* stre
   uint16_t* routed = reinterpret_cast<uint16_t*>(base + o_routed);
   float* logits = reinterpret_cast<float*>(base + o_logits);
   float* sg = reinterpret_cast<float*>(base + o_sg);
-  uint32_t* status = reinterpret_cast<uint32_t*>(base + o_status);
+  uint32_t* status = reinterpret_cast<uint32_t*>(base);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
   // the status words start at zero; everything else is written before it is read
@@ -228,4 +254,38 @@ extern "C" WM_EXPORT int wm_moe_forward_noalloc(const wm_moe_args* a, void* stre
     return report(error, error_size, msg);
   }
   return WM_OK;
+}
+
+extern "C" WM_EXPORT int wm_moe_forward_noalloc_status(void* stream, char* error, size_t error_size) {
+  using namespace wm;
+  char msg[256];
+  int dev = 0;
+  if (!device_setup(&dev, msg, sizeof(msg))) return report(error, error_size, msg);
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    snprintf(msg, sizeof(msg), "stream synchronisation failed: %s", cudaGetErrorString(e));
+    return report(error, error_size, msg);
+  }
+  uint32_t st[2] = {0, 0};
+  e = cudaMemcpy(st, g_scratch_ptr[dev], sizeof(st), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) {
+    snprintf(msg, sizeof(msg), "reading the status words failed: %s", cudaGetErrorString(e));
+    return report(error, error_size, msg);
+  }
+  switch (st[0]) {
+    case kStatusOk:
+      return WM_OK;
+    case kStatusBadExpert:
+      snprintf(msg, sizeof(msg), "expert ID is outside the model (pair %u)", st[1]);
+      break;
+    case kStatusOverflow:
+      snprintf(msg, sizeof(msg), "sorted rows exceeded the scratch array (%u)", st[1]);
+      break;
+    case kStatusNanCode:
+      snprintf(msg, sizeof(msg), "FP8 weights contain reserved NaN codes (row %u)", st[1]);
+      break;
+    default:
+      snprintf(msg, sizeof(msg), "device status %u (%u)", st[0], st[1]);
+  }
+  return report(error, error_size, msg);
 }

@@ -260,6 +260,48 @@ __global__ void __launch_bounds__(256) plan_scatter_kernel(const int32_t* __rest
   if (threadIdx.x < 32) scatter_pairs(idx, t0, t1, K, E, run, p, status);
 }
 
+// The owner's plan of an expert-parallel step: chunk c covers slots
+// [j0, j1) of recv block r = c / per_block, clipped to the block's real pairs
+// (counts[r]); the pairs are single routes (K = 1) in slot order.
+__device__ __forceinline__ void block_chunk(const int32_t* counts, int capacity, int chunk_slots, int per_block,
+                                            int c, int* first, int* last) {
+  const int r = c / per_block, cc = c - r * per_block;
+  const int n = max(0, min(counts[r], capacity));
+  const int j0 = cc * chunk_slots, j1 = min(j0 + chunk_slots, n);
+  *first = r * capacity + j0;
+  *last = r * capacity + max(j0, j1);
+}
+
+__global__ void __launch_bounds__(256) plan_blocks_count_kernel(const int32_t* __restrict__ ids,
+                                                                const int32_t* __restrict__ counts, int capacity,
+                                                                int chunk_slots, int per_block, int E, Plan p) {
+  extern __shared__ int cnt[];  // E + 1
+  int s0, s1;
+  block_chunk(counts, capacity, chunk_slots, per_block, blockIdx.x, &s0, &s1);
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  for (int i = s0 + threadIdx.x; i < s1; i += blockDim.x) {
+    const int e = ids[i];
+    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) p.hist[(int64_t)blockIdx.x * (E + 1) + i] = cnt[i];
+}
+
+__global__ void __launch_bounds__(256) plan_blocks_scatter_kernel(const int32_t* __restrict__ ids,
+                                                                  const int32_t* __restrict__ counts, int capacity,
+                                                                  int chunk_slots, int per_block, int E, Plan p,
+                                                                  int max_rows, uint32_t* status) {
+  extern __shared__ int run[];  // E + 1
+  const int c = blockIdx.x;
+  if (p.offsets[E + 1] > max_rows) return;
+  int s0, s1;
+  block_chunk(counts, capacity, chunk_slots, per_block, c, &s0, &s1);
+  for (int e = threadIdx.x; e < E; e += blockDim.x) run[e] = p.offsets[e] + p.hist[(int64_t)c * (E + 1) + e];
+  __syncthreads();
+  if (threadIdx.x < 32) scatter_pairs(ids, s0, s1, 1, E, run, p, status);
+}
+
 // x_sorted[r] = x[row_token[r]] (zeros for padding rows).  One warp per row.
 __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __restrict__ x, Plan p, int E, int H,
                                                           uint16_t* __restrict__ xs) {
@@ -383,6 +425,22 @@ void launch_plan(const int32_t* idx, int T, int K, int E, bool has_shared, int a
                                                status);
   plan_scatter_kernel<<<chunks, 256, smem1, stream>>>(idx, T, K, E, chunk_tokens, has_shared ? 1 : 0, p, max_rows,
                                                       status);
+  *launches += 3;
+}
+
+void launch_plan_blocks(const int32_t* ids, const int32_t* counts, int world, int capacity, int E, int align,
+                        const Plan& p, int max_rows, int max_mtiles, int max_chunks, uint32_t* status,
+                        cudaStream_t stream, int* launches) {
+  int chunk_slots = 64;
+  while (int64_t(world) * ((capacity + chunk_slots - 1) / chunk_slots) > max_chunks) chunk_slots *= 2;
+  const int per_block = (capacity + chunk_slots - 1) / chunk_slots;
+  const int chunks = world * per_block;
+  const size_t smem1 = size_t(E + 1) * sizeof(int);
+  plan_blocks_count_kernel<<<chunks, 256, smem1, stream>>>(ids, counts, capacity, chunk_slots, per_block, E, p);
+  const size_t smem2 = size_t(2 * (E + 2)) * sizeof(int);
+  plan_scan_kernel<<<1, 1024, smem2, stream>>>(0, E, chunks, 0, align, p, max_rows, max_mtiles, status);
+  plan_blocks_scatter_kernel<<<chunks, 256, smem1, stream>>>(ids, counts, capacity, chunk_slots, per_block, E, p,
+                                                             max_rows, status);
   *launches += 3;
 }
 

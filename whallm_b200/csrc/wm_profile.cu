@@ -66,7 +66,8 @@ void prof_end(Profiler* p, int slot, cudaStream_t s) {
 const char* prof_name(int slot) {
   static const char* names[kProfSlots] = {"router_logits", "router_topk", "plan",     "act_f16",     "gather_rows",
                                           "gemv_gate_up",  "gemv_down",   "gemm_gate_up", "gemm_down", "combine",
-                                          "decode_gate_up", "decode_down", "rmsnorm"};
+                                          "decode_gate_up", "decode_down", "rmsnorm",
+                                          "ep_send", "ep_wait_dispatch", "ep_return", "ep_wait_return"};
   return slot >= 0 && slot < kProfSlots ? names[slot] : "?";
 }
 

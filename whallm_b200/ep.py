@@ -2,7 +2,7 @@
 
 Rank r of W owns the routed experts [r * E/W, (r + 1) * E/W); the router and
 the shared expert are replicated and every rank keeps its own tokens.  One
-layer forward (the survey's hot-path rows a6-a8 split across GPUs):
+layer forward (routing, sort, experts and combine split across GPUs):
 
   1. route the local tokens with the full router -> (w, idx) [T, K];
   2. wm_ep_plan orders the (t, k) pairs by owning rank (stable, so k order
@@ -22,15 +22,17 @@ layer forward (the survey's hot-path rows a6-a8 split across GPUs):
 Expert rows are independent of which other rows share their GPU, so a
 layer split over W GPUs returns what one GPU computes for the same tokens
 whenever both take the same expert kernels (the exchanges only move rows).
-The reference runs its experts on one device; this module is the
-B200-native counterpart of the survey's expert-parallel plan, not a port.
+The reference runs its experts on one device (model.py:181-182 refuses
+more); this module is the B200-native expert-parallel layer, not a port.
 
 With `peer_memory=True` (fixed capacity, one GPU per rank, at most 8) the
 three exchanges of steps 2-5 run without the collective library: every rank
-stores its pairs' rows and ids straight into the owners' exchange buffers over
-NVLink, the owners store the result rows straight back, and bounded device
-waits on per-rank flags replace the all-to-alls (include/whallm_moe.h,
-wm_ep_*).  Only real pairs cross NVLink.
+stores its pairs' rows and ids (and how many it sent) straight into the
+owners' exchange buffers over NVLink; each owner plans over the real rows
+only, runs its experts (decode kernels or grouped GEMM) and stores every
+result row from its sorted rows straight back into the sender's buffer; and
+bounded device waits on per-rank flags replace the all-to-alls
+(include/whallm_moe.h, wm_ep_*).  Only real pairs cross NVLink.
 
 The engine is anything with route / ep_plan / expert_pairs / combine of
 whallm_b200.moe.Engine's signatures, so the exchange logic can be tested with
@@ -69,11 +71,16 @@ class ExpertParallelMoE:
     with lib.FLAG_SKIP_NEGATIVE_ROUTES and room for W * M * K rows."""
 
     def __init__(self, engine, layer: LayerWeights, top_k: int, group=None, shared_engine=None,
-                 fixed_capacity: int = 0, peer_memory: bool = False):
+                 fixed_capacity: int = 0, peer_memory: bool = False, owner_engine=None,
+                 peer_buffer: "lib.EpBuffer | None" = None):
         if not dist.is_initialized():
             raise RuntimeError("torch.distributed is not initialised")
         self.engine, self.layer, self.K, self.group = engine, layer, top_k, group
         self.shared_engine = shared_engine
+        # the handle that runs this rank's experts on the rows it receives
+        # (single routes, up to world * capacity of them); the routing
+        # handle's by default
+        self.owner = owner_engine if owner_engine is not None else engine
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         if layer.E % self.world:
@@ -87,7 +94,15 @@ class ExpertParallelMoE:
         self.fixed = fixed_capacity
         self.stats = EPStats()
         self._side = None
-        self.ep_buf = self._open_exchange() if peer_memory else None
+        # layers that run one after another on one stream can share one exchange buffer
+        self._owns_buffer = peer_memory and peer_buffer is None
+        if peer_buffer is not None:
+            if not peer_memory:
+                raise ValueError("a peer buffer is used only with peer_memory=True")
+            if (peer_buffer.world, peer_buffer.rank, peer_buffer.capacity, peer_buffer.hidden) != (
+                    self.world, self.rank, self.fixed * self.K, layer.H):
+                raise ValueError("the shared exchange buffer was made for another shape or group")
+        self.ep_buf = peer_buffer if peer_buffer is not None else (self._open_exchange() if peer_memory else None)
 
     def _open_exchange(self) -> lib.EpBuffer:
         """This rank's exchange buffer, mapped into every peer (all ranks call this together)."""
@@ -136,6 +151,8 @@ class ExpertParallelMoE:
 
     def close(self) -> None:
         """Release the exchange buffer once every rank has finished (collective)."""
+        if self.ep_buf is not None and not self._owns_buffer:
+            self.ep_buf = None
         if self.ep_buf is not None:
             if torch.cuda.is_available():
                 torch.cuda.synchronize(self.engine.device)
@@ -195,9 +212,9 @@ class ExpertParallelMoE:
         pair_pos = torch.empty((T, self.K), dtype=torch.int32, device=x.device)
         ctx.ep_dispatch(buf, T, self.K, El, idx.data_ptr(), x.data_ptr(), pair_pos.data_ptr(), stream)
         ctx.ep_wait(buf, 0, stream)
-        y = torch.empty((W * C, H), dtype=x.dtype, device=x.device)
-        self.engine.expert_pairs_at(self.local, W * C, buf.buffer(0), buf.buffer(1), y)
-        ctx.ep_return(buf, y.data_ptr(), stream)
+        # this rank's experts on the real rows it received; the results go
+        # straight back into the senders' buffers
+        self.owner.ep_experts(self.local, buf, C)
         ctx.ep_wait(buf, 1, stream)
         self.stats = EPStats(sent=-1, received=-1)
         return buf.buffer(2), pair_pos  # the result rows, in this rank's buffer
@@ -213,7 +230,7 @@ class ExpertParallelMoE:
         recv_e = torch.empty_like(send_eid)
         dist.all_to_all_single(recv_x, send_x, group=self.group)
         dist.all_to_all_single(recv_e, send_eid, group=self.group)
-        y = self.engine.expert_pairs(self.local, recv_x, recv_e.view(W * C, 1)).view(W * C, H)
+        y = self.owner.expert_pairs(self.local, recv_x, recv_e.view(W * C, 1)).view(W * C, H)
         back = torch.empty_like(y)
         dist.all_to_all_single(back, y, group=self.group)
         self.stats = EPStats(sent=-1, received=-1)
@@ -239,7 +256,7 @@ class ExpertParallelMoE:
 
         # this rank's experts on the rows it received
         if n_recv:
-            y = self.engine.expert_pairs(self.local, recv_x, recv_e.view(n_recv, 1)).view(n_recv, H)
+            y = self.owner.expert_pairs(self.local, recv_x, recv_e.view(n_recv, 1)).view(n_recv, H)
         else:
             y = torch.empty((0, H), dtype=x.dtype, device=x.device)
 

@@ -27,9 +27,9 @@ EXPORTS = (
     "wm_create", "wm_destroy", "wm_error", "wm_sync", "wm_counters_get",
     "wm_dequant", "wm_route", "wm_expert_pairs", "wm_combine", "wm_ep_plan", "wm_moe_forward",
     "wm_profile_enable", "wm_profile_read", "wm_profile_reset",
-    "wm_moe_forward_noalloc",
+    "wm_moe_forward_noalloc", "wm_moe_forward_noalloc_status",
     "wm_ep_create", "wm_ep_destroy", "wm_ep_ipc_handle", "wm_ep_open_peer", "wm_ep_buffer",
-    "wm_ep_dispatch", "wm_ep_return", "wm_ep_wait",
+    "wm_ep_dispatch", "wm_ep_return", "wm_ep_wait", "wm_ep_experts",
 )
 
 _P = ctypes.c_void_p
@@ -113,6 +113,8 @@ def load() -> ctypes.CDLL:
     L.wm_profile_reset.restype = None
     L.wm_moe_forward_noalloc.argtypes = [ctypes.POINTER(MoeArgs), _P, ctypes.c_char_p, ctypes.c_size_t]
     L.wm_moe_forward_noalloc.restype = ctypes.c_int
+    L.wm_moe_forward_noalloc_status.argtypes = [_P, ctypes.c_char_p, ctypes.c_size_t]
+    L.wm_moe_forward_noalloc_status.restype = ctypes.c_int
     L.wm_ep_create.argtypes = [_I32, _I32, _I32, _I64, _I32, ctypes.c_char_p, ctypes.c_size_t]
     L.wm_ep_create.restype = _P
     L.wm_ep_destroy.argtypes = [_P]
@@ -124,9 +126,10 @@ def load() -> ctypes.CDLL:
     L.wm_ep_dispatch.argtypes = [_P, _P, _I64, _I32, _I32, _P, _P, _P, _P]
     L.wm_ep_return.argtypes = [_P, _P, _P, _P]
     L.wm_ep_wait.argtypes = [_P, _P, _I32, _P]
+    L.wm_ep_experts.argtypes = [_P, _P, ctypes.POINTER(MoeArgs), _P]
     for name in ("wm_sync", "wm_dequant", "wm_route", "wm_expert_pairs", "wm_combine", "wm_ep_plan",
                  "wm_moe_forward", "wm_ep_ipc_handle", "wm_ep_open_peer", "wm_ep_dispatch", "wm_ep_return",
-                 "wm_ep_wait"):
+                 "wm_ep_wait", "wm_ep_experts"):
         getattr(L, name).restype = ctypes.c_int
     _lib = L
     return L
@@ -221,6 +224,9 @@ class Context:
 
     def ep_wait(self, ep: "EpBuffer", which: int, stream: int | None) -> None:
         self.check(self._lib.wm_ep_wait(self.handle, ep.handle, which, stream))
+
+    def ep_experts(self, ep: "EpBuffer", args: MoeArgs, stream: int | None) -> None:
+        self.check(self._lib.wm_ep_experts(self.handle, ep.handle, ctypes.byref(args), stream))
 
 
 class EpBuffer:

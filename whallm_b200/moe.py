@@ -248,6 +248,20 @@ class Engine:
         self.ctx.expert_pairs(a, out.data_ptr(), _stream())
         return out
 
+    def ep_experts(self, layer: LayerWeights, buf: "lib.EpBuffer", expected_rows: int) -> None:
+        """The owner's half of a peer-memory expert-parallel step (after the
+        dispatch wait): `layer`'s experts (this rank's shard) on the rows the
+        peers sent, results stored straight into the senders' buffers.
+        expected_rows picks the expert kernels (decode or grouped GEMM)."""
+        a = lib.MoeArgs()
+        a.T, a.H, a.I, a.E, a.K = expected_rows, layer.H, layer.I, layer.E, 1
+        a.layout = layer.layout
+        a.w13 = layer.w13.matrix()
+        a.w2 = layer.w2.matrix()
+        a.swiglu_limit = layer.swiglu_limit
+        a.route_scale = 1.0
+        self.ctx.ep_experts(buf, a, _stream())
+
     def combine(self, pairs: torch.Tensor, w: torch.Tensor, shared_rows: torch.Tensor | None = None,
                 shared_gate: int = lib.SHARED_NONE, x: torch.Tensor | None = None,
                 gate_weight: torch.Tensor | None = None, out: torch.Tensor | None = None,
