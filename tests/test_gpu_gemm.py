@@ -148,7 +148,7 @@ def test_config2_prefill_full_size():
     assert torch.isfinite(out.float()).all()
     counts = torch.bincount(idx.reshape(-1).long(), minlength=512)
     assert counts.sum().item() == 16384 * 10 and counts.max().item() > 20 * counts.float().median().item()
-    tokens = _coverage_sample(idx, 512, np.random.default_rng(0), 40)
+    tokens = _coverage_sample(idx, 512, np.random.default_rng(0), 60)
     assert tokens.size >= 64
     assert _check_sampled(wl.layer, wl.x, out, w, idx, tokens) <= TOL
     eng.ctx.close()
@@ -164,7 +164,7 @@ def test_config3_fp8_full_size():
     groups = (idx.long() // 32)
     per_token = [torch.unique(r).numel() for r in groups[:256]]
     assert max(per_token) <= 4
-    tokens = _coverage_sample(idx, 256, np.random.default_rng(1), 30, groups=8)
+    tokens = _coverage_sample(idx, 256, np.random.default_rng(1), 50, groups=8)
     assert tokens.size >= 64
     hit_groups = set((idx.cpu().numpy()[tokens] // 32).reshape(-1).tolist())
     assert hit_groups == set(range(8))
