@@ -278,7 +278,13 @@ def long_ep_section(args, n: int, world: int, rank: int, local: int, pk: dict) -
     if n == 3:
         layers, T_total = [synth.deepseek_fp8_layer(device=dev, seed=0)], 8192
     else:
+        # pre-norm residual blocks, h <- h + MoE(RMSNorm(h)): without the norm
+        # random layers grow the residual stream past fp32 range within a few layers
+        from whallm_b200.moe import PreNorm
         layers, T_total = [synth.deepseek_mxfp4_layer(device=dev, seed=l) for l in range(8)], 256 + 4096
+        for l, lay in enumerate(layers):
+            g = torch.Generator(device=dev).manual_seed(700 + l)
+            lay.norm = PreNorm((1.0 + 0.1 * torch.randn((lay.H,), generator=g, device=dev)).to(torch.bfloat16), 1e-6)
     lay0 = layers[0]
     Hn, In, En, Kn = lay0.H, lay0.I, lay0.E, 8
     if T_total % world or En % world:
@@ -314,13 +320,15 @@ def long_ep_section(args, n: int, world: int, rank: int, local: int, pk: dict) -
             stack(fwd1, x_all)
         torch.cuda.synchronize()
         single = T_total / (timed(fwd1, x_all, steps) / 1e3)
+        single_finite = bool(torch.isfinite(stack(fwd1, x_all).float()).all())
         eng1.ctx.close()
         del eng1
     out = {"workload": EP_SECTIONS[n][1], "tokens_per_step": T_total, "tokens_per_gpu": T_loc, "layers": len(layers),
-           "l2": "flushed (256 MB write) before every timed step"}
+           "l2": "flushed (256 MB write) before every timed step",
+           "pre_moe_norm": n == 4}
     if world == 1:
         out.update({"tokens_per_s": single, "ms_per_step": T_total / single * 1e3, "single_gpu_tokens_per_s": single,
-                    "efficiency": 1.0, "parallelism": "single GPU"})
+                    "efficiency": 1.0, "parallelism": "single GPU", "output_finite": single_finite})
         torch.cuda.empty_cache()
         return out
 
@@ -361,8 +369,10 @@ def long_ep_section(args, n: int, world: int, rank: int, local: int, pk: dict) -
     want = stack(lambda i, lay, h: ref_eng.forward(lay, h, Kn), x)
     torch.cuda.synchronize()
     exact = torch.tensor([1.0 if torch.equal(got.view(torch.int16), want.view(torch.int16)) else 0.0], device=dev)
+    finite = torch.isfinite(got.float()).all().float().reshape(1)
     max_abs = (got.float() - want.float()).abs().max().reshape(1)
     dist.all_reduce(exact, op=dist.ReduceOp.MIN)
+    dist.all_reduce(finite, op=dist.ReduceOp.MIN)
     dist.all_reduce(max_abs, op=dist.ReduceOp.MAX)
     eps[0].close()  # the shared exchange buffer (collective)
     for e_ in (eng, owner, shared, ref_eng):
@@ -374,7 +384,8 @@ def long_ep_section(args, n: int, world: int, rank: int, local: int, pk: dict) -
                 "single_gpu_tokens_per_s": single,
                 "efficiency": (tps / (world * single)) if single else None,
                 "efficiency_note": "tokens/s over N GPUs / (N x one GPU's tokens/s on the whole batch, rank 0, same run)",
-                "parity": {"bit_exact": bool(exact.item() == 1.0), "max_abs": float(max_abs.item()),
+                "parity": {"bit_exact": bool(exact.item() == 1.0), "finite": bool(finite.item() == 1.0),
+                           "max_abs": float(max_abs.item()),
                            "against": "the one-GPU stack on each rank's tokens (grouped GEMM on both)"},
                 "kernels_rank0_per_step": kernels if rank == 0 else None, "limiting_kernel": top})
     del eps, layers
@@ -631,6 +642,47 @@ def decode_batch_line(eng, layer, dev, B: int, steps: int, flush) -> dict:
             "layer_bytes": layer_bytes, "achieved_gbs": layer_bytes / (ms / 1e3) / 1e9}
 
 
+def cpu_baselines(dev, cores: int, threads: int) -> dict:
+    """The CPU oracle (OpenMP over the host cores) on bounded samples of
+    configs 0, 2 and 3 (config 1 is the headline cpu_baseline): routes come
+    from the GPU layer, only the experts the sampled tokens reach are copied
+    to the host, each sample repeats for at least 4 s."""
+    import numpy as np
+    import torch
+    from oracle import adapter
+    from whallm_b200 import synth
+    from whallm_b200.moe import Engine
+
+    out = {}
+    wl = synth.config(0, device=dev)
+    layer_np = adapter.from_layer(wl.layer)
+    T0 = wl.x.shape[0]
+    idx0, w0 = np.zeros((T0, 1), np.int32), np.ones((T0, 1), np.float32)
+    out["config0"] = {"value": cpu_sample(layer_np, adapter.bits(wl.x), idx0, w0, 4.0, T0), "unit": "tokens/s",
+                      "sample": f"the whole config-0 call ({T0} tokens, one expert)"}
+    for n, sample in ((2, 8), (3, 2)):
+        wl = synth.config(n, device=dev)
+        T, Hn = wl.x.shape
+        eng = Engine(dev.index, max_tokens=T, hidden=Hn, inter=wl.layer.I, experts=wl.layer.E, topk=wl.K)
+        _, (w, idx) = eng.forward(wl.layer, wl.x, wl.K, return_routes=True)
+        torch.cuda.synchronize()
+        tokens = np.random.default_rng(n).choice(T, sample, replace=False)
+        ii, ww = idx.cpu().numpy()[tokens], w.cpu().numpy()[tokens]
+        experts = sorted(set(ii.reshape(-1).tolist()))
+        remap = {e: i for i, e in enumerate(experts)}
+        sub_np = adapter.from_layer(wl.layer, experts=experts)
+        tps = cpu_sample(sub_np, adapter.bits(wl.x[torch.as_tensor(tokens, device=dev)]),
+                         np.vectorize(remap.get)(ii).astype(np.int32), ww, 4.0, sample)
+        out[f"config{n}"] = {"value": tps, "unit": "tokens/s",
+                             "sample": f"{sample} tokens of the {T}-token config-{n} call (their {len(experts)} experts)"}
+        eng.ctx.close()
+        del wl, eng, sub_np
+        torch.cuda.empty_cache()
+    for v in out.values():
+        v.update({"cores": threads, "kind": "port", "threads_note": f"OpenMP threads {threads} on {cores} cores"})
+    return out
+
+
 def run(args) -> None:
     import numpy as np
     import torch
@@ -759,6 +811,8 @@ def run(args) -> None:
         tps = cpu_sample(layer_np, xb, ri.cpu().numpy(), rw.cpu().numpy(), min_seconds=10.0, tokens=16)
         cpu = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
                "sample": f"16 tokens of a config-1 batch, repeated for >= 10 s, OpenMP threads {threads} on {cores} cores"}
+        if not args.no_prefill:
+            cpu["other_configs"] = cpu_baselines(dev, cores, threads)
 
     del graph
     decode_batches = [decode_batch_line(eng, layer, dev, b, max(10, min(args.steps, 30)), flush) for b in (1, 8)]

@@ -55,13 +55,31 @@ __device__ __forceinline__ void signal_peers(const EpPeers& pe, int world) {
   if (threadIdx.x == 0) *pe.ticket = 0u;
 }
 
+// One row of H bf16 from src to dst (either may be a peer's memory) by one
+// warp: four 16-byte loads in flight per lane before their stores, so a warp
+// is not bound by one load's latency per 512 bytes.
+__device__ __forceinline__ void copy_row(uint4* __restrict__ dst, const uint4* __restrict__ src, int H, int lane) {
+  const int n = H / 8;
+  int c = lane;
+  for (; c + 96 < n; c += 128) {
+    const uint4 v0 = src[c], v1 = src[c + 32], v2 = src[c + 64], v3 = src[c + 96];
+    dst[c] = v0;
+    dst[c + 32] = v1;
+    dst[c + 64] = v2;
+    dst[c + 96] = v3;
+  }
+  for (; c < n; c += 32) dst[c] = src[c];
+}
+
 }  // namespace
 
 __global__ void ep_begin_kernel(uint32_t* epoch) { epoch[0] += 1u; }
 
 // Dispatch of the pairs after the plan over owners (as ep_finish_kernel with a
 // capacity, but into the owners' buffers).
-__global__ void __launch_bounds__(256) ep_send_kernel(const int32_t* __restrict__ idx, Plan p, int T, int K,
+constexpr int kCopyThreads = 512;  // exchange kernels: 2 CTAs of 16 warps per SM
+
+__global__ void __launch_bounds__(kCopyThreads) ep_send_kernel(const int32_t* __restrict__ idx, Plan p, int T, int K,
                                                       int per_rank, int world, int capacity,
                                                       int32_t* __restrict__ pair_pos, const uint16_t* __restrict__ x,
                                                       int H, const EpPeers pe) {
@@ -87,9 +105,8 @@ __global__ void __launch_bounds__(256) ep_send_kernel(const int32_t* __restrict_
     const int pos = p.pair_pos[i];
     if (pos < 0) continue;
     const int r = idx[i] / per_rank;
-    const uint4* src = reinterpret_cast<const uint4*>(x + int64_t(i / K) * H);
-    uint4* dst = reinterpret_cast<uint4*>(pe.rows[r] + int64_t(pos - p.offsets[r]) * H);
-    for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
+    copy_row(reinterpret_cast<uint4*>(pe.rows[r] + int64_t(pos - p.offsets[r]) * H),
+             reinterpret_cast<const uint4*>(x + int64_t(i / K) * H), H, lane);
   }
   signal_peers(pe, world);
 }
@@ -97,16 +114,15 @@ __global__ void __launch_bounds__(256) ep_send_kernel(const int32_t* __restrict_
 // Result rows back to the ranks that sent the pairs: slot s of recv block r
 // (valid when its expert id is >= 0) goes to slot j of rank r's back block
 // for this rank.
-__global__ void __launch_bounds__(256) ep_return_kernel(const uint16_t* __restrict__ y,
+__global__ void __launch_bounds__(kCopyThreads) ep_return_kernel(const uint16_t* __restrict__ y,
                                                         const int32_t* __restrict__ recv_e, int world, int capacity,
                                                         int H, const EpPeers pe) {
   const int lane = threadIdx.x & 31, warps = gridDim.x * blockDim.x >> 5;
   for (int s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; s < world * capacity; s += warps) {
     if (recv_e[s] < 0) continue;
     const int r = s / capacity, j = s - r * capacity;
-    const uint4* src = reinterpret_cast<const uint4*>(y + int64_t(s) * H);
-    uint4* dst = reinterpret_cast<uint4*>(pe.rows[r] + int64_t(j) * H);
-    for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
+    copy_row(reinterpret_cast<uint4*>(pe.rows[r] + int64_t(j) * H), reinterpret_cast<const uint4*>(y + int64_t(s) * H),
+             H, lane);
   }
   signal_peers(pe, world);
 }
@@ -115,7 +131,7 @@ __global__ void __launch_bounds__(256) ep_return_kernel(const uint16_t* __restri
 // slot j < counts[r] of recv block r is row pair_pos[r * capacity + j] of
 // `routed`, and goes to slot j of rank r's back block for this rank.  Fuses
 // the unpermute of the owner's rows with the return.
-__global__ void __launch_bounds__(256) ep_return_sorted_kernel(const uint16_t* __restrict__ routed,
+__global__ void __launch_bounds__(kCopyThreads) ep_return_sorted_kernel(const uint16_t* __restrict__ routed,
                                                                const int32_t* __restrict__ pair_pos,
                                                                const int32_t* __restrict__ counts, int world,
                                                                int capacity, int H, const EpPeers pe) {
@@ -125,9 +141,8 @@ __global__ void __launch_bounds__(256) ep_return_sorted_kernel(const uint16_t* _
     if (j >= min(counts[r], capacity)) continue;
     const int row = pair_pos[s];
     if (row < 0) continue;
-    const uint4* src = reinterpret_cast<const uint4*>(routed + int64_t(row) * H);
-    uint4* dst = reinterpret_cast<uint4*>(pe.rows[r] + int64_t(j) * H);
-    for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
+    copy_row(reinterpret_cast<uint4*>(pe.rows[r] + int64_t(j) * H),
+             reinterpret_cast<const uint4*>(routed + int64_t(row) * H), H, lane);
   }
   signal_peers(pe, world);
 }
@@ -152,17 +167,17 @@ void launch_ep_begin(uint32_t* epoch, cudaStream_t stream) { ep_begin_kernel<<<1
 void launch_ep_send(const int32_t* idx, const Plan& p, int T, int K, int per_rank, int world, int capacity,
                     int32_t* pair_pos, const uint16_t* x, int H, const EpPeers& pe, int num_sms,
                     cudaStream_t stream) {
-  ep_send_kernel<<<num_sms, 256, 0, stream>>>(idx, p, T, K, per_rank, world, capacity, pair_pos, x, H, pe);
+  ep_send_kernel<<<2 * num_sms, kCopyThreads, 0, stream>>>(idx, p, T, K, per_rank, world, capacity, pair_pos, x, H, pe);
 }
 
 void launch_ep_return(const uint16_t* y, const int32_t* recv_e, int world, int capacity, int H, const EpPeers& pe,
                       int num_sms, cudaStream_t stream) {
-  ep_return_kernel<<<num_sms, 256, 0, stream>>>(y, recv_e, world, capacity, H, pe);
+  ep_return_kernel<<<2 * num_sms, kCopyThreads, 0, stream>>>(y, recv_e, world, capacity, H, pe);
 }
 
 void launch_ep_return_sorted(const uint16_t* routed, const int32_t* pair_pos, const int32_t* counts, int world,
                              int capacity, int H, const EpPeers& pe, int num_sms, cudaStream_t stream) {
-  ep_return_sorted_kernel<<<num_sms, 256, 0, stream>>>(routed, pair_pos, counts, world, capacity, H, pe);
+  ep_return_sorted_kernel<<<2 * num_sms, kCopyThreads, 0, stream>>>(routed, pair_pos, counts, world, capacity, H, pe);
 }
 
 void launch_ep_wait(const uint32_t* flags, int world, const uint32_t* epoch, uint32_t* status, int code,

@@ -168,7 +168,14 @@ class ExpertParallelMoE:
         return eng.expert_pairs(self.shared, x, zero).view(x.shape[0], x.shape[1])
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
-        w, idx = self.engine.route(self.layer, x, self.K)
+        if self.layer.norm is not None:
+            # the pre-MoE RMSNorm: routes, experts and the shared expert all read
+            # the normalised rows, which the router writes
+            xn = torch.empty_like(x)
+            w, idx = self.engine.route(self.layer, x, self.K, x_norm=xn)
+            x = xn
+        else:
+            w, idx = self.engine.route(self.layer, x, self.K)
 
         # the shared expert of the local tokens, beside the exchange
         shared_rows = None
