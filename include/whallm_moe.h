@@ -123,6 +123,13 @@ typedef struct {
    the same products; kept for comparison. */
 #define WM_FLAG_TCGEN05_DECODE 2
 
+/* Short MXFP4 calls take the block-scaled tcgen05 decode kernel: the E2M1
+   weights go from the blob to the tensor cores by TMA with their E8M0 scales
+   as the MMA's scale factors (kind::mxf8f6f4), and each token row enters as
+   two E4M3 parts (hi + lo, power-of-two scales per 32 values; within 2^-8 of
+   the row, layer outputs within ~1e-3 of max|y|). */
+#define WM_FLAG_BS_DECODE 4
+
 /* One projection of every expert: expert e's matrix at weight + e * weight_stride
    bytes, its scales at scale + e * scale_stride bytes (device pointers). */
 typedef struct {

@@ -1,0 +1,556 @@
+// Decode path on tcgen05 block-scaled MMA (kind::mxf8f6f4): the MXFP4 expert
+// weights go from the blob to shared memory by TMA and into the tensor cores
+// as they are -- E2M1 elements with their E8M0 group scales applied by the
+// MMA itself -- so no CUDA core touches a weight.
+//
+// Reference arithmetic: the decode GEMVs expert_linear4 / expert_group<R, K>
+// (QwenNative/kernels.metal:1186-1219, DeepSeekNative/kernels.metal:933-987)
+// and mx.quantized_matmul(mode="mxfp4", group_size=32) (model.py:504-513):
+// exact dequantised weights times the activation rows, fp32 accumulation.
+//
+// Operands of one MMA (M = 128 weight rows, N = 32, K = 32):
+//   A  weights: E2M1 nibbles straight from the blob (the TMA type
+//      16U4_ALIGN16B spreads every 8 packed bytes over 16 bytes of shared
+//      memory, the layout kind::mxf8f6f4 reads), K-major, 128-byte swizzle;
+//      scale factors = the blob's E8M0 bytes (UE8M0), one per row and 32 K.
+//   B  token rows as two E4M3 parts: hi = e4m3(x / s_hi) and lo =
+//      e4m3((x - hi * s_hi) / s_lo) with power-of-two scales per row and 32 K
+//      (UE8M0, chosen so no element saturates), hi rows in N 0..15, lo rows
+//      in N 16..31, so one MMA multiplies the weights by both parts and the
+//      epilogue adds the two column halves.  x = hi * s_hi + lo * s_lo + r
+//      with |r| <= 2^-8 |x| per element: the layer outputs stay within
+//      ~1e-3 of the exact products (measured on the CPU against exact
+//      arithmetic at the config-2 and config-4 shapes: 8.5e-4 and 8.8e-4 of
+//      max|y|; one E4M3 part alone gives 4-5e-2).
+//   D  fp32 in TMEM, 128 lanes (weight rows) x 32 columns.
+// Scale factors reach TMEM with tcgen05.cp (32x128b, copied to the four lane
+// quarters): a 512-byte atom per stage in which row r (16 bytes) holds, for
+// the M rows r, r + 32, r + 64, r + 96, the four UE8M0 bytes of the stage's
+// four 32-K blocks; the MMA of block kk reads byte kk (the scale-factor id).
+//
+// Work: an item is (16-token tile of one expert, 128 weight rows); for
+// gate/up the 128 rows are 64 gate and the 64 up rows of the same features
+// (two TMA boxes), so SwiGLU runs in the epilogue, which also quantises the
+// act rows (hi / lo E4M3 + UE8M0, 32 features per warp = one scale block) for
+// the down kernel.  One persistent CTA per SM; warp roles:
+//   warp 0     TMA producer: A boxes, the B tile image and its scale atom
+//              (bulk copies), the raw E8M0 rows of the next four stages
+//   warp 1     scale warp: raw E8M0 rows -> the stage's scale-factor atom
+//   warp 2     TMEM owner and MMA issuer (one elected lane)
+//   warps 4-7  epilogue (TMEM lane quarters 0..3)
+// Every mbarrier wait is bounded (2 s); on a timeout the kernel records the
+// status, the other roles unwind and TMEM is freed.
+#include <cuda.h>
+
+#include <algorithm>
+
+#include "wm_kernels.h"
+
+namespace wm {
+
+namespace {
+
+constexpr int kBM = 128;         // weight rows per item (MMA M)
+constexpr int kBK = 128;         // K per stage (four 32-K scale blocks)
+constexpr int kTokTile = 16;     // tokens per item; N = 2 x 16 (hi and lo parts)
+constexpr int kN = 2 * kTokTile;
+constexpr int kThreads = 256;
+constexpr int kEpiWarp0 = 4;
+constexpr int kRawSlots = 3;     // raw E8M0 slots, four stages each
+constexpr int kAccCols = kN;     // TMEM columns per accumulator
+constexpr uint32_t kTmemCols = 128;
+constexpr uint32_t kSfCol0 = 2 * kAccCols;  // scale factors after the two accumulators
+
+// Transaction bytes of one 128 x 128 E2M1 box loaded as 16U4_ALIGN16B.
+constexpr uint32_t kATxBytes = kBM * kBK / 2;
+constexpr int kASmem = kBM * kBK;          // unpacked: 16 bytes per 16 elements + 8-byte gaps
+constexpr int kBSmem = kN * kBK;           // 32 rows x 128 bytes
+constexpr int kAtom = 512;
+constexpr int kStageBytes = kASmem + kBSmem + 2 * kAtom;  // A, B, SFA atom, SFB atom
+constexpr int kRawBytes = kBM * 16;        // 128 rows x 16 E8M0 bytes (four stages)
+
+struct BsShared {
+  uint64_t full[16];
+  uint64_t empty[16];
+  uint64_t raw_full[kRawSlots];
+  uint64_t raw_empty[kRawSlots];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint64_t xch_full[2];   // gate/up: the up warps wrote xch[b]
+  uint64_t xch_empty[2];  // the gate warps read it
+  uint64_t mma_done;      // every MMA of this CTA has completed (before TMEM is freed)
+  uint32_t tmem_base;
+  int abort;
+  float xch[2][64][kTokTile];  // gate/up: the up rows' sums for the gate warps
+};
+
+int bs_stages(int) { return 8; }
+
+size_t bs_smem_bytes(int stages) {
+  return size_t(stages) * kStageBytes + size_t(kRawSlots) * kRawBytes + sizeof(BsShared) + 1024;
+}
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(dst),
+      "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory descriptor of a scale-factor atom for tcgen05.cp: 32 rows of
+// 16 bytes, no swizzle, 8-row core matrices 128 bytes apart.
+__device__ __forceinline__ uint64_t sf_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= uint64_t((addr >> 4) & 0x3FFFu);
+  d |= uint64_t(128u >> 4) << 16;
+  d |= uint64_t(128u >> 4) << 32;
+  d |= uint64_t(1u) << 46;
+  return d;
+}
+
+__device__ __forceinline__ void sf_copy(uint32_t taddr, uint64_t desc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc) : "memory");
+}
+
+// kind::mxf8f6f4 instruction descriptor: A E2M1, B E4M3, both K-major,
+// UE8M0 scales, M = 128, N = kN, scale-factor ids kk for A and B.
+__device__ __forceinline__ uint32_t bs_idesc(uint32_t kk) {
+  return (kk << 4) | (5u << 7) | (0u << 10) | (uint32_t(kN >> 3) << 17) | (1u << 23) | (uint32_t(kBM >> 4) << 24) |
+         (kk << 29);
+}
+
+__device__ __forceinline__ void bs_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+
+__device__ __forceinline__ void sts_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+__device__ __forceinline__ uint32_t lds_b32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ the hi / lo E4M3 parts
+
+// Power-of-two scale for a 32-element block of largest magnitude `amax`: the
+// smallest 2^e with amax / 2^e <= 448 (E4M3's largest finite value), as the
+// UE8M0 byte e + 127 (clamped to [1, 254]; 1 for an all-zero block).
+__device__ __forceinline__ uint32_t e4m3_block_scale(float amax) {
+  if (!(amax > 0.0f)) return 1u;
+  const int eb = int((__float_as_uint(amax) >> 23) & 0xFFu);  // biased exponent of amax
+  if (eb == 0) return 1u;
+  // amax in [2^(eb-127), 2^(eb-126)); with e = eb - 127 - 8, amax / 2^e in [256, 512)
+  int e = eb - 127 - 8;
+  if (amax > 448.0f * __uint_as_float(uint32_t(e + 127) << 23)) e += 1;
+  return uint32_t(min(max(e + 127, 1), 254));
+}
+
+// Two floats -> two E4M3 bytes (round to nearest even, saturating), low byte = a.
+__device__ __forceinline__ uint32_t to_e4m3x2(float a, float b) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(b), "f"(a));
+  return r;
+}
+
+// 32 values -> hi and lo E4M3 bytes (32 each) and their UE8M0 scale bytes.
+__device__ __forceinline__ void split_block(const float* v, uint32_t* hi, uint32_t* lo, uint32_t* shi, uint32_t* slo) {
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  const uint32_t bh = e4m3_block_scale(amax);
+  const float inv_h = __uint_as_float((254u - bh) << 23), sc_h = __uint_as_float(bh << 23);
+  float r[32];
+  float rmax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) {
+    const uint32_t p01 = to_e4m3x2(v[i] * inv_h, v[i + 1] * inv_h);
+    const uint32_t p23 = to_e4m3x2(v[i + 2] * inv_h, v[i + 3] * inv_h);
+    hi[i / 4] = p01 | (p23 << 16);
+    float q[4];
+    e4m3x4_to_f32(hi[i / 4], q);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      r[i + j] = v[i + j] - q[j] * sc_h;  // exact: x and its rounded part share a binade
+      rmax = fmaxf(rmax, fabsf(r[i + j]));
+    }
+  }
+  const uint32_t bl = e4m3_block_scale(rmax);
+  const float inv_l = __uint_as_float((254u - bl) << 23);
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) {
+    const uint32_t p01 = to_e4m3x2(r[i] * inv_l, r[i + 1] * inv_l);
+    const uint32_t p23 = to_e4m3x2(r[i + 2] * inv_l, r[i + 3] * inv_l);
+    lo[i / 4] = p01 | (p23 << 16);
+  }
+  *shi = bh;
+  *slo = bl;
+}
+
+// Byte offset of (row n of a 32-row part image, 16-byte chunk c) in the
+// 128-byte swizzled layout the MMA reads (chunk c of row n at c ^ (n % 8)).
+__device__ __forceinline__ int image_off(int n, int c) { return n * 128 + ((c ^ (n & 7)) << 4); }
+
+// x rows (sorted by the plan, 16-row tiles) -> tile images: for tile j and
+// stage s, 4096 bytes = hi rows 0..15 then lo rows 16..31 of K [128 s, 128 s +
+// 128) in the swizzled layout, plus a 512-byte scale atom (row n: bytes 0..3 =
+// the four 32-K blocks' UE8M0 of part row n).  One warp per row, one 32-K
+// block per lane step; padding rows are skipped (their MMA columns are never
+// read).
+__global__ void __launch_bounds__(256) bs_quant_rows_kernel(const uint16_t* __restrict__ x, Plan p, int E, int K,
+                                                            uint8_t* __restrict__ img, uint8_t* __restrict__ sfb) {
+  const int rows = p.offsets[E + 1];
+  const int lane = threadIdx.x & 31;
+  const int S = K / kBK;
+  for (int r = blockIdx.x * 8 + (threadIdx.x >> 5); r < rows; r += gridDim.x * 8) {
+    const int t = p.row_token[r];
+    if (t < 0) continue;
+    const int j = r / kTokTile, n = r % kTokTile;
+    const uint16_t* src = x + int64_t(t) * K;
+    for (int g = lane; g < K / 32; g += 32) {
+      float v[32];
+      const uint4* s4 = reinterpret_cast<const uint4*>(src + g * 32);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 u = s4[q];
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = unpack_bf16x2(w[i]);
+          v[8 * q + 2 * i] = f.x;
+          v[8 * q + 2 * i + 1] = f.y;
+        }
+      }
+      uint32_t hi[8], lo[8], bh, bl;
+      split_block(v, hi, lo, &bh, &bl);
+      const int s = g / 4, kk = g % 4;
+      uint8_t* base = img + (int64_t(j) * S + s) * 4096;
+      uint4* h0 = reinterpret_cast<uint4*>(base + image_off(n, 2 * kk));
+      uint4* h1 = reinterpret_cast<uint4*>(base + image_off(n, 2 * kk + 1));
+      uint4* l0 = reinterpret_cast<uint4*>(base + image_off(kTokTile + n, 2 * kk));
+      uint4* l1 = reinterpret_cast<uint4*>(base + image_off(kTokTile + n, 2 * kk + 1));
+      *h0 = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      *h1 = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+      *l0 = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      *l1 = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+      uint8_t* sa = sfb + (int64_t(j) * S + s) * kAtom;
+      sa[n * 16 + kk] = uint8_t(bh);
+      sa[(kTokTile + n) * 16 + kk] = uint8_t(bl);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ the expert kernel
+
+// KIND 0: gate/up + SwiGLU -> act tile images (hi / lo E4M3 + scale atoms) for
+// KIND 1; KIND 1: down -> routed [rows, H] bf16.
+template <int KIND>
+__global__ void __launch_bounds__(kThreads, 1) bs_decode_kernel(const __grid_constant__ CUtensorMap tm_w,
+                                                                const __grid_constant__ CUtensorMap tm_ws,
+                                                                const __grid_constant__ CUtensorMap tm_s,
+                                                                const __grid_constant__ CUtensorMap tm_ss,
+                                                                const BsArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  const int K = KIND == 0 ? a.H : a.I;
+  const int S = K / kBK;  // stages per item
+  const int nb = KIND == 0 ? a.I / 64 : a.H / kBM;
+  const int NS = a.stages;
+  const int n_items = *a.plan.n_mtiles * nb;
+  const uint32_t raw0 = smem_u32(smem_raw);
+  const uint32_t base = (raw0 + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw0);
+  BsShared& sh = *reinterpret_cast<BsShared*>(gbase + NS * kStageBytes + kRawSlots * kRawBytes);
+  const uint32_t raw_base = base + NS * kStageBytes;
+  auto a_addr = [&](int slot) { return base + slot * kStageBytes; };
+  auto b_addr = [&](int slot) { return base + slot * kStageBytes + kASmem; };
+  auto sfa_addr = [&](int slot) { return base + slot * kStageBytes + kASmem + kBSmem; };
+  auto sfb_addr = [&](int slot) { return base + slot * kStageBytes + kASmem + kBSmem + kAtom; };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&sh.full[i], 2);  // the TMA producer (with bytes) and the scale warp
+      mbar_init(&sh.empty[i], 1);
+    }
+    for (int i = 0; i < kRawSlots; ++i) {
+      mbar_init(&sh.raw_full[i], 1);
+      mbar_init(&sh.raw_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sh.tmem_full[i], 1);
+      mbar_init(&sh.tmem_empty[i], 4);
+      mbar_init(&sh.xch_full[i], 2);
+      mbar_init(&sh.xch_empty[i], 2);
+    }
+    mbar_init(&sh.mma_done, 1);
+    sh.abort = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&sh.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  volatile int* abort = &sh.abort;
+  auto fail = [&](uint32_t role) {
+    if (atomicExch(&sh.abort, 1) == 0) report_status(a.status, kStatusWaitTimeout, role);
+  };
+  auto item = [&](int q, int* e, int* row0, int* blk) {
+    const int tile = q / nb;
+    *blk = q - tile * nb;
+    *e = a.plan.mtiles[2 * tile];
+    *row0 = a.plan.mtiles[2 * tile + 1];
+  };
+  const int gate_base = a.gate_first ? 0 : a.I, up_base = a.gate_first ? a.I : 0;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_w);
+      tma_prefetch_desc(&tm_s);
+      int st = 0, ph = 0, rs = 0, rph = 0;
+      for (int q = blockIdx.x; q < n_items && !*abort; q += gridDim.x) {
+        int e, row0, blk;
+        item(q, &e, &row0, &blk);
+        const bool shared_e = e == a.wts.E;
+        const void* mw = shared_e ? &tm_ws : &tm_w;
+        const void* ms = shared_e ? &tm_ss : &tm_s;
+        const int ez = shared_e ? 0 : e;
+        const int tile = row0 / kTokTile;
+        for (int s = 0; s < S; ++s) {
+          if ((s & 3) == 0) {
+            if (!mbar_wait(&sh.raw_empty[rs], rph ^ 1, abort)) { fail(70 + KIND); break; }
+            const uint32_t dst = raw_base + rs * kRawBytes;
+            mbar_arrive_expect_tx(&sh.raw_full[rs], kRawBytes);
+            if (KIND == 0) {
+              tma_load_3d(dst, ms, 16 * (s >> 2), gate_base + blk * 64, ez, &sh.raw_full[rs]);
+              tma_load_3d(dst + 64 * 16, ms, 16 * (s >> 2), up_base + blk * 64, ez, &sh.raw_full[rs]);
+            } else {
+              tma_load_3d(dst, ms, 16 * (s >> 2), blk * kBM, ez, &sh.raw_full[rs]);
+            }
+            if (++rs == kRawSlots) { rs = 0; rph ^= 1; }
+          }
+          if (!mbar_wait(&sh.empty[st], ph ^ 1, abort)) { fail(72 + KIND); break; }
+          mbar_arrive_expect_tx(&sh.full[st], kATxBytes + 4096u + kAtom);
+          if (KIND == 0) {
+            tma_load_3d(a_addr(st), mw, s * kBK, gate_base + blk * 64, ez, &sh.full[st]);
+            tma_load_3d(a_addr(st) + 64 * 128, mw, s * kBK, up_base + blk * 64, ez, &sh.full[st]);
+          } else {
+            tma_load_3d(a_addr(st), mw, s * kBK, blk * kBM, ez, &sh.full[st]);
+          }
+          const int64_t ti = int64_t(tile) * S + s;
+          bulk_g2s(b_addr(st), a.img + ti * 4096, 4096u, &sh.full[st]);
+          bulk_g2s(sfb_addr(st), a.sfb + ti * kAtom, uint32_t(kAtom), &sh.full[st]);
+          if (++st == NS) { st = 0; ph ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- scale warp
+    int st = 0, ph = 0, rs = 0, rph = 0;
+    for (int q = blockIdx.x; q < n_items; q += gridDim.x) {
+      if (warp_aborted(abort)) break;
+      bool ok = true;
+      for (int s = 0; s < S && ok; ++s) {
+        if ((s & 3) == 0 && !warp_wait(&sh.raw_full[rs], rph, abort)) { ok = false; break; }
+        if (!warp_wait(&sh.empty[st], ph ^ 1, abort)) { ok = false; break; }
+        // row lane + 32 m1 of the tile, bytes of the stage's four 32-K blocks
+        const uint32_t rb = raw_base + rs * kRawBytes + 4 * (s & 3);
+        const uint32_t w0 = lds_b32(rb + (lane)*16), w1 = lds_b32(rb + (lane + 32) * 16),
+                       w2 = lds_b32(rb + (lane + 64) * 16), w3 = lds_b32(rb + (lane + 96) * 16);
+        sts_v4(sfa_addr(st) + lane * 16, w0, w1, w2, w3);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.full[st]);
+        if (++st == NS) { st = 0; ph ^= 1; }
+        if ((s & 3) == 3) {
+          if (lane == 0) mbar_arrive(&sh.raw_empty[rs]);
+          if (++rs == kRawSlots) { rs = 0; rph ^= 1; }
+        }
+      }
+      if (!ok) {
+        if (lane == 0) fail(74 + KIND);
+        break;
+      }
+    }
+  } else if (warp == 2) {
+    // ---------------------------------------------------------------- MMA issuer
+    int st = 0, ph = 0, li = 0;
+    for (int q = blockIdx.x; q < n_items; q += gridDim.x, ++li) {
+      if (warp_aborted(abort)) break;
+      const int acc = li & 1;
+      if (!warp_wait(&sh.tmem_empty[acc], ((li >> 1) & 1) ^ 1, abort)) {
+        if (lane == 0) fail(76 + KIND);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d = tmem + acc * kAccCols;
+      bool ok = true;
+      for (int s = 0; s < S; ++s) {
+        if (!warp_wait(&sh.full[st], ph, abort)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sfa_t = tmem + kSfCol0 + st * 8, sfb_t = sfa_t + 4;
+        uint32_t e;
+        asm volatile("{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.b32 %0, 1, 0, p;\n\t}" : "=r"(e));
+        if (e) {
+          sf_copy(sfa_t, sf_desc(sfa_addr(st)));
+          sf_copy(sfb_t, sf_desc(sfb_addr(st)));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            bs_mma(d, umma_desc_sw128(a_addr(st) + 32 * kk), umma_desc_sw128(b_addr(st) + 32 * kk),
+                   bs_idesc(uint32_t(kk)), sfa_t | (uint32_t(kk) << 30), sfb_t | (uint32_t(kk) << 30),
+                   (s > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&sh.empty[st]);
+        }
+        __syncwarp();
+        if (++st == NS) { st = 0; ph ^= 1; }
+      }
+      if (!ok) {
+        if (lane == 0) fail(78 + KIND);
+        break;
+      }
+      umma_commit_elect(&sh.tmem_full[acc]);
+      __syncwarp();
+    }
+    // every MMA issued here has completed before TMEM is freed (bounded wait)
+    umma_commit_elect(&sh.mma_done);
+    __syncwarp();
+    volatile int keep_waiting = 0;  // this wait ignores the abort flag (0.2 s bound)
+    mbar_wait(&sh.mma_done, 0, &keep_waiting, 0, 200000000ull);
+  } else if (warp >= kEpiWarp0) {
+    // ---------------------------------------------------------------- epilogue
+    const int quarter = warp - kEpiWarp0;  // TMEM lanes 32 quarter .. 32 quarter + 31
+    int li = 0;
+    for (int q = blockIdx.x; q < n_items; q += gridDim.x, ++li) {
+      if (warp_aborted(abort)) break;
+      int e, row0, blk;
+      item(q, &e, &row0, &blk);
+      const int valid = min(kTokTile, a.plan.counts[e] - (row0 - a.plan.offsets[e]));
+      const int acc = li & 1;
+      if (!warp_wait(&sh.tmem_full[acc], (li >> 1) & 1, abort)) {
+        if (lane == 0) fail(80 + KIND);
+        break;
+      }
+      tc_fence_after();
+      uint32_t r[32];
+      tmem_ld_32cols(tmem + acc * kAccCols + (uint32_t(quarter * 32) << 16), r);
+      tmem_ld_wait();
+      float y[kTokTile];
+#pragma unroll
+      for (int n = 0; n < kTokTile; ++n) y[n] = __uint_as_float(r[n]) + __uint_as_float(r[kTokTile + n]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.tmem_empty[acc]);
+      if (KIND == 1) {
+        const int h = blk * kBM + quarter * 32 + lane;
+        for (int n = 0; n < valid; ++n) a.routed[int64_t(row0 + n) * a.H + h] = f32_to_bf16_bits(y[n]);
+      } else {
+        // gate rows in quarters 0, 1; the up rows of the same features in 2, 3
+        const int xb = li & 1;
+        const uint32_t xph = (li >> 1) & 1;
+        if (quarter >= 2) {
+          if (!warp_wait(&sh.xch_empty[xb], xph ^ 1, abort)) {
+            if (lane == 0) fail(82);
+            break;
+          }
+#pragma unroll
+          for (int n = 0; n < kTokTile; ++n) sh.xch[xb][(quarter - 2) * 32 + lane][n] = y[n];
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sh.xch_full[xb]);
+        } else {
+          if (!warp_wait(&sh.xch_full[xb], xph, abort)) {
+            if (lane == 0) fail(83);
+            break;
+          }
+          const int f = blk * 64 + quarter * 32 + lane;  // feature (act column)
+          const int Sd = a.I / kBK, sd = f / kBK, kk = (f % kBK) / 32;
+          const int tile = row0 / kTokTile;
+          uint8_t* img = a.act_img + (int64_t(tile) * Sd + sd) * 4096;
+          uint8_t* sfb = a.act_sfb + (int64_t(tile) * Sd + sd) * kAtom;
+          const int c = (f % kBK) / 16, byte = f % 16;
+          for (int n = 0; n < valid; ++n) {
+            const float gv = bf16_round(y[n]), uv = bf16_round(sh.xch[xb][quarter * 32 + lane][n]);
+            const float act = bf16_round(swiglu_f32(gv, uv, a.limit));
+            // hi / lo parts of this token's 32 features (one scale block per warp)
+            float amax = fabsf(act);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const uint32_t bh = e4m3_block_scale(amax);
+            const uint32_t hb = to_e4m3x2(act * __uint_as_float((254u - bh) << 23), 0.0f) & 0xFFu;
+            float hv[4];
+            e4m3x4_to_f32(hb, hv);
+            const float res = act - hv[0] * __uint_as_float(bh << 23);
+            float rmax = fabsf(res);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, o));
+            const uint32_t bl = e4m3_block_scale(rmax);
+            const uint32_t lb = to_e4m3x2(res * __uint_as_float((254u - bl) << 23), 0.0f) & 0xFFu;
+            img[image_off(n, c) + byte] = uint8_t(hb);
+            img[image_off(kTokTile + n, c) + byte] = uint8_t(lb);
+            if (lane == 0) {
+              sfb[n * 16 + kk] = uint8_t(bh);
+              sfb[(kTokTile + n) * 16 + kk] = uint8_t(bl);
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sh.xch_empty[xb]);  // xch[xb] is free again
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+void bs_init_attributes() {
+  const int bytes = int(bs_smem_bytes(bs_stages(0)));
+  cudaFuncSetAttribute(bs_decode_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  cudaFuncSetAttribute(bs_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+bool bs_shape_ok(int H, int I) { return H % 512 == 0 && I % 512 == 0 && H >= 512 && I >= 512; }
+
+void launch_bs_quant_rows(const uint16_t* x, const Plan& p, int E, int K, uint8_t* img, uint8_t* sfb, int num_sms,
+                          cudaStream_t stream) {
+  bs_quant_rows_kernel<<<num_sms * 4, 256, 0, stream>>>(x, p, E, K, img, sfb);
+}
+
+void launch_bs_decode(const BsArgs& args, int kind, const void* const* maps, int num_sms, cudaStream_t stream) {
+  BsArgs a = args;
+  a.stages = bs_stages(kind == 0 ? a.H : a.I);
+  const size_t smem = bs_smem_bytes(a.stages);
+  const CUtensorMap* m = static_cast<const CUtensorMap*>(maps[0]);
+  const CUtensorMap* ms = static_cast<const CUtensorMap*>(maps[1]);
+  const CUtensorMap* s = static_cast<const CUtensorMap*>(maps[2]);
+  const CUtensorMap* ss = static_cast<const CUtensorMap*>(maps[3]);
+  if (kind == 0)
+    bs_decode_kernel<0><<<num_sms, kThreads, smem, stream>>>(*m, *ms, *s, *ss, a);
+  else
+    bs_decode_kernel<1><<<num_sms, kThreads, smem, stream>>>(*m, *ms, *s, *ss, a);
+}
+
+}  // namespace wm

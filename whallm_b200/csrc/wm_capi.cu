@@ -37,6 +37,8 @@ struct wm_ctx {
   float* actscale = nullptr;   // [rows] prescale of the f16 act rows (decode path)
   uint32_t* rowmax = nullptr;  // [rows] per-row |act| maxima (decode path)
   uint16_t* xn = nullptr;      // [T, H] normalised input rows (pre-MoE RMSNorm)
+  uint8_t* bs_sfb_x = nullptr;    // block-scaled decode: scale atoms of the token tile images
+  uint8_t* bs_sfb_act = nullptr;  // ... and of the act tile images
   int max_rows = 0, max_mtiles = 0, max_chunks = 0;
   PFN_cuTensorMapEncodeTiled_v12000 encode_tiled = nullptr;
   wm::Profiler prof;
@@ -287,7 +289,20 @@ bool use_gemm(const wm_ctx* ctx, const wm_moe_args* a) {
   return gemm && wm::gemm_shape_ok(a->H, a->I) && ctx->encode_tiled != nullptr;
 }
 
-enum Path { kPathGemv = 0, kPathDecode = 1, kPathGemm = 2, kPathDecodeMma = 3 };
+enum Path { kPathGemv = 0, kPathDecode = 1, kPathGemm = 2, kPathDecodeMma = 3, kPathBsDecode = 4 };
+
+// The block-scaled decode kernel's TMA operands: packed weights 32-byte
+// aligned with 32-byte multiple strides (16U4_ALIGN16B), E8M0 rows 16-byte
+// aligned with 16-byte multiple strides.
+bool bs_operands_ok(const wm_ctx* ctx, const wm_moe_args* a, bool has_shared) {
+  if (ctx->encode_tiled == nullptr || is_fp8(a->layout) || !wm::bs_shape_ok(a->H, a->I)) return false;
+  const wm_matrix* ms[4] = {&a->w13, &a->w2, &a->shared_w13, &a->shared_w2};
+  for (int i = 0; i < (has_shared ? 4 : 2); ++i) {
+    if (!aligned(ms[i]->weight, 32) || !aligned(ms[i]->scale, 16)) return false;
+    if (i < 2 && (ms[i]->weight_stride % 32 || ms[i]->scale_stride % 16)) return false;
+  }
+  return true;
+}
 
 // Which expert kernels a call takes: the tcgen05 grouped GEMM for long calls;
 // for short MXFP4 calls whose weights and scale rows allow 16-byte loads the
@@ -299,12 +314,18 @@ Path expert_path(const wm_ctx* ctx, const wm_moe_args* a, bool has_shared) {
   const wm_matrix* ms[4] = {&a->w13, &a->w2, &a->shared_w13, &a->shared_w2};
   for (int i = 0; i < (has_shared ? 4 : 2); ++i)
     if (!aligned(ms[i]->scale, 16) || (i < 2 && ms[i]->scale_stride % 16)) return kPathGemv;
+  if (!is_fp8(a->layout) && (ctx->opt.flags & WM_FLAG_BS_DECODE) && bs_operands_ok(ctx, a, has_shared))
+    return kPathBsDecode;
   if (!is_fp8(a->layout) && (ctx->opt.flags & WM_FLAG_TCGEN05_DECODE))
     return wm::decode_shape_ok(a->H, a->I) ? kPathDecode : kPathGemv;
   for (int i = 0; i < (has_shared ? 4 : 2); ++i)
     if (!aligned(ms[i]->weight, 16) || (i < 2 && ms[i]->weight_stride % 16)) return kPathGemv;
   return wm::decode_mma_shape_ok(a->H, a->I, fmt_of(a->layout)) ? kPathDecodeMma : kPathGemv;
 }
+
+// Rows each expert's group is padded to: the GEMM's 128-row tiles, the
+// block-scaled decode kernel's 16-token tiles, else none.
+int plan_align(Path path) { return path == kPathGemm ? wm::kTileM : path == kPathBsDecode ? 16 : 1; }
 
 // Plan fields of the expert kernels of `path`.
 void plan_for_path(const wm_ctx* ctx, Path path, wm::Plan* plan) {
@@ -388,6 +409,72 @@ int run_decode_mma(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& w
   return check_launch(ctx, "expert decode");
 }
 
+// TMA descriptor over one projection's packed E2M1 weights as the block-scaled
+// MMA reads them: [experts][rows][K] 4-bit elements (16U4_ALIGN16B: every 8
+// packed bytes land in 16 bytes of shared memory), boxes of 128 K x box_rows,
+// 128-byte swizzle.
+bool encode_fp4_weights(wm_ctx* ctx, CUtensorMap* map, const void* base, int64_t K, int64_t rows, int64_t experts,
+                        int64_t expert_stride, int box_rows) {
+  if (ctx->encode_tiled == nullptr) return false;
+  cuuint64_t dims[3] = {cuuint64_t(K), cuuint64_t(rows), cuuint64_t(experts)};
+  cuuint64_t strides[2] = {cuuint64_t(K / 2), cuuint64_t(experts > 1 ? expert_stride : K / 2 * rows)};
+  cuuint32_t box[3] = {128, cuuint32_t(box_rows), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, const_cast<void*>(base), dims, strides,
+                                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// The block-scaled decode path: hi / lo E4M3 token tiles, gate/up (+SwiGLU,
+// act tiles), down.  The plan's groups are padded to 16 rows.
+int run_bs_decode(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts, bool has_shared, cudaStream_t s) {
+  const int H = a->H, I = a->I;
+  CUtensorMap w13, w13s, w2, w2s, s13, s13s, s2, s2s;
+  bool ok = encode_fp4_weights(ctx, &w13, a->w13.weight, H, 2 * I, a->E, a->w13.weight_stride, 64) &&
+            encode_fp4_weights(ctx, &w2, a->w2.weight, I, H, a->E, a->w2.weight_stride, 128) &&
+            encode_weights(ctx, &s13, a->w13.scale, H / 32, 2 * I, a->E, a->w13.scale_stride, 16, 64) &&
+            encode_weights(ctx, &s2, a->w2.scale, I / 32, H, a->E, a->w2.scale_stride, 16, 128);
+  if (has_shared)
+    ok = ok && encode_fp4_weights(ctx, &w13s, a->shared_w13.weight, H, 2 * I, 1, 0, 64) &&
+         encode_fp4_weights(ctx, &w2s, a->shared_w2.weight, I, H, 1, 0, 128) &&
+         encode_weights(ctx, &s13s, a->shared_w13.scale, H / 32, 2 * I, 1, 0, 16, 64) &&
+         encode_weights(ctx, &s2s, a->shared_w2.scale, I / 32, H, 1, 0, 16, 128);
+  if (!ok) return fail(ctx, "cuTensorMapEncodeTiled failed for the block-scaled expert operands");
+  uint8_t* ximg = reinterpret_cast<uint8_t*>(ctx->xs);      // [rows, H] x 2 bytes: the token tile images
+  uint8_t* aimg = reinterpret_cast<uint8_t*>(ctx->act16);   // [rows, I] x 2 bytes: the act tile images
+  wm::BsArgs b{};
+  b.plan = ctx->plan;
+  b.wts = wts;
+  b.H = H;
+  b.I = I;
+  b.gate_first = a->layout == WM_LAYOUT_QWEN_GATE_UP_MXFP4 ? 1 : 0;
+  b.limit = a->swiglu_limit;
+  b.status = ctx->status;
+  b.act_img = aimg;
+  b.act_sfb = ctx->bs_sfb_act;
+  b.routed = ctx->routed;
+  wm::prof_begin(&ctx->prof, wm::kProfGather, s);
+  wm::launch_bs_quant_rows(static_cast<const uint16_t*>(a->x), b.plan, a->E, H, ximg,
+                           ctx->bs_sfb_x, ctx->num_sms, s);
+  wm::prof_end(&ctx->prof, wm::kProfGather, s);
+  b.img = ximg;
+  b.sfb = ctx->bs_sfb_x;
+  wm::prof_begin(&ctx->prof, wm::kProfDecodeGateUp, s);
+  const void* maps0[4] = {&w13, has_shared ? &w13s : &w13, &s13, has_shared ? &s13s : &s13};
+  wm::launch_bs_decode(b, 0, maps0, ctx->num_sms, s);
+  wm::prof_end(&ctx->prof, wm::kProfDecodeGateUp, s);
+  b.img = aimg;
+  b.sfb = ctx->bs_sfb_act;
+  wm::prof_begin(&ctx->prof, wm::kProfDecodeDown, s);
+  const void* maps1[4] = {&w2, has_shared ? &w2s : &w2, &s2, has_shared ? &s2s : &s2};
+  wm::launch_bs_decode(b, 1, maps1, ctx->num_sms, s);
+  wm::prof_end(&ctx->prof, wm::kProfDecodeDown, s);
+  ctx->counters.launches += 3;
+  ctx->counters.decode_calls += 1;
+  return check_launch(ctx, "block-scaled expert decode");
+}
+
 // The tcgen05 decode path: per-token prescale, gate/up (+SwiGLU), down.
 int run_decode(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts, bool has_shared, cudaStream_t s) {
   const int H = a->H, I = a->I;
@@ -451,6 +538,7 @@ int run_experts(wm_ctx* ctx, const wm_moe_args* a, bool has_shared, Path path, c
   const int gate_first = a->layout == WM_LAYOUT_QWEN_GATE_UP_MXFP4 ? 1 : 0;
   if (path == kPathDecode) return run_decode(ctx, a, wts, has_shared, s);
   if (path == kPathDecodeMma) return run_decode_mma(ctx, a, wts, s);
+  if (path == kPathBsDecode) return run_bs_decode(ctx, a, wts, has_shared, s);
   if (path == kPathGemv) {
     wm::GemvArgs g{};
     g.plan = ctx->plan;
@@ -540,7 +628,7 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
     return nullptr;
   }
   wm_options o = *options;
-  if (o.flags & ~int32_t(WM_FLAG_SKIP_NEGATIVE_ROUTES | WM_FLAG_TCGEN05_DECODE)) {
+  if (o.flags & ~int32_t(WM_FLAG_SKIP_NEGATIVE_ROUTES | WM_FLAG_TCGEN05_DECODE | WM_FLAG_BS_DECODE)) {
     report("unknown flags");
     return nullptr;
   }
@@ -594,7 +682,8 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
                o_act = take(rows * I * 2), o_routed = take(rows * H * 2), o_logits = take(T * E * 4),
                o_idx = take(T * K * 4), o_w = take(T * K * 4), o_sg = take(T * 4), o_status = take(16),
                o_act16 = take(rows * I * 2), o_rowscale = take(rows * 4), o_actscale = take(rows * 4),
-               o_rowmax = take(rows * 4), o_xn = take(T * H * 2);
+               o_rowmax = take(rows * 4), o_xn = take(T * H * 2), o_sfbx = take(rows * H / 4),
+               o_sfba = take(rows * I / 4);
   ctx->ws_bytes = off;
   if (cudaMalloc(&ctx->ws, ctx->ws_bytes) != cudaSuccess) {
     cudaGetLastError();
@@ -627,6 +716,8 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
   ctx->actscale = reinterpret_cast<float*>(base + o_actscale);
   ctx->rowmax = reinterpret_cast<uint32_t*>(base + o_rowmax);
   ctx->xn = reinterpret_cast<uint16_t*>(base + o_xn);
+  ctx->bs_sfb_x = base + o_sfbx;
+  ctx->bs_sfb_act = base + o_sfba;
   // the whole workspace starts at zero (status word included); padding rows of
   // the f16 row blocks are never written afterwards, so they hold zeros or an
   // earlier call's finite rows
@@ -648,6 +739,7 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
   wm::gemm_init_attributes();
   wm::decode_init_attributes();
   wm::decode_mma_init_attributes(int(H), int(I));
+  wm::bs_init_attributes();
   wm::router_init_attributes(int(H));
   wm::router_gemm_init_attributes();
   cudaDriverEntryPointQueryResult q{};
@@ -771,7 +863,7 @@ WM_EXPORT int wm_expert_pairs(wm_ctx* ctx, const wm_moe_args* a, void* routed, v
   plan.skip_negative = (ctx->opt.flags & WM_FLAG_SKIP_NEGATIVE_ROUTES) ? 1 : 0;
   int launches = 0;
   wm::prof_begin(&ctx->prof, wm::kProfPlan, s);
-  wm::launch_plan(b.routes_idx, b.T, b.K, b.E, false, path == kPathGemm ? wm::kTileM : 1, plan, ctx->max_rows,
+  wm::launch_plan(b.routes_idx, b.T, b.K, b.E, false, plan_align(path), plan, ctx->max_rows,
                   ctx->max_mtiles, ctx->max_chunks, ctx->status, s, &launches);
   wm::prof_end(&ctx->prof, wm::kProfPlan, s);
   ctx->counters.launches += launches;
@@ -1088,7 +1180,7 @@ WM_EXPORT int wm_ep_experts(wm_ctx* ctx, wm_ep* ep, const wm_moe_args* args, voi
   const int32_t* counts = reinterpret_cast<const int32_t*>(own + ep->o_counts);
   int launches = 0;
   wm::prof_begin(&ctx->prof, wm::kProfPlan, s);
-  wm::launch_plan_blocks(b.routes_idx, counts, ep->world, int(ep->capacity), b.E, path == kPathGemm ? wm::kTileM : 1,
+  wm::launch_plan_blocks(b.routes_idx, counts, ep->world, int(ep->capacity), b.E, plan_align(path),
                          plan, ctx->max_rows, ctx->max_mtiles, ctx->max_chunks, ctx->status, s, &launches);
   wm::prof_end(&ctx->prof, wm::kProfPlan, s);
   ctx->counters.launches += launches;
@@ -1126,7 +1218,7 @@ WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* args, void* stream)
   plan.skip_negative = (ctx->opt.flags & WM_FLAG_SKIP_NEGATIVE_ROUTES) ? 1 : 0;
   const int32_t* idx;
   const float* w;
-  const int align = path == kPathGemm ? wm::kTileM : 1;
+  const int align = plan_align(path);
   if (a->router_weight != nullptr) {
     int32_t* di = a->out_idx ? a->out_idx : ctx->idx;
     float* dw = a->out_w ? a->out_w : ctx->w;
