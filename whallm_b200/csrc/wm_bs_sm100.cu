@@ -30,11 +30,12 @@
 //
 // Work: an item is (16-token tile of one expert, 128 weight rows); for
 // gate/up the 128 rows are 64 gate and the 64 up rows of the same features
-// (two TMA boxes), so SwiGLU runs in the epilogue, which also quantises the
+// (one 4-D TMA box over both halves of w13), so SwiGLU runs in the epilogue, which also quantises the
 // act rows (hi / lo E4M3 + UE8M0, 32 features per warp = one scale block) for
 // the down kernel.  One persistent CTA per SM; warp roles:
-//   warp 0     TMA producer: A boxes, the B tile image and its scale atom
-//              (bulk copies), the raw E8M0 rows of the next four stages
+//   warp 0     TMA producer, two copies per stage: the A box (gate and up
+//              rows in one 4-D box) and the B tile image with its scale atom;
+//              every fourth stage the raw E8M0 rows of the next four stages
 //   warp 1     scale warp: raw E8M0 rows -> the stage's scale-factor atom
 //   warp 2     TMEM owner and MMA issuer (one elected lane)
 //   warps 4-7  epilogue (TMEM lane quarters 0..3)
@@ -60,13 +61,16 @@ constexpr int kRawSlots = 3;     // raw E8M0 slots, four stages each
 constexpr int kAccCols = kN;     // TMEM columns per accumulator
 constexpr uint32_t kTmemCols = 128;
 constexpr uint32_t kSfCol0 = 2 * kAccCols;  // scale factors after the two accumulators
+constexpr int kMaxStages = 8;               // ring slots, 4 SFA + 4 SFB columns each
+static_assert(kSfCol0 + 8 * kMaxStages <= kTmemCols, "scale factors exceed the TMEM allocation");
 
 // Transaction bytes of one 128 x 128 E2M1 box loaded as 16U4_ALIGN16B.
 constexpr uint32_t kATxBytes = kBM * kBK / 2;
 constexpr int kASmem = kBM * kBK;          // unpacked: 16 bytes per 16 elements + 8-byte gaps
 constexpr int kBSmem = kN * kBK;           // 32 rows x 128 bytes
 constexpr int kAtom = 512;
-constexpr int kStageBytes = kASmem + kBSmem + 2 * kAtom;  // A, B, SFA atom, SFB atom
+constexpr int kStageBytes = kASmem + kBSmem + 2 * kAtom;  // A, B, SFB atom, SFA atom
+constexpr int kImage = kBSmem + kAtom;     // a token tile image: 32 part rows + their scale atom
 constexpr int kRawBytes = kBM * 16;        // 128 rows x 16 E8M0 bytes (four stages)
 
 struct BsShared {
@@ -84,7 +88,7 @@ struct BsShared {
   float xch[2][64][kTokTile];  // gate/up: the up rows' sums for the gate warps
 };
 
-int bs_stages(int) { return 8; }
+int bs_stages(int) { return kMaxStages; }
 
 size_t bs_smem_bytes(int stages) {
   return size_t(stages) * kStageBytes + size_t(kRawSlots) * kRawBytes + sizeof(BsShared) + 1024;
@@ -94,6 +98,15 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                "l"(src), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int x, int y, int z, int w,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(dst),
+      "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int x, int y, int z, uint64_t* bar) {
@@ -115,8 +128,15 @@ __device__ __forceinline__ uint64_t sf_desc(uint32_t addr) {
   return d;
 }
 
-__device__ __forceinline__ void sf_copy(uint32_t taddr, uint64_t desc) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc) : "memory");
+// Warp-wide issue: every lane of a converged warp executes these and one
+// elected lane issues the instruction (far cheaper than a one-lane branch).
+__device__ __forceinline__ void sf_copy_elect(uint32_t taddr, uint64_t desc) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;\n\t}" ::"r"(taddr),
+      "l"(desc)
+      : "memory");
 }
 
 // kind::mxf8f6f4 instruction descriptor: A E2M1, B E4M3, both K-major,
@@ -126,12 +146,13 @@ __device__ __forceinline__ uint32_t bs_idesc(uint32_t kk) {
          (kk << 29);
 }
 
-__device__ __forceinline__ void bs_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                       uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
+__device__ __forceinline__ void bs_mma_elect(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
+      "{\n\t.reg .pred p, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+      "@e tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
       : "memory");
 }
@@ -209,13 +230,13 @@ __device__ __forceinline__ void split_block(const float* v, uint32_t* hi, uint32
 __device__ __forceinline__ int image_off(int n, int c) { return n * 128 + ((c ^ (n & 7)) << 4); }
 
 // x rows (sorted by the plan, 16-row tiles) -> tile images: for tile j and
-// stage s, 4096 bytes = hi rows 0..15 then lo rows 16..31 of K [128 s, 128 s +
-// 128) in the swizzled layout, plus a 512-byte scale atom (row n: bytes 0..3 =
-// the four 32-K blocks' UE8M0 of part row n).  One warp per row, one 32-K
+// stage s, 4608 bytes = hi rows 0..15 then lo rows 16..31 of K [128 s, 128 s +
+// 128) in the swizzled layout, then a 512-byte scale atom (row n: bytes 0..3 =
+// the four 32-K blocks' UE8M0 of part row n), so one copy brings both.  One warp per row, one 32-K
 // block per lane step; padding rows are skipped (their MMA columns are never
 // read).
 __global__ void __launch_bounds__(256) bs_quant_rows_kernel(const uint16_t* __restrict__ x, Plan p, int E, int K,
-                                                            uint8_t* __restrict__ img, uint8_t* __restrict__ sfb) {
+                                                            uint8_t* __restrict__ img) {
   const int rows = p.offsets[E + 1];
   const int lane = threadIdx.x & 31;
   const int S = K / kBK;
@@ -241,7 +262,7 @@ __global__ void __launch_bounds__(256) bs_quant_rows_kernel(const uint16_t* __re
       uint32_t hi[8], lo[8], bh, bl;
       split_block(v, hi, lo, &bh, &bl);
       const int s = g / 4, kk = g % 4;
-      uint8_t* base = img + (int64_t(j) * S + s) * 4096;
+      uint8_t* base = img + (int64_t(j) * S + s) * kImage;
       uint4* h0 = reinterpret_cast<uint4*>(base + image_off(n, 2 * kk));
       uint4* h1 = reinterpret_cast<uint4*>(base + image_off(n, 2 * kk + 1));
       uint4* l0 = reinterpret_cast<uint4*>(base + image_off(kTokTile + n, 2 * kk));
@@ -250,7 +271,7 @@ __global__ void __launch_bounds__(256) bs_quant_rows_kernel(const uint16_t* __re
       *h1 = make_uint4(hi[4], hi[5], hi[6], hi[7]);
       *l0 = make_uint4(lo[0], lo[1], lo[2], lo[3]);
       *l1 = make_uint4(lo[4], lo[5], lo[6], lo[7]);
-      uint8_t* sa = sfb + (int64_t(j) * S + s) * kAtom;
+      uint8_t* sa = base + kBSmem;
       sa[n * 16 + kk] = uint8_t(bh);
       sa[(kTokTile + n) * 16 + kk] = uint8_t(bl);
     }
@@ -280,8 +301,8 @@ __global__ void __launch_bounds__(kThreads, 1) bs_decode_kernel(const __grid_con
   const uint32_t raw_base = base + NS * kStageBytes;
   auto a_addr = [&](int slot) { return base + slot * kStageBytes; };
   auto b_addr = [&](int slot) { return base + slot * kStageBytes + kASmem; };
-  auto sfa_addr = [&](int slot) { return base + slot * kStageBytes + kASmem + kBSmem; };
-  auto sfb_addr = [&](int slot) { return base + slot * kStageBytes + kASmem + kBSmem + kAtom; };
+  auto sfb_addr = [&](int slot) { return base + slot * kStageBytes + kASmem + kBSmem; };
+  auto sfa_addr = [&](int slot) { return base + slot * kStageBytes + kASmem + kBSmem + kAtom; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -329,9 +350,14 @@ __global__ void __launch_bounds__(kThreads, 1) bs_decode_kernel(const __grid_con
       tma_prefetch_desc(&tm_w);
       tma_prefetch_desc(&tm_s);
       int st = 0, ph = 0, rs = 0, rph = 0;
+      // item metadata is read two items ahead, so no TMA issue waits on a load
+      int ce = 0, crow0 = 0, cblk = 0, ne = 0, nrow0 = 0, nblk = 0;
+      if (int(blockIdx.x) < n_items) item(blockIdx.x, &ce, &crow0, &cblk);
+      if (int(blockIdx.x + gridDim.x) < n_items) item(blockIdx.x + gridDim.x, &ne, &nrow0, &nblk);
       for (int q = blockIdx.x; q < n_items && !*abort; q += gridDim.x) {
-        int e, row0, blk;
-        item(q, &e, &row0, &blk);
+        const int e = ce, row0 = crow0, blk = cblk;
+        int n2e = 0, n2row0 = 0, n2blk = 0;
+        if (q + 2 * int(gridDim.x) < n_items) item(q + 2 * gridDim.x, &n2e, &n2row0, &n2blk);
         const bool shared_e = e == a.wts.E;
         const void* mw = shared_e ? &tm_ws : &tm_w;
         const void* ms = shared_e ? &tm_ss : &tm_s;
@@ -342,27 +368,25 @@ __global__ void __launch_bounds__(kThreads, 1) bs_decode_kernel(const __grid_con
             if (!mbar_wait(&sh.raw_empty[rs], rph ^ 1, abort)) { fail(70 + KIND); break; }
             const uint32_t dst = raw_base + rs * kRawBytes;
             mbar_arrive_expect_tx(&sh.raw_full[rs], kRawBytes);
-            if (KIND == 0) {
-              tma_load_3d(dst, ms, 16 * (s >> 2), gate_base + blk * 64, ez, &sh.raw_full[rs]);
-              tma_load_3d(dst + 64 * 16, ms, 16 * (s >> 2), up_base + blk * 64, ez, &sh.raw_full[rs]);
+            if (KIND == 0) {  // rows blk * 64 .. + 63 of both halves of w13 (one 4-D box)
+              tma_load_4d(dst, ms, 16 * (s >> 2), blk * 64, 0, ez, &sh.raw_full[rs]);
             } else {
               tma_load_3d(dst, ms, 16 * (s >> 2), blk * kBM, ez, &sh.raw_full[rs]);
             }
             if (++rs == kRawSlots) { rs = 0; rph ^= 1; }
           }
           if (!mbar_wait(&sh.empty[st], ph ^ 1, abort)) { fail(72 + KIND); break; }
-          mbar_arrive_expect_tx(&sh.full[st], kATxBytes + 4096u + kAtom);
-          if (KIND == 0) {
-            tma_load_3d(a_addr(st), mw, s * kBK, gate_base + blk * 64, ez, &sh.full[st]);
-            tma_load_3d(a_addr(st) + 64 * 128, mw, s * kBK, up_base + blk * 64, ez, &sh.full[st]);
-          } else {
+          mbar_arrive_expect_tx(&sh.full[st], kATxBytes + uint32_t(kImage));
+          if (KIND == 0)
+            tma_load_4d(a_addr(st), mw, s * kBK, blk * 64, 0, ez, &sh.full[st]);
+          else
             tma_load_3d(a_addr(st), mw, s * kBK, blk * kBM, ez, &sh.full[st]);
-          }
-          const int64_t ti = int64_t(tile) * S + s;
-          bulk_g2s(b_addr(st), a.img + ti * 4096, 4096u, &sh.full[st]);
-          bulk_g2s(sfb_addr(st), a.sfb + ti * kAtom, uint32_t(kAtom), &sh.full[st]);
+          // the token tile image and its scale atom in one copy
+          bulk_g2s(b_addr(st), a.img + (int64_t(tile) * S + s) * kImage, uint32_t(kImage), &sh.full[st]);
           if (++st == NS) { st = 0; ph ^= 1; }
         }
+        ce = ne, crow0 = nrow0, cblk = nblk;
+        ne = n2e, nrow0 = n2row0, nblk = n2blk;
       }
     }
   } else if (warp == 1) {
@@ -371,22 +395,28 @@ __global__ void __launch_bounds__(kThreads, 1) bs_decode_kernel(const __grid_con
     for (int q = blockIdx.x; q < n_items; q += gridDim.x) {
       if (warp_aborted(abort)) break;
       bool ok = true;
-      for (int s = 0; s < S && ok; ++s) {
-        if ((s & 3) == 0 && !warp_wait(&sh.raw_full[rs], rph, abort)) { ok = false; break; }
-        if (!warp_wait(&sh.empty[st], ph ^ 1, abort)) { ok = false; break; }
-        // row lane + 32 m1 of the tile, bytes of the stage's four 32-K blocks
-        const uint32_t rb = raw_base + rs * kRawBytes + 4 * (s & 3);
-        const uint32_t w0 = lds_b32(rb + (lane)*16), w1 = lds_b32(rb + (lane + 32) * 16),
-                       w2 = lds_b32(rb + (lane + 64) * 16), w3 = lds_b32(rb + (lane + 96) * 16);
-        sts_v4(sfa_addr(st) + lane * 16, w0, w1, w2, w3);
+      // four stages per raw slot: their atoms, then one proxy fence and four arrivals
+      for (int s0 = 0; s0 < S && ok; s0 += 4) {
+        if (!warp_wait(&sh.raw_full[rs], rph, abort)) { ok = false; break; }
+        int st_g[4];
+        for (int j = 0; j < 4; ++j) {
+          if (!warp_wait(&sh.empty[st], ph ^ 1, abort)) { ok = false; break; }
+          // row lane + 32 m1 of the tile, bytes of the stage's four 32-K blocks
+          const uint32_t rb = raw_base + rs * kRawBytes + 4 * j;
+          const uint32_t w0 = lds_b32(rb + (lane)*16), w1 = lds_b32(rb + (lane + 32) * 16),
+                         w2 = lds_b32(rb + (lane + 64) * 16), w3 = lds_b32(rb + (lane + 96) * 16);
+          sts_v4(sfa_addr(st) + lane * 16, w0, w1, w2, w3);
+          st_g[j] = st;
+          if (++st == NS) { st = 0; ph ^= 1; }
+        }
+        if (!ok) break;
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sh.full[st]);
-        if (++st == NS) { st = 0; ph ^= 1; }
-        if ((s & 3) == 3) {
-          if (lane == 0) mbar_arrive(&sh.raw_empty[rs]);
-          if (++rs == kRawSlots) { rs = 0; rph ^= 1; }
+        if (lane == 0) {
+          for (int j = 0; j < 4; ++j) mbar_arrive(&sh.full[st_g[j]]);
+          mbar_arrive(&sh.raw_empty[rs]);
         }
+        if (++rs == kRawSlots) { rs = 0; rph ^= 1; }
       }
       if (!ok) {
         if (lane == 0) fail(74 + KIND);
@@ -409,19 +439,17 @@ __global__ void __launch_bounds__(kThreads, 1) bs_decode_kernel(const __grid_con
       for (int s = 0; s < S; ++s) {
         if (!warp_wait(&sh.full[st], ph, abort)) { ok = false; break; }
         tc_fence_after();
+        // four SFA and four SFB columns per ring slot (the MMA's scale-factor
+        // operands start on 4-column boundaries)
         const uint32_t sfa_t = tmem + kSfCol0 + st * 8, sfb_t = sfa_t + 4;
-        uint32_t e;
-        asm volatile("{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.b32 %0, 1, 0, p;\n\t}" : "=r"(e));
-        if (e) {
-          sf_copy(sfa_t, sf_desc(sfa_addr(st)));
-          sf_copy(sfb_t, sf_desc(sfb_addr(st)));
+        sf_copy_elect(sfa_t, sf_desc(sfa_addr(st)));
+        sf_copy_elect(sfb_t, sf_desc(sfb_addr(st)));
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            bs_mma(d, umma_desc_sw128(a_addr(st) + 32 * kk), umma_desc_sw128(b_addr(st) + 32 * kk),
-                   bs_idesc(uint32_t(kk)), sfa_t | (uint32_t(kk) << 30), sfb_t | (uint32_t(kk) << 30),
-                   (s > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&sh.empty[st]);
-        }
+        for (int kk = 0; kk < 4; ++kk)
+          bs_mma_elect(d, umma_desc_sw128(a_addr(st) + 32 * kk), umma_desc_sw128(b_addr(st) + 32 * kk),
+                       bs_idesc(uint32_t(kk)), sfa_t | (uint32_t(kk) << 30), sfb_t | (uint32_t(kk) << 30),
+                       (s > 0 || kk > 0) ? 1u : 0u);
+        umma_commit_elect(&sh.empty[st]);
         __syncwarp();
         if (++st == NS) { st = 0; ph ^= 1; }
       }
@@ -465,16 +493,20 @@ __global__ void __launch_bounds__(kThreads, 1) bs_decode_kernel(const __grid_con
         const int h = blk * kBM + quarter * 32 + lane;
         for (int n = 0; n < valid; ++n) a.routed[int64_t(row0 + n) * a.H + h] = f32_to_bf16_bits(y[n]);
       } else {
-        // gate rows in quarters 0, 1; the up rows of the same features in 2, 3
+        // tile rows 0..63 are w13 rows blk * 64 .. of the first half (gate for
+        // the Qwen layout, up for w13 = [w3; w1]), rows 64..127 the same rows of
+        // the second half: the up rows' sums go to the gate warps
         const int xb = li & 1;
         const uint32_t xph = (li >> 1) & 1;
-        if (quarter >= 2) {
+        const bool up_warp = a.gate_first ? quarter >= 2 : quarter < 2;
+        const int pair = quarter & 1;  // features blk * 64 + 32 pair .. + 31
+        if (up_warp) {
           if (!warp_wait(&sh.xch_empty[xb], xph ^ 1, abort)) {
             if (lane == 0) fail(82);
             break;
           }
 #pragma unroll
-          for (int n = 0; n < kTokTile; ++n) sh.xch[xb][(quarter - 2) * 32 + lane][n] = y[n];
+          for (int n = 0; n < kTokTile; ++n) sh.xch[xb][pair * 32 + lane][n] = y[n];
           __syncwarp();
           if (lane == 0) mbar_arrive(&sh.xch_full[xb]);
         } else {
@@ -482,14 +514,14 @@ __global__ void __launch_bounds__(kThreads, 1) bs_decode_kernel(const __grid_con
             if (lane == 0) fail(83);
             break;
           }
-          const int f = blk * 64 + quarter * 32 + lane;  // feature (act column)
+          const int f = blk * 64 + pair * 32 + lane;  // feature (act column)
           const int Sd = a.I / kBK, sd = f / kBK, kk = (f % kBK) / 32;
           const int tile = row0 / kTokTile;
-          uint8_t* img = a.act_img + (int64_t(tile) * Sd + sd) * 4096;
-          uint8_t* sfb = a.act_sfb + (int64_t(tile) * Sd + sd) * kAtom;
+          uint8_t* img = a.act_img + (int64_t(tile) * Sd + sd) * kImage;
+          uint8_t* sfb = img + kBSmem;
           const int c = (f % kBK) / 16, byte = f % 16;
           for (int n = 0; n < valid; ++n) {
-            const float gv = bf16_round(y[n]), uv = bf16_round(sh.xch[xb][quarter * 32 + lane][n]);
+            const float gv = bf16_round(y[n]), uv = bf16_round(sh.xch[xb][pair * 32 + lane][n]);
             const float act = bf16_round(swiglu_f32(gv, uv, a.limit));
             // hi / lo parts of this token's 32 features (one scale block per warp)
             float amax = fabsf(act);
@@ -534,9 +566,9 @@ void bs_init_attributes() {
 
 bool bs_shape_ok(int H, int I) { return H % 512 == 0 && I % 512 == 0 && H >= 512 && I >= 512; }
 
-void launch_bs_quant_rows(const uint16_t* x, const Plan& p, int E, int K, uint8_t* img, uint8_t* sfb, int num_sms,
+void launch_bs_quant_rows(const uint16_t* x, const Plan& p, int E, int K, uint8_t* img, int num_sms,
                           cudaStream_t stream) {
-  bs_quant_rows_kernel<<<num_sms * 4, 256, 0, stream>>>(x, p, E, K, img, sfb);
+  bs_quant_rows_kernel<<<num_sms * 4, 256, 0, stream>>>(x, p, E, K, img);
 }
 
 void launch_bs_decode(const BsArgs& args, int kind, const void* const* maps, int num_sms, cudaStream_t stream) {

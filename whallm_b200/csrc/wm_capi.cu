@@ -37,8 +37,8 @@ struct wm_ctx {
   float* actscale = nullptr;   // [rows] prescale of the f16 act rows (decode path)
   uint32_t* rowmax = nullptr;  // [rows] per-row |act| maxima (decode path)
   uint16_t* xn = nullptr;      // [T, H] normalised input rows (pre-MoE RMSNorm)
-  uint8_t* bs_sfb_x = nullptr;    // block-scaled decode: scale atoms of the token tile images
-  uint8_t* bs_sfb_act = nullptr;  // ... and of the act tile images
+  uint8_t* bs_img_x = nullptr;    // block-scaled decode: token tile images (hi / lo E4M3 + scale atoms)
+  uint8_t* bs_img_act = nullptr;  // ... and the act tile images
   int max_rows = 0, max_mtiles = 0, max_chunks = 0;
   PFN_cuTensorMapEncodeTiled_v12000 encode_tiled = nullptr;
   wm::Profiler prof;
@@ -413,15 +413,47 @@ int run_decode_mma(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& w
 // MMA reads them: [experts][rows][K] 4-bit elements (16U4_ALIGN16B: every 8
 // packed bytes land in 16 bytes of shared memory), boxes of 128 K x box_rows,
 // 128-byte swizzle.
+// halves = 2: the matrix is split into two halves of rows / 2 rows (w13's
+// gate and up halves), a 4-D map whose boxes take box_rows rows of both.
 bool encode_fp4_weights(wm_ctx* ctx, CUtensorMap* map, const void* base, int64_t K, int64_t rows, int64_t experts,
-                        int64_t expert_stride, int box_rows) {
+                        int64_t expert_stride, int box_rows, int halves) {
   if (ctx->encode_tiled == nullptr) return false;
-  cuuint64_t dims[3] = {cuuint64_t(K), cuuint64_t(rows), cuuint64_t(experts)};
-  cuuint64_t strides[2] = {cuuint64_t(K / 2), cuuint64_t(experts > 1 ? expert_stride : K / 2 * rows)};
-  cuuint32_t box[3] = {128, cuuint32_t(box_rows), 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, const_cast<void*>(base), dims, strides,
-                                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  const int64_t hr = rows / halves;
+  const int64_t estride = experts > 1 ? expert_stride : K / 2 * rows;
+  cuuint64_t dims[4] = {cuuint64_t(K), cuuint64_t(hr), cuuint64_t(halves), cuuint64_t(experts)};
+  cuuint64_t strides[3] = {cuuint64_t(K / 2), cuuint64_t(K / 2 * hr), cuuint64_t(estride)};
+  cuuint32_t box[4] = {128, cuuint32_t(box_rows), cuuint32_t(halves), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  if (halves == 1) {  // 3-D: [experts][rows][K]
+    dims[2] = cuuint64_t(experts);
+    strides[1] = cuuint64_t(estride);
+    box[2] = 1;
+  }
+  CUresult r = ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, halves == 1 ? 3 : 4,
+                                 const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// E8M0 rows [experts][halves][rows / halves][S] as uint8, boxes of 16 bytes x
+// box_rows (x halves), no swizzle.
+bool encode_scale_rows(wm_ctx* ctx, CUtensorMap* map, const void* base, int64_t S, int64_t rows, int64_t experts,
+                       int64_t expert_stride, int box_rows, int halves) {
+  if (ctx->encode_tiled == nullptr) return false;
+  const int64_t hr = rows / halves;
+  const int64_t estride = experts > 1 ? expert_stride : S * rows;
+  cuuint64_t dims[4] = {cuuint64_t(S), cuuint64_t(hr), cuuint64_t(halves), cuuint64_t(experts)};
+  cuuint64_t strides[3] = {cuuint64_t(S), cuuint64_t(S * hr), cuuint64_t(estride)};
+  cuuint32_t box[4] = {16, cuuint32_t(box_rows), cuuint32_t(halves), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  if (halves == 1) {
+    dims[2] = cuuint64_t(experts);
+    strides[1] = cuuint64_t(estride);
+    box[2] = 1;
+  }
+  CUresult r = ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, halves == 1 ? 3 : 4, const_cast<void*>(base),
+                                 dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -431,18 +463,18 @@ bool encode_fp4_weights(wm_ctx* ctx, CUtensorMap* map, const void* base, int64_t
 int run_bs_decode(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts, bool has_shared, cudaStream_t s) {
   const int H = a->H, I = a->I;
   CUtensorMap w13, w13s, w2, w2s, s13, s13s, s2, s2s;
-  bool ok = encode_fp4_weights(ctx, &w13, a->w13.weight, H, 2 * I, a->E, a->w13.weight_stride, 64) &&
-            encode_fp4_weights(ctx, &w2, a->w2.weight, I, H, a->E, a->w2.weight_stride, 128) &&
-            encode_weights(ctx, &s13, a->w13.scale, H / 32, 2 * I, a->E, a->w13.scale_stride, 16, 64) &&
-            encode_weights(ctx, &s2, a->w2.scale, I / 32, H, a->E, a->w2.scale_stride, 16, 128);
+  bool ok = encode_fp4_weights(ctx, &w13, a->w13.weight, H, 2 * I, a->E, a->w13.weight_stride, 64, 2) &&
+            encode_fp4_weights(ctx, &w2, a->w2.weight, I, H, a->E, a->w2.weight_stride, 128, 1) &&
+            encode_scale_rows(ctx, &s13, a->w13.scale, H / 32, 2 * I, a->E, a->w13.scale_stride, 64, 2) &&
+            encode_scale_rows(ctx, &s2, a->w2.scale, I / 32, H, a->E, a->w2.scale_stride, 128, 1);
   if (has_shared)
-    ok = ok && encode_fp4_weights(ctx, &w13s, a->shared_w13.weight, H, 2 * I, 1, 0, 64) &&
-         encode_fp4_weights(ctx, &w2s, a->shared_w2.weight, I, H, 1, 0, 128) &&
-         encode_weights(ctx, &s13s, a->shared_w13.scale, H / 32, 2 * I, 1, 0, 16, 64) &&
-         encode_weights(ctx, &s2s, a->shared_w2.scale, I / 32, H, 1, 0, 16, 128);
+    ok = ok && encode_fp4_weights(ctx, &w13s, a->shared_w13.weight, H, 2 * I, 1, 0, 64, 2) &&
+         encode_fp4_weights(ctx, &w2s, a->shared_w2.weight, I, H, 1, 0, 128, 1) &&
+         encode_scale_rows(ctx, &s13s, a->shared_w13.scale, H / 32, 2 * I, 1, 0, 64, 2) &&
+         encode_scale_rows(ctx, &s2s, a->shared_w2.scale, I / 32, H, 1, 0, 128, 1);
   if (!ok) return fail(ctx, "cuTensorMapEncodeTiled failed for the block-scaled expert operands");
-  uint8_t* ximg = reinterpret_cast<uint8_t*>(ctx->xs);      // [rows, H] x 2 bytes: the token tile images
-  uint8_t* aimg = reinterpret_cast<uint8_t*>(ctx->act16);   // [rows, I] x 2 bytes: the act tile images
+  uint8_t* ximg = ctx->bs_img_x;    // rows / 16 x H / 128 images of 4608 bytes
+  uint8_t* aimg = ctx->bs_img_act;  // the same for the act rows (K = I)
   wm::BsArgs b{};
   b.plan = ctx->plan;
   b.wts = wts;
@@ -452,20 +484,16 @@ int run_bs_decode(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wt
   b.limit = a->swiglu_limit;
   b.status = ctx->status;
   b.act_img = aimg;
-  b.act_sfb = ctx->bs_sfb_act;
   b.routed = ctx->routed;
   wm::prof_begin(&ctx->prof, wm::kProfGather, s);
-  wm::launch_bs_quant_rows(static_cast<const uint16_t*>(a->x), b.plan, a->E, H, ximg,
-                           ctx->bs_sfb_x, ctx->num_sms, s);
+  wm::launch_bs_quant_rows(static_cast<const uint16_t*>(a->x), b.plan, a->E, H, ximg, ctx->num_sms, s);
   wm::prof_end(&ctx->prof, wm::kProfGather, s);
   b.img = ximg;
-  b.sfb = ctx->bs_sfb_x;
   wm::prof_begin(&ctx->prof, wm::kProfDecodeGateUp, s);
   const void* maps0[4] = {&w13, has_shared ? &w13s : &w13, &s13, has_shared ? &s13s : &s13};
   wm::launch_bs_decode(b, 0, maps0, ctx->num_sms, s);
   wm::prof_end(&ctx->prof, wm::kProfDecodeGateUp, s);
   b.img = aimg;
-  b.sfb = ctx->bs_sfb_act;
   wm::prof_begin(&ctx->prof, wm::kProfDecodeDown, s);
   const void* maps1[4] = {&w2, has_shared ? &w2s : &w2, &s2, has_shared ? &s2s : &s2};
   wm::launch_bs_decode(b, 1, maps1, ctx->num_sms, s);
@@ -682,8 +710,8 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
                o_act = take(rows * I * 2), o_routed = take(rows * H * 2), o_logits = take(T * E * 4),
                o_idx = take(T * K * 4), o_w = take(T * K * 4), o_sg = take(T * 4), o_status = take(16),
                o_act16 = take(rows * I * 2), o_rowscale = take(rows * 4), o_actscale = take(rows * 4),
-               o_rowmax = take(rows * 4), o_xn = take(T * H * 2), o_sfbx = take(rows * H / 4),
-               o_sfba = take(rows * I / 4);
+               o_rowmax = take(rows * 4), o_xn = take(T * H * 2), o_imgx = take(rows * H * 9 / 4),
+               o_imga = take(rows * I * 9 / 4);
   ctx->ws_bytes = off;
   if (cudaMalloc(&ctx->ws, ctx->ws_bytes) != cudaSuccess) {
     cudaGetLastError();
@@ -716,8 +744,8 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
   ctx->actscale = reinterpret_cast<float*>(base + o_actscale);
   ctx->rowmax = reinterpret_cast<uint32_t*>(base + o_rowmax);
   ctx->xn = reinterpret_cast<uint16_t*>(base + o_xn);
-  ctx->bs_sfb_x = base + o_sfbx;
-  ctx->bs_sfb_act = base + o_sfba;
+  ctx->bs_img_x = base + o_imgx;
+  ctx->bs_img_act = base + o_imga;
   // the whole workspace starts at zero (status word included); padding rows of
   // the f16 row blocks are never written afterwards, so they hold zeros or an
   // earlier call's finite rows

@@ -193,10 +193,8 @@ struct BsArgs {
   int gate_first;
   float limit;
   uint32_t* status;
-  const uint8_t* img;    // token tile images [tiles][K / 128][4096] (hi rows 0..15, lo rows 16..31)
-  const uint8_t* sfb;    // their scale atoms [tiles][K / 128][512]
+  const uint8_t* img;    // token tile images [tiles][K / 128][4608]: hi rows 0..15, lo rows 16..31, scale atom
   uint8_t* act_img;      // gate/up: act tile images for the down kernel (K = I)
-  uint8_t* act_sfb;
   uint16_t* routed;      // down: [rows, H] bf16
   int stages;
 };
@@ -204,11 +202,12 @@ void bs_init_attributes();
 // H and I multiples of 512 (four 128-K stages per raw scale load)
 bool bs_shape_ok(int H, int I);
 // x rows (through the plan, 16-row tiles) -> hi / lo E4M3 tile images and scale atoms
-void launch_bs_quant_rows(const uint16_t* x, const Plan& p, int E, int K, uint8_t* img, uint8_t* sfb, int num_sms,
+void launch_bs_quant_rows(const uint16_t* x, const Plan& p, int E, int K, uint8_t* img, int num_sms,
                           cudaStream_t stream);
 // maps[0..3]: CUtensorMaps of the routed and the shared expert's packed weights
-// (16U4_ALIGN16B [E][rows][K], boxes 128 x 64 for gate/up, 128 x 128 for down,
-// 128-byte swizzle) and of their E8M0 rows (uint8 [E][rows][K/32], boxes 16 x 64 / 16 x 128).
+// (16U4_ALIGN16B, 128-byte swizzle; gate/up 4-D [E][2][I][H] with boxes
+// 128 x 64 x 2, down 3-D [E][H][I] with boxes 128 x 128) and of their E8M0
+// rows (uint8, gate/up [E][2][I][H/32] boxes 16 x 64 x 2, down [E][H][I/32] boxes 16 x 128).
 void launch_bs_decode(const BsArgs& a, int kind, const void* const* maps, int num_sms, cudaStream_t stream);
 
 // ---- prefill grouped GEMM on tcgen05 (wm_gemm_sm100.cu)
