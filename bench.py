@@ -703,7 +703,7 @@ def run(args) -> None:
     nb = 8
     xs = [synth.activations(B, H, torch.Generator(device=dev).manual_seed(1000 * rank + i), dev) for i in range(nb)]
     eng = Engine(local, max_tokens=max(B, 64), hidden=H, inter=I, experts=E, topk=K,
-                 flags=lib.FLAG_BS_DECODE if args.decode == "bs" else 0)
+                 flags=lib.FLAG_MMA_DECODE if args.decode == "mma" else 0)
     x_static = xs[0].clone()
     out_static = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
@@ -867,8 +867,8 @@ def main():
     ap.add_argument("--no-long", action="store_true", help="skip the config-3 and config-4 long-call sections")
     ap.add_argument("--clocks-dir", default=None,
                     help="folder for the raw nvidia-smi clock samples (default: the system temp folder)")
-    ap.add_argument("--decode", default="mma", choices=["mma", "bs"],
-                    help="decode expert kernels: register-direct warp MMAs (mma) or block-scaled tcgen05 (bs)")
+    ap.add_argument("--decode", default="bs", choices=["bs", "mma"],
+                    help="decode expert kernels: block-scaled tcgen05 (bs, the default) or register-direct warp MMAs")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="N > 1: expert-parallel exchanges over peer memory (default) or NCCL all-to-all")
     args = ap.parse_args()

@@ -118,17 +118,20 @@ typedef struct {
    exchange buffers (the expert-parallel path). */
 #define WM_FLAG_SKIP_NEGATIVE_ROUTES 1
 
-/* Short MXFP4 calls take the tcgen05 decode kernel (weights dequantised into
-   TMEM) instead of the default register-direct decode kernel.  Both compute
-   the same products; kept for comparison. */
+/* Short MXFP4 calls take the tcgen05 decode kernel that dequantises the
+   weights into TMEM (kind::f16) instead of the default block-scaled one; kept
+   for comparison. */
 #define WM_FLAG_TCGEN05_DECODE 2
 
-/* Short MXFP4 calls take the block-scaled tcgen05 decode kernel: the E2M1
-   weights go from the blob to the tensor cores by TMA with their E8M0 scales
-   as the MMA's scale factors (kind::mxf8f6f4), and each token row enters as
-   two E4M3 parts (hi + lo, power-of-two scales per 32 values; within 2^-8 of
-   the row, layer outputs within ~1e-3 of max|y|). */
-#define WM_FLAG_BS_DECODE 4
+/* Short MXFP4 calls take the register-direct warp-MMA decode kernel (weights
+   dequantised to exact f16 in registers) instead of the default block-scaled
+   tcgen05 kernel.  The default: the E2M1 weights go from the blob to the
+   tensor cores by TMA with their E8M0 scales as the MMA's scale factors
+   (kind::mxf8f6f4), and each token row enters as two E4M3 parts (hi + lo,
+   power-of-two scales per 32 values; within 2^-8 of every element, layer
+   outputs within ~1e-3 of max|y|); it needs H and I multiples of 512,
+   32-byte aligned weight regions and 16-byte aligned scale regions. */
+#define WM_FLAG_MMA_DECODE 4
 
 /* One projection of every expert: expert e's matrix at weight + e * weight_stride
    bytes, its scales at scale + e * scale_stride bytes (device pointers). */
@@ -179,8 +182,8 @@ typedef struct {
   int64_t calls_forward, calls_pairs, calls_route, calls_dequant;
   int64_t launches;            /* kernels enqueued by this handle */
   int64_t gemv_calls, gemm_calls;
-  int64_t decode_calls;        /* calls that took the decode kernels (register-direct mma.sync kernel by
-                                  default, the tcgen05 one with WM_FLAG_TCGEN05_DECODE) */
+  int64_t decode_calls;        /* calls that took the decode kernels (block-scaled tcgen05 by default,
+                                  WM_FLAG_MMA_DECODE / WM_FLAG_TCGEN05_DECODE select the others) */
 } wm_counters;
 
 typedef struct {

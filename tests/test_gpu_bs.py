@@ -1,5 +1,6 @@
-"""The block-scaled tcgen05 decode kernel (WM_FLAG_BS_DECODE) against the CPU
-oracle and against the register-direct decode kernel (needs a B200).
+"""The block-scaled tcgen05 decode kernel (the default for MXFP4 decode calls)
+against the CPU oracle and against the register-direct decode kernel
+(WM_FLAG_MMA_DECODE; needs a B200).
 
 Weights enter the MMA as E2M1 with their E8M0 scales (exact); token rows as
 two E4M3 parts (within 2^-8 of each element).  Tolerance as everywhere:
@@ -30,8 +31,8 @@ def config1():
 
 
 def _engines(T, H, I, E, K):
-    bs = Engine(0, max_tokens=T, hidden=H, inter=I, experts=E, topk=K, flags=lib.FLAG_BS_DECODE)
-    mma = Engine(0, max_tokens=T, hidden=H, inter=I, experts=E, topk=K)
+    bs = Engine(0, max_tokens=T, hidden=H, inter=I, experts=E, topk=K)
+    mma = Engine(0, max_tokens=T, hidden=H, inter=I, experts=E, topk=K, flags=lib.FLAG_MMA_DECODE)
     return bs, mma
 
 
@@ -87,7 +88,7 @@ def test_bs_decode_config4_shape():
     wl = synth.config(4, device=DEV)
     layer = wl.layer
     x = wl.x[:8].contiguous()
-    bs = Engine(0, max_tokens=8, hidden=7168, inter=2048, experts=384, topk=8, flags=lib.FLAG_BS_DECODE)
+    bs = Engine(0, max_tokens=8, hidden=7168, inter=2048, experts=384, topk=8)
     out, (w, idx) = bs.forward(layer, x, 8, return_routes=True)
     bs.sync()
     ii = idx.cpu().numpy()

@@ -314,7 +314,8 @@ Path expert_path(const wm_ctx* ctx, const wm_moe_args* a, bool has_shared) {
   const wm_matrix* ms[4] = {&a->w13, &a->w2, &a->shared_w13, &a->shared_w2};
   for (int i = 0; i < (has_shared ? 4 : 2); ++i)
     if (!aligned(ms[i]->scale, 16) || (i < 2 && ms[i]->scale_stride % 16)) return kPathGemv;
-  if (!is_fp8(a->layout) && (ctx->opt.flags & WM_FLAG_BS_DECODE) && bs_operands_ok(ctx, a, has_shared))
+  if (!is_fp8(a->layout) && !(ctx->opt.flags & (WM_FLAG_MMA_DECODE | WM_FLAG_TCGEN05_DECODE)) &&
+      bs_operands_ok(ctx, a, has_shared))
     return kPathBsDecode;
   if (!is_fp8(a->layout) && (ctx->opt.flags & WM_FLAG_TCGEN05_DECODE))
     return wm::decode_shape_ok(a->H, a->I) ? kPathDecode : kPathGemv;
@@ -656,7 +657,7 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
     return nullptr;
   }
   wm_options o = *options;
-  if (o.flags & ~int32_t(WM_FLAG_SKIP_NEGATIVE_ROUTES | WM_FLAG_TCGEN05_DECODE | WM_FLAG_BS_DECODE)) {
+  if (o.flags & ~int32_t(WM_FLAG_SKIP_NEGATIVE_ROUTES | WM_FLAG_TCGEN05_DECODE | WM_FLAG_MMA_DECODE)) {
     report("unknown flags");
     return nullptr;
   }

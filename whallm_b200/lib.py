@@ -21,7 +21,7 @@ ROUTER_SOFTMAX, ROUTER_SQRTSOFTPLUS, ROUTER_SIGMOID, ROUTER_SIGMOID_GROUPED = 0,
 SHARED_NONE, SHARED_SIGMOID_GATE, SHARED_ONE = 0, 1, 2
 FLAG_SKIP_NEGATIVE_ROUTES = 1
 FLAG_TCGEN05_DECODE = 2
-FLAG_BS_DECODE = 4
+FLAG_MMA_DECODE = 4
 
 # Every entry point the header declares (checked by the CPU test suite).
 EXPORTS = (
