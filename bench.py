@@ -43,7 +43,11 @@ H, I, E, K = 2048, 512, 512, 10
 BLOB = 1_671_168  # bytes of one expert blob (gate_up + scales + down + scales)
 GATE_UP_BYTES = 2 * I * H // 2 + 2 * I * H // 32
 # dram bytes (read + write) of one gate/up decode launch at this workload, from an ncu capture
-NCU_GATE_UP_TRAFFIC = 412.166656e6 + 3.397376e6
+# (profiles/decode_bs_config1_b64.txt: block-scaled kernel; profiles/decode_mma_config1_b64.txt: --decode mma)
+NCU_GATE_UP_TRAFFIC = {"bs": 441.041920e6 + 4.248576e6, "mma": 412.166656e6 + 3.397376e6}
+DECODE_KERNEL = {"bs": "bs_decode_kernel<0> (gate/up + SwiGLU; block-scaled tcgen05, kind::mxf8f6f4)",
+                 "mma": "decode_mma_kernel<0> (gate/up + SwiGLU; register-direct mma.sync)"}
+DECODE_PROFILE = {"bs": "profiles/decode_bs_config1_b64.txt", "mma": "profiles/decode_mma_config1_b64.txt"}
 DOWN_BYTES = H * I // 2 + H * I // 32
 
 
@@ -835,11 +839,11 @@ def run(args) -> None:
                    "timing": "CUDA graph replay per step, device events, max over ranks",
                    "parallelism": "single GPU",
                    "unique_experts_per_step": U},
-        "roofline": {"bound": "hbm", "kernel": "decode_mma_kernel<0> (gate/up + SwiGLU)", "achieved": achieved,
+        "roofline": {"bound": "hbm", "kernel": DECODE_KERNEL[args.decode], "achieved": achieved,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
-                     "peak_source": pk["source"], "traffic": NCU_GATE_UP_TRAFFIC,
+                     "peak_source": pk["source"], "traffic": NCU_GATE_UP_TRAFFIC[args.decode],
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch, "
-                                       "profiles/decode_mma_config1_b64.txt",
+                                       + DECODE_PROFILE[args.decode],
                      "algorithmic_bytes_per_launch": gu_bytes,
                      "down_achieved_gbs": dn_bytes / (dn_ms / dn_n / 1e3) / 1e9},
         "kernels": kernels,
