@@ -44,7 +44,7 @@ BLOB = 1_671_168  # bytes of one expert blob (gate_up + scales + down + scales)
 GATE_UP_BYTES = 2 * I * H // 2 + 2 * I * H // 32
 # dram bytes (read + write) of one gate/up decode launch at this workload, from an ncu capture
 # (profiles/decode_bs_config1_b64.txt: block-scaled kernel; profiles/decode_mma_config1_b64.txt: --decode mma)
-NCU_GATE_UP_TRAFFIC = {"bs": 441.041920e6 + 4.248576e6, "mma": 412.166656e6 + 3.397376e6}
+NCU_GATE_UP_TRAFFIC = {"bs": 436.316416e6 + 6.585344e6, "mma": 412.166656e6 + 3.397376e6}
 DECODE_KERNEL = {"bs": "bs_decode_kernel<0> (gate/up + SwiGLU; block-scaled tcgen05, kind::mxf8f6f4)",
                  "mma": "decode_mma_kernel<0> (gate/up + SwiGLU; register-direct mma.sync)"}
 DECODE_PROFILE = {"bs": "profiles/decode_bs_config1_b64.txt", "mma": "profiles/decode_mma_config1_b64.txt"}
@@ -305,6 +305,8 @@ def long_ep_section(args, n: int, world: int, rank: int, local: int, pk: dict) -
             h = y if len(layers) == 1 else h + y  # bf16 residual add between layers
         return h
 
+    step_ms = []
+
     def timed(fwd, h0, nsteps):
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(nsteps)]
         for i in range(nsteps):
@@ -313,7 +315,8 @@ def long_ep_section(args, n: int, world: int, rank: int, local: int, pk: dict) -
             stack(fwd, h0)
             evs[i][1].record()
         torch.cuda.synchronize()
-        return sum(a.elapsed_time(b) for a, b in evs) / nsteps
+        step_ms[:] = [a.elapsed_time(b) for a, b in evs]
+        return sum(step_ms) / nsteps
 
     # one GPU, the whole batch (rank 0; the grouped GEMM throughout)
     single = None
@@ -353,6 +356,11 @@ def long_ep_section(args, n: int, world: int, rank: int, local: int, pk: dict) -
     torch.cuda.synchronize()
     dist.barrier()
     ms = timed(fwd, x, steps)
+    # per-rank step statistics (mean, min, median, max): a slow rank or a slow step shows here
+    mine = torch.tensor([ms, min(step_ms), statistics.median(step_ms), max(step_ms)], device=dev)
+    every = [torch.zeros_like(mine) for _ in range(world)]
+    dist.all_gather(every, mine)
+    per_rank = [[round(float(v), 3) for v in r.tolist()] for r in every]
     t = torch.tensor([ms], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
@@ -387,6 +395,7 @@ def long_ep_section(args, n: int, world: int, rank: int, local: int, pk: dict) -
                 f"({En // world} experts per GPU per layer), NVLink peer-memory exchanges",
                 "single_gpu_tokens_per_s": single,
                 "efficiency": (tps / (world * single)) if single else None,
+                "step_ms_per_rank": per_rank, "step_ms_fields": "mean, min, median, max over the timed steps",
                 "efficiency_note": "tokens/s over N GPUs / (N x one GPU's tokens/s on the whole batch, rank 0, same run)",
                 "parity": {"bit_exact": bool(exact.item() == 1.0), "finite": bool(finite.item() == 1.0),
                            "max_abs": float(max_abs.item()),
