@@ -118,11 +118,6 @@ typedef struct {
    exchange buffers (the expert-parallel path). */
 #define WM_FLAG_SKIP_NEGATIVE_ROUTES 1
 
-/* Short MXFP4 calls take the tcgen05 decode kernel that dequantises the
-   weights into TMEM (kind::f16) instead of the default block-scaled one; kept
-   for comparison. */
-#define WM_FLAG_TCGEN05_DECODE 2
-
 /* Short MXFP4 calls take the register-direct warp-MMA decode kernel (weights
    dequantised to exact f16 in registers) instead of the default block-scaled
    tcgen05 kernel.  The default: the E2M1 weights go from the blob to the
@@ -183,7 +178,7 @@ typedef struct {
   int64_t launches;            /* kernels enqueued by this handle */
   int64_t gemv_calls, gemm_calls;
   int64_t decode_calls;        /* calls that took the decode kernels (block-scaled tcgen05 by default,
-                                  WM_FLAG_MMA_DECODE / WM_FLAG_TCGEN05_DECODE select the others) */
+                                  WM_FLAG_MMA_DECODE selects the register-direct one) */
 } wm_counters;
 
 typedef struct {

@@ -42,8 +42,7 @@ def layer(layout=lib.LAYOUT_QWEN_GATE_UP_MXFP4, seed=3, gate=lib.SHARED_NONE, li
                         router=RouterWeights(wr, lib.ROUTER_SOFTMAX), swiglu_limit=limit)
 
 
-@pytest.fixture(scope="module", params=[0, lib.FLAG_MMA_DECODE, lib.FLAG_TCGEN05_DECODE],
-                ids=["block_scaled", "mma", "tcgen05"])
+@pytest.fixture(scope="module", params=[0, lib.FLAG_MMA_DECODE], ids=["block_scaled", "mma"])
 def eng(request):
     e = Engine(0, max_tokens=64, hidden=H, inter=I, experts=E, topk=8, flags=request.param)
     yield e

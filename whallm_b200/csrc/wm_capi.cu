@@ -289,7 +289,7 @@ bool use_gemm(const wm_ctx* ctx, const wm_moe_args* a) {
   return gemm && wm::gemm_shape_ok(a->H, a->I) && ctx->encode_tiled != nullptr;
 }
 
-enum Path { kPathGemv = 0, kPathDecode = 1, kPathGemm = 2, kPathDecodeMma = 3, kPathBsDecode = 4 };
+enum Path { kPathGemv = 0, kPathGemm = 2, kPathDecodeMma = 3, kPathBsDecode = 4 };
 
 // The block-scaled decode kernel's TMA operands: packed weights 32-byte
 // aligned with 32-byte multiple strides (16U4_ALIGN16B), E8M0 rows 16-byte
@@ -305,20 +305,18 @@ bool bs_operands_ok(const wm_ctx* ctx, const wm_moe_args* a, bool has_shared) {
 }
 
 // Which expert kernels a call takes: the tcgen05 grouped GEMM for long calls;
-// for short MXFP4 calls whose weights and scale rows allow 16-byte loads the
-// register-direct decode kernel (or, with WM_FLAG_TCGEN05_DECODE, the tcgen05
-// decode kernel); else the CUDA-core GEMV.
+// for short calls the block-scaled tcgen05 decode kernel (MXFP4 experts whose
+// shapes and regions its TMA operands take, unless WM_FLAG_MMA_DECODE), else
+// the register-direct decode kernel where 16-byte loads are possible (MXFP4
+// and FP8), else the CUDA-core GEMV.
 Path expert_path(const wm_ctx* ctx, const wm_moe_args* a, bool has_shared) {
   if (use_gemm(ctx, a)) return kPathGemm;
   if (ctx->encode_tiled == nullptr) return kPathGemv;
   const wm_matrix* ms[4] = {&a->w13, &a->w2, &a->shared_w13, &a->shared_w2};
   for (int i = 0; i < (has_shared ? 4 : 2); ++i)
     if (!aligned(ms[i]->scale, 16) || (i < 2 && ms[i]->scale_stride % 16)) return kPathGemv;
-  if (!is_fp8(a->layout) && !(ctx->opt.flags & (WM_FLAG_MMA_DECODE | WM_FLAG_TCGEN05_DECODE)) &&
-      bs_operands_ok(ctx, a, has_shared))
+  if (!is_fp8(a->layout) && !(ctx->opt.flags & WM_FLAG_MMA_DECODE) && bs_operands_ok(ctx, a, has_shared))
     return kPathBsDecode;
-  if (!is_fp8(a->layout) && (ctx->opt.flags & WM_FLAG_TCGEN05_DECODE))
-    return wm::decode_shape_ok(a->H, a->I) ? kPathDecode : kPathGemv;
   for (int i = 0; i < (has_shared ? 4 : 2); ++i)
     if (!aligned(ms[i]->weight, 16) || (i < 2 && ms[i]->weight_stride % 16)) return kPathGemv;
   return wm::decode_mma_shape_ok(a->H, a->I, fmt_of(a->layout)) ? kPathDecodeMma : kPathGemv;
@@ -330,7 +328,7 @@ int plan_align(Path path) { return path == kPathGemm ? wm::kTileM : path == kPat
 
 // Plan fields of the expert kernels of `path`.
 void plan_for_path(const wm_ctx* ctx, Path path, wm::Plan* plan) {
-  if (path == kPathDecode || path == kPathDecodeMma || path == kPathGemm) plan->rowmax = ctx->rowmax;
+  if (path == kPathDecodeMma || path == kPathGemm) plan->rowmax = ctx->rowmax;
   if (path == kPathDecodeMma) plan->tile_rows = 8;
 }
 
@@ -504,68 +502,10 @@ int run_bs_decode(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wt
   return check_launch(ctx, "block-scaled expert decode");
 }
 
-// The tcgen05 decode path: per-token prescale, gate/up (+SwiGLU), down.
-int run_decode(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts, bool has_shared, cudaStream_t s) {
-  const int H = a->H, I = a->I;
-  // packed weights (128-byte boxes along K = 256 E2M1, 128-byte swizzle) and
-  // E8M0 scales (one box per row tile)
-  CUtensorMap w13, w13s, w2, w2s, s13, s13s, s2, s2s;
-  constexpr CUtensorMapSwizzle kSw = CU_TENSOR_MAP_SWIZZLE_128B;
-  bool ok = encode_weights(ctx, &w13, a->w13.weight, H / 2, 2 * I, a->E, a->w13.weight_stride, 128, 64, kSw) &&
-            encode_weights(ctx, &w2, a->w2.weight, I / 2, H, a->E, a->w2.weight_stride, 128, 128, kSw) &&
-            encode_weights(ctx, &s13, a->w13.scale, H / 32, 2 * I, a->E, a->w13.scale_stride, H / 32, 64) &&
-            encode_weights(ctx, &s2, a->w2.scale, I / 32, H, a->E, a->w2.scale_stride, I / 32, 128);
-  if (has_shared)
-    ok = ok && encode_weights(ctx, &w13s, a->shared_w13.weight, H / 2, 2 * I, 1, 0, 128, 64, kSw) &&
-         encode_weights(ctx, &w2s, a->shared_w2.weight, I / 2, H, 1, 0, 128, 128, kSw) &&
-         encode_weights(ctx, &s13s, a->shared_w13.scale, H / 32, 2 * I, 1, 0, H / 32, 64) &&
-         encode_weights(ctx, &s2s, a->shared_w2.scale, I / 32, H, 1, 0, I / 32, 128);
-  if (!ok) return fail(ctx, "cuTensorMapEncodeTiled failed for the expert weights");
-  // f16 activation rows (the B operand) and their TMA descriptors
-  uint16_t* xh = ctx->xs;      // [max_rows, H]
-  uint16_t* acth = ctx->act16; // [max_rows, I]
-  CUtensorMap bx, bact;
-  if (!encode_rows_box(ctx, &bx, xh, H, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 16) ||
-      !encode_rows_box(ctx, &bact, acth, I, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 16))
-    return fail(ctx, "cuTensorMapEncodeTiled failed for the activation rows");
-  wm::Plan plan = ctx->plan;
-  plan.rowmax = ctx->rowmax;
-  wm::DecodeArgs d{};
-  d.plan = plan;
-  d.wts = wts;
-  d.act = ctx->act;
-  d.routed = ctx->routed;
-  d.H = H;
-  d.I = I;
-  d.gate_first = a->layout == WM_LAYOUT_QWEN_GATE_UP_MXFP4 ? 1 : 0;
-  d.limit = a->swiglu_limit;
-  d.status = ctx->status;
-  wm::prof_begin(&ctx->prof, wm::kProfGather, s);
-  wm::launch_gather_f16(static_cast<const uint16_t*>(a->x), plan, a->E, H, xh, ctx->rowscale, ctx->num_sms, s);
-  wm::prof_end(&ctx->prof, wm::kProfGather, s);
-  d.bscale = ctx->rowscale;
-  wm::prof_begin(&ctx->prof, wm::kProfDecodeGateUp, s);
-  const void* maps0[5] = {&w13, has_shared ? &w13s : &w13, &s13, has_shared ? &s13s : &s13, &bx};
-  wm::launch_decode(d, 0, maps0, ctx->num_sms, s);
-  wm::prof_end(&ctx->prof, wm::kProfDecodeGateUp, s);
-  wm::prof_begin(&ctx->prof, wm::kProfActF16, s);
-  wm::launch_act_f16(ctx->act, plan, a->E, I, acth, ctx->actscale, ctx->num_sms, s);
-  wm::prof_end(&ctx->prof, wm::kProfActF16, s);
-  d.bscale = ctx->actscale;
-  wm::prof_begin(&ctx->prof, wm::kProfDecodeDown, s);
-  const void* maps1[5] = {&w2, has_shared ? &w2s : &w2, &s2, has_shared ? &s2s : &s2, &bact};
-  wm::launch_decode(d, 1, maps1, ctx->num_sms, s);
-  wm::prof_end(&ctx->prof, wm::kProfDecodeDown, s);
-  ctx->counters.launches += 4;
-  ctx->counters.decode_calls += 1;
-  return check_launch(ctx, "expert decode");
-}
-
 // Runs the experts of a plan already built on `s` (rows in ctx->routed).
 int run_experts(wm_ctx* ctx, const wm_moe_args* a, bool has_shared, Path path, cudaStream_t s) {
   const wm::ExpertWeights wts = weights_of(a, has_shared);
   const int gate_first = a->layout == WM_LAYOUT_QWEN_GATE_UP_MXFP4 ? 1 : 0;
-  if (path == kPathDecode) return run_decode(ctx, a, wts, has_shared, s);
   if (path == kPathDecodeMma) return run_decode_mma(ctx, a, wts, s);
   if (path == kPathBsDecode) return run_bs_decode(ctx, a, wts, has_shared, s);
   if (path == kPathGemv) {
@@ -657,7 +597,7 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
     return nullptr;
   }
   wm_options o = *options;
-  if (o.flags & ~int32_t(WM_FLAG_SKIP_NEGATIVE_ROUTES | WM_FLAG_TCGEN05_DECODE | WM_FLAG_MMA_DECODE)) {
+  if (o.flags & ~int32_t(WM_FLAG_SKIP_NEGATIVE_ROUTES | WM_FLAG_MMA_DECODE)) {
     report("unknown flags");
     return nullptr;
   }
@@ -766,7 +706,6 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
   }
   wm::gemv_init_attributes(int(gemv_smem));
   wm::gemm_init_attributes();
-  wm::decode_init_attributes();
   wm::decode_mma_init_attributes(int(H), int(I));
   wm::bs_init_attributes();
   wm::router_init_attributes(int(H));

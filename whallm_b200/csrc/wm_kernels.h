@@ -140,7 +140,7 @@ void gemv_init_attributes(int max_smem);
 size_t gemv_smem_bytes(int H, int I);
 void launch_gemv(const GemvArgs& a, int fmt, int max_unique, cudaStream_t stream, Profiler* prof);
 
-// ---- decode on tcgen05, weights as the M operand (wm_decode_sm100.cu)
+// ---- decode kernel arguments (register-direct warp MMAs, wm_decode_mma.cu)
 struct DecodeArgs {
   Plan plan;            // 16-row tiles, no padding, rowmax set
   ExpertWeights wts;
@@ -153,19 +153,13 @@ struct DecodeArgs {
   uint32_t* status;
   int nbuf;             // decode_mma_kernel: token-tile buffers, 1 or 2 (decode_mma_buffers)
 };
-void decode_init_attributes();
-bool decode_shape_ok(int H, int I);
 // f16 sorted activation rows with their per-row prescale (x rows for gate/up,
 // act rows for down).
 void launch_gather_f16(const uint16_t* x, const Plan& p, int E, int H, uint16_t* out, float* scale, int num_sms,
                        cudaStream_t stream);
 void launch_act_f16(const uint16_t* act, const Plan& p, int E, int I, uint16_t* out, float* scale, int num_sms,
                     cudaStream_t stream);
-// maps[0..4]: CUtensorMaps of the routed experts' packed weights, the shared
-// expert's packed weights (3-D uint8 [E][rows][row bytes], boxes 32 x 64 for
-// gate/up, 32 x 128 for down), the routed and shared E8M0 scales (boxes
-// K/32 x 64 or 128), and the f16 activation rows (2-D, 64 x 16, 128B swizzle).
-void launch_decode(const DecodeArgs& a, int kind, const void* const* maps, int num_sms, cudaStream_t stream);
+
 
 // ---- decode, register-direct warp MMAs (wm_decode_mma.cu): plan tiles of 8
 // rows; tmap_x points to a CUtensorMap of the f16 activation rows [max_rows, K]

@@ -537,4 +537,159 @@ void launch_unpermute(const uint16_t* routed, const Plan& p, int TK, int H, uint
   unpermute_kernel<<<num_sms * 4, 256, 0, stream>>>(routed, p, TK, H, out);
 }
 
+
+// ------------------------------------------------------------------ f16 row copies
+// The prescaled f16 copies of the sorted rows that the register-direct decode
+// kernel and the MXFP4 grouped GEMM multiply (exact: a power-of-two scale per row).
+
+// 2^k for a row whose largest magnitude has float bits `maxbits`: the scaled
+// row's largest element lands in [2^14, 2^15).
+__device__ __forceinline__ float row_prescale(uint32_t maxbits) {
+  if (maxbits == 0u || maxbits >= 0x7f800000u) return 1.0f;
+  const int e = int(maxbits >> 23) - 127;  // floor(log2(max)) for normal values
+  const int k = min(max(14 - e, -100), 100);
+  return exp2f(float(k));
+}
+
+// One row of bf16 pieces (16 bytes) -> f16 pieces scaled by k2.
+__device__ __forceinline__ uint4 f16_piece(const uint4 v, float k2) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t q[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = unpack_bf16x2(w[j]);
+    const __half2 hh = __floats2half2_rn(f.x * k2, f.y * k2);
+    q[j] = *reinterpret_cast<const uint32_t*>(&hh);
+  }
+  return make_uint4(q[0], q[1], q[2], q[3]);
+}
+
+// Largest |bf16| of a piece, as ordered bits (a positive float's bits order like its value).
+__device__ __forceinline__ uint32_t piece_absmax_bits(const uint4 v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t m = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) m = max(m, max((w[j] & 0x7fffu) << 16, w[j] & 0x7fff0000u));
+  return m;
+}
+
+// Sorted f16 copy of the activation rows: out[r] = x[row_token[r]] * 2^k,
+// scale[r] = 2^k (largest magnitude of the row lands in [2^14, 2^15)).
+// One warp per sorted row; with NV > 0 (rows of at most 256 NV bf16) the row
+// stays in registers, so it is read once with all its loads in flight.
+// Padding rows (row_token < 0) only get scale 1: their data is left as the
+// workspace holds it (zero from creation, or an earlier call's finite f16
+// row).  Every product and epilogue of the expert kernels is row-local (a row
+// of A gives a row of D, a token column gives a column), and no padding row is
+// read by the combine, so what a padding row holds never reaches an output.
+template <int NV>
+__global__ void __launch_bounds__(256) gather_f16_kernel(const uint16_t* __restrict__ x, Plan p, int E, int H,
+                                                         uint16_t* __restrict__ out, float* __restrict__ scale) {
+  constexpr int kRowPieces = NV > 0 ? NV : 1;
+  const int rows = p.offsets[E + 1];
+  const int lane = threadIdx.x & 31;
+  const int pieces = H / 8, per_lane = (pieces + 31) / 32;
+  for (int r = blockIdx.x * 8 + (threadIdx.x >> 5); r < rows; r += gridDim.x * 8) {
+    const int t = p.row_token[r];
+    if (t < 0) {
+      if (lane == 0) scale[r] = 1.0f;
+      continue;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(x + int64_t(t) * H);
+    uint4* dst = reinterpret_cast<uint4*>(out + int64_t(r) * H);
+    if (NV > 0) {
+      // the whole row in registers: one read of it, all loads in flight at once
+      uint4 v[kRowPieces];
+      uint32_t m = 0;
+#pragma unroll
+      for (int j = 0; j < kRowPieces; ++j) {
+        const int i = lane + 32 * j;
+        v[j] = (t >= 0 && j < per_lane && i < pieces) ? src[i] : make_uint4(0, 0, 0, 0);
+        m = max(m, piece_absmax_bits(v[j]));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const float k2 = row_prescale(m);
+#pragma unroll
+      for (int j = 0; j < kRowPieces; ++j) {
+        const int i = lane + 32 * j;
+        if (j < per_lane && i < pieces) dst[i] = t >= 0 ? f16_piece(v[j], k2) : make_uint4(0, 0, 0, 0);
+      }
+      if (lane == 0) scale[r] = k2;
+      continue;
+    }
+    uint32_t m = 0;
+    if (t >= 0)
+      for (int i = lane; i < pieces; i += 32) m = max(m, piece_absmax_bits(src[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float k2 = row_prescale(m);
+    for (int i = lane; i < pieces; i += 32) dst[i] = t >= 0 ? f16_piece(src[i], k2) : make_uint4(0, 0, 0, 0);
+    if (lane == 0) scale[r] = k2;
+  }
+}
+
+// act rows -> f16 with the prescale of their |act| maxima; a warp takes two
+// rows per step (four when a row is at most 64 pieces) so their loads overlap.
+__global__ void __launch_bounds__(256) act_f16_kernel(const uint16_t* __restrict__ act, Plan p, int E, int I,
+                                                      uint16_t* __restrict__ out, float* __restrict__ scale) {
+  constexpr int R = 4;
+  const int rows = p.offsets[E + 1];
+  const int lane = threadIdx.x & 31;
+  const int pieces = I / 8;
+  const int warps = gridDim.x * 8;
+  for (int r0 = (blockIdx.x * 8 + (threadIdx.x >> 5)) * R; r0 < rows; r0 += warps * R) {
+    float k2[R];
+#pragma unroll
+    for (int q = 0; q < R; ++q) k2[q] = r0 + q < rows ? row_prescale(p.rowmax[r0 + q]) : 1.0f;
+    for (int i0 = lane; i0 < pieces; i0 += 32 * 2) {
+      uint4 v[R][2];
+#pragma unroll
+      for (int q = 0; q < R; ++q)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int i = i0 + 32 * h;
+          v[q][h] = (r0 + q < rows && i < pieces) ? reinterpret_cast<const uint4*>(act + int64_t(r0 + q) * I)[i]
+                                                  : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+      for (int q = 0; q < R; ++q)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int i = i0 + 32 * h;
+          if (r0 + q < rows && i < pieces)
+            reinterpret_cast<uint4*>(out + int64_t(r0 + q) * I)[i] = f16_piece(v[q][h], k2[q]);
+        }
+    }
+    if (lane < R && r0 + lane < rows) {
+      float k = 1.0f;
+#pragma unroll
+      for (int q = 0; q < R; ++q)
+        if (q == lane) k = k2[q];
+      scale[r0 + lane] = k;
+    }
+  }
+}
+
+// Tiles of 128 weight rows and 64 K; a row's E8M0 bytes (a multiple of 16)
+// come as one TMA box; the two scale slots fit shared memory up to K = 7168.
+bool decode_shape_ok(int H, int I) { return H % 512 == 0 && I % 512 == 0 && H <= 7168 && I <= 7168; }
+
+
+void launch_gather_f16(const uint16_t* x, const Plan& p, int E, int H, uint16_t* out, float* scale, int num_sms,
+                       cudaStream_t stream) {
+  const int per_lane = (H / 8 + 31) / 32;
+  if (per_lane <= 8)
+    gather_f16_kernel<8><<<num_sms * 4, 256, 0, stream>>>(x, p, E, H, out, scale);
+  else if (per_lane <= 16)
+    gather_f16_kernel<16><<<num_sms * 4, 256, 0, stream>>>(x, p, E, H, out, scale);
+  else
+    gather_f16_kernel<0><<<num_sms * 4, 256, 0, stream>>>(x, p, E, H, out, scale);
+}
+
+void launch_act_f16(const uint16_t* act, const Plan& p, int E, int I, uint16_t* out, float* scale, int num_sms,
+                    cudaStream_t stream) {
+  act_f16_kernel<<<num_sms * 4, 256, 0, stream>>>(act, p, E, I, out, scale);
+}
+
 }  // namespace wm

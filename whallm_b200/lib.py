@@ -20,7 +20,6 @@ CONV_MLX, CONV_METAL = 0, 1
 ROUTER_SOFTMAX, ROUTER_SQRTSOFTPLUS, ROUTER_SIGMOID, ROUTER_SIGMOID_GROUPED = 0, 1, 2, 3
 SHARED_NONE, SHARED_SIGMOID_GATE, SHARED_ONE = 0, 1, 2
 FLAG_SKIP_NEGATIVE_ROUTES = 1
-FLAG_TCGEN05_DECODE = 2
 FLAG_MMA_DECODE = 4
 
 # Every entry point the header declares (checked by the CPU test suite).

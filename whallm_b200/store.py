@@ -87,9 +87,9 @@ def _fused_slot(regions: dict[str, Region], blob: int) -> dict[str, Region]:
     with the virtual w13 = [w3; w1]; the blob's own offsets must be these."""
     w1, w3, s1, s3 = regions["w1.weight"], regions["w3.weight"], regions["w1.scale"], regions["w3.scale"]
     if w1.dtype != w3.dtype or w1.shape[1:] != w3.shape[1:]:
-        raise ValueError("w1 and w3 weights cannot use one fused projection")
+        raise ValueError(f"w1 ({w1.dtype}, {w1.shape}) and w3 ({w3.dtype}, {w3.shape}) differ in type or row shape: no fused w13 view")
     if s1.dtype != s3.dtype or s1.shape[1:] != s3.shape[1:]:
-        raise ValueError("w1 and w3 scales cannot use one fused projection")
+        raise ValueError(f"w1.scale ({s1.dtype}, {s1.shape}) and w3.scale ({s3.dtype}, {s3.shape}) differ in type or row shape: no fused w13 view")
     slot, off = {}, 0
     for name in ("w3.weight", "w1.weight", "w2.weight", "w3.scale", "w1.scale", "w2.scale"):
         src = regions[name]
@@ -98,7 +98,7 @@ def _fused_slot(regions: dict[str, Region], blob: int) -> dict[str, Region]:
         slot[name] = src
         off += src.length
     if off != blob:
-        raise ValueError("fused expert slot size does not match the manifest")
+        raise ValueError(f"the fused slot adds up to {off} bytes, the manifest says {blob}")
     slot["w13.weight"] = Region("w13.weight", w3.dtype, (w3.shape[0] + w1.shape[0], *w3.shape[1:]), 0,
                                 w3.length + w1.length)
     slot["w13.scale"] = Region("w13.scale", s3.dtype, (s3.shape[0] + s1.shape[0], *s3.shape[1:]), s3.offset,
@@ -113,13 +113,13 @@ def read_manifest(root: str | os.PathLike) -> ExpertManifest:
         raw = json.load(f)
     files = {item["path"]: int(item["size"]) for item in raw.get("files", [])}
     if len(files) != len(raw.get("files", [])):
-        raise ValueError("installed manifest contains duplicate file paths")
+        raise ValueError("manifest.json lists a file path more than once")
     for path, size in files.items():
         target = (root / path).resolve()
         if root not in target.parents or not target.is_file():
-            raise ValueError(f"installed model has an unsafe or missing file: {path}")
+            raise ValueError(f"manifest file {path} lies outside the model directory or does not exist")
         if target.stat().st_size != size:
-            raise ValueError(f"installed file size does not match the manifest: {path}")
+            raise ValueError(f"{path} has {target.stat().st_size} bytes, manifest.json says {size}")
     try:
         layers, experts = int(raw["layerCount"]), int(raw["expertCount"])
         selected, blob = int(raw["selectedExpertCount"]), int(raw["expertBlobSize"])
@@ -130,9 +130,9 @@ def read_manifest(root: str | os.PathLike) -> ExpertManifest:
     for layer in range(layers):
         path = layer_path(layer)
         if path not in files:
-            raise ValueError(f"installed model is missing {path}")
+            raise ValueError(f"manifest.json lists no {path}")
         if files[path] != experts * blob:
-            raise ValueError(f"installed expert layer has an invalid size: {path}")
+            raise ValueError(f"{path} has {files[path]} bytes, expected {experts} experts x {blob} bytes")
     regions = _regions_of(raw)
     names = frozenset(regions)
     if names == QWEN_REGION_NAMES:
