@@ -286,9 +286,11 @@ WM_EXPORT int wm_ep_wait(wm_ctx* ctx, wm_ep* ep, int32_t which, void* stream);
 /* The owner's half of a step, in place of wm_expert_pairs + wm_ep_return
    (call it after wm_ep_wait(0)): this rank's experts applied to the rows its
    peers dispatched to it -- only the real ones, each sender records how many
-   it sent -- and every result row stored straight from the sorted expert
-   rows into its sender's `back` block, then the return flags raised (wait
-   with wm_ep_wait(1)).  args gives this rank's experts (E = experts_per_rank,
+   it sent -- and every result row stored into its sender's `back` block (by
+   the down kernel's epilogue itself on the grouped GEMM and the block-scaled
+   decode kernel, so the return overlaps the math; from the sorted rows by a
+   copy kernel otherwise), then the return flags raised (wait with
+   wm_ep_wait(1)).  args gives this rank's experts (E = experts_per_rank,
    layout, H equal to the buffer's, I, w13, w2, swiglu_limit); x, routes,
    router, norm and shared fields are ignored; args->T is the number of rows
    this rank expects to receive, in [1, world * capacity], which picks the

@@ -491,7 +491,16 @@ __global__ void __launch_bounds__(kThreads, 1) bs_decode_kernel(const __grid_con
       if (lane == 0) mbar_arrive(&sh.tmem_empty[acc]);
       if (KIND == 1) {
         const int h = blk * kBM + quarter * 32 + lane;
-        for (int n = 0; n < valid; ++n) a.routed[int64_t(row0 + n) * a.H + h] = f32_to_bf16_bits(y[n]);
+        if (a.ret.rows[0] != nullptr) {  // expert-parallel owner: straight into the senders' back blocks
+          for (int n = 0; n < valid; ++n) {
+            const int slot = a.plan.row_token[row0 + n];
+            if (slot >= 0)
+              a.ret.rows[slot / a.ret.capacity][int64_t(slot % a.ret.capacity) * a.H + h] = f32_to_bf16_bits(y[n]);
+          }
+          __threadfence_system();
+        } else {
+          for (int n = 0; n < valid; ++n) a.routed[int64_t(row0 + n) * a.H + h] = f32_to_bf16_bits(y[n]);
+        }
       } else {
         // tile rows 0..63 are w13 rows blk * 64 .. of the first half (gate for
         // the Qwen layout, up for w13 = [w3; w1]), rows 64..127 the same rows of

@@ -459,7 +459,8 @@ bool encode_scale_rows(wm_ctx* ctx, CUtensorMap* map, const void* base, int64_t 
 
 // The block-scaled decode path: hi / lo E4M3 token tiles, gate/up (+SwiGLU,
 // act tiles), down.  The plan's groups are padded to 16 rows.
-int run_bs_decode(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts, bool has_shared, cudaStream_t s) {
+int run_bs_decode(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts, bool has_shared, cudaStream_t s,
+                  const wm::EpReturn* ret) {
   const int H = a->H, I = a->I;
   CUtensorMap w13, w13s, w2, w2s, s13, s13s, s2, s2s;
   bool ok = encode_fp4_weights(ctx, &w13, a->w13.weight, H, 2 * I, a->E, a->w13.weight_stride, 64, 2) &&
@@ -493,6 +494,7 @@ int run_bs_decode(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wt
   wm::launch_bs_decode(b, 0, maps0, ctx->num_sms, s);
   wm::prof_end(&ctx->prof, wm::kProfDecodeGateUp, s);
   b.img = aimg;
+  if (ret != nullptr) b.ret = *ret;
   wm::prof_begin(&ctx->prof, wm::kProfDecodeDown, s);
   const void* maps1[4] = {&w2, has_shared ? &w2s : &w2, &s2, has_shared ? &s2s : &s2};
   wm::launch_bs_decode(b, 1, maps1, ctx->num_sms, s);
@@ -502,12 +504,15 @@ int run_bs_decode(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wt
   return check_launch(ctx, "block-scaled expert decode");
 }
 
-// Runs the experts of a plan already built on `s` (rows in ctx->routed).
-int run_experts(wm_ctx* ctx, const wm_moe_args* a, bool has_shared, Path path, cudaStream_t s) {
+// Runs the experts of a plan already built on `s` (rows in ctx->routed, or,
+// with `ret`, the down rows stored straight into the senders' back blocks:
+// the grouped GEMM and the block-scaled decode path only).
+int run_experts(wm_ctx* ctx, const wm_moe_args* a, bool has_shared, Path path, cudaStream_t s,
+                const wm::EpReturn* ret = nullptr) {
   const wm::ExpertWeights wts = weights_of(a, has_shared);
   const int gate_first = a->layout == WM_LAYOUT_QWEN_GATE_UP_MXFP4 ? 1 : 0;
   if (path == kPathDecodeMma) return run_decode_mma(ctx, a, wts, s);
-  if (path == kPathBsDecode) return run_bs_decode(ctx, a, wts, has_shared, s);
+  if (path == kPathBsDecode) return run_bs_decode(ctx, a, wts, has_shared, s, ret);
   if (path == kPathGemv) {
     wm::GemvArgs g{};
     g.plan = ctx->plan;
@@ -576,6 +581,7 @@ int run_experts(wm_ctx* ctx, const wm_moe_args* a, bool has_shared, Path path, c
   g.N = a->H;
   g.ascale = f16 ? ctx->actscale : nullptr;
   g.rowmax = nullptr;
+  if (ret != nullptr) g.ret = *ret;
   wm::prof_begin(&ctx->prof, wm::kProfGemmDown, s);
   wm::launch_gemm(g, 1, &map_act, ctx->num_sms, s);
   wm::prof_end(&ctx->prof, wm::kProfGemmDown, s);
@@ -1153,10 +1159,23 @@ WM_EXPORT int wm_ep_experts(wm_ctx* ctx, wm_ep* ep, const wm_moe_args* args, voi
   wm::prof_end(&ctx->prof, wm::kProfPlan, s);
   ctx->counters.launches += launches;
   if (int rc = check_launch(ctx, "plan")) return rc;
-  if (int rc = run_experts(ctx, &b, false, path, s)) return rc;
+  // the grouped GEMM and the block-scaled decode kernel store the down rows
+  // straight into the senders' back blocks (the return overlaps the math);
+  // the other kernels leave them sorted and a copy kernel returns them
+  const wm::EpPeers back = ep_peers(ep, 1);
+  const bool fused = path == kPathGemm || path == kPathBsDecode;
+  wm::EpReturn ret{};
+  if (fused) {
+    for (int r = 0; r < ep->world; ++r) ret.rows[r] = back.rows[r];
+    ret.capacity = int(ep->capacity);
+  }
+  if (int rc = run_experts(ctx, &b, false, path, s, fused ? &ret : nullptr)) return rc;
   wm::prof_begin(&ctx->prof, wm::kProfEpReturn, s);
-  wm::launch_ep_return_sorted(ctx->routed, ctx->plan.pair_pos, counts, ep->world, int(ep->capacity), ep->H,
-                              ep_peers(ep, 1), ctx->num_sms, s);
+  if (fused)
+    wm::launch_ep_signal(back, ep->world, s);
+  else
+    wm::launch_ep_return_sorted(ctx->routed, ctx->plan.pair_pos, counts, ep->world, int(ep->capacity), ep->H,
+                                back, ctx->num_sms, s);
   wm::prof_end(&ctx->prof, wm::kProfEpReturn, s);
   ctx->counters.launches += 1;
   ctx->counters.calls_pairs += 1;

@@ -175,6 +175,17 @@ void launch_ep_return(const uint16_t* y, const int32_t* recv_e, int world, int c
   ep_return_kernel<<<2 * num_sms, kCopyThreads, 0, stream>>>(y, recv_e, world, capacity, H, pe);
 }
 
+// Raises this rank's return flag on every peer to the step number.
+__global__ void ep_signal_kernel(const EpPeers pe, int world) {
+  __threadfence_system();
+  const uint32_t step = *pe.epoch;
+  if (threadIdx.x < world) st_release_sys(pe.flag[threadIdx.x], step);
+}
+
+void launch_ep_signal(const EpPeers& pe, int world, cudaStream_t stream) {
+  ep_signal_kernel<<<1, 32, 0, stream>>>(pe, world);
+}
+
 void launch_ep_return_sorted(const uint16_t* routed, const int32_t* pair_pos, const int32_t* counts, int world,
                              int capacity, int H, const EpPeers& pe, int num_sms, cudaStream_t stream) {
   ep_return_sorted_kernel<<<2 * num_sms, kCopyThreads, 0, stream>>>(routed, pair_pos, counts, world, capacity, H, pe);

@@ -435,6 +435,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (a.rowmax != nullptr) atomicMax(a.rowmax + row, __float_as_uint(amax));
       } else {
         uint16_t* dst = a.out + int64_t(row) * a.N + nt * BN;
+        if (a.ret.rows[0] != nullptr) {  // expert-parallel owner: straight into the sender's back block
+          const int slot = a.plan.row_token[row];
+          dst = slot < 0 ? nullptr
+                         : a.ret.rows[slot / a.ret.capacity] + int64_t(slot % a.ret.capacity) * a.N + nt * BN;
+        }
 #pragma unroll 1
         for (int jc = 0; jc < 8; ++jc) {
           uint32_t v[32];
@@ -450,9 +455,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             pk[i] = pack_bf16x2(v0, v1);
           }
-          stg_v8(dst + jc * 32, pk);
-          stg_v8(dst + jc * 32 + 16, pk + 8);
+          if (dst != nullptr) {
+            stg_v8(dst + jc * 32, pk);
+            stg_v8(dst + jc * 32 + 16, pk + 8);
+          }
         }
+        if (a.ret.rows[0] != nullptr) __threadfence_system();  // before the flags of the next kernel
       }
       tc_fence_before();
       __syncwarp();

@@ -97,6 +97,14 @@ void launch_ep_finish(const int32_t* idx, const Plan& p, int T, int K, int per_r
 constexpr int kMaxEpRanks = 8;
 // The blocks this rank writes in every rank's exchange buffer (peer r's
 // address space mapped here), and this rank's own step state.
+// Down-projection rows of an expert-parallel owner stored straight into the
+// senders' `back` blocks: sorted row r holds slot s = plan.row_token[r] (s <
+// 0: padding), which goes to rows[s / capacity] + (s % capacity) * H.
+struct EpReturn {
+  uint16_t* rows[kMaxEpRanks];  // every rank's back block for this rank; rows[0] == nullptr: off
+  int capacity;
+};
+
 struct EpPeers {
   uint16_t* rows[kMaxEpRanks];  // rank r's recv_x (dispatch) or back (return) block for this rank
   int32_t* ids[kMaxEpRanks];    // rank r's recv_e block for this rank (dispatch)
@@ -120,6 +128,9 @@ void launch_plan_blocks(const int32_t* ids, const int32_t* counts, int world, in
                         cudaStream_t stream, int* launches);
 // Result rows straight from the owner's sorted rows (routed[pair_pos[slot]])
 // into each sender's back block, then the return flags.
+// After a down kernel that stored the rows itself: raise this rank's return
+// flag on every peer (system-scope fence first).
+void launch_ep_signal(const EpPeers& pe, int world, cudaStream_t stream);
 void launch_ep_return_sorted(const uint16_t* routed, const int32_t* pair_pos, const int32_t* counts, int world,
                              int capacity, int H, const EpPeers& pe, int num_sms, cudaStream_t stream);
 void launch_unpermute(const uint16_t* routed, const Plan& p, int TK, int H, uint16_t* out, int num_sms,
@@ -190,6 +201,7 @@ struct BsArgs {
   const uint8_t* img;    // token tile images [tiles][K / 128][4608]: hi rows 0..15, lo rows 16..31, scale atom
   uint8_t* act_img;      // gate/up: act tile images for the down kernel (K = I)
   uint16_t* routed;      // down: [rows, H] bf16
+  EpReturn ret;          // down: with ret.rows[0] set, rows go to the senders instead of `routed`
   int stages;
 };
 void bs_init_attributes();
@@ -219,6 +231,7 @@ struct GemmArgs {
   const float* ascale;  // MXFP4: [rows] 2^k prescale of the f16 A rows
   uint32_t* rowmax;     // MXFP4 gate/up: [rows] per-row |act| maxima (float bits), or null
   int w32;              // 1: every expert's weight rows start 32-byte aligned (256-bit loads)
+  EpReturn ret;         // down: with ret.rows[0] set, rows go to the senders instead of `out`
 };
 // `kind`: 0 = gate/up + SwiGLU, 1 = down.  MXFP4 takes f16 A rows (gather_f16 /
 // act_f16), FP8 bf16 rows (gather_rows / the bf16 act).  tmap_a points to a CUtensorMap
