@@ -648,11 +648,23 @@ def decode_batch_line(eng, layer, dev, B: int, steps: int, flush) -> dict:
         _, (_, ri) = eng.forward(layer, xs[i], K, return_routes=True)
         uniq.append(int(torch.unique(ri).numel()))
     torch.cuda.synchronize()
+    # where the time goes: per-kernel CUDA-event durations of eager calls (each
+    # includes its launch; the graph-replayed step above has no host gaps)
+    eng.ctx.profile(True)
+    eng.ctx.profile_reset()
+    for i in range(steps):
+        x_static.copy_(xs[i % 8])
+        flush.zero_()
+        eng.forward(layer, x_static, K, out=out)
+    torch.cuda.synchronize()
+    kernels = {n: round(1e3 * t / c, 2) for n, (c, t) in eng.ctx.profile_read().items()}
+    eng.ctx.profile(False)
     del graph
     U = sum(uniq) / len(uniq)
     layer_bytes = (U + 1) * BLOB + E * H * 2 + H * 2 + 4 * B * H  # experts + router + shared gate + x/out
     return {"batch": B, "ms_per_step": ms, "tokens_per_s": B / (ms / 1e3), "unique_experts": U,
-            "layer_bytes": layer_bytes, "achieved_gbs": layer_bytes / (ms / 1e3) / 1e9}
+            "layer_bytes": layer_bytes, "achieved_gbs": layer_bytes / (ms / 1e3) / 1e9,
+            "kernels_avg_us_eager": kernels}
 
 
 def cpu_baselines(dev, cores: int, threads: int) -> dict:

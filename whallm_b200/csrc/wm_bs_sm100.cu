@@ -469,11 +469,24 @@ __global__ void __launch_bounds__(kThreads, 1) bs_decode_kernel(const __grid_con
     // ---------------------------------------------------------------- epilogue
     const int quarter = warp - kEpiWarp0;  // TMEM lanes 32 quarter .. 32 quarter + 31
     int li = 0;
+    // item metadata read ahead (the tile entry two items early, the expert's
+    // row count one item early), off the path from one accumulator to the next
+    int ce = 0, crow0 = 0, cblk = 0, cvalid = 0, ne = 0, nrow0 = 0, nblk = 0;
+    if (int(blockIdx.x) < n_items) {
+      item(blockIdx.x, &ce, &crow0, &cblk);
+      cvalid = min(kTokTile, a.plan.counts[ce] - (crow0 - a.plan.offsets[ce]));
+    }
+    if (int(blockIdx.x + gridDim.x) < n_items) item(blockIdx.x + gridDim.x, &ne, &nrow0, &nblk);
     for (int q = blockIdx.x; q < n_items; q += gridDim.x, ++li) {
       if (warp_aborted(abort)) break;
-      int e, row0, blk;
-      item(q, &e, &row0, &blk);
-      const int valid = min(kTokTile, a.plan.counts[e] - (row0 - a.plan.offsets[e]));
+      const int e = ce, row0 = crow0, blk = cblk, valid = cvalid;
+      int n2e = 0, n2row0 = 0, n2blk = 0, ncount = 0, noff = 0;
+      if (q + 2 * int(gridDim.x) < n_items) item(q + 2 * gridDim.x, &n2e, &n2row0, &n2blk);
+      if (q + int(gridDim.x) < n_items) {
+        ncount = a.plan.counts[ne];
+        noff = a.plan.offsets[ne];
+      }
+      (void)e;
       const int acc = li & 1;
       if (!warp_wait(&sh.tmem_full[acc], (li >> 1) & 1, abort)) {
         if (lane == 0) fail(80 + KIND);
@@ -497,7 +510,6 @@ __global__ void __launch_bounds__(kThreads, 1) bs_decode_kernel(const __grid_con
             if (slot >= 0)
               a.ret.rows[slot / a.ret.capacity][int64_t(slot % a.ret.capacity) * a.H + h] = f32_to_bf16_bits(y[n]);
           }
-          __threadfence_system();
         } else {
           for (int n = 0; n < valid; ++n) a.routed[int64_t(row0 + n) * a.H + h] = f32_to_bf16_bits(y[n]);
         }
@@ -557,7 +569,13 @@ __global__ void __launch_bounds__(kThreads, 1) bs_decode_kernel(const __grid_con
           if (lane == 0) mbar_arrive(&sh.xch_empty[xb]);  // xch[xb] is free again
         }
       }
+      ce = ne, crow0 = nrow0, cblk = nblk;
+      cvalid = min(kTokTile, ncount - (nrow0 - noff));
+      ne = n2e, nrow0 = n2row0, nblk = n2blk;
     }
+    // rows stored into other GPUs' memory: one system-scope fence per thread,
+    // after its last store (a fence per item would wait out NVLink each time)
+    if (KIND == 1 && a.ret.rows[0] != nullptr) __threadfence_system();
   }
   tc_fence_before();
   __syncthreads();

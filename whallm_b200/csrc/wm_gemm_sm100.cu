@@ -460,12 +460,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             stg_v8(dst + jc * 32 + 16, pk + 8);
           }
         }
-        if (a.ret.rows[0] != nullptr) __threadfence_system();  // before the flags of the next kernel
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh.tmem_empty[acc]);
     }
+    // rows stored into other GPUs' memory: one system-scope fence per thread
+    // after its last store, before the next kernel raises the flags
+    if (KIND == 1 && a.ret.rows[0] != nullptr) __threadfence_system();
   }
 
   tc_fence_before();
