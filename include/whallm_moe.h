@@ -128,6 +128,14 @@ typedef struct {
    32-byte aligned weight regions and 16-byte aligned scale regions. */
 #define WM_FLAG_MMA_DECODE 4
 
+/* Long MXFP4 calls take the kind::f16 tcgen05 grouped GEMM (weights
+   dequantised to exact f16 by producer warps, activation rows as f16)
+   instead of the default block-scaled one.  The default: E2M1 weights by TMA
+   with their E8M0 scales as the MMA's scale factors (kind::mxf8f6f4), token
+   and act rows as hi + lo E4M3 parts (as for WM_FLAG_MMA_DECODE's default);
+   same shape and alignment needs as the block-scaled decode kernel. */
+#define WM_FLAG_F16_GEMM 8
+
 /* One projection of every expert: expert e's matrix at weight + e * weight_stride
    bytes, its scales at scale + e * scale_stride bytes (device pointers). */
 typedef struct {
@@ -179,6 +187,8 @@ typedef struct {
   int64_t gemv_calls, gemm_calls;
   int64_t decode_calls;        /* calls that took the decode kernels (block-scaled tcgen05 by default,
                                   WM_FLAG_MMA_DECODE selects the register-direct one) */
+  int64_t bs_gemm_calls;       /* the gemm_calls that took the block-scaled grouped GEMM (the default
+                                  for MXFP4; WM_FLAG_F16_GEMM selects the kind::f16 one) */
 } wm_counters;
 
 typedef struct {

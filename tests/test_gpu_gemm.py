@@ -1,4 +1,6 @@
-"""The tcgen05 grouped-GEMM (prefill) path vs the CPU oracle (needs a B200).
+"""The tcgen05 grouped-GEMM (prefill) paths vs the CPU oracle (needs a B200): the
+block-scaled GEMM for the full-size MXFP4 configs, the kind::f16 GEMM for the
+small shapes and FP8.
 
 Same tolerance as the decode path: max|y - y_ref| / max|y_ref| <= 1e-2 on bf16
 outputs.  Full-size layers are checked on sampled tokens (the oracle runs only
@@ -144,7 +146,7 @@ def test_config2_prefill_full_size():
     eng = Engine(0, max_tokens=16384, hidden=2048, inter=512, experts=512, topk=10)
     out, (w, idx) = eng.forward(wl.layer, wl.x, wl.K, return_routes=True)
     eng.sync()
-    assert eng.ctx.counters().gemm_calls == 1
+    assert eng.ctx.counters().gemm_calls == 1 and eng.ctx.counters().bs_gemm_calls == 1
     assert torch.isfinite(out.float()).all()
     counts = torch.bincount(idx.reshape(-1).long(), minlength=512)
     assert counts.sum().item() == 16384 * 10 and counts.max().item() > 20 * counts.float().median().item()
@@ -186,7 +188,7 @@ def test_config4_layer_full_size():
     eng = Engine(0, max_tokens=T, hidden=7168, inter=2048, experts=384, topk=8)
     out, (w, idx) = eng.forward(layer, wl.x, wl.K, return_routes=True)
     eng.sync()
-    assert eng.ctx.counters().gemm_calls == 1
+    assert eng.ctx.counters().gemm_calls == 1 and eng.ctx.counters().bs_gemm_calls == 1
     assert torch.isfinite(out.float()).all()
     tokens = _coverage_sample(idx, 384, np.random.default_rng(2), 16)
     tokens = np.union1d(tokens, np.array([1, 100, 255, 256, 257], dtype=np.int64))  # decode / prefill boundary

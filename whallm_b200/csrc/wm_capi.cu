@@ -37,7 +37,7 @@ struct wm_ctx {
   float* actscale = nullptr;   // [rows] prescale of the f16 act rows (decode path)
   uint32_t* rowmax = nullptr;  // [rows] per-row |act| maxima (decode path)
   uint16_t* xn = nullptr;      // [T, H] normalised input rows (pre-MoE RMSNorm)
-  uint8_t* bs_img_x = nullptr;    // block-scaled decode: token tile images (hi / lo E4M3 + scale atoms)
+  uint8_t* bs_img_x = nullptr;    // block-scaled decode / GEMM: token tile images (hi / lo E4M3 + scale atoms)
   uint8_t* bs_img_act = nullptr;  // ... and the act tile images
   int max_rows = 0, max_mtiles = 0, max_chunks = 0;
   PFN_cuTensorMapEncodeTiled_v12000 encode_tiled = nullptr;
@@ -289,7 +289,7 @@ bool use_gemm(const wm_ctx* ctx, const wm_moe_args* a) {
   return gemm && wm::gemm_shape_ok(a->H, a->I) && ctx->encode_tiled != nullptr;
 }
 
-enum Path { kPathGemv = 0, kPathGemm = 2, kPathDecodeMma = 3, kPathBsDecode = 4 };
+enum Path { kPathGemv = 0, kPathGemm = 2, kPathDecodeMma = 3, kPathBsDecode = 4, kPathBsGemm = 5 };
 
 // The block-scaled decode kernel's TMA operands: packed weights 32-byte
 // aligned with 32-byte multiple strides (16U4_ALIGN16B), E8M0 rows 16-byte
@@ -304,13 +304,16 @@ bool bs_operands_ok(const wm_ctx* ctx, const wm_moe_args* a, bool has_shared) {
   return true;
 }
 
-// Which expert kernels a call takes: the tcgen05 grouped GEMM for long calls;
-// for short calls the block-scaled tcgen05 decode kernel (MXFP4 experts whose
+// Which expert kernels a call takes: for long calls the block-scaled tcgen05
+// grouped GEMM (MXFP4 experts whose shapes and regions its TMA operands take,
+// unless WM_FLAG_F16_GEMM), else the kind::f16 tcgen05 grouped GEMM; for short
+// calls the block-scaled tcgen05 decode kernel (MXFP4 experts whose
 // shapes and regions its TMA operands take, unless WM_FLAG_MMA_DECODE), else
 // the register-direct decode kernel where 16-byte loads are possible (MXFP4
 // and FP8), else the CUDA-core GEMV.
 Path expert_path(const wm_ctx* ctx, const wm_moe_args* a, bool has_shared) {
-  if (use_gemm(ctx, a)) return kPathGemm;
+  if (use_gemm(ctx, a))
+    return !(ctx->opt.flags & WM_FLAG_F16_GEMM) && bs_operands_ok(ctx, a, has_shared) ? kPathBsGemm : kPathGemm;
   if (ctx->encode_tiled == nullptr) return kPathGemv;
   const wm_matrix* ms[4] = {&a->w13, &a->w2, &a->shared_w13, &a->shared_w2};
   for (int i = 0; i < (has_shared ? 4 : 2); ++i)
@@ -322,9 +325,11 @@ Path expert_path(const wm_ctx* ctx, const wm_moe_args* a, bool has_shared) {
   return wm::decode_mma_shape_ok(a->H, a->I, fmt_of(a->layout)) ? kPathDecodeMma : kPathGemv;
 }
 
-// Rows each expert's group is padded to: the GEMM's 128-row tiles, the
+// Rows each expert's group is padded to: the GEMMs' 128-row tiles, the
 // block-scaled decode kernel's 16-token tiles, else none.
-int plan_align(Path path) { return path == kPathGemm ? wm::kTileM : path == kPathBsDecode ? 16 : 1; }
+int plan_align(Path path) {
+  return path == kPathGemm || path == kPathBsGemm ? wm::kTileM : path == kPathBsDecode ? 16 : 1;
+}
 
 // Plan fields of the expert kernels of `path`.
 void plan_for_path(const wm_ctx* ctx, Path path, wm::Plan* plan) {
@@ -504,15 +509,63 @@ int run_bs_decode(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wt
   return check_launch(ctx, "block-scaled expert decode");
 }
 
+// The block-scaled grouped GEMM path: hi / lo E4M3 tile images of the x
+// rows, gate/up (+SwiGLU, act tile images), down.  The plan's groups are
+// padded to 128 rows.
+int run_bs_gemm(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts, bool has_shared, cudaStream_t s,
+                const wm::EpReturn* ret) {
+  const int H = a->H, I = a->I;
+  CUtensorMap w13, w13s, w2, w2s, s13, s13s, s2, s2s;
+  bool ok = encode_fp4_weights(ctx, &w13, a->w13.weight, H, 2 * I, a->E, a->w13.weight_stride, 64, 2) &&
+            encode_fp4_weights(ctx, &w2, a->w2.weight, I, H, a->E, a->w2.weight_stride, 128, 1) &&
+            encode_scale_rows(ctx, &s13, a->w13.scale, H / 32, 2 * I, a->E, a->w13.scale_stride, 64, 2) &&
+            encode_scale_rows(ctx, &s2, a->w2.scale, I / 32, H, a->E, a->w2.scale_stride, 128, 1);
+  if (has_shared)
+    ok = ok && encode_fp4_weights(ctx, &w13s, a->shared_w13.weight, H, 2 * I, 1, 0, 64, 2) &&
+         encode_fp4_weights(ctx, &w2s, a->shared_w2.weight, I, H, 1, 0, 128, 1) &&
+         encode_scale_rows(ctx, &s13s, a->shared_w13.scale, H / 32, 2 * I, 1, 0, 64, 2) &&
+         encode_scale_rows(ctx, &s2s, a->shared_w2.scale, I / 32, H, 1, 0, 128, 1);
+  if (!ok) return fail(ctx, "cuTensorMapEncodeTiled failed for the block-scaled expert operands");
+  wm::BsArgs b{};
+  b.plan = ctx->plan;
+  b.wts = wts;
+  b.H = H;
+  b.I = I;
+  b.gate_first = a->layout == WM_LAYOUT_QWEN_GATE_UP_MXFP4 ? 1 : 0;
+  b.limit = a->swiglu_limit;
+  b.status = ctx->status;
+  b.act_img = ctx->bs_img_act;
+  b.routed = ctx->routed;
+  wm::prof_begin(&ctx->prof, wm::kProfGather, s);
+  wm::launch_bsg_quant_rows(static_cast<const uint16_t*>(a->x), b.plan, H, ctx->bs_img_x, ctx->num_sms, s);
+  wm::prof_end(&ctx->prof, wm::kProfGather, s);
+  b.img = ctx->bs_img_x;
+  wm::prof_begin(&ctx->prof, wm::kProfGemmGateUp, s);
+  const void* maps0[4] = {&w13, has_shared ? &w13s : &w13, &s13, has_shared ? &s13s : &s13};
+  wm::launch_bsg(b, 0, maps0, ctx->num_sms, s);
+  wm::prof_end(&ctx->prof, wm::kProfGemmGateUp, s);
+  b.img = ctx->bs_img_act;
+  if (ret != nullptr) b.ret = *ret;
+  wm::prof_begin(&ctx->prof, wm::kProfGemmDown, s);
+  const void* maps1[4] = {&w2, has_shared ? &w2s : &w2, &s2, has_shared ? &s2s : &s2};
+  wm::launch_bsg(b, 1, maps1, ctx->num_sms, s);
+  wm::prof_end(&ctx->prof, wm::kProfGemmDown, s);
+  ctx->counters.launches += 3;
+  ctx->counters.gemm_calls += 1;
+  ctx->counters.bs_gemm_calls += 1;
+  return check_launch(ctx, "block-scaled expert GEMM");
+}
+
 // Runs the experts of a plan already built on `s` (rows in ctx->routed, or,
 // with `ret`, the down rows stored straight into the senders' back blocks:
-// the grouped GEMM and the block-scaled decode path only).
+// the grouped GEMMs and the block-scaled decode path only).
 int run_experts(wm_ctx* ctx, const wm_moe_args* a, bool has_shared, Path path, cudaStream_t s,
                 const wm::EpReturn* ret = nullptr) {
   const wm::ExpertWeights wts = weights_of(a, has_shared);
   const int gate_first = a->layout == WM_LAYOUT_QWEN_GATE_UP_MXFP4 ? 1 : 0;
   if (path == kPathDecodeMma) return run_decode_mma(ctx, a, wts, s);
   if (path == kPathBsDecode) return run_bs_decode(ctx, a, wts, has_shared, s, ret);
+  if (path == kPathBsGemm) return run_bs_gemm(ctx, a, wts, has_shared, s, ret);
   if (path == kPathGemv) {
     wm::GemvArgs g{};
     g.plan = ctx->plan;
@@ -603,7 +656,7 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
     return nullptr;
   }
   wm_options o = *options;
-  if (o.flags & ~int32_t(WM_FLAG_SKIP_NEGATIVE_ROUTES | WM_FLAG_MMA_DECODE)) {
+  if (o.flags & ~int32_t(WM_FLAG_SKIP_NEGATIVE_ROUTES | WM_FLAG_MMA_DECODE | WM_FLAG_F16_GEMM)) {
     report("unknown flags");
     return nullptr;
   }
@@ -657,8 +710,10 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
                o_act = take(rows * I * 2), o_routed = take(rows * H * 2), o_logits = take(T * E * 4),
                o_idx = take(T * K * 4), o_w = take(T * K * 4), o_sg = take(T * 4), o_status = take(16),
                o_act16 = take(rows * I * 2), o_rowscale = take(rows * 4), o_actscale = take(rows * 4),
-               o_rowmax = take(rows * 4), o_xn = take(T * H * 2), o_imgx = take(rows * H * 9 / 4),
-               o_imga = take(rows * I * 9 / 4);
+               o_rowmax = take(rows * 4), o_xn = take(T * H * 2),
+               // tile images: the decode kernel's 16-row tiles or the GEMM's 128-row tiles
+               o_imgx = take(std::max<size_t>(rows * H * 9 / 4, wm::bsg_image_bytes(rows / wm::kTileM + 2, int(H)))),
+               o_imga = take(std::max<size_t>(rows * I * 9 / 4, wm::bsg_image_bytes(rows / wm::kTileM + 2, int(I))));
   ctx->ws_bytes = off;
   if (cudaMalloc(&ctx->ws, ctx->ws_bytes) != cudaSuccess) {
     cudaGetLastError();
@@ -714,6 +769,7 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
   wm::gemm_init_attributes();
   wm::decode_mma_init_attributes(int(H), int(I));
   wm::bs_init_attributes();
+  wm::bsg_init_attributes();
   wm::router_init_attributes(int(H));
   wm::router_gemm_init_attributes();
   cudaDriverEntryPointQueryResult q{};
@@ -1163,7 +1219,7 @@ WM_EXPORT int wm_ep_experts(wm_ctx* ctx, wm_ep* ep, const wm_moe_args* args, voi
   // straight into the senders' back blocks (the return overlaps the math);
   // the other kernels leave them sorted and a copy kernel returns them
   const wm::EpPeers back = ep_peers(ep, 1);
-  const bool fused = path == kPathGemm || path == kPathBsDecode;
+  const bool fused = path == kPathGemm || path == kPathBsGemm || path == kPathBsDecode;
   wm::EpReturn ret{};
   if (fused) {
     for (int r = 0; r < ep->world; ++r) ret.rows[r] = back.rows[r];

@@ -216,6 +216,16 @@ void launch_bs_quant_rows(const uint16_t* x, const Plan& p, int E, int K, uint8_
 // rows (uint8, gate/up [E][2][I][H/32] boxes 16 x 64 x 2, down [E][H][I/32] boxes 16 x 128).
 void launch_bs_decode(const BsArgs& a, int kind, const void* const* maps, int num_sms, cudaStream_t stream);
 
+// ---- prefill grouped GEMM on tcgen05 block-scaled MMA (wm_bsgemm_sm100.cu):
+// 128 token rows (hi / lo E4M3 tile images) x 256 weight rows per tile.  The
+// same BsArgs (plan with 128-row tiles; img / act_img hold 33,792-byte images
+// per 128-row tile and 128-K stage, bsg_image_bytes) and the same tensor maps
+// as launch_bs_decode; shapes as bs_shape_ok.
+void bsg_init_attributes();
+size_t bsg_image_bytes(int64_t mtiles, int K);
+void launch_bsg_quant_rows(const uint16_t* x, const Plan& p, int K, uint8_t* img, int num_sms, cudaStream_t stream);
+void launch_bsg(const BsArgs& a, int kind, const void* const* maps, int num_sms, cudaStream_t stream);
+
 // ---- prefill grouped GEMM on tcgen05 (wm_gemm_sm100.cu)
 struct GemmArgs {
   Plan plan;

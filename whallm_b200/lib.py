@@ -21,6 +21,7 @@ ROUTER_SOFTMAX, ROUTER_SQRTSOFTPLUS, ROUTER_SIGMOID, ROUTER_SIGMOID_GROUPED = 0,
 SHARED_NONE, SHARED_SIGMOID_GATE, SHARED_ONE = 0, 1, 2
 FLAG_SKIP_NEGATIVE_ROUTES = 1
 FLAG_MMA_DECODE = 4
+FLAG_F16_GEMM = 8
 
 # Every entry point the header declares (checked by the CPU test suite).
 EXPORTS = (
@@ -72,6 +73,7 @@ class Counters(ctypes.Structure):
     _fields_ = [
         ("calls_forward", _I64), ("calls_pairs", _I64), ("calls_route", _I64), ("calls_dequant", _I64),
         ("launches", _I64), ("gemv_calls", _I64), ("gemm_calls", _I64), ("decode_calls", _I64),
+        ("bs_gemm_calls", _I64),
     ]
 
 
