@@ -228,6 +228,11 @@ def prefill_section(args, dev, pk, n: int = 2) -> dict:
     layer_tf = (gu_flops + dn_flops) / (ms / 1e3) / 1e12
     fp8 = lay.layout == lib_layout_fp8()
     nominal = 4500.0 if fp8 else 9000.0
+    bs = eng.ctx.counters().bs_gemm_calls > 0
+    # rows the 128-row tiles cover (each expert's group padded to 128; the MMA runs on them all)
+    tile_rows = int(((counts + 127) // 128).sum()) * 128 + (T + 127) // 128 * 128
+    mma = ("kind::mxf8f6f4.block_scale (E2M1 weights with E8M0 scale factors; activation rows as hi + lo "
+           "E4M3 parts, two MMAs per K step)" if bs else "kind::f16 (bf16 operands, exact dequantised weights)")
     out = {
         "workload": LONG_CONFIGS[n], "tokens_per_s": T / (ms / 1e3),
         "ms_per_layer": ms, "layer_tflops": layer_tf,
@@ -235,8 +240,11 @@ def prefill_section(args, dev, pk, n: int = 2) -> dict:
                      "peak_bf16": pk["bf16_tflops"], "frac_bf16": tf_gu / pk["bf16_tflops"],
                      ("peak_fp8_nominal" if fp8 else "peak_fp4_nominal"): nominal,
                      ("frac_fp8_nominal" if fp8 else "frac_fp4_nominal"): tf_gu / nominal,
-                     "mma_kind": "kind::f16 (bf16 operands, exact dequantised weights)", "peak_source": pk["source"],
-                     "down_tflops": tf_dn, "algorithmic_flops_per_launch": gu_flops},
+                     "mma_kind": mma, "peak_source": pk["source"],
+                     "down_tflops": tf_dn, "algorithmic_flops_per_launch": gu_flops,
+                     "tile_row_utilisation": rows / tile_rows,
+                     **({"tensor_pipe_tflops": 2.0 * tf_gu * tile_rows / rows, "peak_mxf8f6f4_nominal": 4500.0,
+                         "frac_tensor_pipe_nominal": 2.0 * tf_gu * tile_rows / rows / 4500.0} if bs else {})},
         "kernels": {nm: {"launches": c, "avg_us": 1e3 * t / c} for nm, (c, t) in prof.items()},
         "expert_rows": {"max": int(counts.max()), "median": float(counts.float().median()), "min": int(counts.min())},
         "l2": "flushed before every timed step",

@@ -24,11 +24,15 @@
 //      up rows, so SwiGLU runs in the epilogue.
 //   D  fp32, TMEM lanes = token rows, 256 columns.
 //
-// Token rows reach shared memory as tile images built by bsg_quant_rows
-// (x rows) or by the gate/up epilogue (act rows): for the plan's 128-row
-// tile j and 128-K stage s one 33,792-byte block at (j * S + s) * 33,792 -- hi rows (16 KB) and lo rows (16 KB)
-// in the swizzled layout the MMA reads, then the hi and the lo scale atoms --
-// so one bulk copy brings a stage's A operands and their scale factors.
+// Token rows reach shared memory as tile images: for the plan's 128-row
+// tile j and 128-K stage s one 33,792-byte block at (j * S + s) * 33,792 --
+// hi rows (16 KB) and lo rows (16 KB) in the swizzled layout the MMA reads,
+// then the hi and the lo scale atoms -- so one bulk copy brings a stage's A
+// operands and their scale factors.  x rows are quantised once per row
+// (bsg_quant_tokens) and copied into the images of every tile that holds
+// them (bsg_images); the gate/up epilogue writes the act images directly.
+// (Gathering the tile rows inside the GEMM with TMA tile::gather4, 64
+// requests of 4 rows per stage, measured 3x slower than these copies.)
 //
 // One persistent CTA per SM walks the (128-row tile, 256-row weight tile)
 // work list; 12 warps:
@@ -95,58 +99,91 @@ __device__ __forceinline__ int atom_off(int n, int kk) { return (n & 31) * 16 + 
 
 }  // namespace
 
-// x rows (sorted by the plan, 128-row tiles) -> tile images (layout above).
-// A CTA builds one image at a time in shared memory -- thread i quantises
-// two 32-K blocks of tile row i / 2 -- and then writes it with coalesced
-// 16-byte stores; the part rows past the tile's last real row are not
-// written (padding rows are MMA lanes whose results are never stored).
-__global__ void __launch_bounds__(256) bsg_quant_rows_kernel(const uint16_t* __restrict__ x, Plan p, int K,
-                                                             uint8_t* __restrict__ img) {
-  __shared__ __align__(128) uint8_t buf[kImg];
+// x rows -> their hi / lo E4M3 parts and UE8M0 scales: hi, lo [rows][K],
+// shi, slo [rows][K / 32].  One warp per row, one 32-K block per lane step.
+// With `counts` the rows are expert-parallel slots (block r = row / capacity
+// holds counts[r] real rows) and the others are skipped.
+__global__ void __launch_bounds__(256) bsg_quant_tokens_kernel(const uint16_t* __restrict__ x, int rows, int K,
+                                                               const int32_t* __restrict__ counts, int capacity,
+                                                               uint8_t* __restrict__ hi, uint8_t* __restrict__ lo,
+                                                               uint8_t* __restrict__ shi, uint8_t* __restrict__ slo) {
+  const int lane = threadIdx.x & 31;
+  for (int t = blockIdx.x * 8 + (threadIdx.x >> 5); t < rows; t += gridDim.x * 8) {
+    if (counts != nullptr && t % capacity >= counts[t / capacity]) continue;
+    const uint16_t* src = x + int64_t(t) * K;
+    for (int g = lane; g < K / 32; g += 32) {
+      float v[32];
+      const uint4* s4 = reinterpret_cast<const uint4*>(src + g * 32);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 u = __ldg(s4 + q);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = unpack_bf16x2(w[i]);
+          v[8 * q + 2 * i] = f.x;
+          v[8 * q + 2 * i + 1] = f.y;
+        }
+      }
+      uint32_t h[8], l[8], bh, bl;
+      split_block(v, h, l, &bh, &bl);
+      uint4* hd = reinterpret_cast<uint4*>(hi + int64_t(t) * K + g * 32);
+      uint4* ld = reinterpret_cast<uint4*>(lo + int64_t(t) * K + g * 32);
+      hd[0] = make_uint4(h[0], h[1], h[2], h[3]);
+      hd[1] = make_uint4(h[4], h[5], h[6], h[7]);
+      ld[0] = make_uint4(l[0], l[1], l[2], l[3]);
+      ld[1] = make_uint4(l[4], l[5], l[6], l[7]);
+      shi[int64_t(t) * (K / 32) + g] = uint8_t(bh);
+      slo[int64_t(t) * (K / 32) + g] = uint8_t(bl);
+    }
+  }
+}
+
+__device__ __forceinline__ uint4 ld_keep_v4(const void* p, uint64_t policy) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p), "l"(policy));
+  return v;
+}
+
+__device__ __forceinline__ void st_stream_v4(void* p, uint4 v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// Quantised x rows -> the tile images of the sorted rows (plan order, 128-row
+// tiles).  Eight lanes copy one part row: lane c moves 16-byte chunk c of the
+// row's 128 K to its swizzled place, so each group writes a whole 128-byte
+// line; the first lane of the group copies the row's four scale bytes into
+// the atom.  Rows past the tile's last real row are not written (padding
+// rows are MMA lanes whose results are never stored).
+__global__ void __launch_bounds__(256) bsg_images_kernel(Plan p, int K, const uint8_t* __restrict__ hi,
+                                                         const uint8_t* __restrict__ lo,
+                                                         const uint8_t* __restrict__ shi,
+                                                         const uint8_t* __restrict__ slo, uint8_t* __restrict__ img) {
   const int S = K / kBK;
   const int n_img = *p.n_mtiles * S;
-  const int n = threadIdx.x >> 1, hb = threadIdx.x & 1;
+  const int c = threadIdx.x & 7;          // 16-byte chunk of the part row
+  const int g = threadIdx.x >> 3;         // part row group of this pass, 0..31
+  // the quantised rows (read once per expert a token reaches) stay in L2; the
+  // images (written once, read by the GEMM much later) stream past it
+  uint64_t keep;
+  asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(keep));
   for (int q = blockIdx.x; q < n_img; q += gridDim.x) {
     const int j = q / S, s = q - j * S;
     const int e = p.mtiles[2 * j], row0 = p.mtiles[2 * j + 1];
     const int valid = min(kTM, p.offsets[e] + p.counts[e] - row0);  // real rows of the tile
-    const int t = n < valid ? p.row_token[row0 + n] : -1;
-#pragma unroll
-    for (int b = 0; b < 2; ++b) {
-      const int kk = 2 * hb + b;
-      uint32_t hi[8] = {}, lo[8] = {}, bh = 127, bl = 127;
-      if (t >= 0) {
-        float v[32];
-        const uint4* s4 = reinterpret_cast<const uint4*>(x + int64_t(t) * K + s * kBK + kk * 32);
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const uint4 u = __ldg(s4 + q4);
-          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float2 f = unpack_bf16x2(w[i]);
-            v[8 * q4 + 2 * i] = f.x;
-            v[8 * q4 + 2 * i + 1] = f.y;
-          }
-        }
-        split_block(v, hi, lo, &bh, &bl);
-      }
-      *reinterpret_cast<uint4*>(buf + image_off(n, 2 * kk)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-      *reinterpret_cast<uint4*>(buf + image_off(n, 2 * kk + 1)) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
-      *reinterpret_cast<uint4*>(buf + kPart + image_off(n, 2 * kk)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-      *reinterpret_cast<uint4*>(buf + kPart + image_off(n, 2 * kk + 1)) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
-      buf[2 * kPart + atom_off(n, kk)] = uint8_t(bh);
-      buf[2 * kPart + kAtom + atom_off(n, kk)] = uint8_t(bl);
+    uint8_t* dst = img + int64_t(q) * kImg;
+    for (int pr = g; pr < 2 * valid; pr += 32) {
+      const int n = pr >> 1, part = pr & 1;
+      const int t = __ldg(p.row_token + row0 + n);
+      const uint8_t* src = (part ? lo : hi) + int64_t(t) * K + s * kBK + c * 16;
+      st_stream_v4(dst + part * kPart + image_off(n, c), ld_keep_v4(src, keep));
+      if (c == 0)
+        *reinterpret_cast<uint32_t*>(dst + 2 * kPart + part * kAtom + atom_off(n, 0)) =
+            __ldg(reinterpret_cast<const uint32_t*>((part ? slo : shi) + int64_t(t) * (K / 32) + s * 4));
     }
-    __syncthreads();
-    uint4* dst = reinterpret_cast<uint4*>(img + int64_t(q) * kImg);
-    const uint4* src = reinterpret_cast<const uint4*>(buf);
-    const int part16 = valid * 8;  // 16-byte words of a part's real rows
-    for (int i = threadIdx.x; i < kImg / 16; i += blockDim.x) {
-      const int in_part = i % (kPart / 16);
-      if (i >= 2 * (kPart / 16) || in_part < part16) dst[i] = src[i];
-    }
-    __syncthreads();
   }
 }
 
@@ -373,11 +410,12 @@ __global__ void __launch_bounds__(kThreads, 1) bsg_kernel(const __grid_constant_
       } else {
         const int row = row0 + r;
         const int col = nt * kTN + half * 128;
-        uint16_t* dst = a.routed + int64_t(row) * a.H + col;
-        if (a.ret.rows[0] != nullptr) {  // expert-parallel owner: straight into the sender's back block
-          const int slot = a.plan.row_token[row];
-          dst = slot < 0 ? nullptr : a.ret.rows[slot / a.ret.capacity] + int64_t(slot % a.ret.capacity) * a.H + col;
-        }
+        // padding rows (row_token < 0) are not stored; with ret set (expert-parallel
+        // owner) the rows go straight into the senders' back blocks
+        const int slot = a.plan.row_token[row];
+        uint16_t* dst = slot < 0 ? nullptr : a.routed + int64_t(row) * a.H + col;
+        if (a.ret.rows[0] != nullptr && slot >= 0)
+          dst = a.ret.rows[slot / a.ret.capacity] + int64_t(slot % a.ret.capacity) * a.H + col;
         if (dst != nullptr) {
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
@@ -411,8 +449,14 @@ void bsg_init_attributes() {
 
 size_t bsg_image_bytes(int64_t mtiles, int K) { return size_t(mtiles) * size_t(K / kBK) * kImg; }
 
-void launch_bsg_quant_rows(const uint16_t* x, const Plan& p, int K, uint8_t* img, int num_sms, cudaStream_t stream) {
-  bsg_quant_rows_kernel<<<num_sms * 6, 256, 0, stream>>>(x, p, K, img);
+void launch_bsg_quant_tokens(const uint16_t* x, int rows, int K, const int32_t* counts, int capacity, uint8_t* hi,
+                             uint8_t* lo, uint8_t* shi, uint8_t* slo, int num_sms, cudaStream_t stream) {
+  bsg_quant_tokens_kernel<<<num_sms * 8, 256, 0, stream>>>(x, rows, K, counts, capacity, hi, lo, shi, slo);
+}
+
+void launch_bsg_images(const Plan& p, int K, const uint8_t* hi, const uint8_t* lo, const uint8_t* shi,
+                       const uint8_t* slo, uint8_t* img, int num_sms, cudaStream_t stream) {
+  bsg_images_kernel<<<num_sms * 8, 256, 0, stream>>>(p, K, hi, lo, shi, slo, img);
 }
 
 void launch_bsg(const BsArgs& a, int kind, const void* const* maps, int num_sms, cudaStream_t stream) {

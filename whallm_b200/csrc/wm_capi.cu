@@ -37,6 +37,8 @@ struct wm_ctx {
   float* actscale = nullptr;   // [rows] prescale of the f16 act rows (decode path)
   uint32_t* rowmax = nullptr;  // [rows] per-row |act| maxima (decode path)
   uint16_t* xn = nullptr;      // [T, H] normalised input rows (pre-MoE RMSNorm)
+  uint8_t* xq = nullptr;       // block-scaled GEMM: hi / lo E4M3 parts and UE8M0 scales of the x rows
+  size_t xq_bytes = 0;
   uint8_t* bs_img_x = nullptr;    // block-scaled decode / GEMM: token tile images (hi / lo E4M3 + scale atoms)
   uint8_t* bs_img_act = nullptr;  // ... and the act tile images
   int max_rows = 0, max_mtiles = 0, max_chunks = 0;
@@ -509,11 +511,20 @@ int run_bs_decode(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wt
   return check_launch(ctx, "block-scaled expert decode");
 }
 
-// The block-scaled grouped GEMM path: hi / lo E4M3 tile images of the x
-// rows, gate/up (+SwiGLU, act tile images), down.  The plan's groups are
-// padded to 128 rows.
+// The x rows a call's plan may reference: rows [0, rows); with counts, rows
+// are expert-parallel slots and block r = row / capacity holds counts[r].
+struct XRows {
+  int64_t rows;
+  const int32_t* counts;
+  int capacity;
+};
+
+// The block-scaled grouped GEMM path: every x row quantised once (hi / lo
+// E4M3 + UE8M0 scales) and copied into the tile images of the sorted rows,
+// gate/up (+SwiGLU, act tile images), down.  The plan's groups are padded to
+// 128 rows.
 int run_bs_gemm(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts, bool has_shared, cudaStream_t s,
-                const wm::EpReturn* ret) {
+                const wm::EpReturn* ret, const XRows& xr) {
   const int H = a->H, I = a->I;
   CUtensorMap w13, w13s, w2, w2s, s13, s13s, s2, s2s;
   bool ok = encode_fp4_weights(ctx, &w13, a->w13.weight, H, 2 * I, a->E, a->w13.weight_stride, 64, 2) &&
@@ -525,7 +536,15 @@ int run_bs_gemm(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts,
          encode_fp4_weights(ctx, &w2s, a->shared_w2.weight, I, H, 1, 0, 128, 1) &&
          encode_scale_rows(ctx, &s13s, a->shared_w13.scale, H / 32, 2 * I, 1, 0, 64, 2) &&
          encode_scale_rows(ctx, &s2s, a->shared_w2.scale, I / 32, H, 1, 0, 128, 1);
-  if (!ok) return fail(ctx, "cuTensorMapEncodeTiled failed for the block-scaled expert operands");
+  // per-row parts: hi [rows][H], lo [rows][H], then their scale rows [rows][H / 32]
+  const int64_t rows = xr.rows;
+  auto up256 = [](size_t v) { return (v + 255) & ~size_t(255); };
+  uint8_t* xh = ctx->xq;
+  uint8_t* xl = xh + up256(size_t(rows) * H);
+  uint8_t* xsh = xl + up256(size_t(rows) * H);
+  uint8_t* xsl = xsh + up256(size_t(rows) * (H / 32));
+  if (size_t(xsl + size_t(rows) * (H / 32) - xh) > ctx->xq_bytes)
+    return fail(ctx, "%lld x rows of H = %d exceed the quantised-row workspace", (long long)rows, H);
   wm::BsArgs b{};
   b.plan = ctx->plan;
   b.wts = wts;
@@ -537,7 +556,9 @@ int run_bs_gemm(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts,
   b.act_img = ctx->bs_img_act;
   b.routed = ctx->routed;
   wm::prof_begin(&ctx->prof, wm::kProfGather, s);
-  wm::launch_bsg_quant_rows(static_cast<const uint16_t*>(a->x), b.plan, H, ctx->bs_img_x, ctx->num_sms, s);
+  wm::launch_bsg_quant_tokens(static_cast<const uint16_t*>(a->x), int(rows), H, xr.counts, xr.capacity, xh, xl, xsh,
+                              xsl, ctx->num_sms, s);
+  wm::launch_bsg_images(b.plan, H, xh, xl, xsh, xsl, ctx->bs_img_x, ctx->num_sms, s);
   wm::prof_end(&ctx->prof, wm::kProfGather, s);
   b.img = ctx->bs_img_x;
   wm::prof_begin(&ctx->prof, wm::kProfGemmGateUp, s);
@@ -550,7 +571,7 @@ int run_bs_gemm(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts,
   const void* maps1[4] = {&w2, has_shared ? &w2s : &w2, &s2, has_shared ? &s2s : &s2};
   wm::launch_bsg(b, 1, maps1, ctx->num_sms, s);
   wm::prof_end(&ctx->prof, wm::kProfGemmDown, s);
-  ctx->counters.launches += 3;
+  ctx->counters.launches += 4;
   ctx->counters.gemm_calls += 1;
   ctx->counters.bs_gemm_calls += 1;
   return check_launch(ctx, "block-scaled expert GEMM");
@@ -560,12 +581,12 @@ int run_bs_gemm(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts,
 // with `ret`, the down rows stored straight into the senders' back blocks:
 // the grouped GEMMs and the block-scaled decode path only).
 int run_experts(wm_ctx* ctx, const wm_moe_args* a, bool has_shared, Path path, cudaStream_t s,
-                const wm::EpReturn* ret = nullptr) {
+                const wm::EpReturn* ret = nullptr, const XRows* xr = nullptr) {
   const wm::ExpertWeights wts = weights_of(a, has_shared);
   const int gate_first = a->layout == WM_LAYOUT_QWEN_GATE_UP_MXFP4 ? 1 : 0;
   if (path == kPathDecodeMma) return run_decode_mma(ctx, a, wts, s);
   if (path == kPathBsDecode) return run_bs_decode(ctx, a, wts, has_shared, s, ret);
-  if (path == kPathBsGemm) return run_bs_gemm(ctx, a, wts, has_shared, s, ret);
+  if (path == kPathBsGemm) return run_bs_gemm(ctx, a, wts, has_shared, s, ret, xr ? *xr : XRows{a->T, nullptr, 0});
   if (path == kPathGemv) {
     wm::GemvArgs g{};
     g.plan = ctx->plan;
@@ -710,7 +731,7 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
                o_act = take(rows * I * 2), o_routed = take(rows * H * 2), o_logits = take(T * E * 4),
                o_idx = take(T * K * 4), o_w = take(T * K * 4), o_sg = take(T * 4), o_status = take(16),
                o_act16 = take(rows * I * 2), o_rowscale = take(rows * 4), o_actscale = take(rows * 4),
-               o_rowmax = take(rows * 4), o_xn = take(T * H * 2),
+               o_rowmax = take(rows * 4), o_xn = take(T * H * 2), o_xq = take(T * H * 2 + T * (H / 32 + 1) * 2 + 1024),
                // tile images: the decode kernel's 16-row tiles or the GEMM's 128-row tiles
                o_imgx = take(std::max<size_t>(rows * H * 9 / 4, wm::bsg_image_bytes(rows / wm::kTileM + 2, int(H)))),
                o_imga = take(std::max<size_t>(rows * I * 9 / 4, wm::bsg_image_bytes(rows / wm::kTileM + 2, int(I))));
@@ -746,6 +767,8 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
   ctx->actscale = reinterpret_cast<float*>(base + o_actscale);
   ctx->rowmax = reinterpret_cast<uint32_t*>(base + o_rowmax);
   ctx->xn = reinterpret_cast<uint16_t*>(base + o_xn);
+  ctx->xq = base + o_xq;
+  ctx->xq_bytes = size_t(T * H * 2 + T * (H / 32 + 1) * 2 + 1024);
   ctx->bs_img_x = base + o_imgx;
   ctx->bs_img_act = base + o_imga;
   // the whole workspace starts at zero (status word included); padding rows of
@@ -1225,7 +1248,8 @@ WM_EXPORT int wm_ep_experts(wm_ctx* ctx, wm_ep* ep, const wm_moe_args* args, voi
     for (int r = 0; r < ep->world; ++r) ret.rows[r] = back.rows[r];
     ret.capacity = int(ep->capacity);
   }
-  if (int rc = run_experts(ctx, &b, false, path, s, fused ? &ret : nullptr)) return rc;
+  const XRows xr{slots, counts, int(ep->capacity)};  // the x rows are the recv slots
+  if (int rc = run_experts(ctx, &b, false, path, s, fused ? &ret : nullptr, &xr)) return rc;
   wm::prof_begin(&ctx->prof, wm::kProfEpReturn, s);
   if (fused)
     wm::launch_ep_signal(back, ep->world, s);
