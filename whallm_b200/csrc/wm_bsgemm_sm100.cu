@@ -24,21 +24,27 @@
 //      up rows, so SwiGLU runs in the epilogue.
 //   D  fp32, TMEM lanes = token rows, 256 columns.
 //
-// Token rows reach shared memory as tile images: for the plan's 128-row
-// tile j and 128-K stage s one 33,792-byte block at (j * S + s) * 33,792 --
-// hi rows (16 KB) and lo rows (16 KB) in the swizzled layout the MMA reads,
-// then the hi and the lo scale atoms -- so one bulk copy brings a stage's A
-// operands and their scale factors.  x rows are quantised once per row
-// (bsg_quant_tokens) and copied into the images of every tile that holds
-// them (bsg_images); the gate/up epilogue writes the act images directly.
-// (Gathering the tile rows inside the GEMM with TMA tile::gather4, 64
-// requests of 4 rows per stage, measured 3x slower than these copies.)
+// Token rows reach shared memory two ways.  Gate/up: bsg_quant_scatter
+// quantises each x row once and writes its parts to every sorted row that
+// holds it (hi, lo [rows][H] E4M3, shi, slo [rows][H / 32] UE8M0, plan
+// order), and the producer loads a stage's 128 x 128-byte hi and lo tiles by
+// TMA (128-byte swizzle) and, every fourth stage, the rows' scale bytes for
+// the scale warp, which builds the A scale atoms beside the weight atoms.
+// Down: the gate/up epilogue writes act tile images -- for the plan's
+// 128-row tile j and 128-K stage s one 33,792-byte block at (j * S + s) *
+// 33,792: hi rows (16 KB) and lo rows (16 KB) in the swizzled layout, then
+// the hi and the lo scale atoms -- and one bulk copy brings a stage's A
+// operands and scale factors.  (Measured and dropped: gathering the x rows
+// inside the GEMM with TMA tile::gather4, 64 requests of 4 rows per stage,
+// 3x slower; quantising per row and copying into images, 250 us against
+// ~150 for the scatter at config 2.)
 //
 // One persistent CTA per SM walks the (128-row tile, 256-row weight tile)
 // work list; 12 warps:
-//   warp 0      TMA producer: per stage the tile image and two weight boxes;
-//               every fourth stage the raw E8M0 rows of the next four
-//   warp 1      scale warp: raw E8M0 rows -> the stage's two weight atoms
+//   warp 0      TMA producer: per stage the token rows (two tiles, or the
+//               act image) and two weight boxes; every fourth stage the raw
+//               scale rows of the next four stages
+//   warp 1      scale warp: raw scale rows -> the stage's scale atoms
 //   warp 2      TMEM owner and MMA issuer (one elected lane, warp-wide)
 //   warps 4-11  epilogue: lane quarter warp % 4, column half (warp - 4) / 4;
 //               each thread loads its 128 columns into registers and frees
@@ -66,12 +72,16 @@ constexpr int kBBytes = kTN * kBK;             // 256 weight rows, unpacked
 constexpr uint32_t kBTx = kTN * kBK / 2;       // their packed bytes (TMA transaction count)
 constexpr int kStageBytes = kImg + kBBytes + 2 * kAtom;
 constexpr int kRawSlots = 2;
-constexpr int kRawBytes = kTN * 16;            // 256 rows x 16 E8M0 bytes (four stages)
+constexpr int kRawW = kTN * 16;                // 256 weight rows x 16 E8M0 bytes (four stages)
+constexpr int kRawX = 2 * kTM * 16;            // gate/up: 128 token rows x 16 bytes, hi then lo
+constexpr int kRawBytes = kRawW + kRawX;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSfCol0 = kTN;              // scale factors after the accumulator
 constexpr uint32_t kSfStage = 16;              // SFA hi 4, SFA lo 4, SFB 8 columns
 static_assert(kSfCol0 + kSfStage * kStages <= kTmemCols, "scale factors exceed the TMEM allocation");
 static_assert(kImg % 1024 == 0 && kStageBytes % 1024 == 0, "swizzled operands need 1024-byte alignment");
+static_assert(kPart % 128 == 0 && kRawW % 128 == 0 && kRawX % 256 == 0 && kRawBytes % 128 == 0,
+              "every TMA destination in shared memory must be 128-byte aligned");
 
 struct GShared {
   uint64_t full[kStages];
@@ -86,6 +96,7 @@ struct GShared {
 };
 
 constexpr size_t kSmemBytes = size_t(kStages) * kStageBytes + size_t(kRawSlots) * kRawBytes + sizeof(GShared) + 1024;
+static_assert(kSmemBytes <= 232448, "more shared memory than a B200 CTA may have");
 
 // kind::mxf8f6f4 instruction descriptor: A E4M3, B E2M1, both K-major, UE8M0
 // scales, M = 128, N = 256, scale-factor ids kk for A and B.
@@ -99,90 +110,70 @@ __device__ __forceinline__ int atom_off(int n, int kk) { return (n & 31) * 16 + 
 
 }  // namespace
 
-// x rows -> their hi / lo E4M3 parts and UE8M0 scales: hi, lo [rows][K],
-// shi, slo [rows][K / 32].  One warp per row, one 32-K block per lane step.
-// With `counts` the rows are expert-parallel slots (block r = row / capacity
-// holds counts[r] real rows) and the others are skipped.
-__global__ void __launch_bounds__(256) bsg_quant_tokens_kernel(const uint16_t* __restrict__ x, int rows, int K,
-                                                               const int32_t* __restrict__ counts, int capacity,
-                                                               uint8_t* __restrict__ hi, uint8_t* __restrict__ lo,
-                                                               uint8_t* __restrict__ shi, uint8_t* __restrict__ slo) {
+// x rows -> their hi / lo E4M3 parts and UE8M0 scales, written to every
+// sorted row that holds them: hi, lo [rows][K], shi, slo [rows][K / 32] in
+// plan order.  Source row t goes to rows pair_pos[t * topk + k] (k < topk;
+// none when < 0) and, with has_shared, offsets[E] + t.  With `counts` the
+// source rows are expert-parallel slots (block r = t / capacity holds
+// counts[r]) and the others are skipped.  One warp per source row; per pass
+// each lane splits two 32-K blocks once and stores them to every destination
+// (a warp writes 1 KB of a row per store, coalesced).
+__global__ void __launch_bounds__(256) bsg_quant_scatter_kernel(const uint16_t* __restrict__ x, int rows, int K,
+                                                                Plan p, int topk, int has_shared, int E,
+                                                                const int32_t* __restrict__ counts, int capacity,
+                                                                uint8_t* __restrict__ hi, uint8_t* __restrict__ lo,
+                                                                uint8_t* __restrict__ shi, uint8_t* __restrict__ slo) {
   const int lane = threadIdx.x & 31;
+  const int nblk = K / 32;
   for (int t = blockIdx.x * 8 + (threadIdx.x >> 5); t < rows; t += gridDim.x * 8) {
     if (counts != nullptr && t % capacity >= counts[t / capacity]) continue;
+    // destination rows: lane j holds pair_pos[t * topk + j] and [.. + 32 + j]
+    const int pp0 = lane < topk ? p.pair_pos[int64_t(t) * topk + lane] : -1;
+    const int pp1 = lane + 32 < topk ? p.pair_pos[int64_t(t) * topk + 32 + lane] : -1;
+    const int ndst = topk + (has_shared ? 1 : 0);
+    const int shared_row = has_shared ? p.offsets[E] + t : -1;
     const uint16_t* src = x + int64_t(t) * K;
-    for (int g = lane; g < K / 32; g += 32) {
-      float v[32];
-      const uint4* s4 = reinterpret_cast<const uint4*>(src + g * 32);
+    for (int g0 = 0; g0 < nblk; g0 += 64) {
+      uint32_t h[2][8], l[2][8], bh[2], bl[2];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint4 u = __ldg(s4 + q);
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+      for (int j = 0; j < 2; ++j) {
+        const int g = g0 + 32 * j + lane;
+        if (g < nblk) {
+          float v[32];
+          const uint4* s4 = reinterpret_cast<const uint4*>(src + g * 32);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = unpack_bf16x2(w[i]);
-          v[8 * q + 2 * i] = f.x;
-          v[8 * q + 2 * i + 1] = f.y;
+          for (int q = 0; q < 4; ++q) {
+            const uint4 u = __ldg(s4 + q);
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float2 f = unpack_bf16x2(w[i]);
+              v[8 * q + 2 * i] = f.x;
+              v[8 * q + 2 * i + 1] = f.y;
+            }
+          }
+          split_block(v, h[j], l[j], &bh[j], &bl[j]);
         }
       }
-      uint32_t h[8], l[8], bh, bl;
-      split_block(v, h, l, &bh, &bl);
-      uint4* hd = reinterpret_cast<uint4*>(hi + int64_t(t) * K + g * 32);
-      uint4* ld = reinterpret_cast<uint4*>(lo + int64_t(t) * K + g * 32);
-      hd[0] = make_uint4(h[0], h[1], h[2], h[3]);
-      hd[1] = make_uint4(h[4], h[5], h[6], h[7]);
-      ld[0] = make_uint4(l[0], l[1], l[2], l[3]);
-      ld[1] = make_uint4(l[4], l[5], l[6], l[7]);
-      shi[int64_t(t) * (K / 32) + g] = uint8_t(bh);
-      slo[int64_t(t) * (K / 32) + g] = uint8_t(bl);
-    }
-  }
-}
-
-__device__ __forceinline__ uint4 ld_keep_v4(const void* p, uint64_t policy) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p), "l"(policy));
-  return v;
-}
-
-__device__ __forceinline__ void st_stream_v4(void* p, uint4 v) {
-  asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-               : "memory");
-}
-
-// Quantised x rows -> the tile images of the sorted rows (plan order, 128-row
-// tiles).  Eight lanes copy one part row: lane c moves 16-byte chunk c of the
-// row's 128 K to its swizzled place, so each group writes a whole 128-byte
-// line; the first lane of the group copies the row's four scale bytes into
-// the atom.  Rows past the tile's last real row are not written (padding
-// rows are MMA lanes whose results are never stored).
-__global__ void __launch_bounds__(256) bsg_images_kernel(Plan p, int K, const uint8_t* __restrict__ hi,
-                                                         const uint8_t* __restrict__ lo,
-                                                         const uint8_t* __restrict__ shi,
-                                                         const uint8_t* __restrict__ slo, uint8_t* __restrict__ img) {
-  const int S = K / kBK;
-  const int n_img = *p.n_mtiles * S;
-  const int c = threadIdx.x & 7;          // 16-byte chunk of the part row
-  const int g = threadIdx.x >> 3;         // part row group of this pass, 0..31
-  // the quantised rows (read once per expert a token reaches) stay in L2; the
-  // images (written once, read by the GEMM much later) stream past it
-  uint64_t keep;
-  asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(keep));
-  for (int q = blockIdx.x; q < n_img; q += gridDim.x) {
-    const int j = q / S, s = q - j * S;
-    const int e = p.mtiles[2 * j], row0 = p.mtiles[2 * j + 1];
-    const int valid = min(kTM, p.offsets[e] + p.counts[e] - row0);  // real rows of the tile
-    uint8_t* dst = img + int64_t(q) * kImg;
-    for (int pr = g; pr < 2 * valid; pr += 32) {
-      const int n = pr >> 1, part = pr & 1;
-      const int t = __ldg(p.row_token + row0 + n);
-      const uint8_t* src = (part ? lo : hi) + int64_t(t) * K + s * kBK + c * 16;
-      st_stream_v4(dst + part * kPart + image_off(n, c), ld_keep_v4(src, keep));
-      if (c == 0)
-        *reinterpret_cast<uint32_t*>(dst + 2 * kPart + part * kAtom + atom_off(n, 0)) =
-            __ldg(reinterpret_cast<const uint32_t*>((part ? slo : shi) + int64_t(t) * (K / 32) + s * 4));
+      for (int k = 0; k < ndst; ++k) {
+        const int rk = __shfl_sync(0xffffffffu, k < 32 ? pp0 : pp1, k & 31);
+        const int r = k < topk ? rk : shared_row;
+        if (r < 0) continue;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int g = g0 + 32 * j + lane;
+          if (g < nblk) {
+            uint4* hd = reinterpret_cast<uint4*>(hi + int64_t(r) * K + g * 32);
+            uint4* ld = reinterpret_cast<uint4*>(lo + int64_t(r) * K + g * 32);
+            hd[0] = make_uint4(h[j][0], h[j][1], h[j][2], h[j][3]);
+            hd[1] = make_uint4(h[j][4], h[j][5], h[j][6], h[j][7]);
+            ld[0] = make_uint4(l[j][0], l[j][1], l[j][2], l[j][3]);
+            ld[1] = make_uint4(l[j][4], l[j][5], l[j][6], l[j][7]);
+            shi[int64_t(r) * nblk + g] = uint8_t(bh[j]);
+            slo[int64_t(r) * nblk + g] = uint8_t(bl[j]);
+          }
+        }
+      }
     }
   }
 }
@@ -195,6 +186,10 @@ __global__ void __launch_bounds__(kThreads, 1) bsg_kernel(const __grid_constant_
                                                           const __grid_constant__ CUtensorMap tm_ws,
                                                           const __grid_constant__ CUtensorMap tm_s,
                                                           const __grid_constant__ CUtensorMap tm_ss,
+                                                          const __grid_constant__ CUtensorMap tm_xh,
+                                                          const __grid_constant__ CUtensorMap tm_xl,
+                                                          const __grid_constant__ CUtensorMap tm_xsh,
+                                                          const __grid_constant__ CUtensorMap tm_xsl,
                                                           const BsArgs a) {
   extern __shared__ uint8_t smem_raw[];
   const int K = KIND == 0 ? a.H : a.I;
@@ -244,32 +239,44 @@ __global__ void __launch_bounds__(kThreads, 1) bsg_kernel(const __grid_constant_
     if (lane == 0) {
       tma_prefetch_desc(&tm_w);
       tma_prefetch_desc(&tm_s);
+      if (KIND == 0) {
+        tma_prefetch_desc(&tm_xh);
+        tma_prefetch_desc(&tm_xsh);
+      }
       int st = 0, ph = 0, rs = 0, rph = 0;
       for (int q = blockIdx.x; q < n_items && !*abort; q += gridDim.x) {
         const int tile = q / n_nt, nt = q - tile * n_nt;
-        const int e = a.plan.mtiles[2 * tile];
+        const int e = a.plan.mtiles[2 * tile], row0 = a.plan.mtiles[2 * tile + 1];
         const bool shared_e = e == a.wts.E;
         const void* mw = shared_e ? &tm_ws : &tm_w;
         const void* ms = shared_e ? &tm_ss : &tm_s;
         const int ez = shared_e ? 0 : e;
-        const uint8_t* src = a.img + int64_t(tile) * S * kImg;  // image (tile, s) at (tile * S + s) * kImg
+        const uint8_t* src = a.img + int64_t(tile) * S * kImg;  // down: image (tile, s) at (tile * S + s) * kImg
         for (int s = 0; s < S; ++s) {
           if ((s & 3) == 0) {
             if (!mbar_wait(&sh.raw_empty[rs], rph ^ 1, abort)) { fail(90 + KIND); break; }
             const uint32_t dst = raw_base + rs * kRawBytes;
-            mbar_arrive_expect_tx(&sh.raw_full[rs], kRawBytes);
+            mbar_arrive_expect_tx(&sh.raw_full[rs], KIND == 0 ? uint32_t(kRawBytes) : uint32_t(kRawW));
             if (KIND == 0) {  // tile rows 0..127: E8M0 rows nt * 128 .. + 63 of both halves; 128..255: the next 64
               tma_load_4d(dst, ms, 16 * (s >> 2), nt * 128, 0, ez, &sh.raw_full[rs]);
-              tma_load_4d(dst + kRawBytes / 2, ms, 16 * (s >> 2), nt * 128 + 64, 0, ez, &sh.raw_full[rs]);
+              tma_load_4d(dst + kRawW / 2, ms, 16 * (s >> 2), nt * 128 + 64, 0, ez, &sh.raw_full[rs]);
+              // the token rows' scale bytes, hi then lo
+              tma_load_2d_s(dst + kRawW, &tm_xsh, 16 * (s >> 2), row0, &sh.raw_full[rs]);
+              tma_load_2d_s(dst + kRawW + kRawX / 2, &tm_xsl, 16 * (s >> 2), row0, &sh.raw_full[rs]);
             } else {
               tma_load_3d(dst, ms, 16 * (s >> 2), nt * kTN, ez, &sh.raw_full[rs]);
-              tma_load_3d(dst + kRawBytes / 2, ms, 16 * (s >> 2), nt * kTN + 128, ez, &sh.raw_full[rs]);
+              tma_load_3d(dst + kRawW / 2, ms, 16 * (s >> 2), nt * kTN + 128, ez, &sh.raw_full[rs]);
             }
             if (++rs == kRawSlots) { rs = 0; rph ^= 1; }
           }
           if (!mbar_wait(&sh.empty[st], ph ^ 1, abort)) { fail(92 + KIND); break; }
-          mbar_arrive_expect_tx(&sh.full[st], uint32_t(kImg) + kBTx);
-          bulk_g2s(img_addr(st), src + int64_t(s) * kImg, uint32_t(kImg), &sh.full[st]);
+          mbar_arrive_expect_tx(&sh.full[st], (KIND == 0 ? uint32_t(2 * kPart) : uint32_t(kImg)) + kBTx);
+          if (KIND == 0) {  // the tile's hi and lo rows of this stage's 128 K
+            tma_load_2d_s(img_addr(st), &tm_xh, s * kBK, row0, &sh.full[st]);
+            tma_load_2d_s(img_addr(st) + kPart, &tm_xl, s * kBK, row0, &sh.full[st]);
+          } else {
+            bulk_g2s(img_addr(st), src + int64_t(s) * kImg, uint32_t(kImg), &sh.full[st]);
+          }
           if (KIND == 0) {
             tma_load_4d(b_addr(st), mw, s * kBK, nt * 128, 0, ez, &sh.full[st]);
             tma_load_4d(b_addr(st) + kBBytes / 2, mw, s * kBK, nt * 128 + 64, 0, ez, &sh.full[st]);
@@ -297,6 +304,17 @@ __global__ void __launch_bounds__(kThreads, 1) bsg_kernel(const __grid_constant_
           const uint32_t w0 = lds_b32(rb + (128 * h + lane) * 16), w1 = lds_b32(rb + (128 * h + lane + 32) * 16),
                          w2 = lds_b32(rb + (128 * h + lane + 64) * 16), w3 = lds_b32(rb + (128 * h + lane + 96) * 16);
           sts_v4(sfb_addr(st) + h * kAtom + lane * 16, w0, w1, w2, w3);
+        }
+        if (KIND == 0) {  // the token rows' scale bytes: hi atom, lo atom (the down images carry theirs)
+          const uint32_t rx = raw_base + rs * kRawBytes + kRawW + 4 * (s & 3);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t w0 = lds_b32(rx + h * (kRawX / 2) + lane * 16),
+                           w1 = lds_b32(rx + h * (kRawX / 2) + (lane + 32) * 16),
+                           w2 = lds_b32(rx + h * (kRawX / 2) + (lane + 64) * 16),
+                           w3 = lds_b32(rx + h * (kRawX / 2) + (lane + 96) * 16);
+            sts_v4(img_addr(st) + 2 * kPart + h * kAtom + lane * 16, w0, w1, w2, w3);
+          }
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -449,25 +467,22 @@ void bsg_init_attributes() {
 
 size_t bsg_image_bytes(int64_t mtiles, int K) { return size_t(mtiles) * size_t(K / kBK) * kImg; }
 
-void launch_bsg_quant_tokens(const uint16_t* x, int rows, int K, const int32_t* counts, int capacity, uint8_t* hi,
-                             uint8_t* lo, uint8_t* shi, uint8_t* slo, int num_sms, cudaStream_t stream) {
-  bsg_quant_tokens_kernel<<<num_sms * 8, 256, 0, stream>>>(x, rows, K, counts, capacity, hi, lo, shi, slo);
-}
-
-void launch_bsg_images(const Plan& p, int K, const uint8_t* hi, const uint8_t* lo, const uint8_t* shi,
-                       const uint8_t* slo, uint8_t* img, int num_sms, cudaStream_t stream) {
-  bsg_images_kernel<<<num_sms * 8, 256, 0, stream>>>(p, K, hi, lo, shi, slo, img);
+void launch_bsg_quant_scatter(const uint16_t* x, int rows, int K, const Plan& p, int topk, bool has_shared, int E,
+                               const int32_t* counts, int capacity, uint8_t* hi, uint8_t* lo, uint8_t* shi,
+                               uint8_t* slo, int num_sms, cudaStream_t stream) {
+  bsg_quant_scatter_kernel<<<num_sms * 8, 256, 0, stream>>>(x, rows, K, p, topk, has_shared ? 1 : 0, E, counts,
+                                                            capacity, hi, lo, shi, slo);
 }
 
 void launch_bsg(const BsArgs& a, int kind, const void* const* maps, int num_sms, cudaStream_t stream) {
-  const CUtensorMap* m = static_cast<const CUtensorMap*>(maps[0]);
-  const CUtensorMap* ms = static_cast<const CUtensorMap*>(maps[1]);
-  const CUtensorMap* s = static_cast<const CUtensorMap*>(maps[2]);
-  const CUtensorMap* ss = static_cast<const CUtensorMap*>(maps[3]);
+  const CUtensorMap* m[8];
+  for (int i = 0; i < 8; ++i) m[i] = static_cast<const CUtensorMap*>(maps[kind == 0 || i < 4 ? i : 0]);
   if (kind == 0)
-    bsg_kernel<0><<<num_sms, kThreads, kSmemBytes, stream>>>(*m, *ms, *s, *ss, a);
+    bsg_kernel<0><<<num_sms, kThreads, kSmemBytes, stream>>>(*m[0], *m[1], *m[2], *m[3], *m[4], *m[5], *m[6], *m[7],
+                                                             a);
   else
-    bsg_kernel<1><<<num_sms, kThreads, kSmemBytes, stream>>>(*m, *ms, *s, *ss, a);
+    bsg_kernel<1><<<num_sms, kThreads, kSmemBytes, stream>>>(*m[0], *m[1], *m[2], *m[3], *m[4], *m[5], *m[6], *m[7],
+                                                             a);
 }
 
 }  // namespace wm

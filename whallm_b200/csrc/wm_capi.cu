@@ -37,8 +37,7 @@ struct wm_ctx {
   float* actscale = nullptr;   // [rows] prescale of the f16 act rows (decode path)
   uint32_t* rowmax = nullptr;  // [rows] per-row |act| maxima (decode path)
   uint16_t* xn = nullptr;      // [T, H] normalised input rows (pre-MoE RMSNorm)
-  uint8_t* xq = nullptr;       // block-scaled GEMM: hi / lo E4M3 parts and UE8M0 scales of the x rows
-  size_t xq_bytes = 0;
+  uint8_t* xss = nullptr;      // block-scaled GEMM: the sorted x rows' UE8M0 scale rows (hi, lo)
   uint8_t* bs_img_x = nullptr;    // block-scaled decode / GEMM: token tile images (hi / lo E4M3 + scale atoms)
   uint8_t* bs_img_act = nullptr;  // ... and the act tile images
   int max_rows = 0, max_mtiles = 0, max_chunks = 0;
@@ -519,10 +518,23 @@ struct XRows {
   int capacity;
 };
 
+// 2-D uint8 map [rows][cols] with boxes of box_cols x box_rows.
+bool encode_bytes_2d(wm_ctx* ctx, CUtensorMap* map, const void* base, int64_t cols, int64_t rows, int box_cols,
+                     int box_rows, CUtensorMapSwizzle swizzle) {
+  if (ctx->encode_tiled == nullptr) return false;
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(cols)};
+  cuuint32_t box[2] = {cuuint32_t(box_cols), cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  return ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // The block-scaled grouped GEMM path: every x row quantised once (hi / lo
-// E4M3 + UE8M0 scales) and copied into the tile images of the sorted rows,
-// gate/up (+SwiGLU, act tile images), down.  The plan's groups are padded to
-// 128 rows.
+// E4M3 + UE8M0 scales) and written to each sorted row that holds it, gate/up
+// (+SwiGLU, act tile images), down.  The plan's groups are padded to 128
+// rows.
 int run_bs_gemm(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts, bool has_shared, cudaStream_t s,
                 const wm::EpReturn* ret, const XRows& xr) {
   const int H = a->H, I = a->I;
@@ -536,15 +548,18 @@ int run_bs_gemm(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts,
          encode_fp4_weights(ctx, &w2s, a->shared_w2.weight, I, H, 1, 0, 128, 1) &&
          encode_scale_rows(ctx, &s13s, a->shared_w13.scale, H / 32, 2 * I, 1, 0, 64, 2) &&
          encode_scale_rows(ctx, &s2s, a->shared_w2.scale, I / 32, H, 1, 0, 128, 1);
-  // per-row parts: hi [rows][H], lo [rows][H], then their scale rows [rows][H / 32]
-  const int64_t rows = xr.rows;
-  auto up256 = [](size_t v) { return (v + 255) & ~size_t(255); };
-  uint8_t* xh = ctx->xq;
-  uint8_t* xl = xh + up256(size_t(rows) * H);
-  uint8_t* xsh = xl + up256(size_t(rows) * H);
-  uint8_t* xsl = xsh + up256(size_t(rows) * (H / 32));
-  if (size_t(xsl + size_t(rows) * (H / 32) - xh) > ctx->xq_bytes)
-    return fail(ctx, "%lld x rows of H = %d exceed the quantised-row workspace", (long long)rows, H);
+  // sorted rows' parts: hi, lo [max_rows][H] in the f16 row block, scale rows [max_rows][H / 32]
+  const int64_t mr = ctx->max_rows;
+  uint8_t* xh = reinterpret_cast<uint8_t*>(ctx->xs);
+  uint8_t* xl = xh + mr * H;
+  uint8_t* xsh = ctx->xss;
+  uint8_t* xsl = xsh + ((mr * (H / 32) + 255) & ~int64_t(255));
+  CUtensorMap mxh, mxl, mxsh, mxsl;
+  ok = encode_bytes_2d(ctx, &mxh, xh, H, mr, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B) &&
+       encode_bytes_2d(ctx, &mxl, xl, H, mr, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B) &&
+       encode_bytes_2d(ctx, &mxsh, xsh, H / 32, mr, 16, 128, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+       encode_bytes_2d(ctx, &mxsl, xsl, H / 32, mr, 16, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!ok) return fail(ctx, "cuTensorMapEncodeTiled failed for the sorted-row operands");
   wm::BsArgs b{};
   b.plan = ctx->plan;
   b.wts = wts;
@@ -556,13 +571,11 @@ int run_bs_gemm(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts,
   b.act_img = ctx->bs_img_act;
   b.routed = ctx->routed;
   wm::prof_begin(&ctx->prof, wm::kProfGather, s);
-  wm::launch_bsg_quant_tokens(static_cast<const uint16_t*>(a->x), int(rows), H, xr.counts, xr.capacity, xh, xl, xsh,
-                              xsl, ctx->num_sms, s);
-  wm::launch_bsg_images(b.plan, H, xh, xl, xsh, xsl, ctx->bs_img_x, ctx->num_sms, s);
+  wm::launch_bsg_quant_scatter(static_cast<const uint16_t*>(a->x), int(xr.rows), H, b.plan, a->K, has_shared, a->E,
+                               xr.counts, xr.capacity, xh, xl, xsh, xsl, ctx->num_sms, s);
   wm::prof_end(&ctx->prof, wm::kProfGather, s);
-  b.img = ctx->bs_img_x;
   wm::prof_begin(&ctx->prof, wm::kProfGemmGateUp, s);
-  const void* maps0[4] = {&w13, has_shared ? &w13s : &w13, &s13, has_shared ? &s13s : &s13};
+  const void* maps0[8] = {&w13, has_shared ? &w13s : &w13, &s13, has_shared ? &s13s : &s13, &mxh, &mxl, &mxsh, &mxsl};
   wm::launch_bsg(b, 0, maps0, ctx->num_sms, s);
   wm::prof_end(&ctx->prof, wm::kProfGemmGateUp, s);
   b.img = ctx->bs_img_act;
@@ -571,7 +584,7 @@ int run_bs_gemm(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts,
   const void* maps1[4] = {&w2, has_shared ? &w2s : &w2, &s2, has_shared ? &s2s : &s2};
   wm::launch_bsg(b, 1, maps1, ctx->num_sms, s);
   wm::prof_end(&ctx->prof, wm::kProfGemmDown, s);
-  ctx->counters.launches += 4;
+  ctx->counters.launches += 3;
   ctx->counters.gemm_calls += 1;
   ctx->counters.bs_gemm_calls += 1;
   return check_launch(ctx, "block-scaled expert GEMM");
@@ -731,9 +744,9 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
                o_act = take(rows * I * 2), o_routed = take(rows * H * 2), o_logits = take(T * E * 4),
                o_idx = take(T * K * 4), o_w = take(T * K * 4), o_sg = take(T * 4), o_status = take(16),
                o_act16 = take(rows * I * 2), o_rowscale = take(rows * 4), o_actscale = take(rows * 4),
-               o_rowmax = take(rows * 4), o_xn = take(T * H * 2), o_xq = take(T * H * 2 + T * (H / 32 + 1) * 2 + 1024),
-               // tile images: the decode kernel's 16-row tiles or the GEMM's 128-row tiles
-               o_imgx = take(std::max<size_t>(rows * H * 9 / 4, wm::bsg_image_bytes(rows / wm::kTileM + 2, int(H)))),
+               o_rowmax = take(rows * 4), o_xn = take(T * H * 2), o_xss = take(rows * (H / 32 + 1) * 2 + 1024),
+               // tile images: the decode kernel's 16-row tiles (x and act) or the GEMM's 128-row act tiles
+               o_imgx = take(rows * H * 9 / 4),
                o_imga = take(std::max<size_t>(rows * I * 9 / 4, wm::bsg_image_bytes(rows / wm::kTileM + 2, int(I))));
   ctx->ws_bytes = off;
   if (cudaMalloc(&ctx->ws, ctx->ws_bytes) != cudaSuccess) {
@@ -767,8 +780,7 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
   ctx->actscale = reinterpret_cast<float*>(base + o_actscale);
   ctx->rowmax = reinterpret_cast<uint32_t*>(base + o_rowmax);
   ctx->xn = reinterpret_cast<uint16_t*>(base + o_xn);
-  ctx->xq = base + o_xq;
-  ctx->xq_bytes = size_t(T * H * 2 + T * (H / 32 + 1) * 2 + 1024);
+  ctx->xss = base + o_xss;
   ctx->bs_img_x = base + o_imgx;
   ctx->bs_img_act = base + o_imga;
   // the whole workspace starts at zero (status word included); padding rows of

@@ -218,19 +218,21 @@ void launch_bs_decode(const BsArgs& a, int kind, const void* const* maps, int nu
 
 // ---- prefill grouped GEMM on tcgen05 block-scaled MMA (wm_bsgemm_sm100.cu):
 // 128 token rows (hi / lo E4M3) x 256 weight rows per tile.  The same BsArgs
-// (plan with 128-row tiles; img / act_img hold 33,792-byte images per
-// 128-row tile and 128-K stage, bsg_image_bytes) and weight maps as launch_bs_decode;
+// (plan with 128-row tiles; act_img holds 33,792-byte images per 128-row
+// tile and 128-K stage, bsg_image_bytes) and weight maps as launch_bs_decode;
 // shapes as bs_shape_ok.
 void bsg_init_attributes();
 size_t bsg_image_bytes(int64_t mtiles, int K);
 // x rows [0, rows) (with counts: expert-parallel slots, block r = row / capacity
-// holding counts[r]) -> hi, lo [rows][K] E4M3 and shi, slo [rows][K / 32] UE8M0
-void launch_bsg_quant_tokens(const uint16_t* x, int rows, int K, const int32_t* counts, int capacity, uint8_t* hi,
-                             uint8_t* lo, uint8_t* shi, uint8_t* slo, int num_sms, cudaStream_t stream);
-// quantised rows -> the tile images of the plan's sorted rows (K = H)
-void launch_bsg_images(const Plan& p, int K, const uint8_t* hi, const uint8_t* lo, const uint8_t* shi,
-                       const uint8_t* slo, uint8_t* img, int num_sms, cudaStream_t stream);
-// maps[0..3] as launch_bs_decode
+// holding counts[r]) -> hi / lo E4M3 parts and UE8M0 scales at every sorted
+// row that holds them (pair_pos[t * topk + k], and offsets[E] + t with
+// has_shared): hi, lo [sorted rows][K], shi, slo [sorted rows][K / 32]
+void launch_bsg_quant_scatter(const uint16_t* x, int rows, int K, const Plan& p, int topk, bool has_shared, int E,
+                              const int32_t* counts, int capacity, uint8_t* hi, uint8_t* lo, uint8_t* shi,
+                              uint8_t* slo, int num_sms, cudaStream_t stream);
+// maps[0..3] as launch_bs_decode; gate/up (kind 0) also maps[4..7]: the
+// sorted rows' hi and lo parts (uint8 [rows][H], boxes 128 x 128, 128-byte
+// swizzle) and their scale rows (uint8 [rows][H / 32], boxes 16 x 128)
 void launch_bsg(const BsArgs& a, int kind, const void* const* maps, int num_sms, cudaStream_t stream);
 
 // ---- prefill grouped GEMM on tcgen05 (wm_gemm_sm100.cu)
