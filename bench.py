@@ -26,6 +26,7 @@ arithmetic) on a bounded sample of the same workload.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 import statistics
@@ -201,6 +202,7 @@ def prefill_section(args, dev, pk, n: int = 2) -> dict:
     eng = Engine(dev.index, max_tokens=T, hidden=Hn, inter=In, experts=En, topk=Kn)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     for _ in range(3):
+        flush.zero_()
         eng.forward(lay, wl.x, Kn)
     torch.cuda.synchronize()
     steps = max(3, min(args.steps, 10))
@@ -332,6 +334,7 @@ def long_ep_section(args, n: int, world: int, rank: int, local: int, pk: dict) -
         eng1 = Engine(local, max_tokens=T_total, hidden=Hn, inter=In, experts=En, topk=Kn, gemv_max_tokens=-1)
         fwd1 = lambda i, lay, h: eng1.forward(lay, h, Kn)  # noqa: E731
         for _ in range(2):
+            flush.zero_()
             stack(fwd1, x_all)
         torch.cuda.synchronize()
         single = T_total / (timed(fwd1, x_all, steps) / 1e3)
@@ -360,6 +363,7 @@ def long_ep_section(args, n: int, world: int, rank: int, local: int, pk: dict) -
                                      owner_engine=owner, peer_buffer=eps[0].ep_buf if eps else None))
     fwd = lambda i, lay, h: eps[i](h)  # noqa: E731
     for _ in range(2):
+        flush.zero_()
         stack(fwd, x)
     torch.cuda.synchronize()
     dist.barrier()
@@ -907,6 +911,11 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    # Python's cyclic collector stays off while the bench runs (reference
+    # counting still frees almost everything): a collection pause on one rank
+    # in a timed region stalls every rank's bounded peer waits with it
+    gc.collect()
+    gc.disable()
     if args.impl == "reference":
         run_reference(args)
     else:
