@@ -267,10 +267,6 @@ bool encode_2d_bf16(wm_ctx* ctx, CUtensorMap* map, const void* base, int cols, i
   return r == CUDA_SUCCESS;
 }
 
-bool encode_rows(wm_ctx* ctx, CUtensorMap* map, const void* base, int kdim) {
-  return encode_rows_box(ctx, map, base, kdim, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 128);
-}
-
 // Expert rows per expert (on average) above which a call takes the grouped
 // GEMM: its 128-row tiles read each expert's weights once, the decode
 // kernels' 16-row tiles once per 16 rows.
@@ -336,23 +332,6 @@ int plan_align(Path path) {
 void plan_for_path(const wm_ctx* ctx, Path path, wm::Plan* plan) {
   if (path == kPathDecodeMma || path == kPathGemm) plan->rowmax = ctx->rowmax;
   if (path == kPathDecodeMma) plan->tile_rows = 8;
-}
-
-// TMA descriptor over one projection's packed weights (or scales) of
-// `experts` experts: uint8 [experts][rows][row_bytes], boxes of box_bytes x
-// box_rows x 1.
-bool encode_weights(wm_ctx* ctx, CUtensorMap* map, const void* base, int64_t row_bytes, int64_t rows,
-                    int64_t experts, int64_t expert_stride, int box_bytes, int box_rows,
-                    CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
-  if (ctx->encode_tiled == nullptr) return false;
-  cuuint64_t dims[3] = {cuuint64_t(row_bytes), cuuint64_t(rows), cuuint64_t(experts)};
-  cuuint64_t strides[2] = {cuuint64_t(row_bytes), cuuint64_t(experts > 1 ? expert_stride : row_bytes * rows)};
-  cuuint32_t box[3] = {cuuint32_t(box_bytes), cuuint32_t(box_rows), 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box,
-                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
-                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
 }
 
 // The register-direct decode path: per-token prescale, gate/up (+SwiGLU), down.

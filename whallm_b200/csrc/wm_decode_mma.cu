@@ -553,37 +553,37 @@ __global__ void __launch_bounds__(kThreads, kCtas) decode_mma_kernel(const __gri
   auto chunk = [&](const uint4 (&w)[2 * kRG], int cc) {
     if constexpr (!kFp4) {
       chunk_fp8(w, cc);
-      return;
-    }
-    uint32_t mult[2 * kRG];
-#pragma unroll
-    for (int j = 0; j < 2 * kRG; ++j) mult[j] = group_mult(lds_u8q(sb + srow[j] * S + 4 * cc + t), rinv[j]);
-    // token operand: 32 f16 at K offset 128cc + 32t of token row g (4 swizzled 16-byte units)
-    const int kb = 2 * cc + (t >> 1);
-    const uint32_t xrow = xb + kb * 1024 + g * 128;
-    uint4 xv[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) xv[u] = lds_v4q(xrow + (((4 * (t & 1) + u) ^ g) << 4));
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {  // word q of the 16 bytes: K offsets 8q .. 8q + 7 = steps 2q, 2q + 1
-      const uint32_t xw[4] = {xv[q].x, xv[q].y, xv[q].z, xv[q].w};
-#pragma unroll
-      for (int r = 0; r < kRG; ++r) {
-        const uint4& wa = w[2 * r];
-        const uint4& wb = w[2 * r + 1];
-        const uint32_t va = q == 0 ? wa.x : q == 1 ? wa.y : q == 2 ? wa.z : wa.w;
-        const uint32_t vb = q == 0 ? wb.x : q == 1 ? wb.y : q == 2 ? wb.z : wb.w;
-        uint32_t ha[4], hb[4];
-        e2m1x8_f16x2(va, ha);
-        e2m1x8_f16x2(vb, hb);
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          ha[p] = hmul2q(ha[p], mult[2 * r]);
-          hb[p] = hmul2q(hb[p], mult[2 * r + 1]);
+    } else {
+      uint32_t mult[2 * kRG];
+  #pragma unroll
+      for (int j = 0; j < 2 * kRG; ++j) mult[j] = group_mult(lds_u8q(sb + srow[j] * S + 4 * cc + t), rinv[j]);
+      // token operand: 32 f16 at K offset 128cc + 32t of token row g (4 swizzled 16-byte units)
+      const int kb = 2 * cc + (t >> 1);
+      const uint32_t xrow = xb + kb * 1024 + g * 128;
+      uint4 xv[4];
+  #pragma unroll
+      for (int u = 0; u < 4; ++u) xv[u] = lds_v4q(xrow + (((4 * (t & 1) + u) ^ g) << 4));
+  #pragma unroll
+      for (int q = 0; q < 4; ++q) {  // word q of the 16 bytes: K offsets 8q .. 8q + 7 = steps 2q, 2q + 1
+        const uint32_t xw[4] = {xv[q].x, xv[q].y, xv[q].z, xv[q].w};
+  #pragma unroll
+        for (int r = 0; r < kRG; ++r) {
+          const uint4& wa = w[2 * r];
+          const uint4& wb = w[2 * r + 1];
+          const uint32_t va = q == 0 ? wa.x : q == 1 ? wa.y : q == 2 ? wa.z : wa.w;
+          const uint32_t vb = q == 0 ? wb.x : q == 1 ? wb.y : q == 2 ? wb.z : wb.w;
+          uint32_t ha[4], hb[4];
+          e2m1x8_f16x2(va, ha);
+          e2m1x8_f16x2(vb, hb);
+  #pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            ha[p] = hmul2q(ha[p], mult[2 * r]);
+            hb[p] = hmul2q(hb[p], mult[2 * r + 1]);
+          }
+          // step 2q: bytes 0, 1 (K 8q .. 8q+3); step 2q + 1: bytes 2, 3 (K 8q+4 .. 8q+7)
+          mma_f16(acc[r][0], ha[0], hb[0], ha[1], hb[1], xw[0], xw[1]);
+          mma_f16(acc[r][1], ha[2], hb[2], ha[3], hb[3], xw[2], xw[3]);
         }
-        // step 2q: bytes 0, 1 (K 8q .. 8q+3); step 2q + 1: bytes 2, 3 (K 8q+4 .. 8q+7)
-        mma_f16(acc[r][0], ha[0], hb[0], ha[1], hb[1], xw[0], xw[1]);
-        mma_f16(acc[r][1], ha[2], hb[2], ha[3], hb[3], xw[2], xw[3]);
       }
     }
   };
