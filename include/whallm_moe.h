@@ -128,12 +128,17 @@ typedef struct {
    32-byte aligned weight regions and 16-byte aligned scale regions. */
 #define WM_FLAG_MMA_DECODE 4
 
-/* Long MXFP4 calls take the kind::f16 tcgen05 grouped GEMM (weights
-   dequantised to exact f16 by producer warps, activation rows as f16)
-   instead of the default block-scaled one.  The default: E2M1 weights by TMA
-   with their E8M0 scales as the MMA's scale factors (kind::mxf8f6f4), token
-   and act rows as hi + lo E4M3 parts (as for WM_FLAG_MMA_DECODE's default);
-   same shape and alignment needs as the block-scaled decode kernel. */
+/* Long MXFP4 and FP8 (128 x 128 fp32 block scales) calls take the kind::f16
+   tcgen05 grouped GEMM (weights dequantised by producer warps: MXFP4 to exact
+   f16, FP8 to bf16(e4m3 * scale) as the reference rounds them) instead of the
+   default block-scaled one.  The default: the blob's E2M1 or E4M3 weights by
+   TMA into kind::mxf8f6f4 MMAs, MXFP4's E8M0 scales as the MMA's scale
+   factors, FP8's fp32 block scales applied to each 128-K block's partial sum
+   in registers (the weights stay exact, so FP8 results differ from the
+   reference's bf16-rounded weights by up to ~1e-2 of max|y|: 5-8.5e-3 on the
+   benchmark weights, against 2-4.3e-3 for the kind::f16 GEMM); token and act
+   rows as hi + lo E4M3 parts (as for WM_FLAG_MMA_DECODE's default); H and I
+   multiples of 512 and the block-scaled decode kernel's alignment needs. */
 #define WM_FLAG_F16_GEMM 8
 
 /* One projection of every expert: expert e's matrix at weight + e * weight_stride
@@ -187,8 +192,8 @@ typedef struct {
   int64_t gemv_calls, gemm_calls;
   int64_t decode_calls;        /* calls that took the decode kernels (block-scaled tcgen05 by default,
                                   WM_FLAG_MMA_DECODE selects the register-direct one) */
-  int64_t bs_gemm_calls;       /* the gemm_calls that took the block-scaled grouped GEMM (the default
-                                  for MXFP4; WM_FLAG_F16_GEMM selects the kind::f16 one) */
+  int64_t bs_gemm_calls;       /* the gemm_calls that took a block-scaled grouped GEMM (the default for
+                                  MXFP4 and 128 x 128 FP8; WM_FLAG_F16_GEMM selects the kind::f16 one) */
 } wm_counters;
 
 typedef struct {

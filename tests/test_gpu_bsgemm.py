@@ -125,3 +125,54 @@ def test_bs_gemm_repeat_is_deterministic(bs_engine):
     b = bs_engine.expert_pairs(layer, x, idx).clone()
     bs_engine.sync()
     assert torch.equal(a, b)
+
+
+def fp8_layer(E, H, I, seed, gate=lib.SHARED_NONE):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    w13, s13 = synth.fp8_projection(E, 2 * I, H, g, DEV)
+    w2, s2 = synth.fp8_projection(E, H, I, g, DEV)
+    shared = None
+    if gate != lib.SHARED_NONE:
+        a, b = synth.fp8_projection(1, 2 * I, H, g, DEV)
+        c, d = synth.fp8_projection(1, H, I, g, DEV)
+        shared = SharedExpert(Projection.stacked(a, b), Projection.stacked(c, d), gate)
+    wr = (torch.randn((E, H), generator=g, device=DEV) / H ** 0.5).to(torch.bfloat16)
+    return LayerWeights(lib.LAYOUT_W13_FP8_B128, H, I, E, Projection.stacked(w13, s13), Projection.stacked(w2, s2),
+                        shared=shared, router=RouterWeights(wr, lib.ROUTER_SOFTMAX))
+
+
+@pytest.mark.parametrize("T", [1, 65, 300])
+def test_fp8_block_scaled_gemm_pairs_match_oracle(bs_engine, T):
+    """FP8 experts with fp32 128 x 128 block scales: E4M3 weights straight into
+    block-scaled MMAs, each 128-K block's partial scaled in registers."""
+    E, H, I, K = 16, 512, 512, 4
+    layer = fp8_layer(E, H, I, seed=80 + T)
+    x = synth.activations(T, H, torch.Generator(device=DEV).manual_seed(81 + T), DEV)
+    idx = _routes(T, E, K, 82 + T)
+    before = bs_engine.ctx.counters().bs_gemm_calls
+    out = bs_engine.expert_pairs(layer, x, idx)
+    bs_engine.sync()
+    assert bs_engine.ctx.counters().bs_gemm_calls == before + 1
+    ref = adapter.from_layer(layer).pairs(adapter.bits(x), idx.cpu().numpy())
+    assert rel(adapter.bits(out), ref) <= TOL
+
+
+def test_fp8_block_scaled_gemm_forward_matches_f16_gemm(bs_engine, f16_engine):
+    """Routed + shared FP8 experts through the layer: the block-scaled FP8 GEMM
+    against the oracle and against the kind::f16 GEMM on the same routes.  The
+    kind::f16 GEMM rounds every dequantised weight to bf16 as the reference
+    does; the block-scaled one multiplies the exact E4M3 values and scales each
+    128-K block's sum, so the two differ by that rounding (up to 2^-9 of a
+    weight; 5-8e-3 of max|y| with these weights spread over every E4M3 code)
+    and the cross-check takes the layer tolerance."""
+    E, H, I, K, T = 16, 1024, 512, 8, 257
+    layer = fp8_layer(E, H, I, seed=90, gate=lib.SHARED_ONE)
+    x = synth.activations(T, H, torch.Generator(device=DEV).manual_seed(91), DEV)
+    out_a, (w, idx) = bs_engine.forward(layer, x, K, return_routes=True)
+    out_b = f16_engine.forward(layer, x, K, routes=(w, idx))
+    bs_engine.sync()
+    f16_engine.sync()
+    ref = adapter.from_layer(layer).forward(adapter.bits(x), idx.cpu().numpy(), w.cpu().numpy())
+    assert rel(adapter.bits(out_a), ref) <= TOL
+    assert rel(adapter.bits(out_b), ref) <= TOL
+    assert rel(adapter.bits(out_a), adapter.bits(out_b)) <= TOL

@@ -286,7 +286,7 @@ bool use_gemm(const wm_ctx* ctx, const wm_moe_args* a) {
   return gemm && wm::gemm_shape_ok(a->H, a->I) && ctx->encode_tiled != nullptr;
 }
 
-enum Path { kPathGemv = 0, kPathGemm = 2, kPathDecodeMma = 3, kPathBsDecode = 4, kPathBsGemm = 5 };
+enum Path { kPathGemv = 0, kPathGemm = 2, kPathDecodeMma = 3, kPathBsDecode = 4, kPathBsGemm = 5, kPathFp8Gemm = 6 };
 
 // The block-scaled decode kernel's TMA operands: packed weights 32-byte
 // aligned with 32-byte multiple strides (16U4_ALIGN16B), E8M0 rows 16-byte
@@ -308,9 +308,25 @@ bool bs_operands_ok(const wm_ctx* ctx, const wm_moe_args* a, bool has_shared) {
 // shapes and regions its TMA operands take, unless WM_FLAG_MMA_DECODE), else
 // the register-direct decode kernel where 16-byte loads are possible (MXFP4
 // and FP8), else the CUDA-core GEMV.
+// The FP8 grouped GEMM's TMA operands: E4M3 weights 16-byte aligned with
+// 16-byte multiple strides (fp32 128 x 128 block scales, read directly).
+bool fp8g_operands_ok(const wm_ctx* ctx, const wm_moe_args* a, bool has_shared) {
+  if (ctx->encode_tiled == nullptr || a->layout != WM_LAYOUT_W13_FP8_B128 || !wm::fp8g_shape_ok(a->H, a->I))
+    return false;
+  const wm_matrix* ms[4] = {&a->w13, &a->w2, &a->shared_w13, &a->shared_w2};
+  for (int i = 0; i < (has_shared ? 4 : 2); ++i) {
+    if (!aligned(ms[i]->weight, 16) || !aligned(ms[i]->scale, 4)) return false;
+    if (i < 2 && (ms[i]->weight_stride % 16 || ms[i]->scale_stride % 4)) return false;
+  }
+  return true;
+}
+
 Path expert_path(const wm_ctx* ctx, const wm_moe_args* a, bool has_shared) {
-  if (use_gemm(ctx, a))
-    return !(ctx->opt.flags & WM_FLAG_F16_GEMM) && bs_operands_ok(ctx, a, has_shared) ? kPathBsGemm : kPathGemm;
+  if (use_gemm(ctx, a)) {
+    if (ctx->opt.flags & WM_FLAG_F16_GEMM) return kPathGemm;
+    if (bs_operands_ok(ctx, a, has_shared)) return kPathBsGemm;
+    return fp8g_operands_ok(ctx, a, has_shared) ? kPathFp8Gemm : kPathGemm;
+  }
   if (ctx->encode_tiled == nullptr) return kPathGemv;
   const wm_matrix* ms[4] = {&a->w13, &a->w2, &a->shared_w13, &a->shared_w2};
   for (int i = 0; i < (has_shared ? 4 : 2); ++i)
@@ -325,7 +341,8 @@ Path expert_path(const wm_ctx* ctx, const wm_moe_args* a, bool has_shared) {
 // Rows each expert's group is padded to: the GEMMs' 128-row tiles, the
 // block-scaled decode kernel's 16-token tiles, else none.
 int plan_align(Path path) {
-  return path == kPathGemm || path == kPathBsGemm ? wm::kTileM : path == kPathBsDecode ? 16 : 1;
+  return path == kPathGemm || path == kPathBsGemm || path == kPathFp8Gemm ? wm::kTileM
+                                                                           : path == kPathBsDecode ? 16 : 1;
 }
 
 // Plan fields of the expert kernels of `path`.
@@ -418,6 +435,27 @@ bool encode_fp4_weights(wm_ctx* ctx, CUtensorMap* map, const void* base, int64_t
                                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+// E4M3 weights [experts][halves][rows / halves][K] as uint8, boxes of 128
+// bytes x box_rows (x halves), 128-byte swizzle (the FP8 grouped GEMM's B).
+bool encode_fp8_weights(wm_ctx* ctx, CUtensorMap* map, const void* base, int64_t K, int64_t rows, int64_t experts,
+                        int64_t expert_stride, int box_rows, int halves) {
+  if (ctx->encode_tiled == nullptr) return false;
+  const int64_t hr = rows / halves;
+  const int64_t estride = experts > 1 ? expert_stride : K * rows;
+  cuuint64_t dims[4] = {cuuint64_t(K), cuuint64_t(hr), cuuint64_t(halves), cuuint64_t(experts)};
+  cuuint64_t strides[3] = {cuuint64_t(K), cuuint64_t(K * hr), cuuint64_t(estride)};
+  cuuint32_t box[4] = {128, cuuint32_t(box_rows), cuuint32_t(halves), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  if (halves == 1) {  // 3-D: [experts][rows][K]
+    dims[2] = cuuint64_t(experts);
+    strides[1] = cuuint64_t(estride);
+    box[2] = 1;
+  }
+  return ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, halves == 1 ? 3 : 4, const_cast<void*>(base), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // E8M0 rows [experts][halves][rows / halves][S] as uint8, boxes of 16 bytes x
@@ -515,18 +553,28 @@ bool encode_bytes_2d(wm_ctx* ctx, CUtensorMap* map, const void* base, int64_t co
 // (+SwiGLU, act tile images), down.  The plan's groups are padded to 128
 // rows.
 int run_bs_gemm(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts, bool has_shared, cudaStream_t s,
-                const wm::EpReturn* ret, const XRows& xr) {
+                const wm::EpReturn* ret, const XRows& xr, bool fp8) {
   const int H = a->H, I = a->I;
   CUtensorMap w13, w13s, w2, w2s, s13, s13s, s2, s2s;
-  bool ok = encode_fp4_weights(ctx, &w13, a->w13.weight, H, 2 * I, a->E, a->w13.weight_stride, 64, 2) &&
-            encode_fp4_weights(ctx, &w2, a->w2.weight, I, H, a->E, a->w2.weight_stride, 128, 1) &&
-            encode_scale_rows(ctx, &s13, a->w13.scale, H / 32, 2 * I, a->E, a->w13.scale_stride, 64, 2) &&
-            encode_scale_rows(ctx, &s2, a->w2.scale, I / 32, H, a->E, a->w2.scale_stride, 128, 1);
-  if (has_shared)
-    ok = ok && encode_fp4_weights(ctx, &w13s, a->shared_w13.weight, H, 2 * I, 1, 0, 64, 2) &&
-         encode_fp4_weights(ctx, &w2s, a->shared_w2.weight, I, H, 1, 0, 128, 1) &&
-         encode_scale_rows(ctx, &s13s, a->shared_w13.scale, H / 32, 2 * I, 1, 0, 64, 2) &&
-         encode_scale_rows(ctx, &s2s, a->shared_w2.scale, I / 32, H, 1, 0, 128, 1);
+  bool ok;
+  if (fp8) {  // E4M3 bytes; the fp32 block scales are read by the kernel itself
+    ok = encode_fp8_weights(ctx, &w13, a->w13.weight, H, 2 * I, a->E, a->w13.weight_stride, 64, 2) &&
+         encode_fp8_weights(ctx, &w2, a->w2.weight, I, H, a->E, a->w2.weight_stride, 128, 1);
+    if (has_shared)
+      ok = ok && encode_fp8_weights(ctx, &w13s, a->shared_w13.weight, H, 2 * I, 1, 0, 64, 2) &&
+           encode_fp8_weights(ctx, &w2s, a->shared_w2.weight, I, H, 1, 0, 128, 1);
+  } else {
+    ok = encode_fp4_weights(ctx, &w13, a->w13.weight, H, 2 * I, a->E, a->w13.weight_stride, 64, 2) &&
+         encode_fp4_weights(ctx, &w2, a->w2.weight, I, H, a->E, a->w2.weight_stride, 128, 1) &&
+         encode_scale_rows(ctx, &s13, a->w13.scale, H / 32, 2 * I, a->E, a->w13.scale_stride, 64, 2) &&
+         encode_scale_rows(ctx, &s2, a->w2.scale, I / 32, H, a->E, a->w2.scale_stride, 128, 1);
+    if (has_shared)
+      ok = ok && encode_fp4_weights(ctx, &w13s, a->shared_w13.weight, H, 2 * I, 1, 0, 64, 2) &&
+           encode_fp4_weights(ctx, &w2s, a->shared_w2.weight, I, H, 1, 0, 128, 1) &&
+           encode_scale_rows(ctx, &s13s, a->shared_w13.scale, H / 32, 2 * I, 1, 0, 64, 2) &&
+           encode_scale_rows(ctx, &s2s, a->shared_w2.scale, I / 32, H, 1, 0, 128, 1);
+  }
+  if (!ok) return fail(ctx, "cuTensorMapEncodeTiled failed for the block-scaled expert operands");
   // sorted rows' parts: hi, lo [max_rows][H] in the f16 row block, scale rows [max_rows][H / 32]
   const int64_t mr = ctx->max_rows;
   uint8_t* xh = reinterpret_cast<uint8_t*>(ctx->xs);
@@ -554,14 +602,25 @@ int run_bs_gemm(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts,
                                xr.counts, xr.capacity, xh, xl, xsh, xsl, ctx->num_sms, s);
   wm::prof_end(&ctx->prof, wm::kProfGather, s);
   wm::prof_begin(&ctx->prof, wm::kProfGemmGateUp, s);
-  const void* maps0[8] = {&w13, has_shared ? &w13s : &w13, &s13, has_shared ? &s13s : &s13, &mxh, &mxl, &mxsh, &mxsl};
-  wm::launch_bsg(b, 0, maps0, ctx->num_sms, s);
+  if (fp8) {
+    const void* maps0[6] = {&w13, has_shared ? &w13s : &w13, &mxh, &mxl, &mxsh, &mxsl};
+    wm::launch_fp8g(b, 0, maps0, ctx->num_sms, s);
+  } else {
+    const void* maps0[8] = {&w13, has_shared ? &w13s : &w13, &s13, has_shared ? &s13s : &s13,
+                            &mxh, &mxl, &mxsh, &mxsl};
+    wm::launch_bsg(b, 0, maps0, ctx->num_sms, s);
+  }
   wm::prof_end(&ctx->prof, wm::kProfGemmGateUp, s);
   b.img = ctx->bs_img_act;
   if (ret != nullptr) b.ret = *ret;
   wm::prof_begin(&ctx->prof, wm::kProfGemmDown, s);
-  const void* maps1[4] = {&w2, has_shared ? &w2s : &w2, &s2, has_shared ? &s2s : &s2};
-  wm::launch_bsg(b, 1, maps1, ctx->num_sms, s);
+  if (fp8) {
+    const void* maps1[2] = {&w2, has_shared ? &w2s : &w2};
+    wm::launch_fp8g(b, 1, maps1, ctx->num_sms, s);
+  } else {
+    const void* maps1[4] = {&w2, has_shared ? &w2s : &w2, &s2, has_shared ? &s2s : &s2};
+    wm::launch_bsg(b, 1, maps1, ctx->num_sms, s);
+  }
   wm::prof_end(&ctx->prof, wm::kProfGemmDown, s);
   ctx->counters.launches += 3;
   ctx->counters.gemm_calls += 1;
@@ -578,7 +637,8 @@ int run_experts(wm_ctx* ctx, const wm_moe_args* a, bool has_shared, Path path, c
   const int gate_first = a->layout == WM_LAYOUT_QWEN_GATE_UP_MXFP4 ? 1 : 0;
   if (path == kPathDecodeMma) return run_decode_mma(ctx, a, wts, s);
   if (path == kPathBsDecode) return run_bs_decode(ctx, a, wts, has_shared, s, ret);
-  if (path == kPathBsGemm) return run_bs_gemm(ctx, a, wts, has_shared, s, ret, xr ? *xr : XRows{a->T, nullptr, 0});
+  if (path == kPathBsGemm || path == kPathFp8Gemm)
+    return run_bs_gemm(ctx, a, wts, has_shared, s, ret, xr ? *xr : XRows{a->T, nullptr, 0}, path == kPathFp8Gemm);
   if (path == kPathGemv) {
     wm::GemvArgs g{};
     g.plan = ctx->plan;
@@ -784,6 +844,7 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
   wm::decode_mma_init_attributes(int(H), int(I));
   wm::bs_init_attributes();
   wm::bsg_init_attributes();
+  wm::fp8g_init_attributes();
   wm::router_init_attributes(int(H));
   wm::router_gemm_init_attributes();
   cudaDriverEntryPointQueryResult q{};
@@ -1233,7 +1294,7 @@ WM_EXPORT int wm_ep_experts(wm_ctx* ctx, wm_ep* ep, const wm_moe_args* args, voi
   // straight into the senders' back blocks (the return overlaps the math);
   // the other kernels leave them sorted and a copy kernel returns them
   const wm::EpPeers back = ep_peers(ep, 1);
-  const bool fused = path == kPathGemm || path == kPathBsGemm || path == kPathBsDecode;
+  const bool fused = path == kPathGemm || path == kPathBsGemm || path == kPathFp8Gemm || path == kPathBsDecode;
   wm::EpReturn ret{};
   if (fused) {
     for (int r = 0; r < ep->world; ++r) ret.rows[r] = back.rows[r];

@@ -230,6 +230,17 @@ size_t bsg_image_bytes(int64_t mtiles, int K);
 void launch_bsg_quant_scatter(const uint16_t* x, int rows, int K, const Plan& p, int topk, bool has_shared, int E,
                               const int32_t* counts, int capacity, uint8_t* hi, uint8_t* lo, uint8_t* shi,
                               uint8_t* slo, int num_sms, cudaStream_t stream);
+// ---- prefill grouped GEMM for FP8 experts with fp32 128 x 128 block scales
+// (wm_fp8gemm_sm100.cu): E4M3 weights by TMA into block-scaled tcgen05 MMAs
+// (weight scale factors 2^0), each 128-K block's fp32 partial scaled by its
+// weight block scale in registers; tokens as for launch_bsg.  maps: gate/up
+// {w13, shared w13, hi, lo, hi scales, lo scales} (w13: uint8 4-D [E][2][I][H],
+// boxes 128 x 64 x 2, 128-byte swizzle), down {w2, shared w2} (uint8 3-D
+// [E][H][I], boxes 128 x 128).
+void fp8g_init_attributes();
+bool fp8g_shape_ok(int H, int I);
+void launch_fp8g(const BsArgs& a, int kind, const void* const* maps, int num_sms, cudaStream_t stream);
+
 // maps[0..3] as launch_bs_decode; gate/up (kind 0) also maps[4..7]: the
 // sorted rows' hi and lo parts (uint8 [rows][H], boxes 128 x 128, 128-byte
 // swizzle) and their scale rows (uint8 [rows][H / 32], boxes 16 x 128)
