@@ -61,14 +61,53 @@ def peaks() -> dict:
 
 
 class Clocks:
-    """nvidia-smi samples during the timed region."""
+    """SM clocks and clock-event reasons sampled during the timed region: NVML
+    polled every millisecond from a side thread, with one sample as the region
+    starts and one as it ends (so even a few-millisecond region has samples);
+    nvidia-smi at 200 ms when NVML is not there.  Samples go to a CSV too."""
+
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
 
     def __init__(self, index: int, log_dir: str | None = None):
         self.index = index
         self.proc = None
+        self.nvml = None
+        self.rows: list[tuple[float, float, int]] = []
         self.path = Path(log_dir or tempfile.gettempdir()) / f"clocks_rank{index}.csv"
 
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(self.index).uuid)
+        return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+
+    def _sample(self):
+        nv, h = self.nvml
+        sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+        mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        self.rows.append((sm, mx, int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))))
+
     def __enter__(self):
+        import threading
+        try:
+            self.nvml = self._nvml_handle()
+            self._sample()
+        except Exception:
+            self.nvml = None
+        if self.nvml is not None:
+            self.stop = threading.Event()
+
+            def poll():
+                while not self.stop.wait(0.001):
+                    try:
+                        self._sample()
+                    except Exception:
+                        return
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            return self
         try:
             self.path.parent.mkdir(parents=True, exist_ok=True)
             self.f = open(self.path, "w")
@@ -83,17 +122,34 @@ class Clocks:
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
+        if self.nvml is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
+            try:
+                self._sample()
+            except Exception:
+                pass
+            try:
+                self.path.parent.mkdir(parents=True, exist_ok=True)
+                self.path.write_text("".join(f"{a},{b},{c:#x}\n" for a, b, c in self.rows))
+            except OSError:
+                pass
+        elif self.proc is not None:
             time.sleep(0.25)
             self.proc.terminate()
             self.proc.wait(timeout=5)
             self.f.close()
 
     def summary(self) -> dict:
+        if self.nvml is not None:
+            sm = [r[0] for r in self.rows]
+            reasons = sorted({name for name, bit in self.REASONS for r in self.rows if r[2] & bit})
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.rows[-1][1] if sm else None,
+                    "reasons": reasons, "samples": len(sm), "source": "nvml, 1 ms"}
         if self.proc is None or not self.path.exists():
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        names = [name for name, _ in self.REASONS]
         for line in self.path.read_text().splitlines():
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 7:
@@ -107,7 +163,7 @@ class Clocks:
                 if v.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi, 200 ms"}
 
 
 def dist_init():
