@@ -1204,8 +1204,16 @@ WM_EXPORT int wm_ep_dispatch(wm_ctx* ctx, wm_ep* ep, int64_t T, int32_t K, int32
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* own = static_cast<uint8_t*>(ep->base);
   wm::prof_begin(&ctx->prof, wm::kProfEpSend, s);
-  wm::launch_ep_begin(reinterpret_cast<uint32_t*>(own + ep->o_epoch), s);
   const int P = int(T) * K;
+  if (P > 0 && wm::ep_dispatch_small_ok(P, ep->world, int(ep->capacity))) {  // decode-sized: one launch
+    wm::launch_ep_dispatch_small(idx, int(T), K, experts_per_rank, ep->world, int(ep->capacity), pair_pos,
+                                 static_cast<const uint16_t*>(x), ep->H, ep_peers(ep, 0),
+                                 reinterpret_cast<uint32_t*>(own + ep->o_epoch), ctx->status, ctx->num_sms, s);
+    wm::prof_end(&ctx->prof, wm::kProfEpSend, s);
+    ctx->counters.launches += 1;
+    return check_launch(ctx, "expert-parallel dispatch");
+  }
+  wm::launch_ep_begin(reinterpret_cast<uint32_t*>(own + ep->o_epoch), s);
   int launches = 0;
   wm::Plan plan = ctx->plan;
   plan.rowmax = nullptr;

@@ -23,6 +23,8 @@
 // device (ep_begin_kernel increments it), so graph replays signal fresh
 // values.  The reference runs its experts on one device; this is the
 // B200-native counterpart of the expert-parallel plan, not a port.
+#include <algorithm>
+
 #include "wm_kernels.h"
 
 namespace wm {
@@ -111,6 +113,73 @@ __global__ void __launch_bounds__(kCopyThreads) ep_send_kernel(const int32_t* __
   signal_peers(pe, world);
 }
 
+// The whole dispatch of a small call (P = T * K <= kSmallPairs pairs) in one
+// launch: every CTA ranks all pairs by owner in shared memory (warp 0, 32
+// pairs a step, a pair's slot = its owner's running count plus the earlier
+// lanes naming the same owner: the (token, k) order of the plan over owners),
+// then the CTAs share the row copies, ids and padding ids; CTA 0 advances the
+// step number first (the last CTA's flags carry it) and writes the counts.
+constexpr int kSmallPairs = 4096;
+
+__global__ void __launch_bounds__(kCopyThreads) ep_dispatch_small_kernel(
+    const int32_t* __restrict__ idx, int T, int K, int per_rank, int world, int capacity, int32_t* __restrict__ pair_pos,
+    const uint16_t* __restrict__ x, int H, const EpPeers pe, uint32_t* epoch, uint32_t* status) {
+  __shared__ int16_t slot[kSmallPairs];  // pair -> slot within its owner's block (-1: bad id)
+  __shared__ int8_t own[kSmallPairs];
+  __shared__ int count[kMaxEpRanks];
+  const int P = T * K;
+  if (blockIdx.x == 0 && threadIdx.x == 0) epoch[0] += 1u;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) {
+    const int e = idx[i];
+    const bool ok = e >= 0 && e < per_rank * world;
+    own[i] = ok ? int8_t(e / per_rank) : int8_t(-1);
+    if (!ok && blockIdx.x == 0) report_status(status, kStatusBadExpert, uint32_t(i));
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    int run = 0;  // lane r < world: owner r's running count
+    const unsigned lt_mask = (1u << lane) - 1u;
+    for (int i0 = 0; i0 < P; i0 += 32) {
+      const int i = i0 + lane;
+      const int r = i < P ? own[i] : -1;
+      const unsigned same = __match_any_sync(0xffffffffu, r);
+      const int base = __shfl_sync(0xffffffffu, run, r < 0 ? 0 : r);
+      if (i < P) slot[i] = r < 0 ? int16_t(-1) : int16_t(base + __popc(same & lt_mask));
+      // owner q's lane adds the pairs of this step that name it
+      for (int q = 0; q < world; ++q) {
+        const unsigned hits = __ballot_sync(0xffffffffu, r == q);
+        if (lane == q) run += __popc(hits);
+      }
+    }
+    if (lane < world) count[lane] = run;
+  }
+  __syncthreads();
+  const int gtid = blockIdx.x * blockDim.x + threadIdx.x, nthreads = gridDim.x * blockDim.x;
+  if (gtid < world) pe.count[gtid][0] = count[gtid];  // the owner plans over real pairs only
+  for (int i = gtid; i < world * capacity; i += nthreads) {
+    const int r = i / capacity, j = i - r * capacity;
+    if (j >= count[r]) pe.ids[r][j] = -1;
+  }
+  for (int i = gtid; i < P; i += nthreads) {
+    const int r = own[i];
+    if (r < 0) {
+      pair_pos[i] = -1;
+      continue;
+    }
+    pair_pos[i] = r * capacity + slot[i];
+    pe.ids[r][slot[i]] = idx[i] - r * per_rank;
+  }
+  const int lane = threadIdx.x & 31, warps = nthreads >> 5;
+  for (int i = gtid >> 5; i < P; i += warps) {
+    const int r = own[i];
+    if (r < 0) continue;
+    copy_row(reinterpret_cast<uint4*>(pe.rows[r] + int64_t(slot[i]) * H),
+             reinterpret_cast<const uint4*>(x + int64_t(i / K) * H), H, lane);
+  }
+  signal_peers(pe, world);
+}
+
 // Result rows back to the ranks that sent the pairs: slot s of recv block r
 // (valid when its expert id is >= 0) goes to slot j of rank r's back block
 // for this rank.
@@ -168,6 +237,19 @@ void launch_ep_send(const int32_t* idx, const Plan& p, int T, int K, int per_ran
                     int32_t* pair_pos, const uint16_t* x, int H, const EpPeers& pe, int num_sms,
                     cudaStream_t stream) {
   ep_send_kernel<<<2 * num_sms, kCopyThreads, 0, stream>>>(idx, p, T, K, per_rank, world, capacity, pair_pos, x, H, pe);
+}
+
+bool ep_dispatch_small_ok(int P, int world, int capacity) {
+  return P <= kSmallPairs && world <= kMaxEpRanks && capacity <= 32767;
+}
+
+void launch_ep_dispatch_small(const int32_t* idx, int T, int K, int per_rank, int world, int capacity,
+                              int32_t* pair_pos, const uint16_t* x, int H, const EpPeers& pe, uint32_t* epoch,
+                              uint32_t* status, int num_sms, cudaStream_t stream) {
+  const int P = T * K;
+  const int grid = std::max(1, std::min(2 * num_sms, (P + 15) / 16));  // 16 rows per CTA at least
+  ep_dispatch_small_kernel<<<grid, kCopyThreads, 0, stream>>>(idx, T, K, per_rank, world, capacity, pair_pos, x, H, pe,
+                                                              epoch, status);
 }
 
 void launch_ep_return(const uint16_t* y, const int32_t* recv_e, int world, int capacity, int H, const EpPeers& pe,

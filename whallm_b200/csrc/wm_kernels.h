@@ -116,6 +116,12 @@ struct EpPeers {
 void launch_ep_begin(uint32_t* epoch, cudaStream_t stream);
 void launch_ep_send(const int32_t* idx, const Plan& p, int T, int K, int per_rank, int world, int capacity,
                     int32_t* pair_pos, const uint16_t* x, int H, const EpPeers& pe, int num_sms, cudaStream_t stream);
+// The whole dispatch of a small call in one launch (step number, owners,
+// slots, ids, rows, flags): P = T * K pairs within ep_dispatch_small_ok.
+bool ep_dispatch_small_ok(int P, int world, int capacity);
+void launch_ep_dispatch_small(const int32_t* idx, int T, int K, int per_rank, int world, int capacity,
+                              int32_t* pair_pos, const uint16_t* x, int H, const EpPeers& pe, uint32_t* epoch,
+                              uint32_t* status, int num_sms, cudaStream_t stream);
 void launch_ep_return(const uint16_t* y, const int32_t* recv_e, int world, int capacity, int H, const EpPeers& pe,
                       int num_sms, cudaStream_t stream);
 void launch_ep_wait(const uint32_t* flags, int world, const uint32_t* epoch, uint32_t* status, int code,
