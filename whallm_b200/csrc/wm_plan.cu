@@ -302,6 +302,37 @@ __global__ void __launch_bounds__(256) plan_blocks_scatter_kernel(const int32_t*
   if (threadIdx.x < 32) scatter_pairs(ids, s0, s1, 1, E, run, p, status);
 }
 
+// The owner's plan of a small exchange (world * capacity <= 4096 slots) in
+// one block: counts over the real slots, finish_plan, then warp 0 walks each
+// sender's block in slot order (row_token[row] = slot, pair_pos[slot] = row).
+__global__ void __launch_bounds__(1024) plan_blocks_small_kernel(const int32_t* __restrict__ ids,
+                                                                 const int32_t* __restrict__ counts, int world,
+                                                                 int capacity, int E, int align, Plan p, int max_rows,
+                                                                 int max_mtiles, uint32_t* status) {
+  extern __shared__ int sm[];
+  int* cnt = sm;            // E + 1
+  int* off = cnt + E + 1;   // E + 2
+  int* run = off + E + 2;   // E + 1
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  for (int r = 0; r < world; ++r) {
+    const int n = min(counts[r], capacity);
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+      const int e = ids[int64_t(r) * capacity + j];
+      if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+    }
+  }
+  __syncthreads();
+  finish_plan(cnt, off, E, align, p, max_rows, max_mtiles, status);
+  __syncthreads();
+  if (off[E + 1] > max_rows) return;
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) run[i] = off[i];
+  __syncthreads();
+  if (threadIdx.x < 32)
+    for (int r = 0; r < world; ++r)
+      scatter_pairs(ids, r * capacity, r * capacity + min(counts[r], capacity), 1, E, run, p, status);
+}
+
 // x_sorted[r] = x[row_token[r]] (zeros for padding rows).  One warp per row.
 __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __restrict__ x, Plan p, int E, int H,
                                                           uint16_t* __restrict__ xs) {
@@ -431,6 +462,13 @@ void launch_plan(const int32_t* idx, int T, int K, int E, bool has_shared, int a
 void launch_plan_blocks(const int32_t* ids, const int32_t* counts, int world, int capacity, int E, int align,
                         const Plan& p, int max_rows, int max_mtiles, int max_chunks, uint32_t* status,
                         cudaStream_t stream, int* launches) {
+  if (int64_t(world) * capacity <= 4096) {  // decode-sized exchanges: one block
+    const size_t smem = size_t(3 * (E + 2)) * sizeof(int);
+    plan_blocks_small_kernel<<<1, 1024, smem, stream>>>(ids, counts, world, capacity, E, align, p, max_rows, max_mtiles,
+                                                        status);
+    *launches += 1;
+    return;
+  }
   int chunk_slots = 64;
   while (int64_t(world) * ((capacity + chunk_slots - 1) / chunk_slots) > max_chunks) chunk_slots *= 2;
   const int per_block = (capacity + chunk_slots - 1) / chunk_slots;
