@@ -112,7 +112,6 @@ __device__ __forceinline__ uint32_t bs_idesc(uint32_t kk) {
 // read).
 __global__ void __launch_bounds__(256) bs_quant_rows_kernel(const uint16_t* __restrict__ x, Plan p, int E, int K,
                                                             uint8_t* __restrict__ img) {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // gate/up may start its weight loads
   const int rows = p.offsets[E + 1];
   const int lane = threadIdx.x & 31;
   const int S = K / kBK;
@@ -165,9 +164,6 @@ __global__ void __launch_bounds__(kThreads, 1) bs_decode_kernel(const __grid_con
                                                                 const __grid_constant__ CUtensorMap tm_ss,
                                                                 const BsArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  // the next kernel (down, or the combine) may be scheduled as this grid's CTAs
-  // leave their SMs; it waits for this grid's results itself
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int K = KIND == 0 ? a.H : a.I;
   const int S = K / kBK;  // stages per item
   const int nb = KIND == 0 ? a.I / 64 : a.H / kBM;
@@ -228,20 +224,6 @@ __global__ void __launch_bounds__(kThreads, 1) bs_decode_kernel(const __grid_con
       tma_prefetch_desc(&tm_w);
       tma_prefetch_desc(&tm_s);
       int st = 0, ph = 0, rs = 0, rph = 0;
-      // The kernel may start while its predecessor (which writes the token
-      // images) still runs: the first ring's weight and scale loads go out at
-      // once, their image copies only after griddepcontrol.wait.
-      bool waited = false;
-      int n_def = 0;
-      int def_st[kMaxStages];
-      const uint8_t* def_src[kMaxStages];
-      auto release_images = [&]() {
-        asm volatile("griddepcontrol.wait;" ::: "memory");
-        waited = true;
-        for (int i = 0; i < n_def; ++i)
-          bulk_g2s(b_addr(def_st[i]), def_src[i], uint32_t(kImage), &sh.full[def_st[i]]);
-        n_def = 0;
-      };
       // item metadata is read two items ahead, so no TMA issue waits on a load
       int ce = 0, crow0 = 0, cblk = 0, ne = 0, nrow0 = 0, nblk = 0;
       if (int(blockIdx.x) < n_items) item(blockIdx.x, &ce, &crow0, &cblk);
@@ -274,20 +256,12 @@ __global__ void __launch_bounds__(kThreads, 1) bs_decode_kernel(const __grid_con
           else
             tma_load_3d(a_addr(st), mw, s * kBK, blk * kBM, ez, &sh.full[st]);
           // the token tile image and its scale atom in one copy
-          const uint8_t* isrc = a.img + (int64_t(tile) * S + s) * kImage;
-          if (waited) {
-            bulk_g2s(b_addr(st), isrc, uint32_t(kImage), &sh.full[st]);
-          } else {
-            def_st[n_def] = st;
-            def_src[n_def] = isrc;
-            if (++n_def == NS) release_images();
-          }
+          bulk_g2s(b_addr(st), a.img + (int64_t(tile) * S + s) * kImage, uint32_t(kImage), &sh.full[st]);
           if (++st == NS) { st = 0; ph ^= 1; }
         }
         ce = ne, crow0 = nrow0, cblk = nblk;
         ne = n2e, nrow0 = n2row0, nblk = n2blk;
       }
-      if (!waited && !*abort) release_images();  // fewer stages than ring slots
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- scale warp
@@ -506,23 +480,10 @@ void launch_bs_decode(const BsArgs& args, int kind, const void* const* maps, int
   const CUtensorMap* ms = static_cast<const CUtensorMap*>(maps[1]);
   const CUtensorMap* s = static_cast<const CUtensorMap*>(maps[2]);
   const CUtensorMap* ss = static_cast<const CUtensorMap*>(maps[3]);
-  // programmatic dependent launch: the CTAs start as the predecessor's leave
-  // their SMs and load weights while it finishes (griddepcontrol.wait guards
-  // the token images)
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(num_sms);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   if (kind == 0)
-    cudaLaunchKernelEx(&cfg, bs_decode_kernel<0>, *m, *ms, *s, *ss, a);
+    bs_decode_kernel<0><<<num_sms, kThreads, smem, stream>>>(*m, *ms, *s, *ss, a);
   else
-    cudaLaunchKernelEx(&cfg, bs_decode_kernel<1>, *m, *ms, *s, *ss, a);
+    bs_decode_kernel<1><<<num_sms, kThreads, smem, stream>>>(*m, *ms, *s, *ss, a);
 }
 
 }  // namespace wm
