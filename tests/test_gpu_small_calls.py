@@ -1,0 +1,125 @@
+"""Small router calls (T <= 8) on the block-scaled decode path: the top-k,
+the plan and the token images in one launch (needs a B200).
+
+The one launch must give the same bits as the three launches it replaces
+(top-k, plan, quantise; WM_FLAG_SPLIT_SMALL_CALLS keeps them): identical
+routes (indices and weights) and identical layer outputs, for every router
+kind, with and without the shared expert and the pre-MoE norm.  One case per
+router kind is also checked against the CPU oracle (max|y - y_ref| /
+max|y_ref| <= 1e-2, identical top-k sets)."""
+import pytest
+import torch
+
+import oracle
+from oracle import adapter
+from whallm_b200 import lib, synth
+from whallm_b200.layout import Projection
+from whallm_b200.moe import Engine, LayerWeights, PreNorm, RouterWeights, SharedExpert
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+DEV = "cuda"
+FLAG_SPLIT = lib.FLAG_SPLIT_SMALL_CALLS
+
+
+def _layer(E, H, I, kind, shared, norm, seed):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    w13, s13 = synth.mxfp4_projection(E, 2 * I, H, g, DEV)
+    w2, s2 = synth.mxfp4_projection(E, H, I, g, DEV)
+    sh = None
+    if shared != lib.SHARED_NONE:
+        a, b = synth.mxfp4_projection(1, 2 * I, H, g, DEV)
+        c, d = synth.mxfp4_projection(1, H, I, g, DEV)
+        gate = (torch.randn((H,), generator=g, device=DEV) / H ** 0.5).to(torch.bfloat16)
+        sh = SharedExpert(Projection.stacked(a, b), Projection.stacked(c, d), shared,
+                          gate if shared == lib.SHARED_SIGMOID_GATE else None)
+    wr = (torch.randn((E, H), generator=g, device=DEV) / H ** 0.5).to(torch.bfloat16)
+    bias = None
+    groups, keep = 1, 1
+    if kind != lib.ROUTER_SOFTMAX:
+        bias = 0.1 * torch.randn((E,), generator=g, device=DEV)
+    if kind == lib.ROUTER_SIGMOID_GROUPED:
+        groups, keep = 8, 4
+    router = RouterWeights(wr, kind, bias, groups, keep, 2.5 if kind != lib.ROUTER_SOFTMAX else 1.0)
+    pre = None
+    if norm:
+        pre = PreNorm((1.0 + 0.2 * torch.randn((H,), generator=g, device=DEV)).to(torch.bfloat16), 1e-6)
+    return LayerWeights(lib.LAYOUT_QWEN_GATE_UP_MXFP4 if kind == lib.ROUTER_SOFTMAX else lib.LAYOUT_DS_W13_MXFP4,
+                        H, I, E, Projection.stacked(w13, s13), Projection.stacked(w2, s2), shared=sh, router=router,
+                        swiglu_limit=0.0 if kind == lib.ROUTER_SOFTMAX else 10.0, norm=pre)
+
+
+def _run(eng, layer, x, K):
+    """Output, routes, the kernels that ran and the normalised rows (or x)."""
+    xn = torch.empty_like(x) if layer.norm is not None else None
+    eng.ctx.profile(True)
+    eng.ctx.profile_reset()
+    out, (w, idx) = eng.forward(layer, x, K, return_routes=True, x_norm=xn)
+    eng.sync()
+    kernels = eng.ctx.profile_read()
+    eng.ctx.profile(False)
+    return out, w, idx, kernels, (x if xn is None else xn)
+
+
+CASES = [
+    # kind, E, K, shared, norm
+    (lib.ROUTER_SOFTMAX, 512, 10, lib.SHARED_SIGMOID_GATE, False),
+    (lib.ROUTER_SOFTMAX, 256, 8, lib.SHARED_NONE, True),
+    (lib.ROUTER_SQRTSOFTPLUS, 256, 6, lib.SHARED_ONE, False),
+    (lib.ROUTER_SIGMOID, 512, 8, lib.SHARED_SIGMOID_GATE, True),
+    (lib.ROUTER_SIGMOID_GROUPED, 256, 8, lib.SHARED_ONE, False),
+]
+
+
+@pytest.mark.parametrize("kind,E,K,shared,norm", CASES)
+@pytest.mark.parametrize("T", [1, 3, 8])
+def test_one_launch_matches_three_launches_bit_for_bit(kind, E, K, shared, norm, T):
+    H, I = 1024, 512
+    layer = _layer(E, H, I, kind, shared, norm, seed=1000 + 10 * kind + E + K)
+    x = synth.activations(T, H, torch.Generator(device=DEV).manual_seed(77 + T), DEV)
+    one = Engine(0, max_tokens=16, hidden=H, inter=I, experts=E, topk=K)
+    three = Engine(0, max_tokens=16, hidden=H, inter=I, experts=E, topk=K, flags=FLAG_SPLIT)
+    o1, w1, i1, k1, xin = _run(one, layer, x, K)
+    o3, w3, i3, k3, _ = _run(three, layer, x, K)
+    assert "route_plan_quant" in k1 and "router_topk" not in k1 and "plan" not in k1 and "gather_rows" not in k1
+    assert "route_plan_quant" not in k3 and "router_topk" in k3 and "plan" in k3
+    assert torch.equal(i1, i3)
+    assert torch.equal(w1.view(torch.int32), w3.view(torch.int32))
+    assert torch.equal(o1.view(torch.int16), o3.view(torch.int16))
+    # a second call on the same handle (workspace reused) gives the same bits
+    o1b = one.forward(layer, x, K)
+    one.sync()
+    assert torch.equal(o1.view(torch.int16), o1b.view(torch.int16))
+    if T == 3:
+        r = layer.router
+        logits = oracle.router_logits(adapter.bits(xin), adapter.bits(r.weight))
+        bias = None if r.bias is None else r.bias.cpu().numpy()
+        want, _ = oracle.route(kind, logits, K, bias, r.n_groups, r.topk_groups, r.route_scale)
+        assert [set(v) for v in i1.cpu().numpy().tolist()] == [set(v) for v in want.tolist()]
+        ref = adapter.from_layer(layer).forward(adapter.bits(xin), i1.cpu().numpy(), w1.cpu().numpy())
+        err = oracle.max_rel_error(oracle.bf16_to_f32(adapter.bits(o1)), oracle.bf16_to_f32(ref))
+        assert err <= TOL
+    one.ctx.close()
+    three.ctx.close()
+
+
+@pytest.mark.parametrize("B", [1, 8])
+def test_config1_small_batches_replayed_match_three_launches(B):
+    """The config-1 layer (H 2048, 512 experts of I 512 + shared, top-10) at
+    batch 1 and 8 through Engine.replay (a captured CUDA graph): the same
+    bits as the three-launch path, and within the tolerance of the oracle."""
+    wl = synth.config(1, device=DEV, batch=B)
+    layer, K = wl.layer, wl.K
+    one = Engine(0, max_tokens=64, hidden=2048, inter=512, experts=512, topk=K)
+    three = Engine(0, max_tokens=64, hidden=2048, inter=512, experts=512, topk=K, flags=FLAG_SPLIT)
+    for call in range(3):
+        x = synth.activations(B, 2048, torch.Generator(device=DEV).manual_seed(900 + call), DEV)
+        got = one.replay(layer, x, K)
+        want, (w, idx) = three.forward(layer, x, K, return_routes=True)
+        torch.cuda.synchronize()
+        assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    ref = adapter.from_layer(layer).forward(adapter.bits(x), idx.cpu().numpy(), w.cpu().numpy())
+    err = oracle.max_rel_error(oracle.bf16_to_f32(adapter.bits(got)), oracle.bf16_to_f32(ref))
+    assert err <= TOL
+    one.ctx.close()
+    three.ctx.close()

@@ -47,6 +47,8 @@
 
 #include "wm_bs_common.cuh"
 #include "wm_kernels.h"
+#include "wm_plan.cuh"
+#include "wm_route.cuh"
 
 namespace wm {
 
@@ -102,6 +104,42 @@ __device__ __forceinline__ uint32_t bs_idesc(uint32_t kk) {
          (kk << 29);
 }
 
+// One 32-value block of a token row -> its hi / lo E4M3 parts and UE8M0
+// bytes, stored into the tile image of sorted row r (tile j = r / 16, row n =
+// r % 16, stage s = g / 4, block kk = g % 4 of the stage).
+__device__ __forceinline__ void store_block(uint8_t* __restrict__ img, int S, int r, int g, const uint32_t* hi,
+                                            const uint32_t* lo, uint32_t bh, uint32_t bl) {
+  const int j = r / kTokTile, n = r % kTokTile;
+  const int s = g / 4, kk = g % 4;
+  uint8_t* base = img + (int64_t(j) * S + s) * kImage;
+  *reinterpret_cast<uint4*>(base + image_off(n, 2 * kk)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  *reinterpret_cast<uint4*>(base + image_off(n, 2 * kk + 1)) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+  *reinterpret_cast<uint4*>(base + image_off(kTokTile + n, 2 * kk)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+  *reinterpret_cast<uint4*>(base + image_off(kTokTile + n, 2 * kk + 1)) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+  uint8_t* sa = base + kBSmem;
+  sa[n * 16 + kk] = uint8_t(bh);
+  sa[(kTokTile + n) * 16 + kk] = uint8_t(bl);
+}
+
+// Block g (32 values) of bf16 row `src` -> hi / lo parts.
+__device__ __forceinline__ void split_row_block(const uint16_t* __restrict__ src, int g, uint32_t* hi, uint32_t* lo,
+                                                uint32_t* bh, uint32_t* bl) {
+  float v[32];
+  const uint4* s4 = reinterpret_cast<const uint4*>(src + g * 32);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 u = s4[q];
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack_bf16x2(w[i]);
+      v[8 * q + 2 * i] = f.x;
+      v[8 * q + 2 * i + 1] = f.y;
+    }
+  }
+  split_block(v, hi, lo, bh, bl);
+}
+
 }  // namespace
 
 // x rows (sorted by the plan, 16-row tiles) -> tile images: for tile j and
@@ -118,37 +156,54 @@ __global__ void __launch_bounds__(256) bs_quant_rows_kernel(const uint16_t* __re
   for (int r = blockIdx.x * 8 + (threadIdx.x >> 5); r < rows; r += gridDim.x * 8) {
     const int t = p.row_token[r];
     if (t < 0) continue;
-    const int j = r / kTokTile, n = r % kTokTile;
     const uint16_t* src = x + int64_t(t) * K;
     for (int g = lane; g < K / 32; g += 32) {
-      float v[32];
-      const uint4* s4 = reinterpret_cast<const uint4*>(src + g * 32);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint4 u = s4[q];
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = unpack_bf16x2(w[i]);
-          v[8 * q + 2 * i] = f.x;
-          v[8 * q + 2 * i + 1] = f.y;
-        }
-      }
       uint32_t hi[8], lo[8], bh, bl;
-      split_block(v, hi, lo, &bh, &bl);
-      const int s = g / 4, kk = g % 4;
-      uint8_t* base = img + (int64_t(j) * S + s) * kImage;
-      uint4* h0 = reinterpret_cast<uint4*>(base + image_off(n, 2 * kk));
-      uint4* h1 = reinterpret_cast<uint4*>(base + image_off(n, 2 * kk + 1));
-      uint4* l0 = reinterpret_cast<uint4*>(base + image_off(kTokTile + n, 2 * kk));
-      uint4* l1 = reinterpret_cast<uint4*>(base + image_off(kTokTile + n, 2 * kk + 1));
-      *h0 = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-      *h1 = make_uint4(hi[4], hi[5], hi[6], hi[7]);
-      *l0 = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-      *l1 = make_uint4(lo[4], lo[5], lo[6], lo[7]);
-      uint8_t* sa = base + kBSmem;
-      sa[n * 16 + kk] = uint8_t(bh);
-      sa[(kTokTile + n) * 16 + kk] = uint8_t(bl);
+      split_row_block(src, g, hi, lo, &bh, &bl);
+      store_block(img, S, r, g, hi, lo, bh, bl);
+    }
+  }
+}
+
+// Small router calls (T <= kSmallCallTokens tokens) in one launch of T
+// blocks.  Every block selects the top-k of every token (warp t, the top-k
+// kernel's own code) and forms the plan of the sorted rows (groups padded to
+// 16 rows) in shared memory -- both are short, so repeating them costs no
+// time -- then block t quantises token t: each 32-value block of the row is
+// split into hi / lo parts once and stored to every sorted row that holds the
+// token (its K pairs and the shared expert's row).  Block 0 also writes the
+// routes and the plan arrays.  The routes, plan and images are the bytes the
+// top-k, plan and quantise kernels write one after another.
+template <int EPL>
+__global__ void __launch_bounds__(kSmallCallThreads) bs_route_plan_quant_kernel(
+    const float* __restrict__ logits, int T, int E, const TopkArgs tk, int has_shared, Plan p, int max_rows,
+    int max_mtiles, uint32_t* status, const uint16_t* __restrict__ x, int H, uint8_t* __restrict__ img) {
+  __shared__ SmallPlan sp;
+  __shared__ float sw[kMaxSmallPairs];
+  const int warp = threadIdx.x >> 5;
+  const bool lead = blockIdx.x == 0;
+  if (warp < T) {
+    TopkArgs st = tk;
+    st.idx = sp.ids;
+    st.w = sw;
+    topk_token<EPL>(logits + int64_t(warp) * E, st, E, warp, threadIdx.x & 31, lead ? tk.idx : nullptr,
+                    lead ? tk.w : nullptr);
+  }
+  __syncthreads();
+  small_plan_block(sp, T, tk.K, E, has_shared, kTokTile, p, max_rows, max_mtiles, status, lead);
+  __syncthreads();
+  if (sp.total > max_rows) return;  // reported by block 0
+  const int t = blockIdx.x, K = tk.K, blocks = H / 32, S = H / kBK;
+  const int nrows = K + (has_shared ? 1 : 0);
+  const int split = max(1, min(nrows, int(blockDim.x) / blocks));  // threads sharing one value block's rows
+  const uint16_t* src = x + int64_t(t) * H;
+  for (int q = threadIdx.x; q < blocks * split; q += blockDim.x) {
+    const int g = q % blocks, part = q / blocks;
+    uint32_t hi[8], lo[8], bh, bl;
+    split_row_block(src, g, hi, lo, &bh, &bl);
+    for (int k = part; k < nrows; k += split) {
+      const int r = k < K ? sp.pos[t * K + k] : sp.shared_row0 + t;
+      if (r >= 0) store_block(img, S, r, g, hi, lo, bh, bl);
     }
   }
 }
@@ -470,6 +525,22 @@ bool bs_shape_ok(int H, int I) { return H % 512 == 0 && I % 512 == 0 && H >= 512
 void launch_bs_quant_rows(const uint16_t* x, const Plan& p, int E, int K, uint8_t* img, int num_sms,
                           cudaStream_t stream) {
   bs_quant_rows_kernel<<<num_sms * 4, 256, 0, stream>>>(x, p, E, K, img);
+}
+
+bool bs_route_plan_quant_ok(int T, int K, int E) {
+  return T >= 1 && T <= kSmallCallTokens && T <= kMaxSmallTokens && K >= 1 && T * K <= kMaxSmallPairs &&
+         T * K <= kSmallCallThreads && E <= kMaxSmallExperts;
+}
+
+void launch_bs_route_plan_quant(const float* logits, int T, int E, const TopkArgs& tk, bool has_shared, const Plan& p,
+                                int max_rows, int max_mtiles, uint32_t* status, const uint16_t* x, int H,
+                                uint8_t* img, cudaStream_t stream) {
+  if (E <= 256)
+    bs_route_plan_quant_kernel<8><<<T, kSmallCallThreads, 0, stream>>>(logits, T, E, tk, has_shared ? 1 : 0, p,
+                                                                       max_rows, max_mtiles, status, x, H, img);
+  else
+    bs_route_plan_quant_kernel<16><<<T, kSmallCallThreads, 0, stream>>>(logits, T, E, tk, has_shared ? 1 : 0, p,
+                                                                        max_rows, max_mtiles, status, x, H, img);
 }
 
 void launch_bs_decode(const BsArgs& args, int kind, const void* const* maps, int num_sms, cudaStream_t stream) {

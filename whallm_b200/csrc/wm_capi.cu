@@ -203,7 +203,10 @@ bool encode_2d_bf16(wm_ctx* ctx, CUtensorMap* map, const void* base, int cols, i
 // With a norm weight the router sees the normalised rows, which it leaves in
 // norm_rows: short calls normalise inside the logits kernel, long calls (and
 // shapes that kernel does not take) run the RMSNorm kernel first.
-int run_router(wm_ctx* ctx, const wm_moe_args* a, float* logits, int32_t* idx, float* w, cudaStream_t s) {
+// With select false only the logits (and the shared gate) are computed: the
+// caller runs the selection itself (the small-call kernel).
+int run_router(wm_ctx* ctx, const wm_moe_args* a, float* logits, int32_t* idx, float* w, cudaStream_t s,
+               bool select = true) {
   const wm::TopkArgs tk{a->router_bias, a->K, a->router, a->n_groups, a->topk_groups, a->route_scale, idx, w};
   const uint16_t* sg_w =
       a->shared_gate == WM_SHARED_SIGMOID_GATE ? static_cast<const uint16_t*>(a->shared_gate_weight) : nullptr;
@@ -231,10 +234,12 @@ int run_router(wm_ctx* ctx, const wm_moe_args* a, float* logits, int32_t* idx, f
                              a->norm_eps, fused ? norm_rows(ctx, a) : nullptr);
   }
   wm::prof_end(&ctx->prof, wm::kProfRouter, s);
+  ctx->counters.launches += 1;
+  if (!select) return check_launch(ctx, "router");
   wm::prof_begin(&ctx->prof, wm::kProfTopk, s);
   wm::launch_router_topk(logits, a->T, a->E, tk, s);
   wm::prof_end(&ctx->prof, wm::kProfTopk, s);
-  ctx->counters.launches += 2;
+  ctx->counters.launches += 1;
   return check_launch(ctx, "router");
 }
 
@@ -483,7 +488,7 @@ bool encode_scale_rows(wm_ctx* ctx, CUtensorMap* map, const void* base, int64_t 
 // The block-scaled decode path: hi / lo E4M3 token tiles, gate/up (+SwiGLU,
 // act tiles), down.  The plan's groups are padded to 16 rows.
 int run_bs_decode(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts, bool has_shared, cudaStream_t s,
-                  const wm::EpReturn* ret) {
+                  const wm::EpReturn* ret, bool images_ready) {
   const int H = a->H, I = a->I;
   CUtensorMap w13, w13s, w2, w2s, s13, s13s, s2, s2s;
   bool ok = encode_fp4_weights(ctx, &w13, a->w13.weight, H, 2 * I, a->E, a->w13.weight_stride, 64, 2) &&
@@ -508,9 +513,12 @@ int run_bs_decode(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wt
   b.status = ctx->status;
   b.act_img = aimg;
   b.routed = ctx->routed;
-  wm::prof_begin(&ctx->prof, wm::kProfGather, s);
-  wm::launch_bs_quant_rows(static_cast<const uint16_t*>(a->x), b.plan, a->E, H, ximg, ctx->num_sms, s);
-  wm::prof_end(&ctx->prof, wm::kProfGather, s);
+  if (!images_ready) {
+    wm::prof_begin(&ctx->prof, wm::kProfGather, s);
+    wm::launch_bs_quant_rows(static_cast<const uint16_t*>(a->x), b.plan, a->E, H, ximg, ctx->num_sms, s);
+    wm::prof_end(&ctx->prof, wm::kProfGather, s);
+    ctx->counters.launches += 1;
+  }
   b.img = ximg;
   wm::prof_begin(&ctx->prof, wm::kProfDecodeGateUp, s);
   const void* maps0[4] = {&w13, has_shared ? &w13s : &w13, &s13, has_shared ? &s13s : &s13};
@@ -522,7 +530,7 @@ int run_bs_decode(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wt
   const void* maps1[4] = {&w2, has_shared ? &w2s : &w2, &s2, has_shared ? &s2s : &s2};
   wm::launch_bs_decode(b, 1, maps1, ctx->num_sms, s);
   wm::prof_end(&ctx->prof, wm::kProfDecodeDown, s);
-  ctx->counters.launches += 3;
+  ctx->counters.launches += 2;
   ctx->counters.decode_calls += 1;
   return check_launch(ctx, "block-scaled expert decode");
 }
@@ -632,11 +640,11 @@ int run_bs_gemm(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wts,
 // with `ret`, the down rows stored straight into the senders' back blocks:
 // the grouped GEMMs and the block-scaled decode path only).
 int run_experts(wm_ctx* ctx, const wm_moe_args* a, bool has_shared, Path path, cudaStream_t s,
-                const wm::EpReturn* ret = nullptr, const XRows* xr = nullptr) {
+                const wm::EpReturn* ret = nullptr, const XRows* xr = nullptr, bool images_ready = false) {
   const wm::ExpertWeights wts = weights_of(a, has_shared);
   const int gate_first = a->layout == WM_LAYOUT_QWEN_GATE_UP_MXFP4 ? 1 : 0;
   if (path == kPathDecodeMma) return run_decode_mma(ctx, a, wts, s);
-  if (path == kPathBsDecode) return run_bs_decode(ctx, a, wts, has_shared, s, ret);
+  if (path == kPathBsDecode) return run_bs_decode(ctx, a, wts, has_shared, s, ret, images_ready);
   if (path == kPathBsGemm || path == kPathFp8Gemm)
     return run_bs_gemm(ctx, a, wts, has_shared, s, ret, xr ? *xr : XRows{a->T, nullptr, 0}, path == kPathFp8Gemm);
   if (path == kPathGemv) {
@@ -729,7 +737,8 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
     return nullptr;
   }
   wm_options o = *options;
-  if (o.flags & ~int32_t(WM_FLAG_SKIP_NEGATIVE_ROUTES | WM_FLAG_MMA_DECODE | WM_FLAG_F16_GEMM)) {
+  if (o.flags & ~int32_t(WM_FLAG_SKIP_NEGATIVE_ROUTES | WM_FLAG_MMA_DECODE | WM_FLAG_F16_GEMM |
+                        WM_FLAG_SPLIT_SMALL_CALLS)) {
     report("unknown flags");
     return nullptr;
   }
@@ -1346,12 +1355,25 @@ WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* args, void* stream)
   const int32_t* idx;
   const float* w;
   const int align = plan_align(path);
+  // Small router calls on the block-scaled decode path select, plan and
+  // quantise the token rows in one launch after the logits.
+  const bool small = a->router_weight != nullptr && path == kPathBsDecode &&
+                     !(ctx->opt.flags & WM_FLAG_SPLIT_SMALL_CALLS) && wm::bs_route_plan_quant_ok(a->T, a->K, a->E);
   if (a->router_weight != nullptr) {
     int32_t* di = a->out_idx ? a->out_idx : ctx->idx;
     float* dw = a->out_w ? a->out_w : ctx->w;
-    if (int rc = run_router(ctx, args, ctx->logits, di, dw, s)) return rc;
+    if (int rc = run_router(ctx, args, ctx->logits, di, dw, s, !small)) return rc;
     idx = di;
     w = dw;
+    if (small) {
+      const wm::TopkArgs tk{a->router_bias, a->K, a->router, a->n_groups, a->topk_groups, a->route_scale, di, dw};
+      wm::prof_begin(&ctx->prof, wm::kProfRoutePlanQuant, s);
+      wm::launch_bs_route_plan_quant(ctx->logits, a->T, a->E, tk, has_shared, plan, ctx->max_rows, ctx->max_mtiles,
+                                     ctx->status, static_cast<const uint16_t*>(a->x), a->H, ctx->bs_img_x, s);
+      wm::prof_end(&ctx->prof, wm::kProfRoutePlanQuant, s);
+      ctx->counters.launches += 1;
+      if (int rc = check_launch(ctx, "route, plan and quantise")) return rc;
+    }
   } else {
     idx = a->routes_idx;
     w = a->routes_w;
@@ -1361,14 +1383,16 @@ WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* args, void* stream)
       ctx->counters.launches += 1;
     }
   }
-  int launches = 0;
-  wm::prof_begin(&ctx->prof, wm::kProfPlan, s);
-  wm::launch_plan(idx, a->T, a->K, a->E, has_shared, align, plan, ctx->max_rows, ctx->max_mtiles, ctx->max_chunks,
-                  ctx->status, s, &launches);
-  wm::prof_end(&ctx->prof, wm::kProfPlan, s);
-  ctx->counters.launches += launches;
-  if (int rc = check_launch(ctx, "plan")) return rc;
-  if (int rc = run_experts(ctx, a, has_shared, path, s)) return rc;
+  if (!small) {
+    int launches = 0;
+    wm::prof_begin(&ctx->prof, wm::kProfPlan, s);
+    wm::launch_plan(idx, a->T, a->K, a->E, has_shared, align, plan, ctx->max_rows, ctx->max_mtiles, ctx->max_chunks,
+                    ctx->status, s, &launches);
+    wm::prof_end(&ctx->prof, wm::kProfPlan, s);
+    ctx->counters.launches += launches;
+    if (int rc = check_launch(ctx, "plan")) return rc;
+  }
+  if (int rc = run_experts(ctx, a, has_shared, path, s, nullptr, nullptr, small)) return rc;
   wm::prof_begin(&ctx->prof, wm::kProfCombine, s);
   wm::launch_combine(ctx->routed, ctx->plan, w, ctx->sg, a->shared_gate, a->T, a->H, a->E, a->K,
                      static_cast<uint16_t*>(a->out), s);

@@ -31,6 +31,7 @@ enum ProfSlot : int {
   kProfEpWaitDispatch,  // waiting for every peer's rows
   kProfEpReturn,        // result rows back to their senders
   kProfEpWaitReturn,    // waiting for every peer's result rows
+  kProfRoutePlanQuant,  // small router calls: top-k, plan and token images in one launch
   kProfSlots
 };
 struct Profiler;  // defined in wm_profile.cu
@@ -216,6 +217,16 @@ bool bs_shape_ok(int H, int I);
 // x rows (through the plan, 16-row tiles) -> hi / lo E4M3 tile images and scale atoms
 void launch_bs_quant_rows(const uint16_t* x, const Plan& p, int E, int K, uint8_t* img, int num_sms,
                           cudaStream_t stream);
+// Small router calls on the block-scaled decode path: top-k, plan (groups
+// padded to 16 rows) and the token images in one launch of T blocks; the same
+// routes, plan and images as launch_router_topk + launch_plan +
+// launch_bs_quant_rows.  For T <= kSmallCallTokens, T * K <= 128, E <= 512.
+constexpr int kSmallCallTokens = 8;
+constexpr int kSmallCallThreads = 512;
+bool bs_route_plan_quant_ok(int T, int K, int E);
+void launch_bs_route_plan_quant(const float* logits, int T, int E, const TopkArgs& tk, bool has_shared, const Plan& p,
+                                int max_rows, int max_mtiles, uint32_t* status, const uint16_t* x, int H,
+                                uint8_t* img, cudaStream_t stream);
 // maps[0..3]: CUtensorMaps of the routed and the shared expert's packed weights
 // (16U4_ALIGN16B, 128-byte swizzle; gate/up 4-D [E][2][I][H] with boxes
 // 128 x 64 x 2, down 3-D [E][H][I] with boxes 128 x 128) and of their E8M0

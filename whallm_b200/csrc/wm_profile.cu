@@ -67,7 +67,8 @@ const char* prof_name(int slot) {
   static const char* names[kProfSlots] = {"router_logits", "router_topk", "plan",     "act_f16",     "gather_rows",
                                           "gemv_gate_up",  "gemv_down",   "gemm_gate_up", "gemm_down", "combine",
                                           "decode_gate_up", "decode_down", "rmsnorm",
-                                          "ep_send", "ep_wait_dispatch", "ep_return", "ep_wait_return"};
+                                          "ep_send", "ep_wait_dispatch", "ep_return", "ep_wait_return",
+                                          "route_plan_quant"};
   return slot >= 0 && slot < kProfSlots ? names[slot] : "?";
 }
 

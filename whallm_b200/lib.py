@@ -22,6 +22,7 @@ SHARED_NONE, SHARED_SIGMOID_GATE, SHARED_ONE = 0, 1, 2
 FLAG_SKIP_NEGATIVE_ROUTES = 1
 FLAG_MMA_DECODE = 4
 FLAG_F16_GEMM = 8
+FLAG_SPLIT_SMALL_CALLS = 16
 
 # Every entry point the header declares (checked by the CPU test suite).
 EXPORTS = (
