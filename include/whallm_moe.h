@@ -141,7 +141,7 @@ typedef struct {
    multiples of 512 and the block-scaled decode kernel's alignment needs. */
 #define WM_FLAG_F16_GEMM 8
 
-/* Small router calls (T <= 8, T * K <= 128, E <= 512) on the block-scaled
+/* Small router calls (T <= 4, T * K <= 128, E <= 512) on the block-scaled
    decode path run the top-k, the plan and the token-row quantisation as three
    launches instead of one.  Both give the same routes, plan and output bits;
    the one launch saves two kernel boundaries per layer. */

@@ -1,4 +1,4 @@
-"""Small router calls (T <= 8) on the block-scaled decode path: the top-k,
+"""Small router calls (T <= 4) on the block-scaled decode path: the top-k,
 the plan and the token images in one launch (needs a B200).
 
 The one launch must give the same bits as the three launches it replaces
@@ -72,7 +72,7 @@ CASES = [
 
 
 @pytest.mark.parametrize("kind,E,K,shared,norm", CASES)
-@pytest.mark.parametrize("T", [1, 3, 8])
+@pytest.mark.parametrize("T", [1, 3, 4])
 def test_one_launch_matches_three_launches_bit_for_bit(kind, E, K, shared, norm, T):
     H, I = 1024, 512
     layer = _layer(E, H, I, kind, shared, norm, seed=1000 + 10 * kind + E + K)
@@ -103,10 +103,10 @@ def test_one_launch_matches_three_launches_bit_for_bit(kind, E, K, shared, norm,
     three.ctx.close()
 
 
-@pytest.mark.parametrize("B", [1, 8])
+@pytest.mark.parametrize("B", [1, 4])
 def test_config1_small_batches_replayed_match_three_launches(B):
     """The config-1 layer (H 2048, 512 experts of I 512 + shared, top-10) at
-    batch 1 and 8 through Engine.replay (a captured CUDA graph): the same
+    batch 1 and 4 through Engine.replay (a captured CUDA graph): the same
     bits as the three-launch path, and within the tolerance of the oracle."""
     wl = synth.config(1, device=DEV, batch=B)
     layer, K = wl.layer, wl.K
