@@ -1,12 +1,13 @@
-"""Small router calls (T <= 4) on the block-scaled decode path: the top-k,
-the plan and the token images in one launch (needs a B200).
+"""Calls of up to 64 tokens on the block-scaled decode path: the plan and the
+token images in one launch, and for router calls of up to 4 tokens the top-k
+in that launch too (needs a B200).
 
-The one launch must give the same bits as the three launches it replaces
-(top-k, plan, quantise; WM_FLAG_SPLIT_SMALL_CALLS keeps them): identical
-routes (indices and weights) and identical layer outputs, for every router
-kind, with and without the shared expert and the pre-MoE norm.  One case per
-router kind is also checked against the CPU oracle (max|y - y_ref| /
-max|y_ref| <= 1e-2, identical top-k sets)."""
+The one launch must give the same bits as the launches it replaces (top-k,
+plan, quantise; WM_FLAG_SPLIT_SMALL_CALLS keeps them): identical routes
+(indices and weights) and identical layer outputs, for every router kind,
+with and without the shared expert and the pre-MoE norm, and for given
+routes.  One case per router kind is also checked against the CPU oracle
+(max|y - y_ref| / max|y_ref| <= 1e-2, identical top-k sets)."""
 import pytest
 import torch
 
@@ -123,3 +124,49 @@ def test_config1_small_batches_replayed_match_three_launches(B):
     assert err <= TOL
     one.ctx.close()
     three.ctx.close()
+
+
+@pytest.mark.parametrize("kind,E,K,shared,norm", CASES[:1] + CASES[3:])
+@pytest.mark.parametrize("T", [5, 17, 64])
+def test_plan_and_images_in_one_launch_match_the_two_launches(kind, E, K, shared, norm, T):
+    """5 to 64 tokens: the top-k kernel, then the plan and the token images in
+    one launch -- the same bits as the plan and quantise kernels."""
+    H, I = 1024, 512
+    layer = _layer(E, H, I, kind, shared, norm, seed=2000 + 10 * kind + E + K)
+    x = synth.activations(T, H, torch.Generator(device=DEV).manual_seed(55 + T), DEV)
+    one = Engine(0, max_tokens=64, hidden=H, inter=I, experts=E, topk=K)
+    two = Engine(0, max_tokens=64, hidden=H, inter=I, experts=E, topk=K, flags=FLAG_SPLIT)
+    o1, w1, i1, k1, _ = _run(one, layer, x, K)
+    o2, w2, i2, k2, _ = _run(two, layer, x, K)
+    assert "route_plan_quant" in k1 and "router_topk" in k1 and "plan" not in k1 and "gather_rows" not in k1
+    assert "route_plan_quant" not in k2 and "plan" in k2 and "gather_rows" in k2
+    assert torch.equal(i1, i2) and torch.equal(w1.view(torch.int32), w2.view(torch.int32))
+    assert torch.equal(o1.view(torch.int16), o2.view(torch.int16))
+    one.ctx.close()
+    two.ctx.close()
+
+
+@pytest.mark.parametrize("T,K,E", [(64, 10, 512), (40, 8, 256), (3, 16, 64)])
+def test_given_routes_in_one_launch_match_the_two_launches(T, K, E):
+    """Caller-given routes (no router), an expert named by many tokens and by
+    none: the same bits as the plan and quantise kernels, and the oracle."""
+    H, I = 1024, 512
+    layer = _layer(E, H, I, lib.ROUTER_SOFTMAX, lib.SHARED_SIGMOID_GATE, False, seed=3000 + T)
+    g = torch.Generator(device=DEV).manual_seed(4000 + T)
+    x = synth.activations(T, H, g, DEV)
+    idx = torch.stack([torch.randperm(E, generator=g, device=DEV)[:K] for _ in range(T)]).to(torch.int32)
+    idx[:, 0] = 3  # every token names expert 3 (more than one 16-row tile at T > 16)
+    idx[:, 1] = torch.where(idx[:, 1] == 3, torch.full_like(idx[:, 1], 5), idx[:, 1])
+    w = torch.rand((T, K), generator=g, device=DEV)
+    one = Engine(0, max_tokens=64, hidden=H, inter=I, experts=E, topk=K)
+    two = Engine(0, max_tokens=64, hidden=H, inter=I, experts=E, topk=K, flags=FLAG_SPLIT)
+    got = one.forward(layer, x, K, routes=(w, idx))
+    want = two.forward(layer, x, K, routes=(w, idx))
+    one.sync()
+    two.sync()
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    ref = adapter.from_layer(layer).forward(adapter.bits(x), idx.cpu().numpy(), w.cpu().numpy())
+    err = oracle.max_rel_error(oracle.bf16_to_f32(adapter.bits(got)), oracle.bf16_to_f32(ref))
+    assert err <= TOL
+    one.ctx.close()
+    two.ctx.close()

@@ -165,29 +165,35 @@ __global__ void __launch_bounds__(256) bs_quant_rows_kernel(const uint16_t* __re
   }
 }
 
-// Small router calls (T <= kSmallCallTokens tokens) in one launch of T
-// blocks.  Every block selects the top-k of every token (warp t, the top-k
-// kernel's own code) and forms the plan of the sorted rows (groups padded to
-// 16 rows) in shared memory -- both are short, so repeating them costs no
-// time -- then block t quantises token t: each 32-value block of the row is
-// split into hi / lo parts once and stored to every sorted row that holds the
-// token (its K pairs and the shared expert's row).  Block 0 also writes the
-// routes and the plan arrays.  The routes, plan and images are the bytes the
-// top-k, plan and quantise kernels write one after another.
+// Calls of up to 64 tokens in one launch of T blocks.  Every block forms the
+// plan of the sorted rows (groups padded to 16 rows) in shared memory -- for
+// router calls of up to kSmallCallTokens tokens (EPL > 0) after selecting the
+// top-k of every token itself (warp t, the top-k kernel's own code), else
+// from the given routes -- which is short, so repeating it in every block
+// costs no time; then block t quantises token t: each 32-value block of the
+// row is split into hi / lo parts once and stored to every sorted row that
+// holds the token (its K pairs and the shared expert's row).  Block 0 also
+// writes the routes and the plan arrays.  The routes, plan and images are the
+// bytes the top-k, plan and quantise kernels write one after another.
 template <int EPL>
 __global__ void __launch_bounds__(kSmallCallThreads) bs_route_plan_quant_kernel(
-    const float* __restrict__ logits, int T, int E, const TopkArgs tk, int has_shared, Plan p, int max_rows,
-    int max_mtiles, uint32_t* status, const uint16_t* __restrict__ x, int H, uint8_t* __restrict__ img) {
+    const float* __restrict__ logits, const int32_t* __restrict__ routes, int T, int E, const TopkArgs tk,
+    int has_shared, Plan p, int max_rows, int max_mtiles, uint32_t* status, const uint16_t* __restrict__ x, int H,
+    uint8_t* __restrict__ img) {
   __shared__ SmallPlan sp;
-  __shared__ float sw[kMaxSmallPairs];
   const int warp = threadIdx.x >> 5;
   const bool lead = blockIdx.x == 0;
-  if (warp < T) {
-    TopkArgs st = tk;
-    st.idx = sp.ids;
-    st.w = sw;
-    topk_token<EPL>(logits + int64_t(warp) * E, st, E, warp, threadIdx.x & 31, lead ? tk.idx : nullptr,
-                    lead ? tk.w : nullptr);
+  if constexpr (EPL > 0) {
+    __shared__ float sw[kSmallCallTokens * 32];
+    if (warp < T) {
+      TopkArgs st = tk;
+      st.idx = sp.ids;
+      st.w = sw;
+      topk_token<EPL>(logits + int64_t(warp) * E, st, E, warp, threadIdx.x & 31, lead ? tk.idx : nullptr,
+                      lead ? tk.w : nullptr);
+    }
+  } else {
+    for (int i = threadIdx.x; i < T * tk.K; i += blockDim.x) sp.ids[i] = routes[i];
   }
   __syncthreads();
   small_plan_block(sp, T, tk.K, E, has_shared, kTokTile, p, max_rows, max_mtiles, status, lead);
@@ -527,20 +533,32 @@ void launch_bs_quant_rows(const uint16_t* x, const Plan& p, int E, int K, uint8_
   bs_quant_rows_kernel<<<num_sms * 4, 256, 0, stream>>>(x, p, E, K, img);
 }
 
+bool bs_plan_quant_ok(int T, int K, int E) {
+  return T >= 1 && T <= kMaxSmallTokens && K >= 1 && T * K <= kMaxSmallPairs && E <= kMaxSmallExperts;
+}
+
 bool bs_route_plan_quant_ok(int T, int K, int E) {
-  return T >= 1 && T <= kSmallCallTokens && T <= kMaxSmallTokens && K >= 1 && T * K <= kMaxSmallPairs &&
-         T * K <= kSmallCallThreads && E <= kMaxSmallExperts;
+  return bs_plan_quant_ok(T, K, E) && T <= kSmallCallTokens && K <= 32;
 }
 
 void launch_bs_route_plan_quant(const float* logits, int T, int E, const TopkArgs& tk, bool has_shared, const Plan& p,
                                 int max_rows, int max_mtiles, uint32_t* status, const uint16_t* x, int H,
                                 uint8_t* img, cudaStream_t stream) {
   if (E <= 256)
-    bs_route_plan_quant_kernel<8><<<T, kSmallCallThreads, 0, stream>>>(logits, T, E, tk, has_shared ? 1 : 0, p,
-                                                                       max_rows, max_mtiles, status, x, H, img);
+    bs_route_plan_quant_kernel<8><<<T, kSmallCallThreads, 0, stream>>>(
+        logits, nullptr, T, E, tk, has_shared ? 1 : 0, p, max_rows, max_mtiles, status, x, H, img);
   else
-    bs_route_plan_quant_kernel<16><<<T, kSmallCallThreads, 0, stream>>>(logits, T, E, tk, has_shared ? 1 : 0, p,
-                                                                        max_rows, max_mtiles, status, x, H, img);
+    bs_route_plan_quant_kernel<16><<<T, kSmallCallThreads, 0, stream>>>(
+        logits, nullptr, T, E, tk, has_shared ? 1 : 0, p, max_rows, max_mtiles, status, x, H, img);
+}
+
+void launch_bs_plan_quant(const int32_t* routes, int T, int K, int E, bool has_shared, const Plan& p, int max_rows,
+                          int max_mtiles, uint32_t* status, const uint16_t* x, int H, uint8_t* img,
+                          cudaStream_t stream) {
+  TopkArgs tk{};
+  tk.K = K;
+  bs_route_plan_quant_kernel<0><<<T, kSmallCallThreads, 0, stream>>>(
+      nullptr, routes, T, E, tk, has_shared ? 1 : 0, p, max_rows, max_mtiles, status, x, H, img);
 }
 
 void launch_bs_decode(const BsArgs& args, int kind, const void* const* maps, int num_sms, cudaStream_t stream) {

@@ -1383,7 +1383,18 @@ WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* args, void* stream)
       ctx->counters.launches += 1;
     }
   }
-  if (!small) {
+  // Calls of up to 64 tokens (after the top-k or with given routes) plan and
+  // quantise the token rows in one launch.
+  const bool mid = !small && path == kPathBsDecode && !(ctx->opt.flags & WM_FLAG_SPLIT_SMALL_CALLS) &&
+                   wm::bs_plan_quant_ok(a->T, a->K, a->E);
+  if (mid) {
+    wm::prof_begin(&ctx->prof, wm::kProfRoutePlanQuant, s);
+    wm::launch_bs_plan_quant(idx, a->T, a->K, a->E, has_shared, plan, ctx->max_rows, ctx->max_mtiles, ctx->status,
+                             static_cast<const uint16_t*>(a->x), a->H, ctx->bs_img_x, s);
+    wm::prof_end(&ctx->prof, wm::kProfRoutePlanQuant, s);
+    ctx->counters.launches += 1;
+    if (int rc = check_launch(ctx, "plan and quantise")) return rc;
+  } else if (!small) {
     int launches = 0;
     wm::prof_begin(&ctx->prof, wm::kProfPlan, s);
     wm::launch_plan(idx, a->T, a->K, a->E, has_shared, align, plan, ctx->max_rows, ctx->max_mtiles, ctx->max_chunks,
@@ -1392,7 +1403,7 @@ WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* args, void* stream)
     ctx->counters.launches += launches;
     if (int rc = check_launch(ctx, "plan")) return rc;
   }
-  if (int rc = run_experts(ctx, a, has_shared, path, s, nullptr, nullptr, small)) return rc;
+  if (int rc = run_experts(ctx, a, has_shared, path, s, nullptr, nullptr, small || mid)) return rc;
   wm::prof_begin(&ctx->prof, wm::kProfCombine, s);
   wm::launch_combine(ctx->routed, ctx->plan, w, ctx->sg, a->shared_gate, a->T, a->H, a->E, a->K,
                      static_cast<uint16_t*>(a->out), s);

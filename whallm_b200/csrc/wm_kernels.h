@@ -217,13 +217,19 @@ bool bs_shape_ok(int H, int I);
 // x rows (through the plan, 16-row tiles) -> hi / lo E4M3 tile images and scale atoms
 void launch_bs_quant_rows(const uint16_t* x, const Plan& p, int E, int K, uint8_t* img, int num_sms,
                           cudaStream_t stream);
-// Small router calls on the block-scaled decode path: top-k, plan (groups
-// padded to 16 rows) and the token images in one launch of T blocks; the same
-// routes, plan and images as launch_router_topk + launch_plan +
-// launch_bs_quant_rows.  For T <= kSmallCallTokens, T * K <= 128, E <= 512.
+// Calls of up to 64 tokens on the block-scaled decode path: the plan (groups
+// padded to 16 rows) and the token images in one launch of T blocks, the same
+// plan and images as launch_plan + launch_bs_quant_rows (T <= 64, T * K <=
+// 1024, E <= 512).  Router calls of up to kSmallCallTokens tokens also select
+// the top-k in that launch (launch_bs_route_plan_quant: the routes of
+// launch_router_topk as well).
 constexpr int kSmallCallTokens = 4;  // measured: batch 1 -1.9 us, batch 8 +1.1 us per layer
 constexpr int kSmallCallThreads = 512;
+bool bs_plan_quant_ok(int T, int K, int E);
 bool bs_route_plan_quant_ok(int T, int K, int E);
+void launch_bs_plan_quant(const int32_t* routes, int T, int K, int E, bool has_shared, const Plan& p, int max_rows,
+                          int max_mtiles, uint32_t* status, const uint16_t* x, int H, uint8_t* img,
+                          cudaStream_t stream);
 void launch_bs_route_plan_quant(const float* logits, int T, int E, const TopkArgs& tk, bool has_shared, const Plan& p,
                                 int max_rows, int max_mtiles, uint32_t* status, const uint16_t* x, int H,
                                 uint8_t* img, cudaStream_t stream);
