@@ -118,9 +118,33 @@ __device__ void small_plan_block(SmallPlan& sp, int T, int K, int E, int has_sha
   __syncthreads();
   const int U = sp.n_u;
   const int n = U + 1;  // the distinct routed experts, then the shared expert
-  // padded rows and tiles of each distinct expert -> offsets and first tiles (block scan)
+  // padded rows and tiles of each distinct expert -> offsets and first tiles:
+  // one warp's scan when they fit it (no block barrier), else a block scan
   int carry_r = 0, carry_t = 0;
-  for (int b = 0; b < n; b += blockDim.x) {
+  if (n <= 32) {
+    if (warp == 0) {
+      const int c = lane < U ? sp.ucnt[lane] : (lane == U && has_shared ? T : 0);
+      const int rows = lane < n ? (c + align - 1) / align * align : 0;
+      const int tiles = lane < n ? (c + tile - 1) / tile : 0;
+      int rs = rows, ts = tiles;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int r2 = __shfl_up_sync(0xffffffffu, rs, o), t2 = __shfl_up_sync(0xffffffffu, ts, o);
+        if (lane >= o) {
+          rs += r2;
+          ts += t2;
+        }
+      }
+      if (lane < n) {
+        sp.uoff[lane] = rs - rows;
+        sp.utile[lane] = ts - tiles;
+        if (lane == U) sp.ucnt[U] = c;
+      }
+      carry_r = __shfl_sync(0xffffffffu, rs, 31);
+      carry_t = __shfl_sync(0xffffffffu, ts, 31);
+    }
+  }
+  for (int b = 0; n > 32 && b < n; b += blockDim.x) {
     const int u = b + threadIdx.x;
     const int c = u < U ? sp.ucnt[u] : (u == U && has_shared ? T : 0);
     const int rows = u < n ? (c + align - 1) / align * align : 0;
