@@ -44,6 +44,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "wm_bs_common.cuh"
 #include "wm_kernels.h"
@@ -180,7 +181,9 @@ __global__ void __launch_bounds__(kSmallCallThreads) bs_route_plan_quant_kernel(
     const float* __restrict__ logits, const int32_t* __restrict__ routes, int T, int E, const TopkArgs tk,
     int has_shared, Plan p, int max_rows, int max_mtiles, uint32_t* status, const uint16_t* __restrict__ x, int H,
     uint8_t* __restrict__ img) {
-  __shared__ SmallPlan sp;
+  using SP = typename std::conditional<(EPL > 0), SmallPlan<8, kSmallCallTokens * 32>,
+                                       SmallPlan<kMaxSmallTokens, kMaxSmallPairs>>::type;
+  __shared__ SP sp;
   const int warp = threadIdx.x >> 5;
   const bool lead = blockIdx.x == 0;
   if constexpr (EPL > 0) {

@@ -4,6 +4,8 @@
 // expert, the shared expert last).
 #pragma once
 
+#include <type_traits>
+
 #include "wm_kernels.h"
 
 namespace wm {
@@ -13,30 +15,51 @@ constexpr int kMaxSmallPairs = 1024;   // T * K of the calls small_plan_block ta
 constexpr int kMaxSmallTokens = 64;    // T of those calls (one bit per token)
 constexpr int kMaxSmallExperts = 512;
 
-// Shared-memory state of small_plan_block.  ids (the pairs' expert ids, in
-// (token, k) order) is the input; pos (each pair's sorted row, -1 for an id
-// outside [0, E)), shared_row0 and total are the results every block needs.
+// Shared-memory state of small_plan_block for calls of up to MAXT tokens and
+// MAXP pairs (the few-token form keeps a byte of token bits per expert and is
+// 6x smaller, which its one-block-per-token launch measured faster).  ids
+// (the pairs' expert ids, in (token, k) order) is the input; pos (each pair's
+// sorted row, -1 for an id outside [0, E)), shared_row0 and total are the
+// results every block needs.
+template <int MAXT, int MAXP>
 struct SmallPlan {
-  int ids[kMaxSmallPairs];
-  int pos[kMaxSmallPairs];
-  uint32_t used[kMaxSmallExperts / 32];        // bit e: some pair names expert e
-  int wpre[kMaxSmallExperts / 32];             // set bits in the words before
-  unsigned long long tmask[kMaxSmallExperts];  // bit t: token t names expert e
-  int ucnt[kMaxSmallExperts + 1];              // per distinct expert, ascending (the shared expert last)
-  int uexp[kMaxSmallExperts + 1];
-  int uoff[kMaxSmallExperts + 2];              // first sorted row; uoff[n_u + 1] = rows used
-  int utile[kMaxSmallExperts + 2];             // first tile
-  int wsum[2][32];                             // per-warp sums of the scan
-  int n_u;                                     // distinct routed experts
-  int repeated;                                // a token names an expert twice
-  int shared_row0;                             // first row of the shared expert (-1 without it)
-  int total;                                   // rows used
-};
+  static_assert(MAXT <= kMaxSmallTokens && MAXP <= kMaxSmallPairs, "small plan limits");
+  static constexpr int kMaxT = MAXT, kMaxP = MAXP;
+  static constexpr int kMaxU = MAXP < kMaxSmallExperts ? MAXP : kMaxSmallExperts;  // distinct experts
+  using Mask = typename std::conditional<(MAXT <= 8), uint32_t, unsigned long long>::type;
+  static constexpr int kMaskWords = MAXT <= 8 ? kMaxSmallExperts / 4 : kMaxSmallExperts;
+  int ids[MAXP];
+  int pos[MAXP];
+  uint32_t used[kMaxSmallExperts / 32];  // bit e: some pair names expert e
+  int wpre[kMaxSmallExperts / 32];       // set bits in the words before
+  Mask tmask[kMaskWords];                // the tokens that name expert e (a byte or a word per expert)
+  int ucnt[kMaxU + 1];                   // per distinct expert, ascending (the shared expert last)
+  int uexp[kMaxU + 1];
+  int uoff[kMaxU + 2];                   // first sorted row; uoff[n_u + 1] = rows used
+  int utile[kMaxU + 2];                  // first tile
+  int wsum[2][32];                       // per-warp sums of the scan
+  int n_u;                               // distinct routed experts
+  int repeated;                          // a token names an expert twice
+  int shared_row0;                       // first row of the shared expert (-1 without it)
+  int total;                             // rows used
 
-// Place of expert e among the distinct experts named (set bits below it).
-__device__ __forceinline__ int small_plan_slot(const SmallPlan& sp, int e) {
-  return sp.wpre[e >> 5] + __popc(sp.used[e >> 5] & ((1u << (e & 31)) - 1u));
-}
+  __device__ __forceinline__ void mark(int e, int t) {
+    if constexpr (MAXT <= 8)
+      atomicOr(&tmask[e >> 2], 1u << ((e & 3) * 8 + t));
+    else
+      atomicOr(&tmask[e], 1ull << t);
+  }
+  __device__ __forceinline__ unsigned long long tokens(int e) const {
+    if constexpr (MAXT <= 8)
+      return (tmask[e >> 2] >> ((e & 3) * 8)) & 0xFFu;
+    else
+      return tmask[e];
+  }
+  // Place of expert e among the distinct experts named (set bits below it).
+  __device__ __forceinline__ int slot(int e) const {
+    return wpre[e >> 5] + __popc(used[e >> 5] & ((1u << (e & 31)) - 1u));
+  }
+};
 
 // The plan of a call of T <= kMaxSmallTokens tokens, P = T * K <=
 // kMaxSmallPairs pairs and E <= kMaxSmallExperts experts: the same plan as
@@ -51,14 +74,15 @@ __device__ __forceinline__ int small_plan_slot(const SmallPlan& sp, int e) {
 // results are formed (a block that needs the rows but leaves the plan arrays
 // to another block).  Every thread of the block calls it; blockDim.x is a
 // multiple of 32 and at least 64.
-__device__ void small_plan_block(SmallPlan& sp, int T, int K, int E, int has_shared, int align, Plan p,
+template <class SP>
+__device__ void small_plan_block(SP& sp, int T, int K, int E, int has_shared, int align, Plan p,
                                  int max_rows, int max_mtiles, uint32_t* status, bool write) {
   const int P = T * K;
   const int tile = align > 1 ? align : (p.tile_rows > 0 ? p.tile_rows : 16);
   const int words = (E + 31) / 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-  for (int w = threadIdx.x; w < kMaxSmallExperts; w += blockDim.x) {
-    sp.tmask[w] = 0ull;
+  for (int w = threadIdx.x; w < SP::kMaskWords; w += blockDim.x) {
+    sp.tmask[w] = 0;
     if (w < kMaxSmallExperts / 32) sp.used[w] = 0u;
   }
   if (threadIdx.x == 0) sp.repeated = 0;
@@ -67,7 +91,7 @@ __device__ void small_plan_block(SmallPlan& sp, int T, int K, int E, int has_sha
     const int e = sp.ids[i], t = i / K;
     if (e >= 0 && e < E) {
       atomicOr(&sp.used[e >> 5], 1u << (e & 31));
-      atomicOr(&sp.tmask[e], 1ull << t);
+      sp.mark(e, t);
       for (int j = t * K; j < i; ++j)
         if (sp.ids[j] == e) sp.repeated = 1;
     } else if (write && (e >= 0 || !p.skip_negative)) {
@@ -98,7 +122,7 @@ __device__ void small_plan_block(SmallPlan& sp, int T, int K, int E, int has_sha
     }
     int rank = 0, cnt = 0;
     if (!rep) {
-      const unsigned long long tm = sp.tmask[e];
+      const unsigned long long tm = sp.tokens(e);
       rank = __popcll(tm & ((1ull << t) - 1ull));
       cnt = __popcll(tm);
     } else {
@@ -110,7 +134,7 @@ __device__ void small_plan_block(SmallPlan& sp, int T, int K, int E, int has_sha
     }
     sp.pos[i] = rank;
     if (rank == 0) {
-      const int slot = small_plan_slot(sp, e);
+      const int slot = sp.slot(e);
       sp.uexp[slot] = e;
       sp.ucnt[slot] = cnt;
     }
@@ -200,13 +224,13 @@ __device__ void small_plan_block(SmallPlan& sp, int T, int K, int E, int has_sha
   }
   __syncthreads();
   for (int i = threadIdx.x; i < P; i += blockDim.x)
-    if (sp.pos[i] >= 0) sp.pos[i] += sp.uoff[small_plan_slot(sp, sp.ids[i])];
+    if (sp.pos[i] >= 0) sp.pos[i] += sp.uoff[sp.slot(sp.ids[i])];
   if (!write) return;
   const int total = sp.total, n_tiles = sp.utile[U + 1];
   // per-expert arrays: an expert's place among the distinct ones from the bitmap
   for (int x = threadIdx.x; x <= E + 1; x += blockDim.x) {
     if (x < E) {
-      const int s = small_plan_slot(sp, x);
+      const int s = sp.slot(x);
       p.counts[x] = (sp.used[x >> 5] >> (x & 31)) & 1u ? sp.ucnt[s] : 0;
       p.offsets[x] = sp.uoff[s];
     } else if (x == E) {
