@@ -141,10 +141,11 @@ typedef struct {
    multiples of 512 and the block-scaled decode kernel's alignment needs. */
 #define WM_FLAG_F16_GEMM 8
 
-/* Small router calls (T <= 4, T * K <= 128, E <= 512) on the block-scaled
-   decode path run the top-k, the plan and the token-row quantisation as three
-   launches instead of one.  Both give the same routes, plan and output bits;
-   the one launch saves two kernel boundaries per layer. */
+/* Decode calls of up to 64 tokens (T * K <= 1024, E <= 512) on the
+   block-scaled decode path run the plan and the token-row quantisation -- and
+   router calls of up to 4 tokens the top-k too -- as separate launches
+   instead of one.  Both give the same routes, plan and output bits; the one
+   launch saves one or two kernel boundaries per layer. */
 #define WM_FLAG_SPLIT_SMALL_CALLS 16
 
 /* One projection of every expert: expert e's matrix at weight + e * weight_stride
