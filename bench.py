@@ -892,6 +892,11 @@ def run(args) -> None:
         e_ms = float(t.item())
     e2e = world * B * args.steps / (e_ms / 1e3)
 
+    del graph
+    # the small batches before the CPU baseline: its OpenMP threads keep
+    # spinning for a while after it returns, and a short step's time depends
+    # on the host enqueueing its launches promptly
+    decode_batches = [decode_batch_line(eng, layer, dev, b, max(10, min(args.steps, 30)), flush) for b in (1, 8)]
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         import oracle
@@ -908,8 +913,6 @@ def run(args) -> None:
         if not args.no_prefill:
             cpu["other_configs"] = cpu_baselines(dev, cores, threads)
 
-    del graph
-    decode_batches = [decode_batch_line(eng, layer, dev, b, max(10, min(args.steps, 30)), flush) for b in (1, 8)]
     prefill = None if args.no_prefill else prefill_section(args, dev, pk, 2)
     long_calls = None
     long_sections = {}
