@@ -170,3 +170,34 @@ def test_given_routes_in_one_launch_match_the_two_launches(T, K, E):
     assert err <= TOL
     one.ctx.close()
     two.ctx.close()
+
+
+@pytest.mark.parametrize("kind", [lib.ROUTER_SOFTMAX, lib.ROUTER_SQRTSOFTPLUS, lib.ROUTER_SIGMOID])
+@pytest.mark.parametrize("E,K", [(512, 10), (384, 8), (1024, 16), (256, 32), (128, 6)])
+def test_group_topk_of_short_calls_matches_the_one_warp_topk(kind, E, K):
+    """Calls of up to 64 tokens select with four warps per token; longer calls
+    with one warp per token.  The first 64 tokens of a 100-token call (one
+    warp per token, the same logits) must get the same routes, bit for bit,
+    as the same 64 tokens routed alone, and both the oracle's selection on
+    those logits."""
+    import numpy as np
+    H = 512
+    g = torch.Generator(device=DEV).manual_seed(6000 + E + K + kind)
+    w13, s13 = synth.mxfp4_projection(8, 128, H, g, DEV)
+    w2, s2 = synth.mxfp4_projection(8, H, 64, g, DEV)
+    wr = (torch.randn((E, H), generator=g, device=DEV) / H ** 0.5).to(torch.bfloat16)
+    bias = None if kind == lib.ROUTER_SOFTMAX else (0.1 * torch.randn((E,), generator=g, device=DEV))
+    layer = LayerWeights(lib.LAYOUT_QWEN_GATE_UP_MXFP4, H, 64, E, Projection.stacked(w13, s13),
+                         Projection.stacked(w2, s2), router=RouterWeights(wr, kind, bias, 1, 1, 1.5))
+    x = synth.activations(100, H, g, DEV)
+    eng = Engine(0, max_tokens=128, hidden=H, inter=64, experts=E, topk=K)
+    w_long, i_long, logits = eng.route(layer, x, K, with_logits=True)
+    w_short, i_short = eng.route(layer, x[:64].contiguous(), K)
+    eng.sync()
+    assert torch.equal(i_short, i_long[:64])
+    assert torch.equal(w_short.view(torch.int32), w_long[:64].view(torch.int32))
+    bn = None if bias is None else bias.cpu().numpy()
+    oi, ow = oracle.route(kind, logits.cpu().numpy(), K, bn, 1, 1, 1.5)
+    np.testing.assert_array_equal(i_long.cpu().numpy(), oi)
+    np.testing.assert_allclose(w_long.cpu().numpy(), ow, rtol=1e-5, atol=1e-7)
+    eng.ctx.close()

@@ -169,7 +169,8 @@ __global__ void __launch_bounds__(256) bs_quant_rows_kernel(const uint16_t* __re
 // Calls of up to 64 tokens in one launch of T blocks.  Every block forms the
 // plan of the sorted rows (groups padded to 16 rows) in shared memory -- for
 // router calls of up to kSmallCallTokens tokens (EPL > 0) after selecting the
-// top-k of every token itself (warp t, the top-k kernel's own code), else
+// top-k of every token itself (a group of four warps per token, the short-call
+// top-k kernel's own code), else
 // from the given routes -- which is short, so repeating it in every block
 // costs no time; then block t quantises token t: each 32-value block of the
 // row is split into hi / lo parts once and stored to every sorted row that
@@ -187,13 +188,18 @@ __global__ void __launch_bounds__(kSmallCallThreads) bs_route_plan_quant_kernel(
   const int warp = threadIdx.x >> 5;
   const bool lead = blockIdx.x == 0;
   if constexpr (EPL > 0) {
+    // token t: warps 4t .. 4t + 3 select from a quarter of the experts each,
+    // then warp 4t from their candidates
     __shared__ float sw[kSmallCallTokens * 32];
-    if (warp < T) {
+    __shared__ TopkCands cands[kSmallCallTokens];
+    const int tt = warp / kTopkGroupWarps, g = warp % kTopkGroupWarps;
+    if (tt < T) topk_group_local<EPL>(logits + int64_t(tt) * E, tk, E, g, threadIdx.x & 31, cands[tt]);
+    __syncthreads();
+    if (tt < T && g == 0) {
       TopkArgs st = tk;
       st.idx = sp.ids;
       st.w = sw;
-      topk_token<EPL>(logits + int64_t(warp) * E, st, E, warp, threadIdx.x & 31, lead ? tk.idx : nullptr,
-                      lead ? tk.w : nullptr);
+      topk_group_merge(cands[tt], st, tt, threadIdx.x & 31, lead ? tk.idx : nullptr, lead ? tk.w : nullptr);
     }
   } else {
     for (int i = threadIdx.x; i < T * tk.K; i += blockDim.x) sp.ids[i] = routes[i];
@@ -540,18 +546,20 @@ bool bs_plan_quant_ok(int T, int K, int E) {
   return T >= 1 && T <= kMaxSmallTokens && K >= 1 && T * K <= kMaxSmallPairs && E <= kMaxSmallExperts;
 }
 
-bool bs_route_plan_quant_ok(int T, int K, int E) {
-  return bs_plan_quant_ok(T, K, E) && T <= kSmallCallTokens && K <= 32;
+bool bs_route_plan_quant_ok(int T, int K, int E, int kind) {
+  static_assert(kSmallCallTokens * kTopkGroupWarps * 32 <= kSmallCallThreads, "a warp group per token");
+  return bs_plan_quant_ok(T, K, E) && T <= kSmallCallTokens && K <= kTopkGroupMaxK && E <= kTopkGroupWarps * 128 &&
+         kind != WM_ROUTER_SIGMOID_GROUPED;
 }
 
 void launch_bs_route_plan_quant(const float* logits, int T, int E, const TopkArgs& tk, bool has_shared, const Plan& p,
                                 int max_rows, int max_mtiles, uint32_t* status, const uint16_t* x, int H,
                                 uint8_t* img, cudaStream_t stream) {
-  if (E <= 256)
-    bs_route_plan_quant_kernel<8><<<T, kSmallCallThreads, 0, stream>>>(
+  if (E <= kTopkGroupWarps * 64)
+    bs_route_plan_quant_kernel<2><<<T, kSmallCallThreads, 0, stream>>>(
         logits, nullptr, T, E, tk, has_shared ? 1 : 0, p, max_rows, max_mtiles, status, x, H, img);
   else
-    bs_route_plan_quant_kernel<16><<<T, kSmallCallThreads, 0, stream>>>(
+    bs_route_plan_quant_kernel<4><<<T, kSmallCallThreads, 0, stream>>>(
         logits, nullptr, T, E, tk, has_shared ? 1 : 0, p, max_rows, max_mtiles, status, x, H, img);
 }
 

@@ -1358,7 +1358,8 @@ WM_EXPORT int wm_moe_forward(wm_ctx* ctx, const wm_moe_args* args, void* stream)
   // Small router calls on the block-scaled decode path select, plan and
   // quantise the token rows in one launch after the logits.
   const bool small = a->router_weight != nullptr && path == kPathBsDecode &&
-                     !(ctx->opt.flags & WM_FLAG_SPLIT_SMALL_CALLS) && wm::bs_route_plan_quant_ok(a->T, a->K, a->E);
+                     !(ctx->opt.flags & WM_FLAG_SPLIT_SMALL_CALLS) &&
+                     wm::bs_route_plan_quant_ok(a->T, a->K, a->E, a->router);
   if (a->router_weight != nullptr) {
     int32_t* di = a->out_idx ? a->out_idx : ctx->idx;
     float* dw = a->out_w ? a->out_w : ctx->w;

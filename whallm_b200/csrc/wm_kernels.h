@@ -67,6 +67,10 @@ void launch_rmsnorm(const uint16_t* x, const uint16_t* nw, int T, int H, float e
                     cudaStream_t stream);
 void launch_shared_gate(const uint16_t* x, const uint16_t* g, int T, int H, float* sg, cudaStream_t stream);
 void launch_router_topk(const float* logits, int T, int E, const TopkArgs& tk, cudaStream_t stream);
+// Calls of up to kTopkGroupCalls tokens select with a block of warps per token
+// (K <= 32, E <= 1024, every router kind but the group-limited one).
+constexpr int kTopkGroupCalls = 64;
+bool router_topk_group_ok(int T, int K, int E, int kind);
 
 // ---- router logits on tcgen05 for long calls (wm_router_sm100.cu); tm_x / tm_w
 // point to CUtensorMaps of x [T, H] and W_r [E, H] (bf16, 64 x 128 boxes, 128B swizzle)
@@ -226,7 +230,7 @@ void launch_bs_quant_rows(const uint16_t* x, const Plan& p, int E, int K, uint8_
 constexpr int kSmallCallTokens = 4;  // measured: batch 1 -1.9 us, batch 8 +1.1 us per layer
 constexpr int kSmallCallThreads = 512;
 bool bs_plan_quant_ok(int T, int K, int E);
-bool bs_route_plan_quant_ok(int T, int K, int E);
+bool bs_route_plan_quant_ok(int T, int K, int E, int kind);
 void launch_bs_plan_quant(const int32_t* routes, int T, int K, int E, bool has_shared, const Plan& p, int max_rows,
                           int max_mtiles, uint32_t* status, const uint16_t* x, int H, uint8_t* img,
                           cudaStream_t stream);

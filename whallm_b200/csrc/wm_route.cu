@@ -359,7 +359,36 @@ void launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t*
   router_logits_kernel<<<blocks, 256, smem, stream>>>(x, wr, sg_w, T, H, E, logits, sg);
 }
 
+// Top-k of short calls: a block of kTopkGroupWarps warps per token, each warp
+// selecting from a quarter of the experts, then one warp from their
+// candidates -- the same selections and weights as router_topk_kernel, with
+// the chain of selection rounds split over two shorter chains.
+template <int EPL>
+__global__ void __launch_bounds__(32 * kTopkGroupWarps) router_topk_group_kernel(const float* __restrict__ logits,
+                                                                               int T, int E, const TopkArgs tk) {
+  __shared__ TopkCands c;
+  const int t = blockIdx.x, g = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  topk_group_local<EPL>(logits + int64_t(t) * E, tk, E, g, lane, c);
+  __syncthreads();
+  if (g == 0) topk_group_merge(c, tk, t, lane);
+}
+
+bool router_topk_group_ok(int T, int K, int E, int kind) {
+  return T <= kTopkGroupCalls && K >= 1 && K <= kTopkGroupMaxK && E <= kTopkGroupWarps * 32 * 8 &&
+         kind != WM_ROUTER_SIGMOID_GROUPED;
+}
+
 void launch_router_topk(const float* logits, int T, int E, const TopkArgs& tk, cudaStream_t stream) {
+  if (router_topk_group_ok(T, tk.K, E, tk.kind)) {
+    const int threads = 32 * kTopkGroupWarps;
+    if (E <= kTopkGroupWarps * 64)
+      router_topk_group_kernel<2><<<T, threads, 0, stream>>>(logits, T, E, tk);
+    else if (E <= kTopkGroupWarps * 128)
+      router_topk_group_kernel<4><<<T, threads, 0, stream>>>(logits, T, E, tk);
+    else
+      router_topk_group_kernel<8><<<T, threads, 0, stream>>>(logits, T, E, tk);
+    return;
+  }
   const int blocks = (T + 1) / 2;
   if (E <= 256)
     router_topk_kernel<8><<<blocks, 64, 0, stream>>>(logits, T, E, tk);
