@@ -68,8 +68,10 @@ void launch_rmsnorm(const uint16_t* x, const uint16_t* nw, int T, int H, float e
 void launch_shared_gate(const uint16_t* x, const uint16_t* g, int T, int H, float* sg, cudaStream_t stream);
 void launch_router_topk(const float* logits, int T, int E, const TopkArgs& tk, cudaStream_t stream);
 // Calls of up to kTopkGroupCalls tokens select with a block of warps per token
-// (K <= 32, E <= 1024, every router kind but the group-limited one).
-constexpr int kTopkGroupCalls = 64;
+// (K <= 32, E <= 1024, every router kind but the group-limited one); measured
+// slower than a warp per token from 8 tokens up (config 1: 10.6 against 9.3 us
+// at 8 tokens, 10.5 against 9.6 us at 64).
+constexpr int kTopkGroupCalls = 4;
 bool router_topk_group_ok(int T, int K, int E, int kind);
 
 // ---- router logits on tcgen05 for long calls (wm_router_sm100.cu); tm_x / tm_w
