@@ -148,6 +148,13 @@ typedef struct {
    launch saves one or two kernel boundaries per layer. */
 #define WM_FLAG_SPLIT_SMALL_CALLS 16
 
+/* The block-scaled decode path's gate/up and down kernels run as one
+   persistent launch: a down item waits (bounded, 2 s, then an error through
+   wm_sync) until the gate/up items of its 16-token tile have written the act
+   rows, so the down weights stream while the last gate/up items finish.  Not
+   on the expert-parallel owner path.  Off by default: not yet measured. */
+#define WM_FLAG_FUSED_DECODE 32
+
 /* One projection of every expert: expert e's matrix at weight + e * weight_stride
    bytes, its scales at scale + e * scale_stride bytes (device pointers). */
 typedef struct {

@@ -529,10 +529,371 @@ __global__ void __launch_bounds__(kThreads, 1) bs_decode_kernel(const __grid_con
   }
 }
 
+// ------------------------------------------------------------------ gate/up and down in one launch
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void red_release_gpu_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Orders generic-proxy global accesses and async-proxy (bulk copy) accesses.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// Both expert kernels of the block-scaled decode path in one persistent
+// launch: items [0, n0) are the gate/up items of bs_decode_kernel<0> (tile
+// q / nb0, 64 features), items [n0, n0 + n1) the down items of
+// bs_decode_kernel<1> (tile, 128 output rows), each CTA taking items
+// blockIdx.x, blockIdx.x + gridDim.x, ... in order, with the same stage ring,
+// MMAs and epilogues.  A down item reads its tile's act images, which the
+// gate warps of that tile's nb0 gate/up items write: each gate warp, after its
+// bytes, fences them toward the async proxy and adds 1 to the tile's count
+// (release); the down item's producer waits (acquire, bounded: 2 s, then the
+// status word and unwinding) for 2 nb0 before the act-image copy.  The down
+// weights stream while the last gate/up items finish, instead of after the
+// first launch's tail.  No wait can close a cycle: every CTA's gate/up items
+// precede its down items, and gate/up items wait for nothing.  The CTA that
+// finishes last clears the counts for the next launch.
+__global__ void __launch_bounds__(kThreads, 1) bs_decode_fused_kernel(
+    const __grid_constant__ CUtensorMap gu_w, const __grid_constant__ CUtensorMap gu_ws,
+    const __grid_constant__ CUtensorMap gu_s, const __grid_constant__ CUtensorMap gu_ss,
+    const __grid_constant__ CUtensorMap dn_w, const __grid_constant__ CUtensorMap dn_ws,
+    const __grid_constant__ CUtensorMap dn_s, const __grid_constant__ CUtensorMap dn_ss, const BsArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  const int S0 = a.H / kBK, S1 = a.I / kBK;  // stages of a gate/up and of a down item
+  const int nb0 = a.I / 64, nb1 = a.H / kBM;
+  const int NS = a.stages;
+  const int n_tiles = *a.plan.n_mtiles;
+  const int n0 = n_tiles * nb0, n_items = n0 + n_tiles * nb1;
+  const uint32_t done_target = 2u * uint32_t(nb0);  // two gate warps per gate/up item
+  const uint32_t raw0 = smem_u32(smem_raw);
+  const uint32_t base = (raw0 + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw0);
+  BsShared& sh = *reinterpret_cast<BsShared*>(gbase + NS * kStageBytes + kRawSlots * kRawBytes);
+  const uint32_t raw_base = base + NS * kStageBytes;
+  auto a_addr = [&](int slot) { return base + slot * kStageBytes; };
+  auto b_addr = [&](int slot) { return base + slot * kStageBytes + kASmem; };
+  auto sfb_addr = [&](int slot) { return base + slot * kStageBytes + kASmem + kBSmem; };
+  auto sfa_addr = [&](int slot) { return base + slot * kStageBytes + kASmem + kBSmem + kAtom; };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&sh.full[i], 2);  // the TMA producer (with bytes) and the scale warp
+      mbar_init(&sh.empty[i], 1);
+    }
+    for (int i = 0; i < kRawSlots; ++i) {
+      mbar_init(&sh.raw_full[i], 1);
+      mbar_init(&sh.raw_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sh.tmem_full[i], 1);
+      mbar_init(&sh.tmem_empty[i], 4);
+      mbar_init(&sh.xch_full[i], 2);
+      mbar_init(&sh.xch_empty[i], 2);
+    }
+    mbar_init(&sh.mma_done, 1);
+    sh.abort = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&sh.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  volatile int* abort = &sh.abort;
+  auto fail = [&](uint32_t role) {
+    if (atomicExch(&sh.abort, 1) == 0) report_status(a.status, kStatusWaitTimeout, role);
+  };
+  // item q: kind (0 gate/up, 1 down), expert, first row, block
+  auto item = [&](int q, int* kind, int* e, int* row0, int* blk) {
+    const int down = q >= n0 ? 1 : 0;
+    const int r = q - down * n0, nb = down ? nb1 : nb0;
+    const int tile = r / nb;
+    *kind = down;
+    *blk = r - tile * nb;
+    *e = a.plan.mtiles[2 * tile];
+    *row0 = a.plan.mtiles[2 * tile + 1];
+  };
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&gu_w);
+      tma_prefetch_desc(&gu_s);
+      tma_prefetch_desc(&dn_w);
+      tma_prefetch_desc(&dn_s);
+      int st = 0, ph = 0, rs = 0, rph = 0;
+      int ck = 0, ce = 0, crow0 = 0, cblk = 0, nk = 0, ne = 0, nrow0 = 0, nblk = 0;
+      if (int(blockIdx.x) < n_items) item(blockIdx.x, &ck, &ce, &crow0, &cblk);
+      if (int(blockIdx.x + gridDim.x) < n_items) item(blockIdx.x + gridDim.x, &nk, &ne, &nrow0, &nblk);
+      for (int q = blockIdx.x; q < n_items && !*abort; q += gridDim.x) {
+        const int kind = ck, e = ce, row0 = crow0, blk = cblk;
+        int n2k = 0, n2e = 0, n2row0 = 0, n2blk = 0;
+        if (q + 2 * int(gridDim.x) < n_items) item(q + 2 * gridDim.x, &n2k, &n2e, &n2row0, &n2blk);
+        const bool shared_e = e == a.wts.E;
+        const void* mw = kind ? (shared_e ? &dn_ws : &dn_w) : (shared_e ? &gu_ws : &gu_w);
+        const void* ms = kind ? (shared_e ? &dn_ss : &dn_s) : (shared_e ? &gu_ss : &gu_s);
+        const int ez = shared_e ? 0 : e;
+        const int tile = row0 / kTokTile;
+        const int S = kind ? S1 : S0;
+        const uint8_t* img = kind ? a.act_img : a.img;
+        bool ok = true;
+        for (int s = 0; s < S; ++s) {
+          if ((s & 3) == 0) {
+            if (!mbar_wait(&sh.raw_empty[rs], rph ^ 1, abort)) { fail(90); ok = false; break; }
+            const uint32_t dst = raw_base + rs * kRawBytes;
+            mbar_arrive_expect_tx(&sh.raw_full[rs], kRawBytes);
+            if (kind == 0)  // rows blk * 64 .. + 63 of both halves of w13 (one 4-D box)
+              tma_load_4d(dst, ms, 16 * (s >> 2), blk * 64, 0, ez, &sh.raw_full[rs]);
+            else
+              tma_load_3d(dst, ms, 16 * (s >> 2), blk * kBM, ez, &sh.raw_full[rs]);
+            if (++rs == kRawSlots) { rs = 0; rph ^= 1; }
+          }
+          if (!mbar_wait(&sh.empty[st], ph ^ 1, abort)) { fail(91); ok = false; break; }
+          mbar_arrive_expect_tx(&sh.full[st], kATxBytes + uint32_t(kImage));
+          if (kind == 0)
+            tma_load_4d(a_addr(st), mw, s * kBK, blk * 64, 0, ez, &sh.full[st]);
+          else
+            tma_load_3d(a_addr(st), mw, s * kBK, blk * kBM, ez, &sh.full[st]);
+          if (kind == 1 && s == 0) {
+            // the tile's act images: every gate warp of its gate/up items has written them
+            const uint64_t t0 = global_timer_ns();
+            for (uint32_t spin = 0; ld_acquire_gpu_u32(a.tile_done + tile) < done_target; ++spin) {
+              if ((spin & 15u) == 15u && (*abort || global_timer_ns() - t0 > 2000000000ull)) {
+                ok = false;
+                break;
+              }
+              __nanosleep(64);
+            }
+            fence_proxy_async_global();
+            if (!ok) {
+              fail(92);
+              // complete the stage's transaction so no wait on it is left pending
+              bulk_g2s(b_addr(st), img + (int64_t(tile) * S + s) * kImage, uint32_t(kImage), &sh.full[st]);
+              break;
+            }
+          }
+          // the token (or act) tile image and its scale atom in one copy
+          bulk_g2s(b_addr(st), img + (int64_t(tile) * S + s) * kImage, uint32_t(kImage), &sh.full[st]);
+          if (++st == NS) { st = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+        ck = nk, ce = ne, crow0 = nrow0, cblk = nblk;
+        nk = n2k, ne = n2e, nrow0 = n2row0, nblk = n2blk;
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- scale warp
+    int st = 0, ph = 0, rs = 0, rph = 0;
+    for (int q = blockIdx.x; q < n_items; q += gridDim.x) {
+      if (warp_aborted(abort)) break;
+      const int S = q >= n0 ? S1 : S0;
+      bool ok = true;
+      for (int s0 = 0; s0 < S && ok; s0 += 4) {
+        if (!warp_wait(&sh.raw_full[rs], rph, abort)) { ok = false; break; }
+        int st_g[4];
+        for (int j = 0; j < 4; ++j) {
+          if (!warp_wait(&sh.empty[st], ph ^ 1, abort)) { ok = false; break; }
+          const uint32_t rb = raw_base + rs * kRawBytes + 4 * j;
+          const uint32_t w0 = lds_b32(rb + (lane)*16), w1 = lds_b32(rb + (lane + 32) * 16),
+                         w2 = lds_b32(rb + (lane + 64) * 16), w3 = lds_b32(rb + (lane + 96) * 16);
+          sts_v4(sfa_addr(st) + lane * 16, w0, w1, w2, w3);
+          st_g[j] = st;
+          if (++st == NS) { st = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          for (int j = 0; j < 4; ++j) mbar_arrive(&sh.full[st_g[j]]);
+          mbar_arrive(&sh.raw_empty[rs]);
+        }
+        if (++rs == kRawSlots) { rs = 0; rph ^= 1; }
+      }
+      if (!ok) {
+        if (lane == 0) fail(93);
+        break;
+      }
+    }
+  } else if (warp == 2) {
+    // ---------------------------------------------------------------- MMA issuer
+    int st = 0, ph = 0, li = 0;
+    for (int q = blockIdx.x; q < n_items; q += gridDim.x, ++li) {
+      if (warp_aborted(abort)) break;
+      const int S = q >= n0 ? S1 : S0;
+      const int acc = li & 1;
+      if (!warp_wait(&sh.tmem_empty[acc], ((li >> 1) & 1) ^ 1, abort)) {
+        if (lane == 0) fail(94);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d = tmem + acc * kAccCols;
+      bool ok = true;
+      for (int s = 0; s < S; ++s) {
+        if (!warp_wait(&sh.full[st], ph, abort)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sfa_t = tmem + kSfCol0 + st * 8, sfb_t = sfa_t + 4;
+        sf_copy_elect(sfa_t, sf_desc(sfa_addr(st)));
+        sf_copy_elect(sfb_t, sf_desc(sfb_addr(st)));
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          bs_mma_elect(d, umma_desc_sw128(a_addr(st) + 32 * kk), umma_desc_sw128(b_addr(st) + 32 * kk),
+                       bs_idesc(uint32_t(kk)), sfa_t | (uint32_t(kk) << 30), sfb_t | (uint32_t(kk) << 30),
+                       (s > 0 || kk > 0) ? 1u : 0u);
+        umma_commit_elect(&sh.empty[st]);
+        __syncwarp();
+        if (++st == NS) { st = 0; ph ^= 1; }
+      }
+      if (!ok) {
+        if (lane == 0) fail(95);
+        break;
+      }
+      umma_commit_elect(&sh.tmem_full[acc]);
+      __syncwarp();
+    }
+    umma_commit_elect(&sh.mma_done);
+    __syncwarp();
+    volatile int keep_waiting = 0;  // this wait ignores the abort flag (0.2 s bound)
+    mbar_wait(&sh.mma_done, 0, &keep_waiting, 0, 200000000ull);
+  } else if (warp >= kEpiWarp0) {
+    // ---------------------------------------------------------------- epilogue
+    const int quarter = warp - kEpiWarp0;
+    int li = 0;
+    int ck = 0, ce = 0, crow0 = 0, cblk = 0, cvalid = 0, nk = 0, ne = 0, nrow0 = 0, nblk = 0;
+    if (int(blockIdx.x) < n_items) {
+      item(blockIdx.x, &ck, &ce, &crow0, &cblk);
+      cvalid = min(kTokTile, a.plan.counts[ce] - (crow0 - a.plan.offsets[ce]));
+    }
+    if (int(blockIdx.x + gridDim.x) < n_items) item(blockIdx.x + gridDim.x, &nk, &ne, &nrow0, &nblk);
+    for (int q = blockIdx.x; q < n_items; q += gridDim.x, ++li) {
+      if (warp_aborted(abort)) break;
+      const int kind = ck, row0 = crow0, blk = cblk, valid = cvalid;
+      int n2k = 0, n2e = 0, n2row0 = 0, n2blk = 0, ncount = 0, noff = 0;
+      if (q + 2 * int(gridDim.x) < n_items) item(q + 2 * gridDim.x, &n2k, &n2e, &n2row0, &n2blk);
+      if (q + int(gridDim.x) < n_items) {
+        ncount = a.plan.counts[ne];
+        noff = a.plan.offsets[ne];
+      }
+      const int acc = li & 1;
+      if (!warp_wait(&sh.tmem_full[acc], (li >> 1) & 1, abort)) {
+        if (lane == 0) fail(96);
+        break;
+      }
+      tc_fence_after();
+      uint32_t r[32];
+      tmem_ld_32cols(tmem + acc * kAccCols + (uint32_t(quarter * 32) << 16), r);
+      tmem_ld_wait();
+      float y[kTokTile];
+#pragma unroll
+      for (int n = 0; n < kTokTile; ++n) y[n] = __uint_as_float(r[n]) + __uint_as_float(r[kTokTile + n]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.tmem_empty[acc]);
+      if (kind == 1) {
+        const int h = blk * kBM + quarter * 32 + lane;
+        if (a.ret.rows[0] != nullptr) {
+          for (int n = 0; n < valid; ++n) {
+            const int slot = a.plan.row_token[row0 + n];
+            if (slot >= 0)
+              a.ret.rows[slot / a.ret.capacity][int64_t(slot % a.ret.capacity) * a.H + h] = f32_to_bf16_bits(y[n]);
+          }
+        } else {
+          for (int n = 0; n < valid; ++n) a.routed[int64_t(row0 + n) * a.H + h] = f32_to_bf16_bits(y[n]);
+        }
+      } else {
+        const int xb = li & 1;
+        const uint32_t xph = (li >> 1) & 1;
+        const bool up_warp = a.gate_first ? quarter >= 2 : quarter < 2;
+        const int pair = quarter & 1;
+        if (up_warp) {
+          if (!warp_wait(&sh.xch_empty[xb], xph ^ 1, abort)) {
+            if (lane == 0) fail(97);
+            break;
+          }
+#pragma unroll
+          for (int n = 0; n < kTokTile; ++n) sh.xch[xb][pair * 32 + lane][n] = y[n];
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sh.xch_full[xb]);
+        } else {
+          if (!warp_wait(&sh.xch_full[xb], xph, abort)) {
+            if (lane == 0) fail(98);
+            break;
+          }
+          const int f = blk * 64 + pair * 32 + lane;
+          const int sd = f / kBK, kk = (f % kBK) / 32;
+          const int tile = row0 / kTokTile;
+          uint8_t* img = a.act_img + (int64_t(tile) * S1 + sd) * kImage;
+          uint8_t* sfb = img + kBSmem;
+          const int c = (f % kBK) / 16, byte = f % 16;
+          for (int n = 0; n < valid; ++n) {
+            const float gv = bf16_round(y[n]), uv = bf16_round(sh.xch[xb][pair * 32 + lane][n]);
+            const float act = bf16_round(swiglu_f32(gv, uv, a.limit));
+            float amax = fabsf(act);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const uint32_t bh = e4m3_block_scale(amax);
+            const uint32_t hb = to_e4m3x2(act * __uint_as_float((254u - bh) << 23), 0.0f) & 0xFFu;
+            float hv[4];
+            e4m3x4_to_f32(hb, hv);
+            const float res = act - hv[0] * __uint_as_float(bh << 23);
+            float rmax = fabsf(res);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, o));
+            const uint32_t bl = e4m3_block_scale(rmax);
+            const uint32_t lb = to_e4m3x2(res * __uint_as_float((254u - bl) << 23), 0.0f) & 0xFFu;
+            img[image_off(n, c) + byte] = uint8_t(hb);
+            img[image_off(kTokTile + n, c) + byte] = uint8_t(lb);
+            if (lane == 0) {
+              sfb[n * 16 + kk] = uint8_t(bh);
+              sfb[(kTokTile + n) * 16 + kk] = uint8_t(bl);
+            }
+          }
+          // this warp's act bytes, then its count for the tile's down items
+          fence_proxy_async_global();
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) {
+            red_release_gpu_add(a.tile_done + tile, 1u);
+            mbar_arrive(&sh.xch_empty[xb]);
+          }
+        }
+      }
+      ck = nk, ce = ne, crow0 = nrow0, cblk = nblk;
+      cvalid = min(kTokTile, ncount - (nrow0 - noff));
+      nk = n2k, ne = n2e, nrow0 = n2row0, nblk = n2blk;
+    }
+    if (a.ret.rows[0] != nullptr) __threadfence_system();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+  // the last CTA to finish clears the tile counts for the next launch
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(a.tile_done + a.max_tiles, 1u) == gridDim.x - 1) {
+      for (int t = 0; t < n_tiles; ++t) a.tile_done[t] = 0u;
+      a.tile_done[a.max_tiles] = 0u;
+      __threadfence();
+    }
+  }
+}
+
 void bs_init_attributes() {
   const int bytes = int(bs_smem_bytes(bs_stages(0)));
   cudaFuncSetAttribute(bs_decode_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   cudaFuncSetAttribute(bs_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  cudaFuncSetAttribute(bs_decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
 bool bs_shape_ok(int H, int I) { return H % 512 == 0 && I % 512 == 0 && H >= 512 && I >= 512; }
@@ -570,6 +931,16 @@ void launch_bs_plan_quant(const int32_t* routes, int T, int K, int E, bool has_s
   tk.K = K;
   bs_route_plan_quant_kernel<0><<<T, kSmallCallThreads, 0, stream>>>(
       nullptr, routes, T, E, tk, has_shared ? 1 : 0, p, max_rows, max_mtiles, status, x, H, img);
+}
+
+void launch_bs_decode_fused(const BsArgs& args, const void* const* maps, int num_sms, cudaStream_t stream) {
+  BsArgs a = args;
+  a.stages = bs_stages(a.H);
+  const size_t smem = bs_smem_bytes(a.stages);
+  const CUtensorMap* m[8];
+  for (int i = 0; i < 8; ++i) m[i] = static_cast<const CUtensorMap*>(maps[i]);
+  bs_decode_fused_kernel<<<num_sms, kThreads, smem, stream>>>(*m[0], *m[1], *m[2], *m[3], *m[4], *m[5], *m[6], *m[7],
+                                                               a);
 }
 
 void launch_bs_decode(const BsArgs& args, int kind, const void* const* maps, int num_sms, cudaStream_t stream) {

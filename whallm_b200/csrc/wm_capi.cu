@@ -40,6 +40,7 @@ struct wm_ctx {
   uint8_t* xss = nullptr;      // block-scaled GEMM: the sorted x rows' UE8M0 scale rows (hi, lo)
   uint8_t* bs_img_x = nullptr;    // block-scaled decode / GEMM: token tile images (hi / lo E4M3 + scale atoms)
   uint8_t* bs_img_act = nullptr;  // ... and the act tile images
+  uint32_t* tile_done = nullptr;  // fused decode launch: per-tile counts (max_mtiles + 1, zero between calls)
   int max_rows = 0, max_mtiles = 0, max_chunks = 0;
   PFN_cuTensorMapEncodeTiled_v12000 encode_tiled = nullptr;
   wm::Profiler prof;
@@ -520,6 +521,20 @@ int run_bs_decode(wm_ctx* ctx, const wm_moe_args* a, const wm::ExpertWeights& wt
     ctx->counters.launches += 1;
   }
   b.img = ximg;
+  if ((ctx->opt.flags & WM_FLAG_FUSED_DECODE) && ret == nullptr) {
+    // both expert kernels in one persistent launch (not on the expert-parallel
+    // owner path, whose side-stream kernels could hold SMs the launch waits on)
+    b.tile_done = ctx->tile_done;
+    b.max_tiles = ctx->max_mtiles;
+    const void* maps[8] = {&w13, has_shared ? &w13s : &w13, &s13, has_shared ? &s13s : &s13,
+                           &w2,  has_shared ? &w2s : &w2,   &s2,  has_shared ? &s2s : &s2};
+    wm::prof_begin(&ctx->prof, wm::kProfDecodeFused, s);
+    wm::launch_bs_decode_fused(b, maps, ctx->num_sms, s);
+    wm::prof_end(&ctx->prof, wm::kProfDecodeFused, s);
+    ctx->counters.launches += 1;
+    ctx->counters.decode_calls += 1;
+    return check_launch(ctx, "block-scaled expert decode (one launch)");
+  }
   wm::prof_begin(&ctx->prof, wm::kProfDecodeGateUp, s);
   const void* maps0[4] = {&w13, has_shared ? &w13s : &w13, &s13, has_shared ? &s13s : &s13};
   wm::launch_bs_decode(b, 0, maps0, ctx->num_sms, s);
@@ -738,7 +753,7 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
   }
   wm_options o = *options;
   if (o.flags & ~int32_t(WM_FLAG_SKIP_NEGATIVE_ROUTES | WM_FLAG_MMA_DECODE | WM_FLAG_F16_GEMM |
-                        WM_FLAG_SPLIT_SMALL_CALLS)) {
+                        WM_FLAG_SPLIT_SMALL_CALLS | WM_FLAG_FUSED_DECODE)) {
     report("unknown flags");
     return nullptr;
   }
@@ -795,7 +810,8 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
                o_rowmax = take(rows * 4), o_xn = take(T * H * 2), o_xss = take(rows * (H / 32 + 1) * 2 + 1024),
                // tile images: the decode kernel's 16-row tiles (x and act) or the GEMM's 128-row act tiles
                o_imgx = take(rows * H * 9 / 4),
-               o_imga = take(std::max<size_t>(rows * I * 9 / 4, wm::bsg_image_bytes(rows / wm::kTileM + 2, int(I))));
+               o_imga = take(std::max<size_t>(rows * I * 9 / 4, wm::bsg_image_bytes(rows / wm::kTileM + 2, int(I)))),
+               o_tiledone = take((size_t(ctx->max_mtiles) + 1) * 4);
   ctx->ws_bytes = off;
   if (cudaMalloc(&ctx->ws, ctx->ws_bytes) != cudaSuccess) {
     cudaGetLastError();
@@ -831,6 +847,7 @@ WM_EXPORT wm_ctx* wm_create(int32_t device, const wm_options* options, char* err
   ctx->xss = base + o_xss;
   ctx->bs_img_x = base + o_imgx;
   ctx->bs_img_act = base + o_imga;
+  ctx->tile_done = reinterpret_cast<uint32_t*>(base + o_tiledone);
   // the whole workspace starts at zero (status word included); padding rows of
   // the f16 row blocks are never written afterwards, so they hold zeros or an
   // earlier call's finite rows

@@ -32,6 +32,7 @@ enum ProfSlot : int {
   kProfEpReturn,        // result rows back to their senders
   kProfEpWaitReturn,    // waiting for every peer's result rows
   kProfRoutePlanQuant,  // small router calls: top-k, plan and token images in one launch
+  kProfDecodeFused,     // block-scaled decode: gate/up and down in one launch (WM_FLAG_FUSED_DECODE)
   kProfSlots
 };
 struct Profiler;  // defined in wm_profile.cu
@@ -216,6 +217,8 @@ struct BsArgs {
   uint16_t* routed;      // down: [rows, H] bf16
   EpReturn ret;          // down: with ret.rows[0] set, rows go to the senders instead of `routed`
   int stages;
+  uint32_t* tile_done;   // fused launch: per-tile counts of act-image writers, then a finish count
+  int max_tiles;         // ... at tile_done[max_tiles]
 };
 void bs_init_attributes();
 // H and I multiples of 512 (four 128-K stages per raw scale load)
@@ -244,6 +247,10 @@ void launch_bs_route_plan_quant(const float* logits, int T, int E, const TopkArg
 // 128 x 64 x 2, down 3-D [E][H][I] with boxes 128 x 128) and of their E8M0
 // rows (uint8, gate/up [E][2][I][H/32] boxes 16 x 64 x 2, down [E][H][I/32] boxes 16 x 128).
 void launch_bs_decode(const BsArgs& a, int kind, const void* const* maps, int num_sms, cudaStream_t stream);
+// Both expert kernels in one persistent launch (down items wait, bounded, for
+// their tile's gate/up items): maps[0..3] as launch_bs_decode's gate/up maps,
+// maps[4..7] its down maps; a.tile_done zero on entry (left zero on exit).
+void launch_bs_decode_fused(const BsArgs& a, const void* const* maps, int num_sms, cudaStream_t stream);
 
 // ---- prefill grouped GEMM on tcgen05 block-scaled MMA (wm_bsgemm_sm100.cu):
 // 128 token rows (hi / lo E4M3) x 256 weight rows per tile.  The same BsArgs

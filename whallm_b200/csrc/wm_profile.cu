@@ -68,7 +68,7 @@ const char* prof_name(int slot) {
                                           "gemv_gate_up",  "gemv_down",   "gemm_gate_up", "gemm_down", "combine",
                                           "decode_gate_up", "decode_down", "rmsnorm",
                                           "ep_send", "ep_wait_dispatch", "ep_return", "ep_wait_return",
-                                          "route_plan_quant"};
+                                          "route_plan_quant", "decode_fused"};
   return slot >= 0 && slot < kProfSlots ? names[slot] : "?";
 }
 

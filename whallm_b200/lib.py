@@ -23,6 +23,7 @@ FLAG_SKIP_NEGATIVE_ROUTES = 1
 FLAG_MMA_DECODE = 4
 FLAG_F16_GEMM = 8
 FLAG_SPLIT_SMALL_CALLS = 16
+FLAG_FUSED_DECODE = 32
 
 # Every entry point the header declares (checked by the CPU test suite).
 EXPORTS = (
