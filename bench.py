@@ -45,10 +45,13 @@ BLOB = 1_671_168  # bytes of one expert blob (gate_up + scales + down + scales)
 GATE_UP_BYTES = 2 * I * H // 2 + 2 * I * H // 32
 # dram bytes (read + write) of one gate/up decode launch at this workload, from an ncu capture
 # (profiles/decode_bs_config1_b64.txt: block-scaled kernel; profiles/decode_mma_config1_b64.txt: --decode mma)
-NCU_GATE_UP_TRAFFIC = {"bs": 436.316416e6 + 6.585344e6, "mma": 412.166656e6 + 3.397376e6}
+NCU_GATE_UP_TRAFFIC = {"bs": 436.316416e6 + 6.585344e6, "mma": 412.166656e6 + 3.397376e6, "fused": None}
 DECODE_KERNEL = {"bs": "bs_decode_kernel<0> (gate/up + SwiGLU; block-scaled tcgen05, kind::mxf8f6f4)",
-                 "mma": "decode_mma_kernel<0> (gate/up + SwiGLU; register-direct mma.sync)"}
-DECODE_PROFILE = {"bs": "profiles/decode_bs_config1_b64.txt", "mma": "profiles/decode_mma_config1_b64.txt"}
+                 "mma": "decode_mma_kernel<0> (gate/up + SwiGLU; register-direct mma.sync)",
+                 "fused": "bs_decode_fused_kernel (gate/up + SwiGLU and down in one launch; block-scaled tcgen05)"}
+DECODE_PROFILE = {"bs": "profiles/decode_bs_config1_b64.txt", "mma": "profiles/decode_mma_config1_b64.txt",
+                  "fused": None}
+DECODE_FLAGS = {"bs": 0, "mma": "FLAG_MMA_DECODE", "fused": "FLAG_FUSED_DECODE"}
 DOWN_BYTES = H * I // 2 + H * I // 32
 
 
@@ -795,8 +798,9 @@ def run(args) -> None:
     layer = wl.layer
     nb = 8
     xs = [synth.activations(B, H, torch.Generator(device=dev).manual_seed(1000 * rank + i), dev) for i in range(nb)]
+    flag = DECODE_FLAGS[args.decode]
     eng = Engine(local, max_tokens=max(B, 64), hidden=H, inter=I, experts=E, topk=K,
-                 flags=lib.FLAG_MMA_DECODE if args.decode == "mma" else 0)
+                 flags=getattr(lib, flag) if flag else 0)
     x_static = xs[0].clone()
     out_static = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
@@ -866,8 +870,13 @@ def run(args) -> None:
     dn_n, dn_ms = prof.get("decode_down", (1, float("nan")))
     gu_bytes = (U + 1) * GATE_UP_BYTES + B * H * 2 + B * 2 * I * 2  # weights + x + act written
     dn_bytes = (U + 1) * DOWN_BYTES + (B * K + B) * (I * 2 + H * 2)
-    gu_avg = gu_ms / gu_n
     pk = peaks()
+    if args.decode == "fused":  # one launch streams both projections: its bytes over its time
+        fu_n, fu_ms = prof.get("decode_fused", (1, float("nan")))
+        gu_bytes, gu_avg = gu_bytes + dn_bytes, fu_ms / fu_n
+        dn_n, dn_ms = fu_n, fu_ms
+    else:
+        gu_avg = gu_ms / gu_n
     achieved = gu_bytes / (gu_avg / 1e3) / 1e9
     kernels = {name: {"launches": n, "avg_us": 1e3 * t / n} for name, (n, t) in prof.items()}
 
@@ -934,10 +943,12 @@ def run(args) -> None:
         "roofline": {"bound": "hbm", "kernel": DECODE_KERNEL[args.decode], "achieved": achieved,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
                      "peak_source": pk["source"], "traffic": NCU_GATE_UP_TRAFFIC[args.decode],
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch, "
-                                       + DECODE_PROFILE[args.decode],
+                     "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch, "
+                                        + DECODE_PROFILE[args.decode]) if DECODE_PROFILE[args.decode]
+                                       else "no ncu capture of this kernel yet",
                      "algorithmic_bytes_per_launch": gu_bytes,
-                     "down_achieved_gbs": dn_bytes / (dn_ms / dn_n / 1e3) / 1e9},
+                     "down_achieved_gbs": (None if args.decode == "fused"
+                                           else dn_bytes / (dn_ms / dn_n / 1e3) / 1e9)},
         "kernels": kernels,
         "cpu_baseline": cpu,
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": B * H * 2, "d2h_bytes_per_step": B * H * 2},
@@ -963,8 +974,9 @@ def main():
     ap.add_argument("--no-long", action="store_true", help="skip the config-3 and config-4 long-call sections")
     ap.add_argument("--clocks-dir", default=None,
                     help="folder for the raw nvidia-smi clock samples (default: the system temp folder)")
-    ap.add_argument("--decode", default="bs", choices=["bs", "mma"],
-                    help="decode expert kernels: block-scaled tcgen05 (bs, the default) or register-direct warp MMAs")
+    ap.add_argument("--decode", default="bs", choices=["bs", "mma", "fused"],
+                    help="decode expert kernels: block-scaled tcgen05 (bs, the default), register-direct warp MMAs, "
+                         "or the block-scaled gate/up and down in one launch (fused)")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="N > 1: expert-parallel exchanges over peer memory (default) or NCCL all-to-all")
     args = ap.parse_args()
