@@ -56,3 +56,14 @@ def test_binding_struct_layout_matches_header():
         sizes = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
     assert sizes == [ctypes.sizeof(lib.Options), ctypes.sizeof(lib.Matrix), ctypes.sizeof(lib.MoeArgs),
                      ctypes.sizeof(lib.Counters)]
+
+
+def test_binding_flags_match_header():
+    """Every WM_FLAG_* of the header has its lib.FLAG_* twin with the same bit, and no other."""
+    from whallm_b200 import lib
+    text = "".join(h.read_text() for h in sorted((ROOT / "include").glob("*.h")))
+    header = {name: int(value) for name, value in re.findall(r"#define\s+WM_(FLAG_\w+)\s+(\d+)", text)}
+    binding = {name: getattr(lib, name) for name in dir(lib) if name.startswith("FLAG_")}
+    assert header == binding
+    bits = list(header.values())
+    assert all(b & (b - 1) == 0 for b in bits) and len(set(bits)) == len(bits)
