@@ -79,6 +79,33 @@ def test_oracle_routes_match_the_numpy_restatement(kind, E, K, biased, scale):
         assert np.all(np.diff(sel, axis=1) <= 0)
 
 
+def test_oracle_group_limited_routes_match_the_numpy_restatement():
+    """The group-limited sigmoid router (config 3; not in the reference): a
+    group's score is the sum of its two largest biased scores, the best
+    topk_groups groups stay eligible, then the top-k of biased scores among
+    them, weighted by the unbiased scores."""
+    rng = np.random.default_rng(3)
+    T, E, K, G, keep, scale = 32, 256, 8, 8, 4, 2.5
+    logits = rng.standard_normal((T, E)).astype(np.float32)
+    bias = (0.1 * rng.standard_normal(E)).astype(np.float32)
+    oi, ow = oracle.route(oracle.ROUTER_SIGMOID_GROUPED, logits, K, bias, G, keep, scale)
+    s = 1.0 / (1.0 + np.exp(-logits.astype(np.float64)))
+    biased = s + bias
+    for t in range(T):
+        groups = biased[t].reshape(G, E // G)
+        gscore = np.sort(groups, axis=1)[:, -2:].sum(axis=1)
+        kept = np.argsort(-gscore, kind="stable")[:keep]
+        mask = np.full(E, -np.inf)
+        for g in kept:
+            mask[g * (E // G):(g + 1) * (E // G)] = 0.0
+        sel = np.argsort(-(biased[t] + mask), kind="stable")[:K]
+        w = s[t, sel] / (s[t, sel].sum() + 1e-20) * scale
+        assert set(oi[t].tolist()) == set(sel.tolist())
+        got = dict(zip(oi[t].tolist(), ow[t].tolist()))
+        for e, v in zip(sel.tolist(), w.tolist()):
+            assert got[e] == pytest.approx(v, rel=1e-5, abs=1e-7)
+
+
 def ffn_numpy(layout, x, w13, s13, w2, s2, limit):
     """One expert on float rows x [R, H]: bf16 gate/up products, bf16 SwiGLU, bf16 down rows."""
     W13, W2 = dequant(w13, s13), dequant(w2, s2)
