@@ -167,3 +167,37 @@ def test_oracle_combine_is_the_fp32_weighted_sum_in_k_order():
     for k in range(K):  # fp32 products and sums, k order
         acc = (acc + w[:, k:k + 1] * rows[:, k]).astype(np.float32)
     assert np.array_equal(layer.forward(x_bits, idx, w), oracle.f32_to_bf16(acc))
+
+
+def dequant_fp8_b128(codes, scales):
+    """E4M3 [rows, cols] x fp32 scale per 128 x 128 block, one fp32 product, then bf16
+    (mimo/weights.py:17-43: the fp32 product rounded to the bf16 weight)."""
+    import torch
+    v = torch.from_numpy(codes).view(torch.float8_e4m3fn).to(torch.float32).numpy()
+    s = np.repeat(np.repeat(scales, 128, axis=0), 128, axis=1)[:codes.shape[0], :codes.shape[1]]
+    return bf16((v * s).astype(np.float32))
+
+
+def test_oracle_fp8_expert_rows_match_the_numpy_restatement():
+    rng = np.random.default_rng(21)
+    E, H, I, T, K = 3, 256, 256, 6, 2
+    def codes(shape):
+        c = rng.integers(0, 254, size=shape)
+        return np.where(c < 127, c, c + 1).astype(np.uint8)  # no NaN codes (0x7F, 0xFF)
+    w13, w2 = codes((E, 2 * I, H)), codes((E, H, I))
+    s13 = (rng.random((E, 2 * I // 128, H // 128)) * 2 ** -6 + 2 ** -8).astype(np.float32)
+    s2 = (rng.random((E, H // 128, I // 128)) * 2 ** -6 + 2 ** -8).astype(np.float32)
+    layer = oracle.Layer(oracle.LAYOUT_W13_FP8_B128, H, I, w13, s13, w2, s2)
+    x_bits = oracle.f32_to_bf16(rng.standard_normal((T, H)).astype(np.float32))
+    idx = np.stack([rng.permutation(E)[:K] for _ in range(T)]).astype(np.int32)
+    got = layer.pairs(x_bits, idx)
+    x = oracle.bf16_to_f32(x_bits).astype(np.float64)
+    for e in range(E):
+        t, k = np.nonzero(idx == e)
+        if t.size == 0:
+            continue
+        W13, W2 = dequant_fp8_b128(w13[e], s13[e]), dequant_fp8_b128(w2[e], s2[e])
+        gu = x[t] @ W13.T
+        up, gate = bf16(gu[:, :I]), bf16(gu[:, I:])  # w13 = [w3; w1]: up rows first
+        act = bf16(gate / (1.0 + np.exp(-gate)) * up)
+        _close_in_bf16(got[t, k], bf16(act @ W2.T))
