@@ -232,7 +232,7 @@ void launch_bs_quant_rows(const uint16_t* x, const Plan& p, int E, int K, uint8_
 // 1024, E <= 512).  Router calls of up to kSmallCallTokens tokens also select
 // the top-k in that launch (launch_bs_route_plan_quant: the routes of
 // launch_router_topk as well).
-constexpr int kSmallCallTokens = 4;  // measured: batch 1 -1.9 us, batch 8 +1.1 us per layer
+constexpr int kSmallCallTokens = 4;  // top-k inside too: batch 1 41.5 against 49.4 us; batch 8 slower (75.2 / 74.1)
 constexpr int kSmallCallThreads = 512;
 bool bs_plan_quant_ok(int T, int K, int E);
 bool bs_route_plan_quant_ok(int T, int K, int E, int kind);
